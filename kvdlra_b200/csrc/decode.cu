@@ -1,0 +1,346 @@
+// Factored decode attention (sm_100a).
+//
+// One query token per problem attends to [sinks | exact tier | middle | ring]
+// without materialising the middle (the reference materialises RoPE(U_k C_k)
+// and U_v C_v in bug_cache.py:1540-1575 and runs dense attention over the
+// peek of 1496-1519):
+//   * middle keys   k_t = RoPE_{pos_t}(U_k,g c_k,t)   per KV group g, built in
+//     registers from the coordinate row and the group's basis rows;
+//   * middle values accumulate in coordinate space, acc_c += p_t c_v,t, and
+//     are expanded once per split by U_v,g in the merge;
+//   * verbatim tiers read K/V rows directly.
+// Split-K over the token axis: each CTA handles `kChunk` tokens of one
+// (problem, KV group) for all G = Hq/Hkv query heads of the group and writes
+// (max, sum, acc_d, acc_c) partials; decode_merge_kernel combines them.
+#include "kernels.cuh"
+
+namespace kvd {
+
+constexpr int kDecThreads = 128;  // 4 warps
+constexpr int kChunk = 256;       // tokens per CTA
+constexpr int kMaxG = 8;          // query heads per KV group
+constexpr int kMaxNV = 4;         // head_dim <= 128 -> 4 values per lane
+constexpr int kMaxNC = 6;         // rank <= 192 -> 6 coordinates per lane
+
+struct DecArgs {
+  int H, D, G, ld, Hq;
+  int sink_len, hh_len, W, ring_len, L;
+  const void* sink_k; const void* sink_v; long sink_sp;
+  const void* hh_k; const void* hh_v; long hh_sp;
+  const void* ring_k; const void* ring_v; long ring_sp;  // offset to the first live slot
+  const float* uk; const float* uv; long u_sp;
+  const int* rk; const int* rv;
+  const float* ck; const float* cv; long c_sp;
+  const int* mid_pos; long mid_sp; int pos_base;
+  const float* inv_freq; float rope_scale;
+  const void* q; void* out;
+  float scaling;
+  float* part; long part_sp_chunk;  // partial record per (problem, group, chunk)
+  int n_chunks;
+};
+
+// Partial record layout (floats): m[G], l[G], acc_d[G][D], acc_c[G][ld]
+__host__ __device__ inline long part_floats(int G, int D, int ld) { return 2L * G + (long)G * D + (long)G * ld; }
+
+template <typename T, int NV, int NC>
+__global__ void __launch_bounds__(kDecThreads) decode_split_kernel(DecArgs a) {
+  extern __shared__ __align__(16) float dsm[];
+  const int chunk = blockIdx.x, g = blockIdx.y, p = blockIdx.z;
+  const int D = a.D, G = a.G, ld = a.ld, n = a.H * a.D, half = D / 2;
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+  const int r_k = a.rk[p], r_v = a.rv[p];
+  float* qs = dsm;                       // [G][D]
+  float* ukT = qs + G * D;               // [ld][D]   U_k,g transposed
+  float* crow = ukT + ld * D;            // [4 warps][ld]
+  float* red = crow + 4 * ld;            // merge scratch
+  const T* qp = reinterpret_cast<const T*>(a.q) + (long)p * a.Hq * D;
+  for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
+    const int qh = e / D, d = e % D;
+    qs[e] = load_f<T>(qp + (long)(g * G + qh) * D + d);
+  }
+  const int t0 = chunk * kChunk;
+  const int t1 = min(a.L, t0 + kChunk);
+  const int mid0 = a.sink_len + a.hh_len, mid1 = mid0 + a.W;
+  const bool has_mid = (t0 < mid1) && (t1 > mid0);
+  if (has_mid) {
+    const float* U = a.uk + p * a.u_sp;
+    for (int e = threadIdx.x; e < ld * D; e += blockDim.x) {
+      const int c = e / D, d = e % D;
+      ukT[e] = c < r_k ? U[(long)(g * D + d) * ld + c] : 0.f;
+    }
+  }
+  __syncthreads();
+  float mrun[kMaxG], lrun[kMaxG], accd[kMaxG][NV], accc[kMaxG][NC];
+#pragma unroll
+  for (int qh = 0; qh < kMaxG; ++qh) {
+    mrun[qh] = -INFINITY; lrun[qh] = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) accd[qh][i] = 0.f;
+#pragma unroll
+    for (int i = 0; i < NC; ++i) accc[qh][i] = 0.f;
+  }
+  float* myrow = crow + warp * ld;
+  for (int t = t0 + warp; t < t1; t += 4) {
+    float kv[NV], vv[NV];
+    bool is_mid = false;
+    if (t < a.sink_len || t >= mid1 || t < mid0) {
+      const T* kr; const T* vr;
+      if (t < a.sink_len) {
+        kr = reinterpret_cast<const T*>(a.sink_k) + p * a.sink_sp + (long)t * n;
+        vr = reinterpret_cast<const T*>(a.sink_v) + p * a.sink_sp + (long)t * n;
+      } else if (t < mid0) {
+        const int j = t - a.sink_len;
+        kr = reinterpret_cast<const T*>(a.hh_k) + p * a.hh_sp + (long)j * n;
+        vr = reinterpret_cast<const T*>(a.hh_v) + p * a.hh_sp + (long)j * n;
+      } else {
+        const int j = t - mid1;
+        kr = reinterpret_cast<const T*>(a.ring_k) + p * a.ring_sp + (long)j * n;
+        vr = reinterpret_cast<const T*>(a.ring_v) + p * a.ring_sp + (long)j * n;
+      }
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int d = lane + 32 * i;
+        kv[i] = d < D ? load_f<T>(kr + g * D + d) : 0.f;
+        vv[i] = d < D ? load_f<T>(vr + g * D + d) : 0.f;
+      }
+    } else {
+      is_mid = true;
+      const int j = t - mid0;
+      const float* ct = a.ck + p * a.c_sp + (long)j * ld;
+      for (int c = lane; c < r_k; c += 32) myrow[c] = ct[c];
+      __syncwarp();
+      float kp[NV];
+#pragma unroll
+      for (int i = 0; i < NV; ++i) kp[i] = 0.f;
+      for (int c = 0; c < r_k; ++c) {
+        const float cc = myrow[c];
+        const float* ur = ukT + c * D;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+          const int d = lane + 32 * i;
+          if (d < D) kp[i] = fmaf(ur[d], cc, kp[i]);
+        }
+      }
+      __syncwarp();
+      // RoPE at the column's true position: pairs (d, d + D/2) = (i, i + NV/2)
+      const int pos = a.mid_pos ? a.mid_pos[p * a.mid_sp + j] : a.pos_base + j;
+#pragma unroll
+      for (int i = 0; i < NV / 2; ++i) {
+        const int f = lane + 32 * i;
+        float c = 1.f, s = 0.f;
+        if (f < half) rope_cs(pos, a.inv_freq[f], a.rope_scale, &c, &s);
+        float y1, y2;
+        rope_apply_pair(kp[i], kp[i + NV / 2], c, s, &y1, &y2);
+        kv[i] = y1;
+        kv[i + NV / 2] = y2;
+      }
+#pragma unroll
+      for (int i = 0; i < NV; ++i) vv[i] = 0.f;
+    }
+    // scores for the group's query heads
+    float cvals[NC];
+    if (is_mid) {
+      const float* cvt = a.cv + p * a.c_sp + (long)(t - mid0) * ld;
+#pragma unroll
+      for (int i = 0; i < NC; ++i) {
+        const int c = lane + 32 * i;
+        cvals[i] = c < r_v ? cvt[c] : 0.f;
+      }
+    }
+#pragma unroll
+    for (int qh = 0; qh < kMaxG; ++qh) {
+      if (qh >= G) break;
+      float sdot = 0.f;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int d = lane + 32 * i;
+        if (d < D) sdot = fmaf(qs[qh * D + d], kv[i], sdot);
+      }
+      sdot = warp_sum(sdot) * a.scaling;
+      const float mnew = fmaxf(mrun[qh], sdot);
+      const float corr = expf(mrun[qh] - mnew);
+      const float pw = expf(sdot - mnew);
+      lrun[qh] = lrun[qh] * corr + pw;
+      mrun[qh] = mnew;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) accd[qh][i] = accd[qh][i] * corr + pw * vv[i];
+#pragma unroll
+      for (int i = 0; i < NC; ++i) accc[qh][i] = accc[qh][i] * corr + (is_mid ? pw * cvals[i] : 0.f);
+    }
+  }
+  // combine the 4 warps of the CTA through shared memory
+  __syncthreads();
+  const long rec = part_floats(G, D, ld);
+  float* wrec = red + warp * rec;  // per-warp record
+  for (int qh = 0; qh < G; ++qh) {
+    if (lane == 0) { wrec[qh] = mrun[qh]; wrec[G + qh] = lrun[qh]; }
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int d = lane + 32 * i;
+      if (d < D) wrec[2 * G + qh * D + d] = accd[qh][i];
+    }
+#pragma unroll
+    for (int i = 0; i < NC; ++i) {
+      const int c = lane + 32 * i;
+      if (c < ld) wrec[2 * G + G * D + qh * ld + c] = accc[qh][i];
+    }
+  }
+  __syncthreads();
+  float* out = a.part + ((long)(p * a.H + g) * a.n_chunks + chunk) * a.part_sp_chunk;
+  for (int e = threadIdx.x; e < rec; e += blockDim.x) {
+    // e indexes the record; find its query head
+    int qh;
+    if (e < 2 * G) qh = e % G;
+    else if (e < 2 * G + G * D) qh = (e - 2 * G) / D;
+    else qh = (e - 2 * G - G * D) / ld;
+    float M = -INFINITY;
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, red[w * rec + qh]);
+    float v;
+    if (e < G) {
+      v = M;
+    } else {
+      v = 0.f;
+      for (int w = 0; w < 4; ++w) {
+        const float mw = red[w * rec + qh];
+        const float sc = (mw == -INFINITY) ? 0.f : expf(mw - M);
+        v += sc * red[w * rec + e];
+      }
+    }
+    out[e] = v;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(128) decode_merge_kernel(DecArgs a) {
+  extern __shared__ __align__(16) float msm2[];
+  const int g = blockIdx.x, p = blockIdx.y;
+  const int D = a.D, G = a.G, ld = a.ld;
+  const long rec = part_floats(G, D, ld);
+  const float* parts = a.part + (long)(p * a.H + g) * a.n_chunks * a.part_sp_chunk;
+  float* accc = msm2;        // [G][ld]
+  float* accd = accc + G * ld;  // [G][D]
+  float* ml = accd + G * D;     // [G][2]: M, Lsum
+  for (int qh = threadIdx.x; qh < G; qh += blockDim.x) {
+    float M = -INFINITY;
+    for (int c = 0; c < a.n_chunks; ++c) M = fmaxf(M, parts[c * a.part_sp_chunk + qh]);
+    float Ls = 0.f;
+    for (int c = 0; c < a.n_chunks; ++c) {
+      const float mc = parts[c * a.part_sp_chunk + qh];
+      if (mc != -INFINITY) Ls += expf(mc - M) * parts[c * a.part_sp_chunk + G + qh];
+    }
+    ml[2 * qh] = M;
+    ml[2 * qh + 1] = Ls;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < G * (D + ld); e += blockDim.x) {
+    int qh; long off;
+    if (e < G * D) { qh = e / D; off = 2 * G + e; }
+    else { qh = (e - G * D) / ld; off = 2 * G + G * D + (e - G * D); }
+    const float M = ml[2 * qh];
+    float v = 0.f;
+    for (int c = 0; c < a.n_chunks; ++c) {
+      const float mc = parts[c * a.part_sp_chunk + qh];
+      if (mc != -INFINITY) v += expf(mc - M) * parts[c * a.part_sp_chunk + off];
+    }
+    if (e < G * D) accd[e] = v;
+    else accc[e - G * D] = v;
+  }
+  __syncthreads();
+  const float* Uv = a.uv + p * a.u_sp;
+  const int r_v = a.rv[p];
+  T* out = reinterpret_cast<T*>(a.out) + (long)p * a.Hq * D;
+  for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
+    const int qh = e / D, d = e % D;
+    float v = accd[e];
+    const float* ur = Uv + (long)(g * D + d) * ld;
+    for (int c = 0; c < r_v; ++c) v = fmaf(ur[c], accc[qh * ld + c], v);
+    store_f<T>(out + (long)(g * G + qh) * D + d, v / ml[2 * qh + 1]);
+  }
+}
+
+}  // namespace kvd
+
+namespace kvd_host {
+using namespace kvd;
+
+static int dec_chunks(int L) { return (L + kChunk - 1) / kChunk; }
+
+size_t decode_ws_bytes(const kvd_config& c, int count, int num_q_heads) {
+  const int G = num_q_heads / c.num_heads;
+  const int L_max = c.n_sink + c.hh_budget + c.w_cap + c.ring_cap;
+  const long rec = part_floats(G, c.head_dim, c.rank);
+  return (size_t)count * c.num_heads * dec_chunks(L_max) * rec * 4 + 256;
+}
+
+template <typename T>
+int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_counters& k, int p0,
+                           int count, const void* q, int Hq, float scaling, void* out, char* ws,
+                           size_t ws_bytes, cudaStream_t s) {
+  DecArgs a;
+  const int n = c.num_heads * c.head_dim;
+  a.H = c.num_heads; a.D = c.head_dim; a.G = Hq / c.num_heads; a.ld = c.rank; a.Hq = Hq;
+  if (a.G > kMaxG || c.head_dim > 32 * kMaxNV || c.rank > 32 * kMaxNC) {
+    set_error("factored decode: unsupported shape (G=%d D=%d r=%d)", a.G, c.head_dim, c.rank);
+    return KVD_ERR_ARG;
+  }
+  a.sink_len = k.sink_len; a.hh_len = k.hh_len; a.W = k.w_len; a.ring_len = k.ring_len;
+  a.L = a.sink_len + a.hh_len + a.W + a.ring_len;
+  if (a.L <= 0) { set_error("factored decode on an empty cache"); return KVD_ERR_ARG; }
+  const long sink_sp = (long)c.n_sink * n, hh_sp = (long)c.hh_budget * n, ring_sp = (long)c.ring_cap * n;
+  const size_t es = sizeof(T);
+  a.sink_k = (const char*)b.sink_k + es * p0 * sink_sp; a.sink_v = (const char*)b.sink_v + es * p0 * sink_sp; a.sink_sp = sink_sp;
+  a.hh_k = (const char*)b.hh_k[k.hh_sel] + es * p0 * hh_sp; a.hh_v = (const char*)b.hh_v[k.hh_sel] + es * p0 * hh_sp; a.hh_sp = hh_sp;
+  a.ring_k = (const char*)b.ring_k + es * (p0 * ring_sp + (long)k.ring_head * n);
+  a.ring_v = (const char*)b.ring_v + es * (p0 * ring_sp + (long)k.ring_head * n);
+  a.ring_sp = ring_sp;
+  a.u_sp = (long)n * c.rank;
+  a.uk = b.u_k[k.u_sel] + p0 * a.u_sp; a.uv = b.u_v[k.u_sel] + p0 * a.u_sp;
+  a.rk = b.r_k + p0; a.rv = b.r_v + p0;
+  a.c_sp = (long)c.w_cap * c.rank;
+  a.ck = b.c_k + p0 * a.c_sp; a.cv = b.c_v + p0 * a.c_sp;
+  const bool track = c.retention != KVD_RETENTION_FIFO;
+  a.mid_pos = track ? b.mid_pos + (long)p0 * c.w_cap : nullptr; a.mid_sp = c.w_cap;
+  a.pos_base = (int)(k.cumulative_length - k.ring_len - (k.hh_len + k.w_len));
+  a.inv_freq = c.inv_freq; a.rope_scale = c.rope_scaling;
+  a.q = q; a.out = out; a.scaling = scaling;
+  a.n_chunks = dec_chunks(a.L);
+  a.part_sp_chunk = part_floats(a.G, a.D, a.ld);
+  const size_t need = (size_t)count * a.H * a.n_chunks * a.part_sp_chunk * 4;
+  if (need > ws_bytes) { set_error("factored decode: workspace too small"); return KVD_ERR_WORKSPACE; }
+  a.part = (float*)ws;
+  const int smem = 4 * (a.G * a.D + a.ld * a.D + 4 * a.ld + 4 * (int)a.part_sp_chunk);
+  dim3 grid(a.n_chunks, a.H, count);
+  const int nv = (a.D + 31) / 32, nc = (a.ld + 31) / 32;
+#define KVD_DEC(NV, NC)                                                                         \
+  {                                                                                             \
+    static bool attr = false;                                                                   \
+    if (!attr) {                                                                                \
+      cudaFuncSetAttribute(decode_split_kernel<T, NV, NC>,                                      \
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);            \
+      attr = true;                                                                              \
+    }                                                                                           \
+    decode_split_kernel<T, NV, NC><<<grid, kDecThreads, smem, s>>>(a);                          \
+  }
+  if (nv <= 2 && nc <= 1) KVD_DEC(2, 1)
+  else if (nv <= 2 && nc <= 2) KVD_DEC(2, 2)
+  else if (nv <= 2 && nc <= 4) KVD_DEC(2, 4)
+  else if (nv <= 2) KVD_DEC(2, 6)
+  else if (nc <= 1) KVD_DEC(4, 1)
+  else if (nc <= 2) KVD_DEC(4, 2)
+  else if (nc <= 4) KVD_DEC(4, 4)
+  else KVD_DEC(4, 6)
+#undef KVD_DEC
+  int rc = check_launch("decode_split_kernel");
+  if (rc) return rc;
+  const int msmem = 4 * (a.G * a.ld + a.G * a.D + 2 * a.G);
+  decode_merge_kernel<T><<<dim3(a.H, count), 128, msmem, s>>>(a);
+  return check_launch("decode_merge_kernel");
+}
+
+template int launch_factored_decode<float>(const kvd_config&, const kvd_buffers&, const kvd_counters&, int, int,
+                                           const void*, int, float, void*, char*, size_t, cudaStream_t);
+template int launch_factored_decode<__nv_bfloat16>(const kvd_config&, const kvd_buffers&, const kvd_counters&, int,
+                                                   int, const void*, int, float, void*, char*, size_t,
+                                                   cudaStream_t);
+
+}  // namespace kvd_host

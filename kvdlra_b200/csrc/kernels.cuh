@@ -1,0 +1,104 @@
+// Kernel argument structs and host launcher declarations shared by the
+// translation units of the library.
+#pragma once
+
+#include "cta_linalg.cuh"
+
+namespace kvd {
+
+struct BugStepArgs {
+  int n, b, rank_cap, ld;
+  const float* u; float* u_out; long u_sp;   // [P][n][ld]
+  float* sigma; long sig_sp;                 // [P][ld]
+  int* r;                                     // [P]
+  const float* x; long x_sp;                  // [P][b][n]
+  float* rot; long rot_sp;                    // [P][ld][ld]  rot[c*ld + k]
+  int* dims;                                  // [P][4]  r_old, keep, m, sweeps
+  float* coords; long coords_sp; int coords_ld;  // coords[p*sp + j*ld + c]
+  int has_theta; float theta;
+  int* status;
+  char* ws; long ws_sp;                       // per-problem workspace bytes
+};
+struct BugStepBatch { BugStepArgs s[2]; };
+
+struct CarryArgs {
+  float* c; long c_sp; int ld;     // [P][w_cap][ld]
+  const float* rot; long rot_sp;   // [P][ld][ld]
+  const int* dims;                 // [P][4]
+};
+struct CarryBatch { CarryArgs s[2]; int W; };
+
+// Candidate pool of one problem: j < hh_len comes from the exact tier, the
+// rest from `grad` (token-major rows, already offset to the first graduating
+// token) at positions grad_start + (j - hh_len).
+template <typename T>
+struct CandSrc {
+  const T* hh_k; const T* hh_v; const int* hh_pos; long hh_sp; long hh_pos_sp;
+  const T* g_k; const T* g_v; long g_sp;
+  int hh_len, grad_start, n;
+  KVD_DEVICE const T* krow(int p, int j) const {
+    return j < hh_len ? hh_k + p * hh_sp + (long)j * n : g_k + p * g_sp + (long)(j - hh_len) * n;
+  }
+  KVD_DEVICE const T* vrow(int p, int j) const {
+    return j < hh_len ? hh_v + p * hh_sp + (long)j * n : g_v + p * g_sp + (long)(j - hh_len) * n;
+  }
+  KVD_DEVICE int pos(int p, int j) const {
+    return j < hh_len ? hh_pos[p * hh_pos_sp + j] : grad_start + (j - hh_len);
+  }
+};
+
+struct RopeArgs {
+  const float* inv_freq;
+  float scale;      // attention_scaling
+  float scale_sq;   // scale * scale (the inverse divides by it)
+};
+
+struct SelectOut {
+  void* hh_k; void* hh_v; int* hh_pos; long hh_sp; long hh_pos_sp;  // destination tier buffer
+  float* xk; float* xv; long x_sp;        // demoted block [P][dmax][n]
+  int* mid_pos; float* mid_surprise; long mid_sp; int w_off;  // written at [w_off + slot]
+  int* dem_count;                          // [P] demoted count (diagnostic)
+};
+
+}  // namespace kvd
+
+namespace kvd_host {
+using kvd::BugStepBatch; using kvd::CarryBatch; using kvd::CandSrc; using kvd::RopeArgs; using kvd::SelectOut;
+long bug_step_ws_per_problem(int n, int b, int ld);
+int launch_bug_step(const BugStepBatch& batch, int n_problems, int n_streams, cudaStream_t stream);
+int launch_carry(const CarryBatch& batch, int n_problems, int n_streams, int ld, cudaStream_t stream);
+int launch_surprise_f32(int nb, int n, int m, int ld, const float* u, long u_sp, const int* r,
+                        const float* x, long x_sp, float* out, long out_sp, cudaStream_t stream);
+int launch_evict(int P, int W, int f_over, int retention, float* c_k, float* c_v, long c_sp, int ld,
+                 const int* rk, const int* rv, int* mid_pos, float* mid_sur, long mid_sp,
+                 int* keep_ws, long kw_sp, cudaStream_t stream);
+template <typename T>
+int launch_slash_score(const CandSrc<T>& src, int P, int m, int H, int D, RopeArgs rope,
+                       const float* u, long u_sp, int ld, const int* rr, float* scores, long sc_sp,
+                       cudaStream_t stream);
+template <typename T>
+int launch_slash_select(const CandSrc<T>& src, int P, int m, int keep_n, int H, int D,
+                        RopeArgs rope, const float* scores, long sc_sp, int hh_neighbor,
+                        const SelectOut& out, cudaStream_t stream);
+template <typename T>
+int launch_gather_block(const T* g_k, const T* g_v, long g_sp, int P, int b, int H, int D,
+                        int start, RopeArgs rope, float* xk, float* xv, long x_sp, int* mid_pos,
+                        long mid_sp, int w_off, cudaStream_t stream);
+template <typename T>
+int launch_hf_to_rows(const kvd_hf_view& v, int P, int H, int D, T* dst, long dst_sp, int slot0,
+                      cudaStream_t s);
+template <typename T>
+int launch_rows_copy(const T* src, long src_sp, T* dst, long dst_sp, int count, int n, int P,
+                     cudaStream_t s);
+template <typename T>
+int launch_ring_compact(T* ring, long sp, int head, int len, int n, int P, cudaStream_t s);
+template <typename T>
+int launch_peek(const kvd_config& c, const kvd_buffers& b, const kvd_counters& k, int p0, int count,
+                const kvd_hf_view& ok_, const kvd_hf_view& ov_, const kvd_hf_view& tk,
+                const kvd_hf_view& tv, cudaStream_t s);
+size_t decode_ws_bytes(const kvd_config& c, int count, int num_q_heads);
+template <typename T>
+int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_counters& k, int p0,
+                           int count, const void* q, int Hq, float scaling, void* out, char* ws,
+                           size_t ws_bytes, cudaStream_t s);
+}  // namespace kvd_host

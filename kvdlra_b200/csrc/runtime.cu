@@ -1,0 +1,452 @@
+// Host runtime of the streaming compressed-KV cache (C ABI).
+//
+// Owns the absorb schedule of one cache group and launches the kernels of one
+// absorb step back to back on the caller's stream -- no host synchronisation
+// inside a step.  The schedule mirrors the reference exactly:
+//   consolidate                 bug_cache.py:1425-1429
+//   _absorb_block_into_stream   bug_cache.py:725-750
+//   _absorb_block_slash         bug_cache.py:752-825
+//   _absorb_columns             bug_cache.py:827-904
+//   _enforce_budgets            bug_cache.py:1010-1067
+//   _prefill                    bug_cache.py:1431-1481
+// Every lengths decision (ring, exact tier, coordinate count) depends only on
+// token counts and so is taken here on the host; the data-dependent basis
+// rank lives on the device (r_k/r_v) and is read by the kernels.
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <cstdint>
+
+#include <type_traits>
+
+#include "kernels.cuh"
+
+
+namespace kvd_host {
+using namespace kvd;
+
+static thread_local char g_err[1024] = "";
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+}
+
+int check_launch(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    set_error("%s: %s", what, cudaGetErrorString(e));
+    return KVD_ERR_CUDA;
+  }
+  return KVD_OK;
+}
+
+// ------------------------------------------------------------ workspace
+
+struct Ws {
+  float* scores; long sc_sp;     // [P][hh_budget + max_block]
+  float* xk; float* xv; long x_sp;  // [P][max_block][n]
+  float* rot[2]; long rot_sp;    // [P][ld][ld]
+  int* dims[2];                  // [P][4]
+  int* dem;                      // [P]
+  int* keep; long keep_sp;       // [P][w_cap]
+  char* step[2]; long step_sp;   // per problem
+  size_t total;
+};
+
+static inline size_t a256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+static Ws plan_ws(const kvd_config& c, char* base) {
+  Ws w{};
+  const int P = c.n_problems, n = c.num_heads * c.head_dim, ld = c.rank, mb = c.max_block;
+  size_t o = 0;
+  auto take = [&](size_t bytes) { char* p = base ? base + o : nullptr; o += a256(bytes); return p; };
+  w.sc_sp = c.hh_budget + mb;
+  w.scores = (float*)take(4ul * P * w.sc_sp);
+  w.x_sp = (long)mb * n;
+  w.xk = (float*)take(4ul * P * w.x_sp);
+  w.xv = (float*)take(4ul * P * w.x_sp);
+  w.rot_sp = (long)ld * ld;
+  w.rot[0] = (float*)take(4ul * P * w.rot_sp);
+  w.rot[1] = (float*)take(4ul * P * w.rot_sp);
+  w.dims[0] = (int*)take(16ul * P);
+  w.dims[1] = (int*)take(16ul * P);
+  w.dem = (int*)take(4ul * P);
+  w.keep_sp = c.w_cap;
+  w.keep = (int*)take(4ul * P * w.keep_sp);
+  w.step_sp = bug_step_ws_per_problem(n, mb, ld);
+  w.step[0] = take((size_t)P * w.step_sp);
+  w.step[1] = take((size_t)P * w.step_sp);
+  w.total = o + 256;
+  return w;
+}
+
+static int validate(const kvd_config* c) {
+  if (!c) { set_error("null config"); return KVD_ERR_ARG; }
+  if (c->n_problems < 1 || c->num_heads < 1 || c->head_dim < 2 || (c->head_dim & 1) ||
+      c->rank < 1 || c->recent_window < 1 || c->absorb_block < 1 || c->n_sink < 0 ||
+      c->prefill_block_size < 1 || c->hh_budget < 0 || c->ring_cap < 1 || c->w_cap < 1 ||
+      c->max_block < c->absorb_block || c->max_block < c->prefill_block_size) {
+    set_error("invalid kvd_config");
+    return KVD_ERR_ARG;
+  }
+  if (c->dtype != KVD_DTYPE_F32 && c->dtype != KVD_DTYPE_BF16) {
+    set_error("unsupported dtype %d", c->dtype);
+    return KVD_ERR_DTYPE;
+  }
+  if (c->rank > 192) { set_error("rank %d > 192 is not supported", c->rank); return KVD_ERR_ARG; }
+  if (c->w_cap < c->coord_budget + c->max_block && c->coord_budget < (1 << 30)) {
+    // allowed: the host grows w_cap before it is needed; checked per step
+  }
+  return KVD_OK;
+}
+
+// ------------------------------------------------------------ one group
+
+template <typename T>
+struct Group {
+  const kvd_config& c;
+  const kvd_buffers& b;
+  kvd_counters& k;
+  Ws w;
+  cudaStream_t s;
+  int n, P, ld;
+  long row_sp_ring, row_sp_hh, u_sp, c_sp;
+  RopeArgs rope;
+
+  Group(const kvd_config& c_, const kvd_buffers& b_, kvd_counters& k_, char* ws, cudaStream_t s_)
+      : c(c_), b(b_), k(k_), w(plan_ws(c_, ws)), s(s_) {
+    n = c.num_heads * c.head_dim;
+    P = c.n_problems;
+    ld = c.rank;
+    row_sp_ring = (long)c.ring_cap * n;
+    row_sp_hh = (long)c.hh_budget * n;
+    u_sp = (long)n * ld;
+    c_sp = (long)c.w_cap * ld;
+    rope.inv_freq = c.inv_freq;
+    rope.scale = c.rope_scaling;
+    rope.scale_sq = c.rope_scaling * c.rope_scaling;
+  }
+
+  bool lowrank() const { return c.rank >= 1 && c.coord_budget >= 1; }
+  bool hh_enabled() const { return c.hh_budget >= 1 && lowrank(); }
+  bool track_surprise() const { return lowrank() && c.retention == KVD_RETENTION_LOWRANK_SURPRISE; }
+
+  // BUG step on the demoted / graduating block held in w.xk / w.xv (d columns,
+  // positions and surprise already written at coordinate slots [w_len, w_len+d)).
+  int absorb_columns(int d) {
+    if (d <= 0) return KVD_OK;
+    if (k.w_len + d > c.w_cap) {
+      set_error("coordinate capacity %d too small (need %d)", c.w_cap, k.w_len + d);
+      return KVD_ERR_ARG;
+    }
+    BugStepBatch bb;
+    for (int sidx = 0; sidx < 2; ++sidx) {
+      BugStepArgs& a = bb.s[sidx];
+      a.n = n; a.b = d; a.rank_cap = c.rank; a.ld = ld;
+      a.u = sidx == 0 ? b.u_k[k.u_sel] : b.u_v[k.u_sel];
+      a.u_out = sidx == 0 ? b.u_k[k.u_sel ^ 1] : b.u_v[k.u_sel ^ 1];
+      a.u_sp = u_sp;
+      a.sigma = sidx == 0 ? b.sig_k : b.sig_v; a.sig_sp = ld;
+      a.r = sidx == 0 ? b.r_k : b.r_v;
+      a.x = sidx == 0 ? w.xk : w.xv; a.x_sp = w.x_sp;
+      a.rot = w.rot[sidx]; a.rot_sp = w.rot_sp;
+      a.dims = w.dims[sidx];
+      a.coords = (sidx == 0 ? b.c_k : b.c_v) + (long)k.w_len * ld;
+      a.coords_sp = c_sp; a.coords_ld = ld;
+      a.has_theta = c.has_theta; a.theta = c.theta;
+      a.status = b.status;
+      a.ws = w.step[sidx]; a.ws_sp = w.step_sp;
+    }
+    int rc = launch_bug_step(bb, P, 2, s);
+    if (rc) return rc;
+    if (k.seeded && k.w_len > 0) {
+      CarryBatch cb;
+      for (int sidx = 0; sidx < 2; ++sidx) {
+        CarryArgs& a = cb.s[sidx];
+        a.c = sidx == 0 ? b.c_k : b.c_v; a.c_sp = c_sp; a.ld = ld;
+        a.rot = w.rot[sidx]; a.rot_sp = w.rot_sp; a.dims = w.dims[sidx];
+      }
+      cb.W = k.w_len;
+      if ((rc = launch_carry(cb, P, 2, ld, s))) return rc;
+    }
+    k.u_sel ^= 1;
+    k.seeded = 1;
+    k.w_len += d;
+    k.n_absorbs += 1;
+    return enforce_budgets();
+  }
+
+  int enforce_budgets() {
+    const int f_over = k.w_len - c.coord_budget;
+    if (f_over <= 0) return KVD_OK;
+    int rc = launch_evict(P, k.w_len, f_over, c.retention, b.c_k, b.c_v, c_sp, ld, b.r_k, b.r_v,
+                          b.mid_pos, track_surprise() ? b.mid_surprise : nullptr, c.w_cap, w.keep,
+                          w.keep_sp, s);
+    if (rc) return rc;
+    k.w_len -= f_over;
+    return KVD_OK;
+  }
+
+  // SLASH on a graduating block of `gb` tokens at ring slot `gslot`, true
+  // positions grad_start.. (bug_cache.py:752-825).
+  int absorb_slash(int gslot, int gb, int grad_start) {
+    const int m = k.hh_len + gb;
+    const int keep_n = m < c.hh_budget ? m : c.hh_budget;
+    const int d = m - keep_n;
+    if (gb > c.max_block) { set_error("graduating block %d > max_block", gb); return KVD_ERR_ARG; }
+    CandSrc<T> src;
+    src.hh_k = (const T*)b.hh_k[k.hh_sel]; src.hh_v = (const T*)b.hh_v[k.hh_sel];
+    src.hh_pos = b.hh_pos[k.hh_sel]; src.hh_sp = row_sp_hh; src.hh_pos_sp = c.hh_budget;
+    src.g_k = (const T*)b.ring_k + (long)gslot * n; src.g_v = (const T*)b.ring_v + (long)gslot * n;
+    src.g_sp = row_sp_ring;
+    src.hh_len = k.hh_len; src.grad_start = grad_start; src.n = n;
+    int rc = launch_slash_score<T>(src, P, m, c.num_heads, c.head_dim, rope, b.u_k[k.u_sel], u_sp,
+                                   ld, b.r_k, w.scores, w.sc_sp, s);
+    if (rc) return rc;
+    if (d > 0 && k.w_len + d > c.w_cap) {
+      set_error("coordinate capacity %d too small (need %d)", c.w_cap, k.w_len + d);
+      return KVD_ERR_ARG;
+    }
+    SelectOut so;
+    so.hh_k = b.hh_k[k.hh_sel ^ 1]; so.hh_v = b.hh_v[k.hh_sel ^ 1]; so.hh_pos = b.hh_pos[k.hh_sel ^ 1];
+    so.hh_sp = row_sp_hh; so.hh_pos_sp = c.hh_budget;
+    so.xk = w.xk; so.xv = w.xv; so.x_sp = w.x_sp;
+    so.mid_pos = b.mid_pos; so.mid_surprise = track_surprise() ? b.mid_surprise : nullptr;
+    so.mid_sp = c.w_cap; so.w_off = k.w_len; so.dem_count = w.dem;
+    rc = launch_slash_select<T>(src, P, m, keep_n, c.num_heads, c.head_dim, rope, w.scores, w.sc_sp,
+                                c.hh_neighbor, so, s);
+    if (rc) return rc;
+    k.hh_sel ^= 1;
+    k.hh_len = keep_n;
+    return absorb_columns(d);
+  }
+
+  // Plain absorb of `gb` ring tokens at slot `gslot`, positions start.. .
+  int absorb_plain(int gslot, int gb, int start) {
+    if (k.w_len + gb > c.w_cap) {
+      set_error("coordinate capacity %d too small (need %d)", c.w_cap, k.w_len + gb);
+      return KVD_ERR_ARG;
+    }
+    const T* gk = (const T*)b.ring_k + (long)gslot * n;
+    const T* gv = (const T*)b.ring_v + (long)gslot * n;
+    int rc = launch_gather_block<T>(gk, gv, row_sp_ring, P, gb, c.num_heads, c.head_dim, start, rope,
+                                    w.xk, w.xv, w.x_sp, b.mid_pos, c.w_cap, k.w_len, s);
+    if (rc) return rc;
+    if (track_surprise()) {
+      rc = launch_surprise_f32(P, n, gb, ld, b.u_k[k.u_sel], u_sp, b.r_k, w.xk, w.x_sp,
+                               b.mid_surprise + k.w_len, c.w_cap, s);
+      if (rc) return rc;
+    }
+    return absorb_columns(gb);
+  }
+
+  int absorb_block_into_stream(int m) {
+    const int gslot = k.ring_head;
+    k.ring_head += m;
+    k.ring_len -= m;
+    if (!lowrank()) return KVD_OK;
+    const int grad_start = (int)(k.cumulative_length - k.ring_len - m);
+    if (hh_enabled()) return absorb_slash(gslot, m, grad_start);
+    return absorb_plain(gslot, m, grad_start);
+  }
+
+  int consolidate() {
+    while (k.ring_len >= c.recent_window + c.absorb_block) {
+      const int rc = absorb_block_into_stream(c.absorb_block);
+      if (rc) return rc;
+    }
+    return KVD_OK;
+  }
+
+  int ensure_ring_room(int q) {
+    if (k.ring_head + k.ring_len + q <= c.ring_cap) return KVD_OK;
+    if (k.ring_len + q > c.ring_cap) {
+      set_error("ring capacity %d too small for %d + %d tokens", c.ring_cap, k.ring_len, q);
+      return KVD_ERR_ARG;
+    }
+    int rc = launch_ring_compact<T>((T*)b.ring_k, row_sp_ring, k.ring_head, k.ring_len, n, P, s);
+    if (rc) return rc;
+    rc = launch_ring_compact<T>((T*)b.ring_v, row_sp_ring, k.ring_head, k.ring_len, n, P, s);
+    if (rc) return rc;
+    k.ring_head = 0;
+    return KVD_OK;
+  }
+
+  int append(const kvd_hf_view& kv, const kvd_hf_view& vv) {
+    const int q = kv.tokens;
+    int rc = ensure_ring_room(q);
+    if (rc) return rc;
+    const int slot0 = k.ring_head + k.ring_len;
+    if ((rc = launch_hf_to_rows<T>(kv, P, c.num_heads, c.head_dim, (T*)b.ring_k, row_sp_ring, slot0, s))) return rc;
+    if ((rc = launch_hf_to_rows<T>(vv, P, c.num_heads, c.head_dim, (T*)b.ring_v, row_sp_ring, slot0, s))) return rc;
+    k.ring_len += q;
+    k.cumulative_length += q;
+    return KVD_OK;
+  }
+
+  int prefill(const kvd_hf_view& kv, const kvd_hf_view& vv) {
+    const int t = kv.tokens;
+    if (t > c.ring_cap) {
+      set_error("prefill of %d tokens exceeds ring capacity %d", t, c.ring_cap);
+      return KVD_ERR_ARG;
+    }
+    const int n_sink = t < c.n_sink ? t : c.n_sink;
+    const int recent = (t - n_sink) < c.recent_window ? (t - n_sink) : c.recent_window;
+    const int mid = t - n_sink - recent;
+    int rc;
+    if ((rc = launch_hf_to_rows<T>(kv, P, c.num_heads, c.head_dim, (T*)b.ring_k, row_sp_ring, 0, s))) return rc;
+    if ((rc = launch_hf_to_rows<T>(vv, P, c.num_heads, c.head_dim, (T*)b.ring_v, row_sp_ring, 0, s))) return rc;
+    const long sink_sp = (long)c.n_sink * n;
+    if ((rc = launch_rows_copy<T>((const T*)b.ring_k, row_sp_ring, (T*)b.sink_k, sink_sp, n_sink, n, P, s))) return rc;
+    if ((rc = launch_rows_copy<T>((const T*)b.ring_v, row_sp_ring, (T*)b.sink_v, sink_sp, n_sink, n, P, s))) return rc;
+    k.sink_len = n_sink;
+    // The ring holds the whole input while the middle is absorbed from it.
+    k.ring_head = 0;
+    k.ring_len = t;
+    if (mid > 0 && lowrank()) {
+      const bool seed = c.seed_hh_warmup && hh_enabled() && k.ingest_mode;
+      for (int start = 0; start < mid; start += c.prefill_block_size) {
+        const int stop = (start + c.prefill_block_size) < mid ? start + c.prefill_block_size : mid;
+        const int slot = n_sink + start;
+        rc = seed ? absorb_slash(slot, stop - start, slot) : absorb_plain(slot, stop - start, slot);
+        if (rc) return rc;
+      }
+    }
+    k.ring_head = n_sink + mid;
+    k.ring_len = recent;
+    k.cumulative_length = t;
+    return KVD_OK;
+  }
+};
+
+template <typename F>
+static int dispatch(const kvd_config* c, F&& f) {
+  if (c->dtype == KVD_DTYPE_F32) return f((float*)nullptr);
+  return f((__nv_bfloat16*)nullptr);
+}
+
+}  // namespace kvd_host
+
+using namespace kvd_host;
+
+extern "C" const char* kvd_last_error(void) { return g_err; }
+extern "C" int kvd_version(void) { return 1; }
+
+extern "C" size_t kvd_workspace_bytes(const kvd_config* cfg) {
+  if (validate(cfg)) return 0;
+  const Ws w = plan_ws(*cfg, nullptr);
+  return w.total;
+}
+
+extern "C" int kvd_check_status(const kvd_buffers* buf, kvd_stream_t stream) {
+  int32_t h[4] = {0, 0, 0, 0};
+  cudaError_t e = cudaMemcpyAsync(h, buf->status, sizeof(h), cudaMemcpyDeviceToHost, (cudaStream_t)stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
+  if (e != cudaSuccess) { set_error("status read: %s", cudaGetErrorString(e)); return KVD_ERR_CUDA; }
+  cudaMemsetAsync(buf->status, 0, sizeof(h), (cudaStream_t)stream);
+  if (h[kvd::kStatusTimeout]) { set_error("device wait timed out (code %d)", h[2]); return KVD_ERR_TIMEOUT; }
+  if (h[kvd::kStatusBounds]) { set_error("device bounds check failed (code %d)", h[1]); return KVD_ERR_ARG; }
+  if (h[kvd::kStatusNumeric]) { set_error("Jacobi eigensolver did not converge (flags %d)", h[0]); return KVD_ERR_NUMERIC; }
+  return KVD_OK;
+}
+
+#define KVD_WS_CHECK(cfg, ws, bytes)                                                    \
+  do {                                                                                  \
+    const size_t need_ = kvd_workspace_bytes(cfg);                                      \
+    if ((bytes) < need_ || !(ws)) {                                                     \
+      set_error("workspace %zu bytes < required %zu", (size_t)(bytes), need_);          \
+      return KVD_ERR_WORKSPACE;                                                         \
+    }                                                                                   \
+  } while (0)
+
+static char* align_ws(void* ws) { return (char*)(((uintptr_t)ws + 255) & ~(uintptr_t)255); }
+
+extern "C" int kvd_prefill(const kvd_config* cfg, const kvd_buffers* buf, kvd_counters* ctr,
+                           kvd_hf_view k, kvd_hf_view v, void* workspace, size_t ws_bytes,
+                           kvd_stream_t stream) {
+  int rc = validate(cfg);
+  if (rc) return rc;
+  KVD_WS_CHECK(cfg, workspace, ws_bytes);
+  if (ctr->cumulative_length != 0) { set_error("kvd_prefill on a non-empty cache"); return KVD_ERR_ARG; }
+  return dispatch(cfg, [&](auto* tag) {
+    using T = std::remove_pointer_t<decltype(tag)>;
+    Group<T> g(*cfg, *buf, *ctr, align_ws(workspace), (cudaStream_t)stream);
+    return g.prefill(k, v);
+  });
+}
+
+extern "C" int kvd_append(const kvd_config* cfg, const kvd_buffers* buf, kvd_counters* ctr,
+                          kvd_hf_view k, kvd_hf_view v, kvd_stream_t stream) {
+  int rc = validate(cfg);
+  if (rc) return rc;
+  if (k.tokens != v.tokens || k.tokens < 0) { set_error("kvd_append: K/V token mismatch"); return KVD_ERR_ARG; }
+  return dispatch(cfg, [&](auto* tag) {
+    using T = std::remove_pointer_t<decltype(tag)>;
+    Group<T> g(*cfg, *buf, *ctr, nullptr, (cudaStream_t)stream);
+    return g.append(k, v);
+  });
+}
+
+extern "C" int kvd_consolidate(const kvd_config* cfg, const kvd_buffers* buf, kvd_counters* ctr,
+                               void* workspace, size_t ws_bytes, kvd_stream_t stream) {
+  int rc = validate(cfg);
+  if (rc) return rc;
+  KVD_WS_CHECK(cfg, workspace, ws_bytes);
+  return dispatch(cfg, [&](auto* tag) {
+    using T = std::remove_pointer_t<decltype(tag)>;
+    Group<T> g(*cfg, *buf, *ctr, align_ws(workspace), (cudaStream_t)stream);
+    return g.consolidate();
+  });
+}
+
+extern "C" int kvd_absorb_block(const kvd_config* cfg, const kvd_buffers* buf, kvd_counters* ctr,
+                                void* workspace, size_t ws_bytes, kvd_stream_t stream) {
+  int rc = validate(cfg);
+  if (rc) return rc;
+  KVD_WS_CHECK(cfg, workspace, ws_bytes);
+  if (ctr->ring_len < cfg->recent_window + cfg->absorb_block) return KVD_OK;
+  return dispatch(cfg, [&](auto* tag) {
+    using T = std::remove_pointer_t<decltype(tag)>;
+    Group<T> g(*cfg, *buf, *ctr, align_ws(workspace), (cudaStream_t)stream);
+    return g.absorb_block_into_stream(cfg->absorb_block);
+  });
+}
+
+extern "C" int kvd_peek(const kvd_config* cfg, const kvd_buffers* buf, const kvd_counters* ctr,
+                        int32_t p0, int32_t count, kvd_hf_view out_k, kvd_hf_view out_v,
+                        kvd_hf_view tail_k, kvd_hf_view tail_v, kvd_stream_t stream) {
+  int rc = validate(cfg);
+  if (rc) return rc;
+  if (p0 < 0 || count < 1 || p0 + count > cfg->n_problems) { set_error("kvd_peek: bad problem range"); return KVD_ERR_ARG; }
+  const int L = ctr->sink_len + ctr->hh_len + ctr->w_len + ctr->ring_len + tail_k.tokens;
+  if (out_k.tokens < L) { set_error("kvd_peek: output holds %d < %d tokens", out_k.tokens, L); return KVD_ERR_ARG; }
+  return dispatch(cfg, [&](auto* tag) {
+    using T = std::remove_pointer_t<decltype(tag)>;
+    return launch_peek<T>(*cfg, *buf, *ctr, p0, count, out_k, out_v, tail_k, tail_v, (cudaStream_t)stream);
+  });
+}
+
+extern "C" int kvd_factored_decode(const kvd_config* cfg, const kvd_buffers* buf,
+                                   const kvd_counters* ctr, int32_t p0, int32_t count,
+                                   const void* q, int32_t num_q_heads, float scaling, void* out,
+                                   void* workspace, size_t ws_bytes, kvd_stream_t stream) {
+  int rc = validate(cfg);
+  if (rc) return rc;
+  if (p0 < 0 || count < 1 || p0 + count > cfg->n_problems) { set_error("kvd_factored_decode: bad problem range"); return KVD_ERR_ARG; }
+  if (num_q_heads < cfg->num_heads || num_q_heads % cfg->num_heads) { set_error("kvd_factored_decode: %d query heads do not group over %d KV heads", num_q_heads, cfg->num_heads); return KVD_ERR_ARG; }
+  const size_t need = decode_ws_bytes(*cfg, count, num_q_heads);
+  if (ws_bytes < need || !workspace) { set_error("kvd_factored_decode: workspace %zu < %zu", ws_bytes, need); return KVD_ERR_WORKSPACE; }
+  return dispatch(cfg, [&](auto* tag) {
+    using T = std::remove_pointer_t<decltype(tag)>;
+    return launch_factored_decode<T>(*cfg, *buf, *ctr, p0, count, q, num_q_heads, scaling, out,
+                                     align_ws(workspace), ws_bytes - 256, (cudaStream_t)stream);
+  });
+}
+
+extern "C" size_t kvd_decode_workspace_bytes(const kvd_config* cfg, int32_t count, int32_t num_q_heads) {
+  return decode_ws_bytes(*cfg, count, num_q_heads) + 256;
+}

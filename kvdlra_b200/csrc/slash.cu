@@ -1,0 +1,424 @@
+// Exact-tier ("SLASH") selection kernels (sm_100a).
+//
+//  * slash_score_kernel   -- un-rotate every candidate of the pool [hh | grad]
+//    (post-RoPE, model dtype) and score its low-rank surprise against the
+//    pre-step basis: bug_cache.py:803-804 + 906-921.  fp64 accumulation of the
+//    fp32 projection so the score is as exact as the basis allows.
+//  * slash_select_kernel  -- optional span boost (923-950), stable descending
+//    top-h (810-812), compaction of the kept tokens into the other exact-tier
+//    buffer and gather of the demoted ones (un-rotated K, fp32 V, positions,
+//    graduation surprise) into the BUG-step block: 813-825 + 871-888.
+//  * gather_block_kernel  -- the no-tier absorb path (743-750).
+//  * evict_kernel         -- coordinate-budget eviction (954-1067).
+#include <cfloat>
+
+#include "kernels.cuh"
+
+namespace kvd {
+
+
+constexpr int kScoreTile = 32;   // candidates per CTA
+constexpr int kScoreMaxQ = 24;   // rank <= 8 * 24 = 192
+
+template <typename T>
+__global__ void __launch_bounds__(256) slash_score_kernel(CandSrc<T> src, int m, int H, int D,
+                                                          RopeArgs rope, const float* u, long u_sp,
+                                                          int ld, const int* rr, float* scores,
+                                                          long sc_sp) {
+  extern __shared__ __align__(16) float ssm[];
+  const int p = blockIdx.y;
+  const int j0 = blockIdx.x * kScoreTile;
+  const int half = D / 2;
+  const int r = rr[p];
+  float* cs = ssm;                                   // [tile][half][2]
+  float* kt = cs + kScoreTile * half * 2;            // [tile][D]
+  float* us = kt + kScoreTile * D;                   // [D][r]
+  const int tid = threadIdx.x;
+  const int jl = tid / 8, sub = tid % 8;
+  const int j = j0 + jl;
+  for (int e = tid; e < kScoreTile * half; e += blockDim.x) {
+    const int a = e / half, f = e % half;
+    const int jj = j0 + a;
+    float c = 1.f, s = 0.f;
+    if (jj < m) rope_cs(src.pos(p, jj), rope.inv_freq[f], rope.scale, &c, &s);
+    cs[2 * e] = c;
+    cs[2 * e + 1] = s;
+  }
+  double acc[kScoreMaxQ];
+#pragma unroll
+  for (int q = 0; q < kScoreMaxQ; ++q) acc[q] = 0.0;
+  double kk = 0.0;
+  const float* U = u + p * u_sp;
+  for (int h = 0; h < H; ++h) {
+    __syncthreads();
+    for (int e = tid; e < kScoreTile * half; e += blockDim.x) {
+      const int a = e / half, f = e % half;
+      const int jj = j0 + a;
+      float y1 = 0.f, y2 = 0.f;
+      if (jj < m) {
+        const T* kr = src.krow(p, jj) + h * D;
+        const float x1 = load_f<T>(kr + f), x2 = load_f<T>(kr + f + half);
+        const float c = cs[2 * e], s = cs[2 * e + 1];
+        y1 = (x1 * c + x2 * s) / rope.scale_sq;
+        y2 = (x2 * c - x1 * s) / rope.scale_sq;
+      }
+      kt[a * D + f] = y1;
+      kt[a * D + f + half] = y2;
+    }
+    if (r > 0) {
+      for (int e = tid; e < D * r; e += blockDim.x) {
+        const int d = e / r, k = e % r;
+        us[e] = U[(long)(h * D + d) * ld + k];
+      }
+    }
+    __syncthreads();
+    const float* krow = kt + jl * D;
+    for (int d = sub; d < D; d += 8) kk += (double)krow[d] * (double)krow[d];
+    if (r > 0) {
+      for (int d = 0; d < D; ++d) {
+        const double kv = (double)krow[d];
+        const float* ur = us + d * r;
+#pragma unroll
+        for (int q = 0; q < kScoreMaxQ; ++q) {
+          const int k = sub + 8 * q;
+          if (k < r) acc[q] += (double)ur[k] * kv;
+        }
+      }
+    }
+  }
+  double cc = 0.0;
+#pragma unroll
+  for (int q = 0; q < kScoreMaxQ; ++q) cc += acc[q] * acc[q];
+#pragma unroll
+  for (int o = 4; o > 0; o >>= 1) {
+    cc += __shfl_xor_sync(0xffffffffu, cc, o);
+    kk += __shfl_xor_sync(0xffffffffu, kk, o);
+  }
+  if (sub == 0 && j < m) {
+    float out;
+    if (r == 0) {
+      out = 1.f;
+    } else {
+      const double kn = sqrt(kk);
+      out = (float)(sqrt(fmax(kk - cc, 0.0)) / fmax(kn, 1e-12));
+    }
+    scores[p * sc_sp + j] = out;
+  }
+}
+
+
+template <typename T>
+__global__ void __launch_bounds__(1024) slash_select_kernel(CandSrc<T> src, int m, int keep_n,
+                                                            int H, int D, RopeArgs rope,
+                                                            const float* scores, long sc_sp,
+                                                            int hh_neighbor, SelectOut out) {
+  extern __shared__ __align__(16) float sel_sm[];
+  __shared__ int scan_scratch[32];
+  const int p = blockIdx.x;
+  const int n = H * D, half = D / 2;
+  float* raw = sel_sm;            // [m]
+  float* sel = raw + m;           // [m]
+  int* keep_src = reinterpret_cast<int*>(sel + m);     // [keep_n]
+  int* dem_src = keep_src + keep_n;                     // [m - keep_n]
+  for (int i = threadIdx.x; i < m; i += blockDim.x) raw[i] = scores[p * sc_sp + i];
+  __syncthreads();
+  for (int i = threadIdx.x; i < m; i += blockDim.x) {
+    float v = raw[i];
+    if (hh_neighbor > 0) {
+      const int pi = src.pos(p, i);
+      const int lo = max(0, i - hh_neighbor), hi = min(m - 1, i + hh_neighbor);
+      for (int j = lo; j <= hi; ++j) {
+        if (j == i) continue;
+        const int pj = src.pos(p, j);
+        if (abs(pj - pi) <= hh_neighbor) v = fmaxf(v, raw[j]);
+      }
+    }
+    sel[i] = v;
+  }
+  __syncthreads();
+  int kbase = 0, dbase = 0;
+  for (int i0 = 0; i0 < m; i0 += blockDim.x) {
+    const int i = i0 + threadIdx.x;
+    int kept = 0;
+    if (i < m) {
+      const float v = sel[i];
+      int rank = 0;
+      for (int j = 0; j < m; ++j) {
+        const float w = sel[j];
+        rank += (w > v) || (w == v && j < i);
+      }
+      kept = rank < keep_n;
+    }
+    int tot;
+    const int pre = cta_exclusive_scan(kept, scan_scratch, &tot);
+    if (i < m) {
+      if (kept) keep_src[kbase + pre] = i;
+      else dem_src[dbase + (i - i0 - pre)] = i;
+    }
+    kbase += tot;
+    dbase += min((int)blockDim.x, m - i0) - tot;
+    __syncthreads();
+  }
+  const int d = m - keep_n;
+  // kept tokens -> new exact tier (verbatim, chronological)
+  T* ok = reinterpret_cast<T*>(out.hh_k) + p * out.hh_sp;
+  T* ov = reinterpret_cast<T*>(out.hh_v) + p * out.hh_sp;
+  for (long e = threadIdx.x; e < (long)keep_n * n; e += blockDim.x) {
+    const int slot = (int)(e / n), i = (int)(e % n);
+    const int jsrc = keep_src[slot];
+    ok[e] = src.krow(p, jsrc)[i];
+    ov[e] = src.vrow(p, jsrc)[i];
+  }
+  for (int slot = threadIdx.x; slot < keep_n; slot += blockDim.x)
+    out.hh_pos[p * out.hh_pos_sp + slot] = src.pos(p, keep_src[slot]);
+  // demoted tokens -> un-rotated fp32 block + positions + graduation surprise
+  float* xk = out.xk + p * out.x_sp;
+  float* xv = out.xv + p * out.x_sp;
+  for (long e = threadIdx.x; e < (long)d * (n / 2); e += blockDim.x) {
+    const int slot = (int)(e / (n / 2));
+    const int rem = (int)(e % (n / 2));
+    const int h = rem / half, f = rem % half;
+    const int jsrc = dem_src[slot];
+    const T* kr = src.krow(p, jsrc) + h * D;
+    float c, s;
+    rope_cs(src.pos(p, jsrc), rope.inv_freq[f], rope.scale, &c, &s);
+    const float x1 = load_f<T>(kr + f), x2 = load_f<T>(kr + f + half);
+    xk[(long)slot * n + h * D + f] = (x1 * c + x2 * s) / rope.scale_sq;
+    xk[(long)slot * n + h * D + f + half] = (x2 * c - x1 * s) / rope.scale_sq;
+  }
+  for (long e = threadIdx.x; e < (long)d * n; e += blockDim.x) {
+    const int slot = (int)(e / n), i = (int)(e % n);
+    xv[e] = load_f<T>(src.vrow(p, dem_src[slot]) + i);
+  }
+  for (int slot = threadIdx.x; slot < d; slot += blockDim.x) {
+    const int jsrc = dem_src[slot];
+    out.mid_pos[p * out.mid_sp + out.w_off + slot] = src.pos(p, jsrc);
+    if (out.mid_surprise) out.mid_surprise[p * out.mid_sp + out.w_off + slot] = raw[jsrc];
+  }
+  if (threadIdx.x == 0 && out.dem_count) out.dem_count[p] = d;
+}
+
+// No-tier absorb: rows [0, b) of `g_k`/`g_v` graduate at positions start + j.
+template <typename T>
+__global__ void __launch_bounds__(256) gather_block_kernel(const T* g_k, const T* g_v, long g_sp,
+                                                           int b, int H, int D, int start,
+                                                           RopeArgs rope, float* xk, float* xv,
+                                                           long x_sp, int* mid_pos, long mid_sp,
+                                                           int w_off) {
+  const int p = blockIdx.y;
+  const int n = H * D, half = D / 2;
+  const long tot = (long)b * (n / 2);
+  for (long e = blockIdx.x * (long)blockDim.x + threadIdx.x; e < tot; e += (long)gridDim.x * blockDim.x) {
+    const int slot = (int)(e / (n / 2));
+    const int rem = (int)(e % (n / 2));
+    const int h = rem / half, f = rem % half;
+    const T* kr = g_k + p * g_sp + (long)slot * n + h * D;
+    const T* vr = g_v + p * g_sp + (long)slot * n + h * D;
+    float c, s;
+    rope_cs(start + slot, rope.inv_freq[f], rope.scale, &c, &s);
+    const float x1 = load_f<T>(kr + f), x2 = load_f<T>(kr + f + half);
+    float* xo = xk + p * x_sp + (long)slot * n + h * D;
+    xo[f] = (x1 * c + x2 * s) / rope.scale_sq;
+    xo[f + half] = (x2 * c - x1 * s) / rope.scale_sq;
+    float* vo = xv + p * x_sp + (long)slot * n + h * D;
+    vo[f] = load_f<T>(vr + f);
+    vo[f + half] = load_f<T>(vr + f + half);
+    if (h == 0 && f == 0) mid_pos[p * mid_sp + w_off + slot] = start + slot;
+  }
+}
+
+// Evict `f_over` coordinate columns of each problem (ascending surprise with
+// ties to the older column under lowrank_surprise; the oldest under fifo),
+// then compact C_k, C_v, positions and surprise in place, keeping order.
+__global__ void __launch_bounds__(1024) evict_kernel(int W, int f_over, int retention, float* c_k,
+                                                     float* c_v, long c_sp, int ld, const int* rk,
+                                                     const int* rv, int* mid_pos, float* mid_sur,
+                                                     long mid_sp, int* keep_ws, long kw_sp) {
+  extern __shared__ __align__(16) unsigned int ev_bits[];  // W bits
+  __shared__ float s_bv[32];
+  __shared__ int s_bi[32];
+  __shared__ int scan_scratch[32];
+  const int p = blockIdx.x;
+  const int nwords = (W + 31) / 32;
+  for (int i = threadIdx.x; i < nwords; i += blockDim.x) ev_bits[i] = 0u;
+  __syncthreads();
+  const float* sur = mid_sur + p * mid_sp;
+  if (retention == KVD_RETENTION_FIFO) {
+    for (int i = threadIdx.x; i < f_over; i += blockDim.x) atomicOr(&ev_bits[i / 32], 1u << (i % 32));
+    __syncthreads();
+  } else {
+    const int lane = threadIdx.x % 32, warp = threadIdx.x / 32, nw = blockDim.x / 32;
+    for (int it = 0; it < f_over; ++it) {
+      float bv = FLT_MAX;
+      int bi = 0x7fffffff;
+      for (int i = threadIdx.x; i < W; i += blockDim.x) {
+        if (ev_bits[i / 32] & (1u << (i % 32))) continue;
+        const float v = sur[i];
+        if (v < bv || (v == bv && i < bi)) { bv = v; bi = i; }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov < bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+      }
+      if (lane == 0) { s_bv[warp] = bv; s_bi[warp] = bi; }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        float v = s_bv[0];
+        int ix = s_bi[0];
+        for (int w2 = 1; w2 < nw; ++w2)
+          if (s_bv[w2] < v || (s_bv[w2] == v && s_bi[w2] < ix)) { v = s_bv[w2]; ix = s_bi[w2]; }
+        if (ix < W) ev_bits[ix / 32] |= 1u << (ix % 32);
+      }
+      __syncthreads();
+    }
+  }
+  // kept index list
+  int* keep = keep_ws + p * kw_sp;
+  int base = 0;
+  for (int i0 = 0; i0 < W; i0 += blockDim.x) {
+    const int i = i0 + threadIdx.x;
+    const int kept = (i < W) && !(ev_bits[i / 32] & (1u << (i % 32)));
+    int tot;
+    const int pre = cta_exclusive_scan(kept, scan_scratch, &tot);
+    if (kept) keep[base + pre] = i;
+    base += tot;
+    __syncthreads();
+  }
+  const int Wk = W - f_over;
+  // in-place compaction, chunk by chunk in increasing destination order
+  const int r = max(rk[p], rv[p]);
+  constexpr int kChunk = 4;  // token rows per chunk per pass (x r floats x 2 streams)
+  float* ck = c_k + p * c_sp;
+  float* cv = c_v + p * c_sp;
+  int* pos = mid_pos + p * mid_sp;
+  float* su = mid_sur ? mid_sur + p * mid_sp : nullptr;
+  float* stage = reinterpret_cast<float*>(ev_bits + nwords + 1);  // [kChunk*? ] reuse smem tail
+  const int rows_per = max(1, (int)(blockDim.x / max(r, 1)));
+  const int chunk = min(1024, kChunk * rows_per);
+  for (int d0 = 0; d0 < Wk; d0 += chunk) {
+    const int cnt = min(chunk, Wk - d0);
+    // stage k, v rows, position, surprise
+    for (int e = threadIdx.x; e < cnt * r; e += blockDim.x) {
+      const int t = e / r, c = e % r;
+      const int s = keep[d0 + t];
+      stage[e] = ck[(long)s * ld + c];
+      stage[cnt * r + e] = cv[(long)s * ld + c];
+    }
+    int spos = 0;
+    float ssur = 0.f;
+    const bool own = threadIdx.x < cnt;
+    if (own) {
+      const int s = keep[d0 + threadIdx.x];
+      spos = pos[s];
+      if (su) ssur = su[s];
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < cnt * r; e += blockDim.x) {
+      const int t = e / r, c = e % r;
+      ck[(long)(d0 + t) * ld + c] = stage[e];
+      cv[(long)(d0 + t) * ld + c] = stage[cnt * r + e];
+    }
+    if (own) {
+      pos[d0 + threadIdx.x] = spos;
+      if (su) su[d0 + threadIdx.x] = ssur;
+    }
+    __syncthreads();
+  }
+}
+
+}  // namespace kvd
+
+// ---------------------------------------------------------------- host glue
+namespace kvd_host {
+using namespace kvd;
+
+template <typename T>
+int launch_slash_score(const CandSrc<T>& src, int P, int m, int H, int D, RopeArgs rope,
+                       const float* u, long u_sp, int ld, const int* rr, float* scores, long sc_sp,
+                       cudaStream_t stream) {
+  if (m <= 0) return KVD_OK;
+  if (ld > 8 * kScoreMaxQ) {
+    set_error("slash score: rank %d exceeds %d", ld, 8 * kScoreMaxQ);
+    return KVD_ERR_ARG;
+  }
+  const int half = D / 2;
+  const int smem = 4 * (kScoreTile * half * 2 + kScoreTile * D + D * ld);
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(slash_score_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    attr = true;
+  }
+  dim3 grid((m + kScoreTile - 1) / kScoreTile, P);
+  slash_score_kernel<T><<<grid, 256, smem, stream>>>(src, m, H, D, rope, u, u_sp, ld, rr, scores, sc_sp);
+  return check_launch("slash_score_kernel");
+}
+
+template <typename T>
+int launch_slash_select(const CandSrc<T>& src, int P, int m, int keep_n, int H, int D,
+                        RopeArgs rope, const float* scores, long sc_sp, int hh_neighbor,
+                        const SelectOut& out, cudaStream_t stream) {
+  if (m <= 0) return KVD_OK;
+  const int smem = 4 * (2 * m) + 4 * m;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(slash_select_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    attr = true;
+  }
+  slash_select_kernel<T><<<P, 1024, smem, stream>>>(src, m, keep_n, H, D, rope, scores, sc_sp,
+                                                   hh_neighbor, out);
+  return check_launch("slash_select_kernel");
+}
+
+template <typename T>
+int launch_gather_block(const T* g_k, const T* g_v, long g_sp, int P, int b, int H, int D,
+                        int start, RopeArgs rope, float* xk, float* xv, long x_sp, int* mid_pos,
+                        long mid_sp, int w_off, cudaStream_t stream) {
+  if (b <= 0) return KVD_OK;
+  const long tot = (long)b * H * D / 2;
+  const long nblk = (tot + 255) / 256;
+  const int blocks = (int)(nblk < 1024 ? nblk : 1024);
+  dim3 grid(blocks, P);
+  gather_block_kernel<T><<<grid, 256, 0, stream>>>(g_k, g_v, g_sp, b, H, D, start, rope, xk, xv,
+                                                   x_sp, mid_pos, mid_sp, w_off);
+  return check_launch("gather_block_kernel");
+}
+
+int launch_evict(int P, int W, int f_over, int retention, float* c_k, float* c_v, long c_sp, int ld,
+                 const int* rk, const int* rv, int* mid_pos, float* mid_sur, long mid_sp,
+                 int* keep_ws, long kw_sp, cudaStream_t stream) {
+  if (f_over <= 0) return KVD_OK;
+  const int nwords = (W + 31) / 32;
+  const int rows_per = 1024 / 1;  // upper bound for staging (r >= 1)
+  (void)rows_per;
+  // stage needs cnt * r * 2 floats with cnt*r <= 4*1024 -> 32 KB
+  const int smem = 4 * (nwords + 1) + 4 * 2 * 4 * 1024 + 64;
+  if (smem > 227 * 1024) {
+    set_error("evict: coordinate count %d too large for the in-block bitmap", W);
+    return KVD_ERR_ARG;
+  }
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(evict_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    attr = true;
+  }
+  evict_kernel<<<P, 1024, smem, stream>>>(W, f_over, retention, c_k, c_v, c_sp, ld, rk, rv, mid_pos,
+                                          mid_sur, mid_sp, keep_ws, kw_sp);
+  return check_launch("evict_kernel");
+}
+
+#define KVD_INST(T)                                                                              \
+  template int launch_slash_score<T>(const CandSrc<T>&, int, int, int, int, RopeArgs,            \
+                                     const float*, long, int, const int*, float*, long,          \
+                                     cudaStream_t);                                              \
+  template int launch_slash_select<T>(const CandSrc<T>&, int, int, int, int, int, RopeArgs,      \
+                                      const float*, long, int, const SelectOut&, cudaStream_t);  \
+  template int launch_gather_block<T>(const T*, const T*, long, int, int, int, int, int,         \
+                                      RopeArgs, float*, float*, long, int*, long, int,           \
+                                      cudaStream_t);
+KVD_INST(float)
+KVD_INST(__nv_bfloat16)
+#undef KVD_INST
+
+}  // namespace kvd_host

@@ -1,0 +1,270 @@
+// Verbatim-tier kernels (sm_100a): HF (B,H,T,D) <-> token-major rows, ring
+// compaction, and the dense peek [sinks | exact tier | RoPE(U_k C_k) | ring |
+// tail] that the reference returns from update() (bug_cache.py:1496-1575,
+// 1390-1402).  The reconstructed middle is computed in fp32 and cast to the
+// model dtype, as the reference's _ensure_mid_cache does.
+#include "kernels.cuh"
+
+namespace kvd {
+
+// rows[p][slot0 + t][h*D + d] = src[b][h][t][d]   (p = b)
+template <typename T>
+__global__ void hf_to_rows_kernel(const T* src, long sb, long sh, long st, int H, int D, int q,
+                                  T* dst, long dst_sp, int slot0) {
+  const int p = blockIdx.y;
+  const int n = H * D;
+  const long tot = (long)q * n;
+  for (long e = blockIdx.x * (long)blockDim.x + threadIdx.x; e < tot; e += (long)gridDim.x * blockDim.x) {
+    const int t = (int)(e / n), i = (int)(e % n);
+    const int h = i / D, d = i % D;
+    dst[p * dst_sp + (long)(slot0 + t) * n + i] = src[p * sb + h * sh + (long)t * st + d];
+  }
+}
+
+// dst rows [0, count) <- src rows [0, count) of the same problem (copy).
+template <typename T>
+__global__ void rows_copy_kernel(const T* src, long src_sp, T* dst, long dst_sp, int count, int n) {
+  const int p = blockIdx.y;
+  const long tot = (long)count * n;
+  for (long e = blockIdx.x * (long)blockDim.x + threadIdx.x; e < tot; e += (long)gridDim.x * blockDim.x)
+    dst[p * dst_sp + e] = src[p * src_sp + e];
+}
+
+// In-place move of rows [head, head+len) to [0, len): one CTA per problem,
+// staged through shared memory chunk by chunk (destination < source).
+template <typename T>
+__global__ void __launch_bounds__(1024) ring_compact_kernel(T* ring, long sp, int head, int len, int n) {
+  extern __shared__ __align__(16) unsigned char rsm[];
+  T* stage = reinterpret_cast<T*>(rsm);
+  const int p = blockIdx.x;
+  T* base = ring + p * sp;
+  const int chunk_elems = 8192;
+  const long tot = (long)len * n;
+  for (long c0 = 0; c0 < tot; c0 += chunk_elems) {
+    const int cnt = (int)((tot - c0) < chunk_elems ? (tot - c0) : chunk_elems);
+    for (int e = threadIdx.x; e < cnt; e += blockDim.x) stage[e] = base[(long)head * n + c0 + e];
+    __syncthreads();
+    for (int e = threadIdx.x; e < cnt; e += blockDim.x) base[c0 + e] = stage[e];
+    __syncthreads();
+  }
+}
+
+struct PeekSeg {
+  const void* k; const void* v; long sp;  // token-major rows [p][slot][n]
+  int len;
+};
+
+// Verbatim segments -> HF output rows [l0, l0 + len).
+template <typename T>
+__global__ void rows_to_hf_kernel(const T* k, const T* v, long sp, int len, int H, int D, T* ok,
+                                  T* ov, long ob, long oh, long ot, int l0) {
+  const int p = blockIdx.y;
+  const int n = H * D;
+  const long tot = (long)len * n;
+  for (long e = blockIdx.x * (long)blockDim.x + threadIdx.x; e < tot; e += (long)gridDim.x * blockDim.x) {
+    const int t = (int)(e / n), i = (int)(e % n);
+    const int h = i / D, d = i % D;
+    const long o = p * ob + h * oh + (long)(l0 + t) * ot + d;
+    ok[o] = k[p * sp + e];
+    ov[o] = v[p * sp + e];
+  }
+}
+
+// HF tail (B,H,q,D) -> HF output rows [l0, l0+q).
+template <typename T>
+__global__ void hf_to_hf_kernel(const T* k, const T* v, long sb, long sh, long st, int q, int H,
+                                int D, T* ok, T* ov, long ob, long oh, long ot, int l0) {
+  const int p = blockIdx.y;
+  const long tot = (long)q * H * D;
+  for (long e = blockIdx.x * (long)blockDim.x + threadIdx.x; e < tot; e += (long)gridDim.x * blockDim.x) {
+    const int t = (int)(e / (H * D));
+    const int i = (int)(e % (H * D));
+    const int h = i / D, d = i % D;
+    const long o = p * ob + h * oh + (long)(l0 + t) * ot + d;
+    const long s = p * sb + h * sh + (long)t * st + d;
+    ok[o] = k[s];
+    ov[o] = v[s];
+  }
+}
+
+// Middle reconstruction: K = RoPE(U_k c_t) at pos_t, V = U_v c_v,t for 32
+// coordinate columns per CTA, written to HF rows [l0, l0+W).
+constexpr int kMidTile = 32;
+
+template <typename T>
+__global__ void __launch_bounds__(256) mid_hat_kernel(const float* uk, const float* uv, long u_sp,
+                                                      int ld, const int* rk, const int* rv,
+                                                      const float* ck, const float* cv, long c_sp,
+                                                      const int* mid_pos, long mid_sp,
+                                                      int pos_base, int W, int H, int D,
+                                                      const float* inv_freq, float scale, T* ok,
+                                                      T* ov, long ob, long oh, long ot, int l0) {
+  extern __shared__ __align__(16) float msm[];
+  const int p = blockIdx.y;
+  const int t0 = blockIdx.x * kMidTile;
+  const int cnt = min(kMidTile, W - t0);
+  const int r_k = rk[p], r_v = rv[p];
+  const int half = D / 2;
+  float* ctk = msm;                        // [tile][ld]
+  float* ctv = ctk + kMidTile * ld;        // [tile][ld]
+  float* usk = ctv + kMidTile * ld;        // [D][ld]
+  float* usv = usk + D * ld;               // [D][ld]
+  float* cs = usv + D * ld;                // [tile][half][2]
+  for (int e = threadIdx.x; e < cnt * ld; e += blockDim.x) {
+    const int t = e / ld, c = e % ld;
+    ctk[e] = c < r_k ? ck[p * c_sp + (long)(t0 + t) * ld + c] : 0.f;
+    ctv[e] = c < r_v ? cv[p * c_sp + (long)(t0 + t) * ld + c] : 0.f;
+  }
+  for (int e = threadIdx.x; e < cnt * half; e += blockDim.x) {
+    const int t = e / half, f = e % half;
+    const int pos = mid_pos ? mid_pos[p * mid_sp + t0 + t] : pos_base + t0 + t;
+    float c, s;
+    rope_cs(pos, inv_freq[f], scale, &c, &s);
+    cs[2 * e] = c;
+    cs[2 * e + 1] = s;
+  }
+  const float* Uk = uk + p * u_sp;
+  const float* Uv = uv + p * u_sp;
+  for (int h = 0; h < H; ++h) {
+    __syncthreads();
+    for (int e = threadIdx.x; e < D * ld; e += blockDim.x) {
+      const int d = e / ld, c = e % ld;
+      usk[e] = c < r_k ? Uk[(long)(h * D + d) * ld + c] : 0.f;
+      usv[e] = c < r_v ? Uv[(long)(h * D + d) * ld + c] : 0.f;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < cnt * half; e += blockDim.x) {
+      const int t = e / half, f = e % half;
+      const float* ckt = ctk + t * ld;
+      const float* cvt = ctv + t * ld;
+      const float* u1 = usk + f * ld;
+      const float* u2 = usk + (f + half) * ld;
+      const float* w1 = usv + f * ld;
+      const float* w2 = usv + (f + half) * ld;
+      float k1 = 0.f, k2 = 0.f, v1 = 0.f, v2 = 0.f;
+      for (int c = 0; c < r_k; ++c) { k1 = fmaf(u1[c], ckt[c], k1); k2 = fmaf(u2[c], ckt[c], k2); }
+      for (int c = 0; c < r_v; ++c) { v1 = fmaf(w1[c], cvt[c], v1); v2 = fmaf(w2[c], cvt[c], v2); }
+      float y1, y2;
+      rope_apply_pair(k1, k2, cs[2 * e], cs[2 * e + 1], &y1, &y2);
+      const long o = p * ob + h * oh + (long)(l0 + t0 + t) * ot;
+      store_f<T>(ok + o + f, y1);
+      store_f<T>(ok + o + f + half, y2);
+      store_f<T>(ov + o + f, v1);
+      store_f<T>(ov + o + f + half, v2);
+    }
+  }
+}
+
+}  // namespace kvd
+
+namespace kvd_host {
+using namespace kvd;
+
+static inline int grid_for(long tot) {
+  const long b = (tot + 255) / 256;
+  return (int)(b < 2048 ? b : 2048);
+}
+
+template <typename T>
+int launch_hf_to_rows(const kvd_hf_view& v, int P, int H, int D, T* dst, long dst_sp, int slot0,
+                      cudaStream_t s) {
+  if (v.tokens <= 0 || P <= 0) return KVD_OK;
+  dim3 grid(grid_for((long)v.tokens * H * D), P);
+  hf_to_rows_kernel<T><<<grid, 256, 0, s>>>((const T*)v.ptr, v.stride_b, v.stride_h, v.stride_t, H,
+                                            D, v.tokens, dst, dst_sp, slot0);
+  return check_launch("hf_to_rows_kernel");
+}
+
+template <typename T>
+int launch_rows_copy(const T* src, long src_sp, T* dst, long dst_sp, int count, int n, int P,
+                     cudaStream_t s) {
+  if (count <= 0 || P <= 0) return KVD_OK;
+  dim3 grid(grid_for((long)count * n), P);
+  rows_copy_kernel<T><<<grid, 256, 0, s>>>(src, src_sp, dst, dst_sp, count, n);
+  return check_launch("rows_copy_kernel");
+}
+
+template <typename T>
+int launch_ring_compact(T* ring, long sp, int head, int len, int n, int P, cudaStream_t s) {
+  if (head == 0 || len <= 0 || P <= 0) return KVD_OK;
+  ring_compact_kernel<T><<<P, 1024, 8192 * sizeof(T), s>>>(ring, sp, head, len, n);
+  return check_launch("ring_compact_kernel");
+}
+
+template <typename T>
+int launch_peek(const kvd_config& c, const kvd_buffers& b, const kvd_counters& k, int p0, int count,
+                const kvd_hf_view& ok_, const kvd_hf_view& ov_, const kvd_hf_view& tk,
+                const kvd_hf_view& tv, cudaStream_t s) {
+  const int H = c.num_heads, D = c.head_dim, n = H * D;
+  const long ob = ok_.stride_b, oh = ok_.stride_h, ot = ok_.stride_t;
+  if (ov_.stride_b != ob || ov_.stride_h != oh || ov_.stride_t != ot) {
+    set_error("kvd_peek: K and V outputs must share strides");
+    return KVD_ERR_ARG;
+  }
+  T* okp = (T*)ok_.ptr;
+  T* ovp = (T*)ov_.ptr;
+  int l0 = 0;
+  auto seg = [&](const void* kk, const void* vv, long sp, int len) -> int {
+    if (len <= 0) return KVD_OK;
+    dim3 grid(grid_for((long)len * n), count);
+    rows_to_hf_kernel<T><<<grid, 256, 0, s>>>((const T*)kk + p0 * sp, (const T*)vv + p0 * sp, sp,
+                                              len, H, D, okp, ovp, ob, oh, ot, l0);
+    l0 += len;
+    return check_launch("rows_to_hf_kernel");
+  };
+  int rc;
+  if ((rc = seg(b.sink_k, b.sink_v, (long)c.n_sink * n, k.sink_len))) return rc;
+  if (k.hh_len > 0) {
+    if ((rc = seg(b.hh_k[k.hh_sel], b.hh_v[k.hh_sel], (long)c.hh_budget * n, k.hh_len))) return rc;
+  }
+  if (k.w_len > 0) {
+    const int ld = c.rank;
+    const long u_sp = (long)n * ld, c_sp = (long)c.w_cap * ld;
+    const int track_pos = c.retention != KVD_RETENTION_FIFO;
+    const int mid_len = k.hh_len + k.w_len;
+    const int pos_base = (int)(k.cumulative_length - k.ring_len - mid_len);
+    const int half = D / 2;
+    const int smem = 4 * (2 * kMidTile * ld + 2 * D * ld + kMidTile * half * 2);
+    static bool attr = false;
+    if (!attr) {
+      cudaFuncSetAttribute(mid_hat_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+      attr = true;
+    }
+    dim3 grid((k.w_len + kMidTile - 1) / kMidTile, count);
+    mid_hat_kernel<T><<<grid, 256, smem, s>>>(
+        b.u_k[k.u_sel] + p0 * u_sp, b.u_v[k.u_sel] + p0 * u_sp, u_sp, ld, b.r_k + p0, b.r_v + p0,
+        b.c_k + p0 * c_sp, b.c_v + p0 * c_sp, c_sp,
+        track_pos ? b.mid_pos + (long)p0 * c.w_cap : nullptr, c.w_cap, pos_base, k.w_len, H, D,
+        c.inv_freq, c.rope_scaling, okp, ovp, ob, oh, ot, l0);
+    if ((rc = check_launch("mid_hat_kernel"))) return rc;
+    l0 += k.w_len;
+  }
+  const long ring_sp = (long)c.ring_cap * n;
+  if (k.ring_len > 0) {
+    const T* rk = (const T*)b.ring_k + (long)k.ring_head * n;
+    const T* rv = (const T*)b.ring_v + (long)k.ring_head * n;
+    if ((rc = seg(rk, rv, ring_sp, k.ring_len))) return rc;
+  }
+  if (tk.tokens > 0) {
+    dim3 grid(grid_for((long)tk.tokens * n), count);
+    hf_to_hf_kernel<T><<<grid, 256, 0, s>>>((const T*)tk.ptr, (const T*)tv.ptr, tk.stride_b,
+                                            tk.stride_h, tk.stride_t, tk.tokens, H, D, okp, ovp,
+                                            ob, oh, ot, l0);
+    if ((rc = check_launch("hf_to_hf_kernel"))) return rc;
+  }
+  return KVD_OK;
+}
+
+#define KVD_INST(T)                                                                             \
+  template int launch_hf_to_rows<T>(const kvd_hf_view&, int, int, int, T*, long, int,          \
+                                    cudaStream_t);                                              \
+  template int launch_rows_copy<T>(const T*, long, T*, long, int, int, int, cudaStream_t);      \
+  template int launch_ring_compact<T>(T*, long, int, int, int, int, cudaStream_t);              \
+  template int launch_peek<T>(const kvd_config&, const kvd_buffers&, const kvd_counters&, int,  \
+                              int, const kvd_hf_view&, const kvd_hf_view&, const kvd_hf_view&, \
+                              const kvd_hf_view&, cudaStream_t);
+KVD_INST(float)
+KVD_INST(__nv_bfloat16)
+#undef KVD_INST
+
+}  // namespace kvd_host

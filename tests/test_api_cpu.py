@@ -1,0 +1,80 @@
+"""Host-side API checks that need no GPU: constructor validation (same
+messages as the reference, bug_cache.py:342-494), scope errors, and the
+no-CPU-fallback guarantee."""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from kvdlra_b200 import BugStreamingCache, BugStreamingLayer, RopeAngles
+
+ROPE = RopeAngles(inv_freq=torch.ones(8))
+
+
+def _cache(**kw):
+    return BugStreamingCache(None, num_layers=2, rope=ROPE, **kw)
+
+
+def test_constructor_validation_messages() -> None:
+    with pytest.raises(ValueError, match="recent_window"):
+        _cache(rank=8, coord_budget=16, recent_window=0)
+    with pytest.raises(ValueError, match=">= 0"):
+        _cache(rank=-1, coord_budget=16)
+    with pytest.raises(ValueError, match="absorb_block"):
+        _cache(rank=8, coord_budget=16, absorb_block=0)
+    with pytest.raises(ValueError, match="hh_select must be"):
+        _cache(rank=4, coord_budget=32, hh_budget=4, hh_select="bogus")
+    with pytest.raises(ValueError, match="requires retention='attn'"):
+        _cache(rank=4, coord_budget=32, retention="lowrank_surprise", hh_budget=4, hh_select="attn")
+    with pytest.raises(ValueError, match=r"hh_neighbor.*requires hh_select='surprise'"):
+        _cache(rank=4, coord_budget=32, retention="attn", hh_budget=4, hh_select="attn", hh_neighbor=1)
+    for kw in ({"merge": True}, {"quant_bits": 4, "quant_budget": 16}):
+        with pytest.raises(ValueError, match="fp32 low-rank tail only"):
+            _cache(rank=4, coord_budget=64, recent_window=8, absorb_block=4,
+                   retention="lowrank_surprise", hh_budget=2, hh_select="surprise",
+                   seed_hh_warmup=True, **kw)
+    with pytest.raises(ValueError, match="hh_budget >= 1"):
+        _cache(rank=4, coord_budget=32, hh_retain=False)
+
+
+def test_in_scope_configs_construct() -> None:
+    _cache(rank=4, coord_budget=32, retention="lowrank_surprise", hh_budget=4, hh_select="surprise")
+    _cache(rank=4, coord_budget=32, retention="fifo", hh_budget=4, hh_select="surprise")
+    _cache(rank=0, coord_budget=0)  # sinks + recent window only
+
+
+@pytest.mark.parametrize("kw", [
+    {"retention": "attn"}, {"retention": "energy"}, {"retention": "blend"},
+    {"quant_bits": 4, "quant_budget": 8},
+])
+def test_out_of_scope_variants_raise_not_implemented(kw) -> None:
+    with pytest.raises(NotImplementedError):
+        _cache(rank=4, coord_budget=32, **kw)
+
+
+def test_cpu_tensors_are_rejected_loudly() -> None:
+    layer = BugStreamingLayer(ROPE, rank=4, coord_budget=32)
+    k = torch.zeros(1, 2, 8, 16)
+    with pytest.raises(RuntimeError, match="CUDA devices only"):
+        layer.update(k, k)
+
+
+def test_fresh_layer_lengths_and_masks() -> None:
+    layer = BugStreamingLayer(ROPE, rank=4, coord_budget=32, recent_window=8, absorb_block=4)
+    assert layer.get_seq_length() == 0
+    assert layer.get_mask_sizes(10) == (10, 0)  # prefill returns the full input
+    assert layer.get_max_cache_shape() == -1
+    assert layer.stored_state_numel() == 0
+
+
+def test_mode_context_managers_restore_normal() -> None:
+    cache = _cache(rank=4, coord_budget=32)
+    with cache.ingesting():
+        assert all(ly._mode == "ingest" for ly in cache.layers)
+    assert all(ly._mode == "normal" for ly in cache.layers)
+    with pytest.raises(KeyError):
+        with cache.frozen_scoring():
+            assert all(ly._mode == "score" for ly in cache.layers)
+            raise KeyError("x")
+    assert all(ly._mode == "normal" for ly in cache.layers)

@@ -1,0 +1,171 @@
+"""GPU parity: the CUDA cache against the CPU oracle, lock-step, on the
+golden workloads and the full-size synthetic single-layer stream.
+
+Rules checked (floating point, stated per assertion):
+ (a) exact-tier positions identical after every selection event, except
+     near-ties whose oracle scores are within 1e-5 relative (re-synced);
+ (b) gist reconstruction error within 1e-3 relative of the oracle's;
+ (c) largest principal angle between bases <= 1e-2 rad;
+ (d) attention outputs within 1e-4 relative (fp32) / 2e-2 relative (bf16).
+"""
+
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from golden.make_golden import CASES
+from lockstep import run_ingest, to_mat
+from oracle.bug_oracle import OracleLayer, RopeSpec, default_inv_freq, gqa_attention, principal_angle
+
+from kvdlra_b200 import BugStreamingLayer, RopeAngles
+from kvdlra_b200.synthetic import lowrank_stream
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda")
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def _make(kw: dict, dtype: str = "float32"):
+    D, theta = kw["head_dim"], kw["theta"]
+    inv = default_inv_freq(D, theta)
+    oracle = OracleLayer(RopeSpec(inv), kw["heads"], D, dtype=dtype, **kw["layer_kw"])
+    layer = BugStreamingLayer(RopeAngles(inv_freq=torch.from_numpy(inv), attention_scaling=1.0),
+                              **kw["layer_kw"])
+    return oracle, layer
+
+
+def _rel(a: np.ndarray, b: np.ndarray) -> float:
+    return float(np.abs(a.astype(np.float64) - b).max() / max(np.abs(b).max(), 1e-30))
+
+
+def _gist_err(u: np.ndarray, c: np.ndarray, pos: np.ndarray, ref_htd: np.ndarray) -> float:
+    ref = np.concatenate([ref_htd[h][pos].T for h in range(ref_htd.shape[0])], axis=0).astype(np.float64)
+    rec = u.astype(np.float64) @ c.astype(np.float64)
+    return float(np.linalg.norm(ref - rec) / np.linalg.norm(ref))
+
+
+@pytest.mark.parametrize("case", list(CASES))
+def test_golden_workload_lockstep(case: str) -> None:
+    kw = CASES[case]
+    H, D, t, chunk = kw["heads"], kw["head_dim"], kw["t"], kw["chunk"]
+    dec = kw.get("decode_tokens", 0)
+    s = lowrank_stream(H, D, t + dec, theta=kw["theta"], seed=kw["seed"], **kw["stream_kw"])
+    oracle, layer = _make(kw)
+    stats = run_ingest(layer, oracle, s.k_post[:, :t], s.v[:, :t], chunk, dtype=torch.float32)
+    assert stats.max_angle_k <= 1e-2 and stats.max_angle_v <= 1e-2, stats  # rule (c)
+    g = np.load(GOLDEN / f"{case}.npz")
+    if stats.near_ties == 0 and "final_hh_pos" in g:
+        assert np.array_equal(layer.hh_pos.cpu().numpy(), g["final_hh_pos"])
+    if stats.near_ties == 0 and "final_mid_pos" in g:
+        assert np.array_equal(layer.mid_pos.cpu().numpy(), g["final_mid_pos"])
+    assert layer.stored_state_numel() == oracle.stored_state_numel() == int(g["final_stored_numel"])
+    if layer.u_k is not None and layer.mid_pos is not None:  # rule (b)
+        pos = layer.mid_pos.cpu().numpy()
+        e_gpu = _gist_err(layer.u_k.cpu().numpy(), layer.c_k.cpu().numpy(), pos, s.k_pre)
+        e_ora = _gist_err(oracle.u_k, oracle.c_k, oracle.mid_pos, s.k_pre)
+        assert abs(e_gpu - e_ora) <= 1e-3 * e_ora + 1e-7, (e_gpu, e_ora)
+    # dense peek equals the oracle's peek (fp32 path: reconstruction tolerance)
+    kr, vr = layer._decode_peek()
+    ok_, ov_ = oracle.decode_peek()
+    assert kr.shape[2] == ok_.shape[1]
+    if stats.near_ties == 0:
+        assert _rel(kr[0].permute(0, 2, 1).reshape(H * D, -1).cpu().numpy(), ok_) < 1e-3
+        assert _rel(vr[0].permute(0, 2, 1).reshape(H * D, -1).cpu().numpy(), ov_) < 1e-3
+    # rule (d): factored decode vs dense attention over the oracle's peek
+    if "queries" in g:
+        for q in g["queries"]:
+            out = layer.factored_attention(torch.from_numpy(q)[None].to(DEV))[0].cpu().numpy()
+            ref = gqa_attention(q, oracle.to_hf(ok_), oracle.to_hf(ov_))
+            assert _rel(out, ref) < 1e-4, _rel(out, ref)
+    # decode steps in normal mode: mask sizes and accounting track the oracle
+    for j in range(dec):
+        p = t + j
+        assert layer.get_mask_sizes(1) == oracle.get_mask_sizes(1)
+        kt = torch.from_numpy(np.ascontiguousarray(s.k_post[:, p : p + 1]))[None].to(DEV)
+        vt = torch.from_numpy(np.ascontiguousarray(s.v[:, p : p + 1]))[None].to(DEV)
+        kr, _ = layer.update(kt, vt)
+        ok_, _ = oracle.update(to_mat(s.k_post[:, p : p + 1]), to_mat(s.v[:, p : p + 1]))
+        assert kr.shape[2] == ok_.shape[1]
+        assert layer.stored_state_numel() == oracle.stored_state_numel()
+    layer._group.check_status()
+
+
+def test_full_size_single_layer_stream() -> None:
+    """The synthetic single-layer workload at full size: 8 KV heads x 64,
+    T=4096, chunk 256, r=32, h=256, 4 sinks, ring 128, absorb 16, fp32."""
+    H, D, T = 8, 64, 4096
+    s = lowrank_stream(H, D, T, n_needles=16, seed=0)
+    layer_kw = dict(rank=32, coord_budget=T + 128 + 16, recent_window=128, absorb_block=16,
+                    n_sink=4, retention="lowrank_surprise", hh_budget=256, hh_select="surprise")
+    kw = dict(heads=H, head_dim=D, theta=500000.0, layer_kw=layer_kw)
+    oracle, layer = _make(kw)
+    stats = run_ingest(layer, oracle, s.k_post, s.v, 256, dtype=torch.float32)
+    assert stats.max_angle_k <= 1e-2 and stats.max_angle_v <= 1e-2, stats
+    hh = set(layer.hh_pos.cpu().tolist())
+    assert set(s.needles.tolist()) <= hh  # every needle verbatim in the exact tier
+    assert layer.stored_state_numel() == oracle.stored_state_numel()
+    rng = np.random.default_rng(1)
+    ok_, ov_ = oracle.decode_peek()
+    for _ in range(8):
+        q = rng.standard_normal((32, D)).astype(np.float32)
+        out = layer.factored_attention(torch.from_numpy(q)[None].to(DEV))[0].cpu().numpy()
+        ref = gqa_attention(q, oracle.to_hf(ok_), oracle.to_hf(ov_))
+        tol = 1e-4 if stats.near_ties == 0 else 5e-3
+        assert _rel(out, ref) < tol
+
+
+def test_bf16_stream_lockstep() -> None:
+    """bf16 verbatim tiers (fp32 BUG math), the dtype of the model workloads."""
+    H, D, T = 8, 64, 1536
+    s = lowrank_stream(H, D, T, n_needles=6, seed=4)
+    k = s.k_post.astype(np.float32)
+    layer_kw = dict(rank=32, coord_budget=T + 144, recent_window=128, absorb_block=16, n_sink=4,
+                    retention="lowrank_surprise", hh_budget=128, hh_select="surprise")
+    kw = dict(heads=H, head_dim=D, theta=500000.0, layer_kw=layer_kw)
+    oracle, layer = _make(kw, dtype="bfloat16")
+    stats = run_ingest(layer, oracle, k, s.v, 256, dtype=torch.bfloat16)
+    assert stats.max_angle_k <= 1e-2 and stats.max_angle_v <= 1e-2
+    ok_, ov_ = oracle.decode_peek()
+    rng = np.random.default_rng(2)
+    q = rng.standard_normal((32, D)).astype(np.float32)
+    qb = torch.from_numpy(q).to(DEV, torch.bfloat16)
+    out = layer.factored_attention(qb[None])[0].float().cpu().numpy()
+    ref = gqa_attention(qb.float().cpu().numpy(), oracle.to_hf(ok_), oracle.to_hf(ov_))
+    assert _rel(out, ref) < 2e-2
+
+
+def test_batched_layers_equal_single() -> None:
+    """A cache group of several (layer, sequence) problems gives each problem
+    the same result as running it alone."""
+    from kvdlra_b200 import BugStreamingCache
+
+    H, D, T, L, B = 4, 32, 640, 3, 2
+    inv = torch.from_numpy(default_inv_freq(D, 500000.0))
+    kw = dict(rank=8, coord_budget=T + 80, recent_window=32, absorb_block=16, n_sink=4,
+              retention="lowrank_surprise", hh_budget=24, hh_select="surprise")
+    streams = [[lowrank_stream(H, D, T, signal_rank=6, n_needles=3, seed=10 * l + b) for b in range(B)]
+               for l in range(L)]
+    keys = torch.stack([torch.stack([torch.from_numpy(streams[l][b].k_post) for b in range(B)]) for l in range(L)]).to(DEV)
+    vals = torch.stack([torch.stack([torch.from_numpy(streams[l][b].v) for b in range(B)]) for l in range(L)]).to(DEV)
+    cache = BugStreamingCache(None, num_layers=L, rope=RopeAngles(inv_freq=inv), **kw)
+    for st in range(0, T, 128):
+        cache.ingest_all(keys[:, :, :, st : st + 128].contiguous(), vals[:, :, :, st : st + 128].contiguous(), peek=False)
+    for l in range(L):
+        for b in range(B):
+            single = BugStreamingLayer(RopeAngles(inv_freq=inv), **kw)
+            single._mode = "ingest"
+            for st in range(0, T, 128):
+                single.update(keys[l, b : b + 1, :, st : st + 128], vals[l, b : b + 1, :, st : st + 128])
+                single.consolidate()
+            lay = cache.layers[l]
+            p = l * B + b
+            g = cache._group
+            sel = lay._ctr.hh_sel
+            got = g.t["hh_pos"][sel, p, : lay._hh_len()].cpu()
+            assert torch.equal(got, single.hh_pos.to(torch.int32).cpu())
+            assert principal_angle(g.t["u_k"][lay._ctr.u_sel, p, :, : int(g.t["r_k"][p])].cpu().numpy(),
+                                   single.u_k.cpu().numpy()) < 1e-4
