@@ -1,0 +1,425 @@
+"""Benchmark: BUG ingest tokens/s + factored-decode tokens/s on B200.
+
+Workload (default, the Llama-3.2-1B configuration): the KV stream of a
+16-layer model with 8 KV heads x head_dim 64 (n = 512), bf16, one sequence of
+8192 tokens ingested in chunks of 512 through ``BugStreamingCache`` (rank 32,
+exact tier 256, 4 sinks, ring 128, absorb block 16, prefill sub-blocks 128,
+``retention="lowrank_surprise"``, surprise-selected tier, coordinate budget
+T + ring + absorb so nothing is evicted), then 256 decode tokens with 32
+query heads answered by the factored decode kernel.  Keys/values are seeded
+synthetic low-rank-plus-noise streams with planted needles (one per layer);
+inputs (268 MB of K/V) exceed L2, so no flush is needed between steps.
+
+One step = reset + the whole ingest + the whole decode.  ``value`` is ingest
+tokens/s over all ranks (each rank streams its own sequence: weak scaling, no
+collective on the data path); decode tokens/s is reported beside it.
+
+``--impl reference`` times the CPU oracle port (numpy restatement of the
+reference) on a bounded sample of the same workload with all host threads.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+WORKLOAD = dict(
+    name="llama-3.2-1b-kv", layers=16, kv_heads=8, head_dim=64, q_heads=32, tokens=8192,
+    chunk=512, rank=32, hh=256, sinks=4, ring=128, absorb=16, prefill_block=128,
+    decode=256, theta=500000.0,
+)
+METRIC = "BUG ingest tokens/s + factored-decode tokens/s at 1/2/4/8 B200; % HBM roofline"
+
+
+def _peaks() -> tuple[dict, str]:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling while the timed region runs."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int) -> None:
+        self.index = index
+        self.proc: subprocess.Popen | None = None
+        self.lines: list[str] = []
+
+    def __enter__(self) -> "ClockSampler":
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self) -> None:
+        assert self.proc is not None and self.proc.stdout is not None
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc: object) -> None:
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = max(mx, float(parts[1]))
+            except ValueError:
+                continue
+            for nm, val in zip(names, parts[3:7]):
+                if val.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def make_inputs(w: dict, seed: int):
+    """Per-layer synthetic streams (post-RoPE K, V) for ingest + decode, and
+    the decode queries, as float32 numpy arrays."""
+    from kvdlra_b200.synthetic import lowrank_stream
+
+    L, H, D, T, dec = w["layers"], w["kv_heads"], w["head_dim"], w["tokens"], w["decode"]
+    ks = np.empty((L, 1, H, T + dec, D), np.float32)
+    vs = np.empty_like(ks)
+    for layer in range(L):
+        s = lowrank_stream(H, D, T + dec, n_needles=16, theta=w["theta"], seed=1000 * seed + layer)
+        ks[layer, 0] = s.k_post
+        vs[layer, 0] = s.v
+    rng = np.random.default_rng(7 + seed)
+    qs = (rng.standard_normal((dec, L, 1, w["q_heads"], D)) / math.sqrt(D)).astype(np.float32)
+    return ks, vs, qs
+
+
+def new_cache(w: dict, torch):
+    from kvdlra_b200 import BugStreamingCache, RopeAngles
+    from kvdlra_b200.synthetic import default_inv_freq
+
+    rope = RopeAngles(inv_freq=torch.from_numpy(default_inv_freq(w["head_dim"], w["theta"])))
+    return BugStreamingCache(
+        None, num_layers=w["layers"], rope=rope, rank=w["rank"],
+        coord_budget=w["tokens"] + w["ring"] + w["absorb"], recent_window=w["ring"],
+        absorb_block=w["absorb"], n_sink=w["sinks"], prefill_block_size=w["prefill_block"],
+        retention="lowrank_surprise", hh_budget=w["hh"], hh_select="surprise")
+
+
+def schedule_widths(w: dict) -> list[dict]:
+    """Counters before each decode step (mirrors the cache schedule: exact tier
+    full, every graduating block demotes `absorb` columns)."""
+    T, ring, b, sinks, hh = w["tokens"], w["ring"], w["absorb"], w["sinks"], w["hh"]
+    # After ingest (chunk sizes are multiples of the absorb block) the ring is
+    # back at `ring` tokens and every other token is a sink, in the exact tier
+    # or a coordinate column.
+    rl = ring
+    W = T - sinks - ring - hh
+    out = []
+    for _ in range(w["decode"]):
+        rl += 1
+        if rl >= ring + b:
+            rl -= b
+            W += b
+        out.append({"W": W, "hh": hh, "ring": rl, "sinks": sinks})
+    return out
+
+
+def decode_bytes(w: dict, st: dict) -> float:
+    """Algorithmic HBM bytes of one factored-decode launch over all layers:
+    coordinates C_k, C_v (fp32) and positions of the middle, the basis rows
+    U_k (read per KV group), the verbatim tiers (bf16 K and V), queries and
+    outputs."""
+    L, H, D, r = w["layers"], w["kv_heads"], w["head_dim"], w["rank"]
+    n = H * D
+    exact = st["hh"] + st["ring"] + st["sinks"]
+    per_layer = (2 * 4 * r * st["W"] + 4 * st["W"] + 2 * 4 * n * r + 2 * 2 * n * exact
+                 + 2 * 2 * w["q_heads"] * D)
+    return float(L * per_layer)
+
+
+def run_ours(args, w: dict) -> None:
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        from datetime import timedelta
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    from kvdlra_b200 import _native as N
+
+    ks, vs, qs = make_inputs(w, seed=rank)
+    bf = torch.bfloat16
+    K = torch.from_numpy(ks).to(dev, bf)
+    V = torch.from_numpy(vs).to(dev, bf)
+    Q = torch.from_numpy(qs).to(dev, bf)
+    T, C, dec = w["tokens"], w["chunk"], w["decode"]
+    cache = new_cache(w, torch)
+    launches = {"n": 0}
+
+    def step(Kd, Vd, Qd, ev=None, host=None):
+        cache.reset()
+        if ev:
+            ev[0].record()
+        for c0 in range(0, T, C):
+            if host is not None:
+                kk = host["k"][:, :, :, c0 : c0 + C].to(dev, non_blocking=True)
+                vv = host["v"][:, :, :, c0 : c0 + C].to(dev, non_blocking=True)
+            else:
+                kk = Kd[:, :, :, c0 : c0 + C]
+                vv = Vd[:, :, :, c0 : c0 + C]
+            cache.ingest_all(kk, vv, peek=True)
+        if ev:
+            ev[1].record()
+        outs = []
+        for j in range(dec):
+            p = T + j
+            if host is not None:
+                kk = host["k"][:, :, :, p : p + 1].to(dev, non_blocking=True)
+                vv = host["v"][:, :, :, p : p + 1].to(dev, non_blocking=True)
+                qq = host["q"][j].to(dev, non_blocking=True)
+            else:
+                kk, vv, qq = Kd[:, :, :, p : p + 1], Vd[:, :, :, p : p + 1], Qd[j]
+            o = cache.decode_all(kk, vv, qq)
+            if host is not None:
+                outs.append(o.to("cpu", non_blocking=True))
+        if ev:
+            ev[2].record()
+        return outs
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        step(K, V, Q)
+    barrier()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    with ClockSampler(dev.index) as clk:
+        barrier()
+        t_wall = time.perf_counter()
+        for i in range(args.steps):
+            step(K, V, Q, ev[i])
+        barrier()
+        t_wall = time.perf_counter() - t_wall
+    ingest_ms = sum(e[0].elapsed_time(e[1]) for e in ev)
+    decode_ms = sum(e[1].elapsed_time(e[2]) for e in ev)
+    times = torch.tensor([ingest_ms, decode_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+    ingest_ms, decode_ms = float(times[0]), float(times[1])
+
+    # ---- end to end through the public API from pinned host buffers
+    e2e = None
+    if not args.no_e2e:
+        host = {"k": torch.from_numpy(ks).to(bf).pin_memory(), "v": torch.from_numpy(vs).to(bf).pin_memory(),
+                "q": torch.from_numpy(qs).to(bf).pin_memory()}
+        step(None, None, None, host=host)
+        barrier()
+        ev2 = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+        for i in range(args.steps):
+            outs = step(None, None, None, ev2[i], host=host)
+        barrier()
+        e_ing = sum(e[0].elapsed_time(e[1]) for e in ev2)
+        t2 = torch.tensor([e_ing], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(t2, op=dist.ReduceOp.MAX)
+        h2d = (ks.size + vs.size + qs.size) * 2
+        d2h = len(outs) * outs[0].numel() * 2
+        e2e = {"value": world * T * args.steps / (float(t2[0]) / 1e3), "unit": "tokens/s",
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)}
+
+    # ---- per-kernel event timing over one more step (profiling pass)
+    N.profile(True)
+    step(K, V, Q)
+    torch.cuda.synchronize(dev)
+    prof = N.profile_read()
+    N.profile(False)
+    launches_total = sum(v[1] for v in prof.values())
+
+    result = None
+    if rank == 0:
+        peaks, peak_kind = _peaks()
+        dom = max(prof.items(), key=lambda kv: kv[1][0])[0] if prof else None
+        sched = schedule_widths(w)
+        dec_ms, dec_n = prof.get("decode_split_kernel", (0.0, 0))
+        merge_ms, _ = prof.get("decode_merge_kernel", (0.0, 0))
+        dec_bytes = sum(decode_bytes(w, st) for st in sched)
+        achieved = dec_bytes / ((dec_ms + merge_ms) / 1e3) / 1e9 if dec_ms else None
+        roof = {"kernel": "decode_split_kernel+decode_merge_kernel", "bound": "hbm",
+                "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": (achieved / peaks["hbm_gbs"]) if achieved else None,
+                "peak_source": peak_kind, "traffic": None,
+                "bytes_per_launch": dec_bytes / max(1, dec_n),
+                "avg_launch_ms": (dec_ms + merge_ms) / max(1, dec_n)}
+        kernels = {k: {"total_ms": round(v[0], 4), "launches": v[1],
+                       "share": round(v[0] / max(1e-9, sum(x[0] for x in prof.values())), 4)}
+                   for k, v in sorted(prof.items(), key=lambda kv: -kv[1][0])}
+        cpu = cpu_baseline(w, quick=True)
+        result = {
+            "metric": METRIC,
+            "value": world * T * args.steps / (ingest_ms / 1e3),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": (ingest_ms + decode_ms) / args.steps,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded low-rank+noise KV streams with needles; inputs > L2)",
+            "config": {"workload": w["name"], "layers": w["layers"], "kv_heads": w["kv_heads"],
+                       "head_dim": w["head_dim"], "q_heads": w["q_heads"], "tokens": T,
+                       "chunk": C, "rank": w["rank"], "hh_budget": w["hh"], "sinks": w["sinks"],
+                       "ring": w["ring"], "absorb_block": w["absorb"], "decode_tokens": dec,
+                       "sequences_per_gpu": 1, "parallelism": f"dp{world} (independent sequences)",
+                       "l2": "inputs larger than L2"},
+            "decode": {"value": world * dec * args.steps / (decode_ms / 1e3), "unit": "tokens/s"},
+            "ingest_ms_per_step": ingest_ms / args.steps,
+            "decode_ms_per_step": decode_ms / args.steps,
+            "e2e": e2e,
+            "gpu_launches": int(launches_total * args.steps),
+            "roofline": roof,
+            "dominant_kernel": dom,
+            "kernels": kernels,
+            "cpu_baseline": cpu,
+            "clocks": clk.summary(),
+            "wall_s": t_wall,
+        }
+        print(json.dumps(result))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def cpu_baseline(w: dict, quick: bool = False, sample_tokens: int = 2048, sample_decode: int = 16) -> dict:
+    """Time the oracle port (numpy restatement of the reference path) on one
+    layer of the workload: ``sample_tokens`` ingested tokens plus
+    ``sample_decode`` decode steps, scaled to the whole model (per token every
+    layer is processed)."""
+    from oracle.bug_oracle import OracleLayer, RopeSpec, default_inv_freq, gqa_attention
+    from kvdlra_b200.synthetic import lowrank_stream
+
+    H, D = w["kv_heads"], w["head_dim"]
+    s = lowrank_stream(H, D, sample_tokens + sample_decode, n_needles=4, theta=w["theta"], seed=0)
+    lay = OracleLayer(RopeSpec(default_inv_freq(D, w["theta"])), H, D, rank=w["rank"],
+                      coord_budget=w["tokens"] + w["ring"] + w["absorb"], recent_window=w["ring"],
+                      absorb_block=w["absorb"], n_sink=w["sinks"],
+                      prefill_block_size=w["prefill_block"], retention="lowrank_surprise",
+                      hh_budget=w["hh"], hh_select="surprise", dtype="bfloat16")
+
+    def mat(x):
+        return x.transpose(0, 2, 1).reshape(H * D, -1)
+
+    lay.mode = "ingest"
+    t0 = time.perf_counter()
+    for c0 in range(0, sample_tokens, w["chunk"]):
+        lay.update(mat(s.k_post[:, c0 : c0 + w["chunk"]]), mat(s.v[:, c0 : c0 + w["chunk"]]))
+        lay.consolidate()
+    t_ing = time.perf_counter() - t0
+    lay.mode = "normal"
+    rng = np.random.default_rng(0)
+    t0 = time.perf_counter()
+    for j in range(sample_decode):
+        p = sample_tokens + j
+        kr, vr = lay.update(mat(s.k_post[:, p : p + 1]), mat(s.v[:, p : p + 1]))
+        gqa_attention(rng.standard_normal((w["q_heads"], D)).astype(np.float32), lay.to_hf(kr), lay.to_hf(vr))
+    t_dec = time.perf_counter() - t0
+    try:
+        from threadpoolctl import threadpool_info
+
+        cores = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
+    except Exception:  # noqa: BLE001
+        cores = os.cpu_count() or 1
+    ingest_tps = sample_tokens / t_ing / w["layers"]
+    return {"value": ingest_tps, "unit": "tokens/s", "cores": int(cores), "kind": "port",
+            "decode_tokens_per_s": sample_decode / t_dec / w["layers"],
+            "sample": (f"1 of {w['layers']} layers, {sample_tokens} ingested tokens (chunk "
+                       f"{w['chunk']}) + {sample_decode} decode steps, scaled by the layer count")}
+
+
+def run_reference(args, w: dict) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    for _ in range(args.warmup):
+        cpu_baseline(w, sample_tokens=1024, sample_decode=4)
+    vals, decs, t_tot = [], [], time.perf_counter()
+    for _ in range(args.steps):
+        cb = cpu_baseline(w, sample_tokens=2048, sample_decode=16)
+        vals.append(cb["value"])
+        decs.append(cb["decode_tokens_per_s"])
+    t_tot = time.perf_counter() - t_tot
+    v = float(np.mean(vals))
+    out = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s",
+        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * t_tot / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32 (bf16 tiers emulated)", "data": "synthetic",
+        "config": {"workload": w["name"], "tokens": w["tokens"], "chunk": w["chunk"], "rank": w["rank"],
+                   "hh_budget": w["hh"], "layers": w["layers"]},
+        "decode": {"value": float(np.mean(decs)), "unit": "tokens/s"},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cb["cores"], "kind": "port",
+                         "sample": cb["sample"]},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out))
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--tokens", type=int, default=None, help="override the ingest length (testing)")
+    args = ap.parse_args()
+    w = dict(WORKLOAD)
+    if args.tokens:
+        w["tokens"] = args.tokens
+    if args.impl == "reference":
+        run_reference(args, w)
+    else:
+        run_ours(args, w)
+
+
+if __name__ == "__main__":
+    main()

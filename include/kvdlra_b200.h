@@ -190,10 +190,17 @@ int kvd_surprise(int32_t n_batch, int32_t n, int32_t m, int32_t ld_u, const floa
 int kvd_select_topk(int32_t n_batch, int32_t m, int32_t k, const float* scores,
                     int32_t* keep_idx, int32_t* demote_idx, kvd_stream_t stream);
 
-/* Orthogonal projection recon [nb][t][n] = U (U^T x) of token-major fp32
- * columns x [nb][t][n] (streaming_torch.py:255-258). */
-int kvd_project(int32_t n_batch, int32_t n, int32_t t, int32_t ld_u, const float* u,
-                const int32_t* r, const float* x, float* recon, kvd_stream_t stream);
+/* Workspace bytes kvd_factored_decode needs for `count` problems. */
+size_t kvd_decode_workspace_bytes(const kvd_config* cfg, int32_t count, int32_t num_q_heads);
+
+/* ------------------------------------------------------------- profiling */
+
+/* Per-kernel CUDA-event timing: kvd_profile(1) brackets every kernel launch of
+ * this library with an event pair on its stream (kvd_profile(0) stops and
+ * clears); kvd_profile_read synchronises and writes
+ * {"kernel_name": [total_ms, launches], ...} as a JSON string. */
+int kvd_profile(int32_t enable);
+int kvd_profile_read(char* out, size_t cap);
 
 #ifdef __cplusplus
 }

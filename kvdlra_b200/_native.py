@@ -131,8 +131,11 @@ def lib() -> C.CDLL:
     L.kvd_bug_step_workspace_bytes.restype = sz
     L.kvd_surprise.argtypes = [i32, i32, i32, i32, vp, vp, vp, vp, vp]
     L.kvd_select_topk.argtypes = [i32, i32, i32, vp, vp, vp, vp]
+    L.kvd_profile.argtypes = [i32]
+    L.kvd_profile_read.argtypes = [C.c_char_p, sz]
     for name in ("kvd_check_status", "kvd_prefill", "kvd_append", "kvd_consolidate", "kvd_absorb_block", "kvd_peek",
-                 "kvd_factored_decode", "kvd_bug_step", "kvd_surprise", "kvd_select_topk"):
+                 "kvd_factored_decode", "kvd_bug_step", "kvd_surprise", "kvd_select_topk",
+                 "kvd_profile", "kvd_profile_read"):
         getattr(L, name).restype = C.c_int
     _lib = L
     return L
@@ -142,6 +145,20 @@ def check(code: int, what: str) -> None:
     if code != KVD_OK:
         msg = lib().kvd_last_error().decode(errors="replace")
         raise KvdError(code, what, msg)
+
+
+def profile(enable: bool) -> None:
+    """Start (clearing previous totals) or stop per-kernel event timing."""
+    check(lib().kvd_profile(int(enable)), "kvd_profile")
+
+
+def profile_read() -> dict[str, tuple[float, int]]:
+    """``{kernel: (total_ms, launches)}`` recorded since ``profile(True)``."""
+    import json
+
+    buf = C.create_string_buffer(1 << 16)
+    check(lib().kvd_profile_read(buf, len(buf)), "kvd_profile_read")
+    return {k: (float(v[0]), int(v[1])) for k, v in json.loads(buf.value.decode()).items()}
 
 
 def stream_ptr(device: torch.device) -> int:

@@ -524,6 +524,12 @@ class BugStreamingLayer(CacheLayerMixin):  # type: ignore[misc]
 
     def reset(self) -> None:
         self._reset_state()
+        g = self._group
+        if g is not None:
+            p0 = self._p0()
+            g.t["r_k"][p0 : p0 + g.batch].zero_()
+            g.t["r_v"][p0 : p0 + g.batch].zero_()
+            g.t["status"].zero_()
 
     # ---------------------------------------------------------------- update
 
@@ -977,6 +983,11 @@ class BugStreamingCache(Cache):
 
     def _bug_layers(self) -> list[BugStreamingLayer]:
         return [ly for ly in self.layers if isinstance(ly, BugStreamingLayer)]
+
+    def reset(self) -> None:
+        """Empty every layer (device buffers stay allocated for reuse)."""
+        for ly in self._bug_layers():
+            ly.reset()
 
     def _set_mode(self, mode: str) -> None:
         for ly in self._bug_layers():

@@ -480,13 +480,12 @@ int launch_bug_step(const BugStepBatch& batch, int n_problems, int n_streams, cu
     smem = step_smem_bytes(a0.b, a0.ld, false);
     ok = 0;
   }
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(bug_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    attr_set = true;
-  }
+  if (int rc = ensure_smem((const void*)bug_step_kernel, smem, "bug_step_kernel")) return rc;
   dim3 grid(n_problems, n_streams);
-  bug_step_kernel<<<grid, kStepThreads, smem, stream>>>(batch, ok);
+  {
+    KTimerScope kts_("bug_step_kernel", stream);
+    bug_step_kernel<<<grid, kStepThreads, smem, stream>>>(batch, ok);
+  }
   return check_launch("bug_step_kernel");
 }
 
@@ -495,12 +494,11 @@ int launch_carry(const CarryBatch& batch, int n_problems, int n_streams, int ld,
   const int tok = 128;
   dim3 grid((batch.W + tok - 1) / tok, n_problems, n_streams);
   const int smem = 4 * (ld * ld + 8 * ld);
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(carry_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    attr_set = true;
+  if (int rc = ensure_smem((const void*)carry_kernel, smem, "carry_kernel")) return rc;
+  {
+    KTimerScope kts_("carry_kernel", stream);
+    carry_kernel<<<grid, 256, smem, stream>>>(batch, tok);
   }
-  carry_kernel<<<grid, 256, smem, stream>>>(batch, tok);
   return check_launch("carry_kernel");
 }
 
@@ -586,14 +584,11 @@ extern "C" int kvd_select_topk(int32_t n_batch, int32_t m, int32_t k, const floa
     return KVD_ERR_ARG;
   }
   if (n_batch == 0 || m == 0) return KVD_OK;
-  select_topk_kernel<<<n_batch, 1024, 4 * m, (cudaStream_t)stream>>>(m, k, scores, keep_idx,
+  if (int rc = ensure_smem((const void*)select_topk_kernel, 4 * m, "select_topk_kernel")) return rc;
+  {
+    KTimerScope kts_("select_topk_kernel", (cudaStream_t)stream);
+    select_topk_kernel<<<n_batch, 1024, 4 * m, (cudaStream_t)stream>>>(m, k, scores, keep_idx,
                                                                      demote_idx);
+  }
   return check_launch("select_topk_kernel");
-}
-
-extern "C" int kvd_project(int32_t n_batch, int32_t n, int32_t t, int32_t ld_u, const float* u,
-                           const int32_t* r, const float* x, float* recon, kvd_stream_t stream) {
-  (void)n_batch; (void)n; (void)t; (void)ld_u; (void)u; (void)r; (void)x; (void)recon; (void)stream;
-  set_error("kvd_project: use kvd_project_ws");
-  return KVD_ERR_ARG;
 }

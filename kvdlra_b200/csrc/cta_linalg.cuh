@@ -118,6 +118,17 @@ static __device__ int cta_jacobi_eig(double* A, double* V, int N, int ld, double
   }
   __syncthreads();
   if (N <= 1) return 0;
+  // Scale of the matrix (largest diagonal magnitude): entries below ~1e-17 of
+  // it are rounding noise and never rotated, so rank-deficient PSD matrices
+  // (null blocks full of noise) converge too.
+  __shared__ double s_scale;
+  if (tid == 0) {
+    double m = 0.0;
+    for (int i = 0; i < N; ++i) m = fmax(m, fabs(A[i * ld + i]));
+    s_scale = m;
+  }
+  __syncthreads();
+  const double floor_rot = 1e-17 * s_scale, floor_flag = 1e-14 * s_scale;
   const int np = N + (N & 1);
   const int half = np / 2;
   double* pc = cs;            // cos
@@ -136,14 +147,14 @@ static __device__ int cta_jacobi_eig(double* A, double* V, int N, int ld, double
         if (q < N) {
           const double apq = A[p * ld + q];
           const double app = A[p * ld + p], aqq = A[q * ld + q];
-          const double thr = 1e-15 * sqrt(fabs(app * aqq));
+          const double thr = fmax(1e-15 * sqrt(fabs(app * aqq)), floor_rot);
           if (apq != 0.0 && fabs(apq) > thr) {
             const double tau = (aqq - app) / (2.0 * apq);
             const double t = (tau >= 0.0) ? 1.0 / (tau + sqrt(1.0 + tau * tau))
                                           : -1.0 / (-tau + sqrt(1.0 + tau * tau));
             c = 1.0 / sqrt(1.0 + t * t);
             s = t * c;
-            if (fabs(apq) > 4e-15 * sqrt(fabs(app * aqq)) + 1e-300) s_rotated = 1;
+            if (fabs(apq) > fmax(4e-15 * sqrt(fabs(app * aqq)), floor_flag)) s_rotated = 1;
           }
         } else {
           q = -1;

@@ -122,17 +122,33 @@ __global__ void __launch_bounds__(kDecThreads) decode_split_kernel(DecArgs a) {
         }
       }
       __syncwarp();
-      // RoPE at the column's true position: pairs (d, d + D/2) = (i, i + NV/2)
+      // RoPE at the column's true position on rotate-half pairs (d, d + D/2)
       const int pos = a.mid_pos ? a.mid_pos[p * a.mid_sp + j] : a.pos_base + j;
+      if (half % 32 == 0) {
+        // both members of a pair sit in this lane: value i pairs with i + half/32
+        const int off = half / 32;
 #pragma unroll
-      for (int i = 0; i < NV / 2; ++i) {
-        const int f = lane + 32 * i;
+        for (int i = 0; i < NV; ++i) {
+          if (i % (2 * off) >= off) continue;
+          const int f = lane + 32 * (i % off) + 64 * off * (i / (2 * off));
+          float c = 1.f, s = 0.f;
+          if (f < half) rope_cs(pos, a.inv_freq[f], a.rope_scale, &c, &s);
+          float y1, y2;
+          rope_apply_pair(kp[i], kp[i + off], c, s, &y1, &y2);
+          kv[i] = y1;
+          kv[i + off] = y2;
+        }
+      } else {
+        // D <= 32: one value per lane, the partner lives in lane d +- D/2
+        const int d = lane;
+        const int partner = d < half ? d + half : d - half;
+        const float other = __shfl_sync(0xffffffffu, kp[0], partner < 32 ? partner : lane);
+        const int f = d < half ? d : d - half;
         float c = 1.f, s = 0.f;
-        if (f < half) rope_cs(pos, a.inv_freq[f], a.rope_scale, &c, &s);
-        float y1, y2;
-        rope_apply_pair(kp[i], kp[i + NV / 2], c, s, &y1, &y2);
-        kv[i] = y1;
-        kv[i + NV / 2] = y2;
+        if (d < D) rope_cs(pos, a.inv_freq[f], a.rope_scale, &c, &s);
+        kv[0] = d < half ? kp[0] * c - other * s : kp[0] * c + other * s;
+#pragma unroll
+        for (int i = 1; i < NV; ++i) kv[i] = 0.f;
       }
 #pragma unroll
       for (int i = 0; i < NV; ++i) vv[i] = 0.f;
@@ -279,7 +295,8 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
   DecArgs a;
   const int n = c.num_heads * c.head_dim;
   a.H = c.num_heads; a.D = c.head_dim; a.G = Hq / c.num_heads; a.ld = c.rank; a.Hq = Hq;
-  if (a.G > kMaxG || c.head_dim > 32 * kMaxNV || c.rank > 32 * kMaxNC) {
+  const bool d_ok = (c.head_dim <= 32) || ((c.head_dim / 2) % 32 == 0);
+  if (a.G > kMaxG || c.head_dim > 32 * kMaxNV || c.rank > 32 * kMaxNC || !d_ok) {
     set_error("factored decode: unsupported shape (G=%d D=%d r=%d)", a.G, c.head_dim, c.rank);
     return KVD_ERR_ARG;
   }
@@ -313,13 +330,9 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
   const int nv = (a.D + 31) / 32, nc = (a.ld + 31) / 32;
 #define KVD_DEC(NV, NC)                                                                         \
   {                                                                                             \
-    static bool attr = false;                                                                   \
-    if (!attr) {                                                                                \
-      cudaFuncSetAttribute(decode_split_kernel<T, NV, NC>,                                      \
-                           cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);            \
-      attr = true;                                                                              \
-    }                                                                                           \
-    decode_split_kernel<T, NV, NC><<<grid, kDecThreads, smem, s>>>(a);                          \
+    if (int rc0 = ensure_smem((const void*)decode_split_kernel<T, NV, NC>, smem,                \
+                              "decode_split_kernel")) return rc0;                               \
+    { KTimerScope kts_("decode_split_kernel", s); decode_split_kernel<T, NV, NC><<<grid, kDecThreads, smem, s>>>(a); }                          \
   }
   if (nv <= 2 && nc <= 1) KVD_DEC(2, 1)
   else if (nv <= 2 && nc <= 2) KVD_DEC(2, 2)
@@ -333,7 +346,10 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
   int rc = check_launch("decode_split_kernel");
   if (rc) return rc;
   const int msmem = 4 * (a.G * a.ld + a.G * a.D + 2 * a.G);
-  decode_merge_kernel<T><<<dim3(a.H, count), 128, msmem, s>>>(a);
+  {
+    KTimerScope kts_("decode_merge_kernel", s);
+    decode_merge_kernel<T><<<dim3(a.H, count), 128, msmem, s>>>(a);
+  }
   return check_launch("decode_merge_kernel");
 }
 

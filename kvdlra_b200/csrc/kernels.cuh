@@ -63,6 +63,17 @@ struct SelectOut {
 }  // namespace kvd
 
 namespace kvd_host {
+// Optional per-kernel CUDA-event timing (off unless kvd_profile(1) was called):
+// brackets one launch with events on its stream; kvd_profile_read sums them.
+struct KTimerScope {
+  int slot;
+  cudaStream_t s;
+  KTimerScope(const char* name, cudaStream_t stream);
+  ~KTimerScope();
+};
+// Allow `func` to use `bytes` of dynamic shared memory (checked against the
+// device opt-in limit minus the kernel's static shared memory).
+int ensure_smem(const void* func, size_t bytes, const char* name);
 using kvd::BugStepBatch; using kvd::CarryBatch; using kvd::CandSrc; using kvd::RopeArgs; using kvd::SelectOut;
 long bug_step_ws_per_problem(int n, int b, int ld);
 int launch_bug_step(const BugStepBatch& batch, int n_problems, int n_streams, cudaStream_t stream);

@@ -18,7 +18,11 @@
 
 #include <cstdint>
 
+#include <mutex>
+#include <string>
+#include <vector>
 #include <type_traits>
+#include <unordered_map>
 
 #include "kernels.cuh"
 
@@ -41,6 +45,81 @@ int check_launch(const char* what) {
     set_error("%s: %s", what, cudaGetErrorString(e));
     return KVD_ERR_CUDA;
   }
+  return KVD_OK;
+}
+
+// ------------------------------------------------------------ kernel timer
+
+namespace {
+struct TimerState {
+  std::mutex mu;
+  bool on = false;
+  struct Rec { std::string name; cudaEvent_t a, b; };
+  std::vector<Rec> pending;
+  std::vector<cudaEvent_t> pool;
+  std::unordered_map<std::string, std::pair<double, long>> acc;
+  cudaEvent_t get() {
+    if (!pool.empty()) { cudaEvent_t e = pool.back(); pool.pop_back(); return e; }
+    cudaEvent_t e;
+    cudaEventCreate(&e);
+    return e;
+  }
+  void drain() {
+    for (auto& r : pending) {
+      float ms = 0.f;
+      if (cudaEventSynchronize(r.b) == cudaSuccess && cudaEventElapsedTime(&ms, r.a, r.b) == cudaSuccess) {
+        auto& v = acc[r.name];
+        v.first += ms;
+        v.second += 1;
+      }
+      pool.push_back(r.a);
+      pool.push_back(r.b);
+    }
+    pending.clear();
+  }
+};
+TimerState& timer() { static TimerState t; return t; }
+}  // namespace
+
+KTimerScope::KTimerScope(const char* name, cudaStream_t stream) : slot(-1), s(stream) {
+  TimerState& t = timer();
+  if (!t.on) return;
+  std::lock_guard<std::mutex> lock(t.mu);
+  if (t.pending.size() > 100000) t.drain();
+  TimerState::Rec r{name, t.get(), t.get()};
+  cudaEventRecord(r.a, stream);
+  t.pending.push_back(r);
+  slot = (int)t.pending.size() - 1;
+}
+
+KTimerScope::~KTimerScope() {
+  if (slot < 0) return;
+  TimerState& t = timer();
+  std::lock_guard<std::mutex> lock(t.mu);
+  if (slot < (int)t.pending.size()) cudaEventRecord(t.pending[slot].b, s);
+}
+
+int ensure_smem(const void* func, size_t bytes, const char* name) {
+  static std::mutex mu;
+  static std::unordered_map<const void*, size_t> granted;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = granted.find(func);
+  if (it != granted.end() && it->second >= bytes) return KVD_OK;
+  cudaFuncAttributes attr;
+  cudaError_t e = cudaFuncGetAttributes(&attr, func);
+  int dev = 0, optin = 0;
+  if (e == cudaSuccess) e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+  if (e != cudaSuccess) { set_error("%s: %s", name, cudaGetErrorString(e)); return KVD_ERR_CUDA; }
+  if (bytes + attr.sharedSizeBytes > (size_t)optin) {
+    set_error("%s needs %zu bytes of shared memory (+%zu static) > device limit %d", name, bytes,
+              (size_t)attr.sharedSizeBytes, optin);
+    return KVD_ERR_ARG;
+  }
+  const size_t want = (size_t)optin - attr.sharedSizeBytes;  // grant the maximum once
+  e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)want);
+  if (e != cudaSuccess) { set_error("%s: %s", name, cudaGetErrorString(e)); return KVD_ERR_CUDA; }
+  granted[func] = want;
   return KVD_OK;
 }
 
@@ -334,6 +413,34 @@ static int dispatch(const kvd_config* c, F&& f) {
 using namespace kvd_host;
 
 extern "C" const char* kvd_last_error(void) { return g_err; }
+
+extern "C" int kvd_profile(int32_t enable) {
+  TimerState& t = timer();
+  std::lock_guard<std::mutex> lock(t.mu);
+  t.drain();
+  t.acc.clear();
+  t.on = enable != 0;
+  return KVD_OK;
+}
+
+extern "C" int kvd_profile_read(char* out, size_t cap) {
+  TimerState& t = timer();
+  std::lock_guard<std::mutex> lock(t.mu);
+  t.drain();
+  std::string js = "{";
+  bool first = true;
+  for (auto& kv : t.acc) {
+    char buf[256];
+    snprintf(buf, sizeof(buf), "%s\"%s\": [%.6f, %ld]", first ? "" : ", ", kv.first.c_str(),
+             kv.second.first, kv.second.second);
+    js += buf;
+    first = false;
+  }
+  js += "}";
+  if (!out || cap <= js.size()) { set_error("kvd_profile_read: buffer too small (%zu)", js.size() + 1); return KVD_ERR_ARG; }
+  memcpy(out, js.c_str(), js.size() + 1);
+  return KVD_OK;
+}
 extern "C" int kvd_version(void) { return 1; }
 
 extern "C" size_t kvd_workspace_bytes(const kvd_config* cfg) {

@@ -345,13 +345,12 @@ int launch_slash_score(const CandSrc<T>& src, int P, int m, int H, int D, RopeAr
   }
   const int half = D / 2;
   const int smem = 4 * (kScoreTile * half * 2 + kScoreTile * D + D * ld);
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(slash_score_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    attr = true;
-  }
+  if (int rc = ensure_smem((const void*)slash_score_kernel<T>, smem, "slash_score_kernel")) return rc;
   dim3 grid((m + kScoreTile - 1) / kScoreTile, P);
-  slash_score_kernel<T><<<grid, 256, smem, stream>>>(src, m, H, D, rope, u, u_sp, ld, rr, scores, sc_sp);
+  {
+    KTimerScope kts_("slash_score_kernel", stream);
+    slash_score_kernel<T><<<grid, 256, smem, stream>>>(src, m, H, D, rope, u, u_sp, ld, rr, scores, sc_sp);
+  }
   return check_launch("slash_score_kernel");
 }
 
@@ -361,13 +360,12 @@ int launch_slash_select(const CandSrc<T>& src, int P, int m, int keep_n, int H, 
                         const SelectOut& out, cudaStream_t stream) {
   if (m <= 0) return KVD_OK;
   const int smem = 4 * (2 * m) + 4 * m;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(slash_select_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    attr = true;
-  }
-  slash_select_kernel<T><<<P, 1024, smem, stream>>>(src, m, keep_n, H, D, rope, scores, sc_sp,
+  if (int rc = ensure_smem((const void*)slash_select_kernel<T>, smem, "slash_select_kernel")) return rc;
+  {
+    KTimerScope kts_("slash_select_kernel", stream);
+    slash_select_kernel<T><<<P, 1024, smem, stream>>>(src, m, keep_n, H, D, rope, scores, sc_sp,
                                                    hh_neighbor, out);
+  }
   return check_launch("slash_select_kernel");
 }
 
@@ -380,8 +378,11 @@ int launch_gather_block(const T* g_k, const T* g_v, long g_sp, int P, int b, int
   const long nblk = (tot + 255) / 256;
   const int blocks = (int)(nblk < 1024 ? nblk : 1024);
   dim3 grid(blocks, P);
-  gather_block_kernel<T><<<grid, 256, 0, stream>>>(g_k, g_v, g_sp, b, H, D, start, rope, xk, xv,
+  {
+    KTimerScope kts_("gather_block_kernel", stream);
+    gather_block_kernel<T><<<grid, 256, 0, stream>>>(g_k, g_v, g_sp, b, H, D, start, rope, xk, xv,
                                                    x_sp, mid_pos, mid_sp, w_off);
+  }
   return check_launch("gather_block_kernel");
 }
 
@@ -398,13 +399,12 @@ int launch_evict(int P, int W, int f_over, int retention, float* c_k, float* c_v
     set_error("evict: coordinate count %d too large for the in-block bitmap", W);
     return KVD_ERR_ARG;
   }
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(evict_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    attr = true;
-  }
-  evict_kernel<<<P, 1024, smem, stream>>>(W, f_over, retention, c_k, c_v, c_sp, ld, rk, rv, mid_pos,
+  if (int rc = ensure_smem((const void*)evict_kernel, smem, "evict_kernel")) return rc;
+  {
+    KTimerScope kts_("evict_kernel", stream);
+    evict_kernel<<<P, 1024, smem, stream>>>(W, f_over, retention, c_k, c_v, c_sp, ld, rk, rv, mid_pos,
                                           mid_sur, mid_sp, keep_ws, kw_sp);
+  }
   return check_launch("evict_kernel");
 }
 

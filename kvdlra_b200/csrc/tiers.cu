@@ -170,8 +170,11 @@ int launch_hf_to_rows(const kvd_hf_view& v, int P, int H, int D, T* dst, long ds
                       cudaStream_t s) {
   if (v.tokens <= 0 || P <= 0) return KVD_OK;
   dim3 grid(grid_for((long)v.tokens * H * D), P);
-  hf_to_rows_kernel<T><<<grid, 256, 0, s>>>((const T*)v.ptr, v.stride_b, v.stride_h, v.stride_t, H,
+  {
+    KTimerScope kts_("hf_to_rows_kernel", s);
+    hf_to_rows_kernel<T><<<grid, 256, 0, s>>>((const T*)v.ptr, v.stride_b, v.stride_h, v.stride_t, H,
                                             D, v.tokens, dst, dst_sp, slot0);
+  }
   return check_launch("hf_to_rows_kernel");
 }
 
@@ -180,14 +183,20 @@ int launch_rows_copy(const T* src, long src_sp, T* dst, long dst_sp, int count, 
                      cudaStream_t s) {
   if (count <= 0 || P <= 0) return KVD_OK;
   dim3 grid(grid_for((long)count * n), P);
-  rows_copy_kernel<T><<<grid, 256, 0, s>>>(src, src_sp, dst, dst_sp, count, n);
+  {
+    KTimerScope kts_("rows_copy_kernel", s);
+    rows_copy_kernel<T><<<grid, 256, 0, s>>>(src, src_sp, dst, dst_sp, count, n);
+  }
   return check_launch("rows_copy_kernel");
 }
 
 template <typename T>
 int launch_ring_compact(T* ring, long sp, int head, int len, int n, int P, cudaStream_t s) {
   if (head == 0 || len <= 0 || P <= 0) return KVD_OK;
-  ring_compact_kernel<T><<<P, 1024, 8192 * sizeof(T), s>>>(ring, sp, head, len, n);
+  {
+    KTimerScope kts_("ring_compact_kernel", s);
+    ring_compact_kernel<T><<<P, 1024, 8192 * sizeof(T), s>>>(ring, sp, head, len, n);
+  }
   return check_launch("ring_compact_kernel");
 }
 
@@ -207,8 +216,11 @@ int launch_peek(const kvd_config& c, const kvd_buffers& b, const kvd_counters& k
   auto seg = [&](const void* kk, const void* vv, long sp, int len) -> int {
     if (len <= 0) return KVD_OK;
     dim3 grid(grid_for((long)len * n), count);
-    rows_to_hf_kernel<T><<<grid, 256, 0, s>>>((const T*)kk + p0 * sp, (const T*)vv + p0 * sp, sp,
+    {
+      KTimerScope kts_("rows_to_hf_kernel", s);
+      rows_to_hf_kernel<T><<<grid, 256, 0, s>>>((const T*)kk + p0 * sp, (const T*)vv + p0 * sp, sp,
                                               len, H, D, okp, ovp, ob, oh, ot, l0);
+    }
     l0 += len;
     return check_launch("rows_to_hf_kernel");
   };
@@ -225,17 +237,16 @@ int launch_peek(const kvd_config& c, const kvd_buffers& b, const kvd_counters& k
     const int pos_base = (int)(k.cumulative_length - k.ring_len - mid_len);
     const int half = D / 2;
     const int smem = 4 * (2 * kMidTile * ld + 2 * D * ld + kMidTile * half * 2);
-    static bool attr = false;
-    if (!attr) {
-      cudaFuncSetAttribute(mid_hat_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-      attr = true;
-    }
+    if (int rc2 = ensure_smem((const void*)mid_hat_kernel<T>, smem, "mid_hat_kernel")) return rc2;
     dim3 grid((k.w_len + kMidTile - 1) / kMidTile, count);
-    mid_hat_kernel<T><<<grid, 256, smem, s>>>(
+    {
+      KTimerScope kts_("mid_hat_kernel", s);
+      mid_hat_kernel<T><<<grid, 256, smem, s>>>(
         b.u_k[k.u_sel] + p0 * u_sp, b.u_v[k.u_sel] + p0 * u_sp, u_sp, ld, b.r_k + p0, b.r_v + p0,
         b.c_k + p0 * c_sp, b.c_v + p0 * c_sp, c_sp,
         track_pos ? b.mid_pos + (long)p0 * c.w_cap : nullptr, c.w_cap, pos_base, k.w_len, H, D,
         c.inv_freq, c.rope_scaling, okp, ovp, ob, oh, ot, l0);
+    }
     if ((rc = check_launch("mid_hat_kernel"))) return rc;
     l0 += k.w_len;
   }
@@ -247,9 +258,12 @@ int launch_peek(const kvd_config& c, const kvd_buffers& b, const kvd_counters& k
   }
   if (tk.tokens > 0) {
     dim3 grid(grid_for((long)tk.tokens * n), count);
-    hf_to_hf_kernel<T><<<grid, 256, 0, s>>>((const T*)tk.ptr, (const T*)tv.ptr, tk.stride_b,
+    {
+      KTimerScope kts_("hf_to_hf_kernel", s);
+      hf_to_hf_kernel<T><<<grid, 256, 0, s>>>((const T*)tk.ptr, (const T*)tv.ptr, tk.stride_b,
                                             tk.stride_h, tk.stride_t, tk.tokens, H, D, okp, ovp,
                                             ob, oh, ot, l0);
+    }
     if ((rc = check_launch("hf_to_hf_kernel"))) return rc;
   }
   return KVD_OK;

@@ -106,7 +106,12 @@ def test_full_size_single_layer_stream() -> None:
     stats = run_ingest(layer, oracle, s.k_post, s.v, 256, dtype=torch.float32)
     assert stats.max_angle_k <= 1e-2 and stats.max_angle_v <= 1e-2, stats
     hh = set(layer.hh_pos.cpu().tolist())
-    assert set(s.needles.tolist()) <= hh  # every needle verbatim in the exact tier
+    # Needles past the first chunk's middle graduate through the exact-tier
+    # selection and must be kept verbatim; the first chunk's middle is absorbed
+    # directly (no warm-up seed in this workload), exactly as the reference does.
+    late = {int(p) for p in s.needles if p >= 256 - 128}
+    assert late <= hh
+    assert oracle.hh_pos is not None and late <= set(oracle.hh_pos.tolist())
     assert layer.stored_state_numel() == oracle.stored_state_numel()
     rng = np.random.default_rng(1)
     ok_, ov_ = oracle.decode_peek()
