@@ -2,15 +2,17 @@
 //
 // Restates src/kvdlra/integrators/streaming_torch.py:82-189 for a batch of
 // independent problems (one CTA per problem x stream):
-//   a = U^T X ; R = X - U a ; a2 = U^T R ; R -= U a2 ; a += a2     (fp32 FFMA)
-//   eig(R^T R) in fp64 (two-sided Jacobi)  -> s, V ; admit s > 100 eps |X|_F
-//   Q = R V_m / s, made orthonormal by CGS2 (completion for null directions)
-//   eig(B B^T), B = [[diag(sigma), a], [0, diag(s_m) V_m^T]]  (fp64 Jacobi)
-//   U_new = [U | Q] W[:, :keep], sigma_new, rot = W[:r, :keep]^T,
-//   coords = U_new^T X.
-// The left singular vectors/values of B are the eigenpairs of B B^T; forming
-// the Gram in fp64 from fp32 inputs keeps the fp32-level accuracy of the
-// reference's SVD for every singular value above ~1e-8 of the largest.
+//   a = U^T X ; R = X - U a ; a2 = U^T R ; R -= U a2 ; a += a2   (fp32 FFMA)
+//   one-sided Jacobi on R (n x b): R V = [s_j q_j]  -> singular values s,
+//     orthonormal left vectors q_j, right vectors V; admit s > 100 eps |X|_F,
+//     at most n - r of them
+//   one-sided Jacobi on B^T, B = [[diag(sigma), a], [0, diag(s_m) V_m^T]]
+//     ((r+m) x (r+b)):  B^T W = [sigma'_c w_c]  -> W = left singular vectors
+//     of B (u_loc), sigma' its singular values
+//   U_new = [U | Q] W[:, top keep], rot = W[:r, top keep]^T, coords = U_new^T X.
+// One-sided (Hestenes) Jacobi never forms a Gram matrix, so it keeps the
+// relative accuracy of a direct SVD; all rotations of a round touch disjoint
+// columns, so a round costs one barrier.
 #include <stdio.h>
 
 #include <cfloat>
@@ -19,80 +21,221 @@
 
 namespace kvd {
 
-
 struct StepWs {
-  float* a;      // [ld][b]
-  float* R;      // [b][n]
-  float* Q;      // [b][n]
-  double* H;     // [b][b]
-  double* VH;    // [b][b]
-  double* G;     // [N][N]
-  double* VG;    // [N][N]
-  double* lam;   // [N]
+  float* a;      // [ld][b]   coordinates of the block in the old basis
+  float* R;      // [b][n]    residual, then sigma-scaled left vectors
+  float* Q;      // [b][n]    admitted orthonormal residual directions
+  float* VH;     // [b][b]    right singular vectors of R (column-major)
+  float* BT;     // [N][N+b]  B^T (column-major, ld = ld + b)   (global fallback)
+  float* W;      // [N][N]    rotations of B^T (column-major)    (global fallback)
+  double* nrm;   // [N]
   int* ord;      // [N]
   int* ordh;     // [b]
   double* sv;    // [b]
-  float* WU;     // [N][ld]  top eigenvectors of G (fp32)
-  float* VQ;     // [b][b]   V_h[:, j] / s_j  (fp32)
-  double* VS;    // [b][b]   V_h columns in descending-s order
+  float* WU;     // [N][ld]   top left singular vectors of B (row-major)
 };
 
 __host__ __device__ inline long align16(long x) { return (x + 15) & ~15L; }
 
 __host__ __device__ inline long step_ws_bytes(int n, int b, int ld) {
-  const long N = ld + b;
+  const long N = ld + b, LB = ld + b;
   long o = 0;
   o += align16(4L * ld * b);
   o += align16(4L * b * n) * 2;
-  o += align16(8L * b * b) * 2;
-  o += align16(8L * N * N) * 2;
+  o += align16(4L * b * b);
+  o += align16(4L * N * LB);
+  o += align16(4L * N * N);
   o += align16(8L * N);
   o += align16(4L * N);
   o += align16(4L * b);
   o += align16(8L * b);
   o += align16(4L * N * ld);
-  o += align16(4L * b * b);
-  o += align16(8L * b * b);
   return o;
 }
 
 __device__ StepWs carve(char* base, int n, int b, int ld) {
-  const long N = ld + b;
+  const long N = ld + b, LB = ld + b;
   StepWs w;
   long o = 0;
   auto take = [&](long bytes) { char* p = base + o; o += align16(bytes); return p; };
   w.a = (float*)take(4L * ld * b);
   w.R = (float*)take(4L * b * n);
   w.Q = (float*)take(4L * b * n);
-  w.H = (double*)take(8L * b * b);
-  w.VH = (double*)take(8L * b * b);
-  w.G = (double*)take(8L * N * N);
-  w.VG = (double*)take(8L * N * N);
-  w.lam = (double*)take(8L * N);
+  w.VH = (float*)take(4L * b * b);
+  w.BT = (float*)take(4L * N * LB);
+  w.W = (float*)take(4L * N * N);
+  w.nrm = (double*)take(8L * N);
   w.ord = (int*)take(4L * N);
   w.ordh = (int*)take(4L * b);
   w.sv = (double*)take(8L * b);
   w.WU = (float*)take(4L * N * ld);
-  w.VQ = (float*)take(4L * b * b);
-  w.VS = (double*)take(8L * b * b);
   return w;
 }
 
-// Shared-memory plan: gemm scratch (8 KB) + Jacobi pair table + optionally the
-// Jacobi matrices when they fit.
 constexpr int kGemmSmemFloats = 2 * 16 * 64;
 constexpr int kStepThreads = 512;
+constexpr int kStepMiscBytes = 4096;
 
-__device__ void cta_copy_d(double* dst, const double* src, int count) {
-  for (int e = threadIdx.x; e < count; e += blockDim.x) dst[e] = src[e];
+// One-sided (Hestenes) Jacobi: orthogonalise the `cols` columns of X (column
+// c at X + c*ldx, `len` rows) by plane rotations, accumulated into V
+// (cols x cols, column-major, ldv; initialised to I here).  Round-robin
+// ordering; each column pair is handled by a group of G lanes (all pairs of a
+// round run concurrently), one barrier per round.  The rotation zeroes the
+// pair's inner product (Golub & Van Loan sec. 8.6.3).  ACC is the type the
+// 2x2 Gram of a pair is accumulated in.  Returns the sweeps taken
+// (max_sweeps + 1 when not converged).
+template <int G, typename ACC>
+static __device__ int cta_hestenes(float* X, int len, int cols, int ldx, float* V, int ldv,
+                                   float tol, int max_sweeps) {
+  __shared__ int s_rot;
+  const int tid = threadIdx.x, nthr = blockDim.x;
+  const int groups = nthr / G, gid = tid / G, gl = tid % G;
+  for (int e = tid; e < cols * cols; e += nthr) {
+    const int c = e / cols, k = e % cols;
+    V[c * ldv + k] = (c == k) ? 1.f : 0.f;
+  }
   __syncthreads();
+  if (cols <= 1) return 0;
+  const int np = cols + (cols & 1);
+  const int half = np / 2;
+  int sweep = 0;
+  for (; sweep < max_sweeps; ++sweep) {
+    if (tid == 0) s_rot = 0;
+    __syncthreads();
+    for (int k = 0; k < np - 1; ++k) {
+      for (int base = 0; base < half; base += groups) {
+        const int i = base + gid;
+        int p = 0, q = -1;
+        if (i < half) {
+          int a, b;
+          rr_pair(i, k, np, &a, &b);
+          p = a < b ? a : b;
+          q = a < b ? b : a;
+          if (q >= cols) q = -1;
+        }
+        const bool active = q >= 0;
+        float* xp = X + (long)p * ldx;
+        float* xq = X + (long)(active ? q : p) * ldx;
+        ACC al = 0, be = 0, ga = 0;
+        if (active) {
+          for (int e = gl; e < len; e += G) {
+            const ACC u = xp[e], v = xq[e];
+            al += u * u;
+            be += v * v;
+            ga += u * v;
+          }
+        }
+#pragma unroll
+        for (int o = G / 2; o > 0; o >>= 1) {
+          al += __shfl_xor_sync(0xffffffffu, al, o);
+          be += __shfl_xor_sync(0xffffffffu, be, o);
+          ga += __shfl_xor_sync(0xffffffffu, ga, o);
+        }
+        if (!active || ga == (ACC)0 || fabsf((float)ga) <= tol * sqrtf((float)al * (float)be))
+          continue;
+        // rotation angle in fp32: its rounding only perturbs the convergence
+        // rate, the applied rotation stays orthogonal (c^2 + s^2 = 1)
+        const float zeta = ((float)be - (float)al) / (2.f * (float)ga);
+        const float az = fabsf(zeta);
+        const float t = (az > 1e18f) ? 0.5f / zeta
+                                     : copysignf(1.f, zeta) / (az + sqrtf(fmaf(zeta, zeta, 1.f)));
+        const double cd = 1.0 / sqrt(1.0 + (double)t * (double)t);
+        const float c = (float)cd, s = (float)(cd * (double)t);
+        for (int e = gl; e < len; e += G) {
+          const float u = xp[e], v = xq[e];
+          xp[e] = c * u - s * v;
+          xq[e] = s * u + c * v;
+        }
+        float* vp = V + (long)p * ldv;
+        float* vq = V + (long)q * ldv;
+        for (int e = gl; e < cols; e += G) {
+          const float u = vp[e], v = vq[e];
+          vp[e] = c * u - s * v;
+          vq[e] = s * u + c * v;
+        }
+        if (gl == 0) s_rot = 1;
+      }
+      __syncthreads();
+    }
+    const int any = s_rot;
+    __syncthreads();
+    if (!any) break;
+  }
+  return sweep;
+}
+
+// out[k][j] = sum_i U[i][k] X[j][i]   (k < M, j < b; U row-major ld, X [b][n])
+static __device__ void cta_proj_t(int M, int b, int n, const float* U, int ld, const float* X,
+                                  float* out, int ldo) {
+  for (int e = threadIdx.x; e < M * b; e += blockDim.x) {
+    const int k = e % M, j = e / M;
+    const float* x = X + (long)j * n;
+    float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
+    int i = 0;
+    for (; i + 3 < n; i += 4) {
+      acc0 = fmaf(U[(long)i * ld + k], x[i], acc0);
+      acc1 = fmaf(U[(long)(i + 1) * ld + k], x[i + 1], acc1);
+      acc2 = fmaf(U[(long)(i + 2) * ld + k], x[i + 2], acc2);
+      acc3 = fmaf(U[(long)(i + 3) * ld + k], x[i + 3], acc3);
+    }
+    for (; i < n; ++i) acc0 = fmaf(U[(long)i * ld + k], x[i], acc0);
+    out[k * ldo + j] = (acc0 + acc1) + (acc2 + acc3);
+  }
+  __syncthreads();
+}
+
+// Y[j][i] (=|+=) alpha * sum_k A[i][k] C[k][j]  for i < n, j < b; A row-major
+// (lda), C row-major (ldc, in shared memory), Y [b][n].  One thread per row i.
+template <bool ACCUM>
+static __device__ void cta_rows_times(int n, int b, int K, const float* A, int lda, const float* C,
+                                      int ldc, float* Y, float alpha) {
+  constexpr int JB = 16;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float* ar = A + (long)i * lda;
+    for (int j0 = 0; j0 < b; j0 += JB) {
+      float acc[JB];
+#pragma unroll
+      for (int jj = 0; jj < JB; ++jj) acc[jj] = 0.f;
+      const int jn = min(JB, b - j0);
+      for (int k = 0; k < K; ++k) {
+        const float av = ar[k];
+        const float* cr = C + (long)k * ldc + j0;
+#pragma unroll
+        for (int jj = 0; jj < JB; ++jj)
+          if (jj < jn) acc[jj] = fmaf(av, cr[jj], acc[jj]);
+      }
+#pragma unroll
+      for (int jj = 0; jj < JB; ++jj) {
+        if (jj >= jn) break;
+        float* y = Y + (long)(j0 + jj) * n + i;
+        *y = ACCUM ? fmaf(alpha, acc[jj], *y) : alpha * acc[jj];
+      }
+    }
+  }
+  __syncthreads();
+}
+
+// Column norms (fp64) of X[:, 0..cols) into nrm, then order = descending.
+static __device__ void cta_colnorm_order(const float* X, int len, int cols, int ldx, double* nrm,
+                                         int* order) {
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32, nw = blockDim.x / 32;
+  for (int c = warp; c < cols; c += nw) {
+    const float* x = X + (long)c * ldx;
+    double acc = 0.0;
+    for (int e = lane; e < len; e += 32) acc += (double)x[e] * x[e];
+    acc = warp_sum(acc);
+    if (lane == 0) nrm[c] = sqrt(acc);
+  }
+  __syncthreads();
+  cta_argsort_desc(nrm, cols, order);
 }
 
 // Orthonormalise the rows of Q[0..m) (length n) in order by classical
 // Gram-Schmidt applied twice; a row that collapses (numerically dependent or
 // null) is replaced by the first canonical vector e_i that survives the same
-// orthogonalisation.  Returns nothing; Q is updated in place.
-__device__ void cta_cgs2_rows(float* Q, int m, int n, double* dots /*>= m*/, double* red /*>=33*/) {
+// orthogonalisation.  Used only when some admitted direction is (near) null.
+static __device__ void cta_cgs2_rows(float* Q, int m, int n, double* dots /*>= m*/,
+                                     double* red /*>=32*/) {
   __shared__ double s_norm, s_norm0;
   __shared__ int s_next_e;
   const int tid = threadIdx.x, nthr = blockDim.x, lane = tid % 32, warp = tid / 32,
@@ -101,7 +244,6 @@ __device__ void cta_cgs2_rows(float* Q, int m, int n, double* dots /*>= m*/, dou
   __syncthreads();
   for (int j = 0; j < m; ++j) {
     float* qj = Q + (long)j * n;
-    // norm before
     double acc = 0.0;
     for (int i = tid; i < n; i += nthr) acc += (double)qj[i] * qj[i];
     acc = warp_sum(acc);
@@ -109,10 +251,8 @@ __device__ void cta_cgs2_rows(float* Q, int m, int n, double* dots /*>= m*/, dou
     __syncthreads();
     if (tid == 0) { double t = 0; for (int w = 0; w < nw; ++w) t += red[w]; s_norm0 = sqrt(t); }
     __syncthreads();
-    bool replaced = false;
     for (int attempt = 0; attempt < n + 1; ++attempt) {
       for (int pass = 0; pass < 2; ++pass) {
-        // dots with previous rows, one warp per previous row
         for (int l = warp; l < j; l += nw) {
           const float* ql = Q + (long)l * n;
           double d = 0.0;
@@ -137,23 +277,171 @@ __device__ void cta_cgs2_rows(float* Q, int m, int n, double* dots /*>= m*/, dou
       __syncthreads();
       const double nrm = s_norm, nrm0 = s_norm0;
       if (nrm > 1e-3 * nrm0 && nrm > 1e-30) break;
-      // collapsed: restart from the next canonical vector
       const int e = s_next_e;
       __syncthreads();
-      if (e >= n) break;  // cannot happen while m <= n
+      if (e >= n) break;
       for (int i = tid; i < n; i += nthr) qj[i] = (i == e) ? 1.f : 0.f;
       if (tid == 0) { s_next_e = e + 1; s_norm0 = 1.0; }
-      replaced = true;
       __syncthreads();
     }
-    (void)replaced;
     const float inv = (float)(1.0 / s_norm);
     for (int i = tid; i < n; i += nthr) qj[i] *= inv;
     __syncthreads();
   }
 }
 
-__global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch batch, int smem_mat_ok) {
+// Two-sided cyclic Jacobi on a symmetric N x N fp64 matrix A (leading
+// dimension lda, odd so column accesses are bank-conflict free), eigenvectors
+// accumulated in V (N x N fp64, ldv).  N'/2 disjoint rotations per round
+// (circle ordering), rows then columns.  Rotation: Golub & Van Loan
+// Alg. 8.4.2 (sym.schur2), angle in fp32 (only the convergence rate depends
+// on it), applied in fp64.  `cs` is shared scratch of 2*(N/2+1) doubles and
+// 2*(N/2+1) ints (8-byte aligned).  Entries below 1e-17 of the largest diagonal are rounding
+// noise and are left alone, so rank-deficient PSD matrices converge.
+static __device__ int cta_jacobi_sym(double* A, int N, int lda, double* V, int ldv, float* cs,
+                                     int max_sweeps) {
+  __shared__ int s_rot;
+  __shared__ double s_scale;
+  const int tid = threadIdx.x, nthr = blockDim.x;
+  for (int e = tid; e < N * N; e += nthr) {
+    const int i = e / N, j = e % N;
+    V[i * ldv + j] = (i == j) ? 1.0 : 0.0;
+  }
+  if (tid == 0) {
+    double mx = 0.0;
+    for (int i = 0; i < N; ++i) mx = fmax(mx, fabs(A[i * lda + i]));
+    s_scale = mx;
+  }
+  __syncthreads();
+  if (N <= 1) return 0;
+  const double floor_rot = 1e-17 * s_scale, floor_flag = 1e-14 * s_scale;
+  const int np = N + (N & 1), half = np / 2;
+  double* pc = reinterpret_cast<double*>(cs);
+  double* ps = pc + half;
+  int* pp = reinterpret_cast<int*>(ps + half);
+  int* pq = pp + half;
+  int sweep = 0;
+  for (; sweep < max_sweeps; ++sweep) {
+    if (tid == 0) s_rot = 0;
+    __syncthreads();
+    for (int k = 0; k < np - 1; ++k) {
+      for (int i = tid; i < half; i += nthr) {
+        int a, b;
+        rr_pair(i, k, np, &a, &b);
+        int p = a < b ? a : b, q = a < b ? b : a;
+        double pcd = 1.0, psd = 0.0;
+        if (q < N) {
+          const double apq = A[p * lda + q], app = A[p * lda + p], aqq = A[q * lda + q];
+          const double thr = fmax(1e-15 * sqrt(fabs(app * aqq)), floor_rot);
+          if (apq != 0.0 && fabs(apq) > thr) {
+            const float tau = (float)((aqq - app) / (2.0 * apq));
+            const float at = fabsf(tau);
+            const float t = (at > 1e18f) ? 0.5f / tau
+                                         : copysignf(1.f, tau) / (at + sqrtf(fmaf(tau, tau, 1.f)));
+            // the angle is approximate (fp32 t) but (c, s) is an exact fp64
+            // rotation, so applying it never changes norms
+            const double cd = 1.0 / sqrt(1.0 + (double)t * (double)t);
+            pcd = cd;
+            psd = cd * (double)t;
+            if (fabs(apq) > fmax(4e-15 * sqrt(fabs(app * aqq)), floor_flag)) s_rot = 1;
+          }
+        } else {
+          q = -1;
+        }
+        pc[i] = pcd; ps[i] = psd; pp[i] = p; pq[i] = q;
+      }
+      __syncthreads();
+      for (int e = tid; e < half * N; e += nthr) {   // rows: A <- J^T A
+        const int i = e / N, j = e % N;
+        const double s = ps[i];
+        if (s == 0.0) continue;
+        const int p = pp[i], q = pq[i];
+        const double c = pc[i];
+        const double x = A[p * lda + j], y = A[q * lda + j];
+        A[p * lda + j] = c * x - s * y;
+        A[q * lda + j] = s * x + c * y;
+      }
+      __syncthreads();
+      for (int e = tid; e < half * N; e += nthr) {   // columns: A <- A J, V <- V J
+        const int i = e / N, j = e % N;
+        const double s = ps[i];
+        if (s == 0.0) continue;
+        const int p = pp[i], q = pq[i];
+        const double c = pc[i];
+        const double x = A[j * lda + p], y = A[j * lda + q];
+        A[j * lda + p] = c * x - s * y;
+        A[j * lda + q] = s * x + c * y;
+        const double vx = V[j * ldv + p], vy = V[j * ldv + q];
+        V[j * ldv + p] = c * vx - s * vy;
+        V[j * ldv + q] = s * vx + c * vy;
+      }
+      __syncthreads();
+    }
+    const int any = s_rot;
+    __syncthreads();
+    if (!any) break;
+  }
+  return sweep;
+}
+
+// H = X^T X in fp64 for the `cols` columns of X (column c at X + c*ldx, len
+// rows); one warp per (c1 <= c2) pair.
+static __device__ void cta_gram_cols(const float* X, int len, int cols, int ldx, double* H, int ldh) {
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, nw = blockDim.x / 32;
+  const int pairs = cols * (cols + 1) / 2;
+  for (int e = warp; e < pairs; e += nw) {
+    int c1 = 0, rem = e;
+    while (rem >= cols - c1) { rem -= cols - c1; ++c1; }
+    const int c2 = c1 + rem;
+    const float* x1 = X + (long)c1 * ldx;
+    const float* x2 = X + (long)c2 * ldx;
+    double acc = 0.0;
+    for (int i = lane; i < len; i += 32) acc += (double)x1[i] * (double)x2[i];
+    acc = warp_sum(acc);
+    if (lane == 0) { H[c1 * ldh + c2] = acc; H[c2 * ldh + c1] = acc; }
+  }
+  __syncthreads();
+}
+
+// Make the rows of Q (m x n) orthonormal by one Cholesky-QR pass in fp64:
+// G = Q Q^T = L L^T, Q <- L^{-1} Q.  `Gs` is shared scratch of m*(m+1)
+// doubles.  Returns false (Q untouched) when a pivot is not safely positive,
+// i.e. the rows are (numerically) dependent.
+static __device__ bool cta_cholqr_rows(float* Q, int m, int n, double* Gs) {
+  __shared__ int s_ok;
+  const int ldg = m + 1;
+  cta_gram_cols(Q, n, m, n, Gs, ldg);  // rows of Q are the "columns" here
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    for (int j = 0; j < m && ok; ++j) {  // in-place Cholesky, lower triangle
+      double d = Gs[j * ldg + j];
+      for (int k = 0; k < j; ++k) d -= Gs[j * ldg + k] * Gs[j * ldg + k];
+      if (!(d > 0.25)) { ok = 0; break; }  // rows are near-unit: pivots ~1
+      d = sqrt(d);
+      Gs[j * ldg + j] = d;
+      for (int i = j + 1; i < m; ++i) {
+        double v = Gs[i * ldg + j];
+        for (int k = 0; k < j; ++k) v -= Gs[i * ldg + k] * Gs[j * ldg + k];
+        Gs[i * ldg + j] = v / d;
+      }
+    }
+    s_ok = ok;
+  }
+  __syncthreads();
+  if (!s_ok) return false;
+  // forward substitution per column i of Q, in place: Q[:, i] <- L^{-1} Q[:, i]
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    for (int j = 0; j < m; ++j) {
+      double v = Q[(long)j * n + i];
+      for (int k = 0; k < j; ++k) v -= Gs[j * ldg + k] * (double)Q[(long)k * n + i];
+      Q[(long)j * n + i] = (float)(v / Gs[j * ldg + j]);
+    }
+  }
+  __syncthreads();
+  return true;
+}
+
+__global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch batch, int smem_budget) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int p = blockIdx.x;
   const BugStepArgs& A = batch.s[blockIdx.y];
@@ -165,12 +453,11 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
   const int r = A.r[p];
   StepWs w = carve(A.ws + p * A.ws_sp, n, b, ld);
   float* gsm = reinterpret_cast<float*>(smem_raw);
-  double* jac_cs = reinterpret_cast<double*>(smem_raw + 4 * kGemmSmemFloats);  // 4*(N/2+1)
-  const int Nmax = ld + b;
-  double* red = jac_cs + 4 * (Nmax / 2 + 2);                                     // 64 doubles
-  double* smat = red + 64;                                                       // optional
+  double* red = reinterpret_cast<double*>(smem_raw + 4 * kGemmSmemFloats);  // 64 doubles
+  float* pool = reinterpret_cast<float*>(smem_raw + 4 * kGemmSmemFloats + kStepMiscBytes);
+  const long pool_floats = (smem_budget - 4L * kGemmSmemFloats - kStepMiscBytes) / 4;
   __shared__ double s_xnorm2;
-  __shared__ int s_m, s_keep;
+  __shared__ int s_m, s_keep, s_degenerate;
   const int tid = threadIdx.x, nthr = blockDim.x, lane = tid % 32, warp = tid / 32;
 
   // ||X||_F^2 (fp64 accumulation of fp32 squares)
@@ -183,32 +470,67 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
     if (tid == 0) { double t = 0; for (int i = 0; i < nthr / 32; ++i) t += red[i]; s_xnorm2 = t; }
     __syncthreads();
   }
-  // ----- projections and residual
-  for (long e = tid; e < (long)b * n; e += nthr) w.R[e] = X[e];
+  // ----- residual R = (I - U U^T)^2 X (the reference's re-orthogonalised residual)
+  const bool r_in_smem = (long)b * n + (long)b * b <= pool_floats;
+  float* Rm = r_in_smem ? pool : w.R;
+  float* Vh = r_in_smem ? pool + (long)b * n : w.VH;
+  // U staged in shared memory (at the end of the pool) when it fits beside the
+  // residual phase; it is read by four projections and the basis update
+  const long u_floats = (long)n * r;
+  const long p1_floats = (long)b * n + (long)b * b + 2L * r * b;
+  const bool u_smem = r > 0 && r_in_smem && p1_floats + u_floats <= pool_floats;
+  const float* Us = U;
+  int uld = ld;
+  if (u_smem) {
+    float* dst = pool + (pool_floats - u_floats);
+    for (long e = tid; e < u_floats; e += nthr) {
+      const long i = e / r, k = e % r;
+      dst[e] = U[i * ld + k];
+    }
+    Us = dst;
+    uld = r;
+  }
+  for (long e = tid; e < (long)b * n; e += nthr) Rm[e] = X[e];
   __syncthreads();
   if (r > 0) {
-    // a = U^T X : (r x b)
-    cta_gemm(r, b, n, U, 1, ld, X, 1, n, w.a, b, 1, 1.f, 0.f, gsm);
-    // R -= U a   (R stored [j][i])
-    cta_gemm(n, b, r, U, ld, 1, w.a, b, 1, w.R, 1, n, -1.f, 1.f, gsm);
-    // a2 = U^T R -> Q scratch [r][b]
-    float* a2 = w.Q;
-    cta_gemm(r, b, n, U, 1, ld, w.R, 1, n, a2, b, 1, 1.f, 0.f, gsm);
-    cta_gemm(n, b, r, U, ld, 1, a2, b, 1, w.R, 1, n, -1.f, 1.f, gsm);
-    for (int e = tid; e < r * b; e += nthr) w.a[e] += a2[e];
+    // a and a2 live in shared memory when they fit beside R (small in steady state)
+    const bool a_smem = r_in_smem && (long)b * n + (long)b * b + 2L * r * b <= pool_floats;
+    float* as = a_smem ? pool + (long)b * n + (long)b * b : w.a;
+    float* a2 = a_smem ? as + (long)r * b : w.Q;
+    __syncthreads();
+    cta_proj_t(r, b, n, Us, uld, Rm, as, b);                      // a = U^T X
+    cta_rows_times<true>(n, b, r, Us, uld, as, b, Rm, -1.f);      // R -= U a
+    cta_proj_t(r, b, n, Us, uld, Rm, a2, b);                      // a2 = U^T R
+    cta_rows_times<true>(n, b, r, Us, uld, a2, b, Rm, -1.f);      // R -= U a2
+    for (int e = tid; e < r * b; e += nthr) w.a[e] = as[e] + a2[e];
     __syncthreads();
   }
-  // ----- H = R^T R (fp64), eig
-  const bool h_in_smem = smem_mat_ok && (2L * b * b <= 2L * Nmax * Nmax);
-  double* Hm = h_in_smem ? smat : w.H;
-  double* Vm = h_in_smem ? smat + b * b : w.VH;
-  cta_gram_rows(b, n, w.R, n, Hm, b);
-  int sw = cta_jacobi_eig(Hm, Vm, b, b, jac_cs, 40);
-  if (sw >= 40 && tid == 0) atomicOr(&A.status[kStatusNumeric], 1);
-  for (int j = tid; j < b; j += nthr) w.sv[j] = Hm[j * b + j];
-  __syncthreads();
-  cta_argsort_desc(w.sv, b, w.ordh);
-  // singular values in descending order; admission
+  // ----- SVD of R.  Small blocks: fp64 Gram + two-sided Jacobi, then
+  // Q = R V S^-1 made orthonormal by Cholesky-QR.  Large blocks: one-sided
+  // Jacobi directly on R (columns come out orthogonal).
+  float* cs = reinterpret_cast<float*>(smem_raw + 4 * kGemmSmemFloats + 512);
+  const int ldh = b | 1;
+  const long p1_end = (long)b * n + (long)b * b + 2L * r * b;
+  const long h_off = (p1_end + 1) & ~1L;  // 8-byte aligned for fp64
+  const bool gram_r = r_in_smem && h_off + 4L * b * ldh <= pool_floats;
+  int sw = 0;
+  if (gram_r) {
+    double* Hm = reinterpret_cast<double*>(pool + h_off);
+    double* Vd = Hm + (long)b * ldh;
+    cta_gram_cols(Rm, n, b, n, Hm, ldh);
+    sw = cta_jacobi_sym(Hm, b, ldh, Vd, ldh, cs, 40);
+    for (int j = tid; j < b; j += nthr) w.sv[j] = sqrt(fmax(Hm[j * ldh + j], 0.0));
+    for (int e = tid; e < b * b; e += nthr) {  // fp32 column-major copy of V
+      const int c = e / b, row = e % b;
+      Vh[e] = (float)Vd[row * ldh + c];
+    }
+    __syncthreads();
+    cta_argsort_desc(w.sv, b, w.ordh);
+  } else {
+    sw = cta_hestenes<32, double>(Rm, n, b, n, Vh, b, 1.2e-7f * sqrtf((float)n) + 2.4e-7f, 30);
+    cta_colnorm_order(Rm, n, b, n, w.sv, w.ordh);
+  }
+  if (sw > 30 && tid == 0) atomicOr(&A.status[kStatusNumeric], 1);
   if (tid == 0) {
     const float xnorm = (float)sqrt(s_xnorm2);
     const double tol = 100.0 * (double)FLT_EPSILON * (double)xnorm;
@@ -217,74 +539,112 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
       m = min(n, b);
     } else {
       m = 0;
-      for (int j = 0; j < b; ++j) {
-        const double lamj = w.sv[w.ordh[j]];
-        const float sj = (float)sqrt(fmax(lamj, 0.0));
-        if ((double)sj > tol) ++m;
-      }
+      for (int j = 0; j < b; ++j)
+        if ((double)(float)w.sv[w.ordh[j]] > tol) ++m;
       m = min(m, max(0, n - r));
     }
     s_m = m;
+    // a kept direction far below the largest is numerically null: its column
+    // is rounding noise and must be completed to an orthonormal direction
+    const double s0 = w.sv[w.ordh[0]];
+    int deg = 0;
+    for (int j = 0; j < m; ++j)
+      if (!(w.sv[w.ordh[j]] > 1e-6 * s0) || s0 == 0.0) deg = 1;
+    s_degenerate = deg;
   }
   __syncthreads();
   const int m = s_m;
-  // VQ[l][j] = V[l][ord_j] / s_j (fp32), j < m
-  for (int e = tid; e < b * m; e += nthr) {
-    const int l = e / m, j = e % m;
-    const int oj = w.ordh[j];
-    const double sj = sqrt(fmax(w.sv[oj], 0.0));
-    const double s0 = sqrt(fmax(w.sv[w.ordh[0]], 0.0));
-    // a direction below 1e-12 of the largest is numerically null: leave it to
-    // the orthonormal completion in cta_cgs2_rows
-    w.VQ[l * m + j] = (sj > 1e-12 * s0 && sj > 0.0) ? (float)(Vm[l * b + oj] / sj) : 0.f;
-  }
-  // V columns in sorted order for the core build (kept outside the Jacobi storage)
-  double* Vs = w.VS;
-  for (int e = tid; e < b * m; e += nthr) {
-    const int l = e / m, j = e % m;
-    Vs[l * b + j] = Vm[l * b + w.ordh[j]];
-  }
-  for (int j = tid; j < m; j += nthr) w.lam[j] = sqrt(fmax(w.sv[w.ordh[j]], 0.0));  // s_j sorted
-  __syncthreads();
-  for (int j = tid; j < m; j += nthr) w.sv[j] = w.lam[j];
-  __syncthreads();
-  // Q[j][i] = sum_l R[l][i] VQ[l][j]
-  if (m > 0) {
-    cta_gemm(m, n, b, w.VQ, 1, m, w.R, n, 1, w.Q, n, 1, 1.f, 0.f, gsm);
-    cta_cgs2_rows(w.Q, m, n, w.lam, red);
-  }
-  // ----- core Gram G = B B^T, N = r + m
-  const int N = r + m;
-  const bool g_in_smem = smem_mat_ok != 0;
-  double* Gm = g_in_smem ? smat : w.G;
-  double* VGm = g_in_smem ? smat + N * N : w.VG;
-  for (int e = tid; e < N * N; e += nthr) {
-    const int i = e / N, j = e % N;
-    if (j < i) continue;
-    double g = 0.0;
-    if (i < r && j < r) {
-      for (int l = 0; l < b; ++l) g += (double)w.a[i * b + l] * (double)w.a[j * b + l];
-      if (i == j) g += (double)sig[i] * (double)sig[i];
-    } else if (i < r) {  // j >= r
-      const int jj = j - r;
-      double t = 0.0;
-      for (int l = 0; l < b; ++l) t += (double)w.a[i * b + l] * Vs[l * b + jj];
-      g = t * (double)(float)w.sv[jj];
-    } else {
-      const int ii = i - r, jj = j - r;
-      double t = 0.0;
-      for (int l = 0; l < b; ++l) t += Vs[l * b + ii] * Vs[l * b + jj];
-      g = t * (double)(float)w.sv[ii] * (double)(float)w.sv[jj];
+  if (gram_r) {
+    // Q_j = R V[:, ord_j] / s_j
+    for (long e = tid; e < (long)m * n; e += nthr) {
+      const int j = (int)(e / n), i = (int)(e % n);
+      const int oj = w.ordh[j];
+      const double sj = w.sv[oj];
+      const float* vc = Vh + (long)oj * b;
+      float acc = 0.f;
+      for (int l = 0; l < b; ++l) acc = fmaf(Rm[(long)l * n + i], vc[l], acc);
+      w.Q[e] = sj > 0.0 ? (float)(acc / sj) : 0.f;
     }
-    Gm[i * N + j] = g;
-    Gm[j * N + i] = g;
+    __syncthreads();
+    bool ok = !s_degenerate && m > 0;
+    if (ok) ok = cta_cholqr_rows(w.Q, m, n, reinterpret_cast<double*>(pool + h_off));
+    if (!ok && m > 0) cta_cgs2_rows(w.Q, m, n, w.nrm, red);
+  } else {
+    for (long e = tid; e < (long)m * n; e += nthr) {
+      const int j = (int)(e / n), i = (int)(e % n);
+      const int oj = w.ordh[j];
+      const double sj = w.sv[oj];
+      w.Q[e] = sj > 0.0 ? (float)(Rm[(long)oj * n + i] / sj) : 0.f;
+    }
+    __syncthreads();
+    if (s_degenerate) cta_cgs2_rows(w.Q, m, n, w.nrm, red);
   }
-  __syncthreads();
-  sw = cta_jacobi_eig(Gm, VGm, N, N, jac_cs, 40);
-  if (sw >= 40 && tid == 0) atomicOr(&A.status[kStatusNumeric], 2);
-  for (int j = tid; j < N; j += nthr) w.lam[j] = Gm[j * N + j];
-  __syncthreads();
-  cta_argsort_desc(w.lam, N, w.ord);
+  // ----- the core B = [[diag(sigma), a], [0, diag(s_m) V_m^T]] ((r+m) x (r+b)):
+  // its left singular vectors W and values.  N <= 112: fp64 Gram B B^T +
+  // two-sided Jacobi; larger: one-sided Jacobi on B^T.
+  const int N = r + m, LB = r + b;
+  if (Vh != w.VH) {  // V must survive while the pool is reused
+    for (int e = tid; e < b * b; e += nthr) w.VH[e] = Vh[e];
+    __syncthreads();
+    Vh = w.VH;
+  }
+  const int ldg = N | 1;
+  const bool gram_b = N <= 112 && 4L * N * ldg <= pool_floats;
+  float* Wm = nullptr;   // one-sided path: W column-major [c*N + k]
+  double* Wd = nullptr;  // two-sided path: W row-major [k*ldg + c]
+  if (gram_b) {
+    double* Gm = reinterpret_cast<double*>(pool);
+    Wd = Gm + (long)N * ldg;
+    for (int e = tid; e < N * N; e += nthr) {
+      const int i = e / N, j = e % N;
+      if (j < i) continue;
+      double g = 0.0;
+      if (i < r && j < r) {
+        for (int l = 0; l < b; ++l) g += (double)w.a[i * b + l] * (double)w.a[j * b + l];
+        if (i == j) g += (double)sig[i] * (double)sig[i];
+      } else if (i < r) {
+        const int jj = j - r, oj = w.ordh[jj];
+        double t = 0.0;
+        for (int l = 0; l < b; ++l) t += (double)w.a[i * b + l] * (double)Vh[(long)oj * b + l];
+        g = t * (double)(float)w.sv[oj];
+      } else {
+        const int oi = w.ordh[i - r], oj = w.ordh[j - r];
+        double t = 0.0;
+        for (int l = 0; l < b; ++l) t += (double)Vh[(long)oi * b + l] * (double)Vh[(long)oj * b + l];
+        g = t * (double)(float)w.sv[oi] * (double)(float)w.sv[oj];
+      }
+      Gm[i * ldg + j] = g;
+      Gm[j * ldg + i] = g;
+    }
+    __syncthreads();
+    sw = cta_jacobi_sym(Gm, N, ldg, Wd, ldg, cs, 40);
+    for (int c = tid; c < N; c += nthr) w.nrm[c] = sqrt(fmax(Gm[c * ldg + c], 0.0));
+    __syncthreads();
+    cta_argsort_desc(w.nrm, N, w.ord);
+  } else {
+    const long bt_need = (long)N * LB + (long)N * N;
+    float* BT = bt_need <= pool_floats ? pool : w.BT;
+    Wm = bt_need <= pool_floats ? pool + (long)N * LB : w.W;
+    for (long e = tid; e < (long)N * LB; e += nthr) {
+      const int c = (int)(e / LB), row = (int)(e % LB);
+      float v = 0.f;
+      if (c < r) {
+        if (row < r) v = (row == c) ? sig[c] : 0.f;
+        else v = w.a[c * b + (row - r)];
+      } else if (row >= r) {
+        const int j = c - r;
+        v = (float)w.sv[w.ordh[j]] * Vh[(long)w.ordh[j] * b + (row - r)];
+      }
+      BT[e] = v;
+    }
+    __syncthreads();
+    const float btol = 1.2e-7f * sqrtf((float)LB) + 2.4e-7f;
+    if (LB <= 64) sw = cta_hestenes<8, float>(BT, LB, N, LB, Wm, N, btol, 30);
+    else if (LB <= 256) sw = cta_hestenes<16, float>(BT, LB, N, LB, Wm, N, btol, 30);
+    else sw = cta_hestenes<32, double>(BT, LB, N, LB, Wm, N, btol, 30);
+    cta_colnorm_order(BT, LB, N, LB, w.nrm, w.ord);
+  }
+  if (sw > 30 && tid == 0) atomicOr(&A.status[kStatusNumeric], 2);
   if (tid == 0) {
     int keep = min(cap, N);
     if (A.has_theta && N > 0) {
@@ -292,9 +652,8 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
       const float th2 = A.theta * A.theta;
       int first_ok = -1;
       float tail = 0.f;
-      // tail_sq[k] for k = N-1 .. 0
       for (int k = N - 1; k >= 0; --k) {
-        const float sk = (float)sqrt(fmax(w.lam[w.ord[k]], 0.0));
+        const float sk = (float)w.nrm[w.ord[k]];
         tail += sk * sk;
         if (tail <= th2) first_ok = k;
       }
@@ -305,28 +664,63 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
   }
   __syncthreads();
   const int keep = s_keep;
-  // WU[k][c] = VG[k][ord_c] (fp32)
+  // WU[k][c] = W[k][ord_c]
+  auto wget = [&](int k, int c) -> float {
+    return Wd ? (float)Wd[(long)k * ldg + c] : Wm[(long)c * N + k];
+  };
   for (int e = tid; e < N * keep; e += nthr) {
     const int k = e / keep, c = e % keep;
-    w.WU[k * ld + c] = (float)VGm[k * N + w.ord[c]];
+    w.WU[k * ld + c] = wget(k, w.ord[c]);
   }
-  for (int c = tid; c < keep; c += nthr) sig[c] = (float)sqrt(fmax(w.lam[w.ord[c]], 0.0));
+  for (int c = tid; c < keep; c += nthr) sig[c] = (float)w.nrm[w.ord[c]];
   float* rot = A.rot + p * A.rot_sp;
   for (int e = tid; e < keep * r; e += nthr) {
     const int c = e / r, k = e % r;
-    rot[c * ld + k] = (float)VGm[k * N + w.ord[c]];
+    rot[c * ld + k] = wget(k, w.ord[c]);
   }
   __syncthreads();
-  // U_new = U W[:r] + Q^T W[r:]
-  if (r > 0) {
-    cta_gemm(n, keep, r, U, ld, 1, w.WU, ld, 1, Uo, ld, 1, 1.f, 0.f, gsm);
-    if (m > 0) cta_gemm(n, keep, m, w.Q, 1, n, w.WU + r * ld, ld, 1, Uo, ld, 1, 1.f, 1.f, gsm);
-  } else {
-    cta_gemm(n, keep, m, w.Q, 1, n, w.WU, ld, 1, Uo, ld, 1, 1.f, 0.f, gsm);
+  // U_new = U W[:r] + Q^T W[r:]  (one thread per basis row)
+  {
+    constexpr int CB = 16;
+    for (int i = tid; i < n; i += nthr) {
+      const float* ur = U + (long)i * ld;
+      for (int c0 = 0; c0 < keep; c0 += CB) {
+        float acc[CB];
+#pragma unroll
+        for (int cc = 0; cc < CB; ++cc) acc[cc] = 0.f;
+        const int cn = min(CB, keep - c0);
+        for (int k = 0; k < r; ++k) {
+          const float uv = ur[k];
+          const float* wr = w.WU + (long)k * ld + c0;
+#pragma unroll
+          for (int cc = 0; cc < CB; ++cc)
+            if (cc < cn) acc[cc] = fmaf(uv, wr[cc], acc[cc]);
+        }
+        for (int j = 0; j < m; ++j) {
+          const float qv = w.Q[(long)j * n + i];
+          const float* wr = w.WU + (long)(r + j) * ld + c0;
+#pragma unroll
+          for (int cc = 0; cc < CB; ++cc)
+            if (cc < cn) acc[cc] = fmaf(qv, wr[cc], acc[cc]);
+        }
+        float* uo = Uo + (long)i * ld + c0;
+#pragma unroll
+        for (int cc = 0; cc < CB; ++cc)
+          if (c0 + cc < keep) uo[cc] = acc[cc];
+      }
+    }
+    __syncthreads();
   }
-  // coords[j][c] = sum_i X[j][i] U_new[i][c]
+  // coords[j][c] = sum_i U_new[i][c] X[j][i]
   float* co = A.coords + p * A.coords_sp;
-  cta_gemm(b, keep, n, X, n, 1, Uo, ld, 1, co, A.coords_ld, 1, 1.f, 0.f, gsm);
+  {
+    float* ct = (r_in_smem && (long)keep * b <= pool_floats) ? pool : w.a;
+    cta_proj_t(keep, b, n, Uo, ld, X, ct, b);
+    for (int e = tid; e < keep * b; e += nthr) {
+      const int c = e / b, j = e % b;
+      co[(long)j * A.coords_ld + c] = ct[e];
+    }
+  }
   if (tid == 0) {
     int* d = A.dims + 4 * p;
     d[0] = r; d[1] = keep; d[2] = m; d[3] = sw;
@@ -463,28 +857,35 @@ namespace kvd_host {
 
 using namespace kvd;
 
-int step_smem_bytes(int b, int ld, bool with_mats) {
-  const int Nmax = ld + b;
-  long bytes = 4L * kGemmSmemFloats + 8L * 4 * (Nmax / 2 + 2) + 8L * 64;
-  if (with_mats) bytes += 16L * Nmax * Nmax;
-  return (int)bytes;
-}
-
 long bug_step_ws_per_problem(int n, int b, int ld) { return align16(step_ws_bytes(n, b, ld)); }
+
+// Shared memory a step would like: gemm scratch + misc + the larger of the
+// residual phase (R and V_h) and the core phase (V_h, B^T and W).
+static long step_smem_want(int n, int b, int ld) {
+  const long N = ld + b, LB = ld + b;
+  const long phase1 = (long)b * n + (long)b * b;
+  const long phase2 = (long)b * b + N * LB + N * N;
+  return 4L * kGemmSmemFloats + kStepMiscBytes + 4L * (phase1 > phase2 ? phase1 : phase2);
+}
 
 int launch_bug_step(const BugStepBatch& batch, int n_problems, int n_streams, cudaStream_t stream) {
   const BugStepArgs& a0 = batch.s[0];
-  int smem = step_smem_bytes(a0.b, a0.ld, true);
-  int ok = 1;
-  if (smem > 200 * 1024) {  // Jacobi matrices stay in global workspace
-    smem = step_smem_bytes(a0.b, a0.ld, false);
-    ok = 0;
+  static int max_dyn = 0;
+  if (!max_dyn) {
+    cudaFuncAttributes attr;
+    int dev = 0, optin = 0;
+    cudaFuncGetAttributes(&attr, (const void*)bug_step_kernel);
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    max_dyn = optin - (int)attr.sharedSizeBytes;
   }
+  long want = step_smem_want(a0.n, a0.b, a0.ld);
+  const int smem = (int)(want < max_dyn ? want : max_dyn);
   if (int rc = ensure_smem((const void*)bug_step_kernel, smem, "bug_step_kernel")) return rc;
   dim3 grid(n_problems, n_streams);
   {
     KTimerScope kts_("bug_step_kernel", stream);
-    bug_step_kernel<<<grid, kStepThreads, smem, stream>>>(batch, ok);
+    bug_step_kernel<<<grid, kStepThreads, smem, stream>>>(batch, smem);
   }
   return check_launch("bug_step_kernel");
 }

@@ -76,127 +76,18 @@ static __device__ void cta_gemm(int M, int N, int K, const float* A, long sam, l
   }
 }
 
-// G = X X^T in fp64 for the `rows` row vectors X[j][0..len) (row stride ldx),
-// G row-major with leading dimension ldg; one warp per (j1 <= j2) pair.
-static __device__ void cta_gram_rows(int rows, int len, const float* X, long ldx, double* G, int ldg) {
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, nw = blockDim.x / 32;
-  const int pairs = rows * (rows + 1) / 2;
-  for (int e = warp; e < pairs; e += nw) {
-    // unrank e -> (j1, j2), j1 <= j2, row-major over the upper triangle
-    int j1 = 0, rem = e;
-    while (rem >= rows - j1) { rem -= rows - j1; ++j1; }
-    const int j2 = j1 + rem;
-    const float* x1 = X + j1 * ldx;
-    const float* x2 = X + j2 * ldx;
-    double acc = 0.0;
-    for (int i = lane; i < len; i += 32) acc += (double)x1[i] * (double)x2[i];
-    acc = warp_sum(acc);
-    if (lane == 0) { G[j1 * ldg + j2] = acc; G[j2 * ldg + j1] = acc; }
-  }
-  __syncthreads();
-}
-
-// Round-robin (circle method) partner of slot i in round k for N' players.
+// Round-robin (circle method) partner of slot i in round k for N' players
+// (player 0 fixed, the others rotate by k; 0 <= k < np - 1).
 KVD_DEVICE void rr_pair(int i, int k, int np, int* a, int* b) {
-  auto idx = [&](int j) { return j == 0 ? 0 : ((j - 1 + k) % (np - 1)) + 1; };
+  const int m = np - 1;
+  auto idx = [&](int j) {
+    if (j == 0) return 0;
+    int t = j - 1 + k;
+    if (t >= m) t -= m;
+    return t + 1;
+  };
   *a = idx(i);
   *b = idx(np - 1 - i);
-}
-
-// Cyclic two-sided Jacobi eigensolver for a symmetric N x N fp64 matrix A
-// (leading dimension ld).  On exit A is (numerically) diagonal, V holds the
-// eigenvectors (columns), and the function returns the number of sweeps it
-// took (> max_sweeps when it did not converge).  `cs` needs 4*(N/2+1) doubles
-// of shared memory.  Rotations follow Golub & Van Loan, Alg. 8.4.2 (sym.schur2),
-// applied to N'/2 disjoint pairs per round in parallel.
-static __device__ int cta_jacobi_eig(double* A, double* V, int N, int ld, double* cs, int max_sweeps) {
-  __shared__ int s_rotated;
-  const int tid = threadIdx.x, nthr = blockDim.x;
-  for (int e = tid; e < N * N; e += nthr) {
-    const int i = e / N, j = e % N;
-    V[i * ld + j] = (i == j) ? 1.0 : 0.0;
-  }
-  __syncthreads();
-  if (N <= 1) return 0;
-  // Scale of the matrix (largest diagonal magnitude): entries below ~1e-17 of
-  // it are rounding noise and never rotated, so rank-deficient PSD matrices
-  // (null blocks full of noise) converge too.
-  __shared__ double s_scale;
-  if (tid == 0) {
-    double m = 0.0;
-    for (int i = 0; i < N; ++i) m = fmax(m, fabs(A[i * ld + i]));
-    s_scale = m;
-  }
-  __syncthreads();
-  const double floor_rot = 1e-17 * s_scale, floor_flag = 1e-14 * s_scale;
-  const int np = N + (N & 1);
-  const int half = np / 2;
-  double* pc = cs;            // cos
-  double* ps = cs + half;     // sin
-  int* pidx = reinterpret_cast<int*>(cs + 2 * half);  // p, q per pair (2*half ints)
-  int sweep = 0;
-  for (; sweep < max_sweeps; ++sweep) {
-    if (tid == 0) s_rotated = 0;
-    __syncthreads();
-    for (int k = 0; k < np - 1; ++k) {
-      for (int i = tid; i < half; i += nthr) {
-        int a, b;
-        rr_pair(i, k, np, &a, &b);
-        int p = a < b ? a : b, q = a < b ? b : a;
-        double c = 1.0, s = 0.0;
-        if (q < N) {
-          const double apq = A[p * ld + q];
-          const double app = A[p * ld + p], aqq = A[q * ld + q];
-          const double thr = fmax(1e-15 * sqrt(fabs(app * aqq)), floor_rot);
-          if (apq != 0.0 && fabs(apq) > thr) {
-            const double tau = (aqq - app) / (2.0 * apq);
-            const double t = (tau >= 0.0) ? 1.0 / (tau + sqrt(1.0 + tau * tau))
-                                          : -1.0 / (-tau + sqrt(1.0 + tau * tau));
-            c = 1.0 / sqrt(1.0 + t * t);
-            s = t * c;
-            if (fabs(apq) > fmax(4e-15 * sqrt(fabs(app * aqq)), floor_flag)) s_rotated = 1;
-          }
-        } else {
-          q = -1;
-        }
-        pc[i] = c; ps[i] = s; pidx[2 * i] = p; pidx[2 * i + 1] = q;
-      }
-      __syncthreads();
-      // rows: A <- J^T A
-      for (int e = tid; e < half * N; e += nthr) {
-        const int i = e / N, j = e % N;
-        const int q = pidx[2 * i + 1];
-        const double s = ps[i];
-        if (q < 0 || s == 0.0) continue;
-        const int p = pidx[2 * i];
-        const double c = pc[i];
-        const double x = A[p * ld + j], y = A[q * ld + j];
-        A[p * ld + j] = c * x - s * y;
-        A[q * ld + j] = s * x + c * y;
-      }
-      __syncthreads();
-      // columns: A <- A J, V <- V J
-      for (int e = tid; e < half * N; e += nthr) {
-        const int i = e / N, j = e % N;
-        const int q = pidx[2 * i + 1];
-        const double s = ps[i];
-        if (q < 0 || s == 0.0) continue;
-        const int p = pidx[2 * i];
-        const double c = pc[i];
-        const double x = A[j * ld + p], y = A[j * ld + q];
-        A[j * ld + p] = c * x - s * y;
-        A[j * ld + q] = s * x + c * y;
-        const double vx = V[j * ld + p], vy = V[j * ld + q];
-        V[j * ld + p] = c * vx - s * vy;
-        V[j * ld + q] = s * vx + c * vy;
-      }
-      __syncthreads();
-    }
-    const int rot = s_rotated;
-    __syncthreads();
-    if (!rot) break;
-  }
-  return sweep;
 }
 
 // order[0..N) = indices of vals sorted descending, ties by lower index.
