@@ -135,36 +135,68 @@ def new_cache(w: dict, torch):
         retention="lowrank_surprise", hh_budget=w["hh"], hh_select="surprise")
 
 
-def schedule_widths(w: dict) -> list[dict]:
-    """Counters before each decode step (mirrors the cache schedule: exact tier
-    full, every graduating block demotes `absorb` columns)."""
-    T, ring, b, sinks, hh = w["tokens"], w["ring"], w["absorb"], w["sinks"], w["hh"]
-    # After ingest (chunk sizes are multiples of the absorb block) the ring is
-    # back at `ring` tokens and every other token is a sink, in the exact tier
-    # or a coordinate column.
-    rl = ring
-    W = T - sinks - ring - hh
-    out = []
+def kernel_bytes(w: dict) -> dict[str, float]:
+    """Algorithmic HBM bytes of one bench step, per kernel, from a replay of
+    the cache's absorb schedule (every length decision is count-driven).
+
+    Per launch, with P = layers problems, n = H*D, bf16 tiers (2 B), fp32 state:
+      bug_step      2 streams x P x (read U n*r*4 + block b*n*4 + write U' n*r*4
+                    + coords b*r*4)
+      slash_score   P x (read candidates m*n*2 + basis n*r*4 + scores m*4)
+      slash_select  P x (read candidates K,V 2*m*n*2 + write tier 2*h*n*2
+                    + demoted block 2*d*n*4)
+      carry         2 x P x W*r*4*2 (read + write the coordinates)
+      mid_hat       P x (read C_k, C_v 2*W*r*4 + write K, V 2*W*n*2)
+      decode        P x (C_k, C_v 2*W*r*4 + positions W*4 + U_k, U_v 2*n*r*4
+                    + verbatim tiers 2*n*(hh+ring+sinks)*2 + q/out)
+    """
+    L, H, D, r = w["layers"], w["kv_heads"], w["head_dim"], w["rank"]
+    n, T, C = H * D, w["tokens"], w["chunk"]
+    sinks, ring, b, h, pbs = w["sinks"], w["ring"], w["absorb"], w["hh"], w["prefill_block"]
+    out = {k: 0.0 for k in ("bug_step_kernel", "slash_score_kernel", "slash_select_kernel",
+                            "carry_kernel", "mid_hat_kernel", "decode_split_kernel")}
+    rk, W, hh, rl, cum = 0, 0, 0, 0, 0
+
+    def bug(bb: int) -> None:
+        nonlocal rk, W
+        out["bug_step_kernel"] += 2 * L * (2 * n * r * 4 + bb * n * 4 + bb * r * 4)
+        if W > 0:
+            out["carry_kernel"] += 2 * L * W * r * 4 * 2
+        rk = min(r, rk + bb)
+        W += bb
+
+    def absorb() -> None:
+        nonlocal hh
+        m = hh + b
+        keep = min(h, m)
+        d = m - keep
+        out["slash_score_kernel"] += L * (m * n * 2 + n * r * 4 + m * 4)
+        out["slash_select_kernel"] += L * (2 * m * n * 2 + 2 * keep * n * 2 + 2 * d * n * 4)
+        hh = keep
+        if d:
+            bug(d)
+
+    # first chunk: sinks, ring, the middle absorbed directly in sub-blocks
+    mid = C - sinks - ring
+    for s0 in range(0, mid, pbs):
+        bug(min(pbs, mid - s0))
+    rl, cum = ring, C
+    for _ in range(C, T, C):
+        rl += C
+        cum += C
+        out["mid_hat_kernel"] += L * (2 * W * r * 4 + 2 * W * n * 2)
+        while rl >= ring + b:
+            rl -= b
+            absorb()
     for _ in range(w["decode"]):
         rl += 1
-        if rl >= ring + b:
+        while rl >= ring + b:
             rl -= b
-            W += b
-        out.append({"W": W, "hh": hh, "ring": rl, "sinks": sinks})
+            absorb()
+        exact = hh + rl + sinks
+        out["decode_split_kernel"] += L * (2 * W * r * 4 + W * 4 + 2 * n * r * 4 + 2 * n * exact * 2
+                                           + 2 * 2 * w["q_heads"] * D)
     return out
-
-
-def decode_bytes(w: dict, st: dict) -> float:
-    """Algorithmic HBM bytes of one factored-decode launch over all layers:
-    coordinates C_k, C_v (fp32) and positions of the middle, the basis rows
-    U_k (read per KV group), the verbatim tiers (bf16 K and V), queries and
-    outputs."""
-    L, H, D, r = w["layers"], w["kv_heads"], w["head_dim"], w["rank"]
-    n = H * D
-    exact = st["hh"] + st["ring"] + st["sinks"]
-    per_layer = (2 * 4 * r * st["W"] + 4 * st["W"] + 2 * 4 * n * r + 2 * 2 * n * exact
-                 + 2 * 2 * w["q_heads"] * D)
-    return float(L * per_layer)
 
 
 def run_ours(args, w: dict) -> None:
@@ -277,20 +309,22 @@ def run_ours(args, w: dict) -> None:
     if rank == 0:
         peaks, peak_kind = _peaks()
         dom = max(prof.items(), key=lambda kv: kv[1][0])[0] if prof else None
-        sched = schedule_widths(w)
-        dec_ms, dec_n = prof.get("decode_split_kernel", (0.0, 0))
-        merge_ms, _ = prof.get("decode_merge_kernel", (0.0, 0))
-        dec_bytes = sum(decode_bytes(w, st) for st in sched)
-        achieved = dec_bytes / ((dec_ms + merge_ms) / 1e3) / 1e9 if dec_ms else None
-        roof = {"kernel": "decode_split_kernel+decode_merge_kernel", "bound": "hbm",
-                "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                "frac": (achieved / peaks["hbm_gbs"]) if achieved else None,
-                "peak_source": peak_kind, "traffic": None,
-                "bytes_per_launch": dec_bytes / max(1, dec_n),
-                "avg_launch_ms": (dec_ms + merge_ms) / max(1, dec_n)}
-        kernels = {k: {"total_ms": round(v[0], 4), "launches": v[1],
-                       "share": round(v[0] / max(1e-9, sum(x[0] for x in prof.values())), 4)}
-                   for k, v in sorted(prof.items(), key=lambda kv: -kv[1][0])}
+        kb = kernel_bytes(w)
+        peak = peaks["hbm_gbs"]
+
+        def roof(name: str) -> dict:
+            ms, launches = prof.get(name, (0.0, 0))
+            if name == "decode_split_kernel":  # split + merge form one decode op
+                ms += prof.get("decode_merge_kernel", (0.0, 0))[0]
+            nbytes = kb.get(name)
+            ach = nbytes / (ms / 1e3) / 1e9 if (nbytes and ms) else None
+            return {"kernel": name, "bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s",
+                    "frac": (ach / peak) if ach else None, "peak_source": peak_kind,
+                    "traffic": None, "bytes_per_launch": (nbytes / launches) if (nbytes and launches) else None,
+                    "avg_launch_ms": (ms / launches) if launches else None}
+
+        roof_all = {k: roof(k) for k in kb if k in prof}
+        roof_dom = roof_all.get(dom) or roof("decode_split_kernel")
         cpu = cpu_baseline(w, quick=True)
         result = {
             "metric": METRIC,
@@ -316,7 +350,8 @@ def run_ours(args, w: dict) -> None:
             "decode_ms_per_step": decode_ms / args.steps,
             "e2e": e2e,
             "gpu_launches": int(launches_total * args.steps),
-            "roofline": roof,
+            "roofline": roof_dom,
+            "roofline_all": roof_all,
             "dominant_kernel": dom,
             "kernels": kernels,
             "cpu_baseline": cpu,
