@@ -179,6 +179,20 @@ int kvd_bug_step(int32_t n_batch, int32_t n, int32_t b, int32_t rank_cap, int32_
                  kvd_stream_t stream);
 size_t kvd_bug_step_workspace_bytes(int32_t n_batch, int32_t n, int32_t b, int32_t ld_u);
 
+/* kvd_bug_step for callers that cannot allocate device memory (no
+ * counterpart in the reference, which has no compiled code): the same step
+ * with no workspace argument.  Its scratch is a fixed 16 MiB array inside the
+ * library (kvd_bug_step_noalloc_max_scratch()), held on every GPU that loads
+ * the library; requests that need more return KVD_ERR_WORKSPACE.  The first
+ * call on a device looks up the array's device address, so make it before any
+ * stream capture.  Calls share the array: calls that overlap on the GPU race
+ * and must be serialised by the caller.  Allocates nothing. */
+int kvd_bug_step_noalloc(int32_t n_batch, int32_t n, int32_t b, int32_t rank_cap, int32_t ld_u,
+                         const float* u, float* u_out, float* sigma, int32_t* r,
+                         const float* block, float* rot_out, int32_t* m_out, float* coords_out,
+                         int32_t has_theta, float theta, int32_t* status, kvd_stream_t stream);
+size_t kvd_bug_step_noalloc_max_scratch(void);
+
 /* Low-rank surprise of token-major fp32 columns x [nb][m][n] against bases
  * u [nb][n][ld_u] of rank r[nb]: sqrt(max(|k|^2-|U^T k|^2,0))/max(|k|,1e-12),
  * 1.0 where r == 0.  bug_cache.py:906-921. */
