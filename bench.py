@@ -325,6 +325,9 @@ def run_ours(args, w: dict) -> None:
 
         roof_all = {k: roof(k) for k in kb if k in prof}
         roof_dom = roof_all.get(dom) or roof("decode_split_kernel")
+        total_ms = sum(x[0] for x in prof.values()) or 1e-9
+        kernels = {k: {"total_ms": round(v[0], 4), "launches": v[1], "share": round(v[0] / total_ms, 4)}
+                   for k, v in sorted(prof.items(), key=lambda kv: -kv[1][0])}
         cpu = cpu_baseline(w, quick=True)
         result = {
             "metric": METRIC,

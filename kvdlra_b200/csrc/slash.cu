@@ -20,7 +20,7 @@ namespace kvd {
 constexpr int kScoreTile = 32;   // candidates per CTA
 constexpr int kScoreMaxQ = 24;   // rank <= 8 * 24 = 192
 
-template <typename T>
+template <typename T, int QN>
 __global__ void __launch_bounds__(256) slash_score_kernel(CandSrc<T> src, int m, int H, int D,
                                                           RopeArgs rope, const float* u, long u_sp,
                                                           int ld, const int* rr, float* scores,
@@ -44,9 +44,9 @@ __global__ void __launch_bounds__(256) slash_score_kernel(CandSrc<T> src, int m,
     cs[2 * e] = c;
     cs[2 * e + 1] = s;
   }
-  double acc[kScoreMaxQ];
+  double acc[QN];
 #pragma unroll
-  for (int q = 0; q < kScoreMaxQ; ++q) acc[q] = 0.0;
+  for (int q = 0; q < QN; ++q) acc[q] = 0.0;
   double kk = 0.0;
   const float* U = u + p * u_sp;
   for (int h = 0; h < H; ++h) {
@@ -79,7 +79,7 @@ __global__ void __launch_bounds__(256) slash_score_kernel(CandSrc<T> src, int m,
         const double kv = (double)krow[d];
         const float* ur = us + d * r;
 #pragma unroll
-        for (int q = 0; q < kScoreMaxQ; ++q) {
+        for (int q = 0; q < QN; ++q) {
           const int k = sub + 8 * q;
           if (k < r) acc[q] += (double)ur[k] * kv;
         }
@@ -88,7 +88,7 @@ __global__ void __launch_bounds__(256) slash_score_kernel(CandSrc<T> src, int m,
   }
   double cc = 0.0;
 #pragma unroll
-  for (int q = 0; q < kScoreMaxQ; ++q) cc += acc[q] * acc[q];
+  for (int q = 0; q < QN; ++q) cc += acc[q] * acc[q];
 #pragma unroll
   for (int o = 4; o > 0; o >>= 1) {
     cc += __shfl_xor_sync(0xffffffffu, cc, o);
@@ -163,11 +163,27 @@ __global__ void __launch_bounds__(1024) slash_select_kernel(CandSrc<T> src, int 
   // kept tokens -> new exact tier (verbatim, chronological)
   T* ok = reinterpret_cast<T*>(out.hh_k) + p * out.hh_sp;
   T* ov = reinterpret_cast<T*>(out.hh_v) + p * out.hh_sp;
-  for (long e = threadIdx.x; e < (long)keep_n * n; e += blockDim.x) {
-    const int slot = (int)(e / n), i = (int)(e % n);
-    const int jsrc = keep_src[slot];
-    ok[e] = src.krow(p, jsrc)[i];
-    ov[e] = src.vrow(p, jsrc)[i];
+  // one warp per kept row, 16-byte vector copies plus a scalar tail
+  {
+    const int lane = threadIdx.x % 32, warp = threadIdx.x / 32, nw = blockDim.x / 32;
+    const int vec = (int)((n * sizeof(T)) / 16);
+    for (int slot = warp; slot < keep_n; slot += nw) {
+      const int jsrc = keep_src[slot];
+      const T* kss = src.krow(p, jsrc);
+      const T* vss = src.vrow(p, jsrc);
+      const uint4* ks = reinterpret_cast<const uint4*>(kss);
+      const uint4* vs = reinterpret_cast<const uint4*>(vss);
+      uint4* kd = reinterpret_cast<uint4*>(ok + (long)slot * n);
+      uint4* vd = reinterpret_cast<uint4*>(ov + (long)slot * n);
+      for (int e = lane; e < vec; e += 32) {
+        kd[e] = ks[e];
+        vd[e] = vs[e];
+      }
+      for (int i = vec * (int)(16 / sizeof(T)) + lane; i < n; i += 32) {
+        ok[(long)slot * n + i] = kss[i];
+        ov[(long)slot * n + i] = vss[i];
+      }
+    }
   }
   for (int slot = threadIdx.x; slot < keep_n; slot += blockDim.x)
     out.hh_pos[p * out.hh_pos_sp + slot] = src.pos(p, keep_src[slot]);
@@ -186,9 +202,13 @@ __global__ void __launch_bounds__(1024) slash_select_kernel(CandSrc<T> src, int 
     xk[(long)slot * n + h * D + f] = (x1 * c + x2 * s) / rope.scale_sq;
     xk[(long)slot * n + h * D + f + half] = (x2 * c - x1 * s) / rope.scale_sq;
   }
-  for (long e = threadIdx.x; e < (long)d * n; e += blockDim.x) {
-    const int slot = (int)(e / n), i = (int)(e % n);
-    xv[e] = load_f<T>(src.vrow(p, dem_src[slot]) + i);
+  {
+    const int lane = threadIdx.x % 32, warp = threadIdx.x / 32, nw = blockDim.x / 32;
+    for (int slot = warp; slot < d; slot += nw) {
+      const T* vr = src.vrow(p, dem_src[slot]);
+      float* xo = xv + (long)slot * n;
+      for (int i = lane; i < n; i += 32) xo[i] = load_f<T>(vr + i);
+    }
   }
   for (int slot = threadIdx.x; slot < d; slot += blockDim.x) {
     const int jsrc = dem_src[slot];
@@ -345,12 +365,19 @@ int launch_slash_score(const CandSrc<T>& src, int P, int m, int H, int D, RopeAr
   }
   const int half = D / 2;
   const int smem = 4 * (kScoreTile * half * 2 + kScoreTile * D + D * ld);
-  if (int rc = ensure_smem((const void*)slash_score_kernel<T>, smem, "slash_score_kernel")) return rc;
   dim3 grid((m + kScoreTile - 1) / kScoreTile, P);
-  {
+  auto go = [&](auto kern) -> int {
+    if (int rc = ensure_smem((const void*)kern, smem, "slash_score_kernel")) return rc;
     KTimerScope kts_("slash_score_kernel", stream);
-    slash_score_kernel<T><<<grid, 256, smem, stream>>>(src, m, H, D, rope, u, u_sp, ld, rr, scores, sc_sp);
-  }
+    kern<<<grid, 256, smem, stream>>>(src, m, H, D, rope, u, u_sp, ld, rr, scores, sc_sp);
+    return KVD_OK;
+  };
+  int rc;
+  if (ld <= 32) rc = go(slash_score_kernel<T, 4>);
+  else if (ld <= 64) rc = go(slash_score_kernel<T, 8>);
+  else if (ld <= 128) rc = go(slash_score_kernel<T, 16>);
+  else rc = go(slash_score_kernel<T, 24>);
+  if (rc) return rc;
   return check_launch("slash_score_kernel");
 }
 

@@ -88,7 +88,8 @@ __global__ void hf_to_hf_kernel(const T* k, const T* v, long sb, long sh, long s
 }
 
 // Middle reconstruction: K = RoPE(U_k c_t) at pos_t, V = U_v c_v,t for 32
-// coordinate columns per CTA, written to HF rows [l0, l0+W).
+// coordinate columns per CTA, written to HF rows [l0, l0+W).  The basis rows of
+// one head are staged transposed ([c][d]) so a warp reads 32 consecutive d.
 constexpr int kMidTile = 32;
 
 template <typename T>
@@ -107,9 +108,9 @@ __global__ void __launch_bounds__(256) mid_hat_kernel(const float* uk, const flo
   const int half = D / 2;
   float* ctk = msm;                        // [tile][ld]
   float* ctv = ctk + kMidTile * ld;        // [tile][ld]
-  float* usk = ctv + kMidTile * ld;        // [D][ld]
-  float* usv = usk + D * ld;               // [D][ld]
-  float* cs = usv + D * ld;                // [tile][half][2]
+  float* ukT = ctv + kMidTile * ld;        // [ld][D]
+  float* uvT = ukT + D * ld;               // [ld][D]
+  float* cs = uvT + D * ld;                // [tile][half][2]
   for (int e = threadIdx.x; e < cnt * ld; e += blockDim.x) {
     const int t = e / ld, c = e % ld;
     ctk[e] = c < r_k ? ck[p * c_sp + (long)(t0 + t) * ld + c] : 0.f;
@@ -125,25 +126,29 @@ __global__ void __launch_bounds__(256) mid_hat_kernel(const float* uk, const flo
   }
   const float* Uk = uk + p * u_sp;
   const float* Uv = uv + p * u_sp;
+  const int rmax = max(r_k, r_v);
   for (int h = 0; h < H; ++h) {
     __syncthreads();
     for (int e = threadIdx.x; e < D * ld; e += blockDim.x) {
-      const int d = e / ld, c = e % ld;
-      usk[e] = c < r_k ? Uk[(long)(h * D + d) * ld + c] : 0.f;
-      usv[e] = c < r_v ? Uv[(long)(h * D + d) * ld + c] : 0.f;
+      const int d = e / ld, c = e % ld;  // coalesced global read along c
+      ukT[c * D + d] = c < r_k ? Uk[(long)(h * D + d) * ld + c] : 0.f;
+      uvT[c * D + d] = c < r_v ? Uv[(long)(h * D + d) * ld + c] : 0.f;
     }
     __syncthreads();
     for (int e = threadIdx.x; e < cnt * half; e += blockDim.x) {
       const int t = e / half, f = e % half;
       const float* ckt = ctk + t * ld;
       const float* cvt = ctv + t * ld;
-      const float* u1 = usk + f * ld;
-      const float* u2 = usk + (f + half) * ld;
-      const float* w1 = usv + f * ld;
-      const float* w2 = usv + (f + half) * ld;
       float k1 = 0.f, k2 = 0.f, v1 = 0.f, v2 = 0.f;
-      for (int c = 0; c < r_k; ++c) { k1 = fmaf(u1[c], ckt[c], k1); k2 = fmaf(u2[c], ckt[c], k2); }
-      for (int c = 0; c < r_v; ++c) { v1 = fmaf(w1[c], cvt[c], v1); v2 = fmaf(w2[c], cvt[c], v2); }
+      for (int c = 0; c < rmax; ++c) {
+        const float a = ckt[c], bv = cvt[c];
+        const float* uk_c = ukT + c * D;
+        const float* uv_c = uvT + c * D;
+        k1 = fmaf(uk_c[f], a, k1);
+        k2 = fmaf(uk_c[f + half], a, k2);
+        v1 = fmaf(uv_c[f], bv, v1);
+        v2 = fmaf(uv_c[f + half], bv, v2);
+      }
       float y1, y2;
       rope_apply_pair(k1, k2, cs[2 * e], cs[2 * e + 1], &y1, &y2);
       const long o = p * ob + h * oh + (long)(l0 + t0 + t) * ot;
