@@ -2,14 +2,19 @@
 //
 // Restates src/kvdlra/integrators/streaming_torch.py:82-189 for a batch of
 // independent problems (one CTA per problem x stream):
-//   a = U^T X ; R = X - U a ; a2 = U^T R ; R -= U a2 ; a += a2   (fp32 FFMA)
+//   a = U^T X ; R = X - U a ; a2 = U^T R ; R -= U a2 ; a += a2   (fp32 FFMA,
+//     K-split with fp64 sums of the split partials)
 //   one-sided Jacobi on R (n x b): R V = [s_j q_j]  -> singular values s,
-//     orthonormal left vectors q_j, right vectors V; admit s > 100 eps |X|_F,
-//     at most n - r of them
+//     left vectors q_j, right vectors V; admit s > 100 eps |X|_F, at most
+//     n - r of them
 //   one-sided Jacobi on B^T, B = [[diag(sigma), a], [0, diag(s_m) V_m^T]]
-//     ((r+m) x (r+b)):  B^T W = [sigma'_c w_c]  -> W = left singular vectors
+//     ((r+m) x (r+b)):  B^T W = [sigma'_c z_c]  -> W = left singular vectors
 //     of B (u_loc), sigma' its singular values
-//   U_new = [U | Q] W[:, top keep], rot = W[:r, top keep]^T, coords = U_new^T X.
+//   U_new = [U | Q] W[:, top keep], rot = W[:r, top keep]^T, and the block's
+//     coordinates U_new^T X = W^T B[:, r:], read off the rotated B^T.
+// U_new is then brought back to orthonormal columns by one Newton-Schulz
+// step U <- U (I - (U^T U - I)/2) with an fp64-summed Gram, so rounding and
+// the Jacobi stopping tolerance cannot accumulate over a long stream.
 // One-sided (Hestenes) Jacobi never forms a Gram matrix, so it keeps the
 // relative accuracy of a direct SVD; all rotations of a round touch disjoint
 // columns, so a round costs one barrier.
@@ -21,81 +26,49 @@
 
 namespace kvd {
 
-struct StepWs {
-  float* a;      // [ld][b]   coordinates of the block in the old basis
-  float* R;      // [b][n]    residual, then sigma-scaled left vectors
-  float* Q;      // [b][n]    admitted orthonormal residual directions
-  float* VH;     // [b][b]    right singular vectors of R (column-major)
-  float* BT;     // [N][N+b]  B^T (column-major, ld = ld + b)   (global fallback)
-  float* W;      // [N][N]    rotations of B^T (column-major)    (global fallback)
-  double* nrm;   // [N]
-  int* ord;      // [N]
-  int* ordh;     // [b]
-  double* sv;    // [b]
-  float* WU;     // [N][ld]   top left singular vectors of B (row-major)
-};
-
 __host__ __device__ inline long align16(long x) { return (x + 15) & ~15L; }
 
-__host__ __device__ inline long step_ws_bytes(int n, int b, int ld) {
-  const long N = ld + b, LB = ld + b;
-  long o = 0;
-  o += align16(4L * ld * b);
-  o += align16(4L * b * n) * 2;
-  o += align16(4L * b * b);
-  o += align16(4L * N * LB);
-  o += align16(4L * N * N);
-  o += align16(8L * N);
-  o += align16(4L * N);
-  o += align16(4L * b);
-  o += align16(8L * b);
-  o += align16(4L * N * ld);
-  return o;
-}
-
-__device__ StepWs carve(char* base, int n, int b, int ld) {
-  const long N = ld + b, LB = ld + b;
-  StepWs w;
-  long o = 0;
-  auto take = [&](long bytes) { char* p = base + o; o += align16(bytes); return p; };
-  w.a = (float*)take(4L * ld * b);
-  w.R = (float*)take(4L * b * n);
-  w.Q = (float*)take(4L * b * n);
-  w.VH = (float*)take(4L * b * b);
-  w.BT = (float*)take(4L * N * LB);
-  w.W = (float*)take(4L * N * N);
-  w.nrm = (double*)take(8L * N);
-  w.ord = (int*)take(4L * N);
-  w.ordh = (int*)take(4L * b);
-  w.sv = (double*)take(8L * b);
-  w.WU = (float*)take(4L * N * ld);
-  return w;
-}
-
-constexpr int kGemmSmemFloats = 2 * 16 * 64;
 constexpr int kStepThreads = 512;
-constexpr int kStepMiscBytes = 4096;
+constexpr int kStepMiscBytes = 1024;   // fp64 reduction scratch
+constexpr int kPartFloats = 8192;      // K-split partials: 16 warps x 32 lanes x 16
+constexpr int kMaxStepLd = 512;        // basis width the K-split partials cover
 
 // One-sided (Hestenes) Jacobi: orthogonalise the `cols` columns of X (column
 // c at X + c*ldx, `len` rows) by plane rotations, accumulated into V
 // (cols x cols, column-major, ldv; initialised to I here).  Round-robin
-// ordering; each column pair is handled by a group of G lanes (all pairs of a
-// round run concurrently), one barrier per round.  The rotation zeroes the
-// pair's inner product (Golub & Van Loan sec. 8.6.3).  ACC is the type the
-// 2x2 Gram of a pair is accumulated in.  Returns the sweeps taken
-// (max_sweeps + 1 when not converged).
-template <int G, typename ACC>
+// ordering; each column pair is handled by a group of G lanes that keeps the
+// pair's two columns in registers: lane gl holds the 4-float units
+// gl, gl + G, ... (EPL values, len <= G*EPL), so a group reads contiguous
+// 16-byte runs.  EPL = 0 streams longer columns from shared memory instead.
+// Only the warps that own a pair in a round issue anything, and the group
+// count per warp (32/G) is chosen by the caller to keep about four warps
+// busy, since a round is issue-bound.  The rotation zeroes the pair's inner
+// product (Golub & Van Loan sec. 8.6.3); its parameters come from the fast
+// reciprocal square root and are renormalised by one Newton step so
+// c^2 + s^2 = 1 to rounding (an inexact angle only slows convergence).  A
+// lane sums its own values in fp32 and the group reduces in ACC.
+// inv_scale2 is 1 / (squared Frobenius scale of the problem).  Returns the
+// sweeps taken (max_sweeps when not converged).
+constexpr double kJacobiFloor = 1e-30;
+
+template <int G, int EPL, typename ACC>
 static __device__ int cta_hestenes(float* X, int len, int cols, int ldx, float* V, int ldv,
-                                   float tol, int max_sweeps) {
+                                   float tol, int max_sweeps, double inv_scale2) {
+  static_assert(EPL % 4 == 0, "values per lane come in 4-float units");
+  constexpr int NU = EPL / 4;  // units per lane
   __shared__ int s_rot;
   const int tid = threadIdx.x, nthr = blockDim.x;
   const int groups = nthr / G, gid = tid / G, gl = tid % G;
+  const int warp_first_group = (tid / 32) * (32 / G);
   for (int e = tid; e < cols * cols; e += nthr) {
     const int c = e / cols, k = e % cols;
     V[c * ldv + k] = (c == k) ? 1.f : 0.f;
   }
   __syncthreads();
   if (cols <= 1) return 0;
+  const bool vec = ((reinterpret_cast<unsigned long>(X) & 15) == 0) && (ldx % 4 == 0);
+  const ACC tol2 = (ACC)tol * (ACC)tol;
+  const ACC is2 = (ACC)inv_scale2;
   const int np = cols + (cols & 1);
   const int half = np / 2;
   int sweep = 0;
@@ -104,6 +77,7 @@ static __device__ int cta_hestenes(float* X, int len, int cols, int ldx, float* 
     __syncthreads();
     for (int k = 0; k < np - 1; ++k) {
       for (int base = 0; base < half; base += groups) {
+        if (base + warp_first_group >= half) continue;  // warp owns no pair this round
         const int i = base + gid;
         int p = 0, q = -1;
         if (i < half) {
@@ -116,13 +90,40 @@ static __device__ int cta_hestenes(float* X, int len, int cols, int ldx, float* 
         const bool active = q >= 0;
         float* xp = X + (long)p * ldx;
         float* xq = X + (long)(active ? q : p) * ldx;
-        ACC al = 0, be = 0, ga = 0;
-        if (active) {
-          for (int e = gl; e < len; e += G) {
-            const ACC u = xp[e], v = xq[e];
-            al += u * u;
-            be += v * v;
-            ga += u * v;
+        float4 up[NU > 0 ? NU : 1], uq[NU > 0 ? NU : 1];
+        float fal = 0.f, fbe = 0.f, fga = 0.f;
+        if constexpr (NU > 0) {
+#pragma unroll
+          for (int t = 0; t < NU; ++t) {
+            const int e = 4 * (gl + t * G);
+            if (active && vec && e + 4 <= len) {
+              up[t] = *reinterpret_cast<const float4*>(xp + e);
+              uq[t] = *reinterpret_cast<const float4*>(xq + e);
+            } else {
+              const bool a0 = active && e < len, a1 = active && e + 1 < len,
+                         a2 = active && e + 2 < len, a3 = active && e + 3 < len;
+              up[t] = make_float4(a0 ? xp[e] : 0.f, a1 ? xp[e + 1] : 0.f, a2 ? xp[e + 2] : 0.f,
+                                  a3 ? xp[e + 3] : 0.f);
+              uq[t] = make_float4(a0 ? xq[e] : 0.f, a1 ? xq[e + 1] : 0.f, a2 ? xq[e + 2] : 0.f,
+                                  a3 ? xq[e + 3] : 0.f);
+            }
+            fal = fmaf(up[t].x, up[t].x, fal); fal = fmaf(up[t].y, up[t].y, fal);
+            fal = fmaf(up[t].z, up[t].z, fal); fal = fmaf(up[t].w, up[t].w, fal);
+            fbe = fmaf(uq[t].x, uq[t].x, fbe); fbe = fmaf(uq[t].y, uq[t].y, fbe);
+            fbe = fmaf(uq[t].z, uq[t].z, fbe); fbe = fmaf(uq[t].w, uq[t].w, fbe);
+            fga = fmaf(up[t].x, uq[t].x, fga); fga = fmaf(up[t].y, uq[t].y, fga);
+            fga = fmaf(up[t].z, uq[t].z, fga); fga = fmaf(up[t].w, uq[t].w, fga);
+          }
+        }
+        ACC al = fal, be = fbe, ga = fga;
+        if constexpr (NU == 0) {  // long columns: stream them from shared memory twice
+          if (active) {
+            for (int e = gl; e < len; e += G) {
+              const ACC u = xp[e], v = xq[e];
+              al += u * u;
+              be += v * v;
+              ga += u * v;
+            }
           }
         }
 #pragma unroll
@@ -131,20 +132,49 @@ static __device__ int cta_hestenes(float* X, int len, int cols, int ldx, float* 
           be += __shfl_xor_sync(0xffffffffu, be, o);
           ga += __shfl_xor_sync(0xffffffffu, ga, o);
         }
-        if (!active || ga == (ACC)0 || fabsf((float)ga) <= tol * sqrtf((float)al * (float)be))
+        // the pair's Gram relative to the problem's scale: a column below
+        // kJacobiFloor of it is numerically null and is left alone, which
+        // also keeps the fp32 rotation parameters clear of underflow
+        al *= is2;
+        be *= is2;
+        ga *= is2;
+        if (!active || !(al > (ACC)kJacobiFloor && be > (ACC)kJacobiFloor) ||
+            ga * ga <= tol2 * al * be)
           continue;
-        // rotation angle in fp32: its rounding only perturbs the convergence
-        // rate, the applied rotation stays orthogonal (c^2 + s^2 = 1)
-        const float zeta = ((float)be - (float)al) / (2.f * (float)ga);
+        const float zeta = __fdividef((float)be - (float)al, 2.f * (float)ga);
         const float az = fabsf(zeta);
-        const float t = (az > 1e18f) ? 0.5f / zeta
-                                     : copysignf(1.f, zeta) / (az + sqrtf(fmaf(zeta, zeta, 1.f)));
-        const double cd = 1.0 / sqrt(1.0 + (double)t * (double)t);
-        const float c = (float)cd, s = (float)(cd * (double)t);
-        for (int e = gl; e < len; e += G) {
-          const float u = xp[e], v = xq[e];
-          xp[e] = c * u - s * v;
-          xq[e] = s * u + c * v;
+        const float x1 = fmaf(zeta, zeta, 1.f);
+        const float hyp = az > 1e18f ? az : x1 * rsqrtf(x1);  // sqrt(1 + zeta^2)
+        const float t = copysignf(__fdividef(1.f, az + hyp), zeta);
+        float c = rsqrtf(fmaf(t, t, 1.f)), s = c * t;
+        const float f = fmaf(-0.5f, fmaf(c, c, s * s), 1.5f);  // Newton step to unit norm
+        c *= f;
+        s *= f;
+        if constexpr (NU > 0) {
+#pragma unroll
+          for (int t2 = 0; t2 < NU; ++t2) {
+            const int e = 4 * (gl + t2 * G);
+            const float4 a = up[t2], bq = uq[t2];
+            const float4 np_ = make_float4(c * a.x - s * bq.x, c * a.y - s * bq.y,
+                                           c * a.z - s * bq.z, c * a.w - s * bq.w);
+            const float4 nq_ = make_float4(s * a.x + c * bq.x, s * a.y + c * bq.y,
+                                           s * a.z + c * bq.z, s * a.w + c * bq.w);
+            if (vec && e + 4 <= len) {
+              *reinterpret_cast<float4*>(xp + e) = np_;
+              *reinterpret_cast<float4*>(xq + e) = nq_;
+            } else {
+              if (e < len) { xp[e] = np_.x; xq[e] = nq_.x; }
+              if (e + 1 < len) { xp[e + 1] = np_.y; xq[e + 1] = nq_.y; }
+              if (e + 2 < len) { xp[e + 2] = np_.z; xq[e + 2] = nq_.z; }
+              if (e + 3 < len) { xp[e + 3] = np_.w; xq[e + 3] = nq_.w; }
+            }
+          }
+        } else {
+          for (int e = gl; e < len; e += G) {
+            const float u = xp[e], v = xq[e];
+            xp[e] = c * u - s * v;
+            xq[e] = s * u + c * v;
+          }
         }
         float* vp = V + (long)p * ldv;
         float* vq = V + (long)q * ldv;
@@ -164,52 +194,202 @@ static __device__ int cta_hestenes(float* X, int len, int cols, int ldx, float* 
   return sweep;
 }
 
-// out[k][j] = sum_i U[i][k] X[j][i]   (k < M, j < b; U row-major ld, X [b][n])
-static __device__ void cta_proj_t(int M, int b, int n, const float* U, int ld, const float* X,
-                                  float* out, int ldo) {
-  for (int e = threadIdx.x; e < M * b; e += blockDim.x) {
-    const int k = e % M, j = e / M;
-    const float* x = X + (long)j * n;
-    float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f;
-    int i = 0;
-    for (; i + 3 < n; i += 4) {
-      acc0 = fmaf(U[(long)i * ld + k], x[i], acc0);
-      acc1 = fmaf(U[(long)(i + 1) * ld + k], x[i + 1], acc1);
-      acc2 = fmaf(U[(long)(i + 2) * ld + k], x[i + 2], acc2);
-      acc3 = fmaf(U[(long)(i + 3) * ld + k], x[i + 3], acc3);
+// Choose the group width: about four warps' worth of pairs per round, and
+// enough lanes that each holds at most 32 values of a column.
+template <typename ACC>
+static __device__ int cta_hestenes_any(float* X, int len, int cols, int ldx, float* V, int ldv,
+                                       float tol, int max_sweeps, double inv_scale2) {
+  const int half = (cols + 1) / 2;
+  int G = 32;
+  while (G > 4 && half * G > 128) G >>= 1;
+  while (G < 32 && G * 32 < len) G <<= 1;
+  const int epl = (len + G - 1) / G;
+#define KVD_HJ(GG, EE)                                                                   \
+  if (G == GG && epl <= EE)                                                              \
+    return cta_hestenes<GG, EE, ACC>(X, len, cols, ldx, V, ldv, tol, max_sweeps, inv_scale2);
+  KVD_HJ(4, 4) KVD_HJ(4, 8) KVD_HJ(4, 12) KVD_HJ(4, 16) KVD_HJ(4, 24) KVD_HJ(4, 32)
+  KVD_HJ(8, 8) KVD_HJ(8, 16) KVD_HJ(8, 32)
+  KVD_HJ(16, 16) KVD_HJ(16, 32)
+  KVD_HJ(32, 16) KVD_HJ(32, 32)
+#undef KVD_HJ
+  return cta_hestenes<32, 0, ACC>(X, len, cols, ldx, V, ldv, tol, max_sweeps, inv_scale2);
+}
+
+// 16 consecutive floats p[j0 .. j0+16) of a row, zero past `nb`; `vec` =
+// the row start and j0 are 16-byte aligned.
+static __device__ __forceinline__ void load16(const float* p, int j0, int nb, bool vec,
+                                              float (&v)[16]) {
+  if (vec && j0 + 16 <= nb) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float4 t = *reinterpret_cast<const float4*>(p + j0 + 4 * q);
+      v[4 * q] = t.x; v[4 * q + 1] = t.y; v[4 * q + 2] = t.z; v[4 * q + 3] = t.w;
     }
-    for (; i < n; ++i) acc0 = fmaf(U[(long)i * ld + k], x[i], acc0);
-    out[k * ldo + j] = (acc0 + acc1) + (acc2 + acc3);
+  } else {
+#pragma unroll
+    for (int jj = 0; jj < 16; ++jj) v[jj] = (j0 + jj < nb) ? p[j0 + jj] : 0.f;
+  }
+}
+
+static __device__ __forceinline__ void store16(float* p, int j0, int nb, bool vec,
+                                               const float (&v)[16]) {
+  if (vec && j0 + 16 <= nb) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      *reinterpret_cast<float4*>(p + j0 + 4 * q) =
+          make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+  } else {
+#pragma unroll
+    for (int jj = 0; jj < 16; ++jj)
+      if (j0 + jj < nb) p[j0 + jj] = v[jj];
+  }
+}
+
+// out[k*ldo + j] = sum_{i<K} A[i*lda + k] B[i*ldb + j] - diag*[k == j]
+// for k < M (<= kMaxStepLd), j < NB.  The warps split into ceil(M/32)
+// k-chunks x ks K-slices; a lane owns one k and 16 j sums in fp32 over its
+// slice, and the slices' partials are added in fp64.  A row of B is read as
+// a broadcast, so B[i] rows are 16-byte vectors when `bvec`.
+static __device__ void cta_tn(int M, int NB, int K, const float* A, int lda, const float* B,
+                              int ldb, bool bvec, float* out, int ldo, float diag, float* part) {
+  const int tid = threadIdx.x, nthr = blockDim.x, lane = tid % 32, warp = tid / 32;
+  const int nw = nthr / 32;
+  const int kc = (M + 31) / 32;
+  const int ks = max(1, nw / kc);
+  const int slice = (K + ks - 1) / ks;
+  for (int j0 = 0; j0 < NB; j0 += 16) {
+    for (int wi = warp; wi < kc * ks; wi += nw) {
+      const int kch = wi % kc, ksl = wi / kc;
+      const int k = kch * 32 + lane;
+      const int i0 = ksl * slice, i1 = min(K, i0 + slice);
+      float acc[16];
+#pragma unroll
+      for (int jj = 0; jj < 16; ++jj) acc[jj] = 0.f;
+#pragma unroll 2
+      for (int i = i0; i < i1; ++i) {
+        const float a = k < M ? A[(long)i * lda + k] : 0.f;
+        float bv[16];
+        load16(B + (long)i * ldb, j0, NB, bvec, bv);
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) acc[jj] = fmaf(a, bv[jj], acc[jj]);
+      }
+      if (k < M) {
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) part[((long)ksl * 16 + jj) * M + k] = acc[jj];
+      }
+    }
+    __syncthreads();
+    for (int e = tid; e < 16 * M; e += nthr) {
+      const int jj = e / M, k = e % M, j = j0 + jj;
+      if (j >= NB) continue;
+      double sum = 0.0;
+      for (int sl = 0; sl < ks; ++sl) sum += (double)part[((long)sl * 16 + jj) * M + k];
+      if (k == j) sum -= (double)diag;
+      out[(long)k * ldo + j] = (float)sum;
+    }
+    __syncthreads();
+  }
+}
+
+// Rows of the residual, one thread per row i, 16 tokens at a time:
+//   v = (from_xr ? XR[i][j] : Rm[j][i]) - sum_{k<K} A[i*lda + k] C[k*ldc + j]
+// written to Rm[j*n + i] (j < b) and, when to_xr, to XR[i*ldb + j].  C rows
+// and XR rows are 16-byte aligned (ldc, ldb multiples of 4).
+static __device__ void cta_rows_sub(int n, int b, int b16, int K, const float* A, int lda,
+                                    const float* C, int ldc, float* XR, int ldb, float* Rm,
+                                    bool from_xr, bool to_xr) {
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float* ar = A + (long)i * lda;
+    float* xr = XR + (long)i * ldb;
+    for (int j0 = 0; j0 < b16; j0 += 16) {
+      float acc[16];
+      if (from_xr) {
+        load16(xr, j0, b16, true, acc);
+      } else {
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) acc[jj] = (j0 + jj < b) ? Rm[(long)(j0 + jj) * n + i] : 0.f;
+      }
+      for (int k = 0; k < K; ++k) {
+        const float av = ar[k];
+        float cv[16];
+        load16(C + (long)k * ldc, j0, b16, true, cv);
+#pragma unroll
+        for (int jj = 0; jj < 16; ++jj) acc[jj] = fmaf(-av, cv[jj], acc[jj]);
+      }
+#pragma unroll
+      for (int jj = 0; jj < 16; ++jj)
+        if (j0 + jj < b) Rm[(long)(j0 + jj) * n + i] = acc[jj];
+      if (to_xr) store16(xr, j0, b16, true, acc);
+    }
   }
   __syncthreads();
 }
 
-// Y[j][i] (=|+=) alpha * sum_k A[i][k] C[k][j]  for i < n, j < b; A row-major
-// (lda), C row-major (ldc, in shared memory), Y [b][n].  One thread per row i.
-template <bool ACCUM>
-static __device__ void cta_rows_times(int n, int b, int K, const float* A, int lda, const float* C,
-                                      int ldc, float* Y, float alpha) {
-  constexpr int JB = 16;
+// Uo[i*ld + c] = sum_{k<r} A[i*lda + k] WU[k*ldw + c] + sum_{j<m} Q[j*n + i] WU[(r+j)*ldw + c]
+// for c < keep; one thread per row, 16 columns at a time (WU rows 16-byte
+// aligned and zero-padded to ldw).
+static __device__ void cta_basis_rows(int n, int keep, int r, int m, const float* A, int lda,
+                                      const float* Q, const float* WU, int ldw, float* Uo, int ld,
+                                      bool uvec) {
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     const float* ar = A + (long)i * lda;
-    for (int j0 = 0; j0 < b; j0 += JB) {
-      float acc[JB];
+    for (int c0 = 0; c0 < keep; c0 += 16) {
+      float acc[16];
 #pragma unroll
-      for (int jj = 0; jj < JB; ++jj) acc[jj] = 0.f;
-      const int jn = min(JB, b - j0);
-      for (int k = 0; k < K; ++k) {
+      for (int cc = 0; cc < 16; ++cc) acc[cc] = 0.f;
+      for (int k = 0; k < r; ++k) {
         const float av = ar[k];
-        const float* cr = C + (long)k * ldc + j0;
+        float wv[16];
+        load16(WU + (long)k * ldw, c0, ldw, true, wv);
 #pragma unroll
-        for (int jj = 0; jj < JB; ++jj)
-          if (jj < jn) acc[jj] = fmaf(av, cr[jj], acc[jj]);
+        for (int cc = 0; cc < 16; ++cc) acc[cc] = fmaf(av, wv[cc], acc[cc]);
       }
+      for (int j = 0; j < m; ++j) {
+        const float qv = Q[(long)j * n + i];
+        float wv[16];
+        load16(WU + (long)(r + j) * ldw, c0, ldw, true, wv);
 #pragma unroll
-      for (int jj = 0; jj < JB; ++jj) {
-        if (jj >= jn) break;
-        float* y = Y + (long)(j0 + jj) * n + i;
-        *y = ACCUM ? fmaf(alpha, acc[jj], *y) : alpha * acc[jj];
+        for (int cc = 0; cc < 16; ++cc) acc[cc] = fmaf(qv, wv[cc], acc[cc]);
       }
+      store16(Uo + (long)i * ld, c0, keep, uvec, acc);
+    }
+  }
+  __syncthreads();
+}
+
+// Uo[i][c] -= 1/2 sum_k Uo[i][k] E[k][c] for c < keep <= 32, one thread per
+// row holding it in registers (E zero-padded to 32 x 32, row stride lde).
+static __device__ void cta_polish_rows(int n, int keep, float* Uo, int ld, bool uvec,
+                                       const float* E, int lde) {
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    float* ur = Uo + (long)i * ld;
+    float row[32];
+    {
+      float t[16];
+      load16(ur, 0, keep, uvec, t);
+#pragma unroll
+      for (int c = 0; c < 16; ++c) row[c] = t[c];
+      load16(ur, 16, keep, uvec, t);
+#pragma unroll
+      for (int c = 0; c < 16; ++c) row[16 + c] = t[c];
+    }
+#pragma unroll
+    for (int c0 = 0; c0 < 32; c0 += 16) {
+      if (c0 >= keep) break;
+      float acc[16];
+#pragma unroll
+      for (int cc = 0; cc < 16; ++cc) acc[cc] = row[c0 + cc];
+#pragma unroll
+      for (int k = 0; k < 32; ++k) {
+        if (k < keep) {
+          const float h = -0.5f * row[k];
+          float ev[16];
+          load16(E + (long)k * lde, c0, 32, true, ev);
+#pragma unroll
+          for (int cc = 0; cc < 16; ++cc) acc[cc] = fmaf(h, ev[cc], acc[cc]);
+        }
+      }
+      store16(ur, c0, keep, uvec, acc);
     }
   }
   __syncthreads();
@@ -290,159 +470,9 @@ static __device__ void cta_cgs2_rows(float* Q, int m, int n, double* dots /*>= m
   }
 }
 
-// Two-sided cyclic Jacobi on a symmetric N x N fp64 matrix A (leading
-// dimension lda, odd so column accesses are bank-conflict free), eigenvectors
-// accumulated in V (N x N fp64, ldv).  N'/2 disjoint rotations per round
-// (circle ordering), rows then columns.  Rotation: Golub & Van Loan
-// Alg. 8.4.2 (sym.schur2), angle in fp32 (only the convergence rate depends
-// on it), applied in fp64.  `cs` is shared scratch of 2*(N/2+1) doubles and
-// 2*(N/2+1) ints (8-byte aligned).  Entries below 1e-17 of the largest diagonal are rounding
-// noise and are left alone, so rank-deficient PSD matrices converge.
-static __device__ int cta_jacobi_sym(double* A, int N, int lda, double* V, int ldv, float* cs,
-                                     int max_sweeps) {
-  __shared__ int s_rot;
-  __shared__ double s_scale;
-  const int tid = threadIdx.x, nthr = blockDim.x;
-  for (int e = tid; e < N * N; e += nthr) {
-    const int i = e / N, j = e % N;
-    V[i * ldv + j] = (i == j) ? 1.0 : 0.0;
-  }
-  if (tid == 0) {
-    double mx = 0.0;
-    for (int i = 0; i < N; ++i) mx = fmax(mx, fabs(A[i * lda + i]));
-    s_scale = mx;
-  }
-  __syncthreads();
-  if (N <= 1) return 0;
-  const double floor_rot = 1e-17 * s_scale, floor_flag = 1e-14 * s_scale;
-  const int np = N + (N & 1), half = np / 2;
-  double* pc = reinterpret_cast<double*>(cs);
-  double* ps = pc + half;
-  int* pp = reinterpret_cast<int*>(ps + half);
-  int* pq = pp + half;
-  int sweep = 0;
-  for (; sweep < max_sweeps; ++sweep) {
-    if (tid == 0) s_rot = 0;
-    __syncthreads();
-    for (int k = 0; k < np - 1; ++k) {
-      for (int i = tid; i < half; i += nthr) {
-        int a, b;
-        rr_pair(i, k, np, &a, &b);
-        int p = a < b ? a : b, q = a < b ? b : a;
-        double pcd = 1.0, psd = 0.0;
-        if (q < N) {
-          const double apq = A[p * lda + q], app = A[p * lda + p], aqq = A[q * lda + q];
-          const double thr = fmax(1e-15 * sqrt(fabs(app * aqq)), floor_rot);
-          if (apq != 0.0 && fabs(apq) > thr) {
-            const float tau = (float)((aqq - app) / (2.0 * apq));
-            const float at = fabsf(tau);
-            const float t = (at > 1e18f) ? 0.5f / tau
-                                         : copysignf(1.f, tau) / (at + sqrtf(fmaf(tau, tau, 1.f)));
-            // the angle is approximate (fp32 t) but (c, s) is an exact fp64
-            // rotation, so applying it never changes norms
-            const double cd = 1.0 / sqrt(1.0 + (double)t * (double)t);
-            pcd = cd;
-            psd = cd * (double)t;
-            if (fabs(apq) > fmax(4e-15 * sqrt(fabs(app * aqq)), floor_flag)) s_rot = 1;
-          }
-        } else {
-          q = -1;
-        }
-        pc[i] = pcd; ps[i] = psd; pp[i] = p; pq[i] = q;
-      }
-      __syncthreads();
-      for (int e = tid; e < half * N; e += nthr) {   // rows: A <- J^T A
-        const int i = e / N, j = e % N;
-        const double s = ps[i];
-        if (s == 0.0) continue;
-        const int p = pp[i], q = pq[i];
-        const double c = pc[i];
-        const double x = A[p * lda + j], y = A[q * lda + j];
-        A[p * lda + j] = c * x - s * y;
-        A[q * lda + j] = s * x + c * y;
-      }
-      __syncthreads();
-      for (int e = tid; e < half * N; e += nthr) {   // columns: A <- A J, V <- V J
-        const int i = e / N, j = e % N;
-        const double s = ps[i];
-        if (s == 0.0) continue;
-        const int p = pp[i], q = pq[i];
-        const double c = pc[i];
-        const double x = A[j * lda + p], y = A[j * lda + q];
-        A[j * lda + p] = c * x - s * y;
-        A[j * lda + q] = s * x + c * y;
-        const double vx = V[j * ldv + p], vy = V[j * ldv + q];
-        V[j * ldv + p] = c * vx - s * vy;
-        V[j * ldv + q] = s * vx + c * vy;
-      }
-      __syncthreads();
-    }
-    const int any = s_rot;
-    __syncthreads();
-    if (!any) break;
-  }
-  return sweep;
-}
-
-// H = X^T X in fp64 for the `cols` columns of X (column c at X + c*ldx, len
-// rows); one warp per (c1 <= c2) pair.
-static __device__ void cta_gram_cols(const float* X, int len, int cols, int ldx, double* H, int ldh) {
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32, nw = blockDim.x / 32;
-  const int pairs = cols * (cols + 1) / 2;
-  for (int e = warp; e < pairs; e += nw) {
-    int c1 = 0, rem = e;
-    while (rem >= cols - c1) { rem -= cols - c1; ++c1; }
-    const int c2 = c1 + rem;
-    const float* x1 = X + (long)c1 * ldx;
-    const float* x2 = X + (long)c2 * ldx;
-    double acc = 0.0;
-    for (int i = lane; i < len; i += 32) acc += (double)x1[i] * (double)x2[i];
-    acc = warp_sum(acc);
-    if (lane == 0) { H[c1 * ldh + c2] = acc; H[c2 * ldh + c1] = acc; }
-  }
-  __syncthreads();
-}
-
-// Make the rows of Q (m x n) orthonormal by one Cholesky-QR pass in fp64:
-// G = Q Q^T = L L^T, Q <- L^{-1} Q.  `Gs` is shared scratch of m*(m+1)
-// doubles.  Returns false (Q untouched) when a pivot is not safely positive,
-// i.e. the rows are (numerically) dependent.
-static __device__ bool cta_cholqr_rows(float* Q, int m, int n, double* Gs) {
-  __shared__ int s_ok;
-  const int ldg = m + 1;
-  cta_gram_cols(Q, n, m, n, Gs, ldg);  // rows of Q are the "columns" here
-  if (threadIdx.x == 0) {
-    int ok = 1;
-    for (int j = 0; j < m && ok; ++j) {  // in-place Cholesky, lower triangle
-      double d = Gs[j * ldg + j];
-      for (int k = 0; k < j; ++k) d -= Gs[j * ldg + k] * Gs[j * ldg + k];
-      if (!(d > 0.25)) { ok = 0; break; }  // rows are near-unit: pivots ~1
-      d = sqrt(d);
-      Gs[j * ldg + j] = d;
-      for (int i = j + 1; i < m; ++i) {
-        double v = Gs[i * ldg + j];
-        for (int k = 0; k < j; ++k) v -= Gs[i * ldg + k] * Gs[j * ldg + k];
-        Gs[i * ldg + j] = v / d;
-      }
-    }
-    s_ok = ok;
-  }
-  __syncthreads();
-  if (!s_ok) return false;
-  // forward substitution per column i of Q, in place: Q[:, i] <- L^{-1} Q[:, i]
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    for (int j = 0; j < m; ++j) {
-      double v = Q[(long)j * n + i];
-      for (int k = 0; k < j; ++k) v -= Gs[j * ldg + k] * (double)Q[(long)k * n + i];
-      Q[(long)j * n + i] = (float)(v / Gs[j * ldg + j]);
-    }
-  }
-  __syncthreads();
-  return true;
-}
-
-__global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch batch, int smem_budget) {
+__global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch batch) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
+  const StepPlan& P = batch.plan;
   const int p = blockIdx.x;
   const BugStepArgs& A = batch.s[blockIdx.y];
   const int n = A.n, b = A.b, cap = A.rank_cap, ld = A.ld;
@@ -451,11 +481,30 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
   float* sig = A.sigma + p * A.sig_sp;
   const float* X = A.x + p * A.x_sp;
   const int r = A.r[p];
-  StepWs w = carve(A.ws + p * A.ws_sp, n, b, ld);
-  float* gsm = reinterpret_cast<float*>(smem_raw);
-  double* red = reinterpret_cast<double*>(smem_raw + 4 * kGemmSmemFloats);  // 64 doubles
-  float* pool = reinterpret_cast<float*>(smem_raw + 4 * kGemmSmemFloats + kStepMiscBytes);
-  const long pool_floats = (smem_budget - 4L * kGemmSmemFloats - kStepMiscBytes) / 4;
+  char* wsb = A.ws + p * A.ws_sp;
+  double* red = reinterpret_cast<double*>(smem_raw);  // 64 doubles
+  float* pool = reinterpret_cast<float*>(smem_raw + kStepMiscBytes);
+  auto region = [&](int g) -> float* {
+    return P.smem[g] >= 0 ? pool + P.smem[g] : reinterpret_cast<float*>(wsb + P.ws[g]);
+  };
+  float* Rm = region(kRgRm);      // [b][n]  residual columns (Jacobi input)
+  float* XR = region(kRgXr);      // [n][ldb] block rows, then residual rows, then Q [m][n]
+  float* part = region(kRgPart);  // K-split partials
+  float* AS = region(kRgAs);      // [ld][b16] a = U^T X
+  float* A2 = region(kRgA2);      // [ld][b16] re-orthogonalisation correction
+  float* Vh = region(kRgVh);      // [b][b] right vectors of R (column-major)
+  float* BT = region(kRgCore);    // [N][ldbt] B^T, then [N][N] W behind it
+  float* Pol = region(kRgPol);    // [ldp][ldp] U_new^T U_new - I
+  float* WU = region(kRgWu);      // [N][ldw] top left vectors of B, ordered
+  double* nrm = reinterpret_cast<double*>(region(kRgSmall));  // [ld+b]
+  double* sv = nrm + (ld + b);                                // [b]
+  int* ord = reinterpret_cast<int*>(sv + b);                  // [ld+b]
+  int* ordh = ord + (ld + b);                                 // [b]
+  const bool us = P.smem[kRgUs] >= 0 && r > 0;
+  const float* Uc = us ? pool + P.smem[kRgUs] : U;
+  const int lda = us ? P.ldu : ld;
+  const int b16 = P.b16, ldb = P.ldb, ldbt = P.ldbt, ldw = P.ldw, ldp = P.ldp;
+  const bool uvec = ((reinterpret_cast<unsigned long>(Uo) & 15) == 0) && (ld % 4 == 0);
   __shared__ double s_xnorm2;
   __shared__ int s_m, s_keep, s_degenerate;
   const int tid = threadIdx.x, nthr = blockDim.x, lane = tid % 32, warp = tid / 32;
@@ -468,183 +517,126 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
     if (lane == 0) red[warp] = acc;
     __syncthreads();
     if (tid == 0) { double t = 0; for (int i = 0; i < nthr / 32; ++i) t += red[i]; s_xnorm2 = t; }
-    __syncthreads();
   }
-  // ----- residual R = (I - U U^T)^2 X (the reference's re-orthogonalised residual)
-  const bool r_in_smem = (long)b * n + (long)b * b <= pool_floats;
-  float* Rm = r_in_smem ? pool : w.R;
-  float* Vh = r_in_smem ? pool + (long)b * n : w.VH;
-  // U staged in shared memory (at the end of the pool) when it fits beside the
-  // residual phase; it is read by four projections and the basis update
-  const long u_floats = (long)n * r;
-  const long p1_floats = (long)b * n + (long)b * b + 2L * r * b;
-  const bool u_smem = r > 0 && r_in_smem && p1_floats + u_floats <= pool_floats;
-  const float* Us = U;
-  int uld = ld;
-  if (u_smem) {
-    float* dst = pool + (pool_floats - u_floats);
-    for (long e = tid; e < u_floats; e += nthr) {
+  // ----- stage the block token-transposed (XR[i][j] = X[j][i], zero past b) and U
+  for (long e = tid; e < (long)b * n; e += nthr) {
+    const int j = (int)(e / n), i = (int)(e % n);
+    XR[(long)i * ldb + j] = X[e];
+  }
+  if (b16 > b) {
+    const int pad = b16 - b;
+    for (long e = tid; e < (long)n * pad; e += nthr)
+      XR[(e / pad) * ldb + b + (int)(e % pad)] = 0.f;
+  }
+  if (us) {
+    float* dst = pool + P.smem[kRgUs];
+    for (long e = tid; e < (long)n * r; e += nthr) {
       const long i = e / r, k = e % r;
-      dst[e] = U[i * ld + k];
+      dst[i * lda + k] = U[i * ld + k];
     }
-    Us = dst;
-    uld = r;
   }
-  for (long e = tid; e < (long)b * n; e += nthr) Rm[e] = X[e];
+  for (int e = tid; e < r * b16; e += nthr) { AS[e] = 0.f; A2[e] = 0.f; }
   __syncthreads();
+  // ----- residual R = (I - U U^T)^2 X (the reference's re-orthogonalised residual)
+  if (r > 0) cta_tn(r, b, n, Uc, lda, XR, ldb, true, AS, b16, 0.f, part);  // a = U^T X
+  cta_rows_sub(n, b, b16, r, Uc, lda, AS, b16, XR, ldb, Rm, true, r > 0);  // R = X - U a
   if (r > 0) {
-    // a and a2 live in shared memory when they fit beside R (small in steady state)
-    const bool a_smem = r_in_smem && (long)b * n + (long)b * b + 2L * r * b <= pool_floats;
-    float* as = a_smem ? pool + (long)b * n + (long)b * b : w.a;
-    float* a2 = a_smem ? as + (long)r * b : w.Q;
-    __syncthreads();
-    cta_proj_t(r, b, n, Us, uld, Rm, as, b);                      // a = U^T X
-    cta_rows_times<true>(n, b, r, Us, uld, as, b, Rm, -1.f);      // R -= U a
-    cta_proj_t(r, b, n, Us, uld, Rm, a2, b);                      // a2 = U^T R
-    cta_rows_times<true>(n, b, r, Us, uld, a2, b, Rm, -1.f);      // R -= U a2
-    for (int e = tid; e < r * b; e += nthr) w.a[e] = as[e] + a2[e];
+    cta_tn(r, b, n, Uc, lda, XR, ldb, true, A2, b16, 0.f, part);             // a2 = U^T R
+    cta_rows_sub(n, b, b16, r, Uc, lda, A2, b16, XR, ldb, Rm, false, false);  // R -= U a2
+    for (int e = tid; e < r * b16; e += nthr) AS[e] += A2[e];
     __syncthreads();
   }
-  // ----- SVD of R.  Small blocks: fp64 Gram + two-sided Jacobi, then
-  // Q = R V S^-1 made orthonormal by Cholesky-QR.  Large blocks: one-sided
-  // Jacobi directly on R (columns come out orthogonal).
-  float* cs = reinterpret_cast<float*>(smem_raw + 4 * kGemmSmemFloats + 512);
-  const int ldh = b | 1;
-  const long p1_end = (long)b * n + (long)b * b + 2L * r * b;
-  const long h_off = (p1_end + 1) & ~1L;  // 8-byte aligned for fp64
-  const bool gram_r = r_in_smem && h_off + 4L * b * ldh <= pool_floats;
-  int sw = 0;
-  if (gram_r) {
-    double* Hm = reinterpret_cast<double*>(pool + h_off);
-    double* Vd = Hm + (long)b * ldh;
-    cta_gram_cols(Rm, n, b, n, Hm, ldh);
-    sw = cta_jacobi_sym(Hm, b, ldh, Vd, ldh, cs, 40);
-    for (int j = tid; j < b; j += nthr) w.sv[j] = sqrt(fmax(Hm[j * ldh + j], 0.0));
-    for (int e = tid; e < b * b; e += nthr) {  // fp32 column-major copy of V
-      const int c = e / b, row = e % b;
-      Vh[e] = (float)Vd[row * ldh + c];
+  // ----- SVD of R by one-sided Jacobi.  b <= n: on R's b columns, R V = [s_j q_j].
+  // b > n (more columns than rows cannot all be made orthogonal): on the n
+  // columns of R^T, R^T J = [s_j v_j], so J holds the left vectors q_j.
+  const bool tr = b > n;
+  const int nsv = tr ? n : b;
+  const double inv_x2 = s_xnorm2 > 0.0 ? 1.0 / s_xnorm2 : 1.0;
+  int sw;
+  if (!tr) {
+    sw = cta_hestenes_any<double>(Rm, n, b, n, Vh, b, 1.2e-7f * sqrtf((float)n) + 2.4e-7f, 30, inv_x2);
+    cta_colnorm_order(Rm, n, b, n, sv, ordh);
+  } else {
+    for (long e = tid; e < (long)b * n; e += nthr) XR[e] = Rm[e];
+    __syncthreads();
+    for (long e = tid; e < (long)b * n; e += nthr) {  // Rm[i*b + j] = R[i][j]
+      const int i = (int)(e / b), j = (int)(e % b);
+      Rm[e] = XR[(long)j * n + i];
     }
     __syncthreads();
-    cta_argsort_desc(w.sv, b, w.ordh);
-  } else {
-    sw = cta_hestenes<32, double>(Rm, n, b, n, Vh, b, 1.2e-7f * sqrtf((float)n) + 2.4e-7f, 30);
-    cta_colnorm_order(Rm, n, b, n, w.sv, w.ordh);
+    sw = cta_hestenes_any<double>(Rm, b, n, b, Vh, n, 1.2e-7f * sqrtf((float)b) + 2.4e-7f, 30, inv_x2);
+    cta_colnorm_order(Rm, b, n, b, sv, ordh);
   }
-  if (sw > 30 && tid == 0) atomicOr(&A.status[kStatusNumeric], 1);
+  if (sw >= 30 && tid == 0) atomicOr(&A.status[kStatusNumeric], 1);
   if (tid == 0) {
     const float xnorm = (float)sqrt(s_xnorm2);
     const double tol = 100.0 * (double)FLT_EPSILON * (double)xnorm;
     int m;
     if (r == 0) {
-      m = min(n, b);
+      m = nsv;
     } else {
       m = 0;
-      for (int j = 0; j < b; ++j)
-        if ((double)(float)w.sv[w.ordh[j]] > tol) ++m;
+      for (int j = 0; j < nsv; ++j)
+        if ((double)(float)sv[ordh[j]] > tol) ++m;
       m = min(m, max(0, n - r));
     }
     s_m = m;
     // a kept direction far below the largest is numerically null: its column
     // is rounding noise and must be completed to an orthonormal direction
-    const double s0 = w.sv[w.ordh[0]];
+    const double s0 = sv[ordh[0]];
+    if (!isfinite(s0)) atomicOr(&A.status[kStatusNumeric], 4);
     int deg = 0;
     for (int j = 0; j < m; ++j)
-      if (!(w.sv[w.ordh[j]] > 1e-6 * s0) || s0 == 0.0) deg = 1;
+      if (!(sv[ordh[j]] > 1e-6 * s0) || s0 == 0.0) deg = 1;
     s_degenerate = deg;
   }
   __syncthreads();
   const int m = s_m;
-  if (gram_r) {
-    // Q_j = R V[:, ord_j] / s_j
+  float* Q = XR;  // [m][n]
+  if (!tr) {
     for (long e = tid; e < (long)m * n; e += nthr) {
       const int j = (int)(e / n), i = (int)(e % n);
-      const int oj = w.ordh[j];
-      const double sj = w.sv[oj];
-      const float* vc = Vh + (long)oj * b;
-      float acc = 0.f;
-      for (int l = 0; l < b; ++l) acc = fmaf(Rm[(long)l * n + i], vc[l], acc);
-      w.Q[e] = sj > 0.0 ? (float)(acc / sj) : 0.f;
+      const int oj = ordh[j];
+      const double sj = sv[oj];
+      Q[e] = sj > 0.0 ? (float)(Rm[(long)oj * n + i] / sj) : 0.f;
     }
-    __syncthreads();
-    bool ok = !s_degenerate && m > 0;
-    if (ok) ok = cta_cholqr_rows(w.Q, m, n, reinterpret_cast<double*>(pool + h_off));
-    if (!ok && m > 0) cta_cgs2_rows(w.Q, m, n, w.nrm, red);
   } else {
-    for (long e = tid; e < (long)m * n; e += nthr) {
+    for (long e = tid; e < (long)m * n; e += nthr) {  // q_j = J[:, ord_j]
       const int j = (int)(e / n), i = (int)(e % n);
-      const int oj = w.ordh[j];
-      const double sj = w.sv[oj];
-      w.Q[e] = sj > 0.0 ? (float)(Rm[(long)oj * n + i] / sj) : 0.f;
+      Q[e] = Vh[(long)ordh[j] * n + i];
     }
-    __syncthreads();
-    if (s_degenerate) cta_cgs2_rows(w.Q, m, n, w.nrm, red);
+    __syncthreads();  // J is overwritten next
+    for (long e = tid; e < (long)n * b; e += nthr) {  // v_c = (R^T J)[:, c] / s_c
+      const int c = (int)(e / b);
+      const double sc = sv[c];
+      Vh[e] = sc > 0.0 ? (float)(Rm[e] / sc) : 0.f;
+    }
   }
+  __syncthreads();
+  if (s_degenerate) cta_cgs2_rows(Q, m, n, nrm, red);
   // ----- the core B = [[diag(sigma), a], [0, diag(s_m) V_m^T]] ((r+m) x (r+b)):
-  // its left singular vectors W and values.  N <= 112: fp64 Gram B B^T +
-  // two-sided Jacobi; larger: one-sided Jacobi on B^T.
+  // its left singular vectors W and values by one-sided Jacobi on B^T.
   const int N = r + m, LB = r + b;
-  if (Vh != w.VH) {  // V must survive while the pool is reused
-    for (int e = tid; e < b * b; e += nthr) w.VH[e] = Vh[e];
-    __syncthreads();
-    Vh = w.VH;
-  }
-  const int ldg = N | 1;
-  const bool gram_b = N <= 112 && 4L * N * ldg <= pool_floats;
-  float* Wm = nullptr;   // one-sided path: W column-major [c*N + k]
-  double* Wd = nullptr;  // two-sided path: W row-major [k*ldg + c]
-  if (gram_b) {
-    double* Gm = reinterpret_cast<double*>(pool);
-    Wd = Gm + (long)N * ldg;
-    for (int e = tid; e < N * N; e += nthr) {
-      const int i = e / N, j = e % N;
-      if (j < i) continue;
-      double g = 0.0;
-      if (i < r && j < r) {
-        for (int l = 0; l < b; ++l) g += (double)w.a[i * b + l] * (double)w.a[j * b + l];
-        if (i == j) g += (double)sig[i] * (double)sig[i];
-      } else if (i < r) {
-        const int jj = j - r, oj = w.ordh[jj];
-        double t = 0.0;
-        for (int l = 0; l < b; ++l) t += (double)w.a[i * b + l] * (double)Vh[(long)oj * b + l];
-        g = t * (double)(float)w.sv[oj];
-      } else {
-        const int oi = w.ordh[i - r], oj = w.ordh[j - r];
-        double t = 0.0;
-        for (int l = 0; l < b; ++l) t += (double)Vh[(long)oi * b + l] * (double)Vh[(long)oj * b + l];
-        g = t * (double)(float)w.sv[oi] * (double)(float)w.sv[oj];
-      }
-      Gm[i * ldg + j] = g;
-      Gm[j * ldg + i] = g;
+  float* Wm = BT + (long)N * ldbt;  // W[c*N + k]
+  for (long e = tid; e < (long)N * LB; e += nthr) {
+    const int c = (int)(e / LB), row = (int)(e % LB);
+    float v = 0.f;
+    if (c < r) {
+      if (row < r) v = (row == c) ? sig[c] : 0.f;
+      else v = AS[c * b16 + (row - r)];
+    } else if (row >= r) {
+      const int oj = ordh[c - r];
+      v = (float)sv[oj] * Vh[(long)oj * b + (row - r)];
     }
-    __syncthreads();
-    sw = cta_jacobi_sym(Gm, N, ldg, Wd, ldg, cs, 40);
-    for (int c = tid; c < N; c += nthr) w.nrm[c] = sqrt(fmax(Gm[c * ldg + c], 0.0));
-    __syncthreads();
-    cta_argsort_desc(w.nrm, N, w.ord);
-  } else {
-    const long bt_need = (long)N * LB + (long)N * N;
-    float* BT = bt_need <= pool_floats ? pool : w.BT;
-    Wm = bt_need <= pool_floats ? pool + (long)N * LB : w.W;
-    for (long e = tid; e < (long)N * LB; e += nthr) {
-      const int c = (int)(e / LB), row = (int)(e % LB);
-      float v = 0.f;
-      if (c < r) {
-        if (row < r) v = (row == c) ? sig[c] : 0.f;
-        else v = w.a[c * b + (row - r)];
-      } else if (row >= r) {
-        const int j = c - r;
-        v = (float)w.sv[w.ordh[j]] * Vh[(long)w.ordh[j] * b + (row - r)];
-      }
-      BT[e] = v;
-    }
-    __syncthreads();
-    const float btol = 1.2e-7f * sqrtf((float)LB) + 2.4e-7f;
-    if (LB <= 64) sw = cta_hestenes<8, float>(BT, LB, N, LB, Wm, N, btol, 30);
-    else if (LB <= 256) sw = cta_hestenes<16, float>(BT, LB, N, LB, Wm, N, btol, 30);
-    else sw = cta_hestenes<32, double>(BT, LB, N, LB, Wm, N, btol, 30);
-    cta_colnorm_order(BT, LB, N, LB, w.nrm, w.ord);
+    BT[(long)c * ldbt + row] = v;
   }
-  if (sw > 30 && tid == 0) atomicOr(&A.status[kStatusNumeric], 2);
+  __syncthreads();
+  double b2 = s_xnorm2;  // ||B||_F^2 <= ||sigma||^2 + ||X||_F^2 sets the core's scale
+  for (int c = 0; c < r; ++c) b2 += (double)sig[c] * sig[c];
+  sw = cta_hestenes_any<float>(BT, LB, N, ldbt, Wm, N, 1.2e-7f * sqrtf((float)LB) + 2.4e-7f, 30,
+                               b2 > 0.0 ? 1.0 / b2 : 1.0);
+  cta_colnorm_order(BT, LB, N, ldbt, nrm, ord);
+  if (sw >= 30 && tid == 0) atomicOr(&A.status[kStatusNumeric], 2);
   if (tid == 0) {
     int keep = min(cap, N);
     if (A.has_theta && N > 0) {
@@ -653,73 +645,57 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
       int first_ok = -1;
       float tail = 0.f;
       for (int k = N - 1; k >= 0; --k) {
-        const float sk = (float)w.nrm[w.ord[k]];
+        const float sk = (float)nrm[ord[k]];
         tail += sk * sk;
         if (tail <= th2) first_ok = k;
       }
-      const int tr = (first_ok < 0) ? N : max(1, first_ok);
-      keep = max(1, min(keep, tr));
+      const int tr_ = (first_ok < 0) ? N : max(1, first_ok);
+      keep = max(1, min(keep, tr_));
     }
     s_keep = keep;
   }
   __syncthreads();
   const int keep = s_keep;
-  // WU[k][c] = W[k][ord_c]
-  auto wget = [&](int k, int c) -> float {
-    return Wd ? (float)Wd[(long)k * ldg + c] : Wm[(long)c * N + k];
-  };
-  for (int e = tid; e < N * keep; e += nthr) {
-    const int k = e / keep, c = e % keep;
-    w.WU[k * ld + c] = wget(k, w.ord[c]);
-  }
-  for (int c = tid; c < keep; c += nthr) sig[c] = (float)w.nrm[w.ord[c]];
+  for (int c = tid; c < keep; c += nthr) sig[c] = (float)nrm[ord[c]];
   float* rot = A.rot + p * A.rot_sp;
   for (int e = tid; e < keep * r; e += nthr) {
     const int c = e / r, k = e % r;
-    rot[c * ld + k] = wget(k, w.ord[c]);
+    rot[c * ld + k] = Wm[(long)ord[c] * N + k];
+  }
+  // the block's coordinates in the new basis: (B^T w_c)[r + j]
+  float* co = A.coords + p * A.coords_sp;
+  for (int e = tid; e < keep * b; e += nthr) {
+    const int j = e / keep, c = e % keep;
+    co[(long)j * A.coords_ld + c] = BT[(long)ord[c] * ldbt + r + j];
+  }
+  for (int e = tid; e < N * ldw; e += nthr) {  // WU[k][c] = W[k][ord_c], zero past keep
+    const int k = e / ldw, c = e % ldw;
+    WU[e] = c < keep ? Wm[(long)ord[c] * N + k] : 0.f;
   }
   __syncthreads();
-  // U_new = U W[:r] + Q^T W[r:]  (one thread per basis row)
-  {
-    constexpr int CB = 16;
-    for (int i = tid; i < n; i += nthr) {
-      const float* ur = U + (long)i * ld;
-      for (int c0 = 0; c0 < keep; c0 += CB) {
-        float acc[CB];
-#pragma unroll
-        for (int cc = 0; cc < CB; ++cc) acc[cc] = 0.f;
-        const int cn = min(CB, keep - c0);
-        for (int k = 0; k < r; ++k) {
-          const float uv = ur[k];
-          const float* wr = w.WU + (long)k * ld + c0;
-#pragma unroll
-          for (int cc = 0; cc < CB; ++cc)
-            if (cc < cn) acc[cc] = fmaf(uv, wr[cc], acc[cc]);
-        }
-        for (int j = 0; j < m; ++j) {
-          const float qv = w.Q[(long)j * n + i];
-          const float* wr = w.WU + (long)(r + j) * ld + c0;
-#pragma unroll
-          for (int cc = 0; cc < CB; ++cc)
-            if (cc < cn) acc[cc] = fmaf(qv, wr[cc], acc[cc]);
-        }
-        float* uo = Uo + (long)i * ld + c0;
-#pragma unroll
-        for (int cc = 0; cc < CB; ++cc)
-          if (c0 + cc < keep) uo[cc] = acc[cc];
+  // ----- U_new = U W[:r] + Q^T W[r:], then one Newton-Schulz step to orthonormal
+  cta_basis_rows(n, keep, r, m, Uc, lda, Q, WU, ldw, Uo, ld, uvec);
+  cta_tn(keep, keep, n, Uo, ld, Uo, ld, uvec, Pol, ldp, 1.f, part);  // E = U^T U - I
+  for (int e = tid; e < ldp * ldp; e += nthr) {
+    const int k = e / ldp, c = e % ldp;
+    if (k >= keep || c >= keep) Pol[e] = 0.f;
+  }
+  __syncthreads();
+  if (keep <= 32) {
+    cta_polish_rows(n, keep, Uo, ld, uvec, Pol, ldp);
+  } else {
+    float* WU2 = region(kRgWu2);  // W (I - E/2), then the basis is formed again
+    for (int e = tid; e < N * ldw; e += nthr) {
+      const int k = e / ldw, c = e % ldw;
+      float v = 0.f;
+      if (c < keep) {
+        v = WU[e];
+        for (int d = 0; d < keep; ++d) v = fmaf(-0.5f * WU[(long)k * ldw + d], Pol[(long)d * ldp + c], v);
       }
+      WU2[e] = v;
     }
     __syncthreads();
-  }
-  // coords[j][c] = sum_i U_new[i][c] X[j][i]
-  float* co = A.coords + p * A.coords_sp;
-  {
-    float* ct = (r_in_smem && (long)keep * b <= pool_floats) ? pool : w.a;
-    cta_proj_t(keep, b, n, Uo, ld, X, ct, b);
-    for (int e = tid; e < keep * b; e += nthr) {
-      const int c = e / b, j = e % b;
-      co[(long)j * A.coords_ld + c] = ct[e];
-    }
+    cta_basis_rows(n, keep, r, m, Uc, lda, Q, WU2, ldw, Uo, ld, uvec);
   }
   if (tid == 0) {
     int* d = A.dims + 4 * p;
@@ -832,23 +808,6 @@ __global__ void __launch_bounds__(1024) select_topk_kernel(int m, int k, const f
 }
 
 // recon[p][t][i] = sum_c U[i][c] (sum_j U[j][c] x[t][j]) for c < r[p].
-__global__ void __launch_bounds__(512) project_kernel(int n, int t, int ld, const float* u,
-                                                      long u_sp, const int* rr, const float* x,
-                                                      long x_sp, float* recon, long r_sp,
-                                                      float* coef_ws, long cw_sp) {
-  extern __shared__ __align__(16) float psm[];
-  const int p = blockIdx.x;
-  const int r = rr[p];
-  const float* U = u + p * u_sp;
-  const float* X = x + p * x_sp;
-  float* Rc = recon + p * r_sp;
-  float* Cf = coef_ws + p * cw_sp;  // [t][ld]
-  // coef[t][c] = sum_i X[t][i] U[i][c]
-  cta_gemm(t, r, n, X, n, 1, U, ld, 1, Cf, ld, 1, 1.f, 0.f, psm);
-  // recon[t][i] = sum_c coef[t][c] U[i][c]
-  cta_gemm(t, n, r, Cf, ld, 1, U, 1, ld, Rc, n, 1, 1.f, 0.f, psm);
-}
-
 }  // namespace kvd
 
 // ---------------------------------------------------------------- host glue
@@ -857,19 +816,54 @@ namespace kvd_host {
 
 using namespace kvd;
 
-long bug_step_ws_per_problem(int n, int b, int ld) { return align16(step_ws_bytes(n, b, ld)); }
-
-// Shared memory a step would like: gemm scratch + misc + the larger of the
-// residual phase (R and V_h) and the core phase (V_h, B^T and W).
-static long step_smem_want(int n, int b, int ld) {
-  const long N = ld + b, LB = ld + b;
-  const long phase1 = (long)b * n + (long)b * b;
-  const long phase2 = (long)b * b + N * LB + N * N;
-  return 4L * kGemmSmemFloats + kStepMiscBytes + 4L * (phase1 > phase2 ? phase1 : phase2);
+// Buffer placement for one launch.  Every region gets a workspace slot; the
+// regions that fit (in priority order) are staged in shared memory.
+static StepPlan plan_bug_step(int n, int b, int ld, long pool_max_floats) {
+  StepPlan P;
+  const long N = (long)ld + b;
+  P.b16 = (b + 15) & ~15;
+  P.ldb = P.b16 + 4;  // = 4 mod 8: a quarter-warp reading 8 rows as float4 is conflict-free
+  P.ldu = ld | 1;     // odd: one thread per row reads U[i][k] conflict-free
+  P.ldbt = (int)((N + 3) & ~3L);
+  P.ldw = (ld + 15) & ~15;
+  P.ldp = P.ldw > 32 ? P.ldw : 32;
+  long fl[kRgCount];
+  fl[kRgRm] = (long)b * n;
+  fl[kRgXr] = (long)n * P.ldb;
+  fl[kRgPart] = kPartFloats;
+  fl[kRgAs] = (long)ld * P.b16;
+  fl[kRgA2] = (long)ld * P.b16;
+  fl[kRgVh] = (long)b * b;
+  fl[kRgSmall] = 3 * (N + b) + 8;
+  fl[kRgCore] = N * P.ldbt + N * N;
+  fl[kRgPol] = (long)P.ldp * P.ldp;
+  fl[kRgWu] = N * P.ldw;
+  fl[kRgWu2] = N * P.ldw;
+  fl[kRgUs] = (long)n * P.ldu;
+  long wo = 0;
+  for (int g = 0; g < kRgCount; ++g) {
+    P.ws[g] = g == kRgUs ? -1 : wo;
+    if (g != kRgUs) wo += align16(4 * fl[g]) + 128;
+  }
+  P.ws_bytes = align16(wo);
+  const int prio[] = {kRgRm, kRgXr, kRgPart, kRgAs, kRgA2, kRgVh, kRgSmall,
+                      kRgCore, kRgPol, kRgWu, kRgUs, kRgWu2};
+  long used = 0;
+  for (int g = 0; g < kRgCount; ++g) P.smem[g] = -1;
+  for (int g : prio) {
+    const long sz = (fl[g] + 31) & ~31L;  // 128-byte aligned slots
+    if (used + sz <= pool_max_floats) {
+      P.smem[g] = used;
+      used += sz;
+    }
+  }
+  P.smem_bytes = (int)(kStepMiscBytes + 4 * used);
+  return P;
 }
 
-int launch_bug_step(const BugStepBatch& batch, int n_problems, int n_streams, cudaStream_t stream) {
-  const BugStepArgs& a0 = batch.s[0];
+long bug_step_ws_per_problem(int n, int b, int ld) { return plan_bug_step(n, b, ld, 0).ws_bytes; }
+
+int launch_bug_step(const BugStepBatch& batch_in, int n_problems, int n_streams, cudaStream_t stream) {
   static int max_dyn = 0;
   if (!max_dyn) {
     cudaFuncAttributes attr;
@@ -879,13 +873,23 @@ int launch_bug_step(const BugStepBatch& batch, int n_problems, int n_streams, cu
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     max_dyn = optin - (int)attr.sharedSizeBytes;
   }
-  long want = step_smem_want(a0.n, a0.b, a0.ld);
-  const int smem = (int)(want < max_dyn ? want : max_dyn);
+  BugStepBatch batch = batch_in;
+  const BugStepArgs& a0 = batch.s[0];
+  if (a0.ld > kMaxStepLd) {
+    set_error("bug step: basis width %d exceeds %d", a0.ld, kMaxStepLd);
+    return KVD_ERR_ARG;
+  }
+  batch.plan = plan_bug_step(a0.n, a0.b, a0.ld, (max_dyn - kStepMiscBytes) / 4);
+  if (a0.ws_sp < batch.plan.ws_bytes) {
+    set_error("bug step: workspace stride %ld < %ld bytes", a0.ws_sp, batch.plan.ws_bytes);
+    return KVD_ERR_WORKSPACE;
+  }
+  const int smem = batch.plan.smem_bytes;
   if (int rc = ensure_smem((const void*)bug_step_kernel, smem, "bug_step_kernel")) return rc;
   dim3 grid(n_problems, n_streams);
   {
     KTimerScope kts_("bug_step_kernel", stream);
-    bug_step_kernel<<<grid, kStepThreads, smem, stream>>>(batch, smem);
+    bug_step_kernel<<<grid, kStepThreads, smem, stream>>>(batch);
   }
   return check_launch("bug_step_kernel");
 }

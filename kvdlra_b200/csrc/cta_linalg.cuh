@@ -90,13 +90,14 @@ KVD_DEVICE void rr_pair(int i, int k, int np, int* a, int* b) {
   *b = idx(np - 1 - i);
 }
 
-// order[0..N) = indices of vals sorted descending, ties by lower index.
+// order[0..N) = indices of vals sorted descending, ties by lower index.  NaN
+// sorts below every number, so order is always a permutation.
 static __device__ void cta_argsort_desc(const double* vals, int N, int* order) {
   for (int i = threadIdx.x; i < N; i += blockDim.x) {
-    const double v = vals[i];
+    const double v = vals[i] == vals[i] ? vals[i] : -INFINITY;
     int rank = 0;
     for (int j = 0; j < N; ++j) {
-      const double w = vals[j];
+      const double w = vals[j] == vals[j] ? vals[j] : -INFINITY;
       rank += (w > v) || (w == v && j < i);
     }
     order[rank] = i;

@@ -19,7 +19,22 @@ struct BugStepArgs {
   int* status;
   char* ws; long ws_sp;                       // per-problem workspace bytes
 };
-struct BugStepBatch { BugStepArgs s[2]; };
+// Placement of the BUG step's buffers.  Every region has a slot in the
+// problem's global workspace (ws[g], bytes); the ones that fit are staged in
+// the dynamic shared-memory pool instead (smem[g] >= 0, floats).  U is staged
+// (kRgUs) only in shared memory; otherwise it is read in place.
+enum StepRegion {
+  kRgRm, kRgXr, kRgPart, kRgAs, kRgA2, kRgVh, kRgSmall, kRgCore, kRgPol, kRgWu, kRgWu2, kRgUs,
+  kRgCount
+};
+struct StepPlan {
+  long smem[kRgCount];  // float offset in the pool, -1 = in the workspace
+  long ws[kRgCount];    // byte offset in the per-problem workspace
+  long ws_bytes;        // per-problem workspace bytes
+  int b16, ldb, ldu, ldbt, ldw, ldp;
+  int smem_bytes;       // dynamic shared memory of the launch
+};
+struct BugStepBatch { BugStepArgs s[2]; StepPlan plan; };
 
 struct CarryArgs {
   float* c; long c_sp; int ld;     // [P][w_cap][ld]

@@ -457,7 +457,7 @@ extern "C" int kvd_check_status(const kvd_buffers* buf, kvd_stream_t stream) {
   cudaMemsetAsync(buf->status, 0, sizeof(h), (cudaStream_t)stream);
   if (h[kvd::kStatusTimeout]) { set_error("device wait timed out (code %d)", h[2]); return KVD_ERR_TIMEOUT; }
   if (h[kvd::kStatusBounds]) { set_error("device bounds check failed (code %d)", h[1]); return KVD_ERR_ARG; }
-  if (h[kvd::kStatusNumeric]) { set_error("Jacobi eigensolver did not converge (flags %d)", h[0]); return KVD_ERR_NUMERIC; }
+  if (h[kvd::kStatusNumeric]) { set_error("BUG step numerics failed (flags %d: 1 residual SVD or 2 core SVD not converged, 4 non-finite)", h[0]); return KVD_ERR_NUMERIC; }
   return KVD_OK;
 }
 

@@ -108,3 +108,23 @@ def test_batched_problems_independent() -> None:
         assert int(r[i]) == uo.shape[1]
         assert principal_angle(u[i, :, : int(r[i])].cpu().numpy(), uo) < 1e-3
         assert np.allclose(sig[i, : int(r[i])].cpu().numpy(), np.diag(bo), rtol=1e-4)
+
+
+@pytest.mark.parametrize("rank", [32, 48])
+def test_long_stream_stays_orthonormal(rank: int) -> None:
+    """300 BUG steps of 16 tokens: the basis stays orthonormal to fp32 level
+    (each step ends with a Newton-Schulz correction, so rounding and the
+    Jacobi stopping tolerance do not accumulate) and tracks the oracle's
+    subspace.  rank 48 exercises the correction for more than 32 columns."""
+    rng = np.random.default_rng(11)
+    n, t = 256, 300 * 16
+    basis = np.linalg.qr(rng.standard_normal((n, rank + 8)))[0]
+    scale = np.concatenate([2.0 ** (-np.arange(rank) / 16), np.full(8, 1e-2)])  # clear gap at rank
+    coef = rng.standard_normal((rank + 8, t)) * scale[:, None]
+    data = (basis @ coef + 1e-3 * rng.standard_normal((n, t))).astype(np.float32)
+    u = blocked_bug_subspace(torch.from_numpy(data).to(DEV), rank, 16).cpu().double().numpy()
+    assert u.shape[1] == rank
+    assert np.abs(u.T @ u - np.eye(rank)).max() < 1e-5
+    uo = oracle_blocked(data[:, :1600], rank, 16)
+    u_short = blocked_bug_subspace(torch.from_numpy(data[:, :1600]).to(DEV), rank, 16).cpu().numpy()
+    assert principal_angle(u_short, uo) < 1e-3
