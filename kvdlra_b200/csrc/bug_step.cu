@@ -33,51 +33,111 @@ constexpr int kStepMiscBytes = 1024;   // fp64 reduction scratch
 constexpr int kPartFloats = 8192;      // K-split partials: 16 warps x 32 lanes x 16
 constexpr int kMaxStepLd = 512;        // basis width the K-split partials cover
 
-// One-sided (Hestenes) Jacobi: orthogonalise the `cols` columns of X (column
-// c at X + c*ldx, `len` rows) by plane rotations, accumulated into V
-// (cols x cols, column-major, ldv; initialised to I here).  Round-robin
-// ordering; each column pair is handled by a group of G lanes that keeps the
-// pair's two columns in registers: lane gl holds the 4-float units
-// gl, gl + G, ... (EPL values, len <= G*EPL), so a group reads contiguous
-// 16-byte runs.  EPL = 0 streams longer columns from shared memory instead.
-// Only the warps that own a pair in a round issue anything, and the group
-// count per warp (32/G) is chosen by the caller to keep about four warps
-// busy, since a round is issue-bound.  The rotation zeroes the pair's inner
+// One-sided (Hestenes) Jacobi on augmented columns.  Column c of X (at
+// X + c*ldx) holds the data in rows [0, len), zeros in [len, voff) and, from
+// row voff (a multiple of 4), the accumulated rotations V[:, c] (cols rows,
+// initialised to e_c here), so one pass rotates data and V together:
+// X[:, :len] V = orthogonal columns, V = X[voff:voff+cols, :].
+// Round-robin ordering; each column pair is handled by a group of G lanes
+// that keeps the pair in registers as 4-float units: lane gl holds units
+// gl, gl + G, ..., NU of them, so a group reads and writes contiguous
+// 16-byte runs.  The column pitch covers the whole tile (ldx >= 4 G NU, rows
+// past the rotations zeroed), so the tile needs no bounds tests; shapes that
+// do not fit a tile stream the columns from shared memory (NU = 0).  Only
+// the warps that own pairs take part: they leave every round on a named
+// barrier of their own, while the other warps return at once and wait at
+// the caller's next __syncthreads.  The rotation zeroes the pair's inner
 // product (Golub & Van Loan sec. 8.6.3); its parameters come from the fast
 // reciprocal square root and are renormalised by one Newton step so
 // c^2 + s^2 = 1 to rounding (an inexact angle only slows convergence).  A
-// lane sums its own values in fp32 and the group reduces in ACC.
+// lane sums its data values in fp32 and the group reduces in ACC.
 // inv_scale2 is 1 / (squared Frobenius scale of the problem).  Returns the
-// sweeps taken (max_sweeps when not converged).
+// sweeps taken (max_sweeps when not converged) in the participating
+// threads.  Callers must __syncthreads() before reading X.
 constexpr double kJacobiFloor = 1e-30;
+constexpr int kJacobiBarrier = 1;  // named barrier id (0 is __syncthreads)
+// A sweep whose largest pair cosine was below this ends the iteration:
+// Jacobi converges quadratically, so the next sweep's cosines would be
+// ~1e-6, at the stopping tolerance, and the confirming sweep is skipped.
+constexpr float kJacobiQuadStop = 1e-3f;
 
-template <int G, int EPL, typename ACC>
-static __device__ int cta_hestenes(float* X, int len, int cols, int ldx, float* V, int ldv,
-                                   float tol, int max_sweeps, double inv_scale2) {
-  static_assert(EPL % 4 == 0, "values per lane come in 4-float units");
-  constexpr int NU = EPL / 4;  // units per lane
-  __shared__ int s_rot;
-  const int tid = threadIdx.x, nthr = blockDim.x;
-  const int groups = nthr / G, gid = tid / G, gl = tid % G;
-  const int warp_first_group = (tid / 32) * (32 / G);
-  for (int e = tid; e < cols * cols; e += nthr) {
-    const int c = e / cols, k = e % cols;
-    V[c * ldv + k] = (c == k) ? 1.f : 0.f;
+__device__ __forceinline__ void named_barrier(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Register tile of the one-sided Jacobi for `cols` columns of `nut` 4-float
+// units: lanes per pair G (about eight warps' worth of pairs, at most 9 units
+// per lane) and units per lane NU (0 = stream from shared memory).  The
+// same choice sizes the column pitch on the host.
+// The instantiated tiles: fp64 sums (long residual columns) G in {16, 32}
+// with NU in {2, 3, 5, 9}; fp32 sums (the core) G in {4, 8, 16}, NU in
+// {2, 3, 4, 6, 9}.  0 = none fits.
+__host__ __device__ inline int jacobi_nu(int g, int need, bool dbl) {
+  if (!(dbl ? (g == 16 || g == 32) : (g == 4 || g == 8 || g == 16))) return 0;
+  if (need <= 2) return 2;
+  if (need <= 3) return 3;
+  if (!dbl && need <= 4) return 4;
+  if (dbl && need <= 5) return 5;
+  if (!dbl && need <= 6) return 6;
+  if (need <= 9) return 9;
+  return 0;
+}
+
+__host__ __device__ inline void jacobi_tile(int nut, int cols, bool dbl, int* G, int* NU) {
+  const int half = (cols + 1) / 2;
+  int g = 32;
+  while (g > 4 && half * g > 256) g >>= 1;
+  while (g < 32 && g * 9 < nut) g <<= 1;
+  int nu = jacobi_nu(g, (nut + g - 1) / g, dbl);
+  // a tile padded far past the column (small problems) wastes shared
+  // memory: fewer lanes per pair then
+  while (nu && g > 4 && 4 * g * nu > 5 * nut + 8) {
+    const int g2 = g >> 1, nu2 = jacobi_nu(g2, (nut + g2 - 1) / g2, dbl);
+    if (!nu2) break;
+    g = g2;
+    nu = nu2;
   }
+  *G = nu ? g : 32;
+  *NU = nu;
+}
+// Column pitch (floats) a Jacobi on `rows` augmented rows x `cols` columns needs.
+__host__ __device__ inline int jacobi_pitch(int rows, int cols, bool dbl) {
+  int g, nu;
+  jacobi_tile((rows + 3) / 4, cols, dbl, &g, &nu);
+  const int r4 = (rows + 3) & ~3;
+  return nu ? (r4 > 4 * g * nu ? r4 : 4 * g * nu) : r4;
+}
+
+template <int G, int NU, typename ACC>
+static __device__ __forceinline__ int cta_hestenes(float* X, int len, int voff, int cols, int ldx,
+                                                   float tol, int max_sweeps, double inv_scale2) {
+  __shared__ int s_rot[3];
+  __shared__ unsigned s_maxc[3];  // largest squared pair cosine of a sweep (float bits)
+  const int tid = threadIdx.x, nthr = blockDim.x, warp = tid / 32, lane = tid % 32;
+  const int gid = tid / G, gl = tid % G;
+  const int vend = voff + ((cols + 3) & ~3);
+  const int rows = NU > 0 ? 4 * G * NU : vend;  // rows the tile touches; [len, rows) zeroed
+  for (long e = tid; e < (long)cols * (rows - len); e += nthr) {
+    const int c = (int)(e / (rows - len)), k = len + (int)(e % (rows - len));
+    X[(long)c * ldx + k] = (k - voff == c) ? 1.f : 0.f;
+  }
+  if (tid < 3) { s_rot[tid] = 0; s_maxc[tid] = 0u; }
   __syncthreads();
   if (cols <= 1) return 0;
-  const bool vec = ((reinterpret_cast<unsigned long>(X) & 15) == 0) && (ldx % 4 == 0);
-  const ACC tol2 = (ACC)tol * (ACC)tol;
-  const ACC is2 = (ACC)inv_scale2;
   const int np = cols + (cols & 1);
   const int half = np / 2;
+  const int groups = nthr / G;
+  const int aw = min(nthr / 32, (half * G + 31) / 32);  // warps that own pairs
+  if (warp >= aw) return 0;
+  const int nbar = aw * 32;
+  const int nud = voff / 4;  // data units
+  const ACC tol2 = (ACC)tol * (ACC)tol;
+  const ACC is2 = (ACC)inv_scale2;
   int sweep = 0;
   for (; sweep < max_sweeps; ++sweep) {
-    if (tid == 0) s_rot = 0;
-    __syncthreads();
+    if (tid == 0) { s_rot[(sweep + 1) % 3] = 0; s_maxc[(sweep + 1) % 3] = 0u; }
     for (int k = 0; k < np - 1; ++k) {
       for (int base = 0; base < half; base += groups) {
-        if (base + warp_first_group >= half) continue;  // warp owns no pair this round
         const int i = base + gid;
         int p = 0, q = -1;
         if (i < half) {
@@ -91,39 +151,31 @@ static __device__ int cta_hestenes(float* X, int len, int cols, int ldx, float* 
         float* xp = X + (long)p * ldx;
         float* xq = X + (long)(active ? q : p) * ldx;
         float4 up[NU > 0 ? NU : 1], uq[NU > 0 ? NU : 1];
-        float fal = 0.f, fbe = 0.f, fga = 0.f;
+        ACC al, be, ga;
         if constexpr (NU > 0) {
+          float fal = 0.f, fbe = 0.f, fga = 0.f;
 #pragma unroll
           for (int t = 0; t < NU; ++t) {
-            const int e = 4 * (gl + t * G);
-            if (active && vec && e + 4 <= len) {
-              up[t] = *reinterpret_cast<const float4*>(xp + e);
-              uq[t] = *reinterpret_cast<const float4*>(xq + e);
-            } else {
-              const bool a0 = active && e < len, a1 = active && e + 1 < len,
-                         a2 = active && e + 2 < len, a3 = active && e + 3 < len;
-              up[t] = make_float4(a0 ? xp[e] : 0.f, a1 ? xp[e + 1] : 0.f, a2 ? xp[e + 2] : 0.f,
-                                  a3 ? xp[e + 3] : 0.f);
-              uq[t] = make_float4(a0 ? xq[e] : 0.f, a1 ? xq[e + 1] : 0.f, a2 ? xq[e + 2] : 0.f,
-                                  a3 ? xq[e + 3] : 0.f);
+            const int u = gl + t * G;
+            up[t] = reinterpret_cast<const float4*>(xp)[u];
+            uq[t] = reinterpret_cast<const float4*>(xq)[u];
+            if (u < nud) {
+              fal = fmaf(up[t].x, up[t].x, fal); fal = fmaf(up[t].y, up[t].y, fal);
+              fal = fmaf(up[t].z, up[t].z, fal); fal = fmaf(up[t].w, up[t].w, fal);
+              fbe = fmaf(uq[t].x, uq[t].x, fbe); fbe = fmaf(uq[t].y, uq[t].y, fbe);
+              fbe = fmaf(uq[t].z, uq[t].z, fbe); fbe = fmaf(uq[t].w, uq[t].w, fbe);
+              fga = fmaf(up[t].x, uq[t].x, fga); fga = fmaf(up[t].y, uq[t].y, fga);
+              fga = fmaf(up[t].z, uq[t].z, fga); fga = fmaf(up[t].w, uq[t].w, fga);
             }
-            fal = fmaf(up[t].x, up[t].x, fal); fal = fmaf(up[t].y, up[t].y, fal);
-            fal = fmaf(up[t].z, up[t].z, fal); fal = fmaf(up[t].w, up[t].w, fal);
-            fbe = fmaf(uq[t].x, uq[t].x, fbe); fbe = fmaf(uq[t].y, uq[t].y, fbe);
-            fbe = fmaf(uq[t].z, uq[t].z, fbe); fbe = fmaf(uq[t].w, uq[t].w, fbe);
-            fga = fmaf(up[t].x, uq[t].x, fga); fga = fmaf(up[t].y, uq[t].y, fga);
-            fga = fmaf(up[t].z, uq[t].z, fga); fga = fmaf(up[t].w, uq[t].w, fga);
           }
-        }
-        ACC al = fal, be = fbe, ga = fga;
-        if constexpr (NU == 0) {  // long columns: stream them from shared memory twice
-          if (active) {
-            for (int e = gl; e < len; e += G) {
-              const ACC u = xp[e], v = xq[e];
-              al += u * u;
-              be += v * v;
-              ga += u * v;
-            }
+          al = fal; be = fbe; ga = fga;
+        } else {  // stream the columns from shared memory twice
+          al = 0; be = 0; ga = 0;
+          for (int e = gl; e < len; e += G) {
+            const ACC u = xp[e], v = xq[e];
+            al += u * u;
+            be += v * v;
+            ga += u * v;
           }
         }
 #pragma unroll
@@ -138,9 +190,13 @@ static __device__ int cta_hestenes(float* X, int len, int cols, int ldx, float* 
         al *= is2;
         be *= is2;
         ga *= is2;
-        if (!active || !(al > (ACC)kJacobiFloor && be > (ACC)kJacobiFloor) ||
-            ga * ga <= tol2 * al * be)
-          continue;
+        const bool live = active && al > (ACC)kJacobiFloor && be > (ACC)kJacobiFloor;
+        {  // the round's largest squared cosine, one shared atomic per warp
+          const float c2 = live ? __fdividef((float)(ga * ga), (float)(al * be)) : 0.f;
+          const unsigned m = __reduce_max_sync(0xffffffffu, __float_as_uint(c2));
+          if (lane == 0 && m) atomicMax(&s_maxc[sweep % 3], m);
+        }
+        if (!live || ga * ga <= tol2 * al * be) continue;
         const float zeta = __fdividef((float)be - (float)al, 2.f * (float)ga);
         const float az = fabsf(zeta);
         const float x1 = fmaf(zeta, zeta, 1.f);
@@ -153,66 +209,56 @@ static __device__ int cta_hestenes(float* X, int len, int cols, int ldx, float* 
         if constexpr (NU > 0) {
 #pragma unroll
           for (int t2 = 0; t2 < NU; ++t2) {
-            const int e = 4 * (gl + t2 * G);
+            const int u = gl + t2 * G;
             const float4 a = up[t2], bq = uq[t2];
-            const float4 np_ = make_float4(c * a.x - s * bq.x, c * a.y - s * bq.y,
-                                           c * a.z - s * bq.z, c * a.w - s * bq.w);
-            const float4 nq_ = make_float4(s * a.x + c * bq.x, s * a.y + c * bq.y,
-                                           s * a.z + c * bq.z, s * a.w + c * bq.w);
-            if (vec && e + 4 <= len) {
-              *reinterpret_cast<float4*>(xp + e) = np_;
-              *reinterpret_cast<float4*>(xq + e) = nq_;
-            } else {
-              if (e < len) { xp[e] = np_.x; xq[e] = nq_.x; }
-              if (e + 1 < len) { xp[e + 1] = np_.y; xq[e + 1] = nq_.y; }
-              if (e + 2 < len) { xp[e + 2] = np_.z; xq[e + 2] = nq_.z; }
-              if (e + 3 < len) { xp[e + 3] = np_.w; xq[e + 3] = nq_.w; }
-            }
+            reinterpret_cast<float4*>(xp)[u] = make_float4(c * a.x - s * bq.x, c * a.y - s * bq.y,
+                                                           c * a.z - s * bq.z, c * a.w - s * bq.w);
+            reinterpret_cast<float4*>(xq)[u] = make_float4(s * a.x + c * bq.x, s * a.y + c * bq.y,
+                                                           s * a.z + c * bq.z, s * a.w + c * bq.w);
           }
         } else {
-          for (int e = gl; e < len; e += G) {
+          for (int e = gl; e < vend; e += G) {
             const float u = xp[e], v = xq[e];
             xp[e] = c * u - s * v;
             xq[e] = s * u + c * v;
           }
         }
-        float* vp = V + (long)p * ldv;
-        float* vq = V + (long)q * ldv;
-        for (int e = gl; e < cols; e += G) {
-          const float u = vp[e], v = vq[e];
-          vp[e] = c * u - s * v;
-          vq[e] = s * u + c * v;
-        }
-        if (gl == 0) s_rot = 1;
+        if (gl == 0) s_rot[sweep % 3] = 1;
       }
-      __syncthreads();
+      named_barrier(kJacobiBarrier, nbar);
     }
-    const int any = s_rot;
-    __syncthreads();
-    if (!any) break;
+    if (!s_rot[sweep % 3]) break;
+    if (__uint_as_float(s_maxc[sweep % 3]) < kJacobiQuadStop * kJacobiQuadStop) break;
   }
   return sweep;
 }
 
-// Choose the group width: about four warps' worth of pairs per round, and
-// enough lanes that each holds at most 32 values of a column.
+// Dispatch to the register tile jacobi_tile picks when X is 16-byte aligned
+// and the pitch covers it, else stream.
 template <typename ACC>
-static __device__ int cta_hestenes_any(float* X, int len, int cols, int ldx, float* V, int ldv,
-                                       float tol, int max_sweeps, double inv_scale2) {
-  const int half = (cols + 1) / 2;
-  int G = 32;
-  while (G > 4 && half * G > 128) G >>= 1;
-  while (G < 32 && G * 32 < len) G <<= 1;
-  const int epl = (len + G - 1) / G;
-#define KVD_HJ(GG, EE)                                                                   \
-  if (G == GG && epl <= EE)                                                              \
-    return cta_hestenes<GG, EE, ACC>(X, len, cols, ldx, V, ldv, tol, max_sweeps, inv_scale2);
-  KVD_HJ(4, 4) KVD_HJ(4, 8) KVD_HJ(4, 12) KVD_HJ(4, 16) KVD_HJ(4, 24) KVD_HJ(4, 32)
-  KVD_HJ(8, 8) KVD_HJ(8, 16) KVD_HJ(8, 32)
-  KVD_HJ(16, 16) KVD_HJ(16, 32)
-  KVD_HJ(32, 16) KVD_HJ(32, 32)
+static __device__ __forceinline__ int cta_hestenes_any(float* X, int len, int voff, int cols,
+                                                       int ldx, float tol, int max_sweeps,
+                                                       double inv_scale2) {
+  const int nut = (voff + ((cols + 3) & ~3)) / 4;
+  int G, NU;
+  jacobi_tile(nut, cols, sizeof(ACC) == 8, &G, &NU);
+  const bool fits = NU > 0 && (reinterpret_cast<unsigned long>(X) & 15) == 0 && ldx % 4 == 0 &&
+                    ldx >= 4 * G * NU;
+  if (fits) {
+#define KVD_HJ(GG, UU)                                                                       \
+    if (G == GG && NU == UU)                                                                 \
+      return cta_hestenes<GG, UU, ACC>(X, len, voff, cols, ldx, tol, max_sweeps, inv_scale2);
+    if constexpr (sizeof(ACC) == 8) {
+      KVD_HJ(16, 2) KVD_HJ(16, 3) KVD_HJ(16, 5) KVD_HJ(16, 9)
+      KVD_HJ(32, 2) KVD_HJ(32, 3) KVD_HJ(32, 5) KVD_HJ(32, 9)
+    } else {
+      KVD_HJ(4, 2) KVD_HJ(4, 3) KVD_HJ(4, 4) KVD_HJ(4, 6) KVD_HJ(4, 9)
+      KVD_HJ(8, 2) KVD_HJ(8, 3) KVD_HJ(8, 4) KVD_HJ(8, 6) KVD_HJ(8, 9)
+      KVD_HJ(16, 2) KVD_HJ(16, 3) KVD_HJ(16, 4) KVD_HJ(16, 6) KVD_HJ(16, 9)
+    }
 #undef KVD_HJ
-  return cta_hestenes<32, 0, ACC>(X, len, cols, ldx, V, ldv, tol, max_sweeps, inv_scale2);
+  }
+  return cta_hestenes<32, 0, ACC>(X, len, voff, cols, ldx, tol, max_sweeps, inv_scale2);
 }
 
 // 16 consecutive floats p[j0 .. j0+16) of a row, zero past `nb`; `vec` =
@@ -250,7 +296,7 @@ static __device__ __forceinline__ void store16(float* p, int j0, int nb, bool ve
 // k-chunks x ks K-slices; a lane owns one k and 16 j sums in fp32 over its
 // slice, and the slices' partials are added in fp64.  A row of B is read as
 // a broadcast, so B[i] rows are 16-byte vectors when `bvec`.
-static __device__ void cta_tn(int M, int NB, int K, const float* A, int lda, const float* B,
+static __device__ __forceinline__ void cta_tn(int M, int NB, int K, const float* A, int lda, const float* B,
                               int ldb, bool bvec, float* out, int ldo, float diag, float* part) {
   const int tid = threadIdx.x, nthr = blockDim.x, lane = tid % 32, warp = tid / 32;
   const int nw = nthr / 32;
@@ -293,11 +339,12 @@ static __device__ void cta_tn(int M, int NB, int K, const float* A, int lda, con
 
 // Rows of the residual, one thread per row i, 16 tokens at a time:
 //   v = (from_xr ? XR[i][j] : Rm[j][i]) - sum_{k<K} A[i*lda + k] C[k*ldc + j]
-// written to Rm[j*n + i] (j < b) and, when to_xr, to XR[i*ldb + j].  C rows
+// written to Rm[j*ldr + i] (j < b) and, when to_xr, to XR[i*ldb + j].  C rows
 // and XR rows are 16-byte aligned (ldc, ldb multiples of 4).
-static __device__ void cta_rows_sub(int n, int b, int b16, int K, const float* A, int lda,
+static __device__ __forceinline__ void cta_rows_sub(int n, int b, int b16, int K, const float* A, int lda,
                                     const float* C, int ldc, float* XR, int ldb, float* Rm,
-                                    bool from_xr, bool to_xr) {
+                                    int ldr, bool from_xr, bool to_xr) {
+  const bool avec = ((reinterpret_cast<unsigned long>(A) & 15) == 0) && (lda % 4 == 0);
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     const float* ar = A + (long)i * lda;
     float* xr = XR + (long)i * ldb;
@@ -307,9 +354,23 @@ static __device__ void cta_rows_sub(int n, int b, int b16, int K, const float* A
         load16(xr, j0, b16, true, acc);
       } else {
 #pragma unroll
-        for (int jj = 0; jj < 16; ++jj) acc[jj] = (j0 + jj < b) ? Rm[(long)(j0 + jj) * n + i] : 0.f;
+        for (int jj = 0; jj < 16; ++jj) acc[jj] = (j0 + jj < b) ? Rm[(long)(j0 + jj) * ldr + i] : 0.f;
       }
-      for (int k = 0; k < K; ++k) {
+      int k = 0;
+      if (avec) {
+        for (; k + 4 <= K; k += 4) {
+          const float4 a4 = *reinterpret_cast<const float4*>(ar + k);
+          const float av[4] = {a4.x, a4.y, a4.z, a4.w};
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            float cv[16];
+            load16(C + (long)(k + kk) * ldc, j0, b16, true, cv);
+#pragma unroll
+            for (int jj = 0; jj < 16; ++jj) acc[jj] = fmaf(-av[kk], cv[jj], acc[jj]);
+          }
+        }
+      }
+      for (; k < K; ++k) {
         const float av = ar[k];
         float cv[16];
         load16(C + (long)k * ldc, j0, b16, true, cv);
@@ -318,7 +379,7 @@ static __device__ void cta_rows_sub(int n, int b, int b16, int K, const float* A
       }
 #pragma unroll
       for (int jj = 0; jj < 16; ++jj)
-        if (j0 + jj < b) Rm[(long)(j0 + jj) * n + i] = acc[jj];
+        if (j0 + jj < b) Rm[(long)(j0 + jj) * ldr + i] = acc[jj];
       if (to_xr) store16(xr, j0, b16, true, acc);
     }
   }
@@ -328,7 +389,7 @@ static __device__ void cta_rows_sub(int n, int b, int b16, int K, const float* A
 // Uo[i*ld + c] = sum_{k<r} A[i*lda + k] WU[k*ldw + c] + sum_{j<m} Q[j*n + i] WU[(r+j)*ldw + c]
 // for c < keep; one thread per row, 16 columns at a time (WU rows 16-byte
 // aligned and zero-padded to ldw).
-static __device__ void cta_basis_rows(int n, int keep, int r, int m, const float* A, int lda,
+static __device__ __forceinline__ void cta_basis_rows(int n, int keep, int r, int m, const float* A, int lda,
                                       const float* Q, const float* WU, int ldw, float* Uo, int ld,
                                       bool uvec) {
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
@@ -357,19 +418,21 @@ static __device__ void cta_basis_rows(int n, int keep, int r, int m, const float
   __syncthreads();
 }
 
-// Uo[i][c] -= 1/2 sum_k Uo[i][k] E[k][c] for c < keep <= 32, one thread per
-// row holding it in registers (E zero-padded to 32 x 32, row stride lde).
-static __device__ void cta_polish_rows(int n, int keep, float* Uo, int ld, bool uvec,
-                                       const float* E, int lde) {
+// Uo[i][c] = S[i][c] - 1/2 sum_k S[i][k] E[k][c] for c < keep <= 32, one
+// thread per row holding it in registers (E zero-padded to 32 x 32, row
+// stride lde).  S may be Uo itself.
+static __device__ __forceinline__ void cta_polish_rows(int n, int keep, const float* S, int lds,
+                                                       bool svec, float* Uo, int ld, bool uvec,
+                                                       const float* E, int lde) {
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    float* ur = Uo + (long)i * ld;
+    const float* sr = S + (long)i * lds;
     float row[32];
     {
       float t[16];
-      load16(ur, 0, keep, uvec, t);
+      load16(sr, 0, keep, svec, t);
 #pragma unroll
       for (int c = 0; c < 16; ++c) row[c] = t[c];
-      load16(ur, 16, keep, uvec, t);
+      load16(sr, 16, keep, svec, t);
 #pragma unroll
       for (int c = 0; c < 16; ++c) row[16 + c] = t[c];
     }
@@ -389,14 +452,59 @@ static __device__ void cta_polish_rows(int n, int keep, float* Uo, int ld, bool 
           for (int cc = 0; cc < 16; ++cc) acc[cc] = fmaf(h, ev[cc], acc[cc]);
         }
       }
-      store16(ur, c0, keep, uvec, acc);
+      store16(Uo + (long)i * ld, c0, keep, uvec, acc);
     }
   }
   __syncthreads();
 }
 
+// Un[i*ldn + c] = sum_{k<r} Un[i*ldn + k] WU[k*ldw + c] + sum_{j<m} Q[j*n + i] WU[(r+j)*ldw + c]
+// for c < keep <= 32, in place: a thread reads its whole row of U before it
+// writes the row of U_new.  WU and Un rows are 16-byte aligned (ldw, ldn
+// multiples of 4), WU zero past keep.
+static __device__ __forceinline__ void cta_basis_rows32(int n, int keep, int r, int m, float* Un,
+                                                        int ldn, const float* Q, const float* WU,
+                                                        int ldw) {
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    float* ur = Un + (long)i * ldn;
+    float acc[32];
+#pragma unroll
+    for (int c = 0; c < 32; ++c) acc[c] = 0.f;
+    float u4[4];
+    for (int k = 0; k < r + m; ++k) {
+      float av;
+      if (k < r) {
+        if ((k & 3) == 0) {
+          if (k + 4 <= r) {
+            const float4 t = *reinterpret_cast<const float4*>(ur + k);
+            u4[0] = t.x; u4[1] = t.y; u4[2] = t.z; u4[3] = t.w;
+          } else {
+            for (int kk = 0; kk < 4; ++kk) u4[kk] = k + kk < r ? ur[k + kk] : 0.f;
+          }
+        }
+        av = u4[k & 3];
+      } else {
+        av = Q[(long)(k - r) * n + i];
+      }
+      float w[16];
+      load16(WU + (long)k * ldw, 0, ldw, true, w);
+#pragma unroll
+      for (int c = 0; c < 16; ++c) acc[c] = fmaf(av, w[c], acc[c]);
+      if (keep > 16) {
+        load16(WU + (long)k * ldw, 16, ldw, true, w);
+#pragma unroll
+        for (int c = 0; c < 16; ++c) acc[16 + c] = fmaf(av, w[c], acc[16 + c]);
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < 32; ++c)
+      if (c < keep) ur[c] = acc[c];
+  }
+  __syncthreads();
+}
+
 // Column norms (fp64) of X[:, 0..cols) into nrm, then order = descending.
-static __device__ void cta_colnorm_order(const float* X, int len, int cols, int ldx, double* nrm,
+static __device__ __forceinline__ void cta_colnorm_order(const float* X, int len, int cols, int ldx, double* nrm,
                                          int* order) {
   const int lane = threadIdx.x % 32, warp = threadIdx.x / 32, nw = blockDim.x / 32;
   for (int c = warp; c < cols; c += nw) {
@@ -414,7 +522,7 @@ static __device__ void cta_colnorm_order(const float* X, int len, int cols, int 
 // Gram-Schmidt applied twice; a row that collapses (numerically dependent or
 // null) is replaced by the first canonical vector e_i that survives the same
 // orthogonalisation.  Used only when some admitted direction is (near) null.
-static __device__ void cta_cgs2_rows(float* Q, int m, int n, double* dots /*>= m*/,
+static __device__ __forceinline__ void cta_cgs2_rows(float* Q, int m, int n, double* dots /*>= m*/,
                                      double* red /*>=32*/) {
   __shared__ double s_norm, s_norm0;
   __shared__ int s_next_e;
@@ -470,6 +578,10 @@ static __device__ void cta_cgs2_rows(float* Q, int m, int n, double* dots /*>= m
   }
 }
 
+// kSmem: every buffer of the plan is staged in shared memory, so all of them
+// are addressed from the shared pool and compile to shared-memory loads and
+// stores; otherwise each region may live in the global workspace.
+template <bool kSmem>
 __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch batch) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const StepPlan& P = batch.plan;
@@ -485,15 +597,15 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
   double* red = reinterpret_cast<double*>(smem_raw);  // 64 doubles
   float* pool = reinterpret_cast<float*>(smem_raw + kStepMiscBytes);
   auto region = [&](int g) -> float* {
+    if constexpr (kSmem) return pool + P.smem[g];
     return P.smem[g] >= 0 ? pool + P.smem[g] : reinterpret_cast<float*>(wsb + P.ws[g]);
   };
-  float* Rm = region(kRgRm);      // [b][n]  residual columns (Jacobi input)
+  float* Rm = region(kRgRm);      // residual columns (pitch n, then ldr with V below)
   float* XR = region(kRgXr);      // [n][ldb] block rows, then residual rows, then Q [m][n]
   float* part = region(kRgPart);  // K-split partials
   float* AS = region(kRgAs);      // [ld][b16] a = U^T X
   float* A2 = region(kRgA2);      // [ld][b16] re-orthogonalisation correction
-  float* Vh = region(kRgVh);      // [b][b] right vectors of R (column-major)
-  float* BT = region(kRgCore);    // [N][ldbt] B^T, then [N][N] W behind it
+  float* BT = region(kRgCore);    // [N][ldbt] B^T columns with W below them
   float* Pol = region(kRgPol);    // [ldp][ldp] U_new^T U_new - I
   float* WU = region(kRgWu);      // [N][ldw] top left vectors of B, ordered
   double* nrm = reinterpret_cast<double*>(region(kRgSmall));  // [ld+b]
@@ -501,7 +613,9 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
   int* ord = reinterpret_cast<int*>(sv + b);                  // [ld+b]
   int* ordh = ord + (ld + b);                                 // [b]
   const bool us = P.smem[kRgUs] >= 0 && r > 0;
-  const float* Uc = us ? pool + P.smem[kRgUs] : U;
+  const float* Uc;
+  if constexpr (kSmem) Uc = pool + P.smem[kRgUs];  // read only when r > 0
+  else Uc = us ? pool + P.smem[kRgUs] : U;
   const int lda = us ? P.ldu : ld;
   const int b16 = P.b16, ldb = P.ldb, ldbt = P.ldbt, ldw = P.ldw, ldp = P.ldp;
   const bool uvec = ((reinterpret_cast<unsigned long>(Uo) & 15) == 0) && (ld % 4 == 0);
@@ -518,10 +632,33 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
     __syncthreads();
     if (tid == 0) { double t = 0; for (int i = 0; i < nthr / 32; ++i) t += red[i]; s_xnorm2 = t; }
   }
-  // ----- stage the block token-transposed (XR[i][j] = X[j][i], zero past b) and U
-  for (long e = tid; e < (long)b * n; e += nthr) {
-    const int j = (int)(e / n), i = (int)(e % n);
-    XR[(long)i * ldb + j] = X[e];
+  // ----- stage the block token-transposed (XR[i][j] = X[j][i], zero past b) and U,
+  // 16-byte loads with four in flight per thread where the layout allows
+  if ((n & 3) == 0 && (reinterpret_cast<unsigned long>(X) & 15) == 0) {
+    const float4* X4 = reinterpret_cast<const float4*>(X);
+    const long n4 = (long)b * n / 4;
+    for (long e0 = tid; e0 < n4; e0 += 4L * nthr) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const long e = e0 + (long)u * nthr;
+        if (e < n4) v[u] = X4[e];
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const long e = e0 + (long)u * nthr;
+        if (e < n4) {
+          const int j = (int)(4 * e / n), i = (int)(4 * e % n);
+          float* d = XR + (long)i * ldb + j;
+          d[0] = v[u].x; d[ldb] = v[u].y; d[2 * ldb] = v[u].z; d[3 * ldb] = v[u].w;
+        }
+      }
+    }
+  } else {
+    for (long e = tid; e < (long)b * n; e += nthr) {
+      const int j = (int)(e / n), i = (int)(e % n);
+      XR[(long)i * ldb + j] = X[e];
+    }
   }
   if (b16 > b) {
     const int pad = b16 - b;
@@ -530,43 +667,68 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
   }
   if (us) {
     float* dst = pool + P.smem[kRgUs];
-    for (long e = tid; e < (long)n * r; e += nthr) {
-      const long i = e / r, k = e % r;
-      dst[i * lda + k] = U[i * ld + k];
+    if ((r & 3) == 0 && (ld & 3) == 0 && (reinterpret_cast<unsigned long>(U) & 15) == 0) {
+      const int r4 = r / 4;
+      const long n4 = (long)n * r4;
+      for (long e0 = tid; e0 < n4; e0 += 4L * nthr) {
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const long e = e0 + (long)u * nthr;
+          if (e < n4) v[u] = *reinterpret_cast<const float4*>(U + (e / r4) * ld + 4 * (e % r4));
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const long e = e0 + (long)u * nthr;
+          if (e < n4) {
+            float* d = dst + (e / r4) * lda + 4 * (e % r4);
+            d[0] = v[u].x; d[1] = v[u].y; d[2] = v[u].z; d[3] = v[u].w;
+          }
+        }
+      }
+    } else {
+      for (long e = tid; e < (long)n * r; e += nthr) {
+        const long i = e / r, k = e % r;
+        dst[i * lda + k] = U[i * ld + k];
+      }
     }
   }
   for (int e = tid; e < r * b16; e += nthr) { AS[e] = 0.f; A2[e] = 0.f; }
   __syncthreads();
+  // SVD geometry.  b <= n: one-sided Jacobi on R's b columns, R V = [s_j q_j].
+  // b > n (more columns than rows cannot all be made orthogonal): on the n
+  // columns of R^T, R^T J = [s_j v_j], so J holds the left vectors q_j.
+  // The rotations accumulate below the data in each column (rows voff..).
+  const bool tr = b > n;
+  const int nsv = tr ? n : b;
+  const int rlen = tr ? b : n;
+  const int voff = (rlen + 3) & ~3;
+  const int ldr = jacobi_pitch(voff + nsv, nsv, true);
+  const int ldr0 = tr ? n : ldr;  // pitch the residual is formed with
   // ----- residual R = (I - U U^T)^2 X (the reference's re-orthogonalised residual)
   if (r > 0) cta_tn(r, b, n, Uc, lda, XR, ldb, true, AS, b16, 0.f, part);  // a = U^T X
-  cta_rows_sub(n, b, b16, r, Uc, lda, AS, b16, XR, ldb, Rm, true, r > 0);  // R = X - U a
+  cta_rows_sub(n, b, b16, r, Uc, lda, AS, b16, XR, ldb, Rm, ldr0, true, r > 0);  // R = X - U a
   if (r > 0) {
     cta_tn(r, b, n, Uc, lda, XR, ldb, true, A2, b16, 0.f, part);             // a2 = U^T R
-    cta_rows_sub(n, b, b16, r, Uc, lda, A2, b16, XR, ldb, Rm, false, false);  // R -= U a2
+    cta_rows_sub(n, b, b16, r, Uc, lda, A2, b16, XR, ldb, Rm, ldr0, false, false);  // R -= U a2
     for (int e = tid; e < r * b16; e += nthr) AS[e] += A2[e];
     __syncthreads();
   }
-  // ----- SVD of R by one-sided Jacobi.  b <= n: on R's b columns, R V = [s_j q_j].
-  // b > n (more columns than rows cannot all be made orthogonal): on the n
-  // columns of R^T, R^T J = [s_j v_j], so J holds the left vectors q_j.
-  const bool tr = b > n;
-  const int nsv = tr ? n : b;
+  // ----- SVD of R
   const double inv_x2 = s_xnorm2 > 0.0 ? 1.0 / s_xnorm2 : 1.0;
-  int sw;
-  if (!tr) {
-    sw = cta_hestenes_any<double>(Rm, n, b, n, Vh, b, 1.2e-7f * sqrtf((float)n) + 2.4e-7f, 30, inv_x2);
-    cta_colnorm_order(Rm, n, b, n, sv, ordh);
-  } else {
+  if (tr) {
     for (long e = tid; e < (long)b * n; e += nthr) XR[e] = Rm[e];
     __syncthreads();
-    for (long e = tid; e < (long)b * n; e += nthr) {  // Rm[i*b + j] = R[i][j]
+    for (long e = tid; e < (long)b * n; e += nthr) {  // column i of R^T: R[i][0..b)
       const int i = (int)(e / b), j = (int)(e % b);
-      Rm[e] = XR[(long)j * n + i];
+      Rm[(long)i * ldr + j] = XR[(long)j * n + i];
     }
     __syncthreads();
-    sw = cta_hestenes_any<double>(Rm, b, n, b, Vh, n, 1.2e-7f * sqrtf((float)b) + 2.4e-7f, 30, inv_x2);
-    cta_colnorm_order(Rm, b, n, b, sv, ordh);
   }
+  int sw = cta_hestenes_any<double>(Rm, rlen, voff, nsv, ldr,
+                                    1.2e-7f * sqrtf((float)rlen) + 2.4e-7f, 30, inv_x2);
+  __syncthreads();
+  cta_colnorm_order(Rm, rlen, nsv, ldr, sv, ordh);
   if (sw >= 30 && tid == 0) atomicOr(&A.status[kStatusNumeric], 1);
   if (tid == 0) {
     const float xnorm = (float)sqrt(s_xnorm2);
@@ -593,48 +755,41 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
   __syncthreads();
   const int m = s_m;
   float* Q = XR;  // [m][n]
-  if (!tr) {
-    for (long e = tid; e < (long)m * n; e += nthr) {
-      const int j = (int)(e / n), i = (int)(e % n);
-      const int oj = ordh[j];
+  for (long e = tid; e < (long)m * n; e += nthr) {
+    const int j = (int)(e / n), i = (int)(e % n);
+    const int oj = ordh[j];
+    if (!tr) {  // q_j = (R V)[:, o_j] / s_j
       const double sj = sv[oj];
-      Q[e] = sj > 0.0 ? (float)(Rm[(long)oj * n + i] / sj) : 0.f;
-    }
-  } else {
-    for (long e = tid; e < (long)m * n; e += nthr) {  // q_j = J[:, ord_j]
-      const int j = (int)(e / n), i = (int)(e % n);
-      Q[e] = Vh[(long)ordh[j] * n + i];
-    }
-    __syncthreads();  // J is overwritten next
-    for (long e = tid; e < (long)n * b; e += nthr) {  // v_c = (R^T J)[:, c] / s_c
-      const int c = (int)(e / b);
-      const double sc = sv[c];
-      Vh[e] = sc > 0.0 ? (float)(Rm[e] / sc) : 0.f;
+      Q[e] = sj > 0.0 ? (float)(Rm[(long)oj * ldr + i] / sj) : 0.f;
+    } else {    // q_j = J[:, o_j]
+      Q[e] = Rm[(long)oj * ldr + voff + i];
     }
   }
   __syncthreads();
   if (s_degenerate) cta_cgs2_rows(Q, m, n, nrm, red);
   // ----- the core B = [[diag(sigma), a], [0, diag(s_m) V_m^T]] ((r+m) x (r+b)):
-  // its left singular vectors W and values by one-sided Jacobi on B^T.
+  // its left singular vectors W and values by one-sided Jacobi on B^T, with
+  // W accumulated below each column.
   const int N = r + m, LB = r + b;
-  float* Wm = BT + (long)N * ldbt;  // W[c*N + k]
+  const int woff = (LB + 3) & ~3;
   for (long e = tid; e < (long)N * LB; e += nthr) {
     const int c = (int)(e / LB), row = (int)(e % LB);
     float v = 0.f;
     if (c < r) {
       if (row < r) v = (row == c) ? sig[c] : 0.f;
       else v = AS[c * b16 + (row - r)];
-    } else if (row >= r) {
-      const int oj = ordh[c - r];
-      v = (float)sv[oj] * Vh[(long)oj * b + (row - r)];
+    } else if (row >= r) {  // s_j v_j^T, the residual's right part
+      const int oj = ordh[c - r], l = row - r;
+      v = tr ? Rm[(long)oj * ldr + l] : (float)sv[oj] * Rm[(long)oj * ldr + voff + l];
     }
     BT[(long)c * ldbt + row] = v;
   }
   __syncthreads();
   double b2 = s_xnorm2;  // ||B||_F^2 <= ||sigma||^2 + ||X||_F^2 sets the core's scale
   for (int c = 0; c < r; ++c) b2 += (double)sig[c] * sig[c];
-  sw = cta_hestenes_any<float>(BT, LB, N, ldbt, Wm, N, 1.2e-7f * sqrtf((float)LB) + 2.4e-7f, 30,
+  sw = cta_hestenes_any<float>(BT, LB, woff, N, ldbt, 1.2e-7f * sqrtf((float)LB) + 2.4e-7f, 30,
                                b2 > 0.0 ? 1.0 / b2 : 1.0);
+  __syncthreads();
   cta_colnorm_order(BT, LB, N, ldbt, nrm, ord);
   if (sw >= 30 && tid == 0) atomicOr(&A.status[kStatusNumeric], 2);
   if (tid == 0) {
@@ -657,32 +812,56 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
   __syncthreads();
   const int keep = s_keep;
   for (int c = tid; c < keep; c += nthr) sig[c] = (float)nrm[ord[c]];
-  float* rot = A.rot + p * A.rot_sp;
-  for (int e = tid; e < keep * r; e += nthr) {
-    const int c = e / r, k = e % r;
-    rot[c * ld + k] = Wm[(long)ord[c] * N + k];
-  }
-  // the block's coordinates in the new basis: (B^T w_c)[r + j]
-  float* co = A.coords + p * A.coords_sp;
-  for (int e = tid; e < keep * b; e += nthr) {
-    const int j = e / keep, c = e % keep;
-    co[(long)j * A.coords_ld + c] = BT[(long)ord[c] * ldbt + r + j];
-  }
+  float* CB = A2;  // [keep][b16] the block's coordinates W^T B[:, r:], ordered
   for (int e = tid; e < N * ldw; e += nthr) {  // WU[k][c] = W[k][ord_c], zero past keep
     const int k = e / ldw, c = e % ldw;
-    WU[e] = c < keep ? Wm[(long)ord[c] * N + k] : 0.f;
+    WU[e] = c < keep ? BT[(long)ord[c] * ldbt + woff + k] : 0.f;
+  }
+  for (int e = tid; e < keep * b; e += nthr) {  // the rotated B^T column holds (B^T w_c)[r + j]
+    const int c = e / b, j = e % b;
+    CB[c * b16 + j] = BT[(long)ord[c] * ldbt + r + j];
   }
   __syncthreads();
-  // ----- U_new = U W[:r] + Q^T W[r:], then one Newton-Schulz step to orthonormal
-  cta_basis_rows(n, keep, r, m, Uc, lda, Q, WU, ldw, Uo, ld, uvec);
-  cta_tn(keep, keep, n, Uo, ld, Uo, ld, uvec, Pol, ldp, 1.f, part);  // E = U^T U - I
+  // ----- U_new = U W[:r] + Q^T W[r:], then one Newton-Schulz step to orthonormal.
+  // Up to 32 columns with everything staged: U_new is formed in place of the
+  // staged U (each thread owns its rows) and polished from there.
+  const bool un_smem = kSmem && keep <= 32;
+  if (un_smem) {
+    float* Un = pool + P.smem[kRgUs];
+    cta_basis_rows32(n, keep, r, m, Un, P.ldu, Q, WU, ldw);
+    cta_tn(keep, keep, n, Un, P.ldu, Un, P.ldu, true, Pol, ldp, 1.f, part);  // E = U^T U - I
+  } else {
+    cta_basis_rows(n, keep, r, m, Uc, lda, Q, WU, ldw, Uo, ld, uvec);
+    cta_tn(keep, keep, n, Uo, ld, Uo, ld, uvec, Pol, ldp, 1.f, part);
+  }
   for (int e = tid; e < ldp * ldp; e += nthr) {
     const int k = e / ldp, c = e % ldp;
     if (k >= keep || c >= keep) Pol[e] = 0.f;
   }
   __syncthreads();
-  if (keep <= 32) {
-    cta_polish_rows(n, keep, Uo, ld, uvec, Pol, ldp);
+  // The carry map and the block's coordinates refer to the polished basis
+  // U' = U (I - E/2):  rot' = U'^T U_old = (I - E/2) W[:r]^T and
+  // c' = U'^T x = (I - E/2) W^T B[:, r:], where the rotated B^T column of
+  // ordered value c holds W^T B's row c (its rows r.. are (B^T w_c)[r + j]).
+  float* rot = A.rot + p * A.rot_sp;
+  for (int e = tid; e < keep * r; e += nthr) {  // rot'[c][k] = W[k][c] - 1/2 sum_d W[k][d] E[d][c]
+    const int k = e / keep, c = e % keep;
+    const float* wr = WU + (long)k * ldw;
+    float corr = 0.f;
+    for (int d = 0; d < keep; ++d) corr = fmaf(wr[d], Pol[(long)d * ldp + c], corr);
+    rot[c * ld + k] = fmaf(-0.5f, corr, wr[c]);
+  }
+  float* co = A.coords + p * A.coords_sp;
+  for (int e = tid; e < keep * b; e += nthr) {  // c'[j][c] = CB[c][j] - 1/2 sum_d E[d][c] CB[d][j]
+    const int j = e / keep, c = e % keep;   // (E is exactly symmetric: both halves sum alike)
+    float corr = 0.f;
+    for (int d = 0; d < keep; ++d) corr = fmaf(Pol[(long)d * ldp + c], CB[d * b16 + j], corr);
+    co[(long)j * A.coords_ld + c] = fmaf(-0.5f, corr, CB[c * b16 + j]);
+  }
+  if (un_smem) {
+    cta_polish_rows(n, keep, pool + P.smem[kRgUs], P.ldu, true, Uo, ld, uvec, Pol, ldp);
+  } else if (keep <= 32) {
+    cta_polish_rows(n, keep, Uo, ld, uvec, Uo, ld, uvec, Pol, ldp);
   } else {
     float* WU2 = region(kRgWu2);  // W (I - E/2), then the basis is formed again
     for (int e = tid; e < N * ldw; e += nthr) {
@@ -823,19 +1002,33 @@ static StepPlan plan_bug_step(int n, int b, int ld, long pool_max_floats) {
   const long N = (long)ld + b;
   P.b16 = (b + 15) & ~15;
   P.ldb = P.b16 + 4;  // = 4 mod 8: a quarter-warp reading 8 rows as float4 is conflict-free
-  P.ldu = ld | 1;     // odd: one thread per row reads U[i][k] conflict-free
-  P.ldbt = (int)((N + 3) & ~3L);
+  // = 4 mod 8: one thread per row reading its row as float4 (a quarter-warp
+  // covers 8 rows) and a warp reading a row as a broadcast are conflict-free
+  P.ldu = (ld + 3) & ~3;
+  if (P.ldu % 8 == 0) P.ldu += 4;
+  // B^T rows (<= ld + b) then W rows (<= ld + b), padded for the largest tile
+  P.ldbt = 0;
+  for (int nn = 1; nn <= N; ++nn) {
+    const int pb = jacobi_pitch((int)((N + 3) & ~3L) + nn, nn, false);
+    if (pb > P.ldbt) P.ldbt = pb;
+  }
+  P.ldbt = (P.ldbt + 3) & ~3;
   P.ldw = (ld + 15) & ~15;
   P.ldp = P.ldw > 32 ? P.ldw : 32;
   long fl[kRgCount];
-  fl[kRgRm] = (long)b * n;
+  // residual columns with their rotations below: min(n, b) columns of
+  // round4(n) + round4(b) rows (b > n transposes R first)
+  {
+    const int nsv = n < b ? n : b, rlen = n < b ? b : n;
+    fl[kRgRm] = (long)nsv * jacobi_pitch(((rlen + 3) & ~3) + nsv, nsv, true);
+  }
+  if (fl[kRgRm] < (long)b * n) fl[kRgRm] = (long)b * n;
   fl[kRgXr] = (long)n * P.ldb;
   fl[kRgPart] = kPartFloats;
   fl[kRgAs] = (long)ld * P.b16;
   fl[kRgA2] = (long)ld * P.b16;
-  fl[kRgVh] = (long)b * b;
   fl[kRgSmall] = 3 * (N + b) + 8;
-  fl[kRgCore] = N * P.ldbt + N * N;
+  fl[kRgCore] = N * P.ldbt;
   fl[kRgPol] = (long)P.ldp * P.ldp;
   fl[kRgWu] = N * P.ldw;
   fl[kRgWu2] = N * P.ldw;
@@ -846,7 +1039,7 @@ static StepPlan plan_bug_step(int n, int b, int ld, long pool_max_floats) {
     if (g != kRgUs) wo += align16(4 * fl[g]) + 128;
   }
   P.ws_bytes = align16(wo);
-  const int prio[] = {kRgRm, kRgXr, kRgPart, kRgAs, kRgA2, kRgVh, kRgSmall,
+  const int prio[] = {kRgRm, kRgXr, kRgPart, kRgAs, kRgA2, kRgSmall,
                       kRgCore, kRgPol, kRgWu, kRgUs, kRgWu2};
   long used = 0;
   for (int g = 0; g < kRgCount; ++g) P.smem[g] = -1;
@@ -866,12 +1059,14 @@ long bug_step_ws_per_problem(int n, int b, int ld) { return plan_bug_step(n, b, 
 int launch_bug_step(const BugStepBatch& batch_in, int n_problems, int n_streams, cudaStream_t stream) {
   static int max_dyn = 0;
   if (!max_dyn) {
-    cudaFuncAttributes attr;
+    cudaFuncAttributes a1, a2;
     int dev = 0, optin = 0;
-    cudaFuncGetAttributes(&attr, (const void*)bug_step_kernel);
+    cudaFuncGetAttributes(&a1, (const void*)bug_step_kernel<true>);
+    cudaFuncGetAttributes(&a2, (const void*)bug_step_kernel<false>);
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    max_dyn = optin - (int)attr.sharedSizeBytes;
+    const int st = (int)(a1.sharedSizeBytes > a2.sharedSizeBytes ? a1.sharedSizeBytes : a2.sharedSizeBytes);
+    max_dyn = optin - st;
   }
   BugStepBatch batch = batch_in;
   const BugStepArgs& a0 = batch.s[0];
@@ -884,12 +1079,16 @@ int launch_bug_step(const BugStepBatch& batch_in, int n_problems, int n_streams,
     set_error("bug step: workspace stride %ld < %ld bytes", a0.ws_sp, batch.plan.ws_bytes);
     return KVD_ERR_WORKSPACE;
   }
+  bool all_smem = true;
+  for (int g = 0; g < kRgCount; ++g) all_smem = all_smem && batch.plan.smem[g] >= 0;
   const int smem = batch.plan.smem_bytes;
-  if (int rc = ensure_smem((const void*)bug_step_kernel, smem, "bug_step_kernel")) return rc;
+  const void* fn = all_smem ? (const void*)bug_step_kernel<true> : (const void*)bug_step_kernel<false>;
+  if (int rc = ensure_smem(fn, smem, "bug_step_kernel")) return rc;
   dim3 grid(n_problems, n_streams);
   {
     KTimerScope kts_("bug_step_kernel", stream);
-    bug_step_kernel<<<grid, kStepThreads, smem, stream>>>(batch);
+    if (all_smem) bug_step_kernel<true><<<grid, kStepThreads, smem, stream>>>(batch);
+    else bug_step_kernel<false><<<grid, kStepThreads, smem, stream>>>(batch);
   }
   return check_launch("bug_step_kernel");
 }

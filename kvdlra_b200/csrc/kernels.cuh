@@ -24,7 +24,7 @@ struct BugStepArgs {
 // the dynamic shared-memory pool instead (smem[g] >= 0, floats).  U is staged
 // (kRgUs) only in shared memory; otherwise it is read in place.
 enum StepRegion {
-  kRgRm, kRgXr, kRgPart, kRgAs, kRgA2, kRgVh, kRgSmall, kRgCore, kRgPol, kRgWu, kRgWu2, kRgUs,
+  kRgRm, kRgXr, kRgPart, kRgAs, kRgA2, kRgSmall, kRgCore, kRgPol, kRgWu, kRgWu2, kRgUs,
   kRgCount
 };
 struct StepPlan {
