@@ -226,6 +226,228 @@ __global__ void __launch_bounds__(kDecThreads) decode_split_kernel(DecArgs a) {
   }
 }
 
+// ---------------------------------------------------------------- tiled decode
+// Tokens in tiles of kTT, a CTA walking kTilesPerCta consecutive tiles of one
+// (problem, KV group) with the online-softmax state in registers.  A tile is
+// either verbatim (sinks + exact tier, or the ring: K/V rows read directly)
+// or middle: its keys are rebuilt as the register-tiled product
+// C_k (kTT x r) U_k,g^T (r x D) -- a thread owns 4 tokens x 2*DPT dims that
+// form DPT rotate-half pairs, so RoPE is applied in registers -- and its
+// values accumulate in coordinate space.  One partial record per CTA.
+constexpr int kTT = 64;
+constexpr int kTileThreads = 128;
+constexpr int kTilesPerCta = 8;
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kTileThreads) decode_tile_kernel(DecArgs a, int nv0, int nm,
+                                                                   int n_tiles) {
+  constexpr int half = D / 2, DPT = half / 8;  // pairs per thread
+  constexpr int ldk = D + 4;                   // = 4 mod 8: row-per-lane float4 reads conflict-free
+  extern __shared__ __align__(16) float tsm[];
+  const int chunk = blockIdx.x, g = blockIdx.y, p = blockIdx.z;
+  const int G = a.G, ld = a.ld, n = a.H * D;
+  const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
+  const int r_k = a.rk[p], r_v = a.rv[p];
+  const int ldc = ld + 4;
+  float* qs = tsm;                    // [G][D]
+  float* ks = qs + G * D;             // [kTT][ldk] keys of the tile
+  float* vs = ks + kTT * ldk;         // [kTT][ldk] values, or [kTT][ldc] value coordinates
+  float* ps = vs + kTT * ldk;         // [G][kTT] scores, then probabilities
+  float* ut = ps + G * kTT;           // [ld][D] U_k,g^T
+  constexpr int kTTp = kTT + 4;       // = 4 mod 8: transposing writes spread over banks
+  float* ct = ut + ld * D;            // [ld][kTTp] key coordinates, transposed
+  float* st = ct + ld * kTTp;         // [G][4] -, -, running max, rescale of the tile
+  const T* qp = reinterpret_cast<const T*>(a.q) + (long)p * a.Hq * D;
+  for (int e = tid; e < G * D; e += kTileThreads) qs[e] = load_f<T>(qp + (long)(g * G + e / D) * D + e % D);
+  const int mid0 = a.sink_len + a.hh_len;
+  // running state: outputs o = tid + kTileThreads * k over [acc_d (G x D) | acc_c (G x ld)]
+  const int n_out = G * (D + ld);
+  constexpr int kMaxOut = 12;  // (G <= 8) x (D + ld <= 192) / 128
+  float acc[kMaxOut];
+#pragma unroll
+  for (int k = 0; k < kMaxOut; ++k) acc[k] = 0.f;
+  float m_run = -INFINITY, l_run = 0.f;  // of head `warp`-strided: kept in st for all threads
+  if (tid < G) { st[4 * tid + 2] = -INFINITY; }
+  float lsum[2] = {0.f, 0.f};  // l_run of heads warp, warp + 4 (owned by lane 0 of each warp)
+  (void)m_run; (void)l_run;
+  // the thread's inverse frequencies (middle tiles)
+  const int dg = tid % 8, tg = tid / 8;
+  float invf[DPT];
+#pragma unroll
+  for (int j = 0; j < DPT; ++j) invf[j] = a.inv_freq[dg * DPT + j];
+  const int t_begin = chunk * kTilesPerCta, t_end = min(n_tiles, t_begin + kTilesPerCta);
+  if (t_end > nv0 && t_begin < nv0 + nm) {  // U_k,g^T, once for the CTA's middle tiles
+    const float* U = a.uk + p * a.u_sp;
+    for (int e = tid; e < ld * D; e += kTileThreads) {
+      const int d = e / ld, c = e % ld;
+      ut[c * D + d] = c < r_k ? U[(long)(g * D + d) * ld + c] : 0.f;
+    }
+  }
+  for (int tile = t_begin; tile < t_end; ++tile) {
+    __syncthreads();  // previous tile's buffers are free
+    int kind, j0, ntok;
+    if (tile < nv0) { kind = 0; j0 = tile * kTT; ntok = min(kTT, mid0 - j0); }
+    else if (tile < nv0 + nm) { kind = 1; j0 = (tile - nv0) * kTT; ntok = min(kTT, a.W - j0); }
+    else { kind = 2; j0 = (tile - nv0 - nm) * kTT; ntok = min(kTT, a.ring_len - j0); }
+    if (kind != 1) {
+      for (int e = tid; e < kTT * D; e += kTileThreads) {
+        const int tt = e / D, d = e % D;
+        float kv = 0.f, vv = 0.f;
+        if (tt < ntok) {
+          const int t = j0 + tt;
+          const T* kr; const T* vr;
+          if (kind == 2) {
+            kr = reinterpret_cast<const T*>(a.ring_k) + p * a.ring_sp + (long)t * n;
+            vr = reinterpret_cast<const T*>(a.ring_v) + p * a.ring_sp + (long)t * n;
+          } else if (t < a.sink_len) {
+            kr = reinterpret_cast<const T*>(a.sink_k) + p * a.sink_sp + (long)t * n;
+            vr = reinterpret_cast<const T*>(a.sink_v) + p * a.sink_sp + (long)t * n;
+          } else {
+            kr = reinterpret_cast<const T*>(a.hh_k) + p * a.hh_sp + (long)(t - a.sink_len) * n;
+            vr = reinterpret_cast<const T*>(a.hh_v) + p * a.hh_sp + (long)(t - a.sink_len) * n;
+          }
+          kv = load_f<T>(kr + g * D + d);
+          vv = load_f<T>(vr + g * D + d);
+        }
+        ks[tt * ldk + d] = kv;
+        vs[tt * ldk + d] = vv;
+      }
+    } else {
+      const float* Ck = a.ck + p * a.c_sp + (long)j0 * ld;
+      const float* Cv = a.cv + p * a.c_sp + (long)j0 * ld;
+      for (int e = tid; e < kTT * ld; e += kTileThreads) {
+        const int tt = e / ld, c = e % ld;
+        const bool in = tt < ntok;
+        ct[c * kTTp + tt] = (in && c < r_k) ? Ck[(long)tt * ld + c] : 0.f;
+        vs[tt * ldc + c] = (in && c < r_v) ? Cv[(long)tt * ld + c] : 0.f;
+      }
+      __syncthreads();
+      float kacc[4][2 * DPT];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 2 * DPT; ++j) kacc[i][j] = 0.f;
+      for (int c = 0; c < r_k; ++c) {
+        const float4 cv4 = *reinterpret_cast<const float4*>(ct + c * kTTp + 4 * tg);
+        const float cc[4] = {cv4.x, cv4.y, cv4.z, cv4.w};
+        float uu[2 * DPT];
+#pragma unroll
+        for (int j = 0; j < DPT; j += 4) {
+          const float4 lo = *reinterpret_cast<const float4*>(ut + c * D + dg * DPT + j);
+          const float4 hi = *reinterpret_cast<const float4*>(ut + c * D + half + dg * DPT + j);
+          uu[j] = lo.x; uu[j + 1] = lo.y; uu[j + 2] = lo.z; uu[j + 3] = lo.w;
+          uu[DPT + j] = hi.x; uu[DPT + j + 1] = hi.y; uu[DPT + j + 2] = hi.z; uu[DPT + j + 3] = hi.w;
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 2 * DPT; ++j) kacc[i][j] = fmaf(cc[i], uu[j], kacc[i][j]);
+      }
+      // RoPE at each column's true position on the pairs (f, f + D/2)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int tt = 4 * tg + i;
+        const int jj = j0 + tt;
+        const int pos = tt < ntok ? (a.mid_pos ? a.mid_pos[p * a.mid_sp + jj] : a.pos_base + jj) : 0;
+#pragma unroll
+        for (int j = 0; j < DPT; ++j) {
+          float cs, sn;
+          rope_cs(pos, invf[j], a.rope_scale, &cs, &sn);
+          float y1, y2;
+          rope_apply_pair(kacc[i][j], kacc[i][DPT + j], cs, sn, &y1, &y2);
+          ks[tt * ldk + dg * DPT + j] = y1;
+          ks[tt * ldk + half + dg * DPT + j] = y2;
+        }
+      }
+    }
+    __syncthreads();
+    // scores of the group's query heads: thread -> token tt, heads hs, hs + 2, ...
+    {
+      const int tt = tid % kTT, hs = tid / kTT;
+      const float* kr = ks + tt * ldk;
+      for (int h = hs; h < G; h += kTileThreads / kTT) {
+        const float* qr = qs + h * D;
+        float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+        for (int d = 0; d < D; d += 8) {
+          const float4 k0 = *reinterpret_cast<const float4*>(kr + d);
+          const float4 k1 = *reinterpret_cast<const float4*>(kr + d + 4);
+          const float4 q0 = *reinterpret_cast<const float4*>(qr + d);
+          const float4 q1 = *reinterpret_cast<const float4*>(qr + d + 4);
+          s0 = fmaf(q0.x, k0.x, s0); s0 = fmaf(q0.y, k0.y, s0); s0 = fmaf(q0.z, k0.z, s0); s0 = fmaf(q0.w, k0.w, s0);
+          s1 = fmaf(q1.x, k1.x, s1); s1 = fmaf(q1.y, k1.y, s1); s1 = fmaf(q1.z, k1.z, s1); s1 = fmaf(q1.w, k1.w, s1);
+        }
+        ps[h * kTT + tt] = tt < ntok ? (s0 + s1) * a.scaling : -INFINITY;
+      }
+    }
+    __syncthreads();
+    // per head: tile max and probabilities relative to the new running max
+    for (int h = warp; h < G; h += kTileThreads / 32) {
+      float* pr = ps + h * kTT;
+      const float x0 = pr[lane], x1 = pr[lane + 32];
+      float mt = fmaxf(x0, x1);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o));
+      const float mold = st[4 * h + 2];
+      const float mnew = fmaxf(mold, mt);
+      const float e0 = mnew == -INFINITY ? 0.f : expf(x0 - mnew);
+      const float e1 = mnew == -INFINITY ? 0.f : expf(x1 - mnew);
+      pr[lane] = e0;
+      pr[lane + 32] = e1;
+      float ls = e0 + e1;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
+      const float corr = (mold == -INFINITY) ? 0.f : expf(mold - mnew);
+      if (lane == 0) {
+        const int slot = h / (kTileThreads / 32);
+        lsum[slot] = lsum[slot] * corr + ls;
+        st[4 * h + 2] = mnew;
+        st[4 * h + 3] = corr;
+      }
+    }
+    __syncthreads();
+    // accumulate: acc_d over verbatim tokens, acc_c over middle tokens
+#pragma unroll
+    for (int k = 0; k < kMaxOut; ++k) {
+      const int o = tid + kTileThreads * k;
+      if (o >= n_out) break;
+      int h;
+      float add = 0.f;
+      if (o < G * D) {
+        h = o / D;
+        if (kind != 1) {
+          const int d = o % D;
+          const float* pr = ps + h * kTT;
+          for (int tt = 0; tt < ntok; ++tt) add = fmaf(pr[tt], vs[tt * ldk + d], add);
+        }
+      } else {
+        const int oc = o - G * D;
+        h = oc / ld;
+        if (kind == 1) {
+          const int c = oc % ld;
+          const float* pr = ps + h * kTT;
+          for (int tt = 0; tt < ntok; ++tt) add = fmaf(pr[tt], vs[tt * ldc + c], add);
+        }
+      }
+      acc[k] = fmaf(acc[k], st[4 * h + 3], add);
+    }
+  }
+  __syncthreads();
+  // the CTA's partial record: m[G], l[G], acc_d[G][D], acc_c[G][ld]
+  float* out = a.part + ((long)(p * a.H + g) * a.n_chunks + chunk) * a.part_sp_chunk;
+  for (int h = warp; h < G; h += kTileThreads / 32)
+    if (lane == 0) {
+      out[h] = t_begin < t_end ? st[4 * h + 2] : -INFINITY;
+      out[G + h] = lsum[h / (kTileThreads / 32)];
+    }
+#pragma unroll
+  for (int k = 0; k < kMaxOut; ++k) {
+    const int o = tid + kTileThreads * k;
+    if (o >= n_out) break;
+    out[2 * G + o] = acc[k];
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(128) decode_merge_kernel(DecArgs a) {
   extern __shared__ __align__(16) float msm2[];
@@ -320,11 +542,27 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
   a.pos_base = (int)(k.cumulative_length - k.ring_len - (k.hh_len + k.w_len));
   a.inv_freq = c.inv_freq; a.rope_scale = c.rope_scaling;
   a.q = q; a.out = out; a.scaling = scaling;
-  a.n_chunks = dec_chunks(a.L);
   a.part_sp_chunk = part_floats(a.G, a.D, a.ld);
+  // tiled kernel: head_dim 64 or 128, rank <= head_dim, G <= 8
+  const bool tiled = (a.D == 64 || a.D == 128) && a.ld <= a.D && a.G <= 8 &&
+                     a.G * (a.D + a.ld) <= 12 * kTileThreads;
+  const int mid0 = a.sink_len + a.hh_len;
+  const int nv0 = (mid0 + kTT - 1) / kTT, nm = (a.W + kTT - 1) / kTT,
+            nr = (a.ring_len + kTT - 1) / kTT;
+  const int n_tiles = nv0 + nm + nr;
+  a.n_chunks = tiled ? (n_tiles + kTilesPerCta - 1) / kTilesPerCta : dec_chunks(a.L);
   const size_t need = (size_t)count * a.H * a.n_chunks * a.part_sp_chunk * 4;
   if (need > ws_bytes) { set_error("factored decode: workspace too small"); return KVD_ERR_WORKSPACE; }
   a.part = (float*)ws;
+  if (tiled) {
+    const int tsmem = 4 * (a.G * a.D + 2 * kTT * (a.D + 4) + a.G * kTT + a.ld * a.D +
+                           a.ld * (kTT + 4) + 4 * a.G);
+    dim3 tgrid(a.n_chunks, a.H, count);
+#define KVD_TDEC(DD)                                                                                {                                                                                                 if (int rc0 = ensure_smem((const void*)decode_tile_kernel<T, DD>, tsmem,                                                  "decode_tile_kernel")) return rc0;                                    KTimerScope kts_("decode_tile_kernel", s);                                                      decode_tile_kernel<T, DD><<<tgrid, kTileThreads, tsmem, s>>>(a, nv0, nm, n_tiles);            }
+    if (a.D == 64) KVD_TDEC(64)
+    else KVD_TDEC(128)
+#undef KVD_TDEC
+  } else {
   const int smem = 4 * (a.G * a.D + a.ld * a.D + 4 * a.ld + 4 * (int)a.part_sp_chunk);
   dim3 grid(a.n_chunks, a.H, count);
   const int nv = (a.D + 31) / 32, nc = (a.ld + 31) / 32;
@@ -343,6 +581,7 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
   else if (nc <= 4) KVD_DEC(4, 4)
   else KVD_DEC(4, 6)
 #undef KVD_DEC
+  }
   int rc = check_launch("decode_split_kernel");
   if (rc) return rc;
   const int msmem = 4 * (a.G * a.ld + a.G * a.D + 2 * a.G);
