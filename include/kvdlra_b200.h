@@ -204,6 +204,25 @@ int kvd_surprise(int32_t n_batch, int32_t n, int32_t m, int32_t ld_u, const floa
 int kvd_select_topk(int32_t n_batch, int32_t m, int32_t k, const float* scores,
                     int32_t* keep_idx, int32_t* demote_idx, kvd_stream_t stream);
 
+/* ------------------------------------------------------- prefill press */
+
+/* Blocked BUG projection of one feature-by-token matrix, held token-major as
+ * x [t][n] fp32 (replaces bug_press.py:231-304 _exact_mask /
+ * _lowrank_reconstruct on top of streaming_torch.py:192-258
+ * blocked_bug_subspace / blocked_bug_project).  Columns c < n_sink and the
+ * n_exact largest-norm columns after them (ties to the lower index) form the
+ * exact set; the rest, in order, drive augmented BUG steps over blocks of
+ * block_size columns (rank_cap <= 512, theta if has_theta) and are written as
+ * U U^T x_c to out [t][n]; exact columns are copied.  mask_out [t] (may be
+ * NULL) receives 1 for exact columns.  out == NULL computes the exact set
+ * only.  Synchronises the stream once to read the sweep's numerical status. */
+int kvd_blocked_project(int32_t n, int32_t t, int32_t rank_cap, int32_t block_size,
+                        int32_t n_sink, int32_t n_exact, int32_t has_theta, float theta,
+                        const float* x, float* out, uint8_t* mask_out, void* workspace,
+                        size_t ws_bytes, kvd_stream_t stream);
+size_t kvd_blocked_project_workspace_bytes(int32_t n, int32_t t, int32_t rank_cap,
+                                           int32_t block_size);
+
 /* Workspace bytes kvd_factored_decode needs for `count` problems. */
 size_t kvd_decode_workspace_bytes(const kvd_config* cfg, int32_t count, int32_t num_q_heads);
 

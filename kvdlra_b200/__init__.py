@@ -5,6 +5,7 @@ Public surface (drop-in for kvdlra's):
   cache (src/kvdlra/cache/bug_cache.py);
 * :func:`augmented_bug_step`, :func:`blocked_bug_subspace`,
   :func:`blocked_bug_project` -- the integrator (streaming_torch.py);
+* :class:`BUGPress` -- the prefill low-rank press (src/kvdlra/press/bug_press.py);
 * :mod:`kvdlra_b200.accounting` -- the float-equivalent charge (accounting.py).
 
 The compute runs in ``_lib/libkvdlra_b200.so`` (built by
@@ -13,9 +14,10 @@ The compute runs in ``_lib/libkvdlra_b200.so`` (built by
 
 from .cache import BugStreamingCache, BugStreamingLayer, RopeAngles
 from .integrator import augmented_bug_step, blocked_bug_project, blocked_bug_subspace
+from .press import BUGPress
 
 __all__ = [
     "BugStreamingCache", "BugStreamingLayer", "RopeAngles",
-    "augmented_bug_step", "blocked_bug_project", "blocked_bug_subspace",
+    "augmented_bug_step", "blocked_bug_project", "blocked_bug_subspace", "BUGPress",
 ]
 __version__ = "0.1.0"

@@ -31,7 +31,6 @@ __host__ __device__ inline long align16(long x) { return (x + 15) & ~15L; }
 constexpr int kStepThreads = 512;
 constexpr int kStepMiscBytes = 1024;   // fp64 reduction scratch
 constexpr int kPartFloats = 8192;      // K-split partials: 16 warps x 32 lanes x 16
-constexpr int kMaxStepLd = 512;        // basis width the K-split partials cover
 
 // One-sided (Hestenes) Jacobi on augmented columns.  Column c of X (at
 // X + c*ldx) holds the data in rows [0, len), zeros in [len, voff) and, from

@@ -91,6 +91,7 @@ struct KTimerScope {
 int ensure_smem(const void* func, size_t bytes, const char* name);
 using kvd::BugStepBatch; using kvd::CarryBatch; using kvd::CandSrc; using kvd::RopeArgs; using kvd::SelectOut;
 long bug_step_ws_per_problem(int n, int b, int ld);
+constexpr int kMaxStepLd = 512;  // widest basis the BUG step supports
 int launch_bug_step(const BugStepBatch& batch, int n_problems, int n_streams, cudaStream_t stream);
 int launch_carry(const CarryBatch& batch, int n_problems, int n_streams, int ld, cudaStream_t stream);
 int launch_surprise_f32(int nb, int n, int m, int ld, const float* u, long u_sp, const int* r,

@@ -108,7 +108,26 @@ def blocked_bug_subspace(M: Tensor, rank_cap: int, block_size: int = 128, *,
 def blocked_bug_project(M: Tensor, rank_cap: int, block_size: int = 128, *,
                         theta: float | None = None,
                         compute_dtype: torch.dtype = torch.float32) -> Tensor:
-    """``U (U^T M)`` onto the tracked subspace (streaming_torch.py:241-258)."""
-    u = blocked_bug_subspace(M, rank_cap, block_size, theta=theta, compute_dtype=compute_dtype)
-    mc = M.to(torch.float32)
-    return (u @ (u.mT @ mc)).to(M.dtype)
+    """``U (U^T M)`` onto the tracked subspace (streaming_torch.py:241-258):
+    the BUG sweep and the projection run in ``kvd_blocked_project``."""
+    if not M.is_cuda:
+        raise RuntimeError("kvdlra_b200 integrator runs on CUDA tensors only")
+    if rank_cap < 1:
+        raise ValueError(f"rank_cap must be >= 1, got {rank_cap}")
+    if block_size < 1:
+        raise ValueError(f"block_size must be >= 1, got {block_size}")
+    if compute_dtype != torch.float32:
+        raise NotImplementedError("the GPU integrator computes in float32")
+    n, t = M.shape
+    if t == 0:
+        return M.clone()
+    xt = M.T.to(torch.float32).contiguous()
+    out = torch.empty_like(xt)
+    L = N.lib()
+    wsb = int(L.kvd_blocked_project_workspace_bytes(n, t, rank_cap, block_size)) + 256
+    ws = torch.empty(wsb, dtype=torch.uint8, device=M.device)
+    N.check(L.kvd_blocked_project(n, t, rank_cap, block_size, 0, 0, int(theta is not None),
+                                  float(theta or 0.0), xt.data_ptr(), out.data_ptr(), None,
+                                  ws.data_ptr(), wsb, N.stream_ptr(M.device)),
+            "kvd_blocked_project")
+    return out.T.to(M.dtype)
