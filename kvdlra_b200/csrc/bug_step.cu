@@ -917,6 +917,81 @@ __global__ void __launch_bounds__(256) carry_kernel(CarryBatch batch, int tokens
   }
 }
 
+// The same carry with each thread owning two token rows (t, t + W/2 of the
+// CTA's range): the rows (R >= r_old floats, read as 16-byte vectors) and
+// their R outputs stay in registers, and every rot^T vector broadcast from
+// shared memory feeds both rows.  Needs ld % 4 == 0 and ld <= R.
+template <int R>
+__global__ void __launch_bounds__(256) carry_reg_kernel(CarryBatch batch) {
+  extern __shared__ __align__(16) float rsm[];  // rotT [R][R]
+  const CarryArgs A = blockIdx.z ? batch.s[1] : batch.s[0];  // no dynamic indexing of the parameter
+  const int p = blockIdx.y;
+  const int r_old = A.dims[4 * p], keep = A.dims[4 * p + 1];
+  const int ld = A.ld;
+  if (r_old == 0) return;
+  const float* rot = A.rot + p * A.rot_sp;
+  for (int e = threadIdx.x; e < R * R; e += blockDim.x) {
+    const int k = e / R, c = e % R;
+    rsm[e] = (k < r_old && c < keep) ? rot[c * ld + k] : 0.f;
+  }
+  __syncthreads();
+  const int t0 = blockIdx.x * 2 * blockDim.x + threadIdx.x;
+  const int t1 = t0 + blockDim.x;
+  if (t0 >= batch.W) return;
+  const bool two = t1 < batch.W;
+  float* c0 = A.c + p * A.c_sp + (long)t0 * ld;
+  float* c1 = A.c + p * A.c_sp + (long)(two ? t1 : t0) * ld;
+  float row0[R], row1[R];
+#pragma unroll
+  for (int q = 0; q < R / 4; ++q) {
+    float4 v0 = make_float4(0.f, 0.f, 0.f, 0.f), v1 = v0;
+    if (4 * q < ld) {
+      v0 = reinterpret_cast<const float4*>(c0)[q];
+      v1 = reinterpret_cast<const float4*>(c1)[q];
+    }
+    const float a0[4] = {v0.x, v0.y, v0.z, v0.w}, a1[4] = {v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      row0[4 * q + i] = 4 * q + i < r_old ? a0[i] : 0.f;
+      row1[4 * q + i] = 4 * q + i < r_old ? a1[i] : 0.f;
+    }
+  }
+  float acc0[R], acc1[R];
+#pragma unroll
+  for (int c = 0; c < R; ++c) { acc0[c] = 0.f; acc1[c] = 0.f; }
+  const float4* rt4 = reinterpret_cast<const float4*>(rsm);
+#pragma unroll
+  for (int k = 0; k < R; ++k) {
+    const float x0 = row0[k], x1 = row1[k];
+#pragma unroll
+    for (int q = 0; q < R / 4; ++q) {
+      const float4 w = rt4[k * (R / 4) + q];
+      acc0[4 * q] = fmaf(w.x, x0, acc0[4 * q]);
+      acc0[4 * q + 1] = fmaf(w.y, x0, acc0[4 * q + 1]);
+      acc0[4 * q + 2] = fmaf(w.z, x0, acc0[4 * q + 2]);
+      acc0[4 * q + 3] = fmaf(w.w, x0, acc0[4 * q + 3]);
+      acc1[4 * q] = fmaf(w.x, x1, acc1[4 * q]);
+      acc1[4 * q + 1] = fmaf(w.y, x1, acc1[4 * q + 1]);
+      acc1[4 * q + 2] = fmaf(w.z, x1, acc1[4 * q + 2]);
+      acc1[4 * q + 3] = fmaf(w.w, x1, acc1[4 * q + 3]);
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < R / 4; ++q) {
+    if (4 * q + 3 < keep) {
+      reinterpret_cast<float4*>(c0)[q] = make_float4(acc0[4 * q], acc0[4 * q + 1], acc0[4 * q + 2], acc0[4 * q + 3]);
+      if (two) reinterpret_cast<float4*>(c1)[q] = make_float4(acc1[4 * q], acc1[4 * q + 1], acc1[4 * q + 2], acc1[4 * q + 3]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        if (4 * q + i < keep) {
+          c0[4 * q + i] = acc0[4 * q + i];
+          if (two) c1[4 * q + i] = acc1[4 * q + i];
+        }
+    }
+  }
+}
+
 // Low-rank surprise of fp32 token-major columns (bug_cache.py:906-921).
 __global__ void __launch_bounds__(256) surprise_f32_kernel(int n, int m, int ld, const float* u,
                                                             long u_sp, const int* rr,
@@ -1094,6 +1169,22 @@ int launch_bug_step(const BugStepBatch& batch_in, int n_problems, int n_streams,
 
 int launch_carry(const CarryBatch& batch, int n_problems, int n_streams, int ld, cudaStream_t stream) {
   if (batch.W <= 0) return KVD_OK;
+  bool aligned = ld % 4 == 0;
+  for (int i = 0; i < n_streams; ++i)
+    aligned = aligned && (reinterpret_cast<uintptr_t>(batch.s[i].c) % 16 == 0) && batch.s[i].c_sp % 4 == 0;
+  if (aligned && ld <= 64) {
+    if (ld > 32)
+      if (int rc = ensure_smem((const void*)carry_reg_kernel<64>, 4 * 64 * 64, "carry_kernel")) return rc;
+    KTimerScope kts_("carry_kernel", stream);
+    if (ld <= 32) {  // 128 threads x 2 rows: ~170 registers each, several CTAs per SM
+      dim3 grid((batch.W + 255) / 256, n_problems, n_streams);
+      carry_reg_kernel<32><<<grid, 128, 4 * 32 * 32, stream>>>(batch);
+    } else {
+      dim3 grid((batch.W + 511) / 512, n_problems, n_streams);
+      carry_reg_kernel<64><<<grid, 256, 4 * 64 * 64, stream>>>(batch);
+    }
+    return check_launch("carry_kernel");
+  }
   const int tok = 128;
   dim3 grid((batch.W + tok - 1) / tok, n_problems, n_streams);
   const int smem = 4 * (ld * ld + 8 * ld);

@@ -107,6 +107,142 @@ __global__ void __launch_bounds__(256) slash_score_kernel(CandSrc<T> src, int m,
 }
 
 
+// The same scores with the projection on the fp64 tensor cores
+// (mma.m8n8k4.f64: exact products of the fp32 values, fp64 sums), for
+// rank <= 32 and head_dim a multiple of 8.  A CTA takes kScT candidates: their
+// un-rotated rows (all heads) and the basis are staged once, in fp32 at padded
+// pitches (conflict-free fragment loads), then the K = n product runs in one
+// pass; warp w owns the candidate tile w % 2 and the coordinate tiles
+// 2 (w / 2) + {0, 1}.
+constexpr int kScT = 32;
+constexpr int kScThreads = 2 * kScT * 4;  // (kScT / 8) candidate tiles x 2 coordinate-tile pairs
+
+__device__ __forceinline__ void dmma_8x8x4(double& d0, double& d1, double a, double b) {
+  asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0, %1}, {%2}, {%3}, {%0, %1};\n"
+               : "+d"(d0), "+d"(d1)
+               : "d"(a), "d"(b));
+}
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+  const unsigned sa = (unsigned)__cvta_generic_to_shared(smem_dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(sa), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
+}
+
+// Requires rows of n*sizeof(T) and of ld floats in 16-byte multiples, 16-byte
+// aligned (checked by the launcher): the basis and the candidates' raw rows
+// are copied with cp.async, all in flight at once, then un-rotated in place.
+template <typename T>
+__global__ void __launch_bounds__(kScThreads) slash_score_dmma_kernel(CandSrc<T> src, int m, int H, int D,
+                                                               RopeArgs rope, const float* u,
+                                                               long u_sp, int ld, const int* rr,
+                                                               float* scores, long sc_sp) {
+  extern __shared__ __align__(16) double dsm[];
+  const int p = blockIdx.y;
+  const int j0 = blockIdx.x * kScT;
+  const int half = D / 2, n = H * D;
+  const int r = rr[p];
+  const int ldx = n + 4, ldu = 40;                 // floats: 4 / 8 mod 32 (conflict-free fragments)
+  double* kk = dsm;                                // [kScT]     |k|^2
+  double* ccp = kk + kScT;                         // [2][kScT]  |c|^2 halves
+  float* xs = reinterpret_cast<float*>(ccp + 2 * kScT);  // [kScT][ldx] un-rotated rows
+  float* us = xs + kScT * ldx;                     // [n][ldu]   basis, zero past r
+  float* cs = us + (long)n * ldu;                  // [kScT][half][2] RoPE
+  T* kraw = reinterpret_cast<T*>(cs + kScT * half * 2);  // [kScT][n] raw candidate rows
+  const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
+  const int mt = warp % (kScT / 8), nt0 = 2 * (warp / (kScT / 8));
+  const int grp = lane >> 2, tig = lane & 3;
+  const float* U = u + p * u_sp;
+  const int nu = r < 32 ? r : 32;
+  // asynchronous copies: the basis rows (first 32 columns) and the raw candidate rows
+  {
+    const int q4 = (nu + 3) / 4;  // 16-byte chunks per basis row actually needed
+    for (int e = tid; e < n * q4; e += blockDim.x) {
+      const int f = e / q4, q = e % q4;
+      cp_async16(us + (long)f * ldu + 4 * q, U + (long)f * ld + 4 * q);
+    }
+    constexpr int per = 16 / sizeof(T);
+    const int rq = n / per;
+    for (int e = tid; e < kScT * rq; e += blockDim.x) {
+      const int a = e / rq, q = e % rq;
+      const int jj = j0 + a;
+      if (jj < m) cp_async16(kraw + (long)a * n + q * per, src.krow(p, jj) + q * per);
+    }
+  }
+  for (int e = tid; e < kScT * half; e += blockDim.x) {
+    const int a = e / half, f = e % half;
+    const int jj = j0 + a;
+    float c = 1.f, s = 0.f;
+    if (jj < m) rope_cs(src.pos(p, jj), rope.inv_freq[f], rope.scale, &c, &s);
+    cs[2 * e] = c;
+    cs[2 * e + 1] = s;
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  if (nu < 32) {  // columns past the rank are zero
+    for (int e = tid; e < n * 32; e += blockDim.x) {
+      const int f = e / 32, k = e % 32;
+      if (k >= 4 * ((nu + 3) / 4) || k >= nu) us[(long)f * ldu + k] = 0.f;
+    }
+  }
+  for (int e = tid; e < kScT * H * half; e += blockDim.x) {  // (candidate, head, pair)
+    const int a = e / (H * half), hf = e % (H * half), h = hf / half, f = hf % half;
+    const int jj = j0 + a;
+    float y1 = 0.f, y2 = 0.f;
+    if (jj < m) {
+      const T* kr = kraw + (long)a * n + h * D;
+      const float x1 = load_f<T>(kr + f), x2 = load_f<T>(kr + f + half);
+      const float c = cs[2 * (a * half + f)], s = cs[2 * (a * half + f) + 1];
+      y1 = (x1 * c + x2 * s) / rope.scale_sq;
+      y2 = (x2 * c - x1 * s) / rope.scale_sq;
+    }
+    xs[a * ldx + h * D + f] = y1;
+    xs[a * ldx + h * D + f + half] = y2;
+  }
+  __syncthreads();
+  {  // |k|^2: 8 threads per candidate, fp64
+    const int a = tid / 8, sub = tid % 8;
+    double sq = 0.0;
+    for (int d = sub; d < n; d += 8) {
+      const double v = xs[a * ldx + d];
+      sq = fma(v, v, sq);
+    }
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    if (sub == 0) kk[a] = sq;
+  }
+  double c00 = 0.0, c01 = 0.0, c10 = 0.0, c11 = 0.0;  // tiles nt0, nt0 + 1
+  const float* xa = xs + (mt * 8 + grp) * ldx + tig;
+  const float* ub = us + tig * ldu + nt0 * 8 + grp;
+#pragma unroll 4
+  for (int k0 = 0; k0 < n; k0 += 4) {
+    const double av = xa[k0];
+    dmma_8x8x4(c00, c01, av, (double)ub[k0 * ldu]);
+    dmma_8x8x4(c10, c11, av, (double)ub[k0 * ldu + 8]);
+  }
+  // |c|^2 of each candidate row: the lane's four values, the row's four lanes, two warps
+  double cc = c00 * c00 + c01 * c01 + c10 * c10 + c11 * c11;
+  cc += __shfl_xor_sync(0xffffffffu, cc, 1);
+  cc += __shfl_xor_sync(0xffffffffu, cc, 2);
+  if (tig == 0) ccp[(warp / (kScT / 8)) * kScT + mt * 8 + grp] = cc;
+  __syncthreads();
+  if (tid < kScT) {
+    const int j = j0 + tid;
+    if (j < m) {
+      float out;
+      if (r == 0) {
+        out = 1.f;
+      } else {
+        const double k2 = kk[tid], c2 = ccp[tid] + ccp[kScT + tid];
+        out = (float)(sqrt(fmax(k2 - c2, 0.0)) / fmax(sqrt(k2), 1e-12));
+      }
+      scores[p * sc_sp + j] = out;
+    }
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(1024) slash_select_kernel(CandSrc<T> src, int m, int keep_n,
                                                             int H, int D, RopeArgs rope,
@@ -364,6 +500,25 @@ int launch_slash_score(const CandSrc<T>& src, int P, int m, int H, int D, RopeAr
     return KVD_ERR_ARG;
   }
   const int half = D / 2;
+  const long n = (long)H * D;
+  const long dsmem_l = 8L * 3 * kScT + 4L * (kScT * (n + 4) + n * 40 + kScT * half * 2) +
+                       (long)sizeof(T) * kScT * n;
+  // cp.async staging: 16-byte rows and bases
+  const bool al = (n * (long)sizeof(T)) % 16 == 0 && ld % 4 == 0 && u_sp % 4 == 0 &&
+                  reinterpret_cast<uintptr_t>(u) % 16 == 0 &&
+                  reinterpret_cast<uintptr_t>(src.g_k) % 16 == 0 &&
+                  (src.hh_len == 0 || reinterpret_cast<uintptr_t>(src.hh_k) % 16 == 0) &&
+                  (src.hh_sp * (long)sizeof(T)) % 16 == 0 && (src.g_sp * (long)sizeof(T)) % 16 == 0;
+  if (ld <= 32 && D % 8 == 0 && al && dsmem_l <= 200 * 1024) {
+    const int dsmem = (int)dsmem_l;
+    if (int rc = ensure_smem((const void*)slash_score_dmma_kernel<T>, dsmem, "slash_score_kernel")) return rc;
+    {
+      KTimerScope kts_("slash_score_kernel", stream);
+      slash_score_dmma_kernel<T><<<dim3((m + kScT - 1) / kScT, P), kScThreads, dsmem, stream>>>(
+          src, m, H, D, rope, u, u_sp, ld, rr, scores, sc_sp);
+    }
+    return check_launch("slash_score_kernel");
+  }
   const int smem = 4 * (kScoreTile * half * 2 + kScoreTile * D + D * ld);
   dim3 grid((m + kScoreTile - 1) / kScoreTile, P);
   auto go = [&](auto kern) -> int {
