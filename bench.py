@@ -135,6 +135,12 @@ def new_cache(w: dict, torch):
         retention="lowrank_surprise", hh_budget=w["hh"], hh_select="surprise")
 
 
+# DRAM bytes (read + write) of one launch, from ncu captures of the same launch
+# shape (profiles/bug_step_kernel_r32_n512_b16.md); kernels not captured at the
+# workload's shape are left out.
+DRAM_BYTES_PER_LAUNCH = {"bug_step_kernel": 3.38e6}
+
+
 def kernel_bytes(w: dict) -> dict[str, float]:
     """Algorithmic HBM bytes of one bench step, per kernel, from a replay of
     the cache's absorb schedule (every length decision is count-driven).
@@ -322,7 +328,7 @@ def run_ours(args, w: dict) -> None:
             ach = nbytes / (ms / 1e3) / 1e9 if (nbytes and ms) else None
             return {"kernel": name, "bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s",
                     "frac": (ach / peak) if ach else None, "peak_source": peak_kind,
-                    "traffic": None, "bytes_per_launch": (nbytes / launches) if (nbytes and launches) else None,
+                    "traffic": DRAM_BYTES_PER_LAUNCH.get(name), "bytes_per_launch": (nbytes / launches) if (nbytes and launches) else None,
                     "avg_launch_ms": (ms / launches) if launches else None}
 
         roof_all = {k: roof(k) for k in kb if k in prof}

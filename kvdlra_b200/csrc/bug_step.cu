@@ -55,7 +55,7 @@ constexpr int kPartFloats = 8192;      // K-split partials: 16 warps x 32 lanes 
 // threads.  Callers must __syncthreads() before reading X.
 constexpr double kJacobiFloor = 1e-30;
 constexpr int kJacobiBarrier = 1;  // named barrier id (0 is __syncthreads)
-// A sweep whose largest pair cosine was below this ends the iteration:
+// A sweep that rotated no pair whose cosine exceeded this ends the iteration:
 // Jacobi converges quadratically, so the next sweep's cosines would be
 // ~1e-6, at the stopping tolerance, and the confirming sweep is skipped.
 constexpr float kJacobiQuadStop = 1e-3f;
@@ -84,20 +84,22 @@ __host__ __device__ inline int jacobi_nu(int g, int need, bool dbl) {
 
 __host__ __device__ inline void jacobi_tile(int nut, int cols, bool dbl, int* G, int* NU) {
   const int half = (cols + 1) / 2;
-  int g = 32;
-  while (g > 4 && half * g > 256) g >>= 1;
-  while (g < 32 && g * 9 < nut) g <<= 1;
-  int nu = jacobi_nu(g, (nut + g - 1) / g, dbl);
-  // a tile padded far past the column (small problems) wastes shared
-  // memory: fewer lanes per pair then
-  while (nu && g > 4 && 4 * g * nu > 5 * nut + 8) {
-    const int g2 = g >> 1, nu2 = jacobi_nu(g2, (nut + g2 - 1) / g2, dbl);
-    if (!nu2) break;
-    g = g2;
-    nu = nu2;
+  int g0 = 32;
+  while (g0 > 4 && half * g0 > 256) g0 >>= 1;
+  while (g0 < 32 && g0 * 9 < nut) g0 <<= 1;
+  // the widest instantiated group up to g0 whose tile is not padded far past
+  // the column (small problems would waste shared memory), else the least
+  // padded instantiated one, else streaming
+  int gbest = 0, nubest = 0, gany = 0, nuany = 0;
+  for (int g = g0; g >= 4; g >>= 1) {
+    const int nu = jacobi_nu(g, (nut + g - 1) / g, dbl);
+    if (!nu) continue;
+    if (!gany || g * nu < gany * nuany) { gany = g; nuany = nu; }  // least padding
+    if (4 * g * nu <= 5 * nut + 8) { gbest = g; nubest = nu; break; }
   }
-  *G = nu ? g : 32;
-  *NU = nu;
+  if (!gbest) { gbest = gany; nubest = nuany; }
+  *G = nubest ? gbest : 32;
+  *NU = nubest;
 }
 // Column pitch (floats) a Jacobi on `rows` augmented rows x `cols` columns needs.
 __host__ __device__ inline int jacobi_pitch(int rows, int cols, bool dbl) {
@@ -111,7 +113,7 @@ template <int G, int NU, typename ACC>
 static __device__ __forceinline__ int cta_hestenes(float* X, int len, int voff, int cols, int ldx,
                                                    float tol, int max_sweeps, double inv_scale2) {
   __shared__ int s_rot[3];
-  __shared__ unsigned s_maxc[3];  // largest squared pair cosine of a sweep (float bits)
+  __shared__ int s_big[3];  // a sweep rotated some pair whose cosine exceeded kJacobiQuadStop
   const int tid = threadIdx.x, nthr = blockDim.x, warp = tid / 32, lane = tid % 32;
   const int gid = tid / G, gl = tid % G;
   const int vend = voff + ((cols + 3) & ~3);
@@ -120,7 +122,7 @@ static __device__ __forceinline__ int cta_hestenes(float* X, int len, int voff, 
     const int c = (int)(e / (rows - len)), k = len + (int)(e % (rows - len));
     X[(long)c * ldx + k] = (k - voff == c) ? 1.f : 0.f;
   }
-  if (tid < 3) { s_rot[tid] = 0; s_maxc[tid] = 0u; }
+  if (tid < 3) { s_rot[tid] = 0; s_big[tid] = 0; }
   __syncthreads();
   if (cols <= 1) return 0;
   const int np = cols + (cols & 1);
@@ -134,7 +136,7 @@ static __device__ __forceinline__ int cta_hestenes(float* X, int len, int voff, 
   const ACC is2 = (ACC)inv_scale2;
   int sweep = 0;
   for (; sweep < max_sweeps; ++sweep) {
-    if (tid == 0) { s_rot[(sweep + 1) % 3] = 0; s_maxc[(sweep + 1) % 3] = 0u; }
+    if (tid == 0) { s_rot[(sweep + 1) % 3] = 0; s_big[(sweep + 1) % 3] = 0; }
     for (int k = 0; k < np - 1; ++k) {
       for (int base = 0; base < half; base += groups) {
         const int i = base + gid;
@@ -190,17 +192,13 @@ static __device__ __forceinline__ int cta_hestenes(float* X, int len, int voff, 
         be *= is2;
         ga *= is2;
         const bool live = active && al > (ACC)kJacobiFloor && be > (ACC)kJacobiFloor;
-        {  // the round's largest squared cosine, one shared atomic per warp
-          const float c2 = live ? __fdividef((float)(ga * ga), (float)(al * be)) : 0.f;
-          const unsigned m = __reduce_max_sync(0xffffffffu, __float_as_uint(c2));
-          if (lane == 0 && m) atomicMax(&s_maxc[sweep % 3], m);
-        }
         if (!live || ga * ga <= tol2 * al * be) continue;
-        const float zeta = __fdividef((float)be - (float)al, 2.f * (float)ga);
-        const float az = fabsf(zeta);
-        const float x1 = fmaf(zeta, zeta, 1.f);
-        const float hyp = az > 1e18f ? az : x1 * rsqrtf(x1);  // sqrt(1 + zeta^2)
-        const float t = copysignf(__fdividef(1.f, az + hyp), zeta);
+        // t = tan(theta) = sgn(d) 2g / (|d| + sqrt(d^2 + 4 g^2)), d = be - al, g = ga
+        // (the smaller root of t^2 + (d/g) t - 1 = 0, zeroing the pair's product)
+        const float d = (float)be - (float)al, g2 = 2.f * (float)ga;
+        const float rr = fmaf(d, d, g2 * g2);
+        const float hyp = rr * rsqrtf(rr);
+        const float t = copysignf(1.f, d) * g2 * __fdividef(1.f, fabsf(d) + hyp);
         float c = rsqrtf(fmaf(t, t, 1.f)), s = c * t;
         const float f = fmaf(-0.5f, fmaf(c, c, s * s), 1.5f);  // Newton step to unit norm
         c *= f;
@@ -222,12 +220,15 @@ static __device__ __forceinline__ int cta_hestenes(float* X, int len, int voff, 
             xq[e] = s * u + c * v;
           }
         }
-        if (gl == 0) s_rot[sweep % 3] = 1;
+        if (gl == 0) {
+          s_rot[sweep % 3] = 1;
+          if (ga * ga > (ACC)(kJacobiQuadStop * kJacobiQuadStop) * al * be) s_big[sweep % 3] = 1;
+        }
       }
       named_barrier(kJacobiBarrier, nbar);
     }
     if (!s_rot[sweep % 3]) break;
-    if (__uint_as_float(s_maxc[sweep % 3]) < kJacobiQuadStop * kJacobiQuadStop) break;
+    if (!s_big[sweep % 3]) break;
   }
   return sweep;
 }
@@ -698,12 +699,18 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
   // b > n (more columns than rows cannot all be made orthogonal): on the n
   // columns of R^T, R^T J = [s_j v_j], so J holds the left vectors q_j.
   // The rotations accumulate below the data in each column (rows voff..).
-  const bool tr = b > n;
+  // Blocks of up to 16 tokens (the absorb block): the fp64 Gram R^T R is
+  // factored T^T T (Cholesky, pivots below 1e-14 of the trace taken as null)
+  // and the one-sided Jacobi runs on T's b columns of length b -- T has R's
+  // singular values and right vectors, R V = Q1 U_T S -- in one warp.
+  const bool chol = b <= 16 && b <= n;
+  const bool tr = !chol && b > n;
   const int nsv = tr ? n : b;
   const int rlen = tr ? b : n;
-  const int voff = (rlen + 3) & ~3;
-  const int ldr = jacobi_pitch(voff + nsv, nsv, true);
-  const int ldr0 = tr ? n : ldr;  // pitch the residual is formed with
+  const int voff = chol ? ((b + 3) & ~3) : (rlen + 3) & ~3;
+  const int ldr = chol ? jacobi_pitch(voff + b, b, false) : jacobi_pitch(voff + nsv, nsv, true);
+  const int ldr0 = (tr || chol) ? n : ldr;  // pitch the residual is formed with
+  float* Tm = chol ? part + 2 * (b * (b + 1) + 8) : Rm;  // the factor, augmented columns
   // ----- residual R = (I - U U^T)^2 X (the reference's re-orthogonalised residual)
   if (r > 0) cta_tn(r, b, n, Uc, lda, XR, ldb, true, AS, b16, 0.f, part);  // a = U^T X
   cta_rows_sub(n, b, b16, r, Uc, lda, AS, b16, XR, ldb, Rm, ldr0, true, r > 0);  // R = X - U a
@@ -715,7 +722,48 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
   }
   // ----- SVD of R
   const double inv_x2 = s_xnorm2 > 0.0 ? 1.0 / s_xnorm2 : 1.0;
-  if (tr) {
+  if (chol) {
+    double* GR = reinterpret_cast<double*>(part);  // [b][b+1], T overwrites its upper triangle
+    const int ldg = b + 1;
+    for (int pp = warp; pp < b * b; pp += nthr / 32) {  // fp64 Gram, one warp per pair
+      const int pi = pp / b, qi = pp % b;
+      if (pi > qi) continue;
+      const float* xp = Rm + (long)pi * n;
+      const float* xq = Rm + (long)qi * n;
+      double acc = 0.0;
+      for (int e = lane; e < n; e += 32) acc = fma((double)xp[e], (double)xq[e], acc);
+      acc = warp_sum(acc);
+      if (lane == 0) { GR[pi * ldg + qi] = acc; GR[qi * ldg + pi] = acc; }
+    }
+    __syncthreads();
+    if (warp == 0) {  // right-looking Cholesky of the b x b Gram in one warp
+      double trace = 0.0;
+      for (int j = lane; j < b; j += 32) trace += GR[j * ldg + j];
+      trace = warp_sum(trace);
+      for (int j = 0; j < b; ++j) {
+        const double piv = GR[j * ldg + j];
+        const double t = piv > 1e-14 * trace ? sqrt(piv) : 0.0;
+        __syncwarp();
+        for (int i = j + 1 + lane; i < b; i += 32) GR[j * ldg + i] = t > 0.0 ? GR[j * ldg + i] / t : 0.0;
+        if (lane == 0) GR[j * ldg + j] = t;
+        __syncwarp();
+        for (int e = lane; e < b * b; e += 32) {
+          const int i = e / b, l = e % b;
+          if (i > j && l >= i) {
+            const double v = GR[i * ldg + l] - GR[j * ldg + i] * GR[j * ldg + l];
+            GR[i * ldg + l] = v;
+            GR[l * ldg + i] = v;
+          }
+        }
+        __syncwarp();
+      }
+      for (int e = lane; e < b * b; e += 32) {  // column c of T: rows k <= c
+        const int c = e / b, k = e % b;
+        Tm[c * ldr + k] = k <= c ? (float)GR[k * ldg + c] : 0.f;
+      }
+    }
+    __syncthreads();
+  } else if (tr) {
     for (long e = tid; e < (long)b * n; e += nthr) XR[e] = Rm[e];
     __syncthreads();
     for (long e = tid; e < (long)b * n; e += nthr) {  // column i of R^T: R[i][0..b)
@@ -724,10 +772,18 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
     }
     __syncthreads();
   }
-  int sw = cta_hestenes_any<double>(Rm, rlen, voff, nsv, ldr,
-                                    1.2e-7f * sqrtf((float)rlen) + 2.4e-7f, 30, inv_x2);
-  __syncthreads();
-  cta_colnorm_order(Rm, rlen, nsv, ldr, sv, ordh);
+  int sw;
+  if (chol) {
+    sw = cta_hestenes_any<float>(Tm, b, voff, b, ldr, 1.2e-7f * sqrtf((float)b) + 2.4e-7f, 30,
+                                 inv_x2);
+    __syncthreads();
+    cta_colnorm_order(Tm, b, b, ldr, sv, ordh);
+  } else {
+    sw = cta_hestenes_any<double>(Rm, rlen, voff, nsv, ldr,
+                                  1.2e-7f * sqrtf((float)rlen) + 2.4e-7f, 30, inv_x2);
+    __syncthreads();
+    cta_colnorm_order(Rm, rlen, nsv, ldr, sv, ordh);
+  }
   if (sw >= 30 && tid == 0) atomicOr(&A.status[kStatusNumeric], 1);
   if (tid == 0) {
     const float xnorm = (float)sqrt(s_xnorm2);
@@ -757,10 +813,16 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
   for (long e = tid; e < (long)m * n; e += nthr) {
     const int j = (int)(e / n), i = (int)(e % n);
     const int oj = ordh[j];
-    if (!tr) {  // q_j = (R V)[:, o_j] / s_j
+    if (chol) {       // q_j = R v_j / s_j
+      const double sj = sv[oj];
+      const float* vj = Tm + (long)oj * ldr + voff;
+      float acc = 0.f;
+      for (int l = 0; l < b; ++l) acc = fmaf(Rm[(long)l * n + i], vj[l], acc);
+      Q[e] = sj > 0.0 ? (float)((double)acc / sj) : 0.f;
+    } else if (!tr) {  // q_j = (R V)[:, o_j] / s_j
       const double sj = sv[oj];
       Q[e] = sj > 0.0 ? (float)(Rm[(long)oj * ldr + i] / sj) : 0.f;
-    } else {    // q_j = J[:, o_j]
+    } else {           // q_j = J[:, o_j]
       Q[e] = Rm[(long)oj * ldr + voff + i];
     }
   }
@@ -779,7 +841,8 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
       else v = AS[c * b16 + (row - r)];
     } else if (row >= r) {  // s_j v_j^T, the residual's right part
       const int oj = ordh[c - r], l = row - r;
-      v = tr ? Rm[(long)oj * ldr + l] : (float)sv[oj] * Rm[(long)oj * ldr + voff + l];
+      const float* vsrc = chol ? Tm : Rm;
+      v = tr ? Rm[(long)oj * ldr + l] : (float)sv[oj] * vsrc[(long)oj * ldr + voff + l];
     }
     BT[(long)c * ldbt + row] = v;
   }
