@@ -73,6 +73,7 @@ struct SelectOut {
   float* xk; float* xv; long x_sp;        // demoted block [P][dmax][n]
   int* mid_pos; float* mid_surprise; long mid_sp; int w_off;  // written at [w_off + slot]
   int* dem_count;                          // [P] demoted count (diagnostic)
+  int* order; long order_sp;               // [P][>= m] slot -> candidate (workspace)
 };
 
 }  // namespace kvd

@@ -132,6 +132,7 @@ struct Ws {
   int* dims[2];                  // [P][4]
   int* dem;                      // [P]
   int* keep; long keep_sp;       // [P][w_cap]
+  int* order;                    // [P][hh_budget + max_block] tier slot order
   char* step[2]; long step_sp;   // per problem
   size_t total;
 };
@@ -156,6 +157,7 @@ static Ws plan_ws(const kvd_config& c, char* base) {
   w.dem = (int*)take(4ul * P);
   w.keep_sp = c.w_cap;
   w.keep = (int*)take(4ul * P * w.keep_sp);
+  w.order = (int*)take(4ul * P * w.sc_sp);
   w.step_sp = bug_step_ws_per_problem(n, mb, ld);
   w.step[0] = take((size_t)P * w.step_sp);
   w.step[1] = take((size_t)P * w.step_sp);
@@ -296,6 +298,7 @@ struct Group {
     so.xk = w.xk; so.xv = w.xv; so.x_sp = w.x_sp;
     so.mid_pos = b.mid_pos; so.mid_surprise = track_surprise() ? b.mid_surprise : nullptr;
     so.mid_sp = c.w_cap; so.w_off = k.w_len; so.dem_count = w.dem;
+    so.order = w.order; so.order_sp = w.sc_sp;
     rc = launch_slash_select<T>(src, P, m, keep_n, c.num_heads, c.head_dim, rope, w.scores, w.sc_sp,
                                 c.hh_neighbor, so, s);
     if (rc) return rc;

@@ -4,10 +4,12 @@
 //    (post-RoPE, model dtype) and score its low-rank surprise against the
 //    pre-step basis: bug_cache.py:803-804 + 906-921.  fp64 accumulation of the
 //    fp32 projection so the score is as exact as the basis allows.
-//  * slash_select_kernel  -- optional span boost (923-950), stable descending
-//    top-h (810-812), compaction of the kept tokens into the other exact-tier
-//    buffer and gather of the demoted ones (un-rotated K, fp32 V, positions,
-//    graduation surprise) into the BUG-step block: 813-825 + 871-888.
+//  * slash_rank_kernel    -- optional span boost (923-950), stable descending
+//    top-h (810-812): the slot order of kept and demoted candidates, their
+//    positions and graduation surprise (813-825 + 871-888).
+//  * slash_move_kernel    -- compaction of the kept tokens into the other
+//    exact-tier buffer and gather of the demoted ones (un-rotated K, fp32 V)
+//    into the BUG-step block, one warp per row over the whole GPU.
 //  * gather_block_kernel  -- the no-tier absorb path (743-750).
 //  * evict_kernel         -- coordinate-budget eviction (954-1067).
 #include <cfloat>
@@ -243,35 +245,41 @@ __global__ void __launch_bounds__(kScThreads) slash_score_dmma_kernel(CandSrc<T>
   }
 }
 
+// Ranking half of the tier update, one CTA per problem: span boost, stable
+// descending rank, and the slot order [kept sources (chronological) |
+// demoted sources (chronological)] written to out.order; positions and
+// graduation surprise go straight to their buffers.  The rows move in
+// slash_move_kernel, spread over the whole GPU.
 template <typename T>
-__global__ void __launch_bounds__(1024) slash_select_kernel(CandSrc<T> src, int m, int keep_n,
-                                                            int H, int D, RopeArgs rope,
-                                                            const float* scores, long sc_sp,
-                                                            int hh_neighbor, SelectOut out) {
+__global__ void __launch_bounds__(512) slash_rank_kernel(CandSrc<T> src, int m, int keep_n,
+                                                         const float* scores, long sc_sp,
+                                                         int hh_neighbor, SelectOut out) {
   extern __shared__ __align__(16) float sel_sm[];
   __shared__ int scan_scratch[32];
   const int p = blockIdx.x;
-  const int n = H * D, half = D / 2;
   float* raw = sel_sm;            // [m]
   float* sel = raw + m;           // [m]
-  int* keep_src = reinterpret_cast<int*>(sel + m);     // [keep_n]
-  int* dem_src = keep_src + keep_n;                     // [m - keep_n]
-  for (int i = threadIdx.x; i < m; i += blockDim.x) raw[i] = scores[p * sc_sp + i];
+  int* pos = reinterpret_cast<int*>(sel + m);  // [m]
+  int* order = out.order + p * out.order_sp;
+  for (int i = threadIdx.x; i < m; i += blockDim.x) {
+    raw[i] = scores[p * sc_sp + i];
+    pos[i] = src.pos(p, i);
+  }
   __syncthreads();
   for (int i = threadIdx.x; i < m; i += blockDim.x) {
     float v = raw[i];
     if (hh_neighbor > 0) {
-      const int pi = src.pos(p, i);
+      const int pi = pos[i];
       const int lo = max(0, i - hh_neighbor), hi = min(m - 1, i + hh_neighbor);
       for (int j = lo; j <= hi; ++j) {
         if (j == i) continue;
-        const int pj = src.pos(p, j);
-        if (abs(pj - pi) <= hh_neighbor) v = fmaxf(v, raw[j]);
+        if (abs(pos[j] - pi) <= hh_neighbor) v = fmaxf(v, raw[j]);
       }
     }
     sel[i] = v;
   }
   __syncthreads();
+  const int d = m - keep_n;
   int kbase = 0, dbase = 0;
   for (int i0 = 0; i0 < m; i0 += blockDim.x) {
     const int i = i0 + threadIdx.x;
@@ -288,70 +296,78 @@ __global__ void __launch_bounds__(1024) slash_select_kernel(CandSrc<T> src, int 
     int tot;
     const int pre = cta_exclusive_scan(kept, scan_scratch, &tot);
     if (i < m) {
-      if (kept) keep_src[kbase + pre] = i;
-      else dem_src[dbase + (i - i0 - pre)] = i;
+      if (kept) {
+        const int slot = kbase + pre;
+        order[slot] = i;
+        out.hh_pos[p * out.hh_pos_sp + slot] = pos[i];
+      } else {
+        const int slot = dbase + (i - i0 - pre);
+        order[keep_n + slot] = i;
+        out.mid_pos[p * out.mid_sp + out.w_off + slot] = pos[i];
+        if (out.mid_surprise) out.mid_surprise[p * out.mid_sp + out.w_off + slot] = raw[i];
+      }
     }
     kbase += tot;
     dbase += min((int)blockDim.x, m - i0) - tot;
-    __syncthreads();
-  }
-  const int d = m - keep_n;
-  // kept tokens -> new exact tier (verbatim, chronological)
-  T* ok = reinterpret_cast<T*>(out.hh_k) + p * out.hh_sp;
-  T* ov = reinterpret_cast<T*>(out.hh_v) + p * out.hh_sp;
-  // one warp per kept row, 16-byte vector copies plus a scalar tail
-  {
-    const int lane = threadIdx.x % 32, warp = threadIdx.x / 32, nw = blockDim.x / 32;
-    const int vec = (int)((n * sizeof(T)) / 16);
-    for (int slot = warp; slot < keep_n; slot += nw) {
-      const int jsrc = keep_src[slot];
-      const T* kss = src.krow(p, jsrc);
-      const T* vss = src.vrow(p, jsrc);
-      const uint4* ks = reinterpret_cast<const uint4*>(kss);
-      const uint4* vs = reinterpret_cast<const uint4*>(vss);
-      uint4* kd = reinterpret_cast<uint4*>(ok + (long)slot * n);
-      uint4* vd = reinterpret_cast<uint4*>(ov + (long)slot * n);
-      for (int e = lane; e < vec; e += 32) {
-        kd[e] = ks[e];
-        vd[e] = vs[e];
-      }
-      for (int i = vec * (int)(16 / sizeof(T)) + lane; i < n; i += 32) {
-        ok[(long)slot * n + i] = kss[i];
-        ov[(long)slot * n + i] = vss[i];
-      }
-    }
-  }
-  for (int slot = threadIdx.x; slot < keep_n; slot += blockDim.x)
-    out.hh_pos[p * out.hh_pos_sp + slot] = src.pos(p, keep_src[slot]);
-  // demoted tokens -> un-rotated fp32 block + positions + graduation surprise
-  float* xk = out.xk + p * out.x_sp;
-  float* xv = out.xv + p * out.x_sp;
-  for (long e = threadIdx.x; e < (long)d * (n / 2); e += blockDim.x) {
-    const int slot = (int)(e / (n / 2));
-    const int rem = (int)(e % (n / 2));
-    const int h = rem / half, f = rem % half;
-    const int jsrc = dem_src[slot];
-    const T* kr = src.krow(p, jsrc) + h * D;
-    float c, s;
-    rope_cs(src.pos(p, jsrc), rope.inv_freq[f], rope.scale, &c, &s);
-    const float x1 = load_f<T>(kr + f), x2 = load_f<T>(kr + f + half);
-    xk[(long)slot * n + h * D + f] = (x1 * c + x2 * s) / rope.scale_sq;
-    xk[(long)slot * n + h * D + f + half] = (x2 * c - x1 * s) / rope.scale_sq;
-  }
-  {
-    const int lane = threadIdx.x % 32, warp = threadIdx.x / 32, nw = blockDim.x / 32;
-    for (int slot = warp; slot < d; slot += nw) {
-      const T* vr = src.vrow(p, dem_src[slot]);
-      float* xo = xv + (long)slot * n;
-      for (int i = lane; i < n; i += 32) xo[i] = load_f<T>(vr + i);
-    }
-  }
-  for (int slot = threadIdx.x; slot < d; slot += blockDim.x) {
-    const int jsrc = dem_src[slot];
-    out.mid_pos[p * out.mid_sp + out.w_off + slot] = src.pos(p, jsrc);
-    if (out.mid_surprise) out.mid_surprise[p * out.mid_sp + out.w_off + slot] = raw[jsrc];
   }
   if (threadIdx.x == 0 && out.dem_count) out.dem_count[p] = d;
+}
+
+constexpr int kMoveWarps = 8;   // rows per CTA of slash_move_kernel (one warp each)
+
+// Row half of the tier update: slot s < keep_n copies candidate order[s]
+// verbatim into the new exact tier; slot keep_n + s un-rotates the demoted
+// candidate's key into the fp32 block (cos/sin once per frequency, reused
+// across heads) and widens its value.  Grid (ceil(m / 8), P), one warp per
+// slot, 16-byte copies.
+template <typename T>
+__global__ void __launch_bounds__(32 * kMoveWarps) slash_move_kernel(CandSrc<T> src, int m,
+                                                                     int keep_n, int H, int D,
+                                                                     RopeArgs rope, SelectOut out) {
+  const int p = blockIdx.y;
+  const int lane = threadIdx.x % 32;
+  const int slot = blockIdx.x * kMoveWarps + threadIdx.x / 32;
+  if (slot >= m) return;
+  const int n = H * D, half = D / 2;
+  const int jsrc = out.order[p * out.order_sp + slot];
+  const T* kss = src.krow(p, jsrc);
+  const T* vss = src.vrow(p, jsrc);
+  if (slot < keep_n) {
+    T* ok = reinterpret_cast<T*>(out.hh_k) + p * out.hh_sp + (long)slot * n;
+    T* ov = reinterpret_cast<T*>(out.hh_v) + p * out.hh_sp + (long)slot * n;
+    const bool aligned = ((reinterpret_cast<uintptr_t>(kss) | reinterpret_cast<uintptr_t>(vss) |
+                           reinterpret_cast<uintptr_t>(ok) | reinterpret_cast<uintptr_t>(ov)) &
+                          15) == 0;
+    const int vec = aligned ? (int)((n * sizeof(T)) / 16) : 0;
+    const uint4* ks = reinterpret_cast<const uint4*>(kss);
+    const uint4* vs = reinterpret_cast<const uint4*>(vss);
+    uint4* kd = reinterpret_cast<uint4*>(ok);
+    uint4* vd = reinterpret_cast<uint4*>(ov);
+    for (int e = lane; e < vec; e += 32) {
+      const uint4 a = ks[e], b = vs[e];
+      kd[e] = a;
+      vd[e] = b;
+    }
+    for (int i = vec * (int)(16 / sizeof(T)) + lane; i < n; i += 32) {
+      ok[i] = kss[i];
+      ov[i] = vss[i];
+    }
+    return;
+  }
+  const int ds = slot - keep_n;
+  float* xk = out.xk + p * out.x_sp + (long)ds * n;
+  float* xv = out.xv + p * out.x_sp + (long)ds * n;
+  const int ps = src.pos(p, jsrc);
+  for (int f = lane; f < half; f += 32) {
+    float c, s;
+    rope_cs(ps, rope.inv_freq[f], rope.scale, &c, &s);
+    for (int h = 0; h < H; ++h) {
+      const float x1 = load_f<T>(kss + h * D + f), x2 = load_f<T>(kss + h * D + f + half);
+      xk[h * D + f] = (x1 * c + x2 * s) / rope.scale_sq;
+      xk[h * D + f + half] = (x2 * c - x1 * s) / rope.scale_sq;
+    }
+  }
+  for (int i = lane; i < n; i += 32) xv[i] = load_f<T>(vss + i);
 }
 
 // No-tier absorb: rows [0, b) of `g_k`/`g_v` graduate at positions start + j.
@@ -541,14 +557,23 @@ int launch_slash_select(const CandSrc<T>& src, int P, int m, int keep_n, int H, 
                         RopeArgs rope, const float* scores, long sc_sp, int hh_neighbor,
                         const SelectOut& out, cudaStream_t stream) {
   if (m <= 0) return KVD_OK;
-  const int smem = 4 * (2 * m) + 4 * m;
-  if (int rc = ensure_smem((const void*)slash_select_kernel<T>, smem, "slash_select_kernel")) return rc;
-  {
-    KTimerScope kts_("slash_select_kernel", stream);
-    slash_select_kernel<T><<<P, 1024, smem, stream>>>(src, m, keep_n, H, D, rope, scores, sc_sp,
-                                                   hh_neighbor, out);
+  if (out.order_sp < m) {
+    set_error("slash select: order stride %ld < pool %d", out.order_sp, m);
+    return KVD_ERR_ARG;
   }
-  return check_launch("slash_select_kernel");
+  const int smem = 4 * 3 * m;
+  if (int rc = ensure_smem((const void*)slash_rank_kernel<T>, smem, "slash_rank_kernel")) return rc;
+  {
+    KTimerScope kts_("slash_rank_kernel", stream);
+    slash_rank_kernel<T><<<P, 512, smem, stream>>>(src, m, keep_n, scores, sc_sp, hh_neighbor, out);
+  }
+  if (int rc = check_launch("slash_rank_kernel")) return rc;
+  {
+    KTimerScope kts_("slash_move_kernel", stream);
+    dim3 grid((m + kMoveWarps - 1) / kMoveWarps, P);
+    slash_move_kernel<T><<<grid, 32 * kMoveWarps, 0, stream>>>(src, m, keep_n, H, D, rope, out);
+  }
+  return check_launch("slash_move_kernel");
 }
 
 template <typename T>

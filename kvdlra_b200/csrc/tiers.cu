@@ -160,6 +160,127 @@ __global__ void __launch_bounds__(256) mid_hat_kernel(const float* uk, const flo
   }
 }
 
+// Packed store of N consecutive outputs (N = 2 or 4).
+template <typename T, int N> KVD_DEVICE void store_n(T* p, const float* v);
+template <> KVD_DEVICE void store_n<float, 2>(float* p, const float* v) {
+  *reinterpret_cast<float2*>(p) = make_float2(v[0], v[1]);
+}
+template <> KVD_DEVICE void store_n<float, 4>(float* p, const float* v) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+}
+template <> KVD_DEVICE void store_n<__nv_bfloat16, 2>(__nv_bfloat16* p, const float* v) {
+  *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(v[0], v[1]);
+}
+template <> KVD_DEVICE void store_n<__nv_bfloat16, 4>(__nv_bfloat16* p, const float* v) {
+  const __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]), b = __floats2bfloat162_rn(v[2], v[3]);
+  uint2 u;
+  u.x = *reinterpret_cast<const uint32_t*>(&a);
+  u.y = *reinterpret_cast<const uint32_t*>(&b);
+  *reinterpret_cast<uint2*>(p) = u;
+}
+
+// Register-tiled middle reconstruction (same arithmetic, same order as
+// mid_hat_kernel, so the outputs are bit-identical): 64 tokens per CTA, each
+// thread owns 4 tokens x FP frequency pairs of one head for K and V, so every
+// coordinate / basis vector read from shared memory (16-byte loads) feeds
+// 4 x 2*FP FMAs.  Thread tx owns frequencies tx*FP .. tx*FP+FP-1 and their
+// partners + D/2, so the outputs leave as packed FP-element stores.
+constexpr int kMhTok = 64;
+constexpr int kMhCtPitch = kMhTok + 4;   // coordinate tile pitch (bank spread)
+
+template <typename T, int D>
+__global__ void __launch_bounds__(256) mid_hat_tiled_kernel(
+    const float* uk, const float* uv, long u_sp, int ld, const int* rk, const int* rv,
+    const float* ck, const float* cv, long c_sp, const int* mid_pos, long mid_sp, int pos_base,
+    int W, int H, const float* inv_freq, float scale, T* ok, T* ov, long ob, long oh, long ot,
+    int l0) {
+  constexpr int HALF = D / 2, FP = HALF / 16, NQ = 2 * FP;
+  extern __shared__ __align__(16) float msm[];
+  const int p = blockIdx.y;
+  const int t0 = blockIdx.x * kMhTok;
+  const int cnt = min(kMhTok, W - t0);
+  const int r_k = rk[p], r_v = rv[p];
+  const int rmax = max(r_k, r_v);
+  float* ctk = msm;                          // [ld][kMhCtPitch], token-contiguous
+  float* ctv = ctk + ld * kMhCtPitch;
+  float* usk = ctv + ld * kMhCtPitch;        // [ld][16][NQ]
+  float* usv = usk + ld * D;
+  float* cs = usv + ld * D;                  // [kMhTok][HALF][2]
+  const int tid = threadIdx.x;
+  for (int e = tid; e < kMhTok * ld; e += blockDim.x) {
+    const int t = e / ld, c = e % ld;
+    const bool in = t < cnt;
+    const long g = p * c_sp + (long)(t0 + t) * ld + c;
+    ctk[c * kMhCtPitch + t] = in && c < r_k ? ck[g] : 0.f;
+    ctv[c * kMhCtPitch + t] = in && c < r_v ? cv[g] : 0.f;
+  }
+  for (int e = tid; e < cnt * HALF; e += blockDim.x) {
+    const int t = e / HALF, f = e % HALF;
+    const int pos = mid_pos ? mid_pos[p * mid_sp + t0 + t] : pos_base + t0 + t;
+    float c, s;
+    rope_cs(pos, inv_freq[f], scale, &c, &s);
+    cs[2 * e] = c;
+    cs[2 * e + 1] = s;
+  }
+  const int ty = tid / 16, tx = tid % 16;
+  const float* Uk = uk + p * u_sp;
+  const float* Uv = uv + p * u_sp;
+  for (int h = 0; h < H; ++h) {
+    __syncthreads();
+    for (int e = tid; e < D * ld; e += blockDim.x) {
+      const int d = e / ld, c = e % ld;
+      const int hi = d >= HALF, f = hi ? d - HALF : d;
+      const int q = (c * 16 + f / FP) * NQ + hi * FP + f % FP;
+      usk[q] = c < r_k ? Uk[(long)(h * D + d) * ld + c] : 0.f;
+      usv[q] = c < r_v ? Uv[(long)(h * D + d) * ld + c] : 0.f;
+    }
+    __syncthreads();
+    float ak[4][NQ], av[4][NQ];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int q = 0; q < NQ; ++q) { ak[i][q] = 0.f; av[i][q] = 0.f; }
+#pragma unroll 4
+    for (int c = 0; c < rmax; ++c) {
+      const float4 a4 = *reinterpret_cast<const float4*>(ctk + c * kMhCtPitch + 4 * ty);
+      const float4 b4 = *reinterpret_cast<const float4*>(ctv + c * kMhCtPitch + 4 * ty);
+      const float a[4] = {a4.x, a4.y, a4.z, a4.w}, b[4] = {b4.x, b4.y, b4.z, b4.w};
+      float wk[NQ], wv[NQ];
+#pragma unroll
+      for (int q = 0; q < NQ; q += 4) {
+        const float4 x = *reinterpret_cast<const float4*>(usk + (c * 16 + tx) * NQ + q);
+        const float4 y = *reinterpret_cast<const float4*>(usv + (c * 16 + tx) * NQ + q);
+        wk[q] = x.x; wk[q + 1] = x.y; wk[q + 2] = x.z; wk[q + 3] = x.w;
+        wv[q] = y.x; wv[q + 1] = y.y; wv[q + 2] = y.z; wv[q + 3] = y.w;
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int q = 0; q < NQ; ++q) {
+          ak[i][q] = fmaf(wk[q], a[i], ak[i][q]);
+          av[i][q] = fmaf(wv[q], b[i], av[i][q]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int t = 4 * ty + i;
+      if (t >= cnt) continue;
+      float y1[FP], y2[FP];
+#pragma unroll
+      for (int j = 0; j < FP; ++j) {
+        const int f = tx * FP + j;
+        const float c = cs[2 * (t * HALF + f)], s = cs[2 * (t * HALF + f) + 1];
+        rope_apply_pair(ak[i][j], ak[i][FP + j], c, s, &y1[j], &y2[j]);
+      }
+      const long o = p * ob + h * oh + (long)(l0 + t0 + t) * ot + tx * FP;
+      store_n<T, FP>(ok + o, y1);
+      store_n<T, FP>(ok + o + HALF, y2);
+      store_n<T, FP>(ov + o, &av[i][0]);
+      store_n<T, FP>(ov + o + HALF, &av[i][FP]);
+    }
+  }
+}
+
 }  // namespace kvd
 
 namespace kvd_host {
@@ -241,16 +362,35 @@ int launch_peek(const kvd_config& c, const kvd_buffers& b, const kvd_counters& k
     const int mid_len = k.hh_len + k.w_len;
     const int pos_base = (int)(k.cumulative_length - k.ring_len - mid_len);
     const int half = D / 2;
-    const int smem = 4 * (2 * kMidTile * ld + 2 * D * ld + kMidTile * half * 2);
-    if (int rc2 = ensure_smem((const void*)mid_hat_kernel<T>, smem, "mid_hat_kernel")) return rc2;
-    dim3 grid((k.w_len + kMidTile - 1) / kMidTile, count);
-    {
-      KTimerScope kts_("mid_hat_kernel", s);
-      mid_hat_kernel<T><<<grid, 256, smem, s>>>(
-        b.u_k[k.u_sel] + p0 * u_sp, b.u_v[k.u_sel] + p0 * u_sp, u_sp, ld, b.r_k + p0, b.r_v + p0,
-        b.c_k + p0 * c_sp, b.c_v + p0 * c_sp, c_sp,
-        track_pos ? b.mid_pos + (long)p0 * c.w_cap : nullptr, c.w_cap, pos_base, k.w_len, H, D,
-        c.inv_freq, c.rope_scaling, okp, ovp, ob, oh, ot, l0);
+    const int fp = half / 16;
+    const bool tiled = (D == 64 || D == 128) && ob % fp == 0 && oh % fp == 0 && ot % fp == 0 &&
+                       reinterpret_cast<uintptr_t>(okp) % (fp * sizeof(T)) == 0 &&
+                       reinterpret_cast<uintptr_t>(ovp) % (fp * sizeof(T)) == 0;
+    if (tiled) {
+      const int smem = 4 * (2 * ld * kMhCtPitch + 2 * ld * D + kMhTok * half * 2);
+      auto fn = D == 64 ? mid_hat_tiled_kernel<T, 64> : mid_hat_tiled_kernel<T, 128>;
+      if (int rc2 = ensure_smem((const void*)fn, smem, "mid_hat_kernel")) return rc2;
+      dim3 grid((k.w_len + kMhTok - 1) / kMhTok, count);
+      {
+        KTimerScope kts_("mid_hat_kernel", s);
+        fn<<<grid, 256, smem, s>>>(
+          b.u_k[k.u_sel] + p0 * u_sp, b.u_v[k.u_sel] + p0 * u_sp, u_sp, ld, b.r_k + p0,
+          b.r_v + p0, b.c_k + p0 * c_sp, b.c_v + p0 * c_sp, c_sp,
+          track_pos ? b.mid_pos + (long)p0 * c.w_cap : nullptr, c.w_cap, pos_base, k.w_len, H,
+          c.inv_freq, c.rope_scaling, okp, ovp, ob, oh, ot, l0);
+      }
+    } else {
+      const int smem = 4 * (2 * kMidTile * ld + 2 * D * ld + kMidTile * half * 2);
+      if (int rc2 = ensure_smem((const void*)mid_hat_kernel<T>, smem, "mid_hat_kernel")) return rc2;
+      dim3 grid((k.w_len + kMidTile - 1) / kMidTile, count);
+      {
+        KTimerScope kts_("mid_hat_kernel", s);
+        mid_hat_kernel<T><<<grid, 256, smem, s>>>(
+          b.u_k[k.u_sel] + p0 * u_sp, b.u_v[k.u_sel] + p0 * u_sp, u_sp, ld, b.r_k + p0, b.r_v + p0,
+          b.c_k + p0 * c_sp, b.c_v + p0 * c_sp, c_sp,
+          track_pos ? b.mid_pos + (long)p0 * c.w_cap : nullptr, c.w_cap, pos_base, k.w_len, H, D,
+          c.inv_freq, c.rope_scaling, okp, ovp, ob, oh, ot, l0);
+      }
     }
     if ((rc = check_launch("mid_hat_kernel"))) return rc;
     l0 += k.w_len;
