@@ -226,6 +226,18 @@ size_t kvd_blocked_project_workspace_bytes(int32_t n, int32_t t, int32_t rank_ca
 /* Workspace bytes kvd_factored_decode needs for `count` problems. */
 size_t kvd_decode_workspace_bytes(const kvd_config* cfg, int32_t count, int32_t num_q_heads);
 
+/* ------------------------------------------------------------ RoPE angles */
+
+/* cos/sin tables of the rotary angles, out[i][f] for i < n positions and
+ * f < nf frequencies (fp32, row-major), each scaled by `scale`: fast = 0 is
+ * the full-precision path the cache uses for un-rotation and peeks
+ * (sincosf of the fp32 product pos * inv_freq, as the model's rotary module
+ * forms it), fast = 1 the reduced-instruction path the factored decode
+ * uses inside its tiles (Cody-Waite reduction by 2*pi, hardware sin/cos on
+ * the reduced angle).  Device pointers; asynchronous on `stream`. */
+int kvd_rope_table(int32_t n, const int32_t* pos, int32_t nf, const float* inv_freq, float scale,
+                   int32_t fast, float* cos_out, float* sin_out, kvd_stream_t stream);
+
 /* ------------------------------------------------------------- profiling */
 
 /* Per-kernel CUDA-event timing: kvd_profile(1) brackets every kernel launch of

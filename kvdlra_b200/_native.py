@@ -131,6 +131,7 @@ def lib() -> C.CDLL:
     L.kvd_bug_step_workspace_bytes.restype = sz
     L.kvd_surprise.argtypes = [i32, i32, i32, i32, vp, vp, vp, vp, vp]
     L.kvd_select_topk.argtypes = [i32, i32, i32, vp, vp, vp, vp]
+    L.kvd_rope_table.argtypes = [i32, vp, i32, vp, f32, i32, vp, vp, vp]
     L.kvd_profile.argtypes = [i32]
     L.kvd_profile_read.argtypes = [C.c_char_p, sz]
     L.kvd_blocked_project.argtypes = [i32, i32, i32, i32, i32, i32, i32, f32, vp, vp, vp, vp, sz, vp]
@@ -138,7 +139,7 @@ def lib() -> C.CDLL:
     L.kvd_blocked_project_workspace_bytes.restype = sz
     for name in ("kvd_check_status", "kvd_prefill", "kvd_append", "kvd_consolidate", "kvd_absorb_block", "kvd_peek",
                  "kvd_factored_decode", "kvd_bug_step", "kvd_surprise", "kvd_select_topk",
-                 "kvd_profile", "kvd_profile_read", "kvd_blocked_project"):
+                 "kvd_profile", "kvd_profile_read", "kvd_blocked_project", "kvd_rope_table"):
         getattr(L, name).restype = C.c_int
     _lib = L
     return L

@@ -63,6 +63,17 @@ constexpr float kJacobiQuadStop = 1e-3f;
 __device__ __forceinline__ void named_barrier(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
+// The same barrier, returning whether `pred` held on any participating thread.
+__device__ __forceinline__ bool named_barrier_or(int id, int nthreads, bool pred) {
+  int any;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.s32 p, %1, 0;\n bar.red.or.pred q, %2, %3, p;\n"
+      " selp.s32 %0, 1, 0, q;\n}"
+      : "=r"(any)
+      : "r"((int)pred), "r"(id), "r"(nthreads)
+      : "memory");
+  return any != 0;
+}
 
 // Register tile of the one-sided Jacobi for `cols` columns of `nut` 4-float
 // units: lanes per pair G (about eight warps' worth of pairs, at most 9 units
@@ -82,9 +93,10 @@ __host__ __device__ inline int jacobi_nu(int g, int need, bool dbl) {
   return 0;
 }
 
-__host__ __device__ inline void jacobi_tile(int nut, int cols, bool dbl, int* G, int* NU) {
+__host__ __device__ inline void jacobi_tile(int nut, int cols, bool dbl, int* G, int* NU,
+                                            int gcap = 32) {
   const int half = (cols + 1) / 2;
-  int g0 = 32;
+  int g0 = gcap;
   while (g0 > 4 && half * g0 > 256) g0 >>= 1;
   while (g0 < 32 && g0 * 9 < nut) g0 <<= 1;
   // the widest instantiated group up to g0 whose tile is not padded far past
@@ -102,27 +114,25 @@ __host__ __device__ inline void jacobi_tile(int nut, int cols, bool dbl, int* G,
   *NU = nubest;
 }
 // Column pitch (floats) a Jacobi on `rows` augmented rows x `cols` columns needs.
-__host__ __device__ inline int jacobi_pitch(int rows, int cols, bool dbl) {
+__host__ __device__ inline int jacobi_pitch(int rows, int cols, bool dbl, int gcap = 32) {
   int g, nu;
-  jacobi_tile((rows + 3) / 4, cols, dbl, &g, &nu);
+  jacobi_tile((rows + 3) / 4, cols, dbl, &g, &nu, gcap);
   const int r4 = (rows + 3) & ~3;
   return nu ? (r4 > 4 * g * nu ? r4 : 4 * g * nu) : r4;
 }
 
 template <int G, int NU, typename ACC>
 static __device__ __forceinline__ int cta_hestenes(float* X, int len, int voff, int cols, int ldx,
-                                                   float tol, int max_sweeps, double inv_scale2) {
-  __shared__ int s_rot[3];
-  __shared__ int s_big[3];  // a sweep rotated some pair whose cosine exceeded kJacobiQuadStop
+                                                   float tol, int max_sweeps, double inv_scale2,
+                                                   bool accum) {
   const int tid = threadIdx.x, nthr = blockDim.x, warp = tid / 32, lane = tid % 32;
   const int gid = tid / G, gl = tid % G;
-  const int vend = voff + ((cols + 3) & ~3);
+  const int vend = voff + (accum ? ((cols + 3) & ~3) : 0);
   const int rows = NU > 0 ? 4 * G * NU : vend;  // rows the tile touches; [len, rows) zeroed
   for (long e = tid; e < (long)cols * (rows - len); e += nthr) {
     const int c = (int)(e / (rows - len)), k = len + (int)(e % (rows - len));
-    X[(long)c * ldx + k] = (k - voff == c) ? 1.f : 0.f;
+    X[(long)c * ldx + k] = (accum && k - voff == c) ? 1.f : 0.f;
   }
-  if (tid < 3) { s_rot[tid] = 0; s_big[tid] = 0; }
   __syncthreads();
   if (cols <= 1) return 0;
   const int np = cols + (cols & 1);
@@ -136,7 +146,10 @@ static __device__ __forceinline__ int cta_hestenes(float* X, int len, int voff, 
   const ACC is2 = (ACC)inv_scale2;
   int sweep = 0;
   for (; sweep < max_sweeps; ++sweep) {
-    if (tid == 0) { s_rot[(sweep + 1) % 3] = 0; s_big[(sweep + 1) % 3] = 0; }
+    // a pair rotated this sweep with a cosine above kJacobiQuadStop (which
+    // also means some pair rotated at all); OR-reduced by the sweep's last barrier
+    bool big = false;
+    bool again = false;
     for (int k = 0; k < np - 1; ++k) {
       for (int base = 0; base < half; base += groups) {
         const int i = base + gid;
@@ -220,34 +233,33 @@ static __device__ __forceinline__ int cta_hestenes(float* X, int len, int voff, 
             xq[e] = s * u + c * v;
           }
         }
-        if (gl == 0) {
-          s_rot[sweep % 3] = 1;
-          if (ga * ga > (ACC)(kJacobiQuadStop * kJacobiQuadStop) * al * be) s_big[sweep % 3] = 1;
-        }
+        big = big || ga * ga > (ACC)(kJacobiQuadStop * kJacobiQuadStop) * al * be;
       }
-      named_barrier(kJacobiBarrier, nbar);
+      if (k < np - 2) named_barrier(kJacobiBarrier, nbar);
+      else again = named_barrier_or(kJacobiBarrier, nbar, big);
     }
-    if (!s_rot[sweep % 3]) break;
-    if (!s_big[sweep % 3]) break;
+    if (!again) break;
   }
   return sweep;
 }
 
-// Dispatch to the register tile jacobi_tile picks when X is 16-byte aligned
-// and the pitch covers it, else stream.
+// Dispatch to the register tile jacobi_tile picks (groups of at most `gcap`
+// lanes) when X is 16-byte aligned and the pitch covers it, else stream.
+// accum = false: no rotations are accumulated (rows [len, voff) are padding).
 template <typename ACC>
 static __device__ __forceinline__ int cta_hestenes_any(float* X, int len, int voff, int cols,
                                                        int ldx, float tol, int max_sweeps,
-                                                       double inv_scale2) {
-  const int nut = (voff + ((cols + 3) & ~3)) / 4;
+                                                       double inv_scale2, bool accum = true,
+                                                       int gcap = 32) {
+  const int nut = (voff + (accum ? ((cols + 3) & ~3) : 0)) / 4;
   int G, NU;
-  jacobi_tile(nut, cols, sizeof(ACC) == 8, &G, &NU);
+  jacobi_tile(nut, cols, sizeof(ACC) == 8, &G, &NU, gcap);
   const bool fits = NU > 0 && (reinterpret_cast<unsigned long>(X) & 15) == 0 && ldx % 4 == 0 &&
                     ldx >= 4 * G * NU;
   if (fits) {
 #define KVD_HJ(GG, UU)                                                                       \
     if (G == GG && NU == UU)                                                                 \
-      return cta_hestenes<GG, UU, ACC>(X, len, voff, cols, ldx, tol, max_sweeps, inv_scale2);
+      return cta_hestenes<GG, UU, ACC>(X, len, voff, cols, ldx, tol, max_sweeps, inv_scale2, accum);
     if constexpr (sizeof(ACC) == 8) {
       KVD_HJ(16, 2) KVD_HJ(16, 3) KVD_HJ(16, 5) KVD_HJ(16, 9)
       KVD_HJ(32, 2) KVD_HJ(32, 3) KVD_HJ(32, 5) KVD_HJ(32, 9)
@@ -258,7 +270,7 @@ static __device__ __forceinline__ int cta_hestenes_any(float* X, int len, int vo
     }
 #undef KVD_HJ
   }
-  return cta_hestenes<32, 0, ACC>(X, len, voff, cols, ldx, tol, max_sweeps, inv_scale2);
+  return cta_hestenes<32, 0, ACC>(X, len, voff, cols, ldx, tol, max_sweeps, inv_scale2, accum);
 }
 
 // 16 consecutive floats p[j0 .. j0+16) of a row, zero past `nb`; `vec` =

@@ -448,6 +448,276 @@ __global__ void __launch_bounds__(kTileThreads) decode_tile_kernel(DecArgs a, in
   }
 }
 
+// ------------------------------------------------------- tensor-core decode
+// decode_tile_kernel's tiling with the three products of a middle tile on
+// the tensor cores (warp-level TF32 m16n8k8, fp32 accumulation; SPLIT =
+// 3xTF32 products, ~fp32 accuracy, for fp32 models).  Warp w owns tokens
+// 16w .. 16w+15 of the tile:
+//   * keys     K = C_k (16 x r) U_k,g^T (r x D) in accumulator fragments; a
+//     thread holds columns 8j + 2t, 8j + 2t + 1 of every n-tile j, so the
+//     rotate-half partners (d, d + D/2) sit in its registers and RoPE is
+//     applied there, one angle per (token, frequency);
+//   * scores   S = K q^T: the key fragments are the A operand directly, with
+//     the k index of each 8-column block permuted (accumulator column 2t
+//     and 2t+1 as A columns t and t+4) and q's B fragment permuted alike;
+//   * values   acc_c (heads x r) += P (heads x tokens) C_v (tokens x r), warp
+//     w owning the coordinate n-tiles w, w + 4, ..; kept in fragments across
+//     tiles with the online-softmax rescale.
+// Verbatim tiles (sinks, exact tier, ring) are handled as in decode_tile_kernel.
+constexpr int kMaxCT = 4;  // coordinate n-tiles per warp: rank <= 4 * 4 * 8 = 128
+
+template <typename T, int D, bool SPLIT>
+__global__ void __launch_bounds__(kTileThreads) decode_mma_kernel(DecArgs a, int nv0, int nm,
+                                                                  int n_tiles) {
+  constexpr int half = D / 2, NT = D / 8, HT = D / 16;
+  constexpr int ldk = D + 4;
+  constexpr int ldps = kTT + 4;  // = 4 mod 32: P fragment reads (4g + t) conflict-free
+  extern __shared__ __align__(16) float tsm[];
+  const int chunk = blockIdx.x, g = blockIdx.y, p = blockIdx.z;
+  const int G = a.G, ld = a.ld, n = a.H * D;
+  const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
+  const int gq = lane >> 2, tq = lane & 3;
+  const int r_k = a.rk[p], r_v = a.rv[p];
+  const int ldc = ld + 4;  // key coordinates / basis rows: fragment reads (4g + t) conflict-free
+  const int ldv = ld + 8;  // value coordinates: fragment reads (8t + g) conflict-free
+  const int vsz = kTT * (ldk > ldv ? ldk : ldv);
+  float* qs = tsm;              // [G][D]
+  float* ks = qs + G * D;       // [kTT][ldk] keys | [kTT][ldc] key coordinates
+  float* vs = ks + kTT * ldk;   // [kTT][ldk] values | [kTT][ldv] value coordinates
+  float* ps = vs + vsz;         // [G][ldps] scores, then probabilities
+  float* us = ps + G * ldps;    // [D][ldc] U_k,g rows
+  float* st = us + D * ldc;     // [G][4] -, -, running max, rescale of the tile
+  const T* qp = reinterpret_cast<const T*>(a.q) + (long)p * a.Hq * D;
+  for (int e = tid; e < G * D; e += kTileThreads) qs[e] = load_f<T>(qp + (long)(g * G + e / D) * D + e % D);
+  if (tid < G) st[4 * tid + 2] = -INFINITY;
+  const int mid0 = a.sink_len + a.hh_len;
+  const int t_begin = chunk * kTilesPerCta, t_end = min(n_tiles, t_begin + kTilesPerCta);
+  if (t_end > nv0 && t_begin < nv0 + nm) {  // U_k,g rows, once for the CTA's middle tiles
+    const float* U = a.uk + p * a.u_sp;
+    for (int e = tid; e < D * ld; e += kTileThreads) {
+      const int d = e / ld, c = e % ld;
+      us[d * ldc + c] = c < r_k ? U[(long)(g * D + d) * ld + c] : 0.f;
+    }
+  }
+  __syncthreads();
+  // q's B fragments for the scores product (heads >= G are zero)
+  float qf[NT][2];
+#pragma unroll
+  for (int j = 0; j < NT; ++j) {
+    qf[j][0] = gq < G ? qs[gq * D + 8 * j + 2 * tq] : 0.f;
+    qf[j][1] = gq < G ? qs[gq * D + 8 * j + 2 * tq + 1] : 0.f;
+  }
+  // verbatim outputs acc_d (G x D) strided over the threads; acc_c in fragments
+  const int n_outd = G * D;
+  constexpr int kMaxOutD = 8;  // (G <= 8) x (D <= 128) / 128
+  float acc[kMaxOutD];
+#pragma unroll
+  for (int k = 0; k < kMaxOutD; ++k) acc[k] = 0.f;
+  float cacc[kMaxCT][4];
+#pragma unroll
+  for (int i = 0; i < kMaxCT; ++i)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) cacc[i][q] = 0.f;
+  const int nct = ld / 8;
+  float lsum[2] = {0.f, 0.f};  // running sums of heads warp, warp + 4 (lane 0 of each warp)
+  for (int tile = t_begin; tile < t_end; ++tile) {
+    __syncthreads();  // previous tile's buffers are free
+    int kind, j0, ntok;
+    if (tile < nv0) { kind = 0; j0 = tile * kTT; ntok = min(kTT, mid0 - j0); }
+    else if (tile < nv0 + nm) { kind = 1; j0 = (tile - nv0) * kTT; ntok = min(kTT, a.W - j0); }
+    else { kind = 2; j0 = (tile - nv0 - nm) * kTT; ntok = min(kTT, a.ring_len - j0); }
+    if (kind != 1) {
+      for (int e = tid; e < kTT * D; e += kTileThreads) {
+        const int tt = e / D, d = e % D;
+        float kv = 0.f, vv = 0.f;
+        if (tt < ntok) {
+          const int t = j0 + tt;
+          const T* kr; const T* vr;
+          if (kind == 2) {
+            kr = reinterpret_cast<const T*>(a.ring_k) + p * a.ring_sp + (long)t * n;
+            vr = reinterpret_cast<const T*>(a.ring_v) + p * a.ring_sp + (long)t * n;
+          } else if (t < a.sink_len) {
+            kr = reinterpret_cast<const T*>(a.sink_k) + p * a.sink_sp + (long)t * n;
+            vr = reinterpret_cast<const T*>(a.sink_v) + p * a.sink_sp + (long)t * n;
+          } else {
+            kr = reinterpret_cast<const T*>(a.hh_k) + p * a.hh_sp + (long)(t - a.sink_len) * n;
+            vr = reinterpret_cast<const T*>(a.hh_v) + p * a.hh_sp + (long)(t - a.sink_len) * n;
+          }
+          kv = load_f<T>(kr + g * D + d);
+          vv = load_f<T>(vr + g * D + d);
+        }
+        ks[tt * ldk + d] = kv;
+        vs[tt * ldk + d] = vv;
+      }
+      __syncthreads();
+      const int tt = tid % kTT, hs = tid / kTT;  // thread -> token tt, heads hs, hs + 2, ...
+      const float* kr = ks + tt * ldk;
+      for (int h = hs; h < G; h += kTileThreads / kTT) {
+        const float* qr = qs + h * D;
+        float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+        for (int d = 0; d < D; d += 8) {
+          const float4 k0 = *reinterpret_cast<const float4*>(kr + d);
+          const float4 k1 = *reinterpret_cast<const float4*>(kr + d + 4);
+          const float4 q0 = *reinterpret_cast<const float4*>(qr + d);
+          const float4 q1 = *reinterpret_cast<const float4*>(qr + d + 4);
+          s0 = fmaf(q0.x, k0.x, s0); s0 = fmaf(q0.y, k0.y, s0); s0 = fmaf(q0.z, k0.z, s0); s0 = fmaf(q0.w, k0.w, s0);
+          s1 = fmaf(q1.x, k1.x, s1); s1 = fmaf(q1.y, k1.y, s1); s1 = fmaf(q1.z, k1.z, s1); s1 = fmaf(q1.w, k1.w, s1);
+        }
+        ps[h * ldps + tt] = tt < ntok ? (s0 + s1) * a.scaling : -INFINITY;
+      }
+    } else {
+      const float* Ck = a.ck + p * a.c_sp + (long)j0 * ld;
+      const float* Cv = a.cv + p * a.c_sp + (long)j0 * ld;
+      const int l4 = ld / 4;
+      for (int e = tid; e < kTT * l4; e += kTileThreads) {
+        const int tt = e / l4, c = 4 * (e % l4);
+        float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+        if (tt < ntok) {
+          kv = *reinterpret_cast<const float4*>(Ck + (long)tt * ld + c);
+          vv = *reinterpret_cast<const float4*>(Cv + (long)tt * ld + c);
+          if (c + 4 > r_k) { if (c >= r_k) kv.x = 0.f; if (c + 1 >= r_k) kv.y = 0.f; if (c + 2 >= r_k) kv.z = 0.f; kv.w = 0.f; }
+          if (c + 4 > r_v) { if (c >= r_v) vv.x = 0.f; if (c + 1 >= r_v) vv.y = 0.f; if (c + 2 >= r_v) vv.z = 0.f; vv.w = 0.f; }
+        }
+        *reinterpret_cast<float4*>(ks + tt * ldc + c) = kv;
+        *reinterpret_cast<float4*>(vs + tt * ldv + c) = vv;
+      }
+      __syncthreads();
+      // keys of rows tt0 = 16w + g and tt1 = tt0 + 8
+      const int tt0 = warp * 16 + gq, tt1 = tt0 + 8;
+      float kacc[NT][4];
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) kacc[j][q] = 0.f;
+      const int nkk = (r_k + 7) / 8;
+      for (int kk = 0; kk < nkk; ++kk) {
+        const int c0 = kk * 8 + tq;
+        const float af[4] = {ks[tt0 * ldc + c0], ks[tt1 * ldc + c0], ks[tt0 * ldc + c0 + 4],
+                             ks[tt1 * ldc + c0 + 4]};
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+          const float* ur = us + (j * 8 + gq) * ldc + c0;
+          mma_f32<SPLIT>(kacc[j], af, ur[0], ur[4]);
+        }
+      }
+      // RoPE on the pairs (8j + 2t + e, + D/2) at each row's true position
+      const int pos0 = tt0 < ntok ? (a.mid_pos ? a.mid_pos[p * a.mid_sp + j0 + tt0] : a.pos_base + j0 + tt0) : 0;
+      const int pos1 = tt1 < ntok ? (a.mid_pos ? a.mid_pos[p * a.mid_sp + j0 + tt1] : a.pos_base + j0 + tt1) : 0;
+#pragma unroll
+      for (int j = 0; j < HT; ++j)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float w = a.inv_freq[8 * j + 2 * tq + e];
+          float c0, s0, c1, s1, y1, y2;
+          rope_cs_fast(pos0, w, a.rope_scale, &c0, &s0);
+          rope_cs_fast(pos1, w, a.rope_scale, &c1, &s1);
+          rope_apply_pair(kacc[j][e], kacc[j + HT][e], c0, s0, &y1, &y2);
+          kacc[j][e] = y1; kacc[j + HT][e] = y2;
+          rope_apply_pair(kacc[j][2 + e], kacc[j + HT][2 + e], c1, s1, &y1, &y2);
+          kacc[j][2 + e] = y1; kacc[j + HT][2 + e] = y2;
+        }
+      // scores of the group's heads (n = head, heads >= G zero)
+      float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+        const float af[4] = {kacc[j][0], kacc[j][2], kacc[j][1], kacc[j][3]};
+        mma_f32<SPLIT>(sacc, af, qf[j][0], qf[j][1]);
+      }
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int h = 2 * tq + e;
+        if (h < G) {
+          ps[h * ldps + tt0] = tt0 < ntok ? sacc[e] * a.scaling : -INFINITY;
+          ps[h * ldps + tt1] = tt1 < ntok ? sacc[2 + e] * a.scaling : -INFINITY;
+        }
+      }
+    }
+    __syncthreads();
+    // per head: tile max and probabilities relative to the new running max
+    for (int h = warp; h < G; h += kTileThreads / 32) {
+      float* pr = ps + h * ldps;
+      const float x0 = pr[lane], x1 = pr[lane + 32];
+      float mt = fmaxf(x0, x1);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o));
+      const float mold = st[4 * h + 2];
+      const float mnew = fmaxf(mold, mt);
+      const float e0 = mnew == -INFINITY ? 0.f : expf(x0 - mnew);
+      const float e1 = mnew == -INFINITY ? 0.f : expf(x1 - mnew);
+      pr[lane] = e0;
+      pr[lane + 32] = e1;
+      float ls = e0 + e1;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
+      const float corr = (mold == -INFINITY) ? 0.f : expf(mold - mnew);
+      if (lane == 0) {
+        const int slot = h / (kTileThreads / 32);
+        lsum[slot] = lsum[slot] * corr + ls;
+        st[4 * h + 2] = mnew;
+        st[4 * h + 3] = corr;
+      }
+    }
+    __syncthreads();
+    // acc_d over verbatim tokens
+#pragma unroll
+    for (int k = 0; k < kMaxOutD; ++k) {
+      const int o = tid + kTileThreads * k;
+      if (o >= n_outd) break;
+      const int h = o / D;
+      float add = 0.f;
+      if (kind != 1) {
+        const int d = o % D;
+        const float* pr = ps + h * ldps;
+        for (int tt = 0; tt < ntok; ++tt) add = fmaf(pr[tt], vs[tt * ldk + d], add);
+      }
+      acc[k] = fmaf(acc[k], st[4 * h + 3], add);
+    }
+    // acc_c = corr * acc_c (+ P C_v on middle tiles); fragment rows are heads
+    const float corr_g = gq < G ? st[4 * gq + 3] : 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxCT; ++i) {
+      const int ct = warp + 4 * i;
+      if (ct >= nct) break;
+      cacc[i][0] *= corr_g;
+      cacc[i][1] *= corr_g;
+      if (kind == 1) {
+#pragma unroll 2
+        for (int kk = 0; kk < kTT / 8; ++kk) {
+          const int t0 = kk * 8 + tq;
+          const float af[4] = {gq < G ? ps[gq * ldps + t0] : 0.f, 0.f,
+                               gq < G ? ps[gq * ldps + t0 + 4] : 0.f, 0.f};
+          mma_f32<SPLIT>(cacc[i], af, vs[t0 * ldv + ct * 8 + gq], vs[(t0 + 4) * ldv + ct * 8 + gq]);
+        }
+      }
+    }
+  }
+  __syncthreads();
+  // the CTA's partial record: m[G], l[G], acc_d[G][D], acc_c[G][ld]
+  float* out = a.part + ((long)(p * a.H + g) * a.n_chunks + chunk) * a.part_sp_chunk;
+  for (int h = warp; h < G; h += kTileThreads / 32)
+    if (lane == 0) {
+      out[h] = t_begin < t_end ? st[4 * h + 2] : -INFINITY;
+      out[G + h] = lsum[h / (kTileThreads / 32)];
+    }
+#pragma unroll
+  for (int k = 0; k < kMaxOutD; ++k) {
+    const int o = tid + kTileThreads * k;
+    if (o >= n_outd) break;
+    out[2 * G + o] = acc[k];
+  }
+  if (gq < G) {
+#pragma unroll
+    for (int i = 0; i < kMaxCT; ++i) {
+      const int ct = warp + 4 * i;
+      if (ct >= nct) break;
+      float* oc = out + 2 * G + G * D + gq * ld + ct * 8 + 2 * tq;
+      oc[0] = cacc[i][0];
+      oc[1] = cacc[i][1];
+    }
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(128) decode_merge_kernel(DecArgs a) {
   extern __shared__ __align__(16) float msm2[];
@@ -554,7 +824,20 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
   const size_t need = (size_t)count * a.H * a.n_chunks * a.part_sp_chunk * 4;
   if (need > ws_bytes) { set_error("factored decode: workspace too small"); return KVD_ERR_WORKSPACE; }
   a.part = (float*)ws;
-  if (tiled) {
+  const bool mma = tiled && a.ld % 8 == 0 && a.ld <= 32 * kMaxCT &&
+                   (reinterpret_cast<uintptr_t>(a.ck) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(a.cv) & 15) == 0 && a.c_sp % 4 == 0;
+  if (mma) {
+    const int ldk = a.D + 4, ldv = a.ld + 8, ldc = a.ld + 4;
+    const int tsmem = 4 * (a.G * a.D + kTT * ldk + kTT * (ldk > ldv ? ldk : ldv) +
+                           a.G * (kTT + 4) + a.D * ldc + 4 * a.G);
+    dim3 tgrid(a.n_chunks, a.H, count);
+    constexpr bool kSplit = sizeof(T) == 4;
+    auto fn = a.D == 64 ? decode_mma_kernel<T, 64, kSplit> : decode_mma_kernel<T, 128, kSplit>;
+    if (int rc0 = ensure_smem((const void*)fn, tsmem, "decode_mma_kernel")) return rc0;
+    KTimerScope kts_("decode_mma_kernel", s);
+    fn<<<tgrid, kTileThreads, tsmem, s>>>(a, nv0, nm, n_tiles);
+  } else if (tiled) {
     const int tsmem = 4 * (a.G * a.D + 2 * kTT * (a.D + 4) + a.G * kTT + a.ld * a.D +
                            a.ld * (kTT + 4) + 4 * a.G);
     dim3 tgrid(a.n_chunks, a.H, count);

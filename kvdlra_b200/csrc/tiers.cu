@@ -427,3 +427,35 @@ KVD_INST(__nv_bfloat16)
 #undef KVD_INST
 
 }  // namespace kvd_host
+
+namespace kvd {
+__global__ void rope_table_kernel(int n, const int* pos, int nf, const float* inv_freq, float scale,
+                                  int fast, float* co, float* so) {
+  for (long e = blockIdx.x * (long)blockDim.x + threadIdx.x; e < (long)n * nf;
+       e += (long)gridDim.x * blockDim.x) {
+    const int i = (int)(e / nf), f = (int)(e % nf);
+    float c, s;
+    if (fast) rope_cs_fast(pos[i], inv_freq[f], scale, &c, &s);
+    else rope_cs(pos[i], inv_freq[f], scale, &c, &s);
+    co[e] = c;
+    so[e] = s;
+  }
+}
+}  // namespace kvd
+
+extern "C" int kvd_rope_table(int32_t n, const int32_t* pos, int32_t nf, const float* inv_freq,
+                              float scale, int32_t fast, float* cos_out, float* sin_out,
+                              kvd_stream_t stream) {
+  using namespace kvd_host;
+  if (n < 0 || nf < 0) { set_error("kvd_rope_table: negative size"); return KVD_ERR_ARG; }
+  if ((long)n * nf == 0) return KVD_OK;
+  if (!pos || !inv_freq || !cos_out || !sin_out) {
+    set_error("kvd_rope_table: null pointer");
+    return KVD_ERR_ARG;
+  }
+  const long tot = (long)n * nf;
+  const int grid = (int)((tot + 255) / 256 < 4096 ? (tot + 255) / 256 : 4096);
+  kvd::rope_table_kernel<<<grid, 256, 0, (cudaStream_t)stream>>>(n, pos, nf, inv_freq, scale, fast,
+                                                                 cos_out, sin_out);
+  return check_launch("rope_table_kernel");
+}
