@@ -149,8 +149,7 @@ def kernel_bytes(w: dict) -> dict[str, float]:
       bug_step      2 streams x P x (read U n*r*4 + block b*n*4 + write U' n*r*4
                     + coords b*r*4)
       slash_score   P x (read candidates m*n*2 + basis n*r*4 + scores m*4)
-      slash_move    P x (read candidates K,V 2*m*n*2 + write tier 2*h*n*2
-                    + demoted block 2*d*n*4)
+      slash_keep    P x (read kept K,V rows 2*h*n*2 + write tier 2*h*n*2)
       carry         2 x P x W*r*4*2 (read + write the coordinates)
       mid_hat       P x (read C_k, C_v 2*W*r*4 + write K, V 2*W*n*2)
       decode        P x (C_k, C_v 2*W*r*4 + positions W*4 + U_k, U_v 2*n*r*4   (tile + merge)
@@ -159,7 +158,7 @@ def kernel_bytes(w: dict) -> dict[str, float]:
     L, H, D, r = w["layers"], w["kv_heads"], w["head_dim"], w["rank"]
     n, T, C = H * D, w["tokens"], w["chunk"]
     sinks, ring, b, h, pbs = w["sinks"], w["ring"], w["absorb"], w["hh"], w["prefill_block"]
-    out = {k: 0.0 for k in ("bug_step_kernel", "slash_score_kernel", "slash_move_kernel",
+    out = {k: 0.0 for k in ("bug_step_kernel", "slash_score_kernel", "slash_keep_kernel",
                             "carry_kernel", "mid_hat_kernel", "decode_tile_kernel")}
     rk, W, hh, rl, cum = 0, 0, 0, 0, 0
 
@@ -177,7 +176,7 @@ def kernel_bytes(w: dict) -> dict[str, float]:
         keep = min(h, m)
         d = m - keep
         out["slash_score_kernel"] += L * (m * n * 2 + n * r * 4 + m * 4)
-        out["slash_move_kernel"] += L * (2 * m * n * 2 + 2 * keep * n * 2 + 2 * d * n * 4)
+        out["slash_keep_kernel"] += L * (2 * keep * n * 2 + 2 * keep * n * 2)
         hh = keep
         if d:
             bug(d)

@@ -468,7 +468,7 @@ constexpr int kMaxCT = 4;  // coordinate n-tiles per warp: rank <= 4 * 4 * 8 = 1
 
 template <typename T, int D, bool SPLIT>
 __global__ void __launch_bounds__(kTileThreads) decode_mma_kernel(DecArgs a, int nv0, int nm,
-                                                                  int n_tiles) {
+                                                                  int n_tiles, int tpc) {
   constexpr int half = D / 2, NT = D / 8, HT = D / 16;
   constexpr int ldk = D + 4;
   constexpr int ldps = kTT + 4;  // = 4 mod 32: P fragment reads (4g + t) conflict-free
@@ -491,7 +491,7 @@ __global__ void __launch_bounds__(kTileThreads) decode_mma_kernel(DecArgs a, int
   for (int e = tid; e < G * D; e += kTileThreads) qs[e] = load_f<T>(qp + (long)(g * G + e / D) * D + e % D);
   if (tid < G) st[4 * tid + 2] = -INFINITY;
   const int mid0 = a.sink_len + a.hh_len;
-  const int t_begin = chunk * kTilesPerCta, t_end = min(n_tiles, t_begin + kTilesPerCta);
+  const int t_begin = chunk * tpc, t_end = min(n_tiles, t_begin + tpc);
   if (t_end > nv0 && t_begin < nv0 + nm) {  // U_k,g rows, once for the CTA's middle tiles
     const float* U = a.uk + p * a.u_sp;
     for (int e = tid; e < D * ld; e += kTileThreads) {
@@ -718,6 +718,318 @@ __global__ void __launch_bounds__(kTileThreads) decode_mma_kernel(DecArgs a, int
   }
 }
 
+// ------------------------------------------------ middle tier, all groups
+// One CTA per (chunk of middle tiles, problem) for every KV group at once,
+// so a tile's coordinates are staged once (cp.async, the next tile's copy
+// in flight during this tile's work) and its rotary angles computed once per
+// (token, frequency).  Warps take (16-token row block, group) tasks: key
+// rebuild C_k U_k,g^T, RoPE in the accumulator fragments, scores against the
+// group's heads (as decode_mma_kernel).  The value product runs over all
+// Hq = H*G query heads at once, acc_c (Hq x r) += P (Hq x tokens) C_v, in
+// (16-head m-tile, 8-coordinate n-tile) fragments spread over the warps.
+// Staged operands are masked (tokens past the tile, coordinates past the
+// rank) and, without SPLIT, rounded to TF32 once in shared memory, so the
+// fragment loads feed the MMAs directly.  Each CTA writes one partial record
+// per group (acc_d zero).
+constexpr int kMidThreads = 512;
+constexpr int kMidWarps = kMidThreads / 32;
+constexpr int kMaxPW = 2;   // value-product fragments per warp: ceil(Hq/16) * r/8 <= 32
+constexpr int kMaxRW = 4;   // softmax rows per warp: Hq <= 64
+
+__device__ __forceinline__ void cp_async16_dec(void* smem_dst, const void* gsrc) {
+  const unsigned sa = (unsigned)__cvta_generic_to_shared(smem_dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(sa), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async4_dec(void* smem_dst, const void* gsrc) {
+  const unsigned sa = (unsigned)__cvta_generic_to_shared(smem_dst);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(sa), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit_wait0() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+
+// Shared-memory layout of decode_mid_kernel (floats), host and device alike.
+struct MidSmem {
+  int ldc, ldv, cpitch, us, qs, cbuf, cbsz, cosb, sinb, ps, st, posb, invs, total;
+};
+__host__ __device__ inline MidSmem mid_smem(int n, int Hq, int D, int ld) {
+  MidSmem m;
+  m.ldc = ld + 4;        // key coordinates / basis rows: A and B fragment reads conflict-free
+  m.ldv = ld + 8;        // value coordinates: B fragment reads conflict-free
+  m.cpitch = D / 2 + 4;  // cos / sin rows
+  m.us = 0;                                     // [n][ldc]
+  m.qs = m.us + n * m.ldc;                      // [Hq][D]
+  m.cbuf = m.qs + Hq * D;                       // 2 x ([kTT][ldc] + [kTT][ldv])
+  m.cbsz = kTT * (m.ldc + m.ldv);
+  m.cosb = m.cbuf + 2 * m.cbsz;                 // [kTT][cpitch]
+  m.sinb = m.cosb + kTT * m.cpitch;             // [kTT][cpitch]
+  m.ps = m.sinb + kTT * m.cpitch;               // [Hq + 1][kTT + 4], the last row zero
+  m.st = m.ps + (Hq + 1) * (kTT + 4);           // [Hq][4]
+  m.posb = m.st + 4 * Hq;                       // int [2][kTT]
+  m.invs = m.posb + 2 * kTT;                    // [D/2]
+  m.total = m.invs + D / 2;
+  return m;
+}
+
+template <typename T, int D, bool SPLIT>
+__global__ void __launch_bounds__(kMidThreads) decode_mid_kernel(DecArgs a, int tpc, int chunk0) {
+  constexpr int half = D / 2, NT = D / 8, HT = D / 16;
+  constexpr int ldps = kTT + 4;
+  extern __shared__ __align__(16) float msm3[];
+  const int p = blockIdx.y;
+  const int H = a.H, G = a.G, Hq = a.H * a.G, ld = a.ld, n = a.H * D;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int gq = lane >> 2, tq = lane & 3;
+  const int r_k = a.rk[p], r_v = a.rv[p];
+  const MidSmem L = mid_smem(n, Hq, D, ld);
+  const int ldc = L.ldc, ldv = L.ldv, cp = L.cpitch;
+  float* us = msm3 + L.us;
+  float* qs = msm3 + L.qs;
+  float* cbuf = msm3 + L.cbuf;
+  float* cosb = msm3 + L.cosb;
+  float* sinb = msm3 + L.sinb;
+  float* ps = msm3 + L.ps;
+  float* st = msm3 + L.st;
+  int* posb = reinterpret_cast<int*>(msm3 + L.posb);
+  float* invs = msm3 + L.invs;
+  const int nm = (a.W + kTT - 1) / kTT;
+  const int t_begin = blockIdx.x * tpc, t_end = min(nm, t_begin + tpc);
+  const int l4 = ld / 4;
+  auto prefetch = [&](int tile, int slot) {
+    const int j0 = tile * kTT, ntok = min(kTT, a.W - j0);
+    float* kb = cbuf + slot * L.cbsz;
+    float* vb = kb + kTT * ldc;
+    const float* Ck = a.ck + p * a.c_sp + (long)j0 * ld;
+    const float* Cv = a.cv + p * a.c_sp + (long)j0 * ld;
+    for (int e = tid; e < ntok * l4; e += kMidThreads) {
+      const int tt = e / l4, c = 4 * (e % l4);
+      cp_async16_dec(kb + tt * ldc + c, Ck + (long)tt * ld + c);
+      cp_async16_dec(vb + tt * ldv + c, Cv + (long)tt * ld + c);
+    }
+    if (tid < ntok) {
+      int* pb = posb + slot * kTT;
+      if (a.mid_pos) cp_async4_dec(pb + tid, a.mid_pos + p * a.mid_sp + j0 + tid);
+      else pb[tid] = a.pos_base + j0 + tid;
+    }
+  };
+  // prologue: every group's basis rows, the queries, the first tile
+  {
+    const float* U = a.uk + p * a.u_sp;
+    for (int e = tid; e < n * l4; e += kMidThreads) {
+      const int row = e / l4, c = 4 * (e % l4);
+      cp_async16_dec(us + row * ldc + c, U + (long)row * ld + c);
+    }
+  }
+  prefetch(t_begin, 0);
+  const T* qp = reinterpret_cast<const T*>(a.q) + (long)p * a.Hq * D;
+  for (int e = tid; e < Hq * D; e += kMidThreads) qs[e] = load_f<T>(qp + e);
+  for (int f = tid; f < half; f += kMidThreads) invs[f] = a.inv_freq[f];
+  for (int h = tid; h < Hq; h += kMidThreads) st[4 * h + 2] = -INFINITY;
+  for (int e = tid; e < ldps; e += kMidThreads) ps[Hq * ldps + e] = 0.f;
+  cp_async_commit_wait0();
+  __syncthreads();
+  for (int e = tid; e < n * ld; e += kMidThreads) {  // columns past the rank are not basis
+    const int row = e / ld, c = e % ld;
+    const float x = us[row * ldc + c];
+    us[row * ldc + c] = c < r_k ? (SPLIT ? x : __uint_as_float(tf32_bits(x))) : 0.f;
+  }
+  const int nct = ld / 8, nmt = (Hq + 15) / 16, npairs = nmt * nct;
+  float cacc[kMaxPW][4];
+#pragma unroll
+  for (int i = 0; i < kMaxPW; ++i)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) cacc[i][q] = 0.f;
+  float lsum[kMaxRW];
+#pragma unroll
+  for (int i = 0; i < kMaxRW; ++i) lsum[i] = 0.f;
+  for (int tile = t_begin; tile < t_end; ++tile) {
+    const int slot = (tile - t_begin) & 1;
+    __syncthreads();  // the other slot's previous tile is done; U zeroing visible
+    if (tile + 1 < t_end) prefetch(tile + 1, slot ^ 1);
+    cp_async_commit();
+    const int j0 = tile * kTT, ntok = min(kTT, a.W - j0);
+    const float* kb = cbuf + slot * L.cbsz;
+    const float* vb = kb + kTT * ldc;
+    const int* pb = posb + slot * kTT;
+    for (int e = tid; e < kTT * half; e += kMidThreads) {  // the tile's rotary angles
+      const int tt = e / half, f = e % half;
+      float c = 1.f, sn = 0.f;
+      if (tt < ntok) rope_cs_fast(pb[tt], invs[f], a.rope_scale, &c, &sn);
+      cosb[tt * cp + f] = c;
+      sinb[tt * cp + f] = sn;
+    }
+    {  // mask (and round) the staged coordinates in place
+      float* kw = cbuf + slot * L.cbsz;
+      float* vw = kw + kTT * ldc;
+      for (int e = tid; e < kTT * ld; e += kMidThreads) {
+        const int tt = e / ld, c = e % ld;
+        const float xk = kw[tt * ldc + c], xv = vw[tt * ldv + c];
+        kw[tt * ldc + c] = (tt < ntok && c < r_k) ? (SPLIT ? xk : __uint_as_float(tf32_bits(xk))) : 0.f;
+        vw[tt * ldv + c] = (tt < ntok && c < r_v) ? (SPLIT ? xv : __uint_as_float(tf32_bits(xv))) : 0.f;
+      }
+    }
+    __syncthreads();
+    for (int task = warp; task < 4 * H; task += kMidWarps) {
+      const int g = task >> 2;
+      const int tt0 = (task & 3) * 16 + gq, tt1 = tt0 + 8;
+      float kacc[NT][4];
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) kacc[j][q] = 0.f;
+      const int nkk = (r_k + 7) / 8;
+      for (int kk = 0; kk < nkk; ++kk) {
+        const int c0 = kk * 8 + tq;
+        const float af[4] = {kb[tt0 * ldc + c0], kb[tt1 * ldc + c0], kb[tt0 * ldc + c0 + 4],
+                             kb[tt1 * ldc + c0 + 4]};
+        if constexpr (SPLIT) {
+          uint32_t ah[4], al[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) tf32_split(af[q], &ah[q], &al[q]);
+#pragma unroll
+          for (int j = 0; j < NT; ++j) {
+            const float* ur = us + (g * D + j * 8 + gq) * ldc + c0;
+            uint32_t bh0, bl0, bh1, bl1;
+            tf32_split(ur[0], &bh0, &bl0);
+            tf32_split(ur[4], &bh1, &bl1);
+            mma_tf32(kacc[j], al, bh0, bh1);
+            mma_tf32(kacc[j], ah, bl0, bl1);
+            mma_tf32(kacc[j], ah, bh0, bh1);
+          }
+        } else {
+          const uint32_t ah[4] = {__float_as_uint(af[0]), __float_as_uint(af[1]),
+                                  __float_as_uint(af[2]), __float_as_uint(af[3])};
+#pragma unroll
+          for (int j = 0; j < NT; ++j) {
+            const float* ur = us + (g * D + j * 8 + gq) * ldc + c0;
+            mma_tf32(kacc[j], ah, __float_as_uint(ur[0]), __float_as_uint(ur[4]));
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < HT; ++j) {
+        const int f = 8 * j + 2 * tq;
+        const float2 ca = *reinterpret_cast<const float2*>(cosb + tt0 * cp + f);
+        const float2 sa = *reinterpret_cast<const float2*>(sinb + tt0 * cp + f);
+        const float2 cb = *reinterpret_cast<const float2*>(cosb + tt1 * cp + f);
+        const float2 sb = *reinterpret_cast<const float2*>(sinb + tt1 * cp + f);
+        const float c0s[2] = {ca.x, ca.y}, s0s[2] = {sa.x, sa.y}, c1s[2] = {cb.x, cb.y}, s1s[2] = {sb.x, sb.y};
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          float y1, y2;
+          rope_apply_pair(kacc[j][e], kacc[j + HT][e], c0s[e], s0s[e], &y1, &y2);
+          kacc[j][e] = y1; kacc[j + HT][e] = y2;
+          rope_apply_pair(kacc[j][2 + e], kacc[j + HT][2 + e], c1s[e], s1s[e], &y1, &y2);
+          kacc[j][2 + e] = y1; kacc[j + HT][2 + e] = y2;
+        }
+      }
+      float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+      const float* qr = qs + (g * G + gq) * D + 2 * tq;
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+        const float af[4] = {kacc[j][0], kacc[j][2], kacc[j][1], kacc[j][3]};
+        mma_f32<SPLIT>(sacc, af, gq < G ? qr[8 * j] : 0.f, gq < G ? qr[8 * j + 1] : 0.f);
+      }
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int h = 2 * tq + e;
+        if (h < G) {
+          float* pr = ps + (g * G + h) * ldps;
+          pr[tt0] = tt0 < ntok ? sacc[e] * a.scaling : -INFINITY;
+          pr[tt1] = tt1 < ntok ? sacc[2 + e] * a.scaling : -INFINITY;
+        }
+      }
+    }
+    __syncthreads();
+    // softmax per query head over the tile, online across tiles
+#pragma unroll
+    for (int i = 0; i < kMaxRW; ++i) {
+      const int row = warp + kMidWarps * i;
+      if (row >= Hq) break;
+      float* pr = ps + row * ldps;
+      const float x0 = pr[lane], x1 = pr[lane + 32];
+      float mt = fmaxf(x0, x1);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o));
+      const float mold = st[4 * row + 2];
+      const float mnew = fmaxf(mold, mt);
+      const float e0 = mnew == -INFINITY ? 0.f : expf(x0 - mnew);
+      const float e1 = mnew == -INFINITY ? 0.f : expf(x1 - mnew);
+      pr[lane] = SPLIT ? e0 : __uint_as_float(tf32_bits(e0));  // the value product's A operand
+      pr[lane + 32] = SPLIT ? e1 : __uint_as_float(tf32_bits(e1));
+      float ls = e0 + e1;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, o);
+      const float corr = (mold == -INFINITY) ? 0.f : expf(mold - mnew);
+      lsum[i] = lsum[i] * corr + ls;
+      __syncwarp();
+      if (lane == 0) {
+        st[4 * row + 2] = mnew;
+        st[4 * row + 3] = corr;
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < kMaxPW; ++i) {
+      const int pair = warp + kMidWarps * i;
+      if (pair >= npairs) break;
+      const int mt = pair / nct, ct = pair % nct;
+      const int ra = mt * 16 + gq, rb = ra + 8;
+      const float ca = ra < Hq ? st[4 * ra + 3] : 0.f, cb = rb < Hq ? st[4 * rb + 3] : 0.f;
+      cacc[i][0] *= ca; cacc[i][1] *= ca; cacc[i][2] *= cb; cacc[i][3] *= cb;
+      // rows past Hq read the padding rows of ps (zero), columns are in range
+      const float* pa = ps + (ra < Hq ? ra : Hq) * ldps;
+      const float* pb2 = ps + (rb < Hq ? rb : Hq) * ldps;
+      const float* vc = vb + ct * 8 + gq;
+#pragma unroll 4
+      for (int kk = 0; kk < kTT / 8; ++kk) {
+        const int t0 = kk * 8 + tq;
+        const float af[4] = {pa[t0], pb2[t0], pa[t0 + 4], pb2[t0 + 4]};
+        if constexpr (SPLIT) {
+          mma_f32<true>(cacc[i], af, vc[t0 * ldv], vc[(t0 + 4) * ldv]);
+        } else {
+          const uint32_t ah[4] = {__float_as_uint(af[0]), __float_as_uint(af[1]),
+                                  __float_as_uint(af[2]), __float_as_uint(af[3])};
+          mma_tf32(cacc[i], ah, __float_as_uint(vc[t0 * ldv]), __float_as_uint(vc[(t0 + 4) * ldv]));
+        }
+      }
+    }
+    asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+  }
+  __syncthreads();
+  // one partial record per group: m[G], l[G], acc_d[G][D] = 0, acc_c[G][ld]
+  const int chunk = chunk0 + blockIdx.x;
+  auto rec = [&](int g) { return a.part + ((long)(p * H + g) * a.n_chunks + chunk) * a.part_sp_chunk; };
+#pragma unroll
+  for (int i = 0; i < kMaxRW; ++i) {
+    const int row = warp + kMidWarps * i;
+    if (row >= Hq) break;
+    if (lane == 0) {
+      float* o = rec(row / G);
+      o[row % G] = t_begin < t_end ? st[4 * row + 2] : -INFINITY;
+      o[G + row % G] = lsum[i];
+    }
+  }
+  for (int e = tid; e < H * G * D; e += kMidThreads) rec(e / (G * D))[2 * G + e % (G * D)] = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxPW; ++i) {
+    const int pair = warp + kMidWarps * i;
+    if (pair >= npairs) break;
+    const int mt = pair / nct, ct = pair % nct;
+    const int cc = ct * 8 + 2 * tq;
+#pragma unroll
+    for (int half_ = 0; half_ < 2; ++half_) {
+      const int row = mt * 16 + gq + 8 * half_;
+      if (row < Hq) {
+        float* o = rec(row / G) + 2 * G + G * D + (row % G) * ld + cc;
+        o[0] = cacc[i][2 * half_];
+        o[1] = cacc[i][2 * half_ + 1];
+      }
+    }
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(128) decode_merge_kernel(DecArgs a) {
   extern __shared__ __align__(16) float msm2[];
@@ -728,28 +1040,34 @@ __global__ void __launch_bounds__(128) decode_merge_kernel(DecArgs a) {
   float* accc = msm2;        // [G][ld]
   float* accd = accc + G * ld;  // [G][D]
   float* ml = accd + G * D;     // [G][2]: M, Lsum
-  for (int qh = threadIdx.x; qh < G; qh += blockDim.x) {
+  float* sc = ml + 2 * G;       // [n_chunks][G]: exp(m_c - M) per chunk and head
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32, nw = blockDim.x / 32;
+  const int nch = a.n_chunks;
+  const long sp = a.part_sp_chunk;
+  for (int qh = warp; qh < G; qh += nw) {  // a warp per head, lanes over the chunks
     float M = -INFINITY;
-    for (int c = 0; c < a.n_chunks; ++c) M = fmaxf(M, parts[c * a.part_sp_chunk + qh]);
+    for (int c = lane; c < nch; c += 32) M = fmaxf(M, parts[c * sp + qh]);
+    M = warp_max(M);
     float Ls = 0.f;
-    for (int c = 0; c < a.n_chunks; ++c) {
-      const float mc = parts[c * a.part_sp_chunk + qh];
-      if (mc != -INFINITY) Ls += expf(mc - M) * parts[c * a.part_sp_chunk + G + qh];
+    for (int c = lane; c < nch; c += 32) {
+      const float mc = parts[c * sp + qh];
+      const float f = mc == -INFINITY ? 0.f : expf(mc - M);
+      sc[c * G + qh] = f;
+      Ls = fmaf(f, parts[c * sp + G + qh], Ls);
     }
-    ml[2 * qh] = M;
-    ml[2 * qh + 1] = Ls;
+    Ls = warp_sum(Ls);
+    if (lane == 0) {
+      ml[2 * qh] = M;
+      ml[2 * qh + 1] = Ls;
+    }
   }
   __syncthreads();
   for (int e = threadIdx.x; e < G * (D + ld); e += blockDim.x) {
     int qh; long off;
     if (e < G * D) { qh = e / D; off = 2 * G + e; }
     else { qh = (e - G * D) / ld; off = 2 * G + G * D + (e - G * D); }
-    const float M = ml[2 * qh];
     float v = 0.f;
-    for (int c = 0; c < a.n_chunks; ++c) {
-      const float mc = parts[c * a.part_sp_chunk + qh];
-      if (mc != -INFINITY) v += expf(mc - M) * parts[c * a.part_sp_chunk + off];
-    }
+    for (int c = 0; c < nch; ++c) v = fmaf(sc[c * G + qh], parts[c * sp + off], v);
     if (e < G * D) accd[e] = v;
     else accc[e - G * D] = v;
   }
@@ -777,7 +1095,11 @@ size_t decode_ws_bytes(const kvd_config& c, int count, int num_q_heads) {
   const int G = num_q_heads / c.num_heads;
   const int L_max = c.n_sink + c.hh_budget + c.w_cap + c.ring_cap;
   const long rec = part_floats(G, c.head_dim, c.rank);
-  return (size_t)count * c.num_heads * dec_chunks(L_max) * rec * 4 + 256;
+  // tiled paths: one chunk per verbatim tile plus middle chunks of >= 2 tiles
+  const int nvt = (c.n_sink + c.hh_budget + kTT - 1) / kTT + (c.ring_cap + kTT - 1) / kTT;
+  const int ch_tiled = nvt + ((c.w_cap + kTT - 1) / kTT + 1) / 2;
+  const int ch = dec_chunks(L_max) > ch_tiled ? dec_chunks(L_max) : ch_tiled;
+  return (size_t)count * c.num_heads * ch * rec * 4 + 256;
 }
 
 template <typename T>
@@ -827,7 +1149,42 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
   const bool mma = tiled && a.ld % 8 == 0 && a.ld <= 32 * kMaxCT &&
                    (reinterpret_cast<uintptr_t>(a.ck) & 15) == 0 &&
                    (reinterpret_cast<uintptr_t>(a.cv) & 15) == 0 && a.c_sp % 4 == 0;
-  if (mma) {
+  // middle tier by decode_mid_kernel (every group per CTA) when the basis of
+  // all groups fits in shared memory; verbatim tiles by decode_mma_kernel
+  const int Hq_all = a.H * a.G;
+  const MidSmem ms = mid_smem(n, Hq_all, a.D, a.ld);
+  const bool mid_all = mma && a.W > 0 && Hq_all <= kMidWarps * kMaxRW && a.ld <= 64 &&
+                       ((Hq_all + 15) / 16) * (a.ld / 8) <= kMidWarps * kMaxPW &&
+                       4L * ms.total <= 200 * 1024 &&
+                       (reinterpret_cast<uintptr_t>(a.uk) & 15) == 0 && a.u_sp % 4 == 0;
+  if (mid_all) {
+    const int nvt = nv0 + nr;
+    const int n_vch = nvt;  // one verbatim tile per CTA
+    int tpc = (int)(((long)nm * count + 4 * 148 - 1) / (4 * 148));
+    tpc = tpc < 2 ? 2 : (tpc > 8 ? 8 : tpc);
+    const int n_mch = (nm + tpc - 1) / tpc;
+    a.n_chunks = n_vch + n_mch;
+    const size_t need2 = (size_t)count * a.H * a.n_chunks * a.part_sp_chunk * 4;
+    if (need2 > ws_bytes) { set_error("factored decode: workspace too small"); return KVD_ERR_WORKSPACE; }
+    constexpr bool kSplit = sizeof(T) == 4;
+    if (n_vch > 0) {
+      const int ldk = a.D + 4, ldv = a.ld + 8, ldc = a.ld + 4;
+      const int tsmem = 4 * (a.G * a.D + kTT * ldk + kTT * (ldk > ldv ? ldk : ldv) +
+                             a.G * (kTT + 4) + a.D * ldc + 4 * a.G);
+      auto fn = a.D == 64 ? decode_mma_kernel<T, 64, kSplit> : decode_mma_kernel<T, 128, kSplit>;
+      if (int rc0 = ensure_smem((const void*)fn, tsmem, "decode_mma_kernel")) return rc0;
+      KTimerScope kts_("decode_mma_kernel", s);
+      fn<<<dim3(n_vch, a.H, count), kTileThreads, tsmem, s>>>(a, nv0, 0, nvt, 1);
+    }
+    if (int rc1 = check_launch("decode_mma_kernel")) return rc1;
+    {
+      auto fn = a.D == 64 ? decode_mid_kernel<T, 64, kSplit> : decode_mid_kernel<T, 128, kSplit>;
+      if (int rc0 = ensure_smem((const void*)fn, 4 * ms.total, "decode_mid_kernel")) return rc0;
+      KTimerScope kts_("decode_mid_kernel", s);
+      fn<<<dim3(n_mch, count), kMidThreads, 4 * ms.total, s>>>(a, tpc, n_vch);
+    }
+    if (int rc1 = check_launch("decode_mid_kernel")) return rc1;
+  } else if (mma) {
     const int ldk = a.D + 4, ldv = a.ld + 8, ldc = a.ld + 4;
     const int tsmem = 4 * (a.G * a.D + kTT * ldk + kTT * (ldk > ldv ? ldk : ldv) +
                            a.G * (kTT + 4) + a.D * ldc + 4 * a.G);
@@ -836,7 +1193,7 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
     auto fn = a.D == 64 ? decode_mma_kernel<T, 64, kSplit> : decode_mma_kernel<T, 128, kSplit>;
     if (int rc0 = ensure_smem((const void*)fn, tsmem, "decode_mma_kernel")) return rc0;
     KTimerScope kts_("decode_mma_kernel", s);
-    fn<<<tgrid, kTileThreads, tsmem, s>>>(a, nv0, nm, n_tiles);
+    fn<<<tgrid, kTileThreads, tsmem, s>>>(a, nv0, nm, n_tiles, kTilesPerCta);
   } else if (tiled) {
     const int tsmem = 4 * (a.G * a.D + 2 * kTT * (a.D + 4) + a.G * kTT + a.ld * a.D +
                            a.ld * (kTT + 4) + 4 * a.G);
@@ -867,7 +1224,8 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
   }
   int rc = check_launch("decode_split_kernel");
   if (rc) return rc;
-  const int msmem = 4 * (a.G * a.ld + a.G * a.D + 2 * a.G);
+  const int msmem = 4 * (a.G * a.ld + a.G * a.D + 2 * a.G + a.n_chunks * a.G);
+  if (int rc0 = ensure_smem((const void*)decode_merge_kernel<T>, msmem, "decode_merge_kernel")) return rc0;
   {
     KTimerScope kts_("decode_merge_kernel", s);
     decode_merge_kernel<T><<<dim3(a.H, count), 128, msmem, s>>>(a);

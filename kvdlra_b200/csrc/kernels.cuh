@@ -109,6 +109,9 @@ int launch_slash_select(const CandSrc<T>& src, int P, int m, int keep_n, int H, 
                         RopeArgs rope, const float* scores, long sc_sp, int hh_neighbor,
                         const SelectOut& out, cudaStream_t stream);
 template <typename T>
+int launch_slash_keep(const CandSrc<T>& src, int P, int keep_n, int n, const SelectOut& out,
+                      cudaStream_t stream);
+template <typename T>
 int launch_gather_block(const T* g_k, const T* g_v, long g_sp, int P, int b, int H, int D,
                         int start, RopeArgs rope, float* xk, float* xv, long x_sp, int* mid_pos,
                         long mid_sp, int w_off, cudaStream_t stream);

@@ -128,8 +128,8 @@ int ensure_smem(const void* func, size_t bytes, const char* name) {
 struct Ws {
   float* scores; long sc_sp;     // [P][hh_budget + max_block]
   float* xk; float* xv; long x_sp;  // [P][max_block][n]
-  float* rot[2]; long rot_sp;    // [P][ld][ld]
-  int* dims[2];                  // [P][4]
+  float* rot[4]; long rot_sp;    // [absorb parity][stream] -> [P][ld][ld]
+  int* dims[4];                  // [absorb parity][stream] -> [P][4]
   int* dem;                      // [P]
   int* keep; long keep_sp;       // [P][w_cap]
   int* order;                    // [P][hh_budget + max_block] tier slot order
@@ -150,10 +150,8 @@ static Ws plan_ws(const kvd_config& c, char* base) {
   w.xk = (float*)take(4ul * P * w.x_sp);
   w.xv = (float*)take(4ul * P * w.x_sp);
   w.rot_sp = (long)ld * ld;
-  w.rot[0] = (float*)take(4ul * P * w.rot_sp);
-  w.rot[1] = (float*)take(4ul * P * w.rot_sp);
-  w.dims[0] = (int*)take(16ul * P);
-  w.dims[1] = (int*)take(16ul * P);
+  for (int i = 0; i < 4; ++i) w.rot[i] = (float*)take(4ul * P * w.rot_sp);
+  for (int i = 0; i < 4; ++i) w.dims[i] = (int*)take(16ul * P);
   w.dem = (int*)take(4ul * P);
   w.keep_sp = c.w_cap;
   w.keep = (int*)take(4ul * P * w.keep_sp);
@@ -185,6 +183,46 @@ static int validate(const kvd_config* c) {
   return KVD_OK;
 }
 
+// ------------------------------------------------------------ carry stream
+// The coordinate carry of absorb i (rotating every stored coordinate row into
+// the new basis) is read by nothing the next absorb's scoring, selection and
+// BUG step touch, so it is launched on a per-device side stream just before
+// BUG step i+1 and runs beside it (the BUG step occupies one SM per problem
+// and stream, the carry the rest): carry i waits for everything issued before
+// BUG step i+1; BUG step i+2, which overwrites the rotation carry i reads
+// (double-buffered by absorb parity), waits for carry i; eviction, which moves
+// coordinate rows, flushes and waits for every carry; and each entry point
+// joins the side stream back into the caller's stream before it returns, so
+// callers see plain stream order.
+struct CarryStream {
+  cudaStream_t side = nullptr;
+  cudaEvent_t bug[2] = {nullptr, nullptr}, carry[2] = {nullptr, nullptr}, join = nullptr;
+  cudaEvent_t ranked = nullptr, kept = nullptr;  // the tier copy: after ranking, then done
+};
+
+static CarryStream* carry_stream() {
+  static std::mutex mu;
+  static std::unordered_map<int, CarryStream> per_dev;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = per_dev.find(dev);
+  if (it != per_dev.end()) return it->second.side ? &it->second : nullptr;
+  CarryStream cs;
+  bool ok = cudaStreamCreateWithFlags(&cs.side, cudaStreamNonBlocking) == cudaSuccess;
+  for (int i = 0; ok && i < 2; ++i)
+    ok = cudaEventCreateWithFlags(&cs.bug[i], cudaEventDisableTiming) == cudaSuccess &&
+         cudaEventCreateWithFlags(&cs.carry[i], cudaEventDisableTiming) == cudaSuccess;
+  ok = ok && cudaEventCreateWithFlags(&cs.join, cudaEventDisableTiming) == cudaSuccess &&
+       cudaEventCreateWithFlags(&cs.ranked, cudaEventDisableTiming) == cudaSuccess &&
+       cudaEventCreateWithFlags(&cs.kept, cudaEventDisableTiming) == cudaSuccess;
+  if (!ok) {
+    cudaGetLastError();
+    cs = CarryStream{};  // carries then run on the caller's stream
+  }
+  return (per_dev[dev] = cs).side ? &per_dev[dev] : nullptr;
+}
+
 // ------------------------------------------------------------ one group
 
 template <typename T>
@@ -198,8 +236,15 @@ struct Group {
   long row_sp_ring, row_sp_hh, u_sp, c_sp;
   RopeArgs rope;
 
+  CarryStream* cs = nullptr;
+  bool carry_pending = false;  // a carry on the side stream not yet joined
+  CarryBatch pend_cb;          // the last absorb's carry, not yet launched
+  int pend_par = -1;
+  bool keep_pending = false;   // a tier copy on the side stream the next scoring must wait for
+
   Group(const kvd_config& c_, const kvd_buffers& b_, kvd_counters& k_, char* ws, cudaStream_t s_)
       : c(c_), b(b_), k(k_), w(plan_ws(c_, ws)), s(s_) {
+    cs = carry_stream();
     n = c.num_heads * c.head_dim;
     P = c.n_problems;
     ld = c.rank;
@@ -210,6 +255,34 @@ struct Group {
     rope.inv_freq = c.inv_freq;
     rope.scale = c.rope_scaling;
     rope.scale_sq = c.rope_scaling * c.rope_scaling;
+  }
+
+  ~Group() {
+    flush_carry();
+    join_carry();
+  }
+
+  // launch the deferred carry: on the side stream after everything issued so
+  // far on the caller's stream, else on the caller's stream
+  int flush_carry() {
+    if (pend_par < 0) return KVD_OK;
+    const int par = pend_par;
+    pend_par = -1;
+    if (!cs) return launch_carry(pend_cb, P, 2, ld, s);
+    cudaEventRecord(cs->bug[par], s);
+    cudaStreamWaitEvent(cs->side, cs->bug[par], 0);
+    const int rc = launch_carry(pend_cb, P, 2, ld, cs->side);
+    cudaEventRecord(cs->carry[par], cs->side);
+    carry_pending = true;
+    return rc;
+  }
+
+  // the caller's stream waits for every carry launched so far
+  void join_carry() {
+    if (!carry_pending) return;
+    cudaEventRecord(cs->join, cs->side);
+    cudaStreamWaitEvent(s, cs->join, 0);
+    carry_pending = false;
   }
 
   bool lowrank() const { return c.rank >= 1 && c.coord_budget >= 1; }
@@ -224,6 +297,11 @@ struct Group {
       set_error("coordinate capacity %d too small (need %d)", c.w_cap, k.w_len + d);
       return KVD_ERR_ARG;
     }
+    const int par = (int)(k.n_absorbs & 1);
+    // the previous absorb's carry runs beside this step
+    if (int rc0 = flush_carry()) return rc0;
+    // this step overwrites rot/dims of parity `par`, last read by the carry two absorbs ago
+    if (carry_pending) cudaStreamWaitEvent(s, cs->carry[par], 0);
     BugStepBatch bb;
     for (int sidx = 0; sidx < 2; ++sidx) {
       BugStepArgs& a = bb.s[sidx];
@@ -234,8 +312,8 @@ struct Group {
       a.sigma = sidx == 0 ? b.sig_k : b.sig_v; a.sig_sp = ld;
       a.r = sidx == 0 ? b.r_k : b.r_v;
       a.x = sidx == 0 ? w.xk : w.xv; a.x_sp = w.x_sp;
-      a.rot = w.rot[sidx]; a.rot_sp = w.rot_sp;
-      a.dims = w.dims[sidx];
+      a.rot = w.rot[2 * par + sidx]; a.rot_sp = w.rot_sp;
+      a.dims = w.dims[2 * par + sidx];
       a.coords = (sidx == 0 ? b.c_k : b.c_v) + (long)k.w_len * ld;
       a.coords_sp = c_sp; a.coords_ld = ld;
       a.has_theta = c.has_theta; a.theta = c.theta;
@@ -249,10 +327,11 @@ struct Group {
       for (int sidx = 0; sidx < 2; ++sidx) {
         CarryArgs& a = cb.s[sidx];
         a.c = sidx == 0 ? b.c_k : b.c_v; a.c_sp = c_sp; a.ld = ld;
-        a.rot = w.rot[sidx]; a.rot_sp = w.rot_sp; a.dims = w.dims[sidx];
+        a.rot = w.rot[2 * par + sidx]; a.rot_sp = w.rot_sp; a.dims = w.dims[2 * par + sidx];
       }
       cb.W = k.w_len;
-      if ((rc = launch_carry(cb, P, 2, ld, s))) return rc;
+      pend_cb = cb;
+      pend_par = par;
     }
     k.u_sel ^= 1;
     k.seeded = 1;
@@ -264,6 +343,8 @@ struct Group {
   int enforce_budgets() {
     const int f_over = k.w_len - c.coord_budget;
     if (f_over <= 0) return KVD_OK;
+    if (int rc0 = flush_carry()) return rc0;
+    join_carry();  // eviction moves coordinate rows
     int rc = launch_evict(P, k.w_len, f_over, c.retention, b.c_k, b.c_v, c_sp, ld, b.r_k, b.r_v,
                           b.mid_pos, track_surprise() ? b.mid_surprise : nullptr, c.w_cap, w.keep,
                           w.keep_sp, s);
@@ -278,6 +359,10 @@ struct Group {
     const int m = k.hh_len + gb;
     const int keep_n = m < c.hh_budget ? m : c.hh_budget;
     const int d = m - keep_n;
+    if (keep_pending) {  // the exact tier this scoring reads was written on the side stream
+      cudaStreamWaitEvent(s, cs->kept, 0);
+      keep_pending = false;
+    }
     if (gb > c.max_block) { set_error("graduating block %d > max_block", gb); return KVD_ERR_ARG; }
     CandSrc<T> src;
     src.hh_k = (const T*)b.hh_k[k.hh_sel]; src.hh_v = (const T*)b.hh_v[k.hh_sel];
@@ -301,6 +386,18 @@ struct Group {
     so.order = w.order; so.order_sp = w.sc_sp;
     rc = launch_slash_select<T>(src, P, m, keep_n, c.num_heads, c.head_dim, rope, w.scores, w.sc_sp,
                                 c.hh_neighbor, so, s);
+    if (rc) return rc;
+    // the kept tokens move into the other tier buffer beside the BUG step
+    if (cs) {
+      cudaEventRecord(cs->ranked, s);
+      cudaStreamWaitEvent(cs->side, cs->ranked, 0);
+      rc = launch_slash_keep<T>(src, P, keep_n, n, so, cs->side);
+      cudaEventRecord(cs->kept, cs->side);
+      keep_pending = true;
+      carry_pending = true;
+    } else {
+      rc = launch_slash_keep<T>(src, P, keep_n, n, so, s);
+    }
     if (rc) return rc;
     k.hh_sel ^= 1;
     k.hh_len = keep_n;

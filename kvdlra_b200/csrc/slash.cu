@@ -6,10 +6,10 @@
 //    fp32 projection so the score is as exact as the basis allows.
 //  * slash_rank_kernel    -- optional span boost (923-950), stable descending
 //    top-h (810-812): the slot order of kept and demoted candidates, their
-//    positions and graduation surprise (813-825 + 871-888).
-//  * slash_move_kernel    -- compaction of the kept tokens into the other
-//    exact-tier buffer and gather of the demoted ones (un-rotated K, fp32 V)
-//    into the BUG-step block, one warp per row over the whole GPU.
+//    positions and graduation surprise, and the gather of the demoted ones
+//    (un-rotated K, fp32 V) into the BUG-step block (813-825 + 871-888).
+//  * slash_keep_kernel    -- compaction of the kept tokens into the other
+//    exact-tier buffer, one warp per row over the whole GPU.
 //  * gather_block_kernel  -- the no-tier absorb path (743-750).
 //  * evict_kernel         -- coordinate-budget eviction (954-1067).
 #include <cfloat>
@@ -215,15 +215,19 @@ __global__ void __launch_bounds__(kScThreads) slash_score_dmma_kernel(CandSrc<T>
     for (int o = 4; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
     if (sub == 0) kk[a] = sq;
   }
-  double c00 = 0.0, c01 = 0.0, c10 = 0.0, c11 = 0.0;  // tiles nt0, nt0 + 1
+  // tiles nt0, nt0 + 1, each as two chains over alternate k-steps (n % 8 == 0)
+  double c00 = 0.0, c01 = 0.0, c10 = 0.0, c11 = 0.0, e00 = 0.0, e01 = 0.0, e10 = 0.0, e11 = 0.0;
   const float* xa = xs + (mt * 8 + grp) * ldx + tig;
   const float* ub = us + tig * ldu + nt0 * 8 + grp;
-#pragma unroll 4
-  for (int k0 = 0; k0 < n; k0 += 4) {
-    const double av = xa[k0];
+#pragma unroll 2
+  for (int k0 = 0; k0 < n; k0 += 8) {
+    const double av = xa[k0], bv = xa[k0 + 4];
     dmma_8x8x4(c00, c01, av, (double)ub[k0 * ldu]);
     dmma_8x8x4(c10, c11, av, (double)ub[k0 * ldu + 8]);
+    dmma_8x8x4(e00, e01, bv, (double)ub[(k0 + 4) * ldu]);
+    dmma_8x8x4(e10, e11, bv, (double)ub[(k0 + 4) * ldu + 8]);
   }
+  c00 += e00; c01 += e01; c10 += e10; c11 += e11;
   // |c|^2 of each candidate row: the lane's four values, the row's four lanes, two warps
   double cc = c00 * c00 + c01 * c01 + c10 * c10 + c11 * c11;
   cc += __shfl_xor_sync(0xffffffffu, cc, 1);
@@ -245,13 +249,34 @@ __global__ void __launch_bounds__(kScThreads) slash_score_dmma_kernel(CandSrc<T>
   }
 }
 
+// The 16/sizeof(T) elements of one 16-byte chunk, widened to fp32 (dst 16-byte aligned).
+template <typename T> __device__ __forceinline__ void widen16(uint4 r, float* dst);
+template <> __device__ __forceinline__ void widen16<float>(uint4 r, float* dst) {
+  *reinterpret_cast<float4*>(dst) =
+      make_float4(__uint_as_float(r.x), __uint_as_float(r.y), __uint_as_float(r.z), __uint_as_float(r.w));
+}
+template <> __device__ __forceinline__ void widen16<__nv_bfloat16>(uint4 r, float* dst) {
+  const unsigned w[4] = {r.x, r.y, r.z, r.w};
+  float v[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {  // bf16 -> fp32 is the 16 bits shifted up
+    v[2 * i] = __uint_as_float(w[i] << 16);
+    v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+  *reinterpret_cast<float4*>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+  *reinterpret_cast<float4*>(dst + 4) = make_float4(v[4], v[5], v[6], v[7]);
+}
+
 // Ranking half of the tier update, one CTA per problem: span boost, stable
 // descending rank, and the slot order [kept sources (chronological) |
 // demoted sources (chronological)] written to out.order; positions and
-// graduation surprise go straight to their buffers.  The rows move in
-// slash_move_kernel, spread over the whole GPU.
+// graduation surprise go straight to their buffers, and the demoted rows --
+// all the BUG step needs -- are gathered here (one warp per row: key
+// un-rotated into the fp32 block with cos/sin once per frequency, value
+// widened).  The kept rows move in slash_keep_kernel, off the critical path.
 template <typename T>
-__global__ void __launch_bounds__(512) slash_rank_kernel(CandSrc<T> src, int m, int keep_n,
+__global__ void __launch_bounds__(512) slash_rank_kernel(CandSrc<T> src, int m, int keep_n, int H,
+                                                         int D, RopeArgs rope,
                                                          const float* scores, long sc_sp,
                                                          int hh_neighbor, SelectOut out) {
   extern __shared__ __align__(16) float sel_sm[];
@@ -260,6 +285,7 @@ __global__ void __launch_bounds__(512) slash_rank_kernel(CandSrc<T> src, int m, 
   float* raw = sel_sm;            // [m]
   float* sel = raw + m;           // [m]
   int* pos = reinterpret_cast<int*>(sel + m);  // [m]
+  int* ords = pos + m;                         // [m] the slot order, shared copy
   int* order = out.order + p * out.order_sp;
   for (int i = threadIdx.x; i < m; i += blockDim.x) {
     raw[i] = scores[p * sc_sp + i];
@@ -299,10 +325,12 @@ __global__ void __launch_bounds__(512) slash_rank_kernel(CandSrc<T> src, int m, 
       if (kept) {
         const int slot = kbase + pre;
         order[slot] = i;
+        ords[slot] = i;
         out.hh_pos[p * out.hh_pos_sp + slot] = pos[i];
       } else {
         const int slot = dbase + (i - i0 - pre);
         order[keep_n + slot] = i;
+        ords[keep_n + slot] = i;
         out.mid_pos[p * out.mid_sp + out.w_off + slot] = pos[i];
         if (out.mid_surprise) out.mid_surprise[p * out.mid_sp + out.w_off + slot] = raw[i];
       }
@@ -311,63 +339,90 @@ __global__ void __launch_bounds__(512) slash_rank_kernel(CandSrc<T> src, int m, 
     dbase += min((int)blockDim.x, m - i0) - tot;
   }
   if (threadIdx.x == 0 && out.dem_count) out.dem_count[p] = d;
+  __syncthreads();
+  // loads are batched ahead of the stores (which the compiler cannot move
+  // past: the rows and the block could alias as far as it knows)
+  const int lane = threadIdx.x % 32, n = H * D, half = D / 2;
+  constexpr int kHB = 8;               // heads per batch of key loads
+  constexpr int kPer = 16 / sizeof(T);  // elements per 16-byte chunk
+  for (int ds = threadIdx.x / 32; ds < d; ds += blockDim.x / 32) {
+    const int jsrc = ords[keep_n + ds];
+    const T* kss = src.krow(p, jsrc);
+    const T* vss = src.vrow(p, jsrc);
+    float* xk = out.xk + p * out.x_sp + (long)ds * n;
+    float* xv = out.xv + p * out.x_sp + (long)ds * n;
+    const int ps = pos[jsrc];
+    for (int f = lane; f < half; f += 32) {
+      float c, sn;
+      rope_cs(ps, rope.inv_freq[f], rope.scale, &c, &sn);
+      for (int h0 = 0; h0 < H; h0 += kHB) {
+        float x1[kHB], x2[kHB];
+#pragma unroll
+        for (int hh = 0; hh < kHB; ++hh)
+          if (h0 + hh < H) {
+            x1[hh] = load_f<T>(kss + (h0 + hh) * D + f);
+            x2[hh] = load_f<T>(kss + (h0 + hh) * D + f + half);
+          }
+#pragma unroll
+        for (int hh = 0; hh < kHB; ++hh)
+          if (h0 + hh < H) {
+            xk[(h0 + hh) * D + f] = (x1[hh] * c + x2[hh] * sn) / rope.scale_sq;
+            xk[(h0 + hh) * D + f + half] = (x2[hh] * c - x1[hh] * sn) / rope.scale_sq;
+          }
+      }
+    }
+    const bool vec = (n % (32 * kPer)) == 0 && ((reinterpret_cast<uintptr_t>(vss) |
+                                                 reinterpret_cast<uintptr_t>(xv)) & 15) == 0;
+    if (vec) {  // 16-byte chunks, two per lane in flight
+      const int nch = n / kPer;
+      for (int e0 = lane; e0 < nch; e0 += 64) {
+        uint4 r0 = make_uint4(0, 0, 0, 0), r1 = r0;
+        const bool two = e0 + 32 < nch;
+        r0 = reinterpret_cast<const uint4*>(vss)[e0];
+        if (two) r1 = reinterpret_cast<const uint4*>(vss)[e0 + 32];
+        widen16<T>(r0, xv + e0 * kPer);
+        if (two) widen16<T>(r1, xv + (e0 + 32) * kPer);
+      }
+    } else {
+      for (int i = lane; i < n; i += 32) xv[i] = load_f<T>(vss + i);
+    }
+  }
 }
 
-constexpr int kMoveWarps = 8;   // rows per CTA of slash_move_kernel (one warp each)
+constexpr int kMoveWarps = 8;   // rows per CTA of slash_keep_kernel (one warp each)
 
 // Row half of the tier update: slot s < keep_n copies candidate order[s]
-// verbatim into the new exact tier; slot keep_n + s un-rotates the demoted
-// candidate's key into the fp32 block (cos/sin once per frequency, reused
-// across heads) and widens its value.  Grid (ceil(m / 8), P), one warp per
+// verbatim into the new exact tier.  Grid (ceil(keep_n / 8), P), one warp per
 // slot, 16-byte copies.
 template <typename T>
-__global__ void __launch_bounds__(32 * kMoveWarps) slash_move_kernel(CandSrc<T> src, int m,
-                                                                     int keep_n, int H, int D,
-                                                                     RopeArgs rope, SelectOut out) {
+__global__ void __launch_bounds__(32 * kMoveWarps) slash_keep_kernel(CandSrc<T> src, int keep_n,
+                                                                     int n, SelectOut out) {
   const int p = blockIdx.y;
   const int lane = threadIdx.x % 32;
   const int slot = blockIdx.x * kMoveWarps + threadIdx.x / 32;
-  if (slot >= m) return;
-  const int n = H * D, half = D / 2;
+  if (slot >= keep_n) return;
   const int jsrc = out.order[p * out.order_sp + slot];
   const T* kss = src.krow(p, jsrc);
   const T* vss = src.vrow(p, jsrc);
-  if (slot < keep_n) {
-    T* ok = reinterpret_cast<T*>(out.hh_k) + p * out.hh_sp + (long)slot * n;
-    T* ov = reinterpret_cast<T*>(out.hh_v) + p * out.hh_sp + (long)slot * n;
-    const bool aligned = ((reinterpret_cast<uintptr_t>(kss) | reinterpret_cast<uintptr_t>(vss) |
-                           reinterpret_cast<uintptr_t>(ok) | reinterpret_cast<uintptr_t>(ov)) &
-                          15) == 0;
-    const int vec = aligned ? (int)((n * sizeof(T)) / 16) : 0;
-    const uint4* ks = reinterpret_cast<const uint4*>(kss);
-    const uint4* vs = reinterpret_cast<const uint4*>(vss);
-    uint4* kd = reinterpret_cast<uint4*>(ok);
-    uint4* vd = reinterpret_cast<uint4*>(ov);
-    for (int e = lane; e < vec; e += 32) {
-      const uint4 a = ks[e], b = vs[e];
-      kd[e] = a;
-      vd[e] = b;
-    }
-    for (int i = vec * (int)(16 / sizeof(T)) + lane; i < n; i += 32) {
-      ok[i] = kss[i];
-      ov[i] = vss[i];
-    }
-    return;
+  T* ok = reinterpret_cast<T*>(out.hh_k) + p * out.hh_sp + (long)slot * n;
+  T* ov = reinterpret_cast<T*>(out.hh_v) + p * out.hh_sp + (long)slot * n;
+  const bool aligned = ((reinterpret_cast<uintptr_t>(kss) | reinterpret_cast<uintptr_t>(vss) |
+                         reinterpret_cast<uintptr_t>(ok) | reinterpret_cast<uintptr_t>(ov)) &
+                        15) == 0;
+  const int vec = aligned ? (int)((n * sizeof(T)) / 16) : 0;
+  const uint4* ks = reinterpret_cast<const uint4*>(kss);
+  const uint4* vs = reinterpret_cast<const uint4*>(vss);
+  uint4* kd = reinterpret_cast<uint4*>(ok);
+  uint4* vd = reinterpret_cast<uint4*>(ov);
+  for (int e = lane; e < vec; e += 32) {
+    const uint4 a = ks[e], b = vs[e];
+    kd[e] = a;
+    vd[e] = b;
   }
-  const int ds = slot - keep_n;
-  float* xk = out.xk + p * out.x_sp + (long)ds * n;
-  float* xv = out.xv + p * out.x_sp + (long)ds * n;
-  const int ps = src.pos(p, jsrc);
-  for (int f = lane; f < half; f += 32) {
-    float c, s;
-    rope_cs(ps, rope.inv_freq[f], rope.scale, &c, &s);
-    for (int h = 0; h < H; ++h) {
-      const float x1 = load_f<T>(kss + h * D + f), x2 = load_f<T>(kss + h * D + f + half);
-      xk[h * D + f] = (x1 * c + x2 * s) / rope.scale_sq;
-      xk[h * D + f + half] = (x2 * c - x1 * s) / rope.scale_sq;
-    }
+  for (int i = vec * (int)(16 / sizeof(T)) + lane; i < n; i += 32) {
+    ok[i] = kss[i];
+    ov[i] = vss[i];
   }
-  for (int i = lane; i < n; i += 32) xv[i] = load_f<T>(vss + i);
 }
 
 // No-tier absorb: rows [0, b) of `g_k`/`g_v` graduate at positions start + j.
@@ -561,19 +616,26 @@ int launch_slash_select(const CandSrc<T>& src, int P, int m, int keep_n, int H, 
     set_error("slash select: order stride %ld < pool %d", out.order_sp, m);
     return KVD_ERR_ARG;
   }
-  const int smem = 4 * 3 * m;
+  const int smem = 4 * 4 * m;
   if (int rc = ensure_smem((const void*)slash_rank_kernel<T>, smem, "slash_rank_kernel")) return rc;
   {
     KTimerScope kts_("slash_rank_kernel", stream);
-    slash_rank_kernel<T><<<P, 512, smem, stream>>>(src, m, keep_n, scores, sc_sp, hh_neighbor, out);
+    slash_rank_kernel<T><<<P, 512, smem, stream>>>(src, m, keep_n, H, D, rope, scores, sc_sp,
+                                                   hh_neighbor, out);
   }
-  if (int rc = check_launch("slash_rank_kernel")) return rc;
+  return check_launch("slash_rank_kernel");
+}
+
+template <typename T>
+int launch_slash_keep(const CandSrc<T>& src, int P, int keep_n, int n, const SelectOut& out,
+                      cudaStream_t stream) {
+  if (keep_n <= 0) return KVD_OK;
   {
-    KTimerScope kts_("slash_move_kernel", stream);
-    dim3 grid((m + kMoveWarps - 1) / kMoveWarps, P);
-    slash_move_kernel<T><<<grid, 32 * kMoveWarps, 0, stream>>>(src, m, keep_n, H, D, rope, out);
+    KTimerScope kts_("slash_keep_kernel", stream);
+    dim3 grid((keep_n + kMoveWarps - 1) / kMoveWarps, P);
+    slash_keep_kernel<T><<<grid, 32 * kMoveWarps, 0, stream>>>(src, keep_n, n, out);
   }
-  return check_launch("slash_move_kernel");
+  return check_launch("slash_keep_kernel");
 }
 
 template <typename T>
@@ -621,6 +683,8 @@ int launch_evict(int P, int W, int f_over, int retention, float* c_k, float* c_v
                                      cudaStream_t);                                              \
   template int launch_slash_select<T>(const CandSrc<T>&, int, int, int, int, int, RopeArgs,      \
                                       const float*, long, int, const SelectOut&, cudaStream_t);  \
+  template int launch_slash_keep<T>(const CandSrc<T>&, int, int, int, const SelectOut&,          \
+                                    cudaStream_t);                                               \
   template int launch_gather_block<T>(const T*, const T*, long, int, int, int, int, int,         \
                                       RopeArgs, float*, float*, long, int*, long, int,           \
                                       cudaStream_t);
