@@ -243,6 +243,184 @@ static __device__ __forceinline__ int cta_hestenes(float* X, int len, int voff, 
   return sweep;
 }
 
+// Warp w's k slice [w n/8, (w+1) n/8) of the fp64 Gram R^T R of the b <= 16
+// columns of R (pitch n, n % 32 == 0) as 2 x 2 tiles of m8n8k4 products; the
+// A (= R^T) and B (= R) fragments of a k-step are the same two values per
+// lane.  Writes gpart[(w * 4 + tile) * 64 + row * 8 + col].
+static __device__ __forceinline__ void warp_gram16_slice(const float* Rm, int n, int b, int w,
+                                                      double* gpart) {
+  const int lane = threadIdx.x & 31, grp = lane >> 2, tig = lane & 3;
+  double c00 = 0.0, c01 = 0.0, c10 = 0.0, c11 = 0.0, c20 = 0.0, c21 = 0.0, c30 = 0.0, c31 = 0.0;
+  const int kw = n / 8, k_begin = w * kw;
+  const float* r0 = Rm + (long)grp * n + tig;
+  const float* r1 = Rm + (long)(8 + grp) * n + tig;
+  const bool h0 = grp < b, h1 = 8 + grp < b;
+#pragma unroll 4
+  for (int k0 = k_begin; k0 < k_begin + kw; k0 += 4) {
+    const double x0 = h0 ? (double)r0[k0] : 0.0, x1 = h1 ? (double)r1[k0] : 0.0;
+    dmma_8x8x4(c00, c01, x0, x0);
+    dmma_8x8x4(c10, c11, x0, x1);
+    dmma_8x8x4(c20, c21, x1, x0);
+    dmma_8x8x4(c30, c31, x1, x1);
+  }
+  double* o = gpart + (long)w * 256 + grp * 8 + 2 * tig;
+  o[0] = c00; o[1] = c01;
+  o[64] = c10; o[65] = c11;
+  o[128] = c20; o[129] = c21;
+  o[192] = c30; o[193] = c31;
+}
+
+// Right-looking Cholesky of the b x b (b <= 16) fp64 Gram G (pitch ldg) by
+// one warp in registers: lane j holds column j; each step broadcasts the
+// pivot column by shuffles (a pivot at or below 1e-14 of the trace is taken
+// as null: its column of the factor is zero).  Writes T = L^T into the
+// columns of Tm (column c, rows k <= c; zero below).  Call from warp 0 only.
+static __device__ __noinline__ void warp_cholesky16(const double* G, int ldg, int b, float* Tm,
+                                                    int ldr) {
+  constexpr unsigned kAll = 0xffffffffu;
+  const int lane = threadIdx.x & 31;
+  double a[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) a[i] = (lane < b && i < b) ? G[i * ldg + lane] : 0.0;
+  const double trace = warp_sum(lane < b ? G[lane * ldg + lane] : 0.0);
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    if (j < b) {  // (no early exit: the loop must unroll for a[] to stay in registers)
+    const double piv = __shfl_sync(kAll, a[j], j);
+    const double t = piv > 1e-14 * trace ? sqrt(piv) : 0.0;
+    const double rt = t > 0.0 ? 1.0 / t : 0.0;
+    if (lane == j) {
+#pragma unroll
+      for (int i = j + 1; i < 16; ++i) a[i] *= rt;
+      a[j] = t;
+    }
+    double l[16];
+    double lk = 0.0;  // l[lane]: this lane's entry of the pivot column
+#pragma unroll
+    for (int i = j + 1; i < 16; ++i) {
+      l[i] = __shfl_sync(kAll, a[i], j);
+      if (i == lane) lk = l[i];
+    }
+    if (lane > j) {
+#pragma unroll
+      for (int i = j + 1; i < 16; ++i) a[i] = fma(-l[i], lk, a[i]);
+    }
+    }
+  }
+  if (lane < b) {  // lane k holds column k of L: T[k][c] = L[c][k] for c >= k
+#pragma unroll
+    for (int c = 0; c < 16; ++c)
+      if (c < b) Tm[c * ldr + lane] = c >= lane ? (float)a[c] : 0.f;
+  }
+  __syncwarp();
+}
+
+// One-sided Jacobi for up to 16 columns of at most 32 augmented rows (data
+// rows [0, len), zero to voff, rotations accumulated in rows [voff,
+// voff + cols)), run by one warp entirely in registers.  Slot i (lanes
+// 4i .. 4i+3) holds the pair (top, bottom); lane 4i + g holds rows g + 4k of
+// both.  Rounds follow the circle method (position 0 fixed, the others
+// advancing one position per round, so np - 1 rounds meet every pair), the
+// columns moving between slots by warp shuffles instead of through shared
+// memory.  Rotation, tolerance, null floor and early stop are cta_hestenes's.
+// Call from warp 0 only; writes the columns back to X and returns the sweeps.
+static __device__ __noinline__ int warp_hestenes16(float* X, int len, int voff, int cols, int ldx,
+                                                   float tol, int max_sweeps, double inv_scale2) {
+  constexpr unsigned kAll = 0xffffffffu;
+  const int lane = threadIdx.x & 31, g = lane & 3, slot = lane >> 2;
+  if (cols <= 1) {  // nothing to rotate: the identity below the data
+    for (int c = 0; c < cols; ++c)
+      for (int row = len + lane; row < voff + cols; row += 32)
+        X[(long)c * ldx + row] = (row - voff == c) ? 1.f : 0.f;
+    __syncwarp();
+    return 0;
+  }
+  const int np = cols + (cols & 1), half = np / 2;
+  int ti = slot < half ? slot : np, bi = slot < half ? np - 1 - slot : np;  // column indices
+  float tp[8], bt[8];
+  auto value = [&](int c, int row) -> float {
+    if (c >= cols) return 0.f;
+    if (row < len) return X[(long)c * ldx + row];
+    return (row - voff == c) ? 1.f : 0.f;
+  };
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    tp[k] = value(ti, g + 4 * k);
+    bt[k] = value(bi, g + 4 * k);
+  }
+  __syncwarp();
+  const float tol2 = tol * tol, is2 = (float)inv_scale2;
+  int sweep = 0;
+  for (; sweep < max_sweeps; ++sweep) {
+    bool big = false;
+    for (int rd = 0; rd < np - 1; ++rd) {
+      float al = 0.f, be = 0.f, ga = 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k)
+        if (g + 4 * k < voff) {
+          al = fmaf(tp[k], tp[k], al);
+          be = fmaf(bt[k], bt[k], be);
+          ga = fmaf(tp[k], bt[k], ga);
+        }
+      al += __shfl_xor_sync(kAll, al, 1); be += __shfl_xor_sync(kAll, be, 1); ga += __shfl_xor_sync(kAll, ga, 1);
+      al += __shfl_xor_sync(kAll, al, 2); be += __shfl_xor_sync(kAll, be, 2); ga += __shfl_xor_sync(kAll, ga, 2);
+      al *= is2;
+      be *= is2;
+      ga *= is2;
+      const bool live = slot < half && al > kJacobiFloor && be > kJacobiFloor;
+      if (live && ga * ga > tol2 * al * be) {
+        const float d = be - al, g2 = 2.f * ga;
+        const float rr = fmaf(d, d, g2 * g2);
+        const float hyp = rr * rsqrtf(rr);
+        const float t = copysignf(1.f, d) * g2 * __fdividef(1.f, fabsf(d) + hyp);
+        float c = rsqrtf(fmaf(t, t, 1.f)), sn = c * t;
+        const float f = fmaf(-0.5f, fmaf(c, c, sn * sn), 1.5f);  // Newton step to unit norm
+        c *= f;
+        sn *= f;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const float a = tp[k], bq = bt[k];
+          tp[k] = c * a - sn * bq;
+          bt[k] = sn * a + c * bq;
+        }
+        big = big || ga * ga > kJacobiQuadStop * kJacobiQuadStop * al * be;
+      }
+      // advance: top of slot i <- top of i-1 (slot 1 <- bottom of 0, slot 0 fixed);
+      // bottom of slot i <- bottom of i+1 (the last slot's bottom <- its own top)
+      const bool first = slot == 0, second = slot == 1, last = slot == half - 1;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float t_prev = __shfl_up_sync(kAll, tp[k], 4);
+        const float b_prev = __shfl_up_sync(kAll, bt[k], 4);
+        const float b_next = __shfl_down_sync(kAll, bt[k], 4);
+        const float nt = first ? tp[k] : (second ? b_prev : t_prev);
+        bt[k] = last ? tp[k] : b_next;
+        tp[k] = nt;
+      }
+      {
+        const int t_prev = __shfl_up_sync(kAll, ti, 4), b_prev = __shfl_up_sync(kAll, bi, 4);
+        const int b_next = __shfl_down_sync(kAll, bi, 4);
+        const int nt = first ? ti : (second ? b_prev : t_prev);
+        bi = last ? ti : b_next;
+        ti = nt;
+      }
+    }
+    if (!__any_sync(kAll, big)) break;
+  }
+  if (slot < half) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int row = g + 4 * k;
+      if (row < voff + cols) {
+        if (ti < cols) X[(long)ti * ldx + row] = tp[k];
+        if (bi < cols) X[(long)bi * ldx + row] = bt[k];
+      }
+    }
+  }
+  __syncwarp();
+  return sweep;
+}
+
 // Dispatch to the register tile jacobi_tile picks (groups of at most `gcap`
 // lanes) when X is 16-byte aligned and the pitch covers it, else stream.
 // accum = false: no rotations are accumulated (rows [len, voff) are padding).
@@ -722,7 +900,7 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
   const int voff = chol ? ((b + 3) & ~3) : (rlen + 3) & ~3;
   const int ldr = chol ? jacobi_pitch(voff + b, b, false) : jacobi_pitch(voff + nsv, nsv, true);
   const int ldr0 = (tr || chol) ? n : ldr;  // pitch the residual is formed with
-  float* Tm = chol ? part + 2 * (b * (b + 1) + 8) : Rm;  // the factor, augmented columns
+  float* Tm = chol ? part + 2 * (16 * 17 + 8) : Rm;  // the factor, augmented columns (after the Gram)
   // ----- residual R = (I - U U^T)^2 X (the reference's re-orthogonalised residual)
   if (r > 0) cta_tn(r, b, n, Uc, lda, XR, ldb, true, AS, b16, 0.f, part);  // a = U^T X
   cta_rows_sub(n, b, b16, r, Uc, lda, AS, b16, XR, ldb, Rm, ldr0, true, r > 0);  // R = X - U a
@@ -735,45 +913,35 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
   // ----- SVD of R
   const double inv_x2 = s_xnorm2 > 0.0 ? 1.0 / s_xnorm2 : 1.0;
   if (chol) {
-    double* GR = reinterpret_cast<double*>(part);  // [b][b+1], T overwrites its upper triangle
-    const int ldg = b + 1;
-    for (int pp = warp; pp < b * b; pp += nthr / 32) {  // fp64 Gram, one warp per pair
-      const int pi = pp / b, qi = pp % b;
-      if (pi > qi) continue;
-      const float* xp = Rm + (long)pi * n;
-      const float* xq = Rm + (long)qi * n;
-      double acc = 0.0;
-      for (int e = lane; e < n; e += 32) acc = fma((double)xp[e], (double)xq[e], acc);
-      acc = warp_sum(acc);
-      if (lane == 0) { GR[pi * ldg + qi] = acc; GR[qi * ldg + pi] = acc; }
+    constexpr int ldg = 17;
+    double* GR = reinterpret_cast<double*>(part);  // [16][17] the Gram
+    if (n % 32 == 0) {
+      // fp64 tensor products, G = R^T R as 2 x 2 tiles of 8 x 8 with the
+      // k range split over 8 warps; the A (= R^T) and B (= R) fragments of
+      // a k-step are the same two values per lane
+      double* gpart = reinterpret_cast<double*>(part + 4096);  // [8 warps][4 tiles][64]
+      if (warp < 8) warp_gram16_slice(Rm, n, b, warp, gpart);
+      __syncthreads();
+      for (int e = tid; e < 256; e += nthr) {  // sum the k slices
+        const int i = e / 16, j = e % 16, t = (i / 8) * 2 + j / 8, w = (i % 8) * 8 + j % 8;
+        double sum = 0.0;
+        for (int wv = 0; wv < 8; ++wv) sum += gpart[(wv * 4 + t) * 64 + w];
+        GR[i * ldg + j] = sum;
+      }
+    } else {
+      for (int pp = warp; pp < b * b; pp += nthr / 32) {  // fp64 Gram, one warp per pair
+        const int pi = pp / b, qi = pp % b;
+        if (pi > qi) continue;
+        const float* xp = Rm + (long)pi * n;
+        const float* xq = Rm + (long)qi * n;
+        double acc = 0.0;
+        for (int e = lane; e < n; e += 32) acc = fma((double)xp[e], (double)xq[e], acc);
+        acc = warp_sum(acc);
+        if (lane == 0) { GR[pi * ldg + qi] = acc; GR[qi * ldg + pi] = acc; }
+      }
     }
     __syncthreads();
-    if (warp == 0) {  // right-looking Cholesky of the b x b Gram in one warp
-      double trace = 0.0;
-      for (int j = lane; j < b; j += 32) trace += GR[j * ldg + j];
-      trace = warp_sum(trace);
-      for (int j = 0; j < b; ++j) {
-        const double piv = GR[j * ldg + j];
-        const double t = piv > 1e-14 * trace ? sqrt(piv) : 0.0;
-        __syncwarp();
-        for (int i = j + 1 + lane; i < b; i += 32) GR[j * ldg + i] = t > 0.0 ? GR[j * ldg + i] / t : 0.0;
-        if (lane == 0) GR[j * ldg + j] = t;
-        __syncwarp();
-        for (int e = lane; e < b * b; e += 32) {
-          const int i = e / b, l = e % b;
-          if (i > j && l >= i) {
-            const double v = GR[i * ldg + l] - GR[j * ldg + i] * GR[j * ldg + l];
-            GR[i * ldg + l] = v;
-            GR[l * ldg + i] = v;
-          }
-        }
-        __syncwarp();
-      }
-      for (int e = lane; e < b * b; e += 32) {  // column c of T: rows k <= c
-        const int c = e / b, k = e % b;
-        Tm[c * ldr + k] = k <= c ? (float)GR[k * ldg + c] : 0.f;
-      }
-    }
+    if (warp == 0) warp_cholesky16(GR, ldg, b, Tm, ldr);
     __syncthreads();
   } else if (tr) {
     for (long e = tid; e < (long)b * n; e += nthr) XR[e] = Rm[e];
@@ -786,8 +954,18 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
   }
   int sw;
   if (chol) {
-    sw = cta_hestenes_any<float>(Tm, b, voff, b, ldr, 1.2e-7f * sqrtf((float)b) + 2.4e-7f, 30,
-                                 inv_x2);
+    if (voff + b <= 32) {  // the whole factor fits one warp's registers
+      if (warp == 0) {
+        const int w = warp_hestenes16(Tm, b, voff, b, ldr, 1.2e-7f * sqrtf((float)b) + 2.4e-7f, 30,
+                                      inv_x2);
+        if (lane == 0) s_m = w;
+      }
+      __syncthreads();
+      sw = s_m;
+    } else {
+      sw = cta_hestenes_any<float>(Tm, b, voff, b, ldr, 1.2e-7f * sqrtf((float)b) + 2.4e-7f, 30,
+                                   inv_x2);
+    }
     __syncthreads();
     cta_colnorm_order(Tm, b, b, ldr, sv, ordh);
   } else {

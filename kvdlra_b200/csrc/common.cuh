@@ -124,6 +124,14 @@ KVD_DEVICE void mma_f32(float (&d)[4], const float (&a)[4], float b0, float b1) 
   }
 }
 
+// One warp-level fp64 m8n8k4 product, d += a b (row-major A, column-major B;
+// g = lane / 4, t = lane % 4): a = A[g][t], b = B[t][g], d0/d1 = D[g][2t], D[g][2t + 1].
+KVD_DEVICE void dmma_8x8x4(double& d0, double& d1, double a, double b) {
+  asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0, %1}, {%2}, {%3}, {%0, %1};\n"
+               : "+d"(d0), "+d"(d1)
+               : "d"(a), "d"(b));
+}
+
 // Inverse rotation of one rotate-half pair (x1 = x[j], x2 = x[j + D/2]):
 // (x cos - rotate_half(x) sin) / scale^2 with rotate_half(x) = [-x2, x1].
 KVD_DEVICE void rope_unapply_pair(float x1, float x2, float c, float s, float inv_scale_sq,

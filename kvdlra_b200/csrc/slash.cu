@@ -119,11 +119,6 @@ __global__ void __launch_bounds__(256) slash_score_kernel(CandSrc<T> src, int m,
 constexpr int kScT = 32;
 constexpr int kScThreads = 2 * kScT * 4;  // (kScT / 8) candidate tiles x 2 coordinate-tile pairs
 
-__device__ __forceinline__ void dmma_8x8x4(double& d0, double& d1, double a, double b) {
-  asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0, %1}, {%2}, {%3}, {%0, %1};\n"
-               : "+d"(d0), "+d"(d1)
-               : "d"(a), "d"(b));
-}
 
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
   const unsigned sa = (unsigned)__cvta_generic_to_shared(smem_dst);
