@@ -386,8 +386,10 @@ static __device__ __noinline__ int warp_hestenes16(float* X, int len, int voff, 
         big = big || ga * ga > kJacobiQuadStop * kJacobiQuadStop * al * be;
       }
       // advance: top of slot i <- top of i-1 (slot 1 <- bottom of 0, slot 0 fixed);
-      // bottom of slot i <- bottom of i+1 (the last slot's bottom <- its own top)
+      // bottom of slot i <- bottom of i+1 (the last slot's bottom <- its own top);
+      // a single pair never moves
       const bool first = slot == 0, second = slot == 1, last = slot == half - 1;
+      if (half > 1) {
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         const float t_prev = __shfl_up_sync(kAll, tp[k], 4);
@@ -403,6 +405,7 @@ static __device__ __noinline__ int warp_hestenes16(float* X, int len, int voff, 
         const int nt = first ? ti : (second ? b_prev : t_prev);
         bi = last ? ti : b_next;
         ti = nt;
+      }
       }
     }
     if (!__any_sync(kAll, big)) break;

@@ -128,3 +128,30 @@ def test_long_stream_stays_orthonormal(rank: int) -> None:
     uo = oracle_blocked(data[:, :1600], rank, 16)
     u_short = blocked_bug_subspace(torch.from_numpy(data[:, :1600]).to(DEV), rank, 16).cpu().numpy()
     assert principal_angle(u_short, uo) < 1e-3
+
+
+@pytest.mark.parametrize("blocks,cap", [([1, 2, 1, 3, 2, 5, 1], 4), ([2, 2, 2, 2], 3), ([3, 1, 2, 7, 16, 2], 9)])
+def test_tiny_and_odd_blocks_match_oracle(blocks: list[int], cap: int) -> None:
+    """Blocks of 1, 2 and odd sizes drive the one-sided Jacobi with one pair,
+    a dummy column and odd column counts (residual factor and core): every
+    step's singular values and subspace match the oracle's."""
+    rng = np.random.default_rng(sum(blocks) + cap)
+    n = 40
+    basis = np.linalg.qr(rng.standard_normal((n, 6)))[0]
+    total = sum(blocks)
+    data = (basis @ (rng.standard_normal((6, total)) * (2.0 ** -np.arange(6))[:, None])
+            + 1e-2 * rng.standard_normal((n, total))).astype(np.float32)
+    u = b = None
+    uo = bo = None
+    start = 0
+    for bs in blocks:
+        blk = data[:, start:start + bs]
+        u, b, _ = augmented_bug_step(u, b, torch.from_numpy(blk).to(DEV), cap)
+        uo, bo, _, _ = oracle_step(uo, bo, blk, cap)
+        sig = torch.diagonal(b).cpu().numpy()
+        assert sig.shape[0] == bo.shape[0]
+        assert np.allclose(sig, np.diag(bo), rtol=1e-4, atol=1e-6 * np.diag(bo).max())
+        assert principal_angle(u.cpu().numpy(), uo) < 1e-3
+        un = u.cpu().double().numpy()
+        assert np.abs(un.T @ un - np.eye(un.shape[1])).max() < 1e-5
+        start += bs
