@@ -30,7 +30,8 @@ __host__ __device__ inline long align16(long x) { return (x + 15) & ~15L; }
 
 constexpr int kStepThreads = 512;
 constexpr int kStepMiscBytes = 1024;   // fp64 reduction scratch
-constexpr int kPartFloats = 8192;      // K-split partials: 16 warps x 32 lanes x 16
+constexpr int kPartFloats = 8192;
+constexpr int kMaxGramB = 128;  // widest block the Gram + Cholesky residual SVD takes      // K-split partials: 16 warps x 32 lanes x 16
 
 // One-sided (Hestenes) Jacobi on augmented columns.  Column c of X (at
 // X + c*ldx) holds the data in rows [0, len), zeros in [len, voff) and, from
@@ -99,6 +100,7 @@ __host__ __device__ inline void jacobi_tile(int nut, int cols, bool dbl, int* G,
   int g0 = gcap;
   while (g0 > 4 && half * g0 > 256) g0 >>= 1;
   while (g0 < 32 && g0 * 9 < nut) g0 <<= 1;
+  if (dbl && g0 < 16) g0 = 16;  // fp64 tiles are instantiated for groups of 16 and 32
   // the widest instantiated group up to g0 whose tile is not padded far past
   // the column (small problems would waste shared memory), else the least
   // padded instantiated one, else streaming
@@ -124,13 +126,14 @@ __host__ __device__ inline int jacobi_pitch(int rows, int cols, bool dbl, int gc
 template <int G, int NU, typename ACC>
 static __device__ __forceinline__ int cta_hestenes(float* X, int len, int voff, int cols, int ldx,
                                                    float tol, int max_sweeps, double inv_scale2,
-                                                   bool accum) {
+                                                   bool accum, bool seeded) {
   const int tid = threadIdx.x, nthr = blockDim.x, warp = tid / 32, lane = tid % 32;
   const int gid = tid / G, gl = tid % G;
   const int vend = voff + (accum ? ((cols + 3) & ~3) : 0);
   const int rows = NU > 0 ? 4 * G * NU : vend;  // rows the tile touches; [len, rows) zeroed
   for (long e = tid; e < (long)cols * (rows - len); e += nthr) {
     const int c = (int)(e / (rows - len)), k = len + (int)(e % (rows - len));
+    if (seeded && k >= voff && k < voff + cols) continue;  // the caller's starting rotations
     X[(long)c * ldx + k] = (accum && k - voff == c) ? 1.f : 0.f;
   }
   __syncthreads();
@@ -426,12 +429,13 @@ static __device__ __noinline__ int warp_hestenes16(float* X, int len, int voff, 
 
 // Dispatch to the register tile jacobi_tile picks (groups of at most `gcap`
 // lanes) when X is 16-byte aligned and the pitch covers it, else stream.
-// accum = false: no rotations are accumulated (rows [len, voff) are padding).
+// accum = false: no rotations are accumulated (rows [len, voff) are padding);
+// seeded = true: rows [voff, voff + cols) already hold starting rotations.
 template <typename ACC>
 static __device__ __forceinline__ int cta_hestenes_any(float* X, int len, int voff, int cols,
                                                        int ldx, float tol, int max_sweeps,
                                                        double inv_scale2, bool accum = true,
-                                                       int gcap = 32) {
+                                                       int gcap = 32, bool seeded = false) {
   const int nut = (voff + (accum ? ((cols + 3) & ~3) : 0)) / 4;
   int G, NU;
   jacobi_tile(nut, cols, sizeof(ACC) == 8, &G, &NU, gcap);
@@ -440,7 +444,7 @@ static __device__ __forceinline__ int cta_hestenes_any(float* X, int len, int vo
   if (fits) {
 #define KVD_HJ(GG, UU)                                                                       \
     if (G == GG && NU == UU)                                                                 \
-      return cta_hestenes<GG, UU, ACC>(X, len, voff, cols, ldx, tol, max_sweeps, inv_scale2, accum);
+      return cta_hestenes<GG, UU, ACC>(X, len, voff, cols, ldx, tol, max_sweeps, inv_scale2, accum, seeded);
     if constexpr (sizeof(ACC) == 8) {
       KVD_HJ(16, 2) KVD_HJ(16, 3) KVD_HJ(16, 5) KVD_HJ(16, 9)
       KVD_HJ(32, 2) KVD_HJ(32, 3) KVD_HJ(32, 5) KVD_HJ(32, 9)
@@ -451,7 +455,7 @@ static __device__ __forceinline__ int cta_hestenes_any(float* X, int len, int vo
     }
 #undef KVD_HJ
   }
-  return cta_hestenes<32, 0, ACC>(X, len, voff, cols, ldx, tol, max_sweeps, inv_scale2, accum);
+  return cta_hestenes<32, 0, ACC>(X, len, voff, cols, ldx, tol, max_sweeps, inv_scale2, accum, seeded);
 }
 
 // 16 consecutive floats p[j0 .. j0+16) of a row, zero past `nb`; `vec` =
@@ -892,18 +896,28 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
   // b > n (more columns than rows cannot all be made orthogonal): on the n
   // columns of R^T, R^T J = [s_j v_j], so J holds the left vectors q_j.
   // The rotations accumulate below the data in each column (rows voff..).
-  // Blocks of up to 16 tokens (the absorb block): the fp64 Gram R^T R is
-  // factored T^T T (Cholesky, pivots below 1e-14 of the trace taken as null)
-  // and the one-sided Jacobi runs on T's b columns of length b -- T has R's
-  // singular values and right vectors, R V = Q1 U_T S -- in one warp.
+  // Blocks of up to 16 tokens (the absorb block): the fp64 Gram R^T R
+  // (tensor-core products) is factored T^T T (Cholesky, pivots below 1e-14
+  // of the trace taken as null) and the one-sided Jacobi runs on T's b
+  // columns of length b -- T has R's singular values and right vectors,
+  // R V = Q1 U_T S -- in one warp's registers.  17..kMaxGramB tokens (the
+  // pre-fill blocks): the same factorisation by the CTA, whose Jacobi (fp64
+  // sums) gives R's right vectors to within the factor's fp32 rounding; they
+  // seed the one-sided Jacobi on R V itself, whose columns are then nearly
+  // orthogonal, so it converges in about one sweep to the accuracy of the
+  // Jacobi on R (the factor alone loses relative accuracy in the smallest
+  // singular directions, and a noisy spectrum at the truncation amplifies it).
   const bool chol = b <= 16 && b <= n;
+  // 17..kMaxGramB columns: the Gram's Cholesky factor preconditions the Jacobi on R
+  const bool bigg = b > 16 && b <= kMaxGramB && b <= n;
   const bool tr = !chol && b > n;
   const int nsv = tr ? n : b;
   const int rlen = tr ? b : n;
   const int voff = chol ? ((b + 3) & ~3) : (rlen + 3) & ~3;
   const int ldr = chol ? jacobi_pitch(voff + b, b, false) : jacobi_pitch(voff + nsv, nsv, true);
-  const int ldr0 = (tr || chol) ? n : ldr;  // pitch the residual is formed with
+  const int ldr0 = (tr || chol || bigg) ? n : ldr;  // pitch the residual is formed with
   float* Tm = chol ? part + 2 * (16 * 17 + 8) : Rm;  // the factor, augmented columns (after the Gram)
+  const int voffT = (b + 3) & ~3, ldrT = jacobi_pitch(voffT + b, b, true);  // bigg: the factor's pitch
   // ----- residual R = (I - U U^T)^2 X (the reference's re-orthogonalised residual)
   if (r > 0) cta_tn(r, b, n, Uc, lda, XR, ldb, true, AS, b16, 0.f, part);  // a = U^T X
   cta_rows_sub(n, b, b16, r, Uc, lda, AS, b16, XR, ldb, Rm, ldr0, true, r > 0);  // R = X - U a
@@ -946,6 +960,90 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
     __syncthreads();
     if (warp == 0) warp_cholesky16(GR, ldg, b, Tm, ldr);
     __syncthreads();
+  } else if (bigg) {
+    // 17..128 columns: the same factorisation by the whole CTA
+    double* G = reinterpret_cast<double*>(region(kRgGram));  // [b][b+1]
+    const int ldgb = b + 1, nt = (b + 7) / 8, ntiles = nt * (nt + 1) / 2;
+    if (n % 4 == 0) {
+      // fp64 tensor products over the 8 x 8 tiles (ti <= tj) of the upper
+      // triangle, mirrored below; one tile per warp at a time
+      const int grp = lane >> 2, tig = lane & 3;
+      for (int t = warp; t < ntiles; t += nthr / 32) {
+        int ti = 0, rem = t;
+        while (rem >= nt - ti) { rem -= nt - ti; ++ti; }
+        const int tj = ti + rem;
+        const int ra = ti * 8 + grp, rb = tj * 8 + grp;
+        const float* pa = Rm + (long)(ra < b ? ra : 0) * n + tig;
+        const float* pb = Rm + (long)(rb < b ? rb : 0) * n + tig;
+        double c0 = 0.0, c1 = 0.0, e0 = 0.0, e1 = 0.0;
+#pragma unroll 2
+        for (int k0 = 0; k0 < n; k0 += 8) {  // two chains over alternate k-steps
+          const double a0 = ra < b ? (double)pa[k0] : 0.0, b0 = rb < b ? (double)pb[k0] : 0.0;
+          const bool more = k0 + 4 < n;
+          const double a1 = (ra < b && more) ? (double)pa[k0 + 4] : 0.0;
+          const double b1 = (rb < b && more) ? (double)pb[k0 + 4] : 0.0;
+          dmma_8x8x4(c0, c1, a0, b0);
+          dmma_8x8x4(e0, e1, a1, b1);
+        }
+        c0 += e0;
+        c1 += e1;
+        const int col = tj * 8 + 2 * tig;
+        const double cv[2] = {c0, c1};
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          if (ra < b && col + q < b) {
+            G[ra * ldgb + col + q] = cv[q];
+            if (ti != tj) G[(col + q) * ldgb + ra] = cv[q];
+          }
+        }
+      }
+    } else {
+      for (int pp = warp; pp < b * b; pp += nthr / 32) {  // fp64 Gram, one warp per pair
+        const int pi = pp / b, qi = pp % b;
+        if (pi > qi) continue;
+        const float* xp = Rm + (long)pi * n;
+        const float* xq = Rm + (long)qi * n;
+        double acc = 0.0;
+        for (int e = lane; e < n; e += 32) acc = fma((double)xp[e], (double)xq[e], acc);
+        acc = warp_sum(acc);
+        if (lane == 0) { G[pi * ldgb + qi] = acc; G[qi * ldgb + pi] = acc; }
+      }
+    }
+    __syncthreads();
+    if (warp == 0) {
+      double trc = 0.0;
+      for (int j = lane; j < b; j += 32) trc += G[j * ldgb + j];
+      trc = warp_sum(trc);
+      if (lane == 0) red[0] = trc;
+    }
+    __syncthreads();
+    const double trace = red[0];
+    // right-looking Cholesky on the lower triangle (pivots at or below 1e-14
+    // of the trace taken as null, as for the small blocks)
+    for (int j = 0; j < b; ++j) {
+      if (tid == 0) {
+        const double piv = G[j * ldgb + j];
+        const double t = piv > 1e-14 * trace ? sqrt(piv) : 0.0;
+        G[j * ldgb + j] = t;
+        red[1] = t > 0.0 ? 1.0 / t : 0.0;
+      }
+      __syncthreads();
+      const double rt = red[1];
+      for (int i = j + 1 + tid; i < b; i += nthr) G[i * ldgb + j] *= rt;
+      __syncthreads();
+      const int w = b - j - 1;
+      for (int e = tid; e < w * w; e += nthr) {
+        const int i = j + 1 + e / w, k = j + 1 + e % w;
+        if (k <= i) G[i * ldgb + k] = fma(-G[i * ldgb + j], G[k * ldgb + j], G[i * ldgb + k]);
+      }
+      __syncthreads();
+    }
+    float* Tf = region(kRgTf);
+    for (int e = tid; e < b * b; e += nthr) {  // column c of T = L^T: rows k <= c
+      const int c = e / b, k = e % b;
+      Tf[(long)c * ldrT + k] = k <= c ? (float)G[c * ldgb + k] : 0.f;
+    }
+    __syncthreads();
   } else if (tr) {
     for (long e = tid; e < (long)b * n; e += nthr) XR[e] = Rm[e];
     __syncthreads();
@@ -972,8 +1070,27 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
     __syncthreads();
     cta_colnorm_order(Tm, b, b, ldr, sv, ordh);
   } else {
+    if (bigg) {
+      float* Tf = region(kRgTf);
+      cta_hestenes_any<double>(Tf, b, voffT, b, ldrT, 1.2e-7f * sqrtf((float)b) + 2.4e-7f, 30, inv_x2);
+      __syncthreads();
+      for (long e = tid; e < (long)b * n; e += nthr) XR[e] = Rm[e];  // R, contiguous columns
+      __syncthreads();
+      for (long e = tid; e < (long)b * n; e += nthr) {  // R V into the augmented columns
+        const int j = (int)(e / n), i = (int)(e % n);
+        const float* vj = Tf + (long)j * ldrT + voffT;
+        float acc = 0.f;
+        for (int l = 0; l < b; ++l) acc = fmaf(XR[(long)l * n + i], vj[l], acc);
+        Rm[(long)j * ldr + i] = acc;
+      }
+      for (int e = tid; e < b * b; e += nthr) {  // and V below them, the Jacobi's start
+        const int j = e / b, l = e % b;
+        Rm[(long)j * ldr + voff + l] = Tf[(long)j * ldrT + voffT + l];
+      }
+      __syncthreads();
+    }
     sw = cta_hestenes_any<double>(Rm, rlen, voff, nsv, ldr,
-                                  1.2e-7f * sqrtf((float)rlen) + 2.4e-7f, 30, inv_x2);
+                                  1.2e-7f * sqrtf((float)rlen) + 2.4e-7f, 30, inv_x2, true, 32, bigg);
     __syncthreads();
     cta_colnorm_order(Rm, rlen, nsv, ldr, sv, ordh);
   }
@@ -1363,14 +1480,20 @@ static StepPlan plan_bug_step(int n, int b, int ld, long pool_max_floats) {
   fl[kRgWu] = N * P.ldw;
   fl[kRgWu2] = N * P.ldw;
   fl[kRgUs] = (long)n * P.ldu;
+  // blocks of 17..kMaxGramB columns factor the Gram (b x (b+1) doubles) and
+  // run the Jacobi (fp64 accumulation) on the b x b factor's columns with
+  // their rotations below
+  const bool big_chol = b > 16 && b <= kMaxGramB && b <= n;
+  fl[kRgGram] = big_chol ? 2L * b * (b + 1) : 0;
+  fl[kRgTf] = big_chol ? (long)b * jacobi_pitch(((b + 3) & ~3) + b, b, true) : 0;
   long wo = 0;
   for (int g = 0; g < kRgCount; ++g) {
     P.ws[g] = g == kRgUs ? -1 : wo;
     if (g != kRgUs) wo += align16(4 * fl[g]) + 128;
   }
   P.ws_bytes = align16(wo);
-  const int prio[] = {kRgRm, kRgXr, kRgPart, kRgAs, kRgA2, kRgSmall,
-                      kRgCore, kRgPol, kRgWu, kRgUs, kRgWu2};
+  const int prio[] = {kRgRm, kRgXr, kRgPart, kRgTf, kRgAs, kRgA2, kRgSmall,
+                      kRgCore, kRgPol, kRgWu, kRgUs, kRgWu2, kRgGram};
   long used = 0;
   for (int g = 0; g < kRgCount; ++g) P.smem[g] = -1;
   for (int g : prio) {

@@ -25,6 +25,7 @@ struct BugStepArgs {
 // (kRgUs) only in shared memory; otherwise it is read in place.
 enum StepRegion {
   kRgRm, kRgXr, kRgPart, kRgAs, kRgA2, kRgSmall, kRgCore, kRgPol, kRgWu, kRgWu2, kRgUs,
+  kRgGram, kRgTf,  // blocks of 17..128 columns: the fp64 Gram and the factor's columns
   kRgCount
 };
 struct StepPlan {
