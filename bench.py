@@ -152,14 +152,15 @@ def kernel_bytes(w: dict) -> dict[str, float]:
       slash_keep    P x (read kept K,V rows 2*h*n*2 + write tier 2*h*n*2)
       carry         2 x P x W*r*4*2 (read + write the coordinates)
       mid_hat       P x (read C_k, C_v 2*W*r*4 + write K, V 2*W*n*2)
-      decode        P x (C_k, C_v 2*W*r*4 + positions W*4 + U_k, U_v 2*n*r*4   (tile + merge)
-                    + verbatim tiers 2*n*(hh+ring+sinks)*2 + q/out)
+      decode_mid    P x (C_k, C_v 2*W*r*4 + positions W*4 + U_k, U_v 2*n*r*4 + q/out)
+      decode_mma    P x (verbatim tiers 2*n*(hh+ring+sinks)*2 + q/out)   (with the merge)
     """
     L, H, D, r = w["layers"], w["kv_heads"], w["head_dim"], w["rank"]
     n, T, C = H * D, w["tokens"], w["chunk"]
     sinks, ring, b, h, pbs = w["sinks"], w["ring"], w["absorb"], w["hh"], w["prefill_block"]
     out = {k: 0.0 for k in ("bug_step_kernel", "slash_score_kernel", "slash_keep_kernel",
-                            "carry_kernel", "mid_hat_kernel", "decode_tile_kernel")}
+                            "carry_kernel", "mid_hat_kernel", "decode_mid_kernel",
+                            "decode_mma_kernel")}
     rk, W, hh, rl, cum = 0, 0, 0, 0, 0
 
     def bug(bb: int) -> None:
@@ -199,8 +200,8 @@ def kernel_bytes(w: dict) -> dict[str, float]:
             rl -= b
             absorb()
         exact = hh + rl + sinks
-        out["decode_tile_kernel"] += L * (2 * W * r * 4 + W * 4 + 2 * n * r * 4 + 2 * n * exact * 2
-                                           + 2 * 2 * w["q_heads"] * D)
+        out["decode_mid_kernel"] += L * (2 * W * r * 4 + W * 4 + 2 * n * r * 4 + 2 * w["q_heads"] * D)
+        out["decode_mma_kernel"] += L * (2 * n * exact * 2 + 2 * w["q_heads"] * D)
     return out
 
 
@@ -321,7 +322,7 @@ def run_ours(args, w: dict) -> None:
 
         def roof(name: str) -> dict:
             ms, launches = prof.get(name, (0.0, 0))
-            if name.startswith("decode_") and name != "decode_merge_kernel":  # split + merge: one op
+            if name == "decode_mma_kernel":  # verbatim tiles + the merge of all partials: one op
                 ms += prof.get("decode_merge_kernel", (0.0, 0))[0]
             nbytes = kb.get(name)
             ach = nbytes / (ms / 1e3) / 1e9 if (nbytes and ms) else None
@@ -331,7 +332,7 @@ def run_ours(args, w: dict) -> None:
                     "avg_launch_ms": (ms / launches) if launches else None}
 
         roof_all = {k: roof(k) for k in kb if k in prof}
-        roof_dom = roof_all.get(dom) or roof("decode_tile_kernel")
+        roof_dom = roof_all.get(dom) or roof("decode_mid_kernel")
         total_ms = sum(x[0] for x in prof.values()) or 1e-9
         kernels = {k: {"total_ms": round(v[0], 4), "launches": v[1], "share": round(v[0] / total_ms, 4)}
                    for k, v in sorted(prof.items(), key=lambda kv: -kv[1][0])}

@@ -448,6 +448,21 @@ __global__ void __launch_bounds__(kTileThreads) decode_tile_kernel(DecArgs a, in
   }
 }
 
+// The 16 / sizeof(T) elements of one 16-byte chunk, widened to fp32.
+template <typename T> __device__ __forceinline__ void widen_chunk(uint4 r, float* v);
+template <> __device__ __forceinline__ void widen_chunk<float>(uint4 r, float* v) {
+  v[0] = __uint_as_float(r.x); v[1] = __uint_as_float(r.y);
+  v[2] = __uint_as_float(r.z); v[3] = __uint_as_float(r.w);
+}
+template <> __device__ __forceinline__ void widen_chunk<__nv_bfloat16>(uint4 r, float* v) {
+  const unsigned w[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {  // bf16 -> fp32 is the 16 bits shifted up
+    v[2 * i] = __uint_as_float(w[i] << 16);
+    v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+
 // ------------------------------------------------------- tensor-core decode
 // decode_tile_kernel's tiling with the three products of a middle tile on
 // the tensor cores (warp-level TF32 m16n8k8, fp32 accumulation; SPLIT =
@@ -527,9 +542,13 @@ __global__ void __launch_bounds__(kTileThreads) decode_mma_kernel(DecArgs a, int
     else if (tile < nv0 + nm) { kind = 1; j0 = (tile - nv0) * kTT; ntok = min(kTT, a.W - j0); }
     else { kind = 2; j0 = (tile - nv0 - nm) * kTT; ntok = min(kTT, a.ring_len - j0); }
     if (kind != 1) {
-      for (int e = tid; e < kTT * D; e += kTileThreads) {
-        const int tt = e / D, d = e % D;
-        float kv = 0.f, vv = 0.f;
+      // the group's rows of the tile as 16-byte chunks (all in flight), widened to fp32
+      constexpr int kPer = 16 / sizeof(T), kQ = D / kPer;
+      for (int e = tid; e < kTT * kQ; e += kTileThreads) {
+        const int tt = e / kQ, c = (e % kQ) * kPer;
+        float kv[kPer], vv[kPer];
+#pragma unroll
+        for (int q = 0; q < kPer; ++q) { kv[q] = 0.f; vv[q] = 0.f; }
         if (tt < ntok) {
           const int t = j0 + tt;
           const T* kr; const T* vr;
@@ -543,11 +562,21 @@ __global__ void __launch_bounds__(kTileThreads) decode_mma_kernel(DecArgs a, int
             kr = reinterpret_cast<const T*>(a.hh_k) + p * a.hh_sp + (long)(t - a.sink_len) * n;
             vr = reinterpret_cast<const T*>(a.hh_v) + p * a.hh_sp + (long)(t - a.sink_len) * n;
           }
-          kv = load_f<T>(kr + g * D + d);
-          vv = load_f<T>(vr + g * D + d);
+          kr += g * D + c;
+          vr += g * D + c;
+          if (((reinterpret_cast<uintptr_t>(kr) | reinterpret_cast<uintptr_t>(vr)) & 15) == 0) {
+            widen_chunk<T>(*reinterpret_cast<const uint4*>(kr), kv);
+            widen_chunk<T>(*reinterpret_cast<const uint4*>(vr), vv);
+          } else {
+#pragma unroll
+            for (int q = 0; q < kPer; ++q) { kv[q] = load_f<T>(kr + q); vv[q] = load_f<T>(vr + q); }
+          }
         }
-        ks[tt * ldk + d] = kv;
-        vs[tt * ldk + d] = vv;
+#pragma unroll
+        for (int q = 0; q < kPer; q += 4) {
+          *reinterpret_cast<float4*>(ks + tt * ldk + c + q) = make_float4(kv[q], kv[q + 1], kv[q + 2], kv[q + 3]);
+          *reinterpret_cast<float4*>(vs + tt * ldk + c + q) = make_float4(vv[q], vv[q + 1], vv[q + 2], vv[q + 3]);
+        }
       }
       __syncthreads();
       const int tt = tid % kTT, hs = tid / kTT;  // thread -> token tt, heads hs, hs + 2, ...
