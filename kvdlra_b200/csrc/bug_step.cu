@@ -30,8 +30,8 @@ __host__ __device__ inline long align16(long x) { return (x + 15) & ~15L; }
 
 constexpr int kStepThreads = 512;
 constexpr int kStepMiscBytes = 1024;   // fp64 reduction scratch
-constexpr int kPartFloats = 8192;
-constexpr int kMaxGramB = 128;  // widest block the Gram + Cholesky residual SVD takes      // K-split partials: 16 warps x 32 lanes x 16
+constexpr int kPartFloats = 8192;      // K-split partials: 16 warps x 32 lanes x 16
+constexpr int kMaxGramB = 128;         // widest block the Gram + Cholesky residual SVD takes
 
 // One-sided (Hestenes) Jacobi on augmented columns.  Column c of X (at
 // X + c*ldx) holds the data in rows [0, len), zeros in [len, voff) and, from
@@ -903,7 +903,7 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
   // R V = Q1 U_T S -- in one warp's registers.  17..kMaxGramB tokens (the
   // pre-fill blocks): the same factorisation by the CTA, whose Jacobi (fp64
   // sums) gives R's right vectors to within the factor's fp32 rounding; they
-  // seed the one-sided Jacobi on R V itself, whose columns are then nearly
+  // seed the one-sided Jacobi (fp64 sums) on R V itself, whose columns are then nearly
   // orthogonal, so it converges in about one sweep to the accuracy of the
   // Jacobi on R (the factor alone loses relative accuracy in the smallest
   // singular directions, and a noisy spectrum at the truncation amplifies it).
@@ -917,7 +917,7 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
   const int ldr = chol ? jacobi_pitch(voff + b, b, false) : jacobi_pitch(voff + nsv, nsv, true);
   const int ldr0 = (tr || chol || bigg) ? n : ldr;  // pitch the residual is formed with
   float* Tm = chol ? part + 2 * (16 * 17 + 8) : Rm;  // the factor, augmented columns (after the Gram)
-  const int voffT = (b + 3) & ~3, ldrT = jacobi_pitch(voffT + b, b, true);  // bigg: the factor's pitch
+  const int voffT = (b + 3) & ~3, ldrT = jacobi_pitch(voffT + b, b, false);  // bigg: the factor's pitch
   // ----- residual R = (I - U U^T)^2 X (the reference's re-orthogonalised residual)
   if (r > 0) cta_tn(r, b, n, Uc, lda, XR, ldb, true, AS, b16, 0.f, part);  // a = U^T X
   cta_rows_sub(n, b, b16, r, Uc, lda, AS, b16, XR, ldb, Rm, ldr0, true, r > 0);  // R = X - U a
@@ -1072,7 +1072,8 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
   } else {
     if (bigg) {
       float* Tf = region(kRgTf);
-      cta_hestenes_any<double>(Tf, b, voffT, b, ldrT, 1.2e-7f * sqrtf((float)b) + 2.4e-7f, 30, inv_x2);
+      // a preconditioner only (the Jacobi on R V below sets the accuracy): fp32 sums
+      cta_hestenes_any<float>(Tf, b, voffT, b, ldrT, 1.2e-7f * sqrtf((float)b) + 2.4e-7f, 30, inv_x2);
       __syncthreads();
       for (long e = tid; e < (long)b * n; e += nthr) XR[e] = Rm[e];  // R, contiguous columns
       __syncthreads();
@@ -1485,7 +1486,7 @@ static StepPlan plan_bug_step(int n, int b, int ld, long pool_max_floats) {
   // their rotations below
   const bool big_chol = b > 16 && b <= kMaxGramB && b <= n;
   fl[kRgGram] = big_chol ? 2L * b * (b + 1) : 0;
-  fl[kRgTf] = big_chol ? (long)b * jacobi_pitch(((b + 3) & ~3) + b, b, true) : 0;
+  fl[kRgTf] = big_chol ? (long)b * jacobi_pitch(((b + 3) & ~3) + b, b, false) : 0;
   long wo = 0;
   for (int g = 0; g < kRgCount; ++g) {
     P.ws[g] = g == kRgUs ? -1 : wo;
