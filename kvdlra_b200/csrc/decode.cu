@@ -899,74 +899,95 @@ __global__ void __launch_bounds__(kMidThreads) decode_mid_kernel(DecArgs a, int 
       }
     }
     __syncthreads();
-    for (int task = warp; task < 4 * H; task += kMidWarps) {
-      const int g = task >> 2;
-      const int tt0 = (task & 3) * 16 + gq, tt1 = tt0 + 8;
-      float kacc[NT][4];
+    // task = (group, RB consecutive 16-token row blocks); each basis fragment
+    // loaded from shared memory feeds RB products
+    constexpr int RB = (!SPLIT && D == 64) ? 2 : 1;
+    constexpr int kBlocks = 4 / RB;
+    for (int task = warp; task < kBlocks * H; task += kMidWarps) {
+      const int g = task / kBlocks, rb0 = (task % kBlocks) * RB;
+      float kacc[RB][NT][4];
 #pragma unroll
-      for (int j = 0; j < NT; ++j)
+      for (int r = 0; r < RB; ++r)
 #pragma unroll
-        for (int q = 0; q < 4; ++q) kacc[j][q] = 0.f;
+        for (int j = 0; j < NT; ++j)
+#pragma unroll
+          for (int q = 0; q < 4; ++q) kacc[r][j][q] = 0.f;
       const int nkk = (r_k + 7) / 8;
       for (int kk = 0; kk < nkk; ++kk) {
         const int c0 = kk * 8 + tq;
-        const float af[4] = {kb[tt0 * ldc + c0], kb[tt1 * ldc + c0], kb[tt0 * ldc + c0 + 4],
-                             kb[tt1 * ldc + c0 + 4]};
+        float af[RB][4];
+#pragma unroll
+        for (int r = 0; r < RB; ++r) {
+          const int t0 = (rb0 + r) * 16 + gq;
+          af[r][0] = kb[t0 * ldc + c0];
+          af[r][1] = kb[(t0 + 8) * ldc + c0];
+          af[r][2] = kb[t0 * ldc + c0 + 4];
+          af[r][3] = kb[(t0 + 8) * ldc + c0 + 4];
+        }
         if constexpr (SPLIT) {
           uint32_t ah[4], al[4];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) tf32_split(af[q], &ah[q], &al[q]);
+          for (int q = 0; q < 4; ++q) tf32_split(af[0][q], &ah[q], &al[q]);
 #pragma unroll
           for (int j = 0; j < NT; ++j) {
             const float* ur = us + (g * D + j * 8 + gq) * ldc + c0;
             uint32_t bh0, bl0, bh1, bl1;
             tf32_split(ur[0], &bh0, &bl0);
             tf32_split(ur[4], &bh1, &bl1);
-            mma_tf32(kacc[j], al, bh0, bh1);
-            mma_tf32(kacc[j], ah, bl0, bl1);
-            mma_tf32(kacc[j], ah, bh0, bh1);
+            mma_tf32(kacc[0][j], al, bh0, bh1);
+            mma_tf32(kacc[0][j], ah, bl0, bl1);
+            mma_tf32(kacc[0][j], ah, bh0, bh1);
           }
         } else {
-          const uint32_t ah[4] = {__float_as_uint(af[0]), __float_as_uint(af[1]),
-                                  __float_as_uint(af[2]), __float_as_uint(af[3])};
+          uint32_t ah[RB][4];
+#pragma unroll
+          for (int r = 0; r < RB; ++r)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) ah[r][q] = __float_as_uint(af[r][q]);
 #pragma unroll
           for (int j = 0; j < NT; ++j) {
             const float* ur = us + (g * D + j * 8 + gq) * ldc + c0;
-            mma_tf32(kacc[j], ah, __float_as_uint(ur[0]), __float_as_uint(ur[4]));
+            const uint32_t b0 = __float_as_uint(ur[0]), b1 = __float_as_uint(ur[4]);
+#pragma unroll
+            for (int r = 0; r < RB; ++r) mma_tf32(kacc[r][j], ah[r], b0, b1);
           }
         }
       }
 #pragma unroll
-      for (int j = 0; j < HT; ++j) {
-        const int f = 8 * j + 2 * tq;
-        const float2 ca = *reinterpret_cast<const float2*>(cosb + tt0 * cp + f);
-        const float2 sa = *reinterpret_cast<const float2*>(sinb + tt0 * cp + f);
-        const float2 cb = *reinterpret_cast<const float2*>(cosb + tt1 * cp + f);
-        const float2 sb = *reinterpret_cast<const float2*>(sinb + tt1 * cp + f);
-        const float c0s[2] = {ca.x, ca.y}, s0s[2] = {sa.x, sa.y}, c1s[2] = {cb.x, cb.y}, s1s[2] = {sb.x, sb.y};
+      for (int r = 0; r < RB; ++r) {
+        const int tt0 = (rb0 + r) * 16 + gq, tt1 = tt0 + 8;
+#pragma unroll
+        for (int j = 0; j < HT; ++j) {
+          const int f = 8 * j + 2 * tq;
+          const float2 ca = *reinterpret_cast<const float2*>(cosb + tt0 * cp + f);
+          const float2 sa = *reinterpret_cast<const float2*>(sinb + tt0 * cp + f);
+          const float2 cb = *reinterpret_cast<const float2*>(cosb + tt1 * cp + f);
+          const float2 sb = *reinterpret_cast<const float2*>(sinb + tt1 * cp + f);
+          const float c0s[2] = {ca.x, ca.y}, s0s[2] = {sa.x, sa.y}, c1s[2] = {cb.x, cb.y}, s1s[2] = {sb.x, sb.y};
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            float y1, y2;
+            rope_apply_pair(kacc[r][j][e], kacc[r][j + HT][e], c0s[e], s0s[e], &y1, &y2);
+            kacc[r][j][e] = y1; kacc[r][j + HT][e] = y2;
+            rope_apply_pair(kacc[r][j][2 + e], kacc[r][j + HT][2 + e], c1s[e], s1s[e], &y1, &y2);
+            kacc[r][j][2 + e] = y1; kacc[r][j + HT][2 + e] = y2;
+          }
+        }
+        float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+        const float* qr = qs + (g * G + gq) * D + 2 * tq;
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+          const float kf[4] = {kacc[r][j][0], kacc[r][j][2], kacc[r][j][1], kacc[r][j][3]};
+          mma_f32<SPLIT>(sacc, kf, gq < G ? qr[8 * j] : 0.f, gq < G ? qr[8 * j + 1] : 0.f);
+        }
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
-          float y1, y2;
-          rope_apply_pair(kacc[j][e], kacc[j + HT][e], c0s[e], s0s[e], &y1, &y2);
-          kacc[j][e] = y1; kacc[j + HT][e] = y2;
-          rope_apply_pair(kacc[j][2 + e], kacc[j + HT][2 + e], c1s[e], s1s[e], &y1, &y2);
-          kacc[j][2 + e] = y1; kacc[j + HT][2 + e] = y2;
-        }
-      }
-      float sacc[4] = {0.f, 0.f, 0.f, 0.f};
-      const float* qr = qs + (g * G + gq) * D + 2 * tq;
-#pragma unroll
-      for (int j = 0; j < NT; ++j) {
-        const float af[4] = {kacc[j][0], kacc[j][2], kacc[j][1], kacc[j][3]};
-        mma_f32<SPLIT>(sacc, af, gq < G ? qr[8 * j] : 0.f, gq < G ? qr[8 * j + 1] : 0.f);
-      }
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int h = 2 * tq + e;
-        if (h < G) {
-          float* pr = ps + (g * G + h) * ldps;
-          pr[tt0] = tt0 < ntok ? sacc[e] * a.scaling : -INFINITY;
-          pr[tt1] = tt1 < ntok ? sacc[2 + e] * a.scaling : -INFINITY;
+          const int h = 2 * tq + e;
+          if (h < G) {
+            float* pr = ps + (g * G + h) * ldps;
+            pr[tt0] = tt0 < ntok ? sacc[e] * a.scaling : -INFINITY;
+            pr[tt1] = tt1 < ntok ? sacc[2 + e] * a.scaling : -INFINITY;
+          }
         }
       }
     }
