@@ -117,8 +117,8 @@ int launch_gather_block(const T* g_k, const T* g_v, long g_sp, int P, int b, int
                         int start, RopeArgs rope, float* xk, float* xv, long x_sp, int* mid_pos,
                         long mid_sp, int w_off, cudaStream_t stream);
 template <typename T>
-int launch_hf_to_rows(const kvd_hf_view& v, int P, int H, int D, T* dst, long dst_sp, int slot0,
-                      cudaStream_t s);
+int launch_hf_to_rows(const kvd_hf_view& kv, const kvd_hf_view& vv, int P, int H, int D, T* dst_k,
+                      T* dst_v, long dst_sp, int slot0, cudaStream_t s);
 template <typename T>
 int launch_rows_copy(const T* src, long src_sp, T* dst, long dst_sp, int count, int n, int P,
                      cudaStream_t s);

@@ -460,8 +460,9 @@ struct Group {
     int rc = ensure_ring_room(q);
     if (rc) return rc;
     const int slot0 = k.ring_head + k.ring_len;
-    if ((rc = launch_hf_to_rows<T>(kv, P, c.num_heads, c.head_dim, (T*)b.ring_k, row_sp_ring, slot0, s))) return rc;
-    if ((rc = launch_hf_to_rows<T>(vv, P, c.num_heads, c.head_dim, (T*)b.ring_v, row_sp_ring, slot0, s))) return rc;
+    if ((rc = launch_hf_to_rows<T>(kv, vv, P, c.num_heads, c.head_dim, (T*)b.ring_k, (T*)b.ring_v,
+                                   row_sp_ring, slot0, s)))
+      return rc;
     k.ring_len += q;
     k.cumulative_length += q;
     return KVD_OK;
@@ -477,8 +478,9 @@ struct Group {
     const int recent = (t - n_sink) < c.recent_window ? (t - n_sink) : c.recent_window;
     const int mid = t - n_sink - recent;
     int rc;
-    if ((rc = launch_hf_to_rows<T>(kv, P, c.num_heads, c.head_dim, (T*)b.ring_k, row_sp_ring, 0, s))) return rc;
-    if ((rc = launch_hf_to_rows<T>(vv, P, c.num_heads, c.head_dim, (T*)b.ring_v, row_sp_ring, 0, s))) return rc;
+    if ((rc = launch_hf_to_rows<T>(kv, vv, P, c.num_heads, c.head_dim, (T*)b.ring_k, (T*)b.ring_v,
+                                   row_sp_ring, 0, s)))
+      return rc;
     const long sink_sp = (long)c.n_sink * n;
     if ((rc = launch_rows_copy<T>((const T*)b.ring_k, row_sp_ring, (T*)b.sink_k, sink_sp, n_sink, n, P, s))) return rc;
     if ((rc = launch_rows_copy<T>((const T*)b.ring_v, row_sp_ring, (T*)b.sink_v, sink_sp, n_sink, n, P, s))) return rc;

@@ -8,10 +8,19 @@
 namespace kvd {
 
 // rows[p][slot0 + t][h*D + d] = src[b][h][t][d]   (p = b)
+// One side (keys or values) of an HF-layout to ring-rows copy.
 template <typename T>
-__global__ void hf_to_rows_kernel(const T* src, long sb, long sh, long st, int H, int D, int q,
-                                  T* dst, long dst_sp, int slot0) {
+struct HfRowsSide { const T* src; long sb, sh, st; T* dst; };
+template <typename T>
+struct HfRowsPair { HfRowsSide<T> s[2]; };
+
+template <typename T>
+__global__ void hf_to_rows_kernel(HfRowsPair<T> pr, int H, int D, int q, long dst_sp, int slot0) {
   const int p = blockIdx.y;
+  const HfRowsSide<T> sd = blockIdx.z ? pr.s[1] : pr.s[0];  // keys, values
+  const T* src = sd.src;
+  const long sb = sd.sb, sh = sd.sh, st = sd.st;
+  T* dst = sd.dst;
   const int n = H * D;
   const long tot = (long)q * n;
   for (long e = blockIdx.x * (long)blockDim.x + threadIdx.x; e < tot; e += (long)gridDim.x * blockDim.x) {
@@ -292,14 +301,20 @@ static inline int grid_for(long tot) {
 }
 
 template <typename T>
-int launch_hf_to_rows(const kvd_hf_view& v, int P, int H, int D, T* dst, long dst_sp, int slot0,
-                      cudaStream_t s) {
-  if (v.tokens <= 0 || P <= 0) return KVD_OK;
-  dim3 grid(grid_for((long)v.tokens * H * D), P);
+int launch_hf_to_rows(const kvd_hf_view& kv, const kvd_hf_view& vv, int P, int H, int D, T* dst_k,
+                      T* dst_v, long dst_sp, int slot0, cudaStream_t s) {
+  if (kv.tokens <= 0 || P <= 0) return KVD_OK;
+  if (vv.tokens != kv.tokens) {
+    set_error("keys and values carry %d and %d tokens", kv.tokens, vv.tokens);
+    return KVD_ERR_ARG;
+  }
+  HfRowsPair<T> pr;
+  pr.s[0] = {(const T*)kv.ptr, kv.stride_b, kv.stride_h, kv.stride_t, dst_k};
+  pr.s[1] = {(const T*)vv.ptr, vv.stride_b, vv.stride_h, vv.stride_t, dst_v};
+  dim3 grid(grid_for((long)kv.tokens * H * D), P, 2);  // keys and values in one launch
   {
     KTimerScope kts_("hf_to_rows_kernel", s);
-    hf_to_rows_kernel<T><<<grid, 256, 0, s>>>((const T*)v.ptr, v.stride_b, v.stride_h, v.stride_t, H,
-                                            D, v.tokens, dst, dst_sp, slot0);
+    hf_to_rows_kernel<T><<<grid, 256, 0, s>>>(pr, H, D, kv.tokens, dst_sp, slot0);
   }
   return check_launch("hf_to_rows_kernel");
 }
@@ -415,8 +430,8 @@ int launch_peek(const kvd_config& c, const kvd_buffers& b, const kvd_counters& k
 }
 
 #define KVD_INST(T)                                                                             \
-  template int launch_hf_to_rows<T>(const kvd_hf_view&, int, int, int, T*, long, int,          \
-                                    cudaStream_t);                                              \
+  template int launch_hf_to_rows<T>(const kvd_hf_view&, const kvd_hf_view&, int, int, int, T*,  \
+                                    T*, long, int, cudaStream_t);                               \
   template int launch_rows_copy<T>(const T*, long, T*, long, int, int, int, cudaStream_t);      \
   template int launch_ring_compact<T>(T*, long, int, int, int, int, cudaStream_t);              \
   template int launch_peek<T>(const kvd_config&, const kvd_buffers&, const kvd_counters&, int,  \
