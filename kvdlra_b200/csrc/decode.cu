@@ -1155,7 +1155,8 @@ size_t decode_ws_bytes(const kvd_config& c, int count, int num_q_heads) {
 template <typename T>
 int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_counters& k, int p0,
                            int count, const void* q, int Hq, float scaling, void* out, char* ws,
-                           size_t ws_bytes, cudaStream_t s) {
+                           size_t ws_bytes, cudaStream_t s, cudaStream_t side, cudaEvent_t ev_fork,
+                           cudaEvent_t ev_join) {
   DecArgs a;
   const int n = c.num_heads * c.head_dim;
   a.H = c.num_heads; a.D = c.head_dim; a.G = Hq / c.num_heads; a.ld = c.rank; a.Hq = Hq;
@@ -1217,22 +1218,37 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
     const size_t need2 = (size_t)count * a.H * a.n_chunks * a.part_sp_chunk * 4;
     if (need2 > ws_bytes) { set_error("factored decode: workspace too small"); return KVD_ERR_WORKSPACE; }
     constexpr bool kSplit = sizeof(T) == 4;
+    auto mid_fn = a.D == 64 ? decode_mid_kernel<T, 64, kSplit> : decode_mid_kernel<T, 128, kSplit>;
+    if (int rc0 = ensure_smem((const void*)mid_fn, 4 * ms.total, "decode_mid_kernel")) return rc0;
+    // the verbatim tiles run beside the middle tier (disjoint partial records)
+    const bool fork = side && ev_fork && ev_join && n_vch > 0;
     if (n_vch > 0) {
       const int ldk = a.D + 4, ldv = a.ld + 8, ldc = a.ld + 4;
       const int tsmem = 4 * (a.G * a.D + kTT * ldk + kTT * (ldk > ldv ? ldk : ldv) +
                              a.G * (kTT + 4) + a.D * ldc + 4 * a.G);
       auto fn = a.D == 64 ? decode_mma_kernel<T, 64, kSplit> : decode_mma_kernel<T, 128, kSplit>;
       if (int rc0 = ensure_smem((const void*)fn, tsmem, "decode_mma_kernel")) return rc0;
-      KTimerScope kts_("decode_mma_kernel", s);
-      fn<<<dim3(n_vch, a.H, count), kTileThreads, tsmem, s>>>(a, nv0, 0, nvt, 1);
+      cudaStream_t vs = s;
+      if (fork) {
+        cudaEventRecord(ev_fork, s);
+        cudaStreamWaitEvent(side, ev_fork, 0);
+        vs = side;
+      }
+      {
+        KTimerScope kts_("decode_mma_kernel", vs);
+        fn<<<dim3(n_vch, a.H, count), kTileThreads, tsmem, vs>>>(a, nv0, 0, nvt, 1);
+      }
+      if (fork) cudaEventRecord(ev_join, side);
     }
-    if (int rc1 = check_launch("decode_mma_kernel")) return rc1;
+    if (int rc1 = check_launch("decode_mma_kernel")) {
+      if (fork) cudaStreamWaitEvent(s, ev_join, 0);
+      return rc1;
+    }
     {
-      auto fn = a.D == 64 ? decode_mid_kernel<T, 64, kSplit> : decode_mid_kernel<T, 128, kSplit>;
-      if (int rc0 = ensure_smem((const void*)fn, 4 * ms.total, "decode_mid_kernel")) return rc0;
       KTimerScope kts_("decode_mid_kernel", s);
-      fn<<<dim3(n_mch, count), kMidThreads, 4 * ms.total, s>>>(a, tpc, n_vch);
+      mid_fn<<<dim3(n_mch, count), kMidThreads, 4 * ms.total, s>>>(a, tpc, n_vch);
     }
+    if (fork) cudaStreamWaitEvent(s, ev_join, 0);  // the merge reads both kernels' records
     if (int rc1 = check_launch("decode_mid_kernel")) return rc1;
   } else if (mma) {
     const int ldk = a.D + 4, ldv = a.ld + 8, ldc = a.ld + 4;
@@ -1284,9 +1300,10 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
 }
 
 template int launch_factored_decode<float>(const kvd_config&, const kvd_buffers&, const kvd_counters&, int, int,
-                                           const void*, int, float, void*, char*, size_t, cudaStream_t);
+                                           const void*, int, float, void*, char*, size_t, cudaStream_t,
+                                           cudaStream_t, cudaEvent_t, cudaEvent_t);
 template int launch_factored_decode<__nv_bfloat16>(const kvd_config&, const kvd_buffers&, const kvd_counters&, int,
                                                    int, const void*, int, float, void*, char*, size_t,
-                                                   cudaStream_t);
+                                                   cudaStream_t, cudaStream_t, cudaEvent_t, cudaEvent_t);
 
 }  // namespace kvd_host

@@ -130,7 +130,10 @@ int launch_peek(const kvd_config& c, const kvd_buffers& b, const kvd_counters& k
                 const kvd_hf_view& tv, cudaStream_t s);
 size_t decode_ws_bytes(const kvd_config& c, int count, int num_q_heads);
 template <typename T>
+// `side` (with two events), when given, runs the verbatim tiles concurrently
+// with the middle tier; the merge waits for both on `s`.
 int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_counters& k, int p0,
                            int count, const void* q, int Hq, float scaling, void* out, char* ws,
-                           size_t ws_bytes, cudaStream_t s);
+                           size_t ws_bytes, cudaStream_t s, cudaStream_t side = nullptr,
+                           cudaEvent_t ev_fork = nullptr, cudaEvent_t ev_join = nullptr);
 }  // namespace kvd_host

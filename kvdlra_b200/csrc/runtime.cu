@@ -198,6 +198,7 @@ struct CarryStream {
   cudaStream_t side = nullptr;
   cudaEvent_t bug[2] = {nullptr, nullptr}, carry[2] = {nullptr, nullptr}, join = nullptr;
   cudaEvent_t ranked = nullptr, kept = nullptr;  // the tier copy: after ranking, then done
+  cudaEvent_t dfork = nullptr, djoin = nullptr;  // factored decode: verbatim tiles beside the middle
 };
 
 static CarryStream* carry_stream() {
@@ -215,7 +216,9 @@ static CarryStream* carry_stream() {
          cudaEventCreateWithFlags(&cs.carry[i], cudaEventDisableTiming) == cudaSuccess;
   ok = ok && cudaEventCreateWithFlags(&cs.join, cudaEventDisableTiming) == cudaSuccess &&
        cudaEventCreateWithFlags(&cs.ranked, cudaEventDisableTiming) == cudaSuccess &&
-       cudaEventCreateWithFlags(&cs.kept, cudaEventDisableTiming) == cudaSuccess;
+       cudaEventCreateWithFlags(&cs.kept, cudaEventDisableTiming) == cudaSuccess &&
+       cudaEventCreateWithFlags(&cs.dfork, cudaEventDisableTiming) == cudaSuccess &&
+       cudaEventCreateWithFlags(&cs.djoin, cudaEventDisableTiming) == cudaSuccess;
   if (!ok) {
     cudaGetLastError();
     cs = CarryStream{};  // carries then run on the caller's stream
@@ -651,8 +654,11 @@ extern "C" int kvd_factored_decode(const kvd_config* cfg, const kvd_buffers* buf
   if (ws_bytes < need || !workspace) { set_error("kvd_factored_decode: workspace %zu < %zu", ws_bytes, need); return KVD_ERR_WORKSPACE; }
   return dispatch(cfg, [&](auto* tag) {
     using T = std::remove_pointer_t<decltype(tag)>;
+    CarryStream* cs = carry_stream();
     return launch_factored_decode<T>(*cfg, *buf, *ctr, p0, count, q, num_q_heads, scaling, out,
-                                     align_ws(workspace), ws_bytes - 256, (cudaStream_t)stream);
+                                     align_ws(workspace), ws_bytes - 256, (cudaStream_t)stream,
+                                     cs ? cs->side : nullptr, cs ? cs->dfork : nullptr,
+                                     cs ? cs->djoin : nullptr);
   });
 }
 
