@@ -1116,8 +1116,18 @@ __global__ void __launch_bounds__(128) decode_merge_kernel(DecArgs a) {
     int qh; long off;
     if (e < G * D) { qh = e / D; off = 2 * G + e; }
     else { qh = (e - G * D) / ld; off = 2 * G + G * D + (e - G * D); }
-    float v = 0.f;
-    for (int c = 0; c < nch; ++c) v = fmaf(sc[c * G + qh], parts[c * sp + off], v);
+    float v0 = 0.f, v1 = 0.f, v2 = 0.f, v3 = 0.f;  // four chains, their loads in flight together
+    int c = 0;
+    for (; c + 4 <= nch; c += 4) {
+      const float x0 = parts[c * sp + off], x1 = parts[(c + 1) * sp + off];
+      const float x2 = parts[(c + 2) * sp + off], x3 = parts[(c + 3) * sp + off];
+      v0 = fmaf(sc[c * G + qh], x0, v0);
+      v1 = fmaf(sc[(c + 1) * G + qh], x1, v1);
+      v2 = fmaf(sc[(c + 2) * G + qh], x2, v2);
+      v3 = fmaf(sc[(c + 3) * G + qh], x3, v3);
+    }
+    for (; c < nch; ++c) v0 = fmaf(sc[c * G + qh], parts[c * sp + off], v0);
+    const float v = (v0 + v1) + (v2 + v3);
     if (e < G * D) accd[e] = v;
     else accc[e - G * D] = v;
   }
@@ -1129,6 +1139,7 @@ __global__ void __launch_bounds__(128) decode_merge_kernel(DecArgs a) {
     const int qh = e / D, d = e % D;
     float v = accd[e];
     const float* ur = Uv + (long)(g * D + d) * ld;
+#pragma unroll 8
     for (int c = 0; c < r_v; ++c) v = fmaf(ur[c], accc[qh * ld + c], v);
     store_f<T>(out + (long)(g * G + qh) * D + d, v / ml[2 * qh + 1]);
   }
