@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(256) slash_score_kernel(CandSrc<T> src, int m,
 // pass; warp w owns the candidate tile w % 2 and the coordinate tiles
 // 2 (w / 2) + {0, 1}.
 constexpr int kScT = 32;
-constexpr int kScThreads = 2 * kScT * 4;  // (kScT / 8) candidate tiles x 2 coordinate-tile pairs
+constexpr int kScThreads = 4 * kScT * 4;  // (kScT / 8) candidate tiles x 2 coordinate-tile pairs x 2 k halves
 
 
 __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
@@ -144,12 +144,14 @@ __global__ void __launch_bounds__(kScThreads) slash_score_dmma_kernel(CandSrc<T>
   const int ldx = n + 4, ldu = 40;                 // floats: 4 / 8 mod 32 (conflict-free fragments)
   double* kk = dsm;                                // [kScT]     |k|^2
   double* ccp = kk + kScT;                         // [2][kScT]  |c|^2 halves
-  float* xs = reinterpret_cast<float*>(ccp + 2 * kScT);  // [kScT][ldx] un-rotated rows
+  double* pcb = ccp + 2 * kScT;                    // [8 warps][32][4] second k half's tiles
+  float* xs = reinterpret_cast<float*>(pcb + 8 * 32 * 4);  // [kScT][ldx] un-rotated rows
   float* us = xs + kScT * ldx;                     // [n][ldu]   basis, zero past r
   float* cs = us + (long)n * ldu;                  // [kScT][half][2] RoPE
   T* kraw = reinterpret_cast<T*>(cs + kScT * half * 2);  // [kScT][n] raw candidate rows
   const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
-  const int mt = warp % (kScT / 8), nt0 = 2 * (warp / (kScT / 8));
+  const int mt = warp % (kScT / 8), ntp = (warp / (kScT / 8)) % 2, nt0 = 2 * ntp;
+  const int ks = warp / (kScT / 4);  // half of the k range (n % 16 == 0)
   const int grp = lane >> 2, tig = lane & 3;
   const float* U = u + p * u_sp;
   const int nu = r < 32 ? r : 32;
@@ -199,23 +201,24 @@ __global__ void __launch_bounds__(kScThreads) slash_score_dmma_kernel(CandSrc<T>
     xs[a * ldx + h * D + f + half] = y2;
   }
   __syncthreads();
-  {  // |k|^2: 8 threads per candidate, fp64
-    const int a = tid / 8, sub = tid % 8;
+  {  // |k|^2: 16 threads per candidate, fp64
+    const int a = tid / 16, sub = tid % 16;
     double sq = 0.0;
-    for (int d = sub; d < n; d += 8) {
+    for (int d = sub; d < n; d += 16) {
       const double v = xs[a * ldx + d];
       sq = fma(v, v, sq);
     }
 #pragma unroll
-    for (int o = 4; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    for (int o = 8; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
     if (sub == 0) kk[a] = sq;
   }
   // tiles nt0, nt0 + 1, each as two chains over alternate k-steps (n % 8 == 0)
   double c00 = 0.0, c01 = 0.0, c10 = 0.0, c11 = 0.0, e00 = 0.0, e01 = 0.0, e10 = 0.0, e11 = 0.0;
   const float* xa = xs + (mt * 8 + grp) * ldx + tig;
   const float* ub = us + tig * ldu + nt0 * 8 + grp;
+  const int kh = n / 2;
 #pragma unroll 2
-  for (int k0 = 0; k0 < n; k0 += 8) {
+  for (int k0 = ks * kh; k0 < (ks + 1) * kh; k0 += 8) {
     const double av = xa[k0], bv = xa[k0 + 4];
     dmma_8x8x4(c00, c01, av, (double)ub[k0 * ldu]);
     dmma_8x8x4(c10, c11, av, (double)ub[k0 * ldu + 8]);
@@ -223,11 +226,16 @@ __global__ void __launch_bounds__(kScThreads) slash_score_dmma_kernel(CandSrc<T>
     dmma_8x8x4(e10, e11, bv, (double)ub[(k0 + 4) * ldu + 8]);
   }
   c00 += e00; c01 += e01; c10 += e10; c11 += e11;
-  // |c|^2 of each candidate row: the lane's four values, the row's four lanes, two warps
-  double cc = c00 * c00 + c01 * c01 + c10 * c10 + c11 * c11;
-  cc += __shfl_xor_sync(0xffffffffu, cc, 1);
-  cc += __shfl_xor_sync(0xffffffffu, cc, 2);
-  if (tig == 0) ccp[(warp / (kScT / 8)) * kScT + mt * 8 + grp] = cc;
+  double* pw = pcb + ((warp % (kScT / 4)) * 32 + lane) * 4;
+  if (ks == 1) { pw[0] = c00; pw[1] = c01; pw[2] = c10; pw[3] = c11; }
+  __syncthreads();
+  if (ks == 0) {  // the full projection (both k halves), then |c|^2 of each candidate row:
+    c00 += pw[0]; c01 += pw[1]; c10 += pw[2]; c11 += pw[3];  // the lane's four values, the
+    double cc = c00 * c00 + c01 * c01 + c10 * c10 + c11 * c11;  // row's four lanes, two warps
+    cc += __shfl_xor_sync(0xffffffffu, cc, 1);
+    cc += __shfl_xor_sync(0xffffffffu, cc, 2);
+    if (tig == 0) ccp[ntp * kScT + mt * 8 + grp] = cc;
+  }
   __syncthreads();
   if (tid < kScT) {
     const int j = j0 + tid;
@@ -567,7 +575,7 @@ int launch_slash_score(const CandSrc<T>& src, int P, int m, int H, int D, RopeAr
   }
   const int half = D / 2;
   const long n = (long)H * D;
-  const long dsmem_l = 8L * 3 * kScT + 4L * (kScT * (n + 4) + n * 40 + kScT * half * 2) +
+  const long dsmem_l = 8L * (3 * kScT + 8 * 32 * 4) + 4L * (kScT * (n + 4) + n * 40 + kScT * half * 2) +
                        (long)sizeof(T) * kScT * n;
   // cp.async staging: 16-byte rows and bases
   const bool al = (n * (long)sizeof(T)) % 16 == 0 && ld % 4 == 0 && u_sp % 4 == 0 &&
@@ -575,7 +583,7 @@ int launch_slash_score(const CandSrc<T>& src, int P, int m, int H, int D, RopeAr
                   reinterpret_cast<uintptr_t>(src.g_k) % 16 == 0 &&
                   (src.hh_len == 0 || reinterpret_cast<uintptr_t>(src.hh_k) % 16 == 0) &&
                   (src.hh_sp * (long)sizeof(T)) % 16 == 0 && (src.g_sp * (long)sizeof(T)) % 16 == 0;
-  if (ld <= 32 && D % 8 == 0 && al && dsmem_l <= 200 * 1024) {
+  if (ld <= 32 && D % 8 == 0 && n % 16 == 0 && al && dsmem_l <= 200 * 1024) {
     const int dsmem = (int)dsmem_l;
     if (int rc = ensure_smem((const void*)slash_score_dmma_kernel<T>, dsmem, "slash_score_kernel")) return rc;
     {
