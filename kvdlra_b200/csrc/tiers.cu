@@ -290,6 +290,155 @@ __global__ void __launch_bounds__(256) mid_hat_tiled_kernel(
   }
 }
 
+// Pair store of two consecutive outputs (the accumulator fragment's columns 2t, 2t+1).
+template <typename T> KVD_DEVICE void store_pair(T* p, float a, float b);
+template <> KVD_DEVICE void store_pair<float>(float* p, float a, float b) {
+  *reinterpret_cast<float2*>(p) = make_float2(a, b);
+}
+template <> KVD_DEVICE void store_pair<__nv_bfloat16>(__nv_bfloat16* p, float a, float b) {
+  *reinterpret_cast<__nv_bfloat162*>(p) = __floats2bfloat162_rn(a, b);
+}
+
+// The middle reconstruction on warp-level TF32 MMA (SPLIT = 3xTF32 products
+// for fp32 models): K = RoPE(C_k U_k,g^T), V = C_v U_v,g^T for 64-token
+// tiles of one problem, every group's basis rows staged once per CTA (the
+// CTA walks `tpc` tiles).  Warps take (group, 16-token row block, K or V)
+// tasks: the product in accumulator fragments (a lane holds columns 2t, 2t+1
+// of each 8-column block, so the rotate-half partners d, d + D/2 are its
+// own), RoPE on the key fragments, paired stores.
+constexpr int kMhmThreads = 256;
+
+struct MhmSmem { int ldc, cp, uk, uv, ck, cv, cosb, sinb, posb, total; };
+__host__ __device__ inline MhmSmem mhm_smem(int n, int D, int ld) {
+  MhmSmem m;
+  m.ldc = ld + 4;  // fragment reads (4g + t) conflict-free
+  m.cp = D / 2 + 4;
+  m.uk = 0;
+  m.uv = m.uk + n * m.ldc;
+  m.ck = m.uv + n * m.ldc;
+  m.cv = m.ck + kMhTok * m.ldc;
+  m.cosb = m.cv + kMhTok * m.ldc;
+  m.sinb = m.cosb + kMhTok * m.cp;
+  m.posb = m.sinb + kMhTok * m.cp;
+  m.total = m.posb + kMhTok;
+  return m;
+}
+
+template <typename T, int D, bool SPLIT>
+__global__ void __launch_bounds__(kMhmThreads) mid_hat_mma_kernel(
+    const float* uk, const float* uv, long u_sp, int ld, const int* rk, const int* rv,
+    const float* ck, const float* cv, long c_sp, const int* mid_pos, long mid_sp, int pos_base,
+    int W, int H, const float* inv_freq, float scale, T* ok, T* ov, long ob, long oh, long ot,
+    int l0, int tpc) {
+  constexpr int half = D / 2, NT = D / 8, HT = D / 16;
+  extern __shared__ __align__(16) float hsm[];
+  const int p = blockIdx.y;
+  const int n = H * D;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int gq = lane >> 2, tq = lane & 3;
+  const int r_k = rk[p], r_v = rv[p];
+  const MhmSmem L = mhm_smem(n, D, ld);
+  const int ldc = L.ldc, cp = L.cp;
+  float* usk = hsm + L.uk;
+  float* usv = hsm + L.uv;
+  float* ckb = hsm + L.ck;
+  float* cvb = hsm + L.cv;
+  float* cosb = hsm + L.cosb;
+  float* sinb = hsm + L.sinb;
+  int* posb = reinterpret_cast<int*>(hsm + L.posb);
+  const float* Uk = uk + p * u_sp;
+  const float* Uv = uv + p * u_sp;
+  for (int e = tid; e < n * ld; e += kMhmThreads) {  // basis rows, columns past the rank zero
+    const int row = e / ld, c = e % ld;
+    const float xk = Uk[(long)row * ld + c], xv = Uv[(long)row * ld + c];
+    usk[row * ldc + c] = c < r_k ? (SPLIT ? xk : __uint_as_float(tf32_bits(xk))) : 0.f;
+    usv[row * ldc + c] = c < r_v ? (SPLIT ? xv : __uint_as_float(tf32_bits(xv))) : 0.f;
+  }
+  const int nm = (W + kMhTok - 1) / kMhTok;
+  const int t_begin = blockIdx.x * tpc, t_end = min(nm, t_begin + tpc);
+  for (int tile = t_begin; tile < t_end; ++tile) {
+    const int j0 = tile * kMhTok, ntok = min(kMhTok, W - j0);
+    __syncthreads();  // the previous tile is written out
+    for (int e = tid; e < kMhTok * ld; e += kMhmThreads) {
+      const int tt = e / ld, c = e % ld;
+      float xk = 0.f, xv = 0.f;
+      if (tt < ntok) {
+        const long gidx = p * c_sp + (long)(j0 + tt) * ld + c;
+        if (c < r_k) xk = ck[gidx];
+        if (c < r_v) xv = cv[gidx];
+      }
+      ckb[tt * ldc + c] = SPLIT ? xk : __uint_as_float(tf32_bits(xk));
+      cvb[tt * ldc + c] = SPLIT ? xv : __uint_as_float(tf32_bits(xv));
+    }
+    for (int tt = tid; tt < kMhTok; tt += kMhmThreads)
+      posb[tt] = tt < ntok ? (mid_pos ? mid_pos[p * mid_sp + j0 + tt] : pos_base + j0 + tt) : 0;
+    __syncthreads();
+    for (int e = tid; e < kMhTok * half; e += kMhmThreads) {
+      const int tt = e / half, f = e % half;
+      float c = 1.f, sn = 0.f;
+      rope_cs(posb[tt], inv_freq[f], scale, &c, &sn);
+      cosb[tt * cp + f] = c;
+      sinb[tt * cp + f] = sn;
+    }
+    __syncthreads();
+    // tasks: (group, row block, keys / values)
+    for (int task = warp; task < H * 4 * 2; task += kMhmThreads / 32) {
+      const int kv = task & 1, rb = (task >> 1) & 3, g = task >> 3;
+      const float* cb = kv ? cvb : ckb;
+      const float* ub = kv ? usv : usk;
+      const int rr = kv ? r_v : r_k;
+      const int tt0 = rb * 16 + gq, tt1 = tt0 + 8;
+      float acc[NT][4];
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) acc[j][q] = 0.f;
+      const int nkk = (rr + 7) / 8;
+      for (int kk = 0; kk < nkk; ++kk) {
+        const int c0 = kk * 8 + tq;
+        const float af[4] = {cb[tt0 * ldc + c0], cb[tt1 * ldc + c0], cb[tt0 * ldc + c0 + 4],
+                             cb[tt1 * ldc + c0 + 4]};
+        if constexpr (SPLIT) {
+#pragma unroll
+          for (int j = 0; j < NT; ++j) {
+            const float* ur = ub + (g * D + j * 8 + gq) * ldc + c0;
+            mma_f32<true>(acc[j], af, ur[0], ur[4]);
+          }
+        } else {
+          const uint32_t ah[4] = {__float_as_uint(af[0]), __float_as_uint(af[1]),
+                                  __float_as_uint(af[2]), __float_as_uint(af[3])};
+#pragma unroll
+          for (int j = 0; j < NT; ++j) {
+            const float* ur = ub + (g * D + j * 8 + gq) * ldc + c0;
+            mma_tf32(acc[j], ah, __float_as_uint(ur[0]), __float_as_uint(ur[4]));
+          }
+        }
+      }
+      if (!kv) {  // RoPE at each row's true position on the pairs (8j + 2t + e, + D/2)
+#pragma unroll
+        for (int j = 0; j < HT; ++j) {
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int f = 8 * j + 2 * tq + e;
+            float y1, y2;
+            rope_apply_pair(acc[j][e], acc[j + HT][e], cosb[tt0 * cp + f], sinb[tt0 * cp + f], &y1, &y2);
+            acc[j][e] = y1; acc[j + HT][e] = y2;
+            rope_apply_pair(acc[j][2 + e], acc[j + HT][2 + e], cosb[tt1 * cp + f], sinb[tt1 * cp + f], &y1, &y2);
+            acc[j][2 + e] = y1; acc[j + HT][2 + e] = y2;
+          }
+        }
+      }
+      T* o = (kv ? ov : ok) + p * ob + g * oh;
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+        const int d = 8 * j + 2 * tq;
+        if (tt0 < ntok) store_pair<T>(o + (long)(l0 + j0 + tt0) * ot + d, acc[j][0], acc[j][1]);
+        if (tt1 < ntok) store_pair<T>(o + (long)(l0 + j0 + tt1) * ot + d, acc[j][2], acc[j][3]);
+      }
+    }
+  }
+}
+
 }  // namespace kvd
 
 namespace kvd_host {
@@ -381,7 +530,28 @@ int launch_peek(const kvd_config& c, const kvd_buffers& b, const kvd_counters& k
     const bool tiled = (D == 64 || D == 128) && ob % fp == 0 && oh % fp == 0 && ot % fp == 0 &&
                        reinterpret_cast<uintptr_t>(okp) % (fp * sizeof(T)) == 0 &&
                        reinterpret_cast<uintptr_t>(ovp) % (fp * sizeof(T)) == 0;
-    if (tiled) {
+    const MhmSmem hm = mhm_smem(n, D, ld);
+    const bool mma = tiled && ld % 8 == 0 && 4L * hm.total <= 200 * 1024 &&
+                     reinterpret_cast<uintptr_t>(okp) % (2 * sizeof(T)) == 0 &&
+                     reinterpret_cast<uintptr_t>(ovp) % (2 * sizeof(T)) == 0 && ob % 2 == 0 &&
+                     oh % 2 == 0 && ot % 2 == 0;
+    if (mma) {
+      constexpr bool kSplit = sizeof(T) == 4;
+      auto fn = D == 64 ? mid_hat_mma_kernel<T, 64, kSplit> : mid_hat_mma_kernel<T, 128, kSplit>;
+      if (int rc2 = ensure_smem((const void*)fn, 4 * hm.total, "mid_hat_kernel")) return rc2;
+      const int nm = (k.w_len + kMhTok - 1) / kMhTok;
+      int tpc = (int)(((long)nm * count + 2 * 148 - 1) / (2 * 148));  // about two waves of CTAs
+      tpc = tpc < 1 ? 1 : (tpc > 8 ? 8 : tpc);
+      dim3 grid((nm + tpc - 1) / tpc, count);
+      {
+        KTimerScope kts_("mid_hat_kernel", s);
+        fn<<<grid, kMhmThreads, 4 * hm.total, s>>>(
+          b.u_k[k.u_sel] + p0 * u_sp, b.u_v[k.u_sel] + p0 * u_sp, u_sp, ld, b.r_k + p0,
+          b.r_v + p0, b.c_k + p0 * c_sp, b.c_v + p0 * c_sp, c_sp,
+          track_pos ? b.mid_pos + (long)p0 * c.w_cap : nullptr, c.w_cap, pos_base, k.w_len, H,
+          c.inv_freq, c.rope_scaling, okp, ovp, ob, oh, ot, l0, tpc);
+      }
+    } else if (tiled) {
       const int smem = 4 * (2 * ld * kMhCtPitch + 2 * ld * D + kMhTok * half * 2);
       auto fn = D == 64 ? mid_hat_tiled_kernel<T, 64> : mid_hat_tiled_kernel<T, 128>;
       if (int rc2 = ensure_smem((const void*)fn, smem, "mid_hat_kernel")) return rc2;
