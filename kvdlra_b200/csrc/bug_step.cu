@@ -1019,7 +1019,9 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
     __syncthreads();
     const double trace = red[0];
     // right-looking Cholesky on the lower triangle (pivots at or below 1e-14
-    // of the trace taken as null, as for the small blocks)
+    // of the trace taken as null, as for the small blocks); the scaled column
+    // j of the factor goes to row j of the (unused) upper triangle in the same
+    // pass as the update, which scales its products by 1/pivot^2 itself
     for (int j = 0; j < b; ++j) {
       if (tid == 0) {
         const double piv = G[j * ldgb + j];
@@ -1028,20 +1030,19 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
         red[1] = t > 0.0 ? 1.0 / t : 0.0;
       }
       __syncthreads();
-      const double rt = red[1];
-      for (int i = j + 1 + tid; i < b; i += nthr) G[i * ldgb + j] *= rt;
-      __syncthreads();
+      const double rt = red[1], rt2 = rt * rt;
+      for (int i = j + 1 + tid; i < b; i += nthr) G[j * ldgb + i] = G[i * ldgb + j] * rt;
       const int w = b - j - 1;
       for (int e = tid; e < w * w; e += nthr) {
         const int i = j + 1 + e / w, k = j + 1 + e % w;
-        if (k <= i) G[i * ldgb + k] = fma(-G[i * ldgb + j], G[k * ldgb + j], G[i * ldgb + k]);
+        if (k <= i) G[i * ldgb + k] = fma(-G[i * ldgb + j] * rt2, G[k * ldgb + j], G[i * ldgb + k]);
       }
       __syncthreads();
     }
     float* Tf = region(kRgTf);
-    for (int e = tid; e < b * b; e += nthr) {  // column c of T = L^T: rows k <= c
+    for (int e = tid; e < b * b; e += nthr) {  // column c of T = L^T: T[k][c] = L[c][k], k <= c
       const int c = e / b, k = e % b;
-      Tf[(long)c * ldrT + k] = k <= c ? (float)G[c * ldgb + k] : 0.f;
+      Tf[(long)c * ldrT + k] = k < c ? (float)G[k * ldgb + c] : (k == c ? (float)G[c * ldgb + c] : 0.f);
     }
     __syncthreads();
   } else if (tr) {
@@ -1077,12 +1078,28 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
       __syncthreads();
       for (long e = tid; e < (long)b * n; e += nthr) XR[e] = Rm[e];  // R, contiguous columns
       __syncthreads();
-      for (long e = tid; e < (long)b * n; e += nthr) {  // R V into the augmented columns
-        const int j = (int)(e / n), i = (int)(e % n);
-        const float* vj = Tf + (long)j * ldrT + voffT;
-        float acc = 0.f;
-        for (int l = 0; l < b; ++l) acc = fmaf(XR[(long)l * n + i], vj[l], acc);
-        Rm[(long)j * ldr + i] = acc;
+      const int bq = (b + 3) / 4;
+      for (long e = tid; e < (long)bq * n; e += nthr) {  // R V into the augmented columns,
+        const int jq = (int)(e / n), i = (int)(e % n);   // four columns per thread
+        const int j0 = 4 * jq;
+        const float* v0 = Tf + (long)j0 * ldrT + voffT;
+        const bool h1 = j0 + 1 < b, h2 = j0 + 2 < b, h3 = j0 + 3 < b;
+        const float* v1 = h1 ? v0 + ldrT : v0;
+        const float* v2 = h2 ? v0 + 2 * ldrT : v0;
+        const float* v3 = h3 ? v0 + 3 * ldrT : v0;
+        float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll 4
+        for (int l = 0; l < b; ++l) {
+          const float x = XR[(long)l * n + i];
+          a0 = fmaf(x, v0[l], a0);
+          a1 = fmaf(x, v1[l], a1);
+          a2 = fmaf(x, v2[l], a2);
+          a3 = fmaf(x, v3[l], a3);
+        }
+        Rm[(long)j0 * ldr + i] = a0;
+        if (h1) Rm[(long)(j0 + 1) * ldr + i] = a1;
+        if (h2) Rm[(long)(j0 + 2) * ldr + i] = a2;
+        if (h3) Rm[(long)(j0 + 3) * ldr + i] = a3;
       }
       for (int e = tid; e < b * b; e += nthr) {  // and V below them, the Jacobi's start
         const int j = e / b, l = e % b;
