@@ -901,8 +901,8 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
   // of the trace taken as null) and the one-sided Jacobi runs on T's b
   // columns of length b -- T has R's singular values and right vectors,
   // R V = Q1 U_T S -- in one warp's registers.  17..kMaxGramB tokens (the
-  // pre-fill blocks): the same factorisation by the CTA, whose Jacobi (fp64
-  // sums) gives R's right vectors to within the factor's fp32 rounding; they
+  // pre-fill blocks): the same factorisation by the CTA, whose Jacobi (on the
+  // factor's rows) gives R's right vectors to within the factor's rounding; they
   // seed the one-sided Jacobi (fp64 sums) on R V itself, whose columns are then nearly
   // orthogonal, so it converges in about one sweep to the accuracy of the
   // Jacobi on R (the factor alone loses relative accuracy in the smallest
@@ -917,7 +917,7 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
   const int ldr = chol ? jacobi_pitch(voff + b, b, false) : jacobi_pitch(voff + nsv, nsv, true);
   const int ldr0 = (tr || chol || bigg) ? n : ldr;  // pitch the residual is formed with
   float* Tm = chol ? part + 2 * (16 * 17 + 8) : Rm;  // the factor, augmented columns (after the Gram)
-  const int voffT = (b + 3) & ~3, ldrT = jacobi_pitch(voffT + b, b, false);  // bigg: the factor's pitch
+  const int voffT = (b + 3) & ~3, ldrT = jacobi_pitch(voffT, b, false);  // bigg: T^T's column pitch
   // ----- residual R = (I - U U^T)^2 X (the reference's re-orthogonalised residual)
   if (r > 0) cta_tn(r, b, n, Uc, lda, XR, ldb, true, AS, b16, 0.f, part);  // a = U^T X
   cta_rows_sub(n, b, b16, r, Uc, lda, AS, b16, XR, ldb, Rm, ldr0, true, r > 0);  // R = X - U a
@@ -1040,9 +1040,9 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
       __syncthreads();
     }
     float* Tf = region(kRgTf);
-    for (int e = tid; e < b * b; e += nthr) {  // column c of T = L^T: T[k][c] = L[c][k], k <= c
+    for (int e = tid; e < b * b; e += nthr) {  // column c of T^T = L: L[k][c], k >= c
       const int c = e / b, k = e % b;
-      Tf[(long)c * ldrT + k] = k < c ? (float)G[k * ldgb + c] : (k == c ? (float)G[c * ldgb + c] : 0.f);
+      Tf[(long)c * ldrT + k] = k > c ? (float)G[c * ldgb + k] : (k == c ? (float)G[c * ldgb + c] : 0.f);
     }
     __syncthreads();
   } else if (tr) {
@@ -1073,8 +1073,30 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
   } else {
     if (bigg) {
       float* Tf = region(kRgTf);
-      // a preconditioner only (the Jacobi on R V below sets the accuracy): fp32 sums
-      cta_hestenes_any<float>(Tf, b, voffT, b, ldrT, 1.2e-7f * sqrtf((float)b) + 2.4e-7f, 30, inv_x2);
+      // a preconditioner only (the Jacobi on R V below sets the accuracy), fp32
+      // sums: one-sided Jacobi on T^T (T's rows), nothing accumulated -- with
+      // T = U_T S V_T^T the rotated columns are V_T S, so V_T = the columns over
+      // their norms.  A numerically null column leaves V_T = I (no preconditioning).
+      cta_hestenes_any<float>(Tf, b, voffT, b, ldrT, 1.2e-7f * sqrtf((float)b) + 2.4e-7f, 30, inv_x2,
+                              false);
+      __syncthreads();
+      cta_colnorm_order(Tf, b, b, ldrT, sv, ordh);  // sv = the column norms (order unused)
+      if (tid == 0) {
+        double smax = 0.0;
+        for (int j = 0; j < b; ++j) smax = fmax(smax, sv[j]);
+        int deg = !(smax > 0.0);
+        for (int j = 0; j < b; ++j) deg |= !(sv[j] > 1e-6 * smax);
+        s_degenerate = deg;
+      }
+      __syncthreads();
+      if (s_degenerate) {
+        for (int e = tid; e < b * ldrT; e += nthr) Tf[e] = (e / ldrT == e % ldrT) ? 1.f : 0.f;
+      } else {
+        for (int e = tid; e < b * b; e += nthr) {
+          const int j = e / b, l = e % b;
+          Tf[(long)j * ldrT + l] = (float)((double)Tf[(long)j * ldrT + l] / sv[j]);
+        }
+      }
       __syncthreads();
       for (long e = tid; e < (long)b * n; e += nthr) XR[e] = Rm[e];  // R, contiguous columns
       __syncthreads();
@@ -1082,7 +1104,7 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
       for (long e = tid; e < (long)bq * n; e += nthr) {  // R V into the augmented columns,
         const int jq = (int)(e / n), i = (int)(e % n);   // four columns per thread
         const int j0 = 4 * jq;
-        const float* v0 = Tf + (long)j0 * ldrT + voffT;
+        const float* v0 = Tf + (long)j0 * ldrT;
         const bool h1 = j0 + 1 < b, h2 = j0 + 2 < b, h3 = j0 + 3 < b;
         const float* v1 = h1 ? v0 + ldrT : v0;
         const float* v2 = h2 ? v0 + 2 * ldrT : v0;
@@ -1103,7 +1125,7 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
       }
       for (int e = tid; e < b * b; e += nthr) {  // and V below them, the Jacobi's start
         const int j = e / b, l = e % b;
-        Rm[(long)j * ldr + voff + l] = Tf[(long)j * ldrT + voffT + l];
+        Rm[(long)j * ldr + voff + l] = Tf[(long)j * ldrT + l];
       }
       __syncthreads();
     }
@@ -1503,7 +1525,7 @@ static StepPlan plan_bug_step(int n, int b, int ld, long pool_max_floats) {
   // their rotations below
   const bool big_chol = b > 16 && b <= kMaxGramB && b <= n;
   fl[kRgGram] = big_chol ? 2L * b * (b + 1) : 0;
-  fl[kRgTf] = big_chol ? (long)b * jacobi_pitch(((b + 3) & ~3) + b, b, false) : 0;
+  fl[kRgTf] = big_chol ? (long)b * jacobi_pitch((b + 3) & ~3, b, false) : 0;
   long wo = 0;
   for (int g = 0; g < kRgCount; ++g) {
     P.ws[g] = g == kRgUs ? -1 : wo;
