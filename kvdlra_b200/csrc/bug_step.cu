@@ -276,8 +276,9 @@ static __device__ __forceinline__ void warp_gram16_slice(const float* Rm, int n,
 // Right-looking Cholesky of the b x b (b <= 16) fp64 Gram G (pitch ldg) by
 // one warp in registers: lane j holds column j; each step broadcasts the
 // pivot column by shuffles (a pivot at or below 1e-14 of the trace is taken
-// as null: its column of the factor is zero).  Writes T = L^T into the
-// columns of Tm (column c, rows k <= c; zero below).  Call from warp 0 only.
+// as null: its column of the factor is zero).  Writes L's columns (the rows
+// of T = L^T) into the columns of Tm (column c, rows k >= c; zero above).
+// Call from warp 0 only.
 static __device__ __noinline__ void warp_cholesky16(const double* G, int ldg, int b, float* Tm,
                                                     int ldr) {
   constexpr unsigned kAll = 0xffffffffu;
@@ -310,10 +311,10 @@ static __device__ __noinline__ void warp_cholesky16(const double* G, int ldg, in
     }
     }
   }
-  if (lane < b) {  // lane k holds column k of L: T[k][c] = L[c][k] for c >= k
+  if (lane < b) {  // lane c holds column c of L: L[k][c] for k >= c
 #pragma unroll
-    for (int c = 0; c < 16; ++c)
-      if (c < b) Tm[c * ldr + lane] = c >= lane ? (float)a[c] : 0.f;
+    for (int k = 0; k < 16; ++k)
+      if (k < b) Tm[lane * ldr + k] = k >= lane ? (float)a[k] : 0.f;
   }
   __syncwarp();
 }
@@ -899,8 +900,8 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
   // Blocks of up to 16 tokens (the absorb block): the fp64 Gram R^T R
   // (tensor-core products) is factored T^T T (Cholesky, pivots below 1e-14
   // of the trace taken as null) and the one-sided Jacobi runs on T's b
-  // columns of length b -- T has R's singular values and right vectors,
-  // R V = Q1 U_T S -- in one warp's registers.  17..kMaxGramB tokens (the
+  // rows (the columns of L = T^T) -- T has R's singular values and right
+  // vectors, and the rotated rows are V S -- in one warp's registers.  17..kMaxGramB tokens (the
   // pre-fill blocks): the same factorisation by the CTA, whose Jacobi (on the
   // factor's rows) gives R's right vectors to within the factor's rounding; they
   // seed the one-sided Jacobi (fp64 sums) on R V itself, whose columns are then nearly
@@ -1058,15 +1059,17 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
   if (chol) {
     if (voff + b <= 32) {  // the whole factor fits one warp's registers
       if (warp == 0) {
-        const int w = warp_hestenes16(Tm, b, voff, b, ldr, 1.2e-7f * sqrtf((float)b) + 2.4e-7f, 30,
+        // on L's columns (T's rows), nothing accumulated (no rotation rows below
+        // the 32 a warp holds): with T = U_T S V^T the rotated columns are V S
+        const int w = warp_hestenes16(Tm, b, 32, b, ldr, 1.2e-7f * sqrtf((float)b) + 2.4e-7f, 30,
                                       inv_x2);
         if (lane == 0) s_m = w;
       }
       __syncthreads();
       sw = s_m;
-    } else {
+    } else {  // (not reached for b <= 16) the same, by the CTA
       sw = cta_hestenes_any<float>(Tm, b, voff, b, ldr, 1.2e-7f * sqrtf((float)b) + 2.4e-7f, 30,
-                                   inv_x2);
+                                   inv_x2, false);
     }
     __syncthreads();
     cta_colnorm_order(Tm, b, b, ldr, sv, ordh);
@@ -1163,12 +1166,12 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
   for (long e = tid; e < (long)m * n; e += nthr) {
     const int j = (int)(e / n), i = (int)(e % n);
     const int oj = ordh[j];
-    if (chol) {       // q_j = R v_j / s_j
+    if (chol) {       // q_j = R v_j / s_j = R x_j / s_j^2, x_j = s_j v_j the rotated column
       const double sj = sv[oj];
-      const float* vj = Tm + (long)oj * ldr + voff;
+      const float* xj = Tm + (long)oj * ldr;
       float acc = 0.f;
-      for (int l = 0; l < b; ++l) acc = fmaf(Rm[(long)l * n + i], vj[l], acc);
-      Q[e] = sj > 0.0 ? (float)((double)acc / sj) : 0.f;
+      for (int l = 0; l < b; ++l) acc = fmaf(Rm[(long)l * n + i], xj[l], acc);
+      Q[e] = sj > 0.0 ? (float)((double)acc / (sj * sj)) : 0.f;
     } else if (!tr) {  // q_j = (R V)[:, o_j] / s_j
       const double sj = sv[oj];
       Q[e] = sj > 0.0 ? (float)(Rm[(long)oj * ldr + i] / sj) : 0.f;
@@ -1191,8 +1194,8 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
       else v = AS[c * b16 + (row - r)];
     } else if (row >= r) {  // s_j v_j^T, the residual's right part
       const int oj = ordh[c - r], l = row - r;
-      const float* vsrc = chol ? Tm : Rm;
-      v = tr ? Rm[(long)oj * ldr + l] : (float)sv[oj] * vsrc[(long)oj * ldr + voff + l];
+      v = tr ? Rm[(long)oj * ldr + l]
+             : (chol ? Tm[(long)oj * ldr + l] : (float)sv[oj] * Rm[(long)oj * ldr + voff + l]);
     }
     BT[(long)c * ldbt + row] = v;
   }
