@@ -76,6 +76,27 @@ __device__ __forceinline__ bool named_barrier_or(int id, int nthreads, bool pred
   return any != 0;
 }
 
+// The rotation that zeroes a pair's inner product g (d = beta - alpha, g2 =
+// 2 g), the smaller of the two angles (|theta| <= pi/4): with rho = 1 /
+// sqrt(d^2 + g2^2), cos 2theta = |d| rho and sin 2theta = sgn(d) g2 rho, so
+// c = sqrt(x) and s = sin 2theta / (2 c) with x = (1 + cos 2theta) / 2, both
+// from one reciprocal square root of x.  A pair whose d and g2 are both
+// tiny is rescaled first (the angle depends only on their ratio) so the
+// squares cannot underflow.  One Newton step renormalises c^2 + s^2 to 1.
+__device__ __forceinline__ void jacobi_rotation(float d, float g2, float& c, float& s) {
+  const float sc = fmaxf(fabsf(d), fabsf(g2)) < 1e-15f ? 1e20f : 1.f;
+  d *= sc;
+  g2 *= sc;
+  const float rho = rsqrtf(fmaf(d, d, g2 * g2));
+  const float x = fmaf(0.5f * fabsf(d), rho, 0.5f);
+  const float ic = rsqrtf(x);
+  c = x * ic;
+  s = copysignf(0.5f, d) * g2 * rho * ic;
+  const float f = fmaf(-0.5f, fmaf(c, c, s * s), 1.5f);
+  c *= f;
+  s *= f;
+}
+
 // Register tile of the one-sided Jacobi for `cols` columns of `nut` 4-float
 // units: lanes per pair G (about eight warps' worth of pairs, at most 9 units
 // per lane) and units per lane NU (0 = stream from shared memory).  The
@@ -209,16 +230,8 @@ static __device__ __forceinline__ int cta_hestenes(float* X, int len, int voff, 
         ga *= is2;
         const bool live = active && al > (ACC)kJacobiFloor && be > (ACC)kJacobiFloor;
         if (!live || ga * ga <= tol2 * al * be) continue;
-        // t = tan(theta) = sgn(d) 2g / (|d| + sqrt(d^2 + 4 g^2)), d = be - al, g = ga
-        // (the smaller root of t^2 + (d/g) t - 1 = 0, zeroing the pair's product)
-        const float d = (float)be - (float)al, g2 = 2.f * (float)ga;
-        const float rr = fmaf(d, d, g2 * g2);
-        const float hyp = rr * rsqrtf(rr);
-        const float t = copysignf(1.f, d) * g2 * __fdividef(1.f, fabsf(d) + hyp);
-        float c = rsqrtf(fmaf(t, t, 1.f)), s = c * t;
-        const float f = fmaf(-0.5f, fmaf(c, c, s * s), 1.5f);  // Newton step to unit norm
-        c *= f;
-        s *= f;
+        float c, s;
+        jacobi_rotation((float)be - (float)al, 2.f * (float)ga, c, s);
         if constexpr (NU > 0) {
 #pragma unroll
           for (int t2 = 0; t2 < NU; ++t2) {
@@ -373,14 +386,8 @@ static __device__ __noinline__ int warp_hestenes16(float* X, int len, int voff, 
       ga *= is2;
       const bool live = slot < half && al > kJacobiFloor && be > kJacobiFloor;
       if (live && ga * ga > tol2 * al * be) {
-        const float d = be - al, g2 = 2.f * ga;
-        const float rr = fmaf(d, d, g2 * g2);
-        const float hyp = rr * rsqrtf(rr);
-        const float t = copysignf(1.f, d) * g2 * __fdividef(1.f, fabsf(d) + hyp);
-        float c = rsqrtf(fmaf(t, t, 1.f)), sn = c * t;
-        const float f = fmaf(-0.5f, fmaf(c, c, sn * sn), 1.5f);  // Newton step to unit norm
-        c *= f;
-        sn *= f;
+        float c, sn;
+        jacobi_rotation(be - al, 2.f * ga, c, sn);
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const float a = tp[k], bq = bt[k];
