@@ -332,15 +332,16 @@ static __device__ __noinline__ void warp_cholesky16(const double* G, int ldg, in
   __syncwarp();
 }
 
-// One-sided Jacobi for up to 16 columns of at most 32 augmented rows (data
+// One-sided Jacobi for up to 16 columns of at most 4 RK augmented rows (data
 // rows [0, len), zero to voff, rotations accumulated in rows [voff,
 // voff + cols)), run by one warp entirely in registers.  Slot i (lanes
-// 4i .. 4i+3) holds the pair (top, bottom); lane 4i + g holds rows g + 4k of
-// both.  Rounds follow the circle method (position 0 fixed, the others
+// 4i .. 4i+3) holds the pair (top, bottom); lane 4i + g holds rows g + 4k
+// (k < RK) of both.  Rounds follow the circle method (position 0 fixed, the others
 // advancing one position per round, so np - 1 rounds meet every pair), the
 // columns moving between slots by warp shuffles instead of through shared
 // memory.  Rotation, tolerance, null floor and early stop are cta_hestenes's.
 // Call from warp 0 only; writes the columns back to X and returns the sweeps.
+template <int RK>
 static __device__ __noinline__ int warp_hestenes16(float* X, int len, int voff, int cols, int ldx,
                                                    float tol, int max_sweeps, double inv_scale2) {
   constexpr unsigned kAll = 0xffffffffu;
@@ -354,14 +355,14 @@ static __device__ __noinline__ int warp_hestenes16(float* X, int len, int voff, 
   }
   const int np = cols + (cols & 1), half = np / 2;
   int ti = slot < half ? slot : np, bi = slot < half ? np - 1 - slot : np;  // column indices
-  float tp[8], bt[8];
+  float tp[RK], bt[RK];
   auto value = [&](int c, int row) -> float {
     if (c >= cols) return 0.f;
     if (row < len) return X[(long)c * ldx + row];
     return (row - voff == c) ? 1.f : 0.f;
   };
 #pragma unroll
-  for (int k = 0; k < 8; ++k) {
+  for (int k = 0; k < RK; ++k) {
     tp[k] = value(ti, g + 4 * k);
     bt[k] = value(bi, g + 4 * k);
   }
@@ -373,7 +374,7 @@ static __device__ __noinline__ int warp_hestenes16(float* X, int len, int voff, 
     for (int rd = 0; rd < np - 1; ++rd) {
       float al = 0.f, be = 0.f, ga = 0.f;
 #pragma unroll
-      for (int k = 0; k < 8; ++k)
+      for (int k = 0; k < RK; ++k)
         if (g + 4 * k < voff) {
           al = fmaf(tp[k], tp[k], al);
           be = fmaf(bt[k], bt[k], be);
@@ -389,7 +390,7 @@ static __device__ __noinline__ int warp_hestenes16(float* X, int len, int voff, 
         float c, sn;
         jacobi_rotation(be - al, 2.f * ga, c, sn);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
+        for (int k = 0; k < RK; ++k) {
           const float a = tp[k], bq = bt[k];
           tp[k] = c * a - sn * bq;
           bt[k] = sn * a + c * bq;
@@ -402,7 +403,7 @@ static __device__ __noinline__ int warp_hestenes16(float* X, int len, int voff, 
       const bool first = slot == 0, second = slot == 1, last = slot == half - 1;
       if (half > 1) {
 #pragma unroll
-      for (int k = 0; k < 8; ++k) {
+      for (int k = 0; k < RK; ++k) {
         const float t_prev = __shfl_up_sync(kAll, tp[k], 4);
         const float b_prev = __shfl_up_sync(kAll, bt[k], 4);
         const float b_next = __shfl_down_sync(kAll, bt[k], 4);
@@ -423,7 +424,7 @@ static __device__ __noinline__ int warp_hestenes16(float* X, int len, int voff, 
   }
   if (slot < half) {
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
+    for (int k = 0; k < RK; ++k) {
       const int row = g + 4 * k;
       if (row < voff + cols) {
         if (ti < cols) X[(long)ti * ldx + row] = tp[k];
@@ -1066,10 +1067,10 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
   if (chol) {
     if (voff + b <= 32) {  // the whole factor fits one warp's registers
       if (warp == 0) {
-        // on L's columns (T's rows), nothing accumulated (no rotation rows below
-        // the 32 a warp holds): with T = U_T S V^T the rotated columns are V S
-        const int w = warp_hestenes16(Tm, b, 32, b, ldr, 1.2e-7f * sqrtf((float)b) + 2.4e-7f, 30,
-                                      inv_x2);
+        // on L's columns (T's rows, 16 rows held as 4 per lane), nothing
+        // accumulated: with T = U_T S V^T the rotated columns are V S
+        const int w = warp_hestenes16<4>(Tm, b, 16, b, ldr, 1.2e-7f * sqrtf((float)b) + 2.4e-7f,
+                                         30, inv_x2);
         if (lane == 0) s_m = w;
       }
       __syncthreads();
