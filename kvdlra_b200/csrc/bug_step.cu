@@ -829,17 +829,51 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
   __shared__ int s_m, s_keep, s_degenerate;
   const int tid = threadIdx.x, nthr = blockDim.x, lane = tid % 32, warp = tid / 32;
 
-  // ||X||_F^2 (fp64 accumulation of fp32 squares)
-  {
-    double acc = 0.0;
-    for (long e = tid; e < (long)b * n; e += nthr) acc += (double)X[e] * X[e];
-    acc = warp_sum(acc);
-    if (lane == 0) red[warp] = acc;
-    __syncthreads();
-    if (tid == 0) { double t = 0; for (int i = 0; i < nthr / 32; ++i) t += red[i]; s_xnorm2 = t; }
-  }
   // ----- stage the block token-transposed (XR[i][j] = X[j][i], zero past b) and U,
-  // 16-byte loads with four in flight per thread where the layout allows
+  // and ||X||_F^2 (fp64 sums of fp32 squares).  The absorb block's shapes
+  // (b n <= 16 threads' worth, n r <= 32) issue every 16-byte load -- four of
+  // the block and eight of U per thread -- before the first store and square
+  // the block from the same registers; other shapes take the loops below.
+  double xacc = 0.0;
+  const bool xvec = (n & 3) == 0 && (reinterpret_cast<unsigned long>(X) & 15) == 0;
+  const bool uvec4 = (r & 3) == 0 && (ld & 3) == 0 && (reinterpret_cast<unsigned long>(U) & 15) == 0;
+  if (us && xvec && uvec4 && b * n <= 16 * nthr && n * r <= 32 * nthr) {
+    const int nx4 = b * n / 4, r4 = r / 4, nu4 = n * r4;
+    const float4* X4 = reinterpret_cast<const float4*>(X);
+    float4 xv[4], uv[8];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int e = tid + u * nthr;
+      if (e < nx4) xv[u] = X4[e];
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int e = tid + u * nthr;
+      if (e < nu4) uv[u] = *reinterpret_cast<const float4*>(U + (long)(e / r4) * ld + 4 * (e % r4));
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int e = tid + u * nthr;
+      if (e < nx4) {
+        const float4 v = xv[u];
+        xacc += (double)v.x * v.x + (double)v.y * v.y + (double)v.z * v.z + (double)v.w * v.w;
+        const int j = 4 * e / n, i = 4 * e % n;
+        float* d = XR + i * ldb + j;
+        d[0] = v.x; d[ldb] = v.y; d[2 * ldb] = v.z; d[3 * ldb] = v.w;
+      }
+    }
+    float* dst = pool + P.smem[kRgUs];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int e = tid + u * nthr;
+      if (e < nu4) *reinterpret_cast<float4*>(dst + (e / r4) * lda + 4 * (e % r4)) = uv[u];
+    }
+    if (b16 > b) {
+      const int pad = b16 - b;
+      for (int e = tid; e < n * pad; e += nthr) XR[(e / pad) * ldb + b + e % pad] = 0.f;
+    }
+  } else {
+  for (long e = tid; e < (long)b * n; e += nthr) xacc += (double)X[e] * X[e];
   if ((n & 3) == 0 && (reinterpret_cast<unsigned long>(X) & 15) == 0) {
     const float4* X4 = reinterpret_cast<const float4*>(X);
     const long n4 = (long)b * n / 4;
@@ -899,8 +933,12 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
       }
     }
   }
+  }
+  xacc = warp_sum(xacc);
+  if (lane == 0) red[warp] = xacc;
   for (int e = tid; e < r * b16; e += nthr) { AS[e] = 0.f; A2[e] = 0.f; }
   __syncthreads();
+  if (tid == 0) { double t = 0; for (int i = 0; i < nthr / 32; ++i) t += red[i]; s_xnorm2 = t; }
   // SVD geometry.  b <= n: one-sided Jacobi on R's b columns, R V = [s_j q_j].
   // b > n (more columns than rows cannot all be made orthogonal): on the n
   // columns of R^T, R^T J = [s_j v_j], so J holds the left vectors q_j.
@@ -1171,20 +1209,43 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
   __syncthreads();
   const int m = s_m;
   float* Q = XR;  // [m][n]
-  for (long e = tid; e < (long)m * n; e += nthr) {
-    const int j = (int)(e / n), i = (int)(e % n);
-    const int oj = ordh[j];
-    if (chol) {       // q_j = R v_j / s_j = R x_j / s_j^2, x_j = s_j v_j the rotated column
-      const double sj = sv[oj];
-      const float* xj = Tm + (long)oj * ldr;
-      float acc = 0.f;
-      for (int l = 0; l < b; ++l) acc = fmaf(Rm[(long)l * n + i], xj[l], acc);
-      Q[e] = sj > 0.0 ? (float)((double)acc / (sj * sj)) : 0.f;
-    } else if (!tr) {  // q_j = (R V)[:, o_j] / s_j
-      const double sj = sv[oj];
-      Q[e] = sj > 0.0 ? (float)(Rm[(long)oj * ldr + i] / sj) : 0.f;
-    } else {           // q_j = J[:, o_j]
-      Q[e] = Rm[(long)oj * ldr + voff + i];
+  if (chol) {
+    // q_j = R v_j / s_j = R x_j / s_j^2, x_j = s_j v_j the rotated column
+    // (rows b..15 of the factor's columns are zero): 1/s_j^2 in fp64 first,
+    // then a thread per row i holds R's row and runs over the columns
+    if (tid < m) {
+      const double sj = sv[ordh[tid]];
+      nrm[tid] = sj > 0.0 ? 1.0 / (sj * sj) : 0.0;
+    }
+    __syncthreads();
+    for (int i = tid; i < n; i += nthr) {
+      float rrow[16];
+#pragma unroll
+      for (int l = 0; l < 16; ++l) rrow[l] = l < b ? Rm[l * n + i] : 0.f;
+      for (int j = 0; j < m; ++j) {
+        const float4* xj = reinterpret_cast<const float4*>(Tm + ordh[j] * ldr);
+        float acc = 0.f;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 x4 = xj[q];
+          acc = fmaf(rrow[4 * q], x4.x, acc);
+          acc = fmaf(rrow[4 * q + 1], x4.y, acc);
+          acc = fmaf(rrow[4 * q + 2], x4.z, acc);
+          acc = fmaf(rrow[4 * q + 3], x4.w, acc);
+        }
+        Q[j * n + i] = (float)((double)acc * nrm[j]);
+      }
+    }
+  } else {
+    for (long e = tid; e < (long)m * n; e += nthr) {
+      const int j = (int)(e / n), i = (int)(e % n);
+      const int oj = ordh[j];
+      if (!tr) {  // q_j = (R V)[:, o_j] / s_j
+        const double sj = sv[oj];
+        Q[e] = sj > 0.0 ? (float)(Rm[(long)oj * ldr + i] / sj) : 0.f;
+      } else {    // q_j = J[:, o_j]
+        Q[e] = Rm[(long)oj * ldr + voff + i];
+      }
     }
   }
   __syncthreads();
