@@ -709,6 +709,180 @@ static __device__ __forceinline__ void cta_basis_rows32(int n, int keep, int r, 
   __syncthreads();
 }
 
+// Register-blocked forms of the three products that turn the staged basis
+// into the polished U_new (keep <= 32 columns, n % 4 == 0, every pointer and
+// pitch 16-byte aligned): a thread owns a 4-row x 8-column tile, so one
+// 16-byte load of a coefficient row serves four rows instead of one.  Each
+// output keeps the operation order of the row-per-thread forms above (the
+// same fmaf chains over k), so the results are the same bit for bit.
+
+// Un[i][c] = sum_{k<r} Un[i][k] WU[k][c] + sum_{j<m} Q[j][i] WU[r+j][c], c < keep,
+// in place: a row's old values are read only by the four lanes that own its
+// tiles, all reads before the warp's writes.
+static __device__ __forceinline__ void cta_basis_tiles(int n, int keep, int r, int m, float* Un,
+                                                       int ldn, const float* Q, const float* WU,
+                                                       int ldw) {
+  const int tid = threadIdx.x, nthr = blockDim.x, cg = tid & 3;
+  const int ngr = n / 4;
+  for (int rg0 = 0; rg0 < ngr; rg0 += nthr / 4) {  // (uniform trip count: __syncwarp below)
+    const int rg = rg0 + tid / 4;
+    const bool live = rg < ngr;
+    const int i0 = live ? 4 * rg : 0;
+    float acc[4][8];
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+#pragma unroll
+      for (int c = 0; c < 8; ++c) acc[q][c] = 0.f;
+    auto step = [&](int k, const float (&av)[4]) {  // acc += av (x) WU[k][8cg..8cg+8)
+      const float4 w0 = *reinterpret_cast<const float4*>(WU + k * ldw + 8 * cg);
+      const float4 w1 = *reinterpret_cast<const float4*>(WU + k * ldw + 8 * cg + 4);
+      const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int c = 0; c < 8; ++c) acc[q][c] = fmaf(av[q], w[c], acc[q][c]);
+    };
+    int k = 0;
+    for (; k + 4 <= r; k += 4) {  // U's columns four at a time
+      float u4[4][4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 t = *reinterpret_cast<const float4*>(Un + (i0 + q) * ldn + k);
+        u4[q][0] = t.x; u4[q][1] = t.y; u4[q][2] = t.z; u4[q][3] = t.w;
+      }
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const float av[4] = {u4[0][kk], u4[1][kk], u4[2][kk], u4[3][kk]};
+        step(k + kk, av);
+      }
+    }
+    for (; k < r; ++k) {
+      float av[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) av[q] = Un[(i0 + q) * ldn + k];
+      step(k, av);
+    }
+    for (int j = 0; j < m; ++j) {  // then Q's rows
+      const float4 t = *reinterpret_cast<const float4*>(Q + j * n + i0);
+      const float av[4] = {t.x, t.y, t.z, t.w};
+      step(r + j, av);
+    }
+    __syncwarp();
+    if (live) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          if (8 * cg + c < keep) Un[(i0 + q) * ldn + 8 * cg + c] = acc[q][c];
+    }
+    __syncwarp();
+  }
+  __syncthreads();
+}
+
+// out[k][j] = sum_i S[i][k] S[i][j] - [k == j] for k, j < keep: the rows are
+// split into 16 slices (fp32 sums of a slice, in row order; fp64 sum of the
+// slices), a thread owns a 4 x 4 tile of one slice, eight row tiles by four
+// column tiles per pass over two passes (part holds 16 x 16 x 32 partials).
+static __device__ __forceinline__ void cta_gram_tiles(int keep, int n, const float* S, int lds,
+                                                      float* out, int ldo, float* part) {
+  const int tid = threadIdx.x, nthr = blockDim.x;
+  constexpr int ks = 16;
+  const int slice = (n + ks - 1) / ks;
+  for (int j0 = 0; j0 < 32; j0 += 16) {
+    if (j0 >= keep) break;
+    for (int it = tid; it < ks * 8 * 4; it += nthr) {  // (slice, row tile a, column tile c)
+      const int c = it & 3, a = (it >> 2) & 7, sl = it >> 5;
+      const int i0 = sl * slice, i1 = min(n, i0 + slice);
+      float acc[4][4];
+#pragma unroll
+      for (int x = 0; x < 4; ++x)
+#pragma unroll
+        for (int y = 0; y < 4; ++y) acc[x][y] = 0.f;
+      for (int i = i0; i < i1; ++i) {
+        const float4 ua = *reinterpret_cast<const float4*>(S + i * lds + 4 * a);
+        const float4 uc = *reinterpret_cast<const float4*>(S + i * lds + j0 + 4 * c);
+        const float va[4] = {ua.x, ua.y, ua.z, ua.w}, vc[4] = {uc.x, uc.y, uc.z, uc.w};
+#pragma unroll
+        for (int x = 0; x < 4; ++x)
+#pragma unroll
+          for (int y = 0; y < 4; ++y) acc[x][y] = fmaf(va[x], vc[y], acc[x][y]);
+      }
+#pragma unroll
+      for (int x = 0; x < 4; ++x)
+#pragma unroll
+        for (int y = 0; y < 4; ++y) part[(sl * 16 + 4 * c + y) * 32 + 4 * a + x] = acc[x][y];
+    }
+    __syncthreads();
+    for (int e = tid; e < 16 * 32; e += nthr) {
+      const int jj = e / 32, k = e % 32, j = j0 + jj;
+      if (j >= keep || k >= keep) continue;
+      double sum = 0.0;
+      for (int sl = 0; sl < ks; ++sl) sum += (double)part[(sl * 16 + jj) * 32 + k];
+      if (k == j) sum -= 1.0;
+      out[k * ldo + j] = (float)sum;
+    }
+    __syncthreads();
+  }
+}
+
+// Uo[i][c] = S[i][c] - 1/2 sum_k S[i][k] E[k][c] for c < keep (E zero-padded
+// to 32 x 32, row pitch lde), S in shared memory, Uo global.
+static __device__ __forceinline__ void cta_polish_tiles(int n, int keep, const float* S, int lds,
+                                                        float* Uo, int ld, bool uvec,
+                                                        const float* E, int lde) {
+  const int tid = threadIdx.x, nthr = blockDim.x, cg = tid & 3;
+  const int ngr = n / 4;
+  for (int rg = tid / 4; rg < ngr; rg += nthr / 4) {
+    const int i0 = 4 * rg;
+    float acc[4][8];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float4 t0 = *reinterpret_cast<const float4*>(S + (i0 + q) * lds + 8 * cg);
+      const float4 t1 = *reinterpret_cast<const float4*>(S + (i0 + q) * lds + 8 * cg + 4);
+      const float t[8] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w};
+#pragma unroll
+      for (int c = 0; c < 8; ++c) acc[q][c] = 8 * cg + c < keep ? t[c] : 0.f;
+    }
+    for (int k0 = 0; k0 < keep; k0 += 4) {  // (columns past keep are read, not used)
+      float h4[4][4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 t = *reinterpret_cast<const float4*>(S + (i0 + q) * lds + k0);
+        h4[q][0] = t.x; h4[q][1] = t.y; h4[q][2] = t.z; h4[q][3] = t.w;
+      }
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        if (k0 + kk < keep) {
+          const int k = k0 + kk;
+          const float4 e0 = *reinterpret_cast<const float4*>(E + k * lde + 8 * cg);
+          const float4 e1 = *reinterpret_cast<const float4*>(E + k * lde + 8 * cg + 4);
+          const float ev[8] = {e0.x, e0.y, e0.z, e0.w, e1.x, e1.y, e1.z, e1.w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float h = -0.5f * h4[q][kk];
+#pragma unroll
+            for (int c = 0; c < 8; ++c) acc[q][c] = fmaf(h, ev[c], acc[q][c]);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float* dst = Uo + (long)(i0 + q) * ld + 8 * cg;
+      if (uvec && 8 * cg + 8 <= keep) {
+        *reinterpret_cast<float4*>(dst) = make_float4(acc[q][0], acc[q][1], acc[q][2], acc[q][3]);
+        *reinterpret_cast<float4*>(dst + 4) = make_float4(acc[q][4], acc[q][5], acc[q][6], acc[q][7]);
+      } else {
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          if (8 * cg + c < keep) dst[c] = acc[q][c];
+      }
+    }
+  }
+  __syncthreads();
+}
+
 // Column norms (fp64) of X[:, 0..cols) into nrm, then order = descending.
 static __device__ __forceinline__ void cta_colnorm_order(const float* X, int len, int cols, int ldx, double* nrm,
                                          int* order) {
@@ -1310,7 +1484,12 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
   // Up to 32 columns with everything staged: U_new is formed in place of the
   // staged U (each thread owns its rows) and polished from there.
   const bool un_smem = kSmem && keep <= 32;
-  if (un_smem) {
+  const bool tiles = un_smem && n % 4 == 0 && ldp % 4 == 0 && ldw % 4 == 0 && nthr % 32 == 0;
+  if (tiles) {
+    float* Un = pool + P.smem[kRgUs];
+    cta_basis_tiles(n, keep, r, m, Un, P.ldu, Q, WU, ldw);
+    cta_gram_tiles(keep, n, Un, P.ldu, Pol, ldp, part);  // E = U^T U - I
+  } else if (un_smem) {
     float* Un = pool + P.smem[kRgUs];
     cta_basis_rows32(n, keep, r, m, Un, P.ldu, Q, WU, ldw);
     cta_tn(keep, keep, n, Un, P.ldu, Un, P.ldu, true, Pol, ldp, 1.f, part);  // E = U^T U - I
@@ -1342,7 +1521,9 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
     for (int d = 0; d < keep; ++d) corr = fmaf(Pol[(long)d * ldp + c], CB[d * b16 + j], corr);
     co[(long)j * A.coords_ld + c] = fmaf(-0.5f, corr, CB[c * b16 + j]);
   }
-  if (un_smem) {
+  if (tiles) {
+    cta_polish_tiles(n, keep, pool + P.smem[kRgUs], P.ldu, Uo, ld, uvec, Pol, ldp);
+  } else if (un_smem) {
     cta_polish_rows(n, keep, pool + P.smem[kRgUs], P.ldu, true, Uo, ld, uvec, Pol, ldp);
   } else if (keep <= 32) {
     cta_polish_rows(n, keep, Uo, ld, uvec, Uo, ld, uvec, Pol, ldp);
