@@ -780,28 +780,30 @@ static __device__ __forceinline__ void cta_basis_tiles(int n, int keep, int r, i
   __syncthreads();
 }
 
-// out[k][j] = sum_i S[i][k] S[i][j] - [k == j] for k, j < keep: the rows are
-// split into 16 slices (fp32 sums of a slice, in row order; fp64 sum of the
-// slices), a thread owns a 4 x 4 tile of one slice, eight row tiles by four
-// column tiles per pass over two passes (part holds 16 x 16 x 32 partials).
-static __device__ __forceinline__ void cta_gram_tiles(int keep, int n, const float* S, int lds,
-                                                      float* out, int ldo, float* part) {
+// out[k][j] = sum_{i<K} A[i][k] B[i][j] - diag [k == j] for k < M <= 32, j < NB
+// (cta_tn's result bit for bit with 512 threads): the rows are split into
+// 16 slices (fp32 sums of a slice, in row order; fp64 sum of the slices), a
+// thread owns a 4 x 4 tile of one slice -- eight row tiles by four column
+// tiles per pass of 16 columns (part holds 16 x 16 x 32 partials).
+static __device__ __forceinline__ void cta_tn_tiles(int M, int NB, int K, const float* A, int lda,
+                                                    const float* B, int ldb, float* out, int ldo,
+                                                    float diag, float* part) {
   const int tid = threadIdx.x, nthr = blockDim.x;
   constexpr int ks = 16;
-  const int slice = (n + ks - 1) / ks;
-  for (int j0 = 0; j0 < 32; j0 += 16) {
-    if (j0 >= keep) break;
+  const int slice = (K + ks - 1) / ks;
+  for (int j0 = 0; j0 < NB; j0 += 16) {
     for (int it = tid; it < ks * 8 * 4; it += nthr) {  // (slice, row tile a, column tile c)
       const int c = it & 3, a = (it >> 2) & 7, sl = it >> 5;
-      const int i0 = sl * slice, i1 = min(n, i0 + slice);
+      if (4 * a >= M || j0 + 4 * c >= NB) continue;
+      const int i0 = sl * slice, i1 = min(K, i0 + slice);
       float acc[4][4];
 #pragma unroll
       for (int x = 0; x < 4; ++x)
 #pragma unroll
         for (int y = 0; y < 4; ++y) acc[x][y] = 0.f;
       for (int i = i0; i < i1; ++i) {
-        const float4 ua = *reinterpret_cast<const float4*>(S + i * lds + 4 * a);
-        const float4 uc = *reinterpret_cast<const float4*>(S + i * lds + j0 + 4 * c);
+        const float4 ua = *reinterpret_cast<const float4*>(A + i * lda + 4 * a);
+        const float4 uc = *reinterpret_cast<const float4*>(B + i * ldb + j0 + 4 * c);
         const float va[4] = {ua.x, ua.y, ua.z, ua.w}, vc[4] = {uc.x, uc.y, uc.z, uc.w};
 #pragma unroll
         for (int x = 0; x < 4; ++x)
@@ -816,14 +818,79 @@ static __device__ __forceinline__ void cta_gram_tiles(int keep, int n, const flo
     __syncthreads();
     for (int e = tid; e < 16 * 32; e += nthr) {
       const int jj = e / 32, k = e % 32, j = j0 + jj;
-      if (j >= keep || k >= keep) continue;
+      if (j >= NB || k >= M) continue;
       double sum = 0.0;
       for (int sl = 0; sl < ks; ++sl) sum += (double)part[(sl * 16 + jj) * 32 + k];
-      if (k == j) sum -= 1.0;
+      if (k == j) sum -= (double)diag;
       out[k * ldo + j] = (float)sum;
     }
     __syncthreads();
   }
+}
+
+// cta_rows_sub on tiles, for 16-column blocks (b16 == 16): a thread owns
+// four rows n/4 apart (so the column-major stores of R are conflict-free)
+// by four columns; the same fmaf chain over k per output.
+static __device__ __forceinline__ void cta_rows_sub_tiles(int n, int b, int K, const float* A,
+                                                          int lda, const float* C, int ldc,
+                                                          float* XR, int ldb, float* Rm, int ldr,
+                                                          bool from_xr, bool to_xr) {
+  const int tid = threadIdx.x, nthr = blockDim.x;
+  const int ngr = n / 4;
+  for (int it = tid; it < ngr * 4; it += nthr) {
+    const int j0 = 4 * (it / ngr), rb = it % ngr;
+    float acc[4][4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int i = rb + q * ngr;
+      if (from_xr) {
+        const float4 t = *reinterpret_cast<const float4*>(XR + i * ldb + j0);
+        acc[q][0] = t.x; acc[q][1] = t.y; acc[q][2] = t.z; acc[q][3] = t.w;
+      } else {
+#pragma unroll
+        for (int y = 0; y < 4; ++y) acc[q][y] = j0 + y < b ? Rm[(j0 + y) * ldr + i] : 0.f;
+      }
+    }
+    auto step = [&](int k, const float (&av)[4]) {
+      const float4 c4 = *reinterpret_cast<const float4*>(C + k * ldc + j0);
+      const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int y = 0; y < 4; ++y) acc[q][y] = fmaf(-av[q], cv[y], acc[q][y]);
+    };
+    int k = 0;
+    for (; k + 4 <= K; k += 4) {
+      float a4[4][4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 t = *reinterpret_cast<const float4*>(A + (rb + q * ngr) * lda + k);
+        a4[q][0] = t.x; a4[q][1] = t.y; a4[q][2] = t.z; a4[q][3] = t.w;
+      }
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const float av[4] = {a4[0][kk], a4[1][kk], a4[2][kk], a4[3][kk]};
+        step(k + kk, av);
+      }
+    }
+    for (; k < K; ++k) {
+      float av[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) av[q] = A[(rb + q * ngr) * lda + k];
+      step(k, av);
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int i = rb + q * ngr;
+#pragma unroll
+      for (int y = 0; y < 4; ++y)
+        if (j0 + y < b) Rm[(j0 + y) * ldr + i] = acc[q][y];
+      if (to_xr)
+        *reinterpret_cast<float4*>(XR + i * ldb + j0) =
+            make_float4(acc[q][0], acc[q][1], acc[q][2], acc[q][3]);
+    }
+  }
+  __syncthreads();
 }
 
 // Uo[i][c] = S[i][c] - 1/2 sum_k S[i][k] E[k][c] for c < keep (E zero-padded
@@ -1140,11 +1207,24 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
   float* Tm = chol ? part + 2 * (16 * 17 + 8) : Rm;  // the factor, augmented columns (after the Gram)
   const int voffT = (b + 3) & ~3, ldrT = jacobi_pitch(voffT, b, false);  // bigg: T^T's column pitch
   // ----- residual R = (I - U U^T)^2 X (the reference's re-orthogonalised residual)
-  if (r > 0) cta_tn(r, b, n, Uc, lda, XR, ldb, true, AS, b16, 0.f, part);  // a = U^T X
-  cta_rows_sub(n, b, b16, r, Uc, lda, AS, b16, XR, ldb, Rm, ldr0, true, r > 0);  // R = X - U a
+  // the tiled forms when U is staged (16-byte rows of at least 32 floats), the
+  // block has 16 columns and the rank is at most 32
+  const bool ptiles = us && r <= 32 && lda >= 32 && lda % 4 == 0 && b16 == 16 && n % 4 == 0 &&
+                      ldb % 4 == 0 && nthr == kStepThreads;
+  if (r > 0) {  // a = U^T X
+    if (ptiles) cta_tn_tiles(r, b, n, Uc, lda, XR, ldb, AS, b16, 0.f, part);
+    else cta_tn(r, b, n, Uc, lda, XR, ldb, true, AS, b16, 0.f, part);
+  }
+  if (ptiles) cta_rows_sub_tiles(n, b, r, Uc, lda, AS, b16, XR, ldb, Rm, ldr0, true, r > 0);
+  else cta_rows_sub(n, b, b16, r, Uc, lda, AS, b16, XR, ldb, Rm, ldr0, true, r > 0);  // R = X - U a
   if (r > 0) {
-    cta_tn(r, b, n, Uc, lda, XR, ldb, true, A2, b16, 0.f, part);             // a2 = U^T R
-    cta_rows_sub(n, b, b16, r, Uc, lda, A2, b16, XR, ldb, Rm, ldr0, false, false);  // R -= U a2
+    if (ptiles) {  // a2 = U^T R, R -= U a2
+      cta_tn_tiles(r, b, n, Uc, lda, XR, ldb, A2, b16, 0.f, part);
+      cta_rows_sub_tiles(n, b, r, Uc, lda, A2, b16, XR, ldb, Rm, ldr0, false, false);
+    } else {
+      cta_tn(r, b, n, Uc, lda, XR, ldb, true, A2, b16, 0.f, part);
+      cta_rows_sub(n, b, b16, r, Uc, lda, A2, b16, XR, ldb, Rm, ldr0, false, false);
+    }
     for (int e = tid; e < r * b16; e += nthr) AS[e] += A2[e];
     __syncthreads();
   }
@@ -1484,11 +1564,11 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
   // Up to 32 columns with everything staged: U_new is formed in place of the
   // staged U (each thread owns its rows) and polished from there.
   const bool un_smem = kSmem && keep <= 32;
-  const bool tiles = un_smem && n % 4 == 0 && ldp % 4 == 0 && ldw % 4 == 0 && nthr % 32 == 0;
+  const bool tiles = un_smem && n % 4 == 0 && ldp % 4 == 0 && ldw % 4 == 0 && nthr == kStepThreads;
   if (tiles) {
     float* Un = pool + P.smem[kRgUs];
     cta_basis_tiles(n, keep, r, m, Un, P.ldu, Q, WU, ldw);
-    cta_gram_tiles(keep, n, Un, P.ldu, Pol, ldp, part);  // E = U^T U - I
+    cta_tn_tiles(keep, keep, n, Un, P.ldu, Un, P.ldu, Pol, ldp, 1.f, part);  // E = U^T U - I
   } else if (un_smem) {
     float* Un = pool + P.smem[kRgUs];
     cta_basis_rows32(n, keep, r, m, Un, P.ldu, Q, WU, ldw);
