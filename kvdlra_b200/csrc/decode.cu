@@ -1222,8 +1222,24 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
   if (mid_all) {
     const int nvt = nv0 + nr;
     const int n_vch = nvt;  // one verbatim tile per CTA
-    int tpc = (int)(((long)nm * count + 4 * 148 - 1) / (4 * 148));
-    tpc = tpc < 2 ? 2 : (tpc > 8 ? 8 : tpc);
+    // tiles per CTA: one CTA fills an SM, so the launch takes
+    // ceil(chunks / SMs) waves of about (tpc + 1/2) tile times each (the
+    // half: staging the bases); the tpc in [2, 8] with the fewest such times
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) {
+      static int sm_count[64] = {0};
+      if (dev >= 0 && dev < 64) {
+        if (sm_count[dev] == 0) cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
+        if (sm_count[dev] > 0) sms = sm_count[dev];
+      }
+    }
+    int tpc = 2;
+    long best = -1;
+    for (int t = 2; t <= 8; ++t) {
+      const long waves = ((long)((nm + t - 1) / t) * count + sms - 1) / sms;
+      const long cost = waves * (2 * t + 1);
+      if (best < 0 || cost < best) { best = cost; tpc = t; }
+    }
     const int n_mch = (nm + tpc - 1) / tpc;
     a.n_chunks = n_vch + n_mch;
     const size_t need2 = (size_t)count * a.H * a.n_chunks * a.part_sp_chunk * 4;
