@@ -1081,7 +1081,7 @@ __global__ void __launch_bounds__(kMidThreads) decode_mid_kernel(DecArgs a, int 
 }
 
 template <typename T>
-__global__ void __launch_bounds__(128) decode_merge_kernel(DecArgs a) {
+__global__ void __launch_bounds__(512) decode_merge_kernel(DecArgs a) {
   extern __shared__ __align__(16) float msm2[];
   const int g = blockIdx.x, p = blockIdx.y;
   const int D = a.D, G = a.G, ld = a.ld;
@@ -1320,8 +1320,11 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
   const int msmem = 4 * (a.G * a.ld + a.G * a.D + 2 * a.G + a.n_chunks * a.G);
   if (int rc0 = ensure_smem((const void*)decode_merge_kernel<T>, msmem, "decode_merge_kernel")) return rc0;
   {
+    // a thread per combined value (G (D + ld) of them) where that fits 512
+    int mthr = ((a.G * (a.D + a.ld) + 31) / 32) * 32;
+    mthr = mthr < 128 ? 128 : (mthr > 512 ? 512 : mthr);
     KTimerScope kts_("decode_merge_kernel", s);
-    decode_merge_kernel<T><<<dim3(a.H, count), 128, msmem, s>>>(a);
+    decode_merge_kernel<T><<<dim3(a.H, count), mthr, msmem, s>>>(a);
   }
   return check_launch("decode_merge_kernel");
 }
