@@ -4,9 +4,11 @@
 // independent problems (one CTA per problem x stream):
 //   a = U^T X ; R = X - U a ; a2 = U^T R ; R -= U a2 ; a += a2   (fp32 FFMA,
 //     K-split with fp64 sums of the split partials)
-//   one-sided Jacobi on R (n x b): R V = [s_j q_j]  -> singular values s,
-//     left vectors q_j, right vectors V; admit s > 100 eps |X|_F, at most
-//     n - r of them
+//   SVD of R (n x b) -> singular values s, left vectors q_j, right vectors
+//     V: up to 128 columns from the fp64 Gram R^T R = T^T T (Cholesky) and a
+//     one-sided Jacobi on T's rows (rotated rows V S, q_j = R v_j / s_j; the
+//     pre-fill blocks refine with a seeded Jacobi on R V), wider blocks by a
+//     one-sided Jacobi on R itself; admit s > 100 eps |X|_F, at most n - r
 //   one-sided Jacobi on B^T, B = [[diag(sigma), a], [0, diag(s_m) V_m^T]]
 //     ((r+m) x (r+b)):  B^T W = [sigma'_c z_c]  -> W = left singular vectors
 //     of B (u_loc), sigma' its singular values
