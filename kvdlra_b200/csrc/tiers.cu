@@ -30,6 +30,22 @@ __global__ void hf_to_rows_kernel(HfRowsPair<T> pr, int H, int D, int q, long ds
   }
 }
 
+// The same copy in 16-byte pieces (8 bf16 or 4 fp32 of one head's row), for
+// views whose pointers, strides and head size are whole pieces.
+template <typename T>
+__global__ void hf_to_rows_vec_kernel(HfRowsPair<T> pr, int H, int D, int q, long dst_sp, int slot0) {
+  constexpr int kPer = 16 / sizeof(T);
+  const int p = blockIdx.y;
+  const HfRowsSide<T> sd = blockIdx.z ? pr.s[1] : pr.s[0];  // keys, values
+  const int dc = D / kPer, per_t = H * dc, n = H * D;
+  const int tot = q * per_t;
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < tot; e += gridDim.x * blockDim.x) {
+    const int t = e / per_t, rem = e % per_t, h = rem / dc, d = (rem % dc) * kPer;
+    const uint4 v = *reinterpret_cast<const uint4*>(sd.src + p * sd.sb + h * sd.sh + (long)t * sd.st + d);
+    *reinterpret_cast<uint4*>(sd.dst + p * dst_sp + (long)(slot0 + t) * n + h * D + d) = v;
+  }
+}
+
 // dst rows [0, count) <- src rows [0, count) of the same problem (copy).
 template <typename T>
 __global__ void rows_copy_kernel(const T* src, long src_sp, T* dst, long dst_sp, int count, int n) {
@@ -460,10 +476,22 @@ int launch_hf_to_rows(const kvd_hf_view& kv, const kvd_hf_view& vv, int P, int H
   HfRowsPair<T> pr;
   pr.s[0] = {(const T*)kv.ptr, kv.stride_b, kv.stride_h, kv.stride_t, dst_k};
   pr.s[1] = {(const T*)vv.ptr, vv.stride_b, vv.stride_h, vv.stride_t, dst_v};
-  dim3 grid(grid_for((long)kv.tokens * H * D), P, 2);  // keys and values in one launch
+  constexpr int kPer = 16 / sizeof(T);
+  auto whole = [&](const void* ptr, long a, long b, long c) {
+    return (reinterpret_cast<uintptr_t>(ptr) & 15) == 0 && a % kPer == 0 && b % kPer == 0 && c % kPer == 0;
+  };
+  const bool vec = D % kPer == 0 && dst_sp % kPer == 0 && whole(dst_k, 0, 0, 0) && whole(dst_v, 0, 0, 0) &&
+                   whole(kv.ptr, kv.stride_b, kv.stride_h, kv.stride_t) &&
+                   whole(vv.ptr, vv.stride_b, vv.stride_h, vv.stride_t);
   {
     KTimerScope kts_("hf_to_rows_kernel", s);
-    hf_to_rows_kernel<T><<<grid, 256, 0, s>>>(pr, H, D, kv.tokens, dst_sp, slot0);
+    if (vec) {
+      dim3 grid(grid_for((long)kv.tokens * H * (D / kPer)), P, 2);  // keys and values in one launch
+      hf_to_rows_vec_kernel<T><<<grid, 256, 0, s>>>(pr, H, D, kv.tokens, dst_sp, slot0);
+    } else {
+      dim3 grid(grid_for((long)kv.tokens * H * D), P, 2);
+      hf_to_rows_kernel<T><<<grid, 256, 0, s>>>(pr, H, D, kv.tokens, dst_sp, slot0);
+    }
   }
   return check_launch("hf_to_rows_kernel");
 }
