@@ -511,7 +511,17 @@ int launch_rows_copy(const T* src, long src_sp, T* dst, long dst_sp, int count, 
 template <typename T>
 int launch_ring_compact(T* ring, long sp, int head, int len, int n, int P, cudaStream_t s) {
   if (head == 0 || len <= 0 || P <= 0) return KVD_OK;
-  {
+  if ((len + head - 1) / head <= 8) {
+    // rows [head + d, head + d + head) -> [d, d + head): each round's source
+    // starts where its destination ends, so a round is a plain parallel copy
+    for (int d = 0; d < len; d += head) {
+      const int cnt = len - d < head ? len - d : head;
+      if (int rc = launch_rows_copy<T>(ring + (long)(head + d) * n, sp, ring + (long)d * n, sp, cnt, n, P, s))
+        return rc;
+    }
+    return KVD_OK;
+  }
+  {  // a short offset under a long ring: one CTA per problem, staged through shared memory
     KTimerScope kts_("ring_compact_kernel", s);
     ring_compact_kernel<T><<<P, 1024, 8192 * sizeof(T), s>>>(ring, sp, head, len, n);
   }
