@@ -91,6 +91,14 @@ def test_golden_workload_lockstep(case: str) -> None:
         ok_, _ = oracle.update(to_mat(s.k_post[:, p : p + 1]), to_mat(s.v[:, p : p + 1]))
         assert kr.shape[2] == ok_.shape[1]
         assert layer.stored_state_numel() == oracle.stored_state_numel()
+    if dec and stats.near_ties == 0:
+        # after the decode appends (the ring compacted in rounds of the absorbed
+        # offset as it filled) the dense peek still equals the oracle's
+        kr, vr = layer._decode_peek()
+        ok_, ov_ = oracle.decode_peek()
+        assert kr.shape[2] == ok_.shape[1]
+        assert _rel(kr[0].permute(0, 2, 1).reshape(H * D, -1).cpu().numpy(), ok_) < 1e-3
+        assert _rel(vr[0].permute(0, 2, 1).reshape(H * D, -1).cpu().numpy(), ov_) < 1e-3
     layer._group.check_status()
 
 
