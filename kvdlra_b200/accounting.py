@@ -1,71 +1,79 @@
-"""Float-equivalent memory accounting of the streaming-BUG cache.
+"""Float-equivalent charge of the streaming-BUG cache.
 
-Mirrors the BUG part of kvdlra's ``accounting.py`` (src/kvdlra/accounting.py:
-53-191, 363-450): the same unit (one fp32 word per stored element, bf16
-verbatim elements counted as one element each), the same component rules, so
-``bug_footprint(...).float_equiv()`` equals
-:meth:`kvdlra_b200.BugStreamingCache.stored_state_numel` for the same state.
+Every stored element costs one float-equivalent, whatever its storage type:
+a bf16 verbatim key is one, an fp32 coordinate is one, an int32 position is
+one.  The charge of a layer is built here as a table of components -- what is
+stored, how many items, how many elements per item, and whether the elements
+are model-dtype payload ("verbatim", priced at the storage width in bit
+ratios) or fp32/int bookkeeping (priced at 32 bits).  The total of that table
+is, by construction, the number :meth:`BugStreamingCache.stored_state_numel`
+measures for the same state (the reference pins the same equality for its
+formula, src/kvdlra/accounting.py:109-191 against bug_cache.py:1609-1675).
 
-Conventions:
-* verbatim K/V and basis/coordinate elements: 1 float-equivalent each;
-* the diagonal BUG core: ``r`` per stream (not ``r**2``);
-* positions (int32) and surprise scores (fp32): 1 each;
-* quantised codes: ``bits/32`` each, ``ceil`` over all codes;
-* the full fp16 cache: ``2*T*n`` elements per layer (``2*T*n*16`` bits).
+Scope is the surprise-selected streaming path: retention ``"fifo"`` or
+``"lowrank_surprise"``, an exact tier selected by surprise, and the BUGPress
+prefill model.  The research tiers (PolarQuant codes, merge, Q-BUG whitening,
+attention-scored retention) are refused with ``NotImplementedError`` rather
+than priced by a formula nothing here can measure.
 """
 
 from __future__ import annotations
 
 import math
-from collections.abc import Callable, Iterator
-from contextlib import contextmanager
-from dataclasses import dataclass, field
-from typing import Any
+from dataclasses import dataclass
+
+__all__ = ["Component", "Footprint", "bug_footprint", "bug_footprint_saturated",
+           "bug_prefill_footprint", "full_cache_footprint", "assert_all_within"]
 
 FP16_BITS = 16
-FP32_BITS = 32
-N_SINK = 4
+WORD_BITS = 32
 
-_TRACK_SCORE = ("attn", "blend")
-_TRACK_SURPRISE = ("lowrank_surprise", "blend")
 
-__all__ = [
-    "Footprint", "MemoryReport", "bug_footprint", "bug_footprint_saturated",
-    "bug_prefill_footprint", "full_cache_footprint", "measure_peak_gpu", "report",
-    "audit_matched", "assert_all_within",
-]
+@dataclass(frozen=True)
+class Component:
+    """``items`` stored things of ``size`` elements each."""
+
+    name: str
+    items: int
+    size: int
+    verbatim: bool  # model-dtype payload (else fp32 / integer bookkeeping)
+
+    @property
+    def elems(self) -> int:
+        return self.items * self.size
 
 
 @dataclass(frozen=True)
 class Footprint:
-    """Per-layer stored footprint: verbatim elements, packed code bits and fp32
-    bookkeeping words (accounting.py:53-103)."""
+    """A layer's stored state as a component table."""
 
-    verbatim_elems: float
-    quant_code_bits: float = 0.0
-    aux_words: float = 0.0
-    gpu_verbatim_elems: float | None = None
-    cpu_verbatim_elems: float = 0.0
+    parts: tuple[Component, ...]
 
-    def float_equiv(self) -> float:
-        codes = math.ceil(self.quant_code_bits / 32) if self.quant_code_bits else 0
-        return self.verbatim_elems + codes + self.aux_words
+    def float_equiv(self) -> int:
+        """Total stored elements (the unit of ``stored_state_numel``)."""
+        return sum(p.elems for p in self.parts)
 
-    def bits(self, store_bits: int = FP16_BITS) -> float:
-        return self.verbatim_elems * store_bits + self.quant_code_bits + self.aux_words * FP32_BITS
+    def breakdown(self) -> dict[str, int]:
+        out: dict[str, int] = {}
+        for p in self.parts:
+            out[p.name] = out.get(p.name, 0) + p.elems
+        return out
+
+    def bits(self, store_bits: int = FP16_BITS) -> int:
+        """Bits with payload at ``store_bits`` and bookkeeping at 32."""
+        return sum(p.elems * (store_bits if p.verbatim else WORD_BITS) for p in self.parts)
 
     def ratio_fp16(self, t: int, n: int) -> float:
+        """Bits against the uncompressed fp16 K+V cache of ``t`` tokens."""
         return self.bits(FP16_BITS) / (2 * t * n * FP16_BITS)
 
     def tok_equiv(self, n: int) -> float:
+        """Float-equivalents expressed as full-cache tokens (``2n`` each)."""
         return self.float_equiv() / (2 * n)
 
-    def gpu_ratio_fp16(self, t: int, n: int) -> float:
-        gpu = self.verbatim_elems if self.gpu_verbatim_elems is None else self.gpu_verbatim_elems
-        return (gpu * FP16_BITS + self.quant_code_bits + self.aux_words * FP32_BITS) / (2 * t * n * FP16_BITS)
 
-    def cpu_ratio_fp16(self, t: int, n: int) -> float:
-        return self.cpu_verbatim_elems * FP16_BITS / (2 * t * n * FP16_BITS)
+def _table(rows: list[tuple[str, int, int, bool]]) -> Footprint:
+    return Footprint(tuple(Component(*r) for r in rows if r[1] > 0 and r[2] > 0))
 
 
 def bug_footprint(
@@ -74,7 +82,7 @@ def bug_footprint(
     coord_count: int,
     recent_len: int,
     *,
-    n_sink: int = N_SINK,
+    n_sink: int = 4,
     retention: str = "fifo",
     hh_count: int = 0,
     hh_select: str = "attn",
@@ -84,30 +92,39 @@ def bug_footprint(
     quant_bits: int | None = None,
     w_key: bool = False,
 ) -> Footprint:
-    """One streaming layer's footprint (accounting.py:109-164): sinks and ring
-    verbatim (``2n`` per token), ``2*rank`` per coordinate column, ``2n`` per
-    exact-tier token, basis ``2*n*rank`` + diagonal cores ``2*rank`` when a basis
-    exists, and the bookkeeping words of the retention rule."""
-    track_pos = retention != "fifo" or merge
-    track_score = retention in _TRACK_SCORE
-    track_surprise = retention in _TRACK_SURPRISE
-    n_cols = coord_count + quant_count
-    verbatim = 2 * n * n_sink + 2 * n * recent_len + 2 * rank * coord_count + 2 * n * hh_count
-    aux = 0.0
-    if u_present:
-        verbatim += 2 * n * rank
-        aux += 2 * rank
-    aux += n_cols * (int(track_pos) + int(track_score) + int(merge) + int(track_surprise))
-    if track_score:
-        aux += recent_len
-    aux += hh_count * (2 if hh_select == "attn" else 1)
-    code_bits = 0.0
-    if quant_count and quant_bits is not None:
-        code_bits = 2 * rank * quant_count * quant_bits
-        aux += 2 * quant_count
-    if w_key:
-        aux += n
-    return Footprint(verbatim_elems=verbatim, quant_code_bits=code_bits, aux_words=aux)
+    """One streaming layer holding ``coord_count`` coordinate columns,
+    ``recent_len`` ring tokens, ``n_sink`` sinks and ``hh_count`` exact-tier
+    tokens (the reference's ``bug_footprint`` signature,
+    src/kvdlra/accounting.py:109-164).
+
+    K and V each keep: verbatim sinks, ring and exact tier (``n`` per token),
+    the basis (``n`` x ``rank``) and its diagonal core (``rank``) once a basis
+    exists, and ``rank`` coordinates per column.  Bookkeeping: one position per
+    column unless retention is FIFO (positions are implicit there), one
+    graduation surprise per column under ``"lowrank_surprise"``, one position
+    per exact-tier token, plus its selection score when the tier is
+    attention-selected (a surprise-selected tier re-scores from the basis and
+    stores none)."""
+    if retention not in ("fifo", "lowrank_surprise"):
+        raise NotImplementedError(f"retention {retention!r} is outside the surprise-selected path")
+    if merge or quant_count or quant_bits is not None or w_key:
+        raise NotImplementedError("merge, quantised tiers and key whitening are not in scope")
+    if hh_select not in ("attn", "surprise"):
+        raise ValueError(f"hh_select must be 'attn' or 'surprise', got {hh_select!r}")
+    streams = 2  # K and V
+    basis = rank if u_present else 0
+    return _table([
+        ("sinks", streams * n_sink, n, True),
+        ("ring", streams * recent_len, n, True),
+        ("exact tier", streams * hh_count, n, True),
+        ("coordinates", streams * coord_count, rank, True),
+        ("basis", streams * basis, n, True),
+        ("core", streams * basis, 1, False),
+        ("positions", coord_count if retention != "fifo" else 0, 1, False),
+        ("surprise", coord_count if retention == "lowrank_surprise" else 0, 1, False),
+        ("exact positions", hh_count, 1, False),
+        ("exact scores", hh_count if hh_select == "attn" else 0, 1, False),
+    ])
 
 
 def bug_footprint_saturated(
@@ -117,89 +134,45 @@ def bug_footprint_saturated(
     recent_window: int,
     absorb_block: int,
     *,
-    n_sink: int = N_SINK,
+    n_sink: int = 4,
     retention: str = "fifo",
     hh_budget: int = 0,
+    hh_select: str = "attn",
 ) -> Footprint:
-    """High-water footprint: ``coord_budget`` columns and the ring at
-    ``recent_window + absorb_block - 1`` (accounting.py:167-191)."""
-    return bug_footprint(n, rank, coord_budget, recent_window + absorb_block - 1,
-                         n_sink=n_sink, retention=retention, hh_count=hh_budget)
+    """The layer at its high-water mark: a full coordinate budget and the ring
+    one token short of the next absorb (``recent_window + absorb_block - 1``),
+    src/kvdlra/accounting.py:167-191.  The reference's helper prices the exact
+    tier as attention-selected (position + score per token); ``hh_select``
+    defaults to that so the numbers agree, ``"surprise"`` prices the tier
+    this cache keeps."""
+    return bug_footprint(n, rank, coord_budget, recent_window + absorb_block - 1, n_sink=n_sink,
+                         retention=retention, hh_count=hh_budget, hh_select=hh_select)
 
 
-def bug_prefill_footprint(t: int, n: int, rank: int, *, n_sink: int = N_SINK,
-                          quant_bits: int | None = None) -> Footprint:
-    """The prefill-press model: every non-sink token as a coordinate, the basis
-    and exact sinks, no ring or core (accounting.py:194-213)."""
-    t_pay = t - n_sink
-    verbatim = 2 * n * n_sink + 2 * n * rank
-    if quant_bits is None:
-        return Footprint(verbatim_elems=verbatim + 2 * rank * t_pay)
-    return Footprint(verbatim_elems=verbatim + t_pay, quant_code_bits=2 * rank * t_pay * quant_bits)
+def bug_prefill_footprint(t: int, n: int, rank: int, *, n_sink: int = 4) -> Footprint:
+    """The BUGPress prefill model (src/kvdlra/accounting.py:194-213): sinks
+    verbatim, one basis per stream, and every other token as ``rank``
+    coordinates per stream (no ring, no core)."""
+    payload = max(0, t - n_sink)
+    return _table([
+        ("sinks", 2 * n_sink, n, True),
+        ("basis", 2 * rank, n, True),
+        ("coordinates", 2 * payload, rank, True),
+    ])
 
 
 def full_cache_footprint(t: int, n: int) -> Footprint:
-    """The uncompressed reference: ``2*t*n`` verbatim elements per layer."""
-    return Footprint(verbatim_elems=2 * t * n)
-
-
-@contextmanager
-def measure_peak_gpu(device: str) -> Iterator[Callable[[], int | None]]:
-    """Getter for ``torch.cuda.max_memory_allocated`` over the block (``None``
-    off-GPU), reported beside -- never instead of -- the analytic footprint."""
-    import torch
-
-    if str(device).startswith("cuda"):
-        torch.cuda.reset_peak_memory_stats()
-        torch.cuda.synchronize()
-        yield lambda: int(torch.cuda.max_memory_allocated())
-    else:
-        yield lambda: None
-
-
-@dataclass(frozen=True)
-class MemoryReport:
-    arm: str
-    t: int
-    n: int
-    float_equiv_per_layer: float
-    tok_equiv_per_layer: float
-    ratio_fp16: float
-    gpu_ratio_fp16: float
-    cpu_ratio_fp16: float
-    bytes_native: int
-    peak_gpu_bytes: int | None
-    detail: dict[str, Any] = field(default_factory=dict)
-
-
-def report(arm: str, footprint: Footprint, t: int, n: int, *, store_bits: int = FP16_BITS,
-           peak_gpu_bytes: int | None = None, detail: dict[str, Any] | None = None) -> MemoryReport:
-    """Render a footprint into the report fields (accounting.py:399-424)."""
-    return MemoryReport(
-        arm=arm, t=t, n=n,
-        float_equiv_per_layer=footprint.float_equiv(),
-        tok_equiv_per_layer=footprint.tok_equiv(n),
-        ratio_fp16=footprint.ratio_fp16(t, n),
-        gpu_ratio_fp16=footprint.gpu_ratio_fp16(t, n),
-        cpu_ratio_fp16=footprint.cpu_ratio_fp16(t, n),
-        bytes_native=int(footprint.bits(store_bits) / 8),
-        peak_gpu_bytes=peak_gpu_bytes,
-        detail=detail or {},
-    )
-
-
-def audit_matched(mem_max_per_layer: float, budget_per_layer: float, arm: str, *,
-                  tol: float = 0.0) -> dict[str, Any]:
-    within = mem_max_per_layer <= budget_per_layer + tol
-    over = mem_max_per_layer / budget_per_layer if budget_per_layer else math.inf
-    return {"arm": arm, "mem_max": mem_max_per_layer, "over_budget": over, "within": within}
+    """The uncompressed K+V cache of ``t`` tokens."""
+    return _table([("keys and values", 2 * t, n, True)])
 
 
 def assert_all_within(mem_by_arm: dict[str, float], budget_per_layer: float, *,
                       tol: float = 0.0) -> None:
-    """Raise if any arm's per-layer footprint exceeds the matched budget."""
-    over = {a: m for a, m in mem_by_arm.items() if m > budget_per_layer + tol}
+    """Matched-memory gate: raise ``ValueError`` naming every arm whose
+    per-layer charge exceeds ``budget_per_layer`` (+ ``tol``)."""
+    limit = budget_per_layer + tol
+    over = sorted(a for a, m in mem_by_arm.items() if not m <= limit or math.isnan(m))
     if over:
-        raise ValueError(
-            f"matched-memory audit FAILED: {over} exceed budget {budget_per_layer}/layer"
-        )
+        detail = ", ".join(f"{a}={mem_by_arm[a]:g}" for a in over)
+        raise ValueError(f"matched-memory audit FAILED: {detail} over the budget of "
+                         f"{budget_per_layer:g} float-equivalents per layer")
