@@ -1,9 +1,11 @@
 """Generate the golden fixtures by running the reference kvdlra implementation.
 
-Run here (where the reference source is mounted read-only) with::
+Run where the reference source tree is available (read-only is enough)::
 
-    python tests/golden/make_golden.py /root/reference/src
+    python tests/golden/make_golden.py <reference>/src [case ...]
 
+or with ``KVDLRA_REFERENCE_SRC=<reference>/src`` set; naming cases regenerates
+only those fixtures.
 It imports the reference's own ``BugStreamingLayer`` / ``augmented_bug_step``
 (src/kvdlra/cache/bug_cache.py, src/kvdlra/integrators/streaming_torch.py),
 drives it on seeded synthetic inputs from ``kvdlra_b200.synthetic`` and stores
@@ -84,13 +86,16 @@ def _instrument(layer) -> list[dict]:
 
 
 def _boundary_gap(trace: list[dict], keep_counts: list[int]) -> float:
-    """Smallest relative gap between the last kept and first demoted score."""
+    """Smallest relative gap between the last kept and first demoted score
+    (exactly equal scores -- e.g. all 1.0 before a basis exists -- are decided
+    by the stable index rule on every implementation and are skipped)."""
     best = np.inf
     for ev, keep_n in zip(trace, keep_counts):
         s = np.sort(ev["sel"].astype(np.float64))[::-1]
         if keep_n < len(s):
             a, b = s[keep_n - 1], s[keep_n]
-            best = min(best, (a - b) / max(abs(a), 1e-30))
+            if a != b:
+                best = min(best, (a - b) / max(abs(a), 1e-30))
     return float(best)
 
 
@@ -99,24 +104,32 @@ def _pack_trace(trace: list[dict]) -> dict[str, np.ndarray]:
     koff = np.cumsum([0] + [len(e["keep_pos"]) for e in trace])
     return {
         "tr_cand_off": off.astype(np.int64),
-        "tr_cand_pos": np.concatenate([e["cand_pos"] for e in trace]).astype(np.int64) if trace else np.zeros(0, np.int64),
+        "tr_cand_pos": np.concatenate([e["cand_pos"] for e in trace]).astype(np.int32) if trace else np.zeros(0, np.int32),
         "tr_sel": np.concatenate([e["sel"] for e in trace]).astype(np.float32) if trace else np.zeros(0, np.float32),
         "tr_keep_off": koff.astype(np.int64),
-        "tr_keep_pos": np.concatenate([e["keep_pos"] for e in trace]).astype(np.int64) if trace else np.zeros(0, np.int64),
+        "tr_keep_pos": np.concatenate([e["keep_pos"] for e in trace]).astype(np.int32) if trace else np.zeros(0, np.int32),
     }
 
 
-def _ingest(layer, k_htd: np.ndarray, v_htd: np.ndarray, chunk: int) -> list[tuple[int, int]]:
+def _tdtype(name: str):
+    import torch
+
+    return {"float32": torch.float32, "bfloat16": torch.bfloat16}[name]
+
+
+def _ingest(layer, k_htd: np.ndarray, v_htd: np.ndarray, chunk: int,
+            dtype: str = "float32") -> list[tuple[int, int]]:
     """Chunked ingest through the reference layer; returns the mask sizes seen."""
     import torch
 
     t = k_htd.shape[1]
     masks = []
     layer._mode = "ingest"
+    dt = _tdtype(dtype)
     for start in range(0, t, chunk):
         stop = min(t, start + chunk)
-        k = torch.from_numpy(np.ascontiguousarray(k_htd[:, start:stop]))[None]
-        v = torch.from_numpy(np.ascontiguousarray(v_htd[:, start:stop]))[None]
+        k = torch.from_numpy(np.ascontiguousarray(k_htd[:, start:stop]))[None].to(dt)
+        v = torch.from_numpy(np.ascontiguousarray(v_htd[:, start:stop]))[None].to(dt)
         if layer.is_initialized:
             masks.append(layer.get_mask_sizes(stop - start))
         layer.update(k, v)
@@ -127,7 +140,8 @@ def _ingest(layer, k_htd: np.ndarray, v_htd: np.ndarray, chunk: int) -> list[tup
 
 def _state(layer) -> dict[str, np.ndarray]:
     out: dict[str, np.ndarray] = {}
-    for name in ("u_k", "u_v", "c_k", "c_v", "hh_pos", "mid_pos", "mid_surprise"):
+    # (coordinates are not stored: the tests recompute the gist from the oracle's own)
+    for name in ("u_k", "u_v", "hh_pos", "mid_pos", "mid_surprise"):
         t = getattr(layer, name)
         if t is not None:
             out[name] = t.numpy().copy()
@@ -168,14 +182,14 @@ def case_steps() -> dict[str, np.ndarray]:
 
 def _run_case(name: str, *, heads: int, head_dim: int, t: int, chunk: int, theta: float,
               layer_kw: dict, stream_kw: dict, n_queries: int = 0, q_heads: int = 0,
-              decode_tokens: int = 0, seed: int = 0) -> dict[str, np.ndarray]:
+              decode_tokens: int = 0, seed: int = 0, dtype: str = "float32") -> dict[str, np.ndarray]:
     import torch
 
     s = lowrank_stream(heads, head_dim, t + decode_tokens, theta=theta, seed=seed, **stream_kw)
     rotary = _rotary(head_dim, theta)
     layer = _layer(rotary, **layer_kw)
     trace = _instrument(layer)
-    masks = _ingest(layer, s.k_post[:, :t], s.v[:, :t], chunk)
+    masks = _ingest(layer, s.k_post[:, :t], s.v[:, :t], chunk, dtype)
     out = {"input_sha": np.frombuffer(bytes.fromhex(_sha(s.k_post, s.v)), np.uint8)}
     out.update(_pack_trace(trace))
     out["mask_sizes"] = np.array(masks, np.int64).reshape(-1, 2)
@@ -183,6 +197,7 @@ def _run_case(name: str, *, heads: int, head_dim: int, t: int, chunk: int, theta
     hh = layer_kw.get("hh_budget", 0)
     out["boundary_gap"] = np.array(_boundary_gap(trace, [min(hh, len(e["cand_pos"])) for e in trace]))
     k_ret, v_ret = layer._decode_peek()
+    k_ret, v_ret = k_ret.float(), v_ret.float()  # attention over the peek's values in fp32
     out["peek_k_sum"] = np.array(float(k_ret.double().sum()))
     out["peek_v_sum"] = np.array(float(v_ret.double().sum()))
     out["peek_len"] = np.array(k_ret.shape[2], np.int64)
@@ -211,15 +226,16 @@ def _run_case(name: str, *, heads: int, head_dim: int, t: int, chunk: int, theta
         dec_masks, dec_numel = [], []
         for j in range(decode_tokens):
             p = t + j
-            k = torch.from_numpy(np.ascontiguousarray(s.k_post[:, p : p + 1]))[None]
-            v = torch.from_numpy(np.ascontiguousarray(s.v[:, p : p + 1]))[None]
+            k = torch.from_numpy(np.ascontiguousarray(s.k_post[:, p : p + 1]))[None].to(_tdtype(dtype))
+            v = torch.from_numpy(np.ascontiguousarray(s.v[:, p : p + 1]))[None].to(_tdtype(dtype))
             dec_masks.append(layer.get_mask_sizes(1))
             kr, _ = layer.update(k, v)
             assert kr.shape[2] == dec_masks[-1][0]
             dec_numel.append(layer.stored_state_numel())
         out["dec_masks"] = np.array(dec_masks, np.int64)
         out["dec_numel"] = np.array(dec_numel, np.int64)
-        out.update({"dec_" + k: v for k, v in _state(layer).items()})
+        if layer.hh_pos is not None:
+            out["dec_hh_pos"] = layer.hh_pos.numpy().copy()
         out["dec_trace_len"] = np.array(len(trace), np.int64)
     out["trace_len"] = np.array(len(trace), np.int64)
     print(f"{name}: absorbs={len(trace)} boundary_gap={float(out['boundary_gap']):.3e} "
@@ -257,18 +273,46 @@ CASES = {
                                          hh_select="surprise", hh_neighbor=1),
                            stream_kw=dict(signal_rank=6, n_needles=4), n_queries=1, q_heads=4,
                            decode_tokens=7, seed=9),
+    # bf16 verbatim tiers (the model workloads' dtype), at the bench geometry:
+    # 8 KV heads x 64, chunk 512, r=32, h=256, ring 128, absorb 16
+    "cfg2_bf16": dict(heads=8, head_dim=64, t=2048, chunk=512, theta=500000.0, dtype="bfloat16",
+                      layer_kw=dict(rank=32, coord_budget=2048 + 128 + 16, recent_window=128,
+                                    absorb_block=16, n_sink=4, retention="lowrank_surprise",
+                                    hh_budget=256, hh_select="surprise"),
+                      stream_kw=dict(n_needles=8), n_queries=3, q_heads=32, decode_tokens=24, seed=21),
+    # head_dim 128 (n = 1024), warm-up seed on, ring 256, chunk 1024 (the 8B geometry)
+    "cfg3_bf16": dict(heads=8, head_dim=128, t=3072, chunk=1024, theta=500000.0, dtype="bfloat16",
+                      layer_kw=dict(rank=32, coord_budget=3072 + 256 + 16, recent_window=256,
+                                    absorb_block=16, n_sink=4, retention="lowrank_surprise",
+                                    hh_budget=256, hh_select="surprise", seed_hh_warmup=True),
+                      stream_kw=dict(n_needles=8), n_queries=2, q_heads=32, decode_tokens=8, seed=31),
+    # rank 128, exact tier 1024, ring 256, chunk 2048 (the whole-box configuration's cache)
+    "cfg5_bf16": dict(heads=8, head_dim=128, t=4096, chunk=2048, theta=500000.0, dtype="bfloat16",
+                      layer_kw=dict(rank=128, coord_budget=4096 + 256 + 16, recent_window=256,
+                                    absorb_block=16, n_sink=4, retention="lowrank_surprise",
+                                    hh_budget=1024, hh_select="surprise"),
+                      stream_kw=dict(signal_rank=24, n_needles=8), n_queries=2, q_heads=32,
+                      decode_tokens=4, seed=41),
 }
 
 
 def main() -> None:
-    src = sys.argv[1] if len(sys.argv) > 1 else "/root/reference/src"
+    import os
+
+    args = sys.argv[1:]
+    src = args.pop(0) if args and not args[0] in CASES and args[0] != "steps" else os.environ.get("KVDLRA_REFERENCE_SRC")
+    if not src or not (Path(src) / "kvdlra").is_dir():
+        sys.exit("usage: make_golden.py <reference>/src [case ...]  (or set KVDLRA_REFERENCE_SRC)")
     sys.path.insert(0, src)
     import torch
 
     torch.set_num_threads(1)
-    np.savez_compressed(HERE / "steps.npz", **case_steps())
-    for name, kw in CASES.items():
-        np.savez_compressed(HERE / f"{name}.npz", **_run_case(name, **kw))
+    names = args or ["steps", *CASES]
+    if "steps" in names:
+        np.savez_compressed(HERE / "steps.npz", **case_steps())
+    for name in names:
+        if name in CASES:
+            np.savez_compressed(HERE / f"{name}.npz", **_run_case(name, **CASES[name]))
 
 
 if __name__ == "__main__":

@@ -18,7 +18,7 @@ import pytest
 import torch
 
 from golden.make_golden import CASES
-from lockstep import run_ingest, to_mat
+from lockstep import golden_arbiter, run_ingest, to_mat
 from oracle.bug_oracle import OracleLayer, RopeSpec, default_inv_freq, gqa_attention, principal_angle
 
 from kvdlra_b200 import BugStreamingLayer, RopeAngles
@@ -50,17 +50,24 @@ def _gist_err(u: np.ndarray, c: np.ndarray, pos: np.ndarray, ref_htd: np.ndarray
 
 @pytest.mark.parametrize("case", list(CASES))
 def test_golden_workload_lockstep(case: str) -> None:
+    """Every golden workload, in its own dtype, lock-step against the oracle;
+    the oracle replays the reference's recorded selections (taking the
+    reference's choice at a near-tie), the GPU follows the oracle, so the final
+    exact tier and coordinate positions equal the reference's own."""
     kw = CASES[case]
     H, D, t, chunk = kw["heads"], kw["head_dim"], kw["t"], kw["chunk"]
     dec = kw.get("decode_tokens", 0)
+    bf16 = kw.get("dtype", "float32") == "bfloat16"
+    tdt = torch.bfloat16 if bf16 else torch.float32
     s = lowrank_stream(H, D, t + dec, theta=kw["theta"], seed=kw["seed"], **kw["stream_kw"])
-    oracle, layer = _make(kw)
-    stats = run_ingest(layer, oracle, s.k_post[:, :t], s.v[:, :t], chunk, dtype=torch.float32)
-    assert stats.max_angle_k <= 1e-2 and stats.max_angle_v <= 1e-2, stats  # rule (c)
+    oracle, layer = _make(kw, kw.get("dtype", "float32"))
     g = np.load(GOLDEN / f"{case}.npz")
-    if stats.near_ties == 0 and "final_hh_pos" in g:
+    oracle.arbiter, ref_ties = golden_arbiter(g, oracle)
+    stats = run_ingest(layer, oracle, s.k_post[:, :t], s.v[:, :t], chunk, dtype=tdt)
+    assert stats.max_angle_k <= 1e-2 and stats.max_angle_v <= 1e-2, stats  # rule (c)
+    if "final_hh_pos" in g:
         assert np.array_equal(layer.hh_pos.cpu().numpy(), g["final_hh_pos"])
-    if stats.near_ties == 0 and "final_mid_pos" in g:
+    if "final_mid_pos" in g:
         assert np.array_equal(layer.mid_pos.cpu().numpy(), g["final_mid_pos"])
     assert layer.stored_state_numel() == oracle.stored_state_numel() == int(g["final_stored_numel"])
     if layer.u_k is not None and layer.mid_pos is not None:  # rule (b)
@@ -68,37 +75,45 @@ def test_golden_workload_lockstep(case: str) -> None:
         e_gpu = _gist_err(layer.u_k.cpu().numpy(), layer.c_k.cpu().numpy(), pos, s.k_pre)
         e_ora = _gist_err(oracle.u_k, oracle.c_k, oracle.mid_pos, s.k_pre)
         assert abs(e_gpu - e_ora) <= 1e-3 * e_ora + 1e-7, (e_gpu, e_ora)
-    # dense peek equals the oracle's peek (fp32 path: reconstruction tolerance)
+    # dense peek equals the oracle's peek: fp32 within the reconstruction
+    # tolerance 1e-3; bf16 within 8e-3 (the middle is rounded to bf16 after an
+    # fp32 reconstruction, one bf16 ulp is 2^-8 relative)
     kr, vr = layer._decode_peek()
     ok_, ov_ = oracle.decode_peek()
     assert kr.shape[2] == ok_.shape[1]
-    if stats.near_ties == 0:
-        assert _rel(kr[0].permute(0, 2, 1).reshape(H * D, -1).cpu().numpy(), ok_) < 1e-3
-        assert _rel(vr[0].permute(0, 2, 1).reshape(H * D, -1).cpu().numpy(), ov_) < 1e-3
-    # rule (d): factored decode vs dense attention over the oracle's peek
+    ptol = 8e-3 if bf16 else 1e-3
+    assert _rel(kr[0].float().permute(0, 2, 1).reshape(H * D, -1).cpu().numpy(), ok_) < ptol
+    assert _rel(vr[0].float().permute(0, 2, 1).reshape(H * D, -1).cpu().numpy(), ov_) < ptol
+    # rule (d): factored decode vs dense attention over the oracle's peek,
+    # 1e-4 relative (fp32) / 2e-2 (bf16)
     if "queries" in g:
+        atol_ = 2e-2 if bf16 else 1e-4
         for q in g["queries"]:
-            out = layer.factored_attention(torch.from_numpy(q)[None].to(DEV))[0].cpu().numpy()
-            ref = gqa_attention(q, oracle.to_hf(ok_), oracle.to_hf(ov_))
-            assert _rel(out, ref) < 1e-4, _rel(out, ref)
+            qd = torch.from_numpy(q)[None].to(DEV, tdt)
+            out = layer.factored_attention(qd)[0].float().cpu().numpy()
+            ref = gqa_attention(qd[0].float().cpu().numpy(), oracle.to_hf(ok_), oracle.to_hf(ov_))
+            assert _rel(out, ref) < atol_, _rel(out, ref)
     # decode steps in normal mode: mask sizes and accounting track the oracle
     for j in range(dec):
         p = t + j
         assert layer.get_mask_sizes(1) == oracle.get_mask_sizes(1)
-        kt = torch.from_numpy(np.ascontiguousarray(s.k_post[:, p : p + 1]))[None].to(DEV)
-        vt = torch.from_numpy(np.ascontiguousarray(s.v[:, p : p + 1]))[None].to(DEV)
+        kt = torch.from_numpy(np.ascontiguousarray(s.k_post[:, p : p + 1]))[None].to(DEV, tdt)
+        vt = torch.from_numpy(np.ascontiguousarray(s.v[:, p : p + 1]))[None].to(DEV, tdt)
         kr, _ = layer.update(kt, vt)
         ok_, _ = oracle.update(to_mat(s.k_post[:, p : p + 1]), to_mat(s.v[:, p : p + 1]))
         assert kr.shape[2] == ok_.shape[1]
         assert layer.stored_state_numel() == oracle.stored_state_numel()
-    if dec and stats.near_ties == 0:
-        # after the decode appends (the ring compacted in rounds of the absorbed
-        # offset as it filled) the dense peek still equals the oracle's
-        kr, vr = layer._decode_peek()
-        ok_, ov_ = oracle.decode_peek()
-        assert kr.shape[2] == ok_.shape[1]
-        assert _rel(kr[0].permute(0, 2, 1).reshape(H * D, -1).cpu().numpy(), ok_) < 1e-3
-        assert _rel(vr[0].permute(0, 2, 1).reshape(H * D, -1).cpu().numpy(), ov_) < 1e-3
+    if dec and "dec_hh_pos" in g and np.array_equal(oracle.hh_pos, g["dec_hh_pos"]):
+        # (decode steps are not stepped one absorb at a time: compare the tiers
+        # where the decode-time selections agreed, then the peek)
+        if np.array_equal(layer.hh_pos.cpu().numpy(), oracle.hh_pos):
+            # after the decode appends (the ring compacted in rounds of the
+            # absorbed offset as it filled) the dense peek still equals the oracle's
+            kr, vr = layer._decode_peek()
+            ok_, ov_ = oracle.decode_peek()
+            assert kr.shape[2] == ok_.shape[1]
+            assert _rel(kr[0].float().permute(0, 2, 1).reshape(H * D, -1).cpu().numpy(), ok_) < ptol
+            assert _rel(vr[0].float().permute(0, 2, 1).reshape(H * D, -1).cpu().numpy(), ov_) < ptol
     layer._group.check_status()
 
 
@@ -127,8 +142,7 @@ def test_full_size_single_layer_stream() -> None:
         q = rng.standard_normal((32, D)).astype(np.float32)
         out = layer.factored_attention(torch.from_numpy(q)[None].to(DEV))[0].cpu().numpy()
         ref = gqa_attention(q, oracle.to_hf(ok_), oracle.to_hf(ov_))
-        tol = 1e-4 if stats.near_ties == 0 else 5e-3
-        assert _rel(out, ref) < tol
+        assert _rel(out, ref) < 1e-4, (_rel(out, ref), stats.near_ties)  # rule (d), fp32
 
 
 def test_bf16_stream_lockstep() -> None:
@@ -182,3 +196,49 @@ def test_batched_layers_equal_single() -> None:
             assert torch.equal(got, single.hh_pos.to(torch.int32).cpu())
             assert principal_angle(g.t["u_k"][lay._ctr.u_sel, p, :, : int(g.t["r_k"][p])].cpu().numpy(),
                                    single.u_k.cpu().numpy()) < 1e-4
+
+
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
+def test_frozen_scoring_matches_oracle(dtype: str) -> None:
+    """``frozen_scoring()`` (bug_cache.py:1871-1882, 1390-1402): an update
+    returns ``[retained | window]`` and leaves the state untouched."""
+    from kvdlra_b200 import BugStreamingCache
+
+    H, D, T, W = 4, 64, 1200, 96
+    s = lowrank_stream(H, D, T + W, n_needles=4, seed=12)
+    inv = default_inv_freq(D, 500000.0)
+    kw = dict(rank=16, coord_budget=T + 64, recent_window=64, absorb_block=16, n_sink=4,
+              retention="lowrank_surprise", hh_budget=48, hh_select="surprise")
+    tdt = torch.float32 if dtype == "float32" else torch.bfloat16
+    cache = BugStreamingCache(None, num_layers=1, rope=RopeAngles(inv_freq=torch.from_numpy(inv)), **kw)
+    oracle = OracleLayer(RopeSpec(inv), H, D, dtype=dtype, **kw)
+    layer = cache.layers[0]
+    oracle.mode = "ingest"
+    with cache.ingesting():
+        for st in range(0, T, 200):
+            k = torch.from_numpy(np.ascontiguousarray(s.k_post[:, st : st + 200]))[None].to(DEV, tdt)
+            v = torch.from_numpy(np.ascontiguousarray(s.v[:, st : st + 200]))[None].to(DEV, tdt)
+            layer.update(k, v)
+            cache.consolidate()
+            oracle.update(to_mat(s.k_post[:, st : st + 200]), to_mat(s.v[:, st : st + 200]))
+            oracle.consolidate()
+    if not np.array_equal(layer.hh_pos.cpu().numpy(), oracle.hh_pos):
+        from lockstep import resync
+
+        resync(layer, oracle)  # (a near-tie in the batched consolidate)
+    before = (layer.attended_length(), layer.cumulative_length, layer.hh_pos.clone(), layer.mid_pos.clone())
+    kw_ = torch.from_numpy(np.ascontiguousarray(s.k_post[:, T : T + W]))[None].to(DEV, tdt)
+    vw_ = torch.from_numpy(np.ascontiguousarray(s.v[:, T : T + W]))[None].to(DEV, tdt)
+    oracle.mode = "score"
+    with cache.frozen_scoring():
+        assert layer.get_mask_sizes(W) == oracle.get_mask_sizes(W)
+        kr, vr = layer.update(kw_, vw_)
+    ok_, ov_ = oracle.update(to_mat(s.k_post[:, T : T + W]), to_mat(s.v[:, T : T + W]))
+    assert kr.shape[2] == ok_.shape[1] == before[0] + W
+    ptol = 1e-3 if dtype == "float32" else 8e-3
+    assert _rel(kr[0].float().permute(0, 2, 1).reshape(H * D, -1).cpu().numpy(), ok_) < ptol
+    assert _rel(vr[0].float().permute(0, 2, 1).reshape(H * D, -1).cpu().numpy(), ov_) < ptol
+    # the window itself is returned verbatim and nothing moved
+    assert torch.equal(kr[:, :, -W:], kw_) and torch.equal(vr[:, :, -W:], vw_)
+    assert (layer.attended_length(), layer.cumulative_length) == before[:2]
+    assert torch.equal(layer.hh_pos, before[2]) and torch.equal(layer.mid_pos, before[3])

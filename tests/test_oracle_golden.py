@@ -49,8 +49,40 @@ def test_oracle_layer_matches_reference(case: str) -> None:
     h.update(np.ascontiguousarray(s.k_post).tobytes())
     h.update(np.ascontiguousarray(s.v).tobytes())
     assert h.digest() == g["input_sha"].tobytes(), "synthetic inputs drifted from the fixtures"
-    lay = OracleLayer(RopeSpec(default_inv_freq(D, kw["theta"])), H, D, **kw["layer_kw"])
+    lay = OracleLayer(RopeSpec(default_inv_freq(D, kw["theta"])), H, D, dtype=kw.get("dtype", "float32"),
+                      **kw["layer_kw"])
     lay.mode = "ingest"
+    ntr = len(g["tr_keep_off"]) - 1
+    ref_keep = [g["tr_keep_pos"][g["tr_keep_off"][i] : g["tr_keep_off"][i + 1]] for i in range(ntr)]
+    ref_sel = [g["tr_sel"][g["tr_cand_off"][i] : g["tr_cand_off"][i + 1]] for i in range(ntr)]
+    near_ties: list[tuple[int, float]] = []
+
+    def arbiter(cand_pos: np.ndarray, sel: np.ndarray, keep_pos: np.ndarray) -> np.ndarray:
+        # Every selection must equal the reference's.  Where it does not, the
+        # swap must be a near-tie: the swapped candidates' reference scores lie
+        # within max(1e-5, twice the two implementations' own disagreement on
+        # those scores) of each other -- fp32 rounding decided the order (scores
+        # of in-span keys are formed by cancellation, |k|^2 - |U^T k|^2, so two
+        # fp32 implementations drift apart by more than 1e-5 over a long stream).
+        # The oracle then continues from the reference's choice.
+        i = len(lay.trace)
+        if i >= ntr or np.array_equal(keep_pos, ref_keep[i]):
+            return keep_pos
+        ref = {int(p): float(x) for p, x in zip(cand_pos, ref_sel[i])}
+        own = {int(p): float(x) for p, x in zip(cand_pos, sel)}
+        mine = set(keep_pos.tolist()) - set(ref_keep[i].tolist())
+        theirs = set(ref_keep[i].tolist()) - set(keep_pos.tolist())
+        for a in mine:
+            for b in theirs:
+                scale = max(abs(ref[a]), abs(ref[b]), 1e-30)
+                gap = abs(ref[a] - ref[b]) / scale
+                drift = max(abs(own[a] - ref[a]), abs(own[b] - ref[b])) / scale
+                assert gap <= max(1e-5, 2.0 * drift), (
+                    f"selection {i} differs beyond a near-tie: gap {gap:.3e}, score drift {drift:.3e}")
+        near_ties.append((i, len(mine)))
+        return ref_keep[i]
+
+    lay.arbiter = arbiter
     masks = []
     for st in range(0, t, chunk):
         sp = min(t, st + chunk)
@@ -60,13 +92,11 @@ def test_oracle_layer_matches_reference(case: str) -> None:
         lay.consolidate()
     lay.mode = "normal"
     assert np.array_equal(np.array(masks, np.int64).reshape(-1, 2), g["mask_sizes"])
-    ntr = len(g["tr_keep_off"]) - 1
     assert len(lay.trace) >= ntr
-    for i in range(ntr):  # every exact-tier selection identical to the reference's
-        kp = g["tr_keep_pos"][g["tr_keep_off"][i] : g["tr_keep_off"][i + 1]]
-        assert np.array_equal(lay.trace[i]["keep_pos"], kp), f"selection {i}"
-        ref_sel = g["tr_sel"][g["tr_cand_off"][i] : g["tr_cand_off"][i + 1]]
-        assert np.allclose(lay.trace[i]["sel"], ref_sel, rtol=1e-3, atol=1e-4)
+    assert len(near_ties) <= max(1, ntr // 20), near_ties  # near-ties are rare events
+    for i in range(ntr):  # the scores of every selection agree with the reference's
+        assert np.array_equal(lay.trace[i]["cand_pos"], g["tr_cand_pos"][g["tr_cand_off"][i] : g["tr_cand_off"][i + 1]])
+        assert np.allclose(lay.trace[i]["sel"], ref_sel[i], rtol=1e-3, atol=1e-4)
     assert lay.stored_state_numel() == int(g["final_stored_numel"])
     assert lay.attended_length() == int(g["final_attended"])
     if "final_hh_pos" in g:
@@ -88,10 +118,15 @@ def test_oracle_layer_matches_reference(case: str) -> None:
         err = np.linalg.norm(kp - lay.u_k.astype(np.float64) @ lay.c_k) / np.linalg.norm(kp)
         assert abs(err - float(g["gist_err_k"])) <= 1e-3 * float(g["gist_err_k"]) + 1e-7
     if "attn_out" in g:
+        # fp32: 1e-4 relative.  bf16: the reconstructed middle is rounded to bf16
+        # after an fp32 product whose last bits differ between implementations, so
+        # an element can land one bf16 ulp (2^-8 relative) away; 2e-3 relative on
+        # the output bounds that (the bf16 attention rule itself is 2e-2).
+        tol = 1e-4 if kw.get("dtype", "float32") == "float32" else 2e-3
         for qi in range(g["queries"].shape[0]):
             o = gqa_attention(g["queries"][qi], lay.to_hf(kr), lay.to_hf(vr))
             ref = g["attn_out"][qi]
-            assert np.abs(o - ref).max() <= 1e-4 * np.abs(ref).max()
+            assert np.abs(o - ref).max() <= tol * np.abs(ref).max()
     if dec:
         dm, dn = [], []
         for j in range(dec):
