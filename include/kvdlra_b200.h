@@ -185,8 +185,10 @@ size_t kvd_bug_step_workspace_bytes(int32_t n_batch, int32_t n, int32_t b, int32
  * library (kvd_bug_step_noalloc_max_scratch()), held on every GPU that loads
  * the library; requests that need more return KVD_ERR_WORKSPACE.  The first
  * call on a device looks up the array's device address, so make it before any
- * stream capture.  Calls share the array: calls that overlap on the GPU race
- * and must be serialised by the caller.  Allocates nothing. */
+ * stream capture.  The scratch used is the current device's: `stream` must
+ * belong to the device current on the calling thread.  Calls share the array:
+ * calls that overlap on the GPU race and must be serialised by the caller.
+ * Allocates nothing. */
 int kvd_bug_step_noalloc(int32_t n_batch, int32_t n, int32_t b, int32_t rank_cap, int32_t ld_u,
                          const float* u, float* u_out, float* sigma, int32_t* r,
                          const float* block, float* rot_out, int32_t* m_out, float* coords_out,

@@ -151,6 +151,14 @@ def check(code: int, what: str) -> None:
         raise KvdError(code, what, msg)
 
 
+def call(device: torch.device, name: str, *args: object) -> None:
+    """Call entry point ``name`` with ``device`` current (the library launches
+    on, and sizes its per-device tables for, the calling thread's current
+    device) and raise on a non-zero status."""
+    with torch.cuda.device(device):
+        check(getattr(lib(), name)(*args), name)
+
+
 def profile(enable: bool) -> None:
     """Start (clearing previous totals) or stop per-kernel event timing."""
     check(lib().kvd_profile(int(enable)), "kvd_profile")

@@ -337,7 +337,7 @@ class _Group:
 
     def check_status(self) -> None:
         b = self.buffers(0)
-        N.check(N.lib().kvd_check_status(C.byref(b), self.stream()), "device status")
+        N.call(self.device, "kvd_check_status", C.byref(b), self.stream())
 
 
 class BugStreamingLayer(CacheLayerMixin):  # type: ignore[misc]
@@ -576,8 +576,8 @@ class BugStreamingLayer(CacheLayerMixin):  # type: ignore[misc]
         self._ctr.ingest_mode = int(self._mode == "ingest")
         cfg, buf = self._cfg_buf()
         ws, wsb = g.workspace()
-        N.check(N.lib().kvd_prefill(C.byref(cfg), C.byref(buf), C.byref(self._ctr), N.hf_view(k),
-                                    N.hf_view(v), ws, wsb, g.stream()), "kvd_prefill")
+        N.call(g.device, "kvd_prefill", C.byref(cfg), C.byref(buf), C.byref(self._ctr), N.hf_view(k),
+               N.hf_view(v), ws, wsb, g.stream())
         self._started = True
         self._r_cache = None
         return key_states, value_states
@@ -589,8 +589,8 @@ class BugStreamingLayer(CacheLayerMixin):  # type: ignore[misc]
         q = int(k.shape[2])
         g.ensure(self._group_layers(), self._recent_len() + q, 0)
         cfg, buf = self._cfg_buf()
-        N.check(N.lib().kvd_append(C.byref(cfg), C.byref(buf), C.byref(self._ctr), N.hf_view(k),
-                                   N.hf_view(v), g.stream()), "kvd_append")
+        N.call(g.device, "kvd_append", C.byref(cfg), C.byref(buf), C.byref(self._ctr), N.hf_view(k),
+               N.hf_view(v), g.stream())
 
     def _ingest_chunk(self, key_states: Tensor, value_states: Tensor) -> tuple[Tensor, Tensor]:
         """bug_cache.py:1404-1423: append to the ring, defer the absorb."""
@@ -618,8 +618,8 @@ class BugStreamingLayer(CacheLayerMixin):  # type: ignore[misc]
         g.ensure(self._group_layers(), 0, self._w_need())
         cfg, buf = self._cfg_buf()
         ws, wsb = g.workspace()
-        N.check(N.lib().kvd_consolidate(C.byref(cfg), C.byref(buf), C.byref(self._ctr), ws, wsb,
-                                        g.stream()), "kvd_consolidate")
+        N.call(g.device, "kvd_consolidate", C.byref(cfg), C.byref(buf), C.byref(self._ctr), ws, wsb,
+               g.stream())
         self._r_cache = None
 
     def _absorb_block_into_stream(self, m: int | None = None) -> None:
@@ -631,8 +631,8 @@ class BugStreamingLayer(CacheLayerMixin):  # type: ignore[misc]
         g.ensure(self._group_layers(), 0, self._w_need())
         cfg, buf = self._cfg_buf()
         ws, wsb = g.workspace()
-        N.check(N.lib().kvd_absorb_block(C.byref(cfg), C.byref(buf), C.byref(self._ctr), ws, wsb,
-                                         g.stream()), "kvd_absorb_block")
+        N.call(g.device, "kvd_absorb_block", C.byref(cfg), C.byref(buf), C.byref(self._ctr), ws, wsb,
+               g.stream())
         self._r_cache = None
 
     def _decode_step(self, key_states: Tensor, value_states: Tensor) -> tuple[Tensor, Tensor]:
@@ -653,9 +653,9 @@ class BugStreamingLayer(CacheLayerMixin):  # type: ignore[misc]
         cfg, buf = g.config(g.P), g.buffers(0)
         tk = N.hf_view(tail[0] if tail else None)
         tv = N.hf_view(tail[1] if tail else None)
-        N.check(N.lib().kvd_peek(C.byref(cfg), C.byref(buf), C.byref(self._ctr), self._p0(),
-                                 self.batch, N.hf_view(out_k), N.hf_view(out_v), tk, tv,
-                                 g.stream()), "kvd_peek")
+        N.call(g.device, "kvd_peek", C.byref(cfg), C.byref(buf), C.byref(self._ctr), self._p0(),
+               self.batch, N.hf_view(out_k), N.hf_view(out_v), tk, tv,
+               g.stream())
         return out_k, out_v
 
     # -------------------------------------------------------- factored decode
@@ -676,10 +676,9 @@ class BugStreamingLayer(CacheLayerMixin):  # type: ignore[misc]
         sc = (1.0 / math.sqrt(self.head_dim)) if scaling is None else float(scaling)
         cfg, buf = g.config(g.P), g.buffers(0)
         ws, wsb = g.decode_workspace(self.batch, hq)
-        N.check(N.lib().kvd_factored_decode(C.byref(cfg), C.byref(buf), C.byref(self._ctr),
-                                            self._p0(), self.batch, q.data_ptr(), hq, sc,
-                                            out.data_ptr(), ws, wsb, g.stream()),
-                "kvd_factored_decode")
+        N.call(g.device, "kvd_factored_decode", C.byref(cfg), C.byref(buf), C.byref(self._ctr),
+               self._p0(), self.batch, q.data_ptr(), hq, sc,
+               out.data_ptr(), ws, wsb, g.stream())
         return out
 
     # ------------------------------------------------------------ state views
@@ -1038,8 +1037,8 @@ class BugStreamingCache(Cache):
         ctr = first._ctr.clone()
         cfg, buf = g.config(g.P), g.buffers(0)
         ws, wsb = g.workspace()
-        N.check(N.lib().kvd_consolidate(C.byref(cfg), C.byref(buf), C.byref(ctr), ws, wsb,
-                                        g.stream()), "kvd_consolidate")
+        N.call(g.device, "kvd_consolidate", C.byref(cfg), C.byref(buf), C.byref(ctr), ws, wsb,
+               g.stream())
         for ly in layers:
             ly._ctr.copy_from(ctr)
             ly._r_cache = None
@@ -1072,8 +1071,8 @@ class BugStreamingCache(Cache):
             g.ensure(layers, q, min(first.coord_budget, mid) + g.max_block + 1)
             cfg, buf = g.config(g.P), g.buffers(0)
             ws, wsb = g.workspace()
-            N.check(N.lib().kvd_prefill(C.byref(cfg), C.byref(buf), C.byref(ctr), N.hf_view(k),
-                                        N.hf_view(v), ws, wsb, g.stream()), "kvd_prefill")
+            N.call(g.device, "kvd_prefill", C.byref(cfg), C.byref(buf), C.byref(ctr), N.hf_view(k),
+                   N.hf_view(v), ws, wsb, g.stream())
             for ly in layers:
                 ly._ctr.copy_from(ctr)
                 ly._started = True
@@ -1082,8 +1081,8 @@ class BugStreamingCache(Cache):
         else:
             g.ensure(layers, first._recent_len() + q, 0)
             cfg, buf = g.config(g.P), g.buffers(0)
-            N.check(N.lib().kvd_append(C.byref(cfg), C.byref(buf), C.byref(ctr), N.hf_view(k),
-                                       N.hf_view(v), g.stream()), "kvd_append")
+            N.call(g.device, "kvd_append", C.byref(cfg), C.byref(buf), C.byref(ctr), N.hf_view(k),
+                   N.hf_view(v), g.stream())
             for ly in layers:
                 ly._ctr.copy_from(ctr)
             out = self._peek_all() if peek else None
@@ -1100,9 +1099,8 @@ class BugStreamingCache(Cache):
         out_v = torch.empty_like(out_k)
         cfg, buf = g.config(g.P), g.buffers(0)
         empty = N.hf_view(None)
-        N.check(N.lib().kvd_peek(C.byref(cfg), C.byref(buf), C.byref(first._ctr), 0, g.P,
-                                 N.hf_view(out_k), N.hf_view(out_v), empty, empty, g.stream()),
-                "kvd_peek")
+        N.call(g.device, "kvd_peek", C.byref(cfg), C.byref(buf), C.byref(first._ctr), 0, g.P,
+               N.hf_view(out_k), N.hf_view(out_v), empty, empty, g.stream())
         return out_k, out_v
 
     def decode_all(self, keys: Tensor, values: Tensor, queries: Tensor,
@@ -1118,9 +1116,9 @@ class BugStreamingCache(Cache):
         g.ensure(layers, first._recent_len() + 1, 0)
         ctr = first._ctr.clone()
         cfg, buf = g.config(g.P), g.buffers(0)
-        N.check(N.lib().kvd_append(C.byref(cfg), C.byref(buf), C.byref(ctr),
-                                   N.hf_view(keys.reshape(Ls * B, H, 1, D)),
-                                   N.hf_view(values.reshape(Ls * B, H, 1, D)), g.stream()), "kvd_append")
+        N.call(g.device, "kvd_append", C.byref(cfg), C.byref(buf), C.byref(ctr),
+               N.hf_view(keys.reshape(Ls * B, H, 1, D)),
+               N.hf_view(values.reshape(Ls * B, H, 1, D)), g.stream())
         for ly in layers:
             ly._ctr.copy_from(ctr)
         self.consolidate()
@@ -1130,9 +1128,9 @@ class BugStreamingCache(Cache):
         sc = (1.0 / math.sqrt(D)) if scaling is None else float(scaling)
         cfg, buf = g.config(g.P), g.buffers(0)
         ws, wsb = g.decode_workspace(g.P, hq)
-        N.check(N.lib().kvd_factored_decode(C.byref(cfg), C.byref(buf), C.byref(first._ctr), 0, g.P,
-                                            qq.data_ptr(), hq, sc, out.data_ptr(), ws, wsb,
-                                            g.stream()), "kvd_factored_decode")
+        N.call(g.device, "kvd_factored_decode", C.byref(cfg), C.byref(buf), C.byref(first._ctr), 0, g.P,
+               qq.data_ptr(), hq, sc, out.data_ptr(), ws, wsb,
+               g.stream())
         return out.reshape(Ls, B, hq, D)
 
     # ------------------------------------------------------------ accounting

@@ -23,6 +23,7 @@
 #include <stdio.h>
 
 #include <cfloat>
+#include <mutex>
 
 #include "kernels.cuh"
 
@@ -1776,21 +1777,21 @@ __global__ void __launch_bounds__(256) surprise_f32_kernel(int n, int m, int ld,
 // Stable descending top-k (bug_cache.py:810-812): one CTA per problem.
 __global__ void __launch_bounds__(1024) select_topk_kernel(int m, int k, const float* scores,
                                                            int* keep_idx, int* demote_idx) {
-  extern __shared__ float ssc[];
+  extern __shared__ unsigned skey[];
   __shared__ int scan_scratch[32];
   const int p = blockIdx.x;
   const float* s = scores + (long)p * m;
-  for (int i = threadIdx.x; i < m; i += blockDim.x) ssc[i] = s[i];
+  for (int i = threadIdx.x; i < m; i += blockDim.x) skey[i] = order_key(s[i]);
   __syncthreads();
   int keep_base = 0, dem_base = 0;
   for (int i0 = 0; i0 < m; i0 += blockDim.x) {
     const int i = i0 + threadIdx.x;
     int kept = 0;
     if (i < m) {
-      const float v = ssc[i];
+      const unsigned v = skey[i];
       int rank = 0;
       for (int j = 0; j < m; ++j) {
-        const float w = ssc[j];
+        const unsigned w = skey[j];
         rank += (w > v) || (w == v && j < i);
       }
       kept = rank < k;
@@ -1884,18 +1885,38 @@ static StepPlan plan_bug_step(int n, int b, int ld, long pool_max_floats) {
 
 long bug_step_ws_per_problem(int n, int b, int ld) { return plan_bug_step(n, b, ld, 0).ws_bytes; }
 
-int launch_bug_step(const BugStepBatch& batch_in, int n_problems, int n_streams, cudaStream_t stream) {
-  static int max_dyn = 0;
-  if (!max_dyn) {
-    cudaFuncAttributes a1, a2;
-    int dev = 0, optin = 0;
-    cudaFuncGetAttributes(&a1, (const void*)bug_step_kernel<true>);
-    cudaFuncGetAttributes(&a2, (const void*)bug_step_kernel<false>);
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    const int st = (int)(a1.sharedSizeBytes > a2.sharedSizeBytes ? a1.sharedSizeBytes : a2.sharedSizeBytes);
-    max_dyn = optin - st;
+// Dynamic shared memory a BUG-step launch may plan with on the current
+// device: the opt-in limit less the kernels' static shared memory, looked up
+// once per device under a lock (0 on error, with the message set).
+static int step_max_dyn_smem() {
+  static std::mutex mu;
+  static int per_dev[kMaxDevices] = {0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    set_error("bug step: no usable current device (%s)", cudaGetErrorString(e));
+    return 0;
   }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!per_dev[dev]) {
+    cudaFuncAttributes a1, a2;
+    int optin = 0;
+    e = cudaFuncGetAttributes(&a1, (const void*)bug_step_kernel<true>);
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&a2, (const void*)bug_step_kernel<false>);
+    if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e != cudaSuccess) {
+      set_error("bug step: %s", cudaGetErrorString(e));
+      return 0;
+    }
+    const int st = (int)(a1.sharedSizeBytes > a2.sharedSizeBytes ? a1.sharedSizeBytes : a2.sharedSizeBytes);
+    per_dev[dev] = optin - st;
+  }
+  return per_dev[dev];
+}
+
+int launch_bug_step(const BugStepBatch& batch_in, int n_problems, int n_streams, cudaStream_t stream) {
+  const int max_dyn = step_max_dyn_smem();
+  if (max_dyn <= kStepMiscBytes) return KVD_ERR_CUDA;
   BugStepBatch batch = batch_in;
   const BugStepArgs& a0 = batch.s[0];
   if (a0.ld > kMaxStepLd) {
@@ -2009,8 +2030,13 @@ extern "C" int kvd_bug_step(int32_t n_batch, int32_t n, int32_t b, int32_t rank_
   if (rc) return rc;
   if (m_out) {
     // m is dims[p][2]: gather with a strided 2-D copy
-    cudaMemcpy2DAsync(m_out, sizeof(int32_t), dims + 2, 4 * sizeof(int), sizeof(int32_t), n_batch,
-                      cudaMemcpyDeviceToDevice, (cudaStream_t)stream);
+    const cudaError_t e = cudaMemcpy2DAsync(m_out, sizeof(int32_t), dims + 2, 4 * sizeof(int),
+                                            sizeof(int32_t), n_batch, cudaMemcpyDeviceToDevice,
+                                            (cudaStream_t)stream);
+    if (e != cudaSuccess) {
+      set_error("kvd_bug_step: copying m: %s", cudaGetErrorString(e));
+      return KVD_ERR_CUDA;
+    }
   }
   return check_launch("kvd_bug_step");
 }

@@ -29,6 +29,20 @@ template <> struct IO<__nv_bfloat16> {
 template <typename T> KVD_DEVICE float load_f(const T* p) { return IO<T>::load(p); }
 template <typename T> KVD_DEVICE void store_f(T* p, float v) { IO<T>::store(p, v); }
 
+// ------------------------------------------------------------ ranking
+
+// Total-order key of a score for rank counting: a larger value gets a larger
+// key, -0 and +0 tie, and every NaN ties with every other NaN above +inf --
+// the order torch's stable sort gives (bug_cache.py:810 argsorts the scores
+// with it).  Counting ranks over keys is a strict order with the index as tie
+// break, so exactly k candidates have rank < k whatever the inputs hold.
+KVD_DEVICE unsigned order_key(float v) {
+  unsigned b = __float_as_uint(v);
+  if (v != v) b = 0x7fc00000u;
+  else if (v == 0.f) b = 0u;
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
 // ------------------------------------------------------------ reductions
 
 KVD_DEVICE float warp_sum(float v) {

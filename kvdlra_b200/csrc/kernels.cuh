@@ -6,6 +6,9 @@
 
 namespace kvd {
 
+// Devices a process may drive through this library (per-device tables).
+constexpr int kMaxDevices = 64;
+
 struct BugStepArgs {
   int n, b, rank_cap, ld;
   const float* u; float* u_out; long u_sp;   // [P][n][ld]
@@ -91,6 +94,7 @@ struct KTimerScope {
 // Allow `func` to use `bytes` of dynamic shared memory (checked against the
 // device opt-in limit minus the kernel's static shared memory).
 int ensure_smem(const void* func, size_t bytes, const char* name);
+int device_smem_optin();
 using kvd::BugStepBatch; using kvd::CarryBatch; using kvd::CandSrc; using kvd::RopeArgs; using kvd::SelectOut;
 long bug_step_ws_per_problem(int n, int b, int ld);
 constexpr int kMaxStepLd = 512;  // widest basis the BUG step supports

@@ -12,9 +12,11 @@
 // (16 MiB).  Every GPU that loads the library holds it until the process
 // exits.  Its device address is looked up once per device, with that device
 // current, by the first call on that device -- so make that first call before
-// any stream capture.  All calls share the one array and it keeps the last
-// call's contents; nothing in it has to start at zero (the step writes every
-// scratch value before reading it).  Two calls whose executions overlap on the
+// any stream capture.  A call uses the scratch of the device that is current
+// on the calling thread, so the stream it is given must belong to that device
+// (as every entry point of this library assumes).  All calls share the one
+// array and it keeps the last call's contents; nothing in it has to start at
+// zero (the step writes every scratch value before reading it).  Two calls whose executions overlap on the
 // GPU (different streams, or concurrent host threads) race on the scratch and
 // must be serialised by the caller.
 #include <mutex>
@@ -24,7 +26,7 @@
 namespace {
 
 constexpr size_t kNoAllocScratchBytes = size_t(16) << 20;
-constexpr int kMaxDevices = 64;
+using kvd::kMaxDevices;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 

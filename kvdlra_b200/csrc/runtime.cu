@@ -99,16 +99,35 @@ KTimerScope::~KTimerScope() {
   if (slot < (int)t.pending.size()) cudaEventRecord(t.pending[slot].b, s);
 }
 
+// Largest dynamic shared memory a block may opt in to on the current device
+// (cached per device; 0 when it cannot be read).
+int device_smem_optin() {
+  static std::mutex mu;
+  static int per_dev[kvd::kMaxDevices] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kvd::kMaxDevices) return 0;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!per_dev[dev] &&
+      cudaDeviceGetAttribute(&per_dev[dev], cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
+    per_dev[dev] = 0;
+  return per_dev[dev];
+}
+
+// The dynamic shared-memory opt-in is an attribute of the function in the
+// current device's context, so grants are remembered per (device, function):
+// a process driving several GPUs opts in on each of them.
 int ensure_smem(const void* func, size_t bytes, const char* name) {
   static std::mutex mu;
-  static std::unordered_map<const void*, size_t> granted;
-  std::lock_guard<std::mutex> lock(mu);
-  auto it = granted.find(func);
-  if (it != granted.end() && it->second >= bytes) return KVD_OK;
-  cudaFuncAttributes attr;
-  cudaError_t e = cudaFuncGetAttributes(&attr, func);
+  static std::unordered_map<const void*, size_t> granted[kvd::kMaxDevices];
   int dev = 0, optin = 0;
-  if (e == cudaSuccess) e = cudaGetDevice(&dev);
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) { set_error("%s: %s", name, cudaGetErrorString(e)); return KVD_ERR_CUDA; }
+  if (dev < 0 || dev >= kvd::kMaxDevices) { set_error("%s: device %d beyond %d", name, dev, kvd::kMaxDevices); return KVD_ERR_ARG; }
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = granted[dev].find(func);
+  if (it != granted[dev].end() && it->second >= bytes) return KVD_OK;
+  cudaFuncAttributes attr;
+  e = cudaFuncGetAttributes(&attr, func);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
   if (e != cudaSuccess) { set_error("%s: %s", name, cudaGetErrorString(e)); return KVD_ERR_CUDA; }
   if (bytes + attr.sharedSizeBytes > (size_t)optin) {
@@ -119,7 +138,7 @@ int ensure_smem(const void* func, size_t bytes, const char* name) {
   const size_t want = (size_t)optin - attr.sharedSizeBytes;  // grant the maximum once
   e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)want);
   if (e != cudaSuccess) { set_error("%s: %s", name, cudaGetErrorString(e)); return KVD_ERR_CUDA; }
-  granted[func] = want;
+  granted[dev][func] = want;
   return KVD_OK;
 }
 

@@ -308,16 +308,20 @@ __global__ void __launch_bounds__(512) slash_rank_kernel(CandSrc<T> src, int m, 
     sel[i] = v;
   }
   __syncthreads();
+  // the boosted scores become total-order keys in place (NaN-proof ranks)
+  unsigned* skey = reinterpret_cast<unsigned*>(sel);
+  for (int i = threadIdx.x; i < m; i += blockDim.x) skey[i] = order_key(sel[i]);
+  __syncthreads();
   const int d = m - keep_n;
   int kbase = 0, dbase = 0;
   for (int i0 = 0; i0 < m; i0 += blockDim.x) {
     const int i = i0 + threadIdx.x;
     int kept = 0;
     if (i < m) {
-      const float v = sel[i];
+      const unsigned v = skey[i];
       int rank = 0;
       for (int j = 0; j < m; ++j) {
-        const float w = sel[j];
+        const unsigned w = skey[j];
         rank += (w > v) || (w == v && j < i);
       }
       kept = rank < keep_n;

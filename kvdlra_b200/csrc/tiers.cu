@@ -236,7 +236,7 @@ __global__ void __launch_bounds__(256) mid_hat_tiled_kernel(
     const float* uk, const float* uv, long u_sp, int ld, const int* rk, const int* rv,
     const float* ck, const float* cv, long c_sp, const int* mid_pos, long mid_sp, int pos_base,
     int W, int H, const float* inv_freq, float scale, T* ok, T* ov, long ob, long oh, long ot,
-    int l0) {
+    int l0, int rc_cols) {
   constexpr int HALF = D / 2, FP = HALF / 16, NQ = 2 * FP;
   extern __shared__ __align__(16) float msm[];
   const int p = blockIdx.y;
@@ -246,9 +246,9 @@ __global__ void __launch_bounds__(256) mid_hat_tiled_kernel(
   const int rmax = max(r_k, r_v);
   float* ctk = msm;                          // [ld][kMhCtPitch], token-contiguous
   float* ctv = ctk + ld * kMhCtPitch;
-  float* usk = ctv + ld * kMhCtPitch;        // [ld][16][NQ]
-  float* usv = usk + ld * D;
-  float* cs = usv + ld * D;                  // [kMhTok][HALF][2]
+  float* usk = ctv + ld * kMhCtPitch;        // [rc_cols][16][NQ]: a chunk of the head's basis
+  float* usv = usk + rc_cols * D;
+  float* cs = usv + rc_cols * D;             // [kMhTok][HALF][2]
   const int tid = threadIdx.x;
   for (int e = tid; e < kMhTok * ld; e += blockDim.x) {
     const int t = e / ld, c = e % ld;
@@ -269,40 +269,46 @@ __global__ void __launch_bounds__(256) mid_hat_tiled_kernel(
   const float* Uk = uk + p * u_sp;
   const float* Uv = uv + p * u_sp;
   for (int h = 0; h < H; ++h) {
-    __syncthreads();
-    for (int e = tid; e < D * ld; e += blockDim.x) {
-      const int d = e / ld, c = e % ld;
-      const int hi = d >= HALF, f = hi ? d - HALF : d;
-      const int q = (c * 16 + f / FP) * NQ + hi * FP + f % FP;
-      usk[q] = c < r_k ? Uk[(long)(h * D + d) * ld + c] : 0.f;
-      usv[q] = c < r_v ? Uv[(long)(h * D + d) * ld + c] : 0.f;
-    }
-    __syncthreads();
     float ak[4][NQ], av[4][NQ];
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
       for (int q = 0; q < NQ; ++q) { ak[i][q] = 0.f; av[i][q] = 0.f; }
-#pragma unroll 4
-    for (int c = 0; c < rmax; ++c) {
-      const float4 a4 = *reinterpret_cast<const float4*>(ctk + c * kMhCtPitch + 4 * ty);
-      const float4 b4 = *reinterpret_cast<const float4*>(ctv + c * kMhCtPitch + 4 * ty);
-      const float a[4] = {a4.x, a4.y, a4.z, a4.w}, b[4] = {b4.x, b4.y, b4.z, b4.w};
-      float wk[NQ], wv[NQ];
-#pragma unroll
-      for (int q = 0; q < NQ; q += 4) {
-        const float4 x = *reinterpret_cast<const float4*>(usk + (c * 16 + tx) * NQ + q);
-        const float4 y = *reinterpret_cast<const float4*>(usv + (c * 16 + tx) * NQ + q);
-        wk[q] = x.x; wk[q + 1] = x.y; wk[q + 2] = x.z; wk[q + 3] = x.w;
-        wv[q] = y.x; wv[q + 1] = y.y; wv[q + 2] = y.z; wv[q + 3] = y.w;
+    // the head's basis rows are staged rc_cols rank columns at a time (the
+    // whole rank when it fits); the sum over c keeps its order across chunks
+    for (int c0 = 0; c0 < rmax; c0 += rc_cols) {
+      const int cn = min(rc_cols, rmax - c0);
+      __syncthreads();
+      for (int e = tid; e < D * cn; e += blockDim.x) {
+        const int d = e / cn, cl = e % cn, c = c0 + cl;
+        const int hi = d >= HALF, f = hi ? d - HALF : d;
+        const int q = (cl * 16 + f / FP) * NQ + hi * FP + f % FP;
+        usk[q] = c < r_k ? Uk[(long)(h * D + d) * ld + c] : 0.f;
+        usv[q] = c < r_v ? Uv[(long)(h * D + d) * ld + c] : 0.f;
       }
+      __syncthreads();
+#pragma unroll 4
+      for (int cl = 0; cl < cn; ++cl) {
+        const int c = c0 + cl;
+        const float4 a4 = *reinterpret_cast<const float4*>(ctk + c * kMhCtPitch + 4 * ty);
+        const float4 b4 = *reinterpret_cast<const float4*>(ctv + c * kMhCtPitch + 4 * ty);
+        const float a[4] = {a4.x, a4.y, a4.z, a4.w}, b[4] = {b4.x, b4.y, b4.z, b4.w};
+        float wk[NQ], wv[NQ];
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int q = 0; q < NQ; ++q) {
-          ak[i][q] = fmaf(wk[q], a[i], ak[i][q]);
-          av[i][q] = fmaf(wv[q], b[i], av[i][q]);
+        for (int q = 0; q < NQ; q += 4) {
+          const float4 x = *reinterpret_cast<const float4*>(usk + (cl * 16 + tx) * NQ + q);
+          const float4 y = *reinterpret_cast<const float4*>(usv + (cl * 16 + tx) * NQ + q);
+          wk[q] = x.x; wk[q + 1] = x.y; wk[q + 2] = x.z; wk[q + 3] = x.w;
+          wv[q] = y.x; wv[q + 1] = y.y; wv[q + 2] = y.z; wv[q + 3] = y.w;
         }
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int q = 0; q < NQ; ++q) {
+            ak[i][q] = fmaf(wk[q], a[i], ak[i][q]);
+            av[i][q] = fmaf(wv[q], b[i], av[i][q]);
+          }
+      }
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -619,7 +625,13 @@ int launch_peek(const kvd_config& c, const kvd_buffers& b, const kvd_counters& k
           c.inv_freq, c.rope_scaling, okp, ovp, ob, oh, ot, l0, tpc);
       }
     } else if (tiled) {
-      const int smem = 4 * (2 * ld * kMhCtPitch + 2 * ld * D + kMhTok * half * 2);
+      // the coordinate tile stays whole; the basis is staged in rank chunks
+      // sized to the device's shared-memory limit
+      auto smem_for = [&](int rcc) { return 4 * (2 * ld * kMhCtPitch + 2 * rcc * D + kMhTok * half * 2); };
+      const int limit = device_smem_optin();
+      int rcc = ld;
+      while (rcc > 4 && smem_for(rcc) > limit) rcc = ((rcc + 1) / 2 + 3) & ~3;
+      const int smem = smem_for(rcc);
       auto fn = D == 64 ? mid_hat_tiled_kernel<T, 64> : mid_hat_tiled_kernel<T, 128>;
       if (int rc2 = ensure_smem((const void*)fn, smem, "mid_hat_kernel")) return rc2;
       dim3 grid((k.w_len + kMhTok - 1) / kMhTok, count);
@@ -629,7 +641,7 @@ int launch_peek(const kvd_config& c, const kvd_buffers& b, const kvd_counters& k
           b.u_k[k.u_sel] + p0 * u_sp, b.u_v[k.u_sel] + p0 * u_sp, u_sp, ld, b.r_k + p0,
           b.r_v + p0, b.c_k + p0 * c_sp, b.c_v + p0 * c_sp, c_sp,
           track_pos ? b.mid_pos + (long)p0 * c.w_cap : nullptr, c.w_cap, pos_base, k.w_len, H,
-          c.inv_freq, c.rope_scaling, okp, ovp, ob, oh, ot, l0);
+          c.inv_freq, c.rope_scaling, okp, ovp, ob, oh, ot, l0, rcc);
       }
     } else {
       const int smem = 4 * (2 * kMidTile * ld + 2 * D * ld + kMidTile * half * 2);

@@ -43,11 +43,10 @@ def bug_step_batched(u: Tensor, sigma: Tensor, r: Tensor, block: Tensor, rank_ca
     L = N.lib()
     wsb = int(L.kvd_bug_step_workspace_bytes(nb, n, b, ld)) + 16 * nb + 64
     ws = torch.empty(wsb, dtype=torch.uint8, device=u.device)
-    N.check(L.kvd_bug_step(nb, n, b, rank_cap, ld, u.data_ptr(), u_out.data_ptr(), sigma.data_ptr(),
-                           r.data_ptr(), block.contiguous().data_ptr(), rot.data_ptr(), m.data_ptr(),
-                           coords.data_ptr(), int(theta is not None), float(theta or 0.0),
-                           status.data_ptr(), ws.data_ptr(), wsb, N.stream_ptr(u.device)),
-            "kvd_bug_step")
+    N.call(u.device, "kvd_bug_step", nb, n, b, rank_cap, ld, u.data_ptr(), u_out.data_ptr(),
+           sigma.data_ptr(), r.data_ptr(), block.contiguous().data_ptr(), rot.data_ptr(),
+           m.data_ptr(), coords.data_ptr(), int(theta is not None), float(theta or 0.0),
+           status.data_ptr(), ws.data_ptr(), wsb, N.stream_ptr(u.device))
     if int(status.sum()) != 0:
         raise N.KvdError(6, "kvd_bug_step", f"device status {status.tolist()}")
     return u_out, sigma, r, rot, m
@@ -126,8 +125,7 @@ def blocked_bug_project(M: Tensor, rank_cap: int, block_size: int = 128, *,
     L = N.lib()
     wsb = int(L.kvd_blocked_project_workspace_bytes(n, t, rank_cap, block_size)) + 256
     ws = torch.empty(wsb, dtype=torch.uint8, device=M.device)
-    N.check(L.kvd_blocked_project(n, t, rank_cap, block_size, 0, 0, int(theta is not None),
-                                  float(theta or 0.0), xt.data_ptr(), out.data_ptr(), None,
-                                  ws.data_ptr(), wsb, N.stream_ptr(M.device)),
-            "kvd_blocked_project")
+    N.call(M.device, "kvd_blocked_project", n, t, rank_cap, block_size, 0, 0, int(theta is not None),
+           float(theta or 0.0), xt.data_ptr(), out.data_ptr(), None,
+           ws.data_ptr(), wsb, N.stream_ptr(M.device))
     return out.T.to(M.dtype)

@@ -140,10 +140,9 @@ class BUGPress(_HookedPress):
         L = N.lib()
         wsb = int(L.kvd_blocked_project_workspace_bytes(n, t, self.rank, self.block_size)) + 256
         ws = torch.empty(wsb, dtype=torch.uint8, device=dev)
-        N.check(L.kvd_blocked_project(n, t, self.rank, self.block_size, n_sink, n_exact, 0, 0.0,
-                                      xt.data_ptr(), out.data_ptr() if out is not None else None,
-                                      mask.data_ptr(), ws.data_ptr(), wsb, N.stream_ptr(dev)),
-                "kvd_blocked_project")
+        N.call(dev, "kvd_blocked_project", n, t, self.rank, self.block_size, n_sink, n_exact, 0, 0.0,
+               xt.data_ptr(), out.data_ptr() if out is not None else None,
+               mask.data_ptr(), ws.data_ptr(), wsb, N.stream_ptr(dev))
         return out, mask.bool()
 
     def _exact_mask(self, mat: Tensor) -> Tensor:

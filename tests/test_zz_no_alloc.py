@@ -63,11 +63,17 @@ def _step(L, N, noalloc: bool, u, sig, r, x, rank_cap):
     return u_out, sig, r, rot, m, coords
 
 
-def test_noalloc_step_matches_workspace_step_twice() -> None:
+@pytest.mark.parametrize("nb,n,ld,rank_cap,b", [
+    (6, 256, 24, 20, 16),  # every working region in shared memory
+    # a 128-column block's residual SVD does not fit in shared memory: the
+    # kernel keeps its working regions in the scratch array itself, so the
+    # second call runs over what the first one left there
+    (4, 512, 32, 32, 128),
+])
+def test_noalloc_step_matches_workspace_step_twice(nb: int, n: int, ld: int, rank_cap: int, b: int) -> None:
     L, N = _lib()
     dev = torch.device("cuda")
-    rng = np.random.default_rng(42)
-    nb, n, ld, rank_cap, b = 6, 256, 24, 20, 16
+    rng = np.random.default_rng(42 + b)
     basis = np.linalg.qr(rng.standard_normal((n, 30)))[0]
     blocks = []
     for _ in range(2):
