@@ -14,8 +14,11 @@ One step = reset + the whole ingest + the whole decode.  ``value`` is ingest
 tokens/s over all ranks (each rank streams its own sequence: weak scaling, no
 collective on the data path); decode tokens/s is reported beside it.
 
-``--impl reference`` times the CPU oracle port (numpy restatement of the
-reference) on a bounded sample of the same workload with all host threads.
+``--impl reference`` times the reference's own CPU implementation (kvdlra's
+``BugStreamingLayer`` on CPU PyTorch, installed unmodified in
+``baseline/_ref`` by ``baseline/install_ref.py``) on the host cores, each step
+one full-length layer of the same workload scaled by the layer count; without
+that install it times the oracle port (numpy restatement) instead.
 """
 
 from __future__ import annotations
@@ -135,9 +138,9 @@ def new_cache(w: dict, torch):
         retention="lowrank_surprise", hh_budget=w["hh"], hh_select="surprise")
 
 
-# DRAM bytes (read + write) of one launch, from ncu captures of the same launch
-# shape (profiles/bug_step_kernel_r32_n512_b16.md); kernels not captured at the
-# workload's shape are left out.
+# DRAM bytes (read + write) of one launch, from an ncu capture of the same
+# launch shape (the steady-state absorb step: n = 512, r = 32, 16 columns);
+# kernels not captured at the workload's shape are left out.
 DRAM_BYTES_PER_LAUNCH = {"bug_step_kernel": 3.39e6}
 
 
@@ -216,7 +219,8 @@ def run_ours(args, w: dict) -> None:
         from datetime import timedelta
 
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600))
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     from kvdlra_b200 import _native as N
@@ -378,7 +382,7 @@ def run_ours(args, w: dict) -> None:
         total_ms = sum(x[0] for x in prof.values()) or 1e-9
         kernels = {k: {"total_ms": round(v[0], 4), "launches": v[1], "share": round(v[0] / total_ms, 4)}
                    for k, v in sorted(prof.items(), key=lambda kv: -kv[1][0])}
-        cpu = None if args.no_cpu_baseline else cpu_baseline(w, quick=True)
+        cpu = None if args.no_cpu_baseline else cpu_baseline(w)
         result = {
             "metric": METRIC,
             "value": world * T * args.steps / (ingest_ms / 1e3),
@@ -392,12 +396,7 @@ def run_ours(args, w: dict) -> None:
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic (seeded low-rank+noise KV streams with needles; inputs > L2)",
-            "config": {"workload": w["name"], "layers": w["layers"], "kv_heads": w["kv_heads"],
-                       "head_dim": w["head_dim"], "q_heads": w["q_heads"], "tokens": T,
-                       "chunk": C, "rank": w["rank"], "hh_budget": w["hh"], "sinks": w["sinks"],
-                       "ring": w["ring"], "absorb_block": w["absorb"], "decode_tokens": dec,
-                       "sequences_per_gpu": 1, "parallelism": f"dp{world} (independent sequences)",
-                       "l2": "inputs larger than L2"},
+            "config": bench_config(w, world),
             "decode": {"value": world * dec * args.steps / (decode_ms / 1e3), "unit": "tokens/s"},
             "ingest_ms_per_step": ingest_ms / args.steps,
             "decode_ms_per_step": decode_ms / args.steps,
@@ -417,11 +416,87 @@ def run_ours(args, w: dict) -> None:
         dist.destroy_process_group()
 
 
-def cpu_baseline(w: dict, quick: bool = False, sample_tokens: int = 2048, sample_decode: int = 16) -> dict:
-    """Time the oracle port (numpy restatement of the reference path) on one
-    layer of the workload: ``sample_tokens`` ingested tokens plus
-    ``sample_decode`` decode steps, scaled to the whole model (per token every
-    layer is processed)."""
+REF_DIR = REPO / "baseline" / "_ref"
+
+
+def _host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:  # pragma: no cover
+        return os.cpu_count() or 1
+
+
+def _reference_layer(w: dict):
+    """The reference's own ``BugStreamingLayer`` (kvdlra, installed unmodified
+    in ``baseline/_ref``), configured as the workload's layers, with the
+    model's rotary module (transformers' Llama rotary at the workload's
+    head_dim and RoPE theta)."""
+    if str(REF_DIR) not in sys.path:
+        sys.path.insert(0, str(REF_DIR))
+    from kvdlra.cache.bug_cache import BugStreamingLayer, _RopeAngles
+    from transformers import LlamaConfig
+    from transformers.models.llama.modeling_llama import LlamaRotaryEmbedding
+
+    H, D = w["kv_heads"], w["head_dim"]
+    rot = LlamaRotaryEmbedding(LlamaConfig(
+        hidden_size=w["q_heads"] * D, num_attention_heads=w["q_heads"], num_key_value_heads=H,
+        head_dim=D, rope_theta=w["theta"], max_position_embeddings=1 << 18))
+    return BugStreamingLayer(
+        rope=_RopeAngles(rot), rank=w["rank"], coord_budget=w["tokens"] + w["ring"] + w["absorb"],
+        recent_window=w["ring"], absorb_block=w["absorb"], n_sink=w["sinks"],
+        prefill_block_size=w["prefill_block"], retention="lowrank_surprise", hh_budget=w["hh"],
+        hh_select="surprise", seed_hh_warmup=w.get("seed_warmup", False))
+
+
+def cpu_reference(w: dict, sample_tokens: int, sample_decode: int) -> dict:
+    """Time the reference's own CPU implementation of the path (PyTorch on the
+    host cores, every thread): one layer of the workload ingests
+    ``sample_tokens`` tokens in the workload's chunks (update in ingest mode +
+    consolidate, bug_cache.py:1404-1429), then ``sample_decode`` decode steps
+    (update + peek, bug_cache.py:1483-1519) each followed by the GQA attention
+    HF runs over the returned peek (SDPA).  Every layer of the model does the
+    same work per token, so model tokens/s = layer tokens/s / layers."""
+    import torch
+
+    from kvdlra_b200.synthetic import lowrank_stream
+
+    threads = _host_threads()
+    torch.set_num_threads(threads)
+    H, D = w["kv_heads"], w["head_dim"]
+    s = lowrank_stream(H, D, sample_tokens + sample_decode, n_needles=16, theta=w["theta"], seed=0)
+    bf = torch.bfloat16
+    k = torch.from_numpy(s.k_post)[None].to(bf)
+    v = torch.from_numpy(s.v)[None].to(bf)
+    q = (torch.randn(sample_decode, 1, w["q_heads"], 1, D, generator=torch.Generator().manual_seed(0))
+         / math.sqrt(D)).to(bf)
+    layer = _reference_layer(w)
+    with torch.no_grad():
+        layer._mode = "ingest"  # what BugStreamingCache.ingesting() sets (bug_cache.py:1884-1895)
+        t0 = time.perf_counter()
+        for c0 in range(0, sample_tokens, w["chunk"]):
+            c1 = min(sample_tokens, c0 + w["chunk"])
+            layer.update(k[:, :, c0:c1], v[:, :, c0:c1])
+            layer.consolidate()
+        t_ing = time.perf_counter() - t0
+        layer._mode = "normal"
+        t0 = time.perf_counter()
+        for j in range(sample_decode):
+            p = sample_tokens + j
+            kr, vr = layer.update(k[:, :, p : p + 1], v[:, :, p : p + 1])
+            torch.nn.functional.scaled_dot_product_attention(q[j], kr, vr, enable_gqa=True)
+        t_dec = time.perf_counter() - t0
+    L = w["layers"]
+    return {"value": sample_tokens / t_ing / L, "unit": "tokens/s", "cores": threads,
+            "kind": "reference", "decode_tokens_per_s": sample_decode / t_dec / L,
+            "sample": (f"kvdlra BugStreamingLayer (the reference, CPU PyTorch, {threads} threads): "
+                       f"1 of {L} layers, {sample_tokens} ingested tokens in chunks of {w['chunk']} "
+                       f"+ {sample_decode} decode steps with SDPA over the peek, scaled by the layer count")}
+
+
+def cpu_port(w: dict, sample_tokens: int = 2048, sample_decode: int = 16) -> dict:
+    """The oracle port (numpy restatement of the reference path) on one layer,
+    scaled by the layer count: the fallback when the reference itself is not
+    installed, and a labelled second line beside it."""
     from oracle.bug_oracle import OracleLayer, RopeSpec, default_inv_freq, gqa_attention
     from kvdlra_b200.synthetic import lowrank_stream
 
@@ -431,7 +506,8 @@ def cpu_baseline(w: dict, quick: bool = False, sample_tokens: int = 2048, sample
                       coord_budget=w["tokens"] + w["ring"] + w["absorb"], recent_window=w["ring"],
                       absorb_block=w["absorb"], n_sink=w["sinks"],
                       prefill_block_size=w["prefill_block"], retention="lowrank_surprise",
-                      hh_budget=w["hh"], hh_select="surprise", dtype="bfloat16")
+                      hh_budget=w["hh"], hh_select="surprise", dtype="bfloat16",
+                      seed_hh_warmup=w.get("seed_warmup", False))
 
     def mat(x):
         return x.transpose(0, 2, 1).reshape(H * D, -1)
@@ -456,38 +532,66 @@ def cpu_baseline(w: dict, quick: bool = False, sample_tokens: int = 2048, sample
         cores = max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
     except Exception:  # noqa: BLE001
         cores = os.cpu_count() or 1
-    ingest_tps = sample_tokens / t_ing / w["layers"]
-    return {"value": ingest_tps, "unit": "tokens/s", "cores": int(cores), "kind": "port",
-            "decode_tokens_per_s": sample_decode / t_dec / w["layers"],
-            "sample": (f"1 of {w['layers']} layers, {sample_tokens} ingested tokens (chunk "
-                       f"{w['chunk']}) + {sample_decode} decode steps, scaled by the layer count")}
+    return {"value": sample_tokens / t_ing / w["layers"], "unit": "tokens/s", "cores": int(cores),
+            "kind": "port", "decode_tokens_per_s": sample_decode / t_dec / w["layers"],
+            "sample": (f"oracle port (numpy): 1 of {w['layers']} layers, {sample_tokens} ingested tokens "
+                       f"(chunk {w['chunk']}) + {sample_decode} decode steps, scaled by the layer count")}
+
+
+def cpu_baseline(w: dict) -> dict:
+    """The CPU baseline beside our arm's line: the reference itself when it is
+    installed (one full-length layer of the workload), else the oracle port."""
+    if (REF_DIR / "kvdlra").is_dir():
+        return cpu_reference(w, w["tokens"], 32)
+    return cpu_port(w)
+
+
+def bench_config(w: dict, world: int) -> dict:
+    """The ``config`` object both arms print (identical for the same workload)."""
+    return {"workload": w["name"], "layers": w["layers"], "kv_heads": w["kv_heads"],
+            "head_dim": w["head_dim"], "q_heads": w["q_heads"], "tokens": w["tokens"],
+            "chunk": w["chunk"], "rank": w["rank"], "hh_budget": w["hh"], "sinks": w["sinks"],
+            "ring": w["ring"], "absorb_block": w["absorb"], "decode_tokens": w["decode"],
+            "seed_warmup": bool(w.get("seed_warmup", False)),
+            "sequences_per_gpu": w.get("batch", 1),
+            "parallelism": f"dp{world} (independent sequences)", "l2": "inputs larger than L2"}
 
 
 def run_reference(args, w: dict) -> None:
+    """The reference arm: the reference's own CPU implementation on the host
+    cores (rank 0 only), each step one full-length layer of the workload."""
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
+    have_ref = (REF_DIR / "kvdlra").is_dir()
     for _ in range(args.warmup):
-        cpu_baseline(w, sample_tokens=1024, sample_decode=4)
+        if have_ref:
+            cpu_reference(w, min(1024, w["tokens"]), 4)
+        else:
+            cpu_port(w, 512, 4)
     vals, decs, t_tot = [], [], time.perf_counter()
     for _ in range(args.steps):
-        cb = cpu_baseline(w, sample_tokens=2048, sample_decode=16)
+        cb = cpu_reference(w, w["tokens"], 32) if have_ref else cpu_port(w)
         vals.append(cb["value"])
         decs.append(cb["decode_tokens_per_s"])
     t_tot = time.perf_counter() - t_tot
     v = float(np.mean(vals))
+    port = cpu_port(w) if have_ref else None
     out = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s",
-        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1e3 * t_tot / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32 (bf16 tiers emulated)", "data": "synthetic",
-        "config": {"workload": w["name"], "tokens": w["tokens"], "chunk": w["chunk"], "rank": w["rank"],
-                   "hh_budget": w["hh"], "layers": w["layers"]},
+        "vs_baseline": None, "dtype": "bf16 (tiers), f32 (BUG math)", "data": "synthetic",
+        "config": bench_config(w, world),
         "decode": {"value": float(np.mean(decs)), "unit": "tokens/s"},
-        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cb["cores"], "kind": "port",
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cb["cores"], "kind": cb["kind"],
                          "sample": cb["sample"]},
         "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if port is not None:
+        out["oracle_port"] = {"value": port["value"], "decode_tokens_per_s": port["decode_tokens_per_s"],
+                              "cores": port["cores"], "sample": port["sample"]}
     print(json.dumps(out))
 
 
