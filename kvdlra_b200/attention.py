@@ -1,0 +1,82 @@
+"""Factored decode behind transformers' own attention call.
+
+In the reference, a decode step of ``LlamaAttention`` on a
+``BugStreamingCache`` gets the dense retained cache back from
+``past_key_values.update`` -- ``[sinks | exact tier | RoPE(U_k C_k) | ring]``
+re-materialised in the model dtype (bug_cache.py:1483-1519, 1540-1575) -- and
+runs stock SDPA over it.  Here the same call reaches the factored decode
+kernel instead: ``enable_factored_decode(model)`` registers an attention
+function under the name ``"kvdlra_factored"`` (transformers'
+``AttentionInterface``) and selects it for the model.  When the model runs on
+a :class:`kvdlra_b200.BugStreamingCache`, the cache's decode-step ``update``
+(append, due absorbs) returns the step's own key/value tagged with the layer
+instead of a dense peek, and the registered function answers the query with
+``kvd_factored_decode`` over the compressed state -- keys rebuilt from the
+coordinates with RoPE at each token's true position, values accumulated in
+coordinate space, the verbatim tiers read in place.  Every other call
+(single-shot prefill, chunked ingest, frozen scoring, or any cache that is
+not a ``BugStreamingCache``) goes to SDPA over what ``update`` returned,
+exactly as before.  ``update``'s return contract is unchanged for models that
+do not select the function, so lock-step comparisons against the reference's
+dense peek still hold.
+"""
+
+from __future__ import annotations
+
+from typing import Any
+
+import torch
+from transformers import AttentionInterface
+from transformers.integrations.sdpa_attention import sdpa_attention_forward
+from transformers.masking_utils import ALL_MASK_ATTENTION_FUNCTIONS, AttentionMaskInterface
+
+__all__ = ["ATTN_NAME", "enable_factored_decode", "factored_attention_forward", "uses_factored_decode"]
+
+ATTN_NAME = "kvdlra_factored"
+_TAG = "_kvdlra_layer"
+
+
+def factored_attention_forward(module: torch.nn.Module, query: torch.Tensor, key: torch.Tensor,
+                               value: torch.Tensor, attention_mask: torch.Tensor | None,
+                               dropout: float = 0.0, scaling: float | None = None,
+                               **kwargs: Any) -> tuple[torch.Tensor, None]:
+    """transformers attention function: factored decode where the cache
+    tagged the step, SDPA otherwise.  ``query`` is ``(B, Hq, q_len, D)``; the
+    output is ``(B, q_len, Hq, D)`` as transformers expects."""
+    layer = getattr(key, _TAG, None)
+    if layer is None:
+        return sdpa_attention_forward(module, query, key, value, attention_mask, dropout=dropout,
+                                      scaling=scaling, **kwargs)
+    if query.shape[2] != 1:
+        raise RuntimeError("factored decode answers one query token per step")
+    if dropout:
+        raise NotImplementedError("factored decode has no attention dropout (inference only)")
+    out = layer.factored_attention(query[:, :, 0, :], scaling=scaling)  # (B, Hq, D)
+    return out.unsqueeze(1), None
+
+
+AttentionInterface.register(ATTN_NAME, factored_attention_forward)
+AttentionMaskInterface.register(ATTN_NAME, ALL_MASK_ATTENTION_FUNCTIONS["sdpa"])
+
+
+def enable_factored_decode(model: Any) -> Any:
+    """Select the factored decode for ``model``'s attention layers (their
+    non-decode calls keep SDPA).  Returns the model."""
+    if hasattr(model, "set_attn_implementation"):
+        model.set_attn_implementation(ATTN_NAME)
+    else:
+        model.config._attn_implementation = ATTN_NAME
+    return model
+
+
+def uses_factored_decode(config: Any) -> bool:
+    """Whether a model with this config answers decode steps through the
+    factored kernel (the cache then skips its dense peek)."""
+    return config is not None and getattr(config, "_attn_implementation", None) == ATTN_NAME
+
+
+def tag_step(key: torch.Tensor, layer: Any) -> torch.Tensor:
+    """Mark a decode step's key as belonging to ``layer`` (read by
+    :func:`factored_attention_forward`)."""
+    setattr(key, _TAG, layer)
+    return key

@@ -636,9 +636,16 @@ class BugStreamingLayer(CacheLayerMixin):  # type: ignore[misc]
         self._r_cache = None
 
     def _decode_step(self, key_states: Tensor, value_states: Tensor) -> tuple[Tensor, Tensor]:
-        """bug_cache.py:1483-1494."""
+        """bug_cache.py:1483-1494.  When the owning model answers decode steps
+        with the factored kernel (:func:`kvdlra_b200.attention.enable_factored_decode`),
+        the dense peek is skipped: the step's own K/V come back tagged with
+        this layer and the model's attention call reads the compressed state."""
         self._append(key_states, value_states)
         self.consolidate()
+        if self._owner is not None and self._owner._factored_decode():
+            from .attention import tag_step
+
+            return tag_step(key_states, self), value_states
         return self._decode_peek()
 
     def _decode_peek(self, tail: tuple[Tensor, Tensor] | None = None) -> tuple[Tensor, Tensor]:
@@ -955,6 +962,7 @@ class BugStreamingCache(Cache):
             num_layers = int(model.config.num_hidden_layers)
         self._retention = retention
         self._rope = rope
+        self._model_config = getattr(model, "config", None)
         kw = dict(rank=rank, coord_budget=coord_budget, recent_window=recent_window,
                   absorb_block=absorb_block, n_sink=n_sink, theta=theta,
                   prefill_block_size=prefill_block_size, retention=retention,
@@ -979,6 +987,11 @@ class BugStreamingCache(Cache):
                                  key_states.dtype, key_states.device, self._rope,
                                  ring_cap=max(t, first.recent_window + first.absorb_block + t))
         return self._group
+
+    def _factored_decode(self) -> bool:
+        from .attention import uses_factored_decode
+
+        return uses_factored_decode(self._model_config)
 
     def _bug_layers(self) -> list[BugStreamingLayer]:
         return [ly for ly in self.layers if isinstance(ly, BugStreamingLayer)]

@@ -180,6 +180,66 @@ def case_steps() -> dict[str, np.ndarray]:
     return out
 
 
+MODEL_CASE = dict(vocab=256, hidden=256, ffn=512, layers=2, heads=8, kv_heads=2, head_dim=64,
+                  theta=500000.0, tokens=704, chunk=128, decode=24, seed=0,
+                  cache_kw=dict(rank=16, coord_budget=4096, recent_window=32, absorb_block=16,
+                                n_sink=4, retention="lowrank_surprise", hh_budget=32,
+                                hh_select="surprise"))
+
+
+def tiny_llama(case: dict):
+    """The random-init Llama of the model-level fixture (fp32, CPU init:
+    ``torch.manual_seed`` then ``LlamaForCausalLM`` -- the same weights on
+    every machine with this torch)."""
+    import torch
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    cfg = LlamaConfig(vocab_size=case["vocab"], hidden_size=case["hidden"],
+                      intermediate_size=case["ffn"], num_hidden_layers=case["layers"],
+                      num_attention_heads=case["heads"], num_key_value_heads=case["kv_heads"],
+                      head_dim=case["head_dim"], rope_theta=case["theta"],
+                      max_position_embeddings=1 << 16, initializer_range=0.02)
+    torch.manual_seed(case["seed"])
+    return LlamaForCausalLM(cfg).eval()
+
+
+def case_model() -> dict[str, np.ndarray]:
+    """The reference's BugStreamingCache under a random-init Llama, driven as
+    its harness does (scripts/w10_frontier.py:72-91 chunked prefill with
+    consolidate, scripts/w10_ruler.py:176-189 greedy decode): the last
+    position's logits after every chunk, the greedy tokens and their logits."""
+    import torch
+    from kvdlra.cache import BugStreamingCache
+
+    c = MODEL_CASE
+    model = tiny_llama(c)
+    ids = torch.randint(0, c["vocab"], (1, c["tokens"]), generator=torch.Generator().manual_seed(c["seed"] + 1))
+    cache = BugStreamingCache(model, **c["cache_kw"])
+    chunk_logits = []
+    with torch.no_grad():
+        with cache.ingesting():
+            for start in range(0, c["tokens"], c["chunk"]):
+                stop = min(c["tokens"], start + c["chunk"])
+                pos = torch.arange(start, stop).unsqueeze(0)
+                out = model(ids[:, start:stop], past_key_values=cache, use_cache=True, position_ids=pos,
+                            logits_to_keep=1)
+                cache.consolidate()
+                chunk_logits.append(out.logits[0, -1].numpy().copy())
+        nxt = int(out.logits[0, -1].argmax())
+        toks, dec_logits = [], []
+        for j in range(c["decode"]):
+            toks.append(nxt)
+            pos = torch.tensor([[c["tokens"] + j]])
+            out = model(torch.tensor([[nxt]]), past_key_values=cache, use_cache=True, position_ids=pos)
+            dec_logits.append(out.logits[0, -1].numpy().copy())
+            nxt = int(out.logits[0, -1].argmax())
+    lay = cache.layers[0]
+    print(f"model: numel={cache.stored_state_numel()} hh={lay._hh_len()} W={lay._f_len()}")
+    return {"ids": ids.numpy(), "chunk_logits": np.stack(chunk_logits), "dec_tokens": np.array(toks, np.int64),
+            "dec_logits": np.stack(dec_logits), "stored_numel": np.array(cache.stored_state_numel(), np.int64),
+            "hh_pos0": lay.hh_pos.numpy().copy()}
+
+
 def _run_case(name: str, *, heads: int, head_dim: int, t: int, chunk: int, theta: float,
               layer_kw: dict, stream_kw: dict, n_queries: int = 0, q_heads: int = 0,
               decode_tokens: int = 0, seed: int = 0, dtype: str = "float32") -> dict[str, np.ndarray]:
@@ -300,7 +360,8 @@ def main() -> None:
     import os
 
     args = sys.argv[1:]
-    src = args.pop(0) if args and not args[0] in CASES and args[0] != "steps" else os.environ.get("KVDLRA_REFERENCE_SRC")
+    src = (args.pop(0) if args and args[0] not in CASES and args[0] not in ("steps", "model")
+           else os.environ.get("KVDLRA_REFERENCE_SRC"))
     if not src or not (Path(src) / "kvdlra").is_dir():
         sys.exit("usage: make_golden.py <reference>/src [case ...]  (or set KVDLRA_REFERENCE_SRC)")
     sys.path.insert(0, src)
@@ -310,6 +371,8 @@ def main() -> None:
     names = args or ["steps", *CASES]
     if "steps" in names:
         np.savez_compressed(HERE / "steps.npz", **case_steps())
+    if "model" in names or not args:
+        np.savez_compressed(HERE / "model_llama_tiny.npz", **case_model())
     for name in names:
         if name in CASES:
             np.savez_compressed(HERE / f"{name}.npz", **_run_case(name, **CASES[name]))
