@@ -38,11 +38,28 @@ import numpy as np
 REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
-WORKLOAD = dict(
-    name="llama-3.2-1b-kv", layers=16, kv_heads=8, head_dim=64, q_heads=32, tokens=8192,
-    chunk=512, rank=32, hh=256, sinks=4, ring=128, absorb=16, prefill_block=128,
-    decode=256, theta=500000.0,
-)
+WORKLOADS = {
+    # the Llama-3.2-1B configuration's cache (the default line)
+    "llama-3.2-1b-kv": dict(
+        name="llama-3.2-1b-kv", layers=16, kv_heads=8, head_dim=64, q_heads=32, tokens=8192,
+        chunk=512, rank=32, hh=256, sinks=4, ring=128, absorb=16, prefill_block=128, decode=256,
+        theta=500000.0, batch=1, seed_warmup=False, needles=dict(n_needles=16)),
+    # the Llama-3.1-8B configuration's cache: head_dim 128, the warm-up seed,
+    # a 32-token span copied verbatim to 4 places (exact-tier capture reported)
+    "llama-3.1-8b-kv": dict(
+        name="llama-3.1-8b-kv", layers=32, kv_heads=8, head_dim=128, q_heads=32, tokens=32768,
+        chunk=1024, rank=32, hh=256, sinks=4, ring=256, absorb=16, prefill_block=128, decode=128,
+        theta=500000.0, batch=1, seed_warmup=True, needles=dict(span_copies=(4, 32))),
+    # the whole-box configuration's cache: rank 128, exact tier 1024, several
+    # independent sequences per GPU; run at a reduced length (``tokens``),
+    # the configuration's own length is ``config_tokens``
+    "whole-box-kv": dict(
+        name="whole-box-kv", layers=32, kv_heads=8, head_dim=128, q_heads=32, tokens=4096,
+        config_tokens=131072, chunk=2048, rank=128, hh=1024, sinks=4, ring=256, absorb=16,
+        prefill_block=128, decode=64, theta=500000.0, batch=8, seed_warmup=False,
+        needles=dict(n_needles=16)),
+}
+WORKLOAD = WORKLOADS["llama-3.2-1b-kv"]
 METRIC = "BUG ingest tokens/s + factored-decode tokens/s at 1/2/4/8 B200; % HBM roofline"
 
 
@@ -109,21 +126,33 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def make_inputs(w: dict, seed: int):
-    """Per-layer synthetic streams (post-RoPE K, V) for ingest + decode, and
-    the decode queries, as float32 numpy arrays."""
+def make_inputs(w: dict, seed: int, device, torch):
+    """Per-(layer, sequence) synthetic streams -- post-RoPE keys and values of
+    ``tokens + decode`` positions -- as bf16 device tensors ``(L, B, H, T', D)``,
+    the decode queries ``(decode, L, B, Hq, D)`` and the planted needle
+    positions ``[layer][sequence]``.  Each stream is built on the host
+    (numpy, seeded) and moved to the device at once, so host memory holds one
+    stream at a time."""
     from kvdlra_b200.synthetic import lowrank_stream
 
-    L, H, D, T, dec = w["layers"], w["kv_heads"], w["head_dim"], w["tokens"], w["decode"]
-    ks = np.empty((L, 1, H, T + dec, D), np.float32)
-    vs = np.empty_like(ks)
+    L, B, H, D = w["layers"], w["batch"], w["kv_heads"], w["head_dim"]
+    T, dec = w["tokens"], w["decode"]
+    bf = torch.bfloat16
+    K = torch.empty((L, B, H, T + dec, D), dtype=bf, device=device)
+    V = torch.empty_like(K)
+    needles = []
     for layer in range(L):
-        s = lowrank_stream(H, D, T + dec, n_needles=16, theta=w["theta"], seed=1000 * seed + layer)
-        ks[layer, 0] = s.k_post
-        vs[layer, 0] = s.v
-    rng = np.random.default_rng(7 + seed)
-    qs = (rng.standard_normal((dec, L, 1, w["q_heads"], D)) / math.sqrt(D)).astype(np.float32)
-    return ks, vs, qs
+        row = []
+        for b in range(B):
+            s = lowrank_stream(H, D, T + dec, theta=w["theta"], seed=1000 * (seed * B + b) + layer,
+                               **w["needles"])
+            K[layer, b] = torch.from_numpy(s.k_post).to(device, bf)
+            V[layer, b] = torch.from_numpy(s.v).to(device, bf)
+            row.append(s.needles)
+        needles.append(row)
+    g = torch.Generator(device="cpu").manual_seed(7 + seed)
+    Q = (torch.randn((dec, L, B, w["q_heads"], D), generator=g) / math.sqrt(D)).to(device, bf)
+    return K, V, Q, needles
 
 
 def new_cache(w: dict, torch):
@@ -135,20 +164,22 @@ def new_cache(w: dict, torch):
         None, num_layers=w["layers"], rope=rope, rank=w["rank"],
         coord_budget=w["tokens"] + w["ring"] + w["absorb"], recent_window=w["ring"],
         absorb_block=w["absorb"], n_sink=w["sinks"], prefill_block_size=w["prefill_block"],
-        retention="lowrank_surprise", hh_budget=w["hh"], hh_select="surprise")
+        retention="lowrank_surprise", hh_budget=w["hh"], hh_select="surprise",
+        seed_hh_warmup=w["seed_warmup"])
 
 
 # DRAM bytes (read + write) of one launch, from an ncu capture of the same
 # launch shape (the steady-state absorb step: n = 512, r = 32, 16 columns);
 # kernels not captured at the workload's shape are left out.
-DRAM_BYTES_PER_LAUNCH = {"bug_step_kernel": 3.39e6}
+DRAM_BYTES_PER_LAUNCH = {"llama-3.2-1b-kv": {"bug_step_kernel": 3.39e6}}
 
 
 def kernel_bytes(w: dict) -> dict[str, float]:
     """Algorithmic HBM bytes of one bench step, per kernel, from a replay of
     the cache's absorb schedule (every length decision is count-driven).
 
-    Per launch, with P = layers problems, n = H*D, bf16 tiers (2 B), fp32 state:
+    Per launch, with P = layers x sequences problems, n = H*D, bf16 tiers
+    (2 B), fp32 state:
       bug_step      2 streams x P x (read U n*r*4 + block b*n*4 + write U' n*r*4
                     + coords b*r*4)
       slash_score   P x (read candidates m*n*2 + basis n*r*4 + scores m*4)
@@ -158,53 +189,53 @@ def kernel_bytes(w: dict) -> dict[str, float]:
       decode_mid    P x (C_k, C_v 2*W*r*4 + positions W*4 + U_k, U_v 2*n*r*4 + q/out)
       decode_mma    P x (verbatim tiers 2*n*(hh+ring+sinks)*2 + q/out)   (with the merge)
     """
-    L, H, D, r = w["layers"], w["kv_heads"], w["head_dim"], w["rank"]
+    P = w["layers"] * w["batch"]
+    H, D, r = w["kv_heads"], w["head_dim"], w["rank"]
     n, T, C = H * D, w["tokens"], w["chunk"]
     sinks, ring, b, h, pbs = w["sinks"], w["ring"], w["absorb"], w["hh"], w["prefill_block"]
     out = {k: 0.0 for k in ("bug_step_kernel", "slash_score_kernel", "slash_keep_kernel",
                             "carry_kernel", "mid_hat_kernel", "decode_mid_kernel",
                             "decode_mma_kernel")}
-    rk, W, hh, rl, cum = 0, 0, 0, 0, 0
+    rk, W, hh, rl = 0, 0, 0, 0
 
     def bug(bb: int) -> None:
         nonlocal rk, W
-        out["bug_step_kernel"] += 2 * L * (2 * n * r * 4 + bb * n * 4 + bb * r * 4)
+        out["bug_step_kernel"] += 2 * P * (2 * n * r * 4 + bb * n * 4 + bb * r * 4)
         if W > 0:
-            out["carry_kernel"] += 2 * L * W * r * 4 * 2
+            out["carry_kernel"] += 2 * P * W * r * 4 * 2
         rk = min(r, rk + bb)
         W += bb
 
-    def absorb() -> None:
+    def slash(gb: int) -> None:
         nonlocal hh
-        m = hh + b
+        m = hh + gb
         keep = min(h, m)
-        d = m - keep
-        out["slash_score_kernel"] += L * (m * n * 2 + n * r * 4 + m * 4)
-        out["slash_keep_kernel"] += L * (2 * keep * n * 2 + 2 * keep * n * 2)
+        out["slash_score_kernel"] += P * (m * n * 2 + n * r * 4 + m * 4)
+        out["slash_keep_kernel"] += P * (2 * keep * n * 2 + 2 * keep * n * 2)
         hh = keep
-        if d:
-            bug(d)
+        if m - keep:
+            bug(m - keep)
 
-    # first chunk: sinks, ring, the middle absorbed directly in sub-blocks
+    # first chunk: sinks, ring, the middle in prefill sub-blocks (through the
+    # exact-tier selection with the warm-up seed)
     mid = C - sinks - ring
     for s0 in range(0, mid, pbs):
-        bug(min(pbs, mid - s0))
-    rl, cum = ring, C
+        (slash if w["seed_warmup"] else bug)(min(pbs, mid - s0))
+    rl = ring
     for _ in range(C, T, C):
         rl += C
-        cum += C
-        out["mid_hat_kernel"] += L * (2 * W * r * 4 + 2 * W * n * 2)
+        out["mid_hat_kernel"] += P * (2 * W * r * 4 + 2 * W * n * 2)
         while rl >= ring + b:
             rl -= b
-            absorb()
+            slash(b)
     for _ in range(w["decode"]):
         rl += 1
         while rl >= ring + b:
             rl -= b
-            absorb()
+            slash(b)
         exact = hh + rl + sinks
-        out["decode_mid_kernel"] += L * (2 * W * r * 4 + W * 4 + 2 * n * r * 4 + 2 * w["q_heads"] * D)
-        out["decode_mma_kernel"] += L * (2 * n * exact * 2 + 2 * w["q_heads"] * D)
+        out["decode_mid_kernel"] += P * (2 * W * r * 4 + W * 4 + 2 * n * r * 4 + 2 * w["q_heads"] * D)
+        out["decode_mma_kernel"] += P * (2 * n * exact * 2 + 2 * w["q_heads"] * D)
     return out
 
 
@@ -212,27 +243,22 @@ def run_ours(args, w: dict) -> None:
     import torch
     import torch.distributed as dist
 
+    from kvdlra_b200.sharding import init_ranks, max_over_ranks
+
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world > 1:
-        from datetime import timedelta
-
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600),
-                                device_id=torch.device("cuda", local))
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    if world > 1:
+        init_ranks("nccl", dev, timeout_s=600)
     from kvdlra_b200 import _native as N
 
-    ks, vs, qs = make_inputs(w, seed=rank)
-    bf = torch.bfloat16
-    K = torch.from_numpy(ks).to(dev, bf)
-    V = torch.from_numpy(vs).to(dev, bf)
-    Q = torch.from_numpy(qs).to(dev, bf)
-    T, C, dec = w["tokens"], w["chunk"], w["decode"]
+    # each rank streams its own sequences (seeded by rank): data-parallel, no
+    # collective on the data path
+    K, V, Q, needles = make_inputs(w, rank, dev, torch)
+    T, C, dec, B = w["tokens"], w["chunk"], w["decode"], w["batch"]
     cache = new_cache(w, torch)
-    launches = {"n": 0}
 
     def step(Kd, Vd, Qd, ev=None, host=None):
         cache.reset()
@@ -287,9 +313,9 @@ def run_ours(args, w: dict) -> None:
         outs = []
         for j in range(dec):
             p = T + j
-            if host is not None:
-                kk = host["k"][:, :, :, p : p + 1].to(dev, non_blocking=True)
-                vv = host["v"][:, :, :, p : p + 1].to(dev, non_blocking=True)
+            if host is not None:  # (the host copies hold the decode positions only)
+                kk = host["k"][:, :, :, j : j + 1].to(dev, non_blocking=True)
+                vv = host["v"][:, :, :, j : j + 1].to(dev, non_blocking=True)
                 qq = host["q"][j].to(dev, non_blocking=True)
             else:
                 kk, vv, qq = Kd[:, :, :, p : p + 1], Vd[:, :, :, p : p + 1], Qd[j]
@@ -308,6 +334,18 @@ def run_ours(args, w: dict) -> None:
     for _ in range(args.warmup):
         step(K, V, Q)
     barrier()
+    # exact-tier capture of the planted needles that left the ring (the
+    # Llama-3.1-8B configuration's retrieval measure)
+    graduated = cache.layers[0].cumulative_length - cache.layers[0]._recent_len()
+    cap_num = cap_den = 0
+    for li, ly in enumerate(cache.layers):
+        g = cache._group
+        sel = ly._ctr.hh_sel
+        for b in range(B):
+            kept = set(g.t["hh_pos"][sel, li * B + b, : ly._hh_len()].tolist())
+            want = [int(x) for x in needles[li][b] if x < graduated]
+            cap_num += sum(x in kept for x in want)
+            cap_den += len(want)
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
     with ClockSampler(dev.index) as clk:
         barrier()
@@ -320,19 +358,18 @@ def run_ours(args, w: dict) -> None:
         t_wall = time.perf_counter() - t_wall
     ingest_ms = sum(e[0].elapsed_time(e[1]) for e in ev)
     decode_ms = sum(e[1].elapsed_time(e[2]) for e in ev)
-    times = torch.tensor([ingest_ms, decode_ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    ingest_ms, decode_ms = float(times[0]), float(times[1])
+    ingest_ms, decode_ms = max_over_ranks([ingest_ms, decode_ms], dev)
 
     # ---- end to end through the public API from pinned host buffers
     e2e = None
     if not args.no_e2e:
-        host = {"k": torch.from_numpy(ks).to(bf).pin_memory(), "v": torch.from_numpy(vs).to(bf).pin_memory(),
-                "q": torch.from_numpy(qs).to(bf).pin_memory()}
-        kt, vt = torch.from_numpy(ks).to(bf), torch.from_numpy(vs).to(bf)
-        host["kc"] = [kt[:, :, :, c0 : c0 + C].contiguous().pin_memory() for c0 in range(0, T, C)]
-        host["vc"] = [vt[:, :, :, c0 : c0 + C].contiguous().pin_memory() for c0 in range(0, T, C)]
+        kc = K[:, :, :, :T].cpu()
+        vc = V[:, :, :, :T].cpu()
+        host = {"k": K[:, :, :, T:].cpu().pin_memory(), "v": V[:, :, :, T:].cpu().pin_memory(),
+                "q": Q.cpu().pin_memory()}
+        host["kc"] = [kc[:, :, :, c0 : c0 + C].contiguous().pin_memory() for c0 in range(0, T, C)]
+        host["vc"] = [vc[:, :, :, c0 : c0 + C].contiguous().pin_memory() for c0 in range(0, T, C)]
+        del kc, vc
         host["stream"] = torch.cuda.Stream(dev)
         host["bufs"] = [(torch.empty_like(host["kc"][0], device=dev), torch.empty_like(host["vc"][0], device=dev))
                         for _ in range(2)]
@@ -340,16 +377,14 @@ def run_ours(args, w: dict) -> None:
         barrier()
         ev2 = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
         for i in range(args.steps):
-            outs = step(None, None, None, ev2[i], host=host)
+            step(None, None, None, ev2[i], host=host)
         barrier()
-        e_ing = sum(e[0].elapsed_time(e[1]) for e in ev2)
-        t2 = torch.tensor([e_ing], dtype=torch.float64, device=dev)
-        if world > 1:
-            dist.all_reduce(t2, op=dist.ReduceOp.MAX)
+        (e_ing,) = max_over_ranks([sum(e[0].elapsed_time(e[1]) for e in ev2)], dev)
         h2d = sum(t.numel() * t.element_size() for t in host["kc"] + host["vc"])  # the window's copies
         d2h = host["res"].numel() * host["res"].element_size()
-        e2e = {"value": world * T * args.steps / (float(t2[0]) / 1e3), "unit": "tokens/s",
+        e2e = {"value": world * B * T * args.steps / (e_ing / 1e3), "unit": "tokens/s",
                "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)}
+        del host
 
     # ---- per-kernel event timing over one more step (profiling pass)
     N.profile(True)
@@ -359,12 +394,12 @@ def run_ours(args, w: dict) -> None:
     N.profile(False)
     launches_total = sum(v[1] for v in prof.values())
 
-    result = None
     if rank == 0:
         peaks, peak_kind = _peaks()
         dom = max(prof.items(), key=lambda kv: kv[1][0])[0] if prof else None
         kb = kernel_bytes(w)
         peak = peaks["hbm_gbs"]
+        traffic = DRAM_BYTES_PER_LAUNCH.get(w["name"], {})
 
         def roof(name: str) -> dict:
             ms, launches = prof.get(name, (0.0, 0))
@@ -374,7 +409,8 @@ def run_ours(args, w: dict) -> None:
             ach = nbytes / (ms / 1e3) / 1e9 if (nbytes and ms) else None
             return {"kernel": name, "bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s",
                     "frac": (ach / peak) if ach else None, "peak_source": peak_kind,
-                    "traffic": DRAM_BYTES_PER_LAUNCH.get(name), "bytes_per_launch": (nbytes / launches) if (nbytes and launches) else None,
+                    "traffic": traffic.get(name),
+                    "bytes_per_launch": (nbytes / launches) if (nbytes and launches) else None,
                     "avg_launch_ms": (ms / launches) if launches else None}
 
         roof_all = {k: roof(k) for k in kb if k in prof}
@@ -385,7 +421,7 @@ def run_ours(args, w: dict) -> None:
         cpu = None if args.no_cpu_baseline else cpu_baseline(w)
         result = {
             "metric": METRIC,
-            "value": world * T * args.steps / (ingest_ms / 1e3),
+            "value": world * B * T * args.steps / (ingest_ms / 1e3),
             "unit": "tokens/s",
             "n_gpus": world,
             "steps": args.steps,
@@ -397,9 +433,10 @@ def run_ours(args, w: dict) -> None:
             "dtype": "bf16",
             "data": "synthetic (seeded low-rank+noise KV streams with needles; inputs > L2)",
             "config": bench_config(w, world),
-            "decode": {"value": world * dec * args.steps / (decode_ms / 1e3), "unit": "tokens/s"},
+            "decode": {"value": world * B * dec * args.steps / (decode_ms / 1e3), "unit": "tokens/s"},
             "ingest_ms_per_step": ingest_ms / args.steps,
             "decode_ms_per_step": decode_ms / args.steps,
+            "needle_capture": (cap_num / cap_den) if cap_den else None,
             "e2e": e2e,
             "gpu_launches": int(launches_total * args.steps),
             "roofline": roof_dom,
@@ -553,6 +590,7 @@ def bench_config(w: dict, world: int) -> dict:
             "chunk": w["chunk"], "rank": w["rank"], "hh_budget": w["hh"], "sinks": w["sinks"],
             "ring": w["ring"], "absorb_block": w["absorb"], "decode_tokens": w["decode"],
             "seed_warmup": bool(w.get("seed_warmup", False)),
+            "config_tokens": w.get("config_tokens", w["tokens"]),
             "sequences_per_gpu": w.get("batch", 1),
             "parallelism": f"dp{world} (independent sequences)", "l2": "inputs larger than L2"}
 
@@ -595,6 +633,173 @@ def run_reference(args, w: dict) -> None:
     print(json.dumps(out))
 
 
+# ------------------------------------------------------------ decode sweep
+
+SWEEP = dict(batch=(1, 8, 32, 64), rank=(32, 128, 192), hh=(256, 1024), context=(16384, 65536, 131072))
+
+
+def decode_state(cache, B: int, W: int, H: int, D: int, r: int, h: int, ring: int, sinks: int,
+                 torch, seed: int = 0) -> None:
+    """Fill a one-layer cache of ``B`` sequences with the factored-decode
+    microbenchmark's state: bases U_k, U_v orthonormal (QR of N(0,1)),
+    coordinates C = diag(2^(-i/8)) V^T with V orthonormal (QR of a W x r
+    N(0,1) draw), exact tier / ring / sinks N(0,1) bf16, middle positions the
+    sorted values of [4, W + h + 4) the tier's random positions leave."""
+    ly = cache.layers[0]
+    dev = torch.device("cuda")
+    n = H * D
+    kd = torch.zeros((B, H, 1, D), dtype=torch.bfloat16, device=dev)
+    ly.lazy_initialization(kd, kd)
+    g = cache._group
+    g.ensure([ly], ring, W + g.max_block + 1)
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    t = g.t
+    bf = torch.bfloat16
+    for name in ("sink_k", "sink_v"):
+        t[name][:, :sinks] = torch.randn((B, sinks, n), generator=gen, device=dev).to(bf)
+    for name in ("ring_k", "ring_v"):
+        t[name][:, :ring] = torch.randn((B, ring, n), generator=gen, device=dev).to(bf)
+    for name in ("hh_k", "hh_v"):
+        t[name][0, :, :h] = torch.randn((B, h, n), generator=gen, device=dev).to(bf)
+    scale = torch.pow(2.0, -torch.arange(r, device=dev, dtype=torch.float32) / 8)
+    for b in range(B):
+        for name in ("u_k", "u_v"):
+            t[name][0, b, :, :r] = torch.linalg.qr(torch.randn((n, r), generator=gen, device=dev))[0]
+        for name in ("c_k", "c_v"):
+            vq = torch.linalg.qr(torch.randn((W, r), generator=gen, device=dev))[0]
+            t[name][b, :W, :r] = vq * scale
+        perm = torch.randperm(W + h, generator=gen, device=dev) + sinks
+        t["hh_pos"][0, b, :h] = torch.sort(perm[:h])[0].to(torch.int32)
+        t["mid_pos"][b, :W] = torch.sort(perm[h:])[0].to(torch.int32)
+    t["sig_k"][:, :r] = 1.0
+    t["sig_v"][:, :r] = 1.0
+    t["r_k"][:] = r
+    t["r_v"][:] = r
+    c = ly._ctr
+    c.cumulative_length, c.sink_len, c.ring_head, c.ring_len = sinks + h + W + ring, sinks, 0, ring
+    c.hh_len, c.hh_sel, c.u_sel, c.w_len, c.seeded, c.n_absorbs = h, 0, 0, W, 1, 1
+    ly._started = True
+    ly._r_cache = None
+    torch.cuda.synchronize()
+
+
+def run_decode_sweep(args) -> None:
+    """The factored-decode microbenchmark (32 query heads over 8 KV heads,
+    head_dim 128, ring 128, 4 sinks): every (batch, rank, exact tier,
+    compressed context) point, one decode step per call, CUDA-event time of
+    ``steps`` calls after ``warmup``; algorithmic bytes and FLOPs per step
+    give GB/s against the HBM roofline and the binding roofline
+    ``max(bytes / BW, flops / peak)``."""
+    import torch
+
+    from kvdlra_b200 import BugStreamingCache, RopeAngles
+    from kvdlra_b200.synthetic import default_inv_freq
+
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    H, D, Hq, ring, sinks = 8, 128, 32, 128, 4
+    n = H * D
+    peaks, peak_kind = _peaks()
+    bw, fl = peaks["hbm_gbs"] * 1e9, peaks["bf16_tflops"] * 1e12
+    inv = torch.from_numpy(default_inv_freq(D, 500000.0))
+    pts = []
+    grid = [(B, r, h, W) for B in SWEEP["batch"] for r in SWEEP["rank"] for h in SWEEP["hh"]
+            for W in SWEEP["context"]]
+    if args.sweep_points:
+        grid = grid[: args.sweep_points]
+    with ClockSampler(dev.index) as clk:
+        for B, r, h, W in grid:
+            if B * W * r * 8 > 40e9:  # fp32 C_k + C_v beyond 40 GB: skipped, reported
+                pts.append({"batch": B, "rank": r, "hh": h, "context": W, "skipped": "memory"})
+                continue
+            cache = BugStreamingCache(None, num_layers=1, rope=RopeAngles(inv_freq=inv), rank=r,
+                                      coord_budget=W + 64, recent_window=ring, absorb_block=16,
+                                      n_sink=sinks, retention="lowrank_surprise", hh_budget=h,
+                                      hh_select="surprise")
+            decode_state(cache, B, W, H, D, r, h, ring, sinks, torch, seed=B * 7 + r + h + W)
+            q = (torch.randn((B, Hq, D), device=dev) / math.sqrt(D)).to(torch.bfloat16)
+            ly = cache.layers[0]
+            for _ in range(args.warmup):
+                ly.factored_attention(q)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(args.steps):
+                ly.factored_attention(q)
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / args.steps
+            nbytes = B * (8 * r * W + 4 * W + 8 * n * r + 4 * n * (h + ring + sinks) + 4 * Hq * D)
+            flops = B * (2 * r * W * (n + Hq) + 4 * Hq * D * (W + h + ring + sinks))
+            t_bound = max(nbytes / bw, flops / fl)
+            pts.append({"batch": B, "rank": r, "hh": h, "context": W, "ms": ms,
+                        "tokens_per_s": B / (ms / 1e3), "gb_s": nbytes / (ms / 1e3) / 1e9,
+                        "hbm_frac": nbytes / (ms / 1e3) / bw,
+                        "bound": "hbm" if nbytes / bw >= flops / fl else "tensor",
+                        "roofline_frac": t_bound / (ms / 1e3)})
+            del cache
+            torch.cuda.empty_cache()
+    head = next((p for p in pts if p.get("batch") == 64 and p.get("rank") == 32 and p.get("hh") == 256
+                 and p.get("context") == 131072 and "ms" in p), next((p for p in pts if "ms" in p), {}))
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": head.get("tokens_per_s"), "unit": "tokens/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": head.get("ms"),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (orthonormal factors, N(0,1) tiers; inputs > L2 at every point)",
+            "config": {"workload": "decode-sweep", "q_heads": Hq, "kv_heads": H, "head_dim": D,
+                       "ring": ring, "sinks": sinks, "headline_point": {k: head.get(k) for k in ("batch", "rank", "hh", "context")},
+                       "coordinates": "fp32", "l2": "inputs larger than L2"},
+            "roofline": {"bound": head.get("bound"), "achieved": head.get("gb_s"), "peak": peaks["hbm_gbs"],
+                         "unit": "GB/s", "frac": head.get("hbm_frac"), "binding_frac": head.get("roofline_frac"),
+                         "peak_source": peak_kind, "traffic": None},
+            "sweep": pts, "gpu_launches": None, "clocks": clk.summary()}))
+
+
+def run_reference_decode(args) -> None:
+    """The reference's decode step at the sweep's smallest point (one
+    sequence, rank 32, exact tier 256, 16K compressed tokens) on the host
+    cores: the dense peek ``[sinks | tier | middle | ring]`` concatenated as
+    ``_decode_peek`` does (bug_cache.py:1496-1519, the middle already
+    materialised) and SDPA over it with GQA, as HF runs it.  The middle's
+    re-materialisation after each absorb (every 16 steps) is not counted."""
+    import torch
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    threads = _host_threads()
+    torch.set_num_threads(threads)
+    H, D, Hq, ring, sinks, h, W = 8, 128, 32, 128, 4, 256, 16384
+    bf = torch.bfloat16
+    g = torch.Generator().manual_seed(0)
+    parts_k = [torch.randn((1, H, x, D), generator=g).to(bf) for x in (sinks, h, W, ring)]
+    parts_v = [torch.randn((1, H, x, D), generator=g).to(bf) for x in (sinks, h, W, ring)]
+    q = (torch.randn((1, Hq, 1, D), generator=g) / math.sqrt(D)).to(bf)
+
+    def one():
+        k = torch.cat(parts_k, dim=2)
+        v = torch.cat(parts_v, dim=2)
+        return torch.nn.functional.scaled_dot_product_attention(q, k, v, enable_gqa=True)
+
+    for _ in range(args.warmup):
+        one()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        one()
+    ms = 1e3 * (time.perf_counter() - t0) / args.steps
+    v = 1e3 / ms
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "decode-sweep", "batch": 1, "rank": 32, "hh": h, "context": W},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "reference",
+                         "sample": "dense peek concatenation + SDPA (CPU torch), batch 1, rank 32, tier 256, 16K middle"},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -603,12 +808,24 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--tokens", type=int, default=None, help="override the ingest length (testing)")
+    ap.add_argument("--workload", default="llama-3.2-1b-kv", choices=[*WORKLOADS, "decode-sweep"],
+                    help="the configuration to run (default: the Llama-3.2-1B cache)")
+    ap.add_argument("--sweep-points", type=int, default=0, help="decode-sweep: first N points only")
+    ap.add_argument("--batch", type=int, default=None, help="override the sequences per GPU")
     ap.add_argument("--no-cpu-baseline", action="store_true",
                     help="skip the CPU oracle timing (profiling runs)")
     args = ap.parse_args()
-    w = dict(WORKLOAD)
+    if args.workload == "decode-sweep":
+        if args.impl == "reference":
+            run_reference_decode(args)
+        else:
+            run_decode_sweep(args)
+        return
+    w = dict(WORKLOADS[args.workload])
     if args.tokens:
         w["tokens"] = args.tokens
+    if args.batch:
+        w["batch"] = args.batch
     if args.impl == "reference":
         run_reference(args, w)
     else:

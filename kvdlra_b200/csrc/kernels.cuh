@@ -94,6 +94,11 @@ struct KTimerScope {
 // Allow `func` to use `bytes` of dynamic shared memory (checked against the
 // device opt-in limit minus the kernel's static shared memory).
 int ensure_smem(const void* func, size_t bytes, const char* name);
+// The peek's middle on tcgen05 (bf16 caches, head_dim 64/128, rank <= 128);
+// returns -1 when the shape or alignment does not apply (nothing launched).
+int launch_mid_hat_umma(const kvd_config& c, const kvd_buffers& b, const kvd_counters& k, int p0,
+                        int count, void* okp, void* ovp, long ob, long oh, long ot, int l0,
+                        cudaStream_t s);
 int device_smem_optin();
 using kvd::BugStepBatch; using kvd::CarryBatch; using kvd::CandSrc; using kvd::RopeArgs; using kvd::SelectOut;
 long bug_step_ws_per_problem(int n, int b, int ld);

@@ -603,8 +603,13 @@ int launch_peek(const kvd_config& c, const kvd_buffers& b, const kvd_counters& k
     const bool tiled = (D == 64 || D == 128) && ob % fp == 0 && oh % fp == 0 && ot % fp == 0 &&
                        reinterpret_cast<uintptr_t>(okp) % (fp * sizeof(T)) == 0 &&
                        reinterpret_cast<uintptr_t>(ovp) % (fp * sizeof(T)) == 0;
+    int umma_rc = -1;  // bf16: the middle on the 5th-generation tensor cores when the shape allows
+    if (sizeof(T) == 2) {
+      umma_rc = launch_mid_hat_umma(c, b, k, p0, count, okp, ovp, ob, oh, ot, l0, s);
+      if (umma_rc > 0) return umma_rc;
+    }
     const MhmSmem hm = mhm_smem(n, D, ld);
-    const bool mma = tiled && ld % 8 == 0 && 4L * hm.total <= 200 * 1024 &&
+    const bool mma = umma_rc < 0 && tiled && ld % 8 == 0 && 4L * hm.total <= 200 * 1024 &&
                      reinterpret_cast<uintptr_t>(okp) % (2 * sizeof(T)) == 0 &&
                      reinterpret_cast<uintptr_t>(ovp) % (2 * sizeof(T)) == 0 && ob % 2 == 0 &&
                      oh % 2 == 0 && ot % 2 == 0;
@@ -624,6 +629,8 @@ int launch_peek(const kvd_config& c, const kvd_buffers& b, const kvd_counters& k
           track_pos ? b.mid_pos + (long)p0 * c.w_cap : nullptr, c.w_cap, pos_base, k.w_len, H,
           c.inv_freq, c.rope_scaling, okp, ovp, ob, oh, ot, l0, tpc);
       }
+    } else if (umma_rc == 0) {
+      // done on the tensor cores
     } else if (tiled) {
       // the coordinate tile stays whole; the basis is staged in rank chunks
       // sized to the device's shared-memory limit

@@ -55,13 +55,16 @@ def lowrank_stream(
     needle_norm: float = 5.0,
     theta: float = 500000.0,
     seed: int = 0,
+    span_copies: tuple[int, int] | None = None,
 ) -> LowRankStream:
     """The single-layer stream of the synthetic workload: per head,
     ``K = Q diag(sigma) C + E`` with ``Q`` the QR of an N(0,1) ``D x r`` draw,
     ``sigma_i = 2^(-i/4)``, ``C ~ N(0,1)``, ``E ~ noise * N(0,1)``; values are an
     independent draw of the same form.  ``n_needles`` token positions (uniform,
     distinct, never a sink) get a key that is a unit vector orthogonal to that
-    head's ``Q`` scaled to ``needle_norm``."""
+    head's ``Q`` scaled to ``needle_norm``.  ``span_copies = (copies, length)``
+    plants instead one span of ``length`` such keys verbatim at ``copies``
+    random non-overlapping places (the same pre-RoPE content each time)."""
     rng = np.random.default_rng(seed)
     sig = (2.0 ** (-np.arange(signal_rank) / 4.0)).astype(np.float32)
 
@@ -78,13 +81,26 @@ def lowrank_stream(
 
     k_pre, qk = draw(None)
     v, _ = draw(None)
-    needles = np.sort(rng.choice(np.arange(8, t), size=n_needles, replace=False)) if n_needles else np.zeros(0, np.int64)
-    for p in needles:
+    if span_copies is not None:
+        copies, length = span_copies
+        slots = (t - 8) // length
+        starts = 8 + length * np.sort(rng.choice(slots, size=copies, replace=False))
+        span = np.empty((num_heads, length, head_dim))
         for h in range(num_heads):
-            x = rng.standard_normal(head_dim)
-            x = x - qk[h] @ (qk[h].T @ x)
-            x = x / np.linalg.norm(x) * needle_norm
-            k_pre[h, p] = x.astype(np.float32)
+            x = rng.standard_normal((length, head_dim))
+            x = x - (x @ qk[h]) @ qk[h].T
+            span[h] = x / np.linalg.norm(x, axis=1, keepdims=True) * needle_norm
+        needles = np.concatenate([st + np.arange(length) for st in starts])
+        for st in starts:
+            k_pre[:, st : st + length] = span.astype(np.float32)
+    else:
+        needles = np.sort(rng.choice(np.arange(8, t), size=n_needles, replace=False)) if n_needles else np.zeros(0, np.int64)
+        for p in needles:
+            for h in range(num_heads):
+                x = rng.standard_normal(head_dim)
+                x = x - qk[h] @ (qk[h].T @ x)
+                x = x / np.linalg.norm(x) * needle_norm
+                k_pre[h, p] = x.astype(np.float32)
     inv = default_inv_freq(head_dim, theta)
     k_post = apply_rope_htd(k_pre, np.arange(t), inv)
     return LowRankStream(k_post=k_post, v=v, k_pre=k_pre, needles=needles.astype(np.int64))
