@@ -13,6 +13,7 @@
 // (problem, KV group) for all G = Hq/Hkv query heads of the group and writes
 // (max, sum, acc_d, acc_c) partials; decode_merge_kernel combines them.
 #include "kernels.cuh"
+#include "umma.cuh"
 
 namespace kvd {
 
@@ -37,6 +38,7 @@ struct DecArgs {
   float scaling;
   float* part; long part_sp_chunk;  // partial record per (problem, group, chunk)
   int n_chunks;
+  int* status;                      // device status words (bounded waits report here)
 };
 
 // Partial record layout (floats): m[G], l[G], acc_d[G][D], acc_c[G][ld]
@@ -1163,6 +1165,294 @@ size_t decode_ws_bytes(const kvd_config& c, int count, int num_q_heads) {
   return (size_t)count * c.num_heads * ch * rec * 4 + 256;
 }
 
+// ------------------------------------------------------------------
+// The middle tier on the 5th-generation tensor cores (bf16 caches,
+// head_dim 64, n <= 512, rank <= 32).  A CTA of eight warps walks `tpc`
+// tiles of 128 middle tokens of one problem for every KV group: the key
+// rebuild C_k U_k^T of a tile (128 tokens x all n features) is 2 x ceil(r/8)
+// kind::tf32 MMAs of 128 x 256 x 8 into tensor memory (512 columns), issued
+// by one thread from the tile's coordinates and the basis rows staged once
+// per CTA (both K-major, no-swizzle core-matrix layout, TF32-rounded, columns
+// past the rank zero).  Warp w then reads accumulator lanes (tokens)
+// [32 (w % 4), +32) for half of the groups: one token per thread, the
+// rotate-half partners d and d + 32 in the same thread, RoPE at the token's
+// position, the scores against the group's query heads into shared memory;
+// the softmax runs per query head online across tiles, and the value product
+// P C_v accumulates in coordinate space in registers (U_v is applied once in
+// the merge).  Partial records as decode_mid_kernel writes them.
+constexpr int kDuTok = 128;
+constexpr int kDuThreads = 512;
+constexpr int kDuK = 32;  // staged rank columns (rank <= 32)
+constexpr long kDuWaitPolls = 1L << 22;
+
+struct DuSmem { int us, ck, cv, ldv, qs, cs, ps, st, vred, posb, bar, total; };  // bytes
+__host__ __device__ inline DuSmem du_smem(int n, int Hq) {
+  constexpr int D = 64;
+  DuSmem m;
+  m.ldv = kDuK + 4;
+  m.us = 0;                                   // [n][32] basis, core-matrix layout
+  m.ck = m.us + n * kDuK * 4;                 // 2 x [128][32] key coordinates, core-matrix layout
+  m.cv = m.ck + 2 * kDuTok * kDuK * 4;        // 2 x [128][ldv] value coordinates
+  m.qs = m.cv + 2 * kDuTok * m.ldv * 4;       // [Hq][64] queries
+  m.cs = m.qs + Hq * D * 4;                   // [32 frequencies][128 tokens] (cos, sin)
+  m.ps = m.cs + (D / 2) * kDuTok * 8;         // [Hq][128] scores, then probabilities
+  m.st = m.ps + Hq * kDuTok * 4;              // [Hq][4]: running max, correction
+  m.vred = m.st + Hq * 16;                    // [256][4] value-product halves
+  m.posb = m.vred + 256 * 16;                 // 2 x [128] positions
+  m.bar = m.posb + 2 * kDuTok * 4;            // mbarrier, TMEM base
+  m.total = m.bar + 16;
+  return m;
+}
+
+__device__ __forceinline__ int du_off(int row, int k) {  // core-matrix byte offset, K = 32
+  return (row >> 3) * (kDuK * 32) + (k >> 2) * 128 + (row & 7) * 16 + (k & 3) * 4;
+}
+
+// 16-byte cp.async, zero-filled (nothing read) when `valid` is false
+__device__ __forceinline__ void cp16_zfill(void* dst, const void* src, bool valid) {
+  const unsigned sa = (unsigned)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(sa), "l"(src), "r"(valid ? 16 : 0)
+               : "memory");
+}
+
+__global__ void __launch_bounds__(kDuThreads) decode_mid_umma_kernel(DecArgs a, int tpc, int chunk0,
+                                                                     int* status) {
+  constexpr int D = 64, HALF = 32;
+  extern __shared__ __align__(1024) unsigned char dsm4[];
+  const int p = blockIdx.y;
+  const int H = a.H, G = a.G, Hq = a.H * a.G, ld = a.ld, n = a.H * D;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int r_k = a.rk[p];
+  const DuSmem L = du_smem(n, Hq);
+  unsigned char* us = dsm4 + L.us;
+  float* qs = reinterpret_cast<float*>(dsm4 + L.qs);
+  float2* cs = reinterpret_cast<float2*>(dsm4 + L.cs);
+  float* ps = reinterpret_cast<float*>(dsm4 + L.ps);
+  float* st = reinterpret_cast<float*>(dsm4 + L.st);
+  float* vred = reinterpret_cast<float*>(dsm4 + L.vred);
+  int* posb = reinterpret_cast<int*>(dsm4 + L.posb);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(dsm4 + L.bar);
+  uint32_t* tbase = reinterpret_cast<uint32_t*>(dsm4 + L.bar + 8);
+  const int ldv = L.ldv;
+  const int nm = (a.W + kDuTok - 1) / kDuTok;
+  const int t_begin = blockIdx.x * tpc, t_end = min(nm, t_begin + tpc);
+  if (warp == 0) {
+    umma::tmem_alloc(tbase, 512);
+    umma::tmem_relinquish();
+  }
+  if (tid == 0) {
+    umma::mbar_init(bar, 1);
+    umma::mbar_fence_init();
+  }
+  {  // the basis rows of every group (K-major core matrices, TF32, columns past the rank zero)
+    const float* U = a.uk + p * a.u_sp;
+    for (int e = tid; e < n * (kDuK / 4); e += kDuThreads) {
+      const int row = e / (kDuK / 4), k = 4 * (e % (kDuK / 4));
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (k < r_k) {
+        v = *reinterpret_cast<const float4*>(U + (long)row * ld + k);
+        if (k + 1 >= r_k) v.y = 0.f;
+        if (k + 2 >= r_k) v.z = 0.f;
+        if (k + 3 >= r_k) v.w = 0.f;
+      }
+      *reinterpret_cast<float4*>(us + du_off(row, k)) =
+          make_float4(umma::to_tf32(v.x), umma::to_tf32(v.y), umma::to_tf32(v.z), umma::to_tf32(v.w));
+    }
+  }
+  const __nv_bfloat16* qp = reinterpret_cast<const __nv_bfloat16*>(a.q) + (long)p * a.Hq * D;
+  for (int e = tid; e < Hq * D; e += kDuThreads) qs[e] = __bfloat162float(qp[e]);
+  for (int h = tid; h < Hq; h += kDuThreads) st[4 * h] = -INFINITY;
+  // a tile's coordinates land by cp.async straight into the MMA's layout (keys;
+  // rank columns past the basis rank meet zero basis columns) and into a plain
+  // pitch (values); rows past the middle are zero-filled without a read
+  auto prefetch = [&](int tile, int buf) {
+    const int j0 = tile * kDuTok, ntok = min(kDuTok, a.W - j0);
+    const float* Ck = a.ck + p * a.c_sp + (long)j0 * ld;
+    const float* Cv = a.cv + p * a.c_sp + (long)j0 * ld;
+    unsigned char* ckb = dsm4 + L.ck + buf * kDuTok * kDuK * 4;
+    float* cvb = reinterpret_cast<float*>(dsm4 + L.cv) + buf * kDuTok * ldv;
+    for (int e = tid; e < kDuTok * (kDuK / 4); e += kDuThreads) {
+      const int row = e / (kDuK / 4), k = 4 * (e % (kDuK / 4));
+      const bool ok = row < ntok && k < ld;
+      const long off = ok ? (long)row * ld + k : 0;
+      cp16_zfill(ckb + du_off(row, k), Ck + off, ok);
+      cp16_zfill(cvb + row * ldv + k, Cv + off, ok);
+    }
+    if (tid < kDuTok)
+      posb[buf * kDuTok + tid] =
+          tid < ntok ? (a.mid_pos ? a.mid_pos[p * a.mid_sp + j0 + tid] : a.pos_base + j0 + tid) : 0;
+    cp_async_commit();
+  };
+  if (t_begin < t_end) prefetch(t_begin, 0);
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tmem = *tbase;
+  const uint32_t us_addr = (uint32_t)__cvta_generic_to_shared(us);
+  const uint32_t idesc = umma::idesc_tf32(kDuTok, 256);
+  // value product: thread (vh, vc) of token half th accumulates acc_c[vh][vc..vc+4)
+  const int nvq = ld / 4;
+  const int th = tid >> 8, vt = tid & 255;
+  const int vh = vt / nvq, vc = 4 * (vt % nvq);
+  const bool vown = vh < Hq;
+  float vacc[4] = {0.f, 0.f, 0.f, 0.f};
+  float lrow[4] = {0.f, 0.f, 0.f, 0.f};  // sums of the rows warp + 16 i
+  uint32_t phase = 0;
+  bool ok_wait = true;
+  const int tok = 32 * (warp & 3) + lane;  // this thread's TMEM lane (token of the tile)
+  const int gq = warp >> 2;                // which quarter of the groups this warp scores
+  const int gper = (H + 3) / 4;
+  const float4* qs4 = reinterpret_cast<const float4*>(qs);
+  for (int tile = t_begin; tile < t_end && ok_wait; ++tile) {
+    const int buf = (tile - t_begin) & 1;
+    const int j0 = tile * kDuTok, ntok = min(kDuTok, a.W - j0);
+    asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+    umma::fence_proxy_async_smem();
+    __syncthreads();  // the tile is in shared memory for every thread and the tensor core
+    if (tid == 0) {
+      umma::fence_after_sync();
+      const uint32_t ck_addr = (uint32_t)__cvta_generic_to_shared(dsm4 + L.ck + buf * kDuTok * kDuK * 4);
+      for (int nb = 0; nb < n; nb += 256)
+        for (int j = 0; j < kDuK / 8; ++j)
+          umma::mma_tf32(tmem + nb, umma::smem_desc(ck_addr + 256 * j, 128, 32 * kDuK),
+                         umma::smem_desc(us_addr + nb * kDuK * 4 + 256 * j, 128, 32 * kDuK), idesc,
+                         j > 0);
+      umma::commit(bar);
+    }
+    if (tile + 1 < t_end) prefetch(tile + 1, buf ^ 1);  // lands while this tile is processed
+    for (int e = tid; e < HALF * kDuTok; e += kDuThreads) {  // [frequency][token] rotary table
+      const int f = e / kDuTok, t = e % kDuTok;
+      float c = 1.f, sn = 0.f;
+      if (t < ntok) rope_cs_fast(posb[buf * kDuTok + t], a.inv_freq[f], a.rope_scale, &c, &sn);
+      cs[e] = make_float2(c, sn);
+    }
+    __syncthreads();
+    ok_wait = umma::mbar_wait_bounded(bar, phase, kDuWaitPolls);
+    phase ^= 1;
+    umma::fence_after_sync();
+    if (ok_wait) {
+      const uint32_t trow = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
+      const int g_lo = gq * gper, g_hi = min(H, g_lo + gper);
+      for (int g = g_lo; g < g_hi; ++g) {
+        float s1[kMaxG], s2[kMaxG];
+#pragma unroll
+        for (int qh = 0; qh < kMaxG; ++qh) { s1[qh] = 0.f; s2[qh] = 0.f; }
+#pragma unroll
+        for (int f0 = 0; f0 < HALF; f0 += 16) {
+          float x1[16], x2[16];
+          umma::tmem_ld16(trow + g * D + f0, x1);
+          umma::tmem_ld16(trow + g * D + HALF + f0, x2);
+          umma::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float2 c = cs[(f0 + i) * kDuTok + tok];
+            float y1, y2;
+            rope_apply_pair(x1[i], x2[i], c.x, c.y, &y1, &y2);
+            x1[i] = y1;
+            x2[i] = y2;
+          }
+#pragma unroll
+          for (int qh = 0; qh < kMaxG; ++qh) {
+            if (qh < G) {
+              const float4* qa = qs4 + (g * G + qh) * (D / 4) + f0 / 4;
+              const float4* qb = qa + HALF / 4;
+              float u1 = s1[qh], u2 = s2[qh];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const float4 u = qa[i], w = qb[i];
+                u1 = fmaf(x1[4 * i], u.x, u1); u2 = fmaf(x2[4 * i], w.x, u2);
+                u1 = fmaf(x1[4 * i + 1], u.y, u1); u2 = fmaf(x2[4 * i + 1], w.y, u2);
+                u1 = fmaf(x1[4 * i + 2], u.z, u1); u2 = fmaf(x2[4 * i + 2], w.z, u2);
+                u1 = fmaf(x1[4 * i + 3], u.w, u1); u2 = fmaf(x2[4 * i + 3], w.w, u2);
+              }
+              s1[qh] = u1;
+              s2[qh] = u2;
+            }
+          }
+        }
+#pragma unroll
+        for (int qh = 0; qh < kMaxG; ++qh)
+          if (qh < G)
+            ps[(g * G + qh) * kDuTok + tok] = tok < ntok ? (s1[qh] + s2[qh]) * a.scaling : -INFINITY;
+      }
+    }
+    umma::fence_before_sync();
+    __syncthreads();
+    if (!ok_wait) break;
+    // softmax per query head over the tile, online across tiles (warp owns rows warp + 16 i)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int row = warp + 16 * i;
+      if (row >= Hq) continue;
+      float* pr = ps + row * kDuTok;
+      const float x0 = pr[lane], x1 = pr[lane + 32], x2 = pr[lane + 64], x3 = pr[lane + 96];
+      float mt = fmaxf(fmaxf(x0, x1), fmaxf(x2, x3));
+      mt = warp_max(mt);
+      const float mold = st[4 * row];
+      const float mnew = fmaxf(mold, mt);
+      const float e0 = mnew == -INFINITY ? 0.f : expf(x0 - mnew);
+      const float e1 = mnew == -INFINITY ? 0.f : expf(x1 - mnew);
+      const float e2 = mnew == -INFINITY ? 0.f : expf(x2 - mnew);
+      const float e3 = mnew == -INFINITY ? 0.f : expf(x3 - mnew);
+      pr[lane] = e0; pr[lane + 32] = e1; pr[lane + 64] = e2; pr[lane + 96] = e3;
+      const float ls = warp_sum((e0 + e1) + (e2 + e3));
+      const float corr = mold == -INFINITY ? 0.f : expf(mold - mnew);
+      lrow[i] = lrow[i] * corr + ls;
+      __syncwarp();
+      if (lane == 0) {
+        st[4 * row] = mnew;
+        st[4 * row + 1] = corr;
+      }
+    }
+    __syncthreads();
+    if (vown) {  // acc_c[vh][vc..vc+4) = corr * acc + sum_t p[vh][t] c_v[t][vc..] over this half
+      const float corr = st[4 * vh + 1];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) vacc[j] *= corr;
+      const float* pr = ps + vh * kDuTok + 64 * th;
+      const float* cvb = reinterpret_cast<const float*>(dsm4 + L.cv) + buf * kDuTok * ldv + 64 * th * ldv;
+#pragma unroll 8
+      for (int t = 0; t < 64; ++t) {
+        const float pt = pr[t];
+        const float4 cvv = *reinterpret_cast<const float4*>(cvb + t * ldv + vc);
+        vacc[0] = fmaf(pt, cvv.x, vacc[0]);
+        vacc[1] = fmaf(pt, cvv.y, vacc[1]);
+        vacc[2] = fmaf(pt, cvv.z, vacc[2]);
+        vacc[3] = fmaf(pt, cvv.w, vacc[3]);
+      }
+    }
+    __syncthreads();  // this tile's buffers free for the prefetch after next
+  }
+  asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+  if (!ok_wait) {
+    if (tid == 0) atomicOr(&status[kStatusTimeout], 16);
+    umma::mbar_wait_bounded(bar, phase ^ 1, kDuWaitPolls);
+  }
+  if (th == 1 && vown)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) vred[vt * 4 + j] = vacc[j];
+  __syncthreads();
+  if (warp == 0) umma::tmem_dealloc(tmem, 512);
+  // one partial record per group: m[G], l[G], acc_d[G][D] = 0, acc_c[G][ld]
+  const int chunk = chunk0 + blockIdx.x;
+  auto rec = [&](int g) { return a.part + ((long)(p * H + g) * a.n_chunks + chunk) * a.part_sp_chunk; };
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int row = warp + 16 * i;
+    if (row < Hq && lane == 0) {
+      float* o = rec(row / G);
+      o[row % G] = (t_begin < t_end && ok_wait) ? st[4 * row] : -INFINITY;
+      o[G + row % G] = ok_wait ? lrow[i] : 0.f;
+    }
+  }
+  for (int e = tid; e < H * G * D; e += kDuThreads) rec(e / (G * D))[2 * G + e % (G * D)] = 0.f;
+  if (th == 0 && vown) {
+    float* o = rec(vh / G) + 2 * G + G * D + (vh % G) * ld + vc;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[j] = ok_wait ? vacc[j] + vred[vt * 4 + j] : 0.f;
+  }
+}
+
 template <typename T>
 int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_counters& k, int p0,
                            int count, const void* q, int Hq, float scaling, void* out, char* ws,
@@ -1196,6 +1486,7 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
   a.pos_base = (int)(k.cumulative_length - k.ring_len - (k.hh_len + k.w_len));
   a.inv_freq = c.inv_freq; a.rope_scale = c.rope_scaling;
   a.q = q; a.out = out; a.scaling = scaling;
+  a.status = b.status;
   a.part_sp_chunk = part_floats(a.G, a.D, a.ld);
   // tiled kernel: head_dim 64 or 128, rank <= head_dim, G <= 8
   const bool tiled = (a.D == 64 || a.D == 128) && a.ld <= a.D && a.G <= 8 &&
@@ -1233,14 +1524,24 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
         if (sm_count[dev] > 0) sms = sm_count[dev];
       }
     }
-    int tpc = 2;
+    // bf16, head_dim 64, n = 256 or 512, rank <= 32: the middle tier on the
+    // 5th-generation tensor cores (128-token tiles), else decode_mid_kernel
+    const bool umma_mid = sizeof(T) == 2 && a.D == 64 && (n == 256 || n == 512) && a.ld <= kDuK &&
+                          a.ld % 4 == 0 && Hq_all <= 64 && Hq_all * (a.ld / 4) <= 256 &&
+                          a.c_sp % 4 == 0 && (reinterpret_cast<uintptr_t>(a.ck) & 15) == 0 &&
+                          (reinterpret_cast<uintptr_t>(a.cv) & 15) == 0 &&
+                          (reinterpret_cast<uintptr_t>(a.uk) & 15) == 0 &&
+                          du_smem(n, Hq_all).total <= device_smem_optin();
+    const int ttok = umma_mid ? kDuTok : kTT;
+    const int nmt = (a.W + ttok - 1) / ttok;
+    int tpc = umma_mid ? 1 : 2;
     long best = -1;
-    for (int t = 2; t <= 8; ++t) {
-      const long waves = ((long)((nm + t - 1) / t) * count + sms - 1) / sms;
+    for (int t = tpc; t <= 8; ++t) {
+      const long waves = ((long)((nmt + t - 1) / t) * count + sms - 1) / sms;
       const long cost = waves * (2 * t + 1);
       if (best < 0 || cost < best) { best = cost; tpc = t; }
     }
-    const int n_mch = (nm + tpc - 1) / tpc;
+    const int n_mch = (nmt + tpc - 1) / tpc;
     a.n_chunks = n_vch + n_mch;
     const size_t need2 = (size_t)count * a.H * a.n_chunks * a.part_sp_chunk * 4;
     if (need2 > ws_bytes) { set_error("factored decode: workspace too small"); return KVD_ERR_WORKSPACE; }
@@ -1271,7 +1572,15 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
       if (fork) cudaStreamWaitEvent(s, ev_join, 0);
       return rc1;
     }
-    {
+    if (umma_mid) {
+      const int dsm = du_smem(n, Hq_all).total;
+      if (int rc0 = ensure_smem((const void*)decode_mid_umma_kernel, dsm, "decode_mid_kernel")) {
+        if (fork) cudaStreamWaitEvent(s, ev_join, 0);
+        return rc0;
+      }
+      KTimerScope kts_("decode_mid_kernel", s);
+      decode_mid_umma_kernel<<<dim3(n_mch, count), kDuThreads, dsm, s>>>(a, tpc, n_vch, a.status);
+    } else {
       KTimerScope kts_("decode_mid_kernel", s);
       mid_fn<<<dim3(n_mch, count), kMidThreads, 4 * ms.total, s>>>(a, tpc, n_vch);
     }
