@@ -106,13 +106,13 @@ __device__ __forceinline__ void jacobi_rotation(float d, float g2, float& c, flo
 // same choice sizes the column pitch on the host.
 // The instantiated tiles: fp64 sums (long residual columns) G in {16, 32}
 // with NU in {2, 3, 5, 9}; fp32 sums (the core) G in {4, 8, 16}, NU in
-// {2, 3, 4, 6, 9}.  0 = none fits.
+// {2, 3, 4, 5, 6, 9}.  0 = none fits.
 __host__ __device__ inline int jacobi_nu(int g, int need, bool dbl) {
   if (!(dbl ? (g == 16 || g == 32) : (g == 4 || g == 8 || g == 16))) return 0;
   if (need <= 2) return 2;
   if (need <= 3) return 3;
   if (!dbl && need <= 4) return 4;
-  if (dbl && need <= 5) return 5;
+  if (need <= 5) return 5;
   if (!dbl && need <= 6) return 6;
   if (need <= 9) return 9;
   return 0;
@@ -461,9 +461,9 @@ static __device__ __forceinline__ int cta_hestenes_any(float* X, int len, int vo
       KVD_HJ(16, 2) KVD_HJ(16, 3) KVD_HJ(16, 5) KVD_HJ(16, 9)
       KVD_HJ(32, 2) KVD_HJ(32, 3) KVD_HJ(32, 5) KVD_HJ(32, 9)
     } else {
-      KVD_HJ(4, 2) KVD_HJ(4, 3) KVD_HJ(4, 4) KVD_HJ(4, 6) KVD_HJ(4, 9)
-      KVD_HJ(8, 2) KVD_HJ(8, 3) KVD_HJ(8, 4) KVD_HJ(8, 6) KVD_HJ(8, 9)
-      KVD_HJ(16, 2) KVD_HJ(16, 3) KVD_HJ(16, 4) KVD_HJ(16, 6) KVD_HJ(16, 9)
+      KVD_HJ(4, 2) KVD_HJ(4, 3) KVD_HJ(4, 4) KVD_HJ(4, 5) KVD_HJ(4, 6) KVD_HJ(4, 9)
+      KVD_HJ(8, 2) KVD_HJ(8, 3) KVD_HJ(8, 4) KVD_HJ(8, 5) KVD_HJ(8, 6) KVD_HJ(8, 9)
+      KVD_HJ(16, 2) KVD_HJ(16, 3) KVD_HJ(16, 4) KVD_HJ(16, 5) KVD_HJ(16, 6) KVD_HJ(16, 9)
     }
 #undef KVD_HJ
   }
@@ -1877,6 +1877,34 @@ static StepPlan plan_bug_step(int n, int b, int ld, long pool_max_floats) {
     if (used + sz <= pool_max_floats) {
       P.smem[g] = used;
       used += sz;
+    }
+  }
+  // Wide blocks (the pre-fill blocks): the core would not fit beside the
+  // residual's regions, and its Jacobi is the longest phase.  The core then
+  // takes the shared memory from offset 0, overlapping the K-split partials
+  // and the factor's columns: both are dead from the core's build on (the
+  // build reads a, the residual's right factor and the small scalars), and
+  // the partials serve again only as scratch for U_new's Gram, after the
+  // core has been read out.  a and the small scalars sit after the core.
+  const long sz_core = (fl[kRgCore] + 31) & ~31L, sz_as = (fl[kRgAs] + 31) & ~31L;
+  const long sz_small = (fl[kRgSmall] + 31) & ~31L;
+  const long sz_part = (fl[kRgPart] + 31) & ~31L, sz_tf = (fl[kRgTf] + 31) & ~31L;
+  if (b > 16 && P.smem[kRgCore] < 0 && sz_core + sz_as + sz_small <= pool_max_floats &&
+      sz_part + sz_tf <= sz_core) {
+    for (int g = 0; g < kRgCount; ++g) P.smem[g] = -1;
+    P.smem[kRgCore] = 0;
+    P.smem[kRgPart] = 0;
+    P.smem[kRgTf] = fl[kRgTf] ? sz_part : -1;
+    P.smem[kRgAs] = sz_core;
+    P.smem[kRgSmall] = sz_core + sz_as;
+    used = sz_core + sz_as + sz_small;
+    for (int g : prio) {  // what else fits goes after them (never over the core)
+      if (P.smem[g] >= 0 || g == kRgPart || g == kRgTf) continue;
+      const long sz = (fl[g] + 31) & ~31L;
+      if (used + sz <= pool_max_floats) {
+        P.smem[g] = used;
+        used += sz;
+      }
     }
   }
   P.smem_bytes = (int)(kStepMiscBytes + 4 * used);
