@@ -470,6 +470,173 @@ static __device__ __forceinline__ int cta_hestenes_any(float* X, int len, int vo
   return cta_hestenes<32, 0, ACC>(X, len, voff, cols, ldx, tol, max_sweeps, inv_scale2, accum, seeded);
 }
 
+// Block-ordered one-sided Jacobi for the core (fp32 sums, rotations
+// accumulated from row voff as in cta_hestenes), with the columns held in
+// registers between barriers.  Columns form blocks of four; a block round
+// gives warp w two blocks A, B (the circle method over blocks) and group j
+// of eight lanes the column pair (A_j on top, B_j below), lane gl holding the
+// 16-byte units gl + 8 t (t < NU) of both, of which the first NUD per lane
+// can hold data rows.  The warp then runs, without leaving registers: in
+// the first block round of a sweep the full circle over its eight columns
+// (seven rounds, every pair inside A, inside B and across), in the others
+// the four cross rounds (A_j against B_(j+t), the bottoms passed on by warp
+// shuffles).  A sweep therefore meets every pair once in the same 47 rounds
+// (48 columns) as the cyclic order, but the columns cross shared memory and
+// a named barrier only once per block round (11 times a sweep instead of
+// 47).  The rotation, the tolerance, the null floor and the quadratic stop
+// are cta_hestenes's; the stop slides: the iteration ends once nbp - 1
+// consecutive block rounds (each pair once) rotated no pair with a cosine
+// above kJacobiQuadStop, wherever in the sweep that window starts.  Needs X
+// 16-byte aligned, ldx % 4 == 0 and (blocks + 1) / 2 <= warps of the CTA;
+// returns the sweeps taken less one (max_sweeps when not converged).
+constexpr int kBlkLanes = 8;
+template <int NU, int NUD>
+static __device__ __noinline__ int cta_block_hestenes(float* X, int len, int voff, int cols, int ldx,
+                                                      float tol, int max_sweeps, double inv_scale2) {
+  constexpr int G = kBlkLanes, P = 32 / G;
+  constexpr unsigned kAll = 0xffffffffu;
+  const int tid = threadIdx.x, nthr = blockDim.x, warp = tid / 32, lane = tid % 32;
+  const int slot = lane / G, gl = lane % G;
+  const int vend = voff + ((cols + 3) & ~3);
+  for (long e = tid; e < (long)cols * (vend - len); e += nthr) {
+    const int c = (int)(e / (vend - len)), k = len + (int)(e % (vend - len));
+    X[(long)c * ldx + k] = (k - voff == c) ? 1.f : 0.f;
+  }
+  __syncthreads();
+  if (cols <= 1) return 0;
+  const int nut = vend / 4, nud = voff / 4;
+  const int nb = (cols + P - 1) / P, nbp = nb + (nb & 1), aw = nbp / 2;
+  if (warp >= aw) return 0;
+  const int nbar = aw * 32;
+  const float tol2 = tol * tol, is2 = (float)inv_scale2;
+  const int max_br = max_sweeps * (nbp - 1);
+  int br = 0, quiet = 0;
+  for (; br < max_br; ++br) {
+    const int k = br % (nbp - 1);
+    int ba, bb;
+    rr_pair(warp, k, nbp, &ba, &bb);
+    int ti = ba * P + slot, bi = bb * P + slot;  // column ids; >= cols: padding
+    float4 tp[NU], bt[NU];
+#pragma unroll
+    for (int t = 0; t < NU; ++t) {
+      const int u = gl + G * t;
+      const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+      tp[t] = (ti < cols && u < nut) ? reinterpret_cast<const float4*>(X + (long)ti * ldx)[u] : z;
+      bt[t] = (bi < cols && u < nut) ? reinterpret_cast<const float4*>(X + (long)bi * ldx)[u] : z;
+    }
+    bool big = false;
+    const int nr = k == 0 ? 2 * P - 1 : P;
+    for (int rd = 0; rd < nr; ++rd) {
+      // the pair's Gram over the data rows: two accumulator sets halve the chains
+      float al0 = 0.f, be0 = 0.f, ga0 = 0.f, al1 = 0.f, be1 = 0.f, ga1 = 0.f;
+#pragma unroll
+      for (int t = 0; t < NUD; ++t) {
+        const bool d = gl + G * t < nud;
+        const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 a = d ? tp[t] : z, b = d ? bt[t] : z;
+        float& al = (t & 1) ? al1 : al0;
+        float& be = (t & 1) ? be1 : be0;
+        float& ga = (t & 1) ? ga1 : ga0;
+        al = fmaf(a.x, a.x, al); al = fmaf(a.y, a.y, al); al = fmaf(a.z, a.z, al); al = fmaf(a.w, a.w, al);
+        be = fmaf(b.x, b.x, be); be = fmaf(b.y, b.y, be); be = fmaf(b.z, b.z, be); be = fmaf(b.w, b.w, be);
+        ga = fmaf(a.x, b.x, ga); ga = fmaf(a.y, b.y, ga); ga = fmaf(a.z, b.z, ga); ga = fmaf(a.w, b.w, ga);
+      }
+      float al = al0 + al1, be = be0 + be1, ga = ga0 + ga1;
+#pragma unroll
+      for (int o = G / 2; o > 0; o >>= 1) {
+        al += __shfl_xor_sync(kAll, al, o);
+        be += __shfl_xor_sync(kAll, be, o);
+        ga += __shfl_xor_sync(kAll, ga, o);
+      }
+      al *= is2;
+      be *= is2;
+      ga *= is2;
+      const bool live = ti < cols && bi < cols && al > (float)kJacobiFloor && be > (float)kJacobiFloor;
+      if (live && ga * ga > tol2 * al * be) {
+        // the lower column index is the rotation's first column, as in cta_hestenes
+        const bool swp = ti > bi;
+        float c, s;
+        jacobi_rotation(swp ? al - be : be - al, 2.f * ga, c, s);
+        if (swp) s = -s;
+#pragma unroll
+        for (int t = 0; t < NU; ++t) {
+          const float4 a = tp[t], b = bt[t];
+          tp[t] = make_float4(c * a.x - s * b.x, c * a.y - s * b.y, c * a.z - s * b.z, c * a.w - s * b.w);
+          bt[t] = make_float4(s * a.x + c * b.x, s * a.y + c * b.y, s * a.z + c * b.z, s * a.w + c * b.w);
+        }
+        big = big || ga * ga > kJacobiQuadStop * kJacobiQuadStop * al * be;
+      }
+      if (k == 0) {
+        // circle method over the P slots: slot 0's top stays; slot 1's top <-
+        // slot 0's bottom, other tops <- the previous slot's top; bottoms <-
+        // the next slot's bottom, the last slot's bottom <- its own top
+        const bool first = slot == 0, last = slot == P - 1;
+#pragma unroll
+        for (int t = 0; t < NU; ++t) {
+          float* tv = reinterpret_cast<float*>(&tp[t]);
+          float* bv = reinterpret_cast<float*>(&bt[t]);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float up = __shfl_up_sync(kAll, first ? bv[q] : tv[q], G);
+            const float dn = __shfl_down_sync(kAll, bv[q], G);
+            const float nt = first ? tv[q] : up;
+            bv[q] = last ? tv[q] : dn;
+            tv[q] = nt;
+          }
+        }
+        const int up = __shfl_up_sync(kAll, first ? bi : ti, G);
+        const int dn = __shfl_down_sync(kAll, bi, G);
+        const int nt = first ? ti : up;
+        bi = last ? ti : dn;
+        ti = nt;
+      } else if (rd < nr - 1) {  // cross rounds: the bottoms move on one group
+        const int src = (lane + G) & 31;
+#pragma unroll
+        for (int t = 0; t < NU; ++t) {
+          bt[t].x = __shfl_sync(kAll, bt[t].x, src);
+          bt[t].y = __shfl_sync(kAll, bt[t].y, src);
+          bt[t].z = __shfl_sync(kAll, bt[t].z, src);
+          bt[t].w = __shfl_sync(kAll, bt[t].w, src);
+        }
+        bi = __shfl_sync(kAll, bi, src);
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < NU; ++t) {
+      const int u = gl + G * t;
+      if (u < nut) {
+        if (ti < cols) reinterpret_cast<float4*>(X + (long)ti * ldx)[u] = tp[t];
+        if (bi < cols) reinterpret_cast<float4*>(X + (long)bi * ldx)[u] = bt[t];
+      }
+    }
+    quiet = named_barrier_or(kJacobiBarrier, nbar, big) ? 0 : quiet + 1;
+    if (quiet >= nbp - 1) {
+      ++br;
+      break;
+    }
+  }
+  if (quiet < nbp - 1) return max_sweeps;
+  return (br + nbp - 2) / (nbp - 1) - 1;
+}
+
+// The core's Jacobi: the block-ordered register form when the shape fits
+// it (up to 16 warps of block pairs, at most six units per lane), else the
+// cyclic form.  Same contract as cta_hestenes_any with accum = true.
+static __device__ int core_hestenes(float* X, int len, int voff, int cols, int ldx, float tol,
+                                    int max_sweeps, double inv_scale2) {
+  const int nut = (voff + ((cols + 3) & ~3)) / 4, nud = voff / 4;
+  const int nu = (nut + kBlkLanes - 1) / kBlkLanes, nud_l = (nud + kBlkLanes - 1) / kBlkLanes;
+  const int nb = (cols + 3) / 4, aw = (nb + (nb & 1)) / 2;
+  const bool fits = (reinterpret_cast<unsigned long>(X) & 15) == 0 && ldx % 4 == 0 &&
+                    aw <= (int)(blockDim.x / 32);
+#define KVD_BJ(UU, DD)                                                                    \
+  if (fits && nu == UU && nud_l == DD)                                                    \
+    return cta_block_hestenes<UU, DD>(X, len, voff, cols, ldx, tol, max_sweeps, inv_scale2);
+  KVD_BJ(2, 1) KVD_BJ(3, 2) KVD_BJ(4, 2) KVD_BJ(5, 3) KVD_BJ(6, 3)
+#undef KVD_BJ
+  return cta_hestenes_any<float>(X, len, voff, cols, ldx, tol, max_sweeps, inv_scale2);
+}
+
 // 16 consecutive floats p[j0 .. j0+16) of a row, zero past `nb`; `vec` =
 // the row start and j0 are 16-byte aligned.
 static __device__ __forceinline__ void load16(const float* p, int j0, int nb, bool vec,
@@ -1528,8 +1695,8 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
   __syncthreads();
   double b2 = s_xnorm2;  // ||B||_F^2 <= ||sigma||^2 + ||X||_F^2 sets the core's scale
   for (int c = 0; c < r; ++c) b2 += (double)sig[c] * sig[c];
-  sw = cta_hestenes_any<float>(BT, LB, woff, N, ldbt, 1.2e-7f * sqrtf((float)LB) + 2.4e-7f, 30,
-                               b2 > 0.0 ? 1.0 / b2 : 1.0);
+  sw = core_hestenes(BT, LB, woff, N, ldbt, 1.2e-7f * sqrtf((float)LB) + 2.4e-7f, 30,
+                     b2 > 0.0 ? 1.0 / b2 : 1.0);
   __syncthreads();
   cta_colnorm_order(BT, LB, N, ldbt, nrm, ord);
   if (sw >= 30 && tid == 0) atomicOr(&A.status[kStatusNumeric], 2);
