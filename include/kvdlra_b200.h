@@ -164,6 +164,24 @@ int kvd_factored_decode(const kvd_config* cfg, const kvd_buffers* buf, const kvd
                         float scaling, void* out, void* workspace, size_t ws_bytes,
                         kvd_stream_t stream);
 
+/* Factored chunk attention for problems [p0, p0+count): every query of a
+ * chunk, q (count, Hq, q_len, D) post-RoPE with element strides (q_sb, q_sh,
+ * q_st) and unit stride over D, against [sinks | exact tier | RoPE(U_k C_k) |
+ * ring (| tail)] with the causal mask over the last q_len keys, without
+ * materialising the middle: keys rebuilt per 128-token tile on the tensor
+ * cores, values accumulated in coordinate space.  Replaces HF attention over
+ * bug_cache.py:1404-1423's (ingest: the chunk is the end of the ring, tail
+ * empty) and 1390-1402's (frozen scoring: the chunk is `tail`) dense return
+ * value.  out (count, q_len, Hq, D) contiguous.  bf16, head_dim 64, rank <=
+ * 32 with rank % 4 == 0 (kvd_chunk_attention_supported); KVD_ERR_ARG
+ * otherwise. */
+int kvd_factored_chunk_attention(const kvd_config* cfg, const kvd_buffers* buf, const kvd_counters* ctr,
+                                 int32_t p0, int32_t count, const void* q, int64_t q_sb, int64_t q_sh,
+                                 int64_t q_st, int32_t num_q_heads, int32_t q_len, float scaling,
+                                 kvd_hf_view tail_k, kvd_hf_view tail_v, void* out, kvd_stream_t stream);
+/* 1 when kvd_factored_chunk_attention takes this configuration. */
+int kvd_chunk_attention_supported(const kvd_config* cfg, int32_t num_q_heads);
+
 /* ------------------------------------------------ integrator primitives */
 
 /* Batched augmented rank-adaptive BUG step on `n_batch` independent problems

@@ -1,4 +1,4 @@
-"""Factored decode behind transformers' own attention call.
+"""Factored decode and chunk attention behind transformers' own attention call.
 
 In the reference, a decode step of ``LlamaAttention`` on a
 ``BugStreamingCache`` gets the dense retained cache back from
@@ -13,10 +13,13 @@ a :class:`kvdlra_b200.BugStreamingCache`, the cache's decode-step ``update``
 instead of a dense peek, and the registered function answers the query with
 ``kvd_factored_decode`` over the compressed state -- keys rebuilt from the
 coordinates with RoPE at each token's true position, values accumulated in
-coordinate space, the verbatim tiers read in place.  Every other call
-(single-shot prefill, chunked ingest, frozen scoring, or any cache that is
-not a ``BugStreamingCache``) goes to SDPA over what ``update`` returned,
-exactly as before.  ``update``'s return contract is unchanged for models that
+coordinate space, the verbatim tiers read in place.  Chunked ingest
+(bug_cache.py:1404-1423) and frozen scoring (1390-1402) are answered the same
+way by ``kvd_factored_chunk_attention`` (causal over the chunk) where the
+library has a chunk kernel for the shape (bf16, head_dim 64, rank <= 32);
+other shapes, the single-shot prefill and any cache that is not a
+``BugStreamingCache`` go to SDPA over what ``update`` returned, exactly as
+before.  ``update``'s return contract is unchanged for models that
 do not select the function, so lock-step comparisons against the reference's
 dense peek still hold.
 """
@@ -47,10 +50,15 @@ def factored_attention_forward(module: torch.nn.Module, query: torch.Tensor, key
     if layer is None:
         return sdpa_attention_forward(module, query, key, value, attention_mask, dropout=dropout,
                                       scaling=scaling, **kwargs)
+    if dropout:
+        raise NotImplementedError("factored attention has no dropout (inference only)")
+    mode = getattr(layer, "_mode", None)
+    if mode in ("ingest", "score"):
+        # a chunk (or a frozen-scoring window: its own K/V are the tail)
+        tail = (key, value) if mode == "score" else None
+        return layer.factored_chunk_attention(query, scaling=scaling, tail=tail), None
     if query.shape[2] != 1:
         raise RuntimeError("factored decode answers one query token per step")
-    if dropout:
-        raise NotImplementedError("factored decode has no attention dropout (inference only)")
     out = layer.factored_attention(query[:, :, 0, :], scaling=scaling)  # (B, Hq, D)
     return out.unsqueeze(1), None
 

@@ -593,14 +593,41 @@ class BugStreamingLayer(CacheLayerMixin):  # type: ignore[misc]
                N.hf_view(v), g.stream())
 
     def _ingest_chunk(self, key_states: Tensor, value_states: Tensor) -> tuple[Tensor, Tensor]:
-        """bug_cache.py:1404-1423: append to the ring, defer the absorb."""
+        """bug_cache.py:1404-1423: append to the ring, defer the absorb.  When
+        the owning model answers attention with the factored kernels and the
+        shape has a chunk kernel, the chunk's own K/V come back tagged with
+        this layer instead of the dense peek."""
         self._append(key_states, value_states)
+        if self._chunk_factored():
+            from .attention import tag_step
+
+            return tag_step(key_states, self), value_states
         return self._decode_peek()
 
     def _score_forward(self, key_states: Tensor, value_states: Tensor) -> tuple[Tensor, Tensor]:
-        """bug_cache.py:1390-1402: ``[retained | window]`` without mutation."""
+        """bug_cache.py:1390-1402: ``[retained | window]`` without mutation
+        (the window as the factored chunk kernel's tail when the model
+        selected it)."""
         k, v = self._check_kv(key_states, value_states)
+        if self._chunk_factored():
+            from .attention import tag_step
+
+            return tag_step(k, self), v
         return self._decode_peek(tail=(k, v))
+
+    def _chunk_factored(self) -> bool:
+        """Whether chunk queries of this layer go to the factored chunk kernel:
+        the model selected the factored attention and the library has a chunk
+        kernel for this shape (bf16, head_dim 64, rank <= 32)."""
+        own = self._owner
+        if own is None or not own._factored_decode():
+            return False
+        hq = getattr(own._model_config, "num_attention_heads", None)
+        if hq is None:
+            return False
+        g = self._group
+        assert g is not None
+        return bool(N.lib().kvd_chunk_attention_supported(C.byref(g.config(g.P)), int(hq)))
 
     def _w_need(self) -> int:
         g = self._group
@@ -686,6 +713,34 @@ class BugStreamingLayer(CacheLayerMixin):  # type: ignore[misc]
         N.call(g.device, "kvd_factored_decode", C.byref(cfg), C.byref(buf), C.byref(self._ctr),
                self._p0(), self.batch, q.data_ptr(), hq, sc,
                out.data_ptr(), ws, wsb, g.stream())
+        return out
+
+    def factored_chunk_attention(self, query: Tensor, scaling: float | None = None,
+                                 tail: tuple[Tensor, Tensor] | None = None) -> Tensor:
+        """Attention of a chunk of post-RoPE queries ``(B, Hq, q, D)`` against
+        the retained cache, causal over the last ``q`` keys, without
+        materialising the middle tier: ingest (the chunk is the end of the
+        ring, ``tail`` None) or frozen scoring (the chunk is ``tail``, not
+        appended).  Returns ``(B, q, Hq, D)``; equal to softmax attention over
+        :meth:`_decode_peek` (with the tail) and the bottom-right causal mask
+        up to bf16 rounding."""
+        g = self._group
+        assert g is not None
+        if query.dim() != 4 or query.shape[0] != self.batch or query.shape[3] != self.head_dim:
+            raise ValueError(f"expected a ({self.batch}, Hq, q, {self.head_dim}) query, got {tuple(query.shape)}")
+        if query.dtype != self.dtype:
+            raise ValueError(f"query dtype {query.dtype} != cache dtype {self.dtype}")
+        q = query if query.stride(3) == 1 else query.contiguous()
+        hq, q_len = int(q.shape[1]), int(q.shape[2])
+        out = torch.empty(self.batch, q_len, hq, self.head_dim, dtype=self.dtype, device=self.device)
+        sc = (1.0 / math.sqrt(self.head_dim)) if scaling is None else float(scaling)
+        tk = tv = None
+        if tail is not None:
+            tk, tv = self._check_kv(tail[0], tail[1])
+        cfg, buf = g.config(g.P), g.buffers(0)
+        N.call(g.device, "kvd_factored_chunk_attention", C.byref(cfg), C.byref(buf), C.byref(self._ctr),
+               self._p0(), self.batch, q.data_ptr(), q.stride(0), q.stride(1), q.stride(2), hq, q_len, sc,
+               N.hf_view(tk), N.hf_view(tv), out.data_ptr(), g.stream())
         return out
 
     # ------------------------------------------------------------ state views

@@ -145,4 +145,10 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
                            int count, const void* q, int Hq, float scaling, void* out, char* ws,
                            size_t ws_bytes, cudaStream_t s, cudaStream_t side = nullptr,
                            cudaEvent_t ev_fork = nullptr, cudaEvent_t ev_join = nullptr);
+// Factored chunk attention (chunk_attn.cu): bf16, head_dim 64, rank <= 32.
+bool chunk_attention_applicable(const kvd_config& c, int num_q_heads);
+int launch_chunk_attention(const kvd_config& c, const kvd_buffers& bu, const kvd_counters& k, int p0,
+                           int count, const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st, int Hq,
+                           int q_len, float scaling, const kvd_hf_view& tail_k, const kvd_hf_view& tail_v,
+                           void* out, cudaStream_t s);
 }  // namespace kvd_host

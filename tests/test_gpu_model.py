@@ -22,7 +22,7 @@ import torch
 
 from golden.make_golden import MODEL_CASE, tiny_llama
 
-from kvdlra_b200 import BugStreamingCache, enable_factored_decode
+from kvdlra_b200 import BugStreamingCache, BugStreamingLayer, enable_factored_decode
 from kvdlra_b200.harness import decode_greedy, prefill_chunked
 
 pytestmark = pytest.mark.gpu
@@ -64,15 +64,29 @@ def test_tiny_llama_matches_reference_logits(factored: bool) -> None:
     cache.check_status()
 
 
-def test_factored_decode_behind_llama_attention_bf16() -> None:
+def test_factored_decode_behind_llama_attention_bf16(monkeypatch) -> None:
     """bf16: the same prompt and teacher-forced tokens through the factored
-    kernel and through SDPA over the dense peek agree within the bf16 rule,
+    kernels (chunk attention for the ingest chunks, factored decode for the
+    steps) and through SDPA over the dense peek agree within the bf16 rule,
     and greedy ``model.generate`` runs on the factored path."""
     g = np.load(GOLDEN / "model_llama_tiny.npz")
     c = MODEL_CASE
     model = tiny_llama(c).to(DEV, torch.bfloat16)
     ids = torch.from_numpy(g["ids"]).to(DEV)
     forced = torch.from_numpy(g["dec_tokens"])[None]
+    calls = {"chunk": 0, "decode": 0}
+    chunk_fn, dec_fn = BugStreamingLayer.factored_chunk_attention, BugStreamingLayer.factored_attention
+
+    def chunk_spy(self, *a, **k):
+        calls["chunk"] += 1
+        return chunk_fn(self, *a, **k)
+
+    def dec_spy(self, *a, **k):
+        calls["decode"] += 1
+        return dec_fn(self, *a, **k)
+
+    monkeypatch.setattr(BugStreamingLayer, "factored_chunk_attention", chunk_spy)
+    monkeypatch.setattr(BugStreamingLayer, "factored_attention", dec_spy)
     runs = {}
     for mode in ("sdpa", "factored"):
         if mode == "factored":
@@ -82,13 +96,46 @@ def test_factored_decode_behind_llama_attention_bf16() -> None:
         cache = BugStreamingCache(model, **c["cache_kw"])
         first = prefill_chunked(model, cache, ids, c["chunk"], keep_logits=True)
         _, logits = decode_greedy(model, cache, first, c["tokens"], c["decode"], forced=forced)
-        runs[mode] = logits.float()
+        runs[mode] = torch.cat([first[:, None].float(), logits.float()], dim=1)
     ref = runs["sdpa"]
     err = float((runs["factored"] - ref).abs().max() / ref.abs().max())
     assert err < 2e-2, err
+    # every chunk after the first (the single-shot prefill) and every step, per layer
+    n_chunks = -(-c["tokens"] // c["chunk"])
+    assert calls["chunk"] == c["layers"] * (n_chunks - 1), calls
+    assert calls["decode"] == c["layers"] * c["decode"], calls
     # model.generate: single-shot prefill of the prompt, then factored decode steps
     cache = BugStreamingCache(model, **c["cache_kw"])
     out = model.generate(ids[:, :256], past_key_values=cache, max_new_tokens=12, do_sample=False)
     assert out.shape[1] == 256 + 12
     assert cache.get_seq_length() == 256 + 11
     cache.check_status()
+
+
+def test_frozen_scoring_through_chunk_attention_bf16() -> None:
+    """``frozen_scoring()`` (bug_cache.py:1871-1882, 1390-1402) under the
+    factored attention: a window scored against the retained cache (the
+    window as the chunk kernel's tail, nothing mutated) gives the logits SDPA
+    over the dense ``[retained | window]`` gives, within the bf16 rule."""
+    g = np.load(GOLDEN / "model_llama_tiny.npz")
+    c = MODEL_CASE
+    model = tiny_llama(c).to(DEV, torch.bfloat16)
+    ids = torch.from_numpy(g["ids"]).to(DEV)
+    ctx, win = ids[:, :512], ids[:, 512:640]
+    pos = torch.arange(512, 640, device=DEV)[None]
+    out = {}
+    for mode in ("sdpa", "factored"):
+        if mode == "factored":
+            enable_factored_decode(model)
+        else:
+            model.set_attn_implementation("sdpa")
+        cache = BugStreamingCache(model, **c["cache_kw"])
+        prefill_chunked(model, cache, ctx, c["chunk"])
+        n0 = cache.stored_state_numel()
+        with torch.no_grad(), cache.frozen_scoring():
+            out[mode] = model(win, past_key_values=cache, use_cache=True, position_ids=pos).logits.float()
+        assert cache.stored_state_numel() == n0  # scoring does not mutate
+        assert cache.get_seq_length() == 512
+        cache.check_status()
+    err = float((out["factored"] - out["sdpa"]).abs().max() / out["sdpa"].abs().max())
+    assert err < 2e-2, err
