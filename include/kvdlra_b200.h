@@ -178,7 +178,12 @@ int kvd_factored_decode(const kvd_config* cfg, const kvd_buffers* buf, const kvd
 int kvd_factored_chunk_attention(const kvd_config* cfg, const kvd_buffers* buf, const kvd_counters* ctr,
                                  int32_t p0, int32_t count, const void* q, int64_t q_sb, int64_t q_sh,
                                  int64_t q_st, int32_t num_q_heads, int32_t q_len, float scaling,
-                                 kvd_hf_view tail_k, kvd_hf_view tail_v, void* out, kvd_stream_t stream);
+                                 kvd_hf_view tail_k, kvd_hf_view tail_v, void* out, void* workspace,
+                                 size_t ws_bytes, kvd_stream_t stream);
+/* Workspace bytes that let kvd_factored_chunk_attention split the keys over
+ * several CTAs per query tile (a smaller or null workspace runs unsplit). */
+size_t kvd_chunk_attention_workspace_bytes(const kvd_config* cfg, int32_t count, int32_t num_q_heads,
+                                           int32_t q_len);
 /* 1 when kvd_factored_chunk_attention takes this configuration. */
 int kvd_chunk_attention_supported(const kvd_config* cfg, int32_t num_q_heads);
 

@@ -127,7 +127,9 @@ def lib() -> C.CDLL:
                                       vp, vp, sz, vp]
     i64 = C.c_int64
     L.kvd_factored_chunk_attention.argtypes = [P(Config), P(Buffers), P(Counters), i32, i32, vp, i64, i64,
-                                               i64, i32, i32, f32, HFView, HFView, vp, vp]
+                                               i64, i32, i32, f32, HFView, HFView, vp, vp, sz, vp]
+    L.kvd_chunk_attention_workspace_bytes.argtypes = [P(Config), i32, i32, i32]
+    L.kvd_chunk_attention_workspace_bytes.restype = sz
     L.kvd_chunk_attention_supported.argtypes = [P(Config), i32]
     L.kvd_chunk_attention_supported.restype = C.c_int
     L.kvd_bug_step.argtypes = [i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp, i32, f32,

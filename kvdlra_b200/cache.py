@@ -221,6 +221,7 @@ class _Group:
         self._grow_w(max(64, self.max_block * 2), [])
         self._ws: Tensor | None = None
         self._dec_ws: Tensor | None = None
+        self._chunk_ws: torch.Tensor | None = None
 
     # ------------------------------------------------------------ capacity
 
@@ -331,6 +332,13 @@ class _Group:
         if self._dec_ws is None or self._dec_ws.numel() < need:
             self._dec_ws = torch.empty(need, dtype=torch.uint8, device=self.device)
         return self._dec_ws.data_ptr(), self._dec_ws.numel()
+
+    def chunk_workspace(self, count: int, hq: int, q_len: int) -> tuple[int, int]:
+        cfg = self.config(self.P)
+        need = int(N.lib().kvd_chunk_attention_workspace_bytes(C.byref(cfg), count, hq, q_len))
+        if self._chunk_ws is None or self._chunk_ws.numel() < need:
+            self._chunk_ws = torch.empty(need, dtype=torch.uint8, device=self.device)
+        return self._chunk_ws.data_ptr(), self._chunk_ws.numel()
 
     def stream(self) -> int:
         return N.stream_ptr(self.device)
@@ -738,9 +746,10 @@ class BugStreamingLayer(CacheLayerMixin):  # type: ignore[misc]
         if tail is not None:
             tk, tv = self._check_kv(tail[0], tail[1])
         cfg, buf = g.config(g.P), g.buffers(0)
+        ws, wsb = g.chunk_workspace(self.batch, hq, q_len)
         N.call(g.device, "kvd_factored_chunk_attention", C.byref(cfg), C.byref(buf), C.byref(self._ctr),
                self._p0(), self.batch, q.data_ptr(), q.stride(0), q.stride(1), q.stride(2), hq, q_len, sc,
-               N.hf_view(tk), N.hf_view(tv), out.data_ptr(), g.stream())
+               N.hf_view(tk), N.hf_view(tv), out.data_ptr(), ws, wsb, g.stream())
         return out
 
     # ------------------------------------------------------------ state views

@@ -58,7 +58,14 @@ struct CaArgs {
   __nv_bfloat16* out;                  // (count, q_len, Hq, D)
   float scaling;
   int* status;
+  // split of the key tiles over CTAs: split z of nsplit takes tiles
+  // [z * ntiles / nsplit, (z + 1) * ntiles / nsplit) of the concatenation and,
+  // when nsplit > 1, writes a record per row instead of the output:
+  // m, l, O[D] (O unnormalised, U_v,g already applied)
+  int nsplit, ntiles;
+  float* part;
 };
+constexpr int kCaRec = kCaD + 2;  // floats per partial record
 
 struct CaSmem { int qs, ks, ps, vs, ck, uk, uv, pos, bar, total; };  // bytes
 __host__ __device__ inline CaSmem ca_smem() {
@@ -114,8 +121,10 @@ __global__ void __launch_bounds__(kCaThreads) chunk_attn_kernel(CaArgs a) {
   constexpr int D = kCaD, HALF = kCaD / 2;
   extern __shared__ __align__(1024) unsigned char csm[];
   const CaSmem L = ca_smem();
-  const int qt = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+  const int qt = blockIdx.x, g = blockIdx.y, b = blockIdx.z / a.nsplit, split = blockIdx.z % a.nsplit;
   const int tid = threadIdx.x, warp = tid >> 5;
+  const int tile_lo = (int)((long)split * a.ntiles / a.nsplit);
+  const int tile_hi = (int)((long)(split + 1) * a.ntiles / a.nsplit);
   const int G = a.G, ld = a.ld;
   const int r_k = a.rk[b], r_v = a.rv[b];
   unsigned char* qs = csm + L.qs;
@@ -201,10 +210,11 @@ __global__ void __launch_bounds__(kCaThreads) chunk_attn_kernel(CaArgs a) {
   const long vis_cta = a.total - a.q_len + i_last;
   const long vis_row = a.total - a.q_len + qi;
   long x0 = 0;
+  int tile = 0;  // index of the tile in the concatenation
   for (int s = 0; s < kCaSegs && ok; ++s) {
     const int len = a.seg_len[s];
-    for (int t0 = 0; t0 < len && ok; t0 += kCaKeys) {
-      if (x0 + t0 > vis_cta) break;
+    for (int t0 = 0; t0 < len && ok; t0 += kCaKeys, ++tile) {
+      if (tile < tile_lo || tile >= tile_hi || x0 + t0 > vis_cta) continue;
       const int nk = min(kCaKeys, len - t0);
       if (s == 2) {
         // ----- middle tile: stage C_k (tf32) and C_v^T (bf16), rebuild keys on the tensor core
@@ -417,9 +427,15 @@ __global__ void __launch_bounds__(kCaThreads) chunk_attn_kernel(CaArgs a) {
   __syncthreads();
   if (warp == 0) umma::tmem_dealloc(tmem, 256);
   if (!row_ok) return;
-  // out row = (acc_d + U_v,g acc_c) / l
-  const float inv_l = (ok && l_run > 0.f) ? 1.f / l_run : 0.f;
+  // O = acc_d + U_v,g acc_c; the output row O / l, or this split's record
+  const bool rec = a.nsplit > 1;
+  const float inv_l = rec ? 1.f : ((ok && l_run > 0.f) ? 1.f / l_run : 0.f);
   __nv_bfloat16* dst = a.out + (((long)b * a.q_len + qi) * a.Hq + qh) * D;
+  float* pr = a.part + ((((long)b * a.H + g) * a.rows + R) * a.nsplit + split) * kCaRec;
+  if (rec) {
+    pr[0] = ok ? m_run : -INFINITY;
+    pr[1] = ok ? l_run : 0.f;
+  }
 #pragma unroll
   for (int d0 = 0; d0 < D; d0 += 8) {
     float o[8];
@@ -429,11 +445,46 @@ __global__ void __launch_bounds__(kCaThreads) chunk_attn_kernel(CaArgs a) {
       float v = acc_d[d0 + e];
 #pragma unroll
       for (int j = 0; j < kCaR; ++j) v = fmaf(acc_c[j], ur[j], v);
-      o[e] = v * inv_l;
+      o[e] = ok ? v * inv_l : 0.f;
     }
-    *reinterpret_cast<uint4*>(dst + d0) =
-        make_uint4(pack_bf16(o[0], o[1]), pack_bf16(o[2], o[3]), pack_bf16(o[4], o[5]), pack_bf16(o[6], o[7]));
+    if (rec) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) pr[2 + d0 + e] = o[e];
+    } else {
+      *reinterpret_cast<uint4*>(dst + d0) =
+          make_uint4(pack_bf16(o[0], o[1]), pack_bf16(o[2], o[3]), pack_bf16(o[4], o[5]), pack_bf16(o[6], o[7]));
+    }
   }
+}
+
+// Combine the splits' records of a row: M = max m_s, out = sum e^(m_s - M) O_s /
+// sum e^(m_s - M) l_s.  One thread per (row, column), rows of every group and
+// sequence.
+__global__ void __launch_bounds__(256) chunk_merge_kernel(CaArgs a) {
+  constexpr int D = kCaD;
+  const long e = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long nrows = (long)gridDim.y * a.H * a.rows;  // gridDim.y = sequences
+  (void)nrows;
+  const int d = (int)(e % D);
+  const long rr = e / D;  // row within (group, row)
+  if (rr >= (long)a.H * a.rows) return;
+  const int b = blockIdx.y;
+  const int g = (int)(rr / a.rows), R = (int)(rr % a.rows);
+  const float* pr = a.part + (((long)b * a.H + g) * a.rows + R) * a.nsplit * kCaRec;
+  float M = -INFINITY;
+  for (int z = 0; z < a.nsplit; ++z) M = fmaxf(M, pr[z * kCaRec]);
+  float num = 0.f, den = 0.f;
+  if (M != -INFINITY) {
+    for (int z = 0; z < a.nsplit; ++z) {
+      const float mz = pr[z * kCaRec];
+      if (mz == -INFINITY) continue;
+      const float w = __expf(mz - M);
+      den = fmaf(w, pr[z * kCaRec + 1], den);
+      num = fmaf(w, pr[z * kCaRec + 2 + d], num);
+    }
+  }
+  const int qi = R / a.G, qh = g * a.G + R % a.G;
+  a.out[(((long)b * a.q_len + qi) * a.Hq + qh) * D + d] = __float2bfloat16_rn(den > 0.f ? num / den : 0.f);
 }
 
 }  // namespace kvd
@@ -449,10 +500,17 @@ bool chunk_attention_applicable(const kvd_config& c, int num_q_heads) {
          (c.num_heads * c.head_dim) % 8 == 0;
 }
 
+constexpr int kCaMaxSplit = 8;
+
+size_t chunk_attention_ws_bytes(const kvd_config& c, int count, int num_q_heads, int q_len) {
+  const long rows = (long)q_len * (num_q_heads / (c.num_heads > 0 ? c.num_heads : 1));
+  return (size_t)count * c.num_heads * rows * kCaMaxSplit * kCaRec * sizeof(float);
+}
+
 int launch_chunk_attention(const kvd_config& c, const kvd_buffers& bu, const kvd_counters& k, int p0,
                            int count, const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st, int Hq,
                            int q_len, float scaling, const kvd_hf_view& tail_k, const kvd_hf_view& tail_v,
-                           void* out, cudaStream_t s) {
+                           void* out, void* ws, size_t ws_bytes, cudaStream_t s) {
   if (!chunk_attention_applicable(c, Hq)) {
     set_error("factored chunk attention: unsupported shape (bf16, head_dim %d, rank <= %d, rank %% 4 == 0)",
               kCaD, kCaR);
@@ -503,12 +561,37 @@ int launch_chunk_attention(const kvd_config& c, const kvd_buffers& bu, const kvd
   if (!aligned) { set_error("factored chunk attention: operands must be 16-byte aligned"); return KVD_ERR_ARG; }
   const CaSmem L = ca_smem();
   if (int rc = ensure_smem((const void*)chunk_attn_kernel, L.total, "chunk_attn_kernel")) return rc;
-  dim3 grid((a.rows + kCaRows - 1) / kCaRows, a.H, count);
+  // split the key tiles so about two CTAs per SM run (each fits two to an
+  // SM); splits write records that chunk_merge_kernel combines
+  a.ntiles = 0;
+  for (int i = 0; i < kCaSegs; ++i) a.ntiles += (a.seg_len[i] + kCaKeys - 1) / kCaKeys;
+  const int qtiles = (a.rows + kCaRows - 1) / kCaRows;
+  const long ctas = (long)qtiles * a.H * count;
+  static int sm_count[kMaxDevices] = {0};
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess && dev >= 0 && dev < kMaxDevices) {
+    if (sm_count[dev] == 0) cudaDeviceGetAttribute(&sm_count[dev], cudaDevAttrMultiProcessorCount, dev);
+    if (sm_count[dev] > 0) sms = sm_count[dev];
+  }
+  int nsplit = (int)((2L * sms + ctas - 1) / ctas);
+  nsplit = max(1, min(nsplit, min(kCaMaxSplit, a.ntiles / 4)));
+  const size_t need = (size_t)count * a.H * a.rows * nsplit * kCaRec * sizeof(float);
+  if (nsplit > 1 && (!ws || ws_bytes < need || !al16(ws))) nsplit = 1;
+  a.nsplit = nsplit;
+  a.part = (float*)ws;
+  dim3 grid(qtiles, a.H, count * nsplit);
   {
     KTimerScope kts_("chunk_attn_kernel", s);
     chunk_attn_kernel<<<grid, kCaThreads, L.total, s>>>(a);
   }
-  return check_launch("chunk_attn_kernel");
+  if (int rc = check_launch("chunk_attn_kernel")) return rc;
+  if (nsplit > 1) {
+    const long per = (long)a.H * a.rows * kCaD;
+    dim3 mg((unsigned)((per + 255) / 256), count);
+    KTimerScope kts_("chunk_merge_kernel", s);
+    chunk_merge_kernel<<<mg, 256, 0, s>>>(a);
+  }
+  return check_launch("chunk_merge_kernel");
 }
 
 }  // namespace kvd_host

@@ -150,5 +150,6 @@ bool chunk_attention_applicable(const kvd_config& c, int num_q_heads);
 int launch_chunk_attention(const kvd_config& c, const kvd_buffers& bu, const kvd_counters& k, int p0,
                            int count, const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st, int Hq,
                            int q_len, float scaling, const kvd_hf_view& tail_k, const kvd_hf_view& tail_v,
-                           void* out, cudaStream_t s);
+                           void* out, void* ws, size_t ws_bytes, cudaStream_t s);
+size_t chunk_attention_ws_bytes(const kvd_config& c, int count, int num_q_heads, int q_len);
 }  // namespace kvd_host

@@ -686,13 +686,19 @@ extern "C" int kvd_factored_chunk_attention(const kvd_config* cfg, const kvd_buf
                                             const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st,
                                             int32_t num_q_heads, int32_t q_len, float scaling,
                                             kvd_hf_view tail_k, kvd_hf_view tail_v, void* out,
-                                            kvd_stream_t stream) {
+                                            void* workspace, size_t ws_bytes, kvd_stream_t stream) {
   int rc = validate(cfg);
   if (rc) return rc;
   if (p0 < 0 || count < 1 || p0 + count > cfg->n_problems) { set_error("kvd_factored_chunk_attention: bad problem range"); return KVD_ERR_ARG; }
   if (!q || !out) { set_error("kvd_factored_chunk_attention: null query or output"); return KVD_ERR_ARG; }
   return launch_chunk_attention(*cfg, *buf, *ctr, p0, count, q, q_sb, q_sh, q_st, num_q_heads, q_len,
-                                scaling, tail_k, tail_v, out, (cudaStream_t)stream);
+                                scaling, tail_k, tail_v, out, workspace, ws_bytes, (cudaStream_t)stream);
+}
+
+extern "C" size_t kvd_chunk_attention_workspace_bytes(const kvd_config* cfg, int32_t count,
+                                                      int32_t num_q_heads, int32_t q_len) {
+  if (!cfg || count < 1 || q_len < 1 || num_q_heads < 1) return 0;
+  return chunk_attention_ws_bytes(*cfg, count, num_q_heads, q_len);
 }
 
 extern "C" int kvd_chunk_attention_supported(const kvd_config* cfg, int32_t num_q_heads) {
