@@ -1186,15 +1186,15 @@ constexpr int kDuK = 32;  // staged rank columns (rank <= 32)
 constexpr long kDuWaitPolls = 1L << 22;
 
 struct DuSmem { int us, ck, cv, ldv, qs, cs, ps, st, vred, posb, bar, total; };  // bytes
-__host__ __device__ inline DuSmem du_smem(int n, int Hq) {
-  constexpr int D = 64;
+// n = this CTA's features (its KV groups x D), Hq = its query heads
+__host__ __device__ inline DuSmem du_smem(int n, int Hq, int D) {
   DuSmem m;
   m.ldv = kDuK + 4;
   m.us = 0;                                   // [n][32] basis, core-matrix layout
   m.ck = m.us + n * kDuK * 4;                 // 2 x [128][32] key coordinates, core-matrix layout
   m.cv = m.ck + 2 * kDuTok * kDuK * 4;        // 2 x [128][ldv] value coordinates
-  m.qs = m.cv + 2 * kDuTok * m.ldv * 4;       // [Hq][64] queries
-  m.cs = m.qs + Hq * D * 4;                   // [32 frequencies][128 tokens] (cos, sin)
+  m.qs = m.cv + 2 * kDuTok * m.ldv * 4;       // [Hq][D] queries
+  m.cs = m.qs + Hq * D * 4;                   // [D/2 frequencies][128 tokens] (cos, sin)
   m.ps = m.cs + (D / 2) * kDuTok * 8;         // [Hq][128] scores, then probabilities
   m.st = m.ps + Hq * kDuTok * 4;              // [Hq][4]: running max, correction
   m.vred = m.st + Hq * 16;                    // [256][4] value-product halves
@@ -1215,15 +1215,21 @@ __device__ __forceinline__ void cp16_zfill(void* dst, const void* src, bool vali
                : "memory");
 }
 
+// KV groups one CTA covers: as many as fill the 512 TMEM columns (all of
+// them at head_dim 64 with n <= 512; four of eight at head_dim 128)
+__host__ __device__ inline int du_groups(int H, int D) { return H * D <= 512 ? H : 512 / D; }
+
+template <int D>
 __global__ void __launch_bounds__(kDuThreads) decode_mid_umma_kernel(DecArgs a, int tpc, int chunk0,
                                                                      int* status) {
-  constexpr int D = 64, HALF = 32;
+  constexpr int HALF = D / 2;
   extern __shared__ __align__(1024) unsigned char dsm4[];
-  const int p = blockIdx.y;
-  const int H = a.H, G = a.G, Hq = a.H * a.G, ld = a.ld, n = a.H * D;
+  const int hb = du_groups(a.H, D), nsg = a.H / hb;
+  const int p = blockIdx.y / nsg, g0 = (blockIdx.y % nsg) * hb;  // this CTA's groups [g0, g0 + hb)
+  const int H = hb, G = a.G, Hq = hb * a.G, ld = a.ld, n = hb * D;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int r_k = a.rk[p];
-  const DuSmem L = du_smem(n, Hq);
+  const DuSmem L = du_smem(n, Hq, D);
   unsigned char* us = dsm4 + L.us;
   float* qs = reinterpret_cast<float*>(dsm4 + L.qs);
   float2* cs = reinterpret_cast<float2*>(dsm4 + L.cs);
@@ -1245,7 +1251,7 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_umma_kernel(DecArgs a, 
     umma::mbar_fence_init();
   }
   {  // the basis rows of every group (K-major core matrices, TF32, columns past the rank zero)
-    const float* U = a.uk + p * a.u_sp;
+    const float* U = a.uk + p * a.u_sp + (long)g0 * D * ld;
     for (int e = tid; e < n * (kDuK / 4); e += kDuThreads) {
       const int row = e / (kDuK / 4), k = 4 * (e % (kDuK / 4));
       float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -1259,7 +1265,7 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_umma_kernel(DecArgs a, 
           make_float4(umma::to_tf32(v.x), umma::to_tf32(v.y), umma::to_tf32(v.z), umma::to_tf32(v.w));
     }
   }
-  const __nv_bfloat16* qp = reinterpret_cast<const __nv_bfloat16*>(a.q) + (long)p * a.Hq * D;
+  const __nv_bfloat16* qp = reinterpret_cast<const __nv_bfloat16*>(a.q) + ((long)p * a.Hq + g0 * G) * D;
   for (int e = tid; e < Hq * D; e += kDuThreads) qs[e] = __bfloat162float(qp[e]);
   for (int h = tid; h < Hq; h += kDuThreads) st[4 * h] = -INFINITY;
   // a tile's coordinates land by cp.async straight into the MMA's layout (keys;
@@ -1435,7 +1441,9 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_umma_kernel(DecArgs a, 
   if (warp == 0) umma::tmem_dealloc(tmem, 512);
   // one partial record per group: m[G], l[G], acc_d[G][D] = 0, acc_c[G][ld]
   const int chunk = chunk0 + blockIdx.x;
-  auto rec = [&](int g) { return a.part + ((long)(p * H + g) * a.n_chunks + chunk) * a.part_sp_chunk; };
+  auto rec = [&](int g) {  // g: this CTA's group index
+    return a.part + ((long)(p * a.H + g0 + g) * a.n_chunks + chunk) * a.part_sp_chunk;
+  };
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const int row = warp + 16 * i;
@@ -1510,7 +1518,18 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
                        ((Hq_all + 15) / 16) * (a.ld / 8) <= kMidWarps * kMaxPW &&
                        4L * ms.total <= 200 * 1024 &&
                        (reinterpret_cast<uintptr_t>(a.uk) & 15) == 0 && a.u_sp % 4 == 0;
-  if (mid_all) {
+  // bf16, head_dim 64 or 128, rank <= 32: the middle tier on the
+  // 5th-generation tensor cores (128-token tiles; a CTA takes as many KV
+  // groups as fill TMEM, a multiple of 256 features), else decode_mid_kernel
+  const int du_hb = du_groups(a.H, a.D), du_n = du_hb * a.D, du_hq = du_hb * a.G;
+  const bool umma_mid = sizeof(T) == 2 && (a.D == 64 || a.D == 128) && mma && a.W > 0 &&
+                        a.H % du_hb == 0 && du_n % 256 == 0 && a.ld <= kDuK &&
+                        a.ld % 4 == 0 && du_hq <= 64 && du_hq * (a.ld / 4) <= 256 &&
+                        a.c_sp % 4 == 0 && (reinterpret_cast<uintptr_t>(a.ck) & 15) == 0 &&
+                        (reinterpret_cast<uintptr_t>(a.cv) & 15) == 0 &&
+                        (reinterpret_cast<uintptr_t>(a.uk) & 15) == 0 &&
+                        du_smem(du_n, du_hq, a.D).total <= device_smem_optin();
+  if (mid_all || umma_mid) {
     const int nvt = nv0 + nr;
     const int n_vch = nvt;  // one verbatim tile per CTA
     // tiles per CTA: one CTA fills an SM, so the launch takes
@@ -1524,20 +1543,13 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
         if (sm_count[dev] > 0) sms = sm_count[dev];
       }
     }
-    // bf16, head_dim 64, n = 256 or 512, rank <= 32: the middle tier on the
-    // 5th-generation tensor cores (128-token tiles), else decode_mid_kernel
-    const bool umma_mid = sizeof(T) == 2 && a.D == 64 && (n == 256 || n == 512) && a.ld <= kDuK &&
-                          a.ld % 4 == 0 && Hq_all <= 64 && Hq_all * (a.ld / 4) <= 256 &&
-                          a.c_sp % 4 == 0 && (reinterpret_cast<uintptr_t>(a.ck) & 15) == 0 &&
-                          (reinterpret_cast<uintptr_t>(a.cv) & 15) == 0 &&
-                          (reinterpret_cast<uintptr_t>(a.uk) & 15) == 0 &&
-                          du_smem(n, Hq_all).total <= device_smem_optin();
     const int ttok = umma_mid ? kDuTok : kTT;
     const int nmt = (a.W + ttok - 1) / ttok;
     int tpc = umma_mid ? 1 : 2;
     long best = -1;
+    const int nsg = umma_mid ? a.H / du_hb : 1;  // CTAs per tile (group ranges)
     for (int t = tpc; t <= 8; ++t) {
-      const long waves = ((long)((nmt + t - 1) / t) * count + sms - 1) / sms;
+      const long waves = ((long)((nmt + t - 1) / t) * count * nsg + sms - 1) / sms;
       const long cost = waves * (2 * t + 1);
       if (best < 0 || cost < best) { best = cost; tpc = t; }
     }
@@ -1547,7 +1559,8 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
     if (need2 > ws_bytes) { set_error("factored decode: workspace too small"); return KVD_ERR_WORKSPACE; }
     constexpr bool kSplit = sizeof(T) == 4;
     auto mid_fn = a.D == 64 ? decode_mid_kernel<T, 64, kSplit> : decode_mid_kernel<T, 128, kSplit>;
-    if (int rc0 = ensure_smem((const void*)mid_fn, 4 * ms.total, "decode_mid_kernel")) return rc0;
+    if (!umma_mid)
+      if (int rc0 = ensure_smem((const void*)mid_fn, 4 * ms.total, "decode_mid_kernel")) return rc0;
     // the verbatim tiles run beside the middle tier (disjoint partial records)
     const bool fork = side && ev_fork && ev_join && n_vch > 0;
     if (n_vch > 0) {
@@ -1573,13 +1586,14 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
       return rc1;
     }
     if (umma_mid) {
-      const int dsm = du_smem(n, Hq_all).total;
-      if (int rc0 = ensure_smem((const void*)decode_mid_umma_kernel, dsm, "decode_mid_kernel")) {
+      const int dsm = du_smem(du_n, du_hq, a.D).total;
+      auto ufn = a.D == 64 ? decode_mid_umma_kernel<64> : decode_mid_umma_kernel<128>;
+      if (int rc0 = ensure_smem((const void*)ufn, dsm, "decode_mid_kernel")) {
         if (fork) cudaStreamWaitEvent(s, ev_join, 0);
         return rc0;
       }
       KTimerScope kts_("decode_mid_kernel", s);
-      decode_mid_umma_kernel<<<dim3(n_mch, count), kDuThreads, dsm, s>>>(a, tpc, n_vch, a.status);
+      ufn<<<dim3(n_mch, count * nsg), kDuThreads, dsm, s>>>(a, tpc, n_vch, a.status);
     } else {
       KTimerScope kts_("decode_mid_kernel", s);
       mid_fn<<<dim3(n_mch, count), kMidThreads, 4 * ms.total, s>>>(a, tpc, n_vch);

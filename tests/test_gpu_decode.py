@@ -35,6 +35,8 @@ def _rel(a: np.ndarray, b: np.ndarray) -> float:
     (2, 64, 1, 450, torch.float32),
     (3, 128, 2, 600, torch.bfloat16),
     (8, 64, 4, 1300, torch.bfloat16),
+    (8, 128, 4, 1300, torch.bfloat16),  # tcgen05 middle tier, two group ranges per tile
+    (2, 128, 4, 700, torch.bfloat16),   # tcgen05 middle tier, n = 256
 ])
 def test_factored_decode_equals_dense_over_peek(H: int, D: int, G: int, T: int, dtype) -> None:
     s = lowrank_stream(H, D, T, n_needles=5, seed=H * 100 + D + G)
