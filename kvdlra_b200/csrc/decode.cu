@@ -1326,11 +1326,15 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_umma_kernel(DecArgs a, 
       umma::commit(bar);
     }
     if (tile + 1 < t_end) prefetch(tile + 1, buf ^ 1);  // lands while this tile is processed
-    for (int e = tid; e < HALF * kDuTok; e += kDuThreads) {  // [frequency][token] rotary table
-      const int f = e / kDuTok, t = e % kDuTok;
-      float c = 1.f, sn = 0.f;
-      if (t < ntok) rope_cs_fast(posb[buf * kDuTok + t], a.inv_freq[f], a.rope_scale, &c, &sn);
-      cs[e] = make_float2(c, sn);
+    {  // [frequency][token] rotary table: a thread per token and every fourth frequency
+      const int t = tid & (kDuTok - 1);
+      const bool live = t < ntok;
+      const int pos = posb[buf * kDuTok + t];
+      for (int f = tid / kDuTok; f < HALF; f += kDuThreads / kDuTok) {
+        float c = 1.f, sn = 0.f;
+        if (live) rope_cs_fast(pos, a.inv_freq[f], a.rope_scale, &c, &sn);
+        cs[f * kDuTok + t] = make_float2(c, sn);
+      }
     }
     __syncthreads();
     ok_wait = umma::mbar_wait_bounded(bar, phase, kDuWaitPolls);
