@@ -487,7 +487,8 @@ static __device__ __forceinline__ int cta_hestenes_any(float* X, int len, int vo
 // are cta_hestenes's; the stop slides: the iteration ends once nbp - 1
 // consecutive block rounds (each pair once) rotated no pair with a cosine
 // above kJacobiQuadStop, wherever in the sweep that window starts.  Needs X
-// 16-byte aligned, ldx % 4 == 0 and (blocks + 1) / 2 <= warps of the CTA;
+// 16-byte aligned and ldx % 4 == 0; with more block pairs than warps, warp w
+// takes pairs w, w + warps, ... of each block round (they are disjoint);
 // returns the sweeps taken less one (max_sweeps when not converged).
 constexpr int kBlkLanes = 8;
 template <int NU, int NUD>
@@ -505,7 +506,8 @@ static __device__ __noinline__ int cta_block_hestenes(float* X, int len, int vof
   __syncthreads();
   if (cols <= 1) return 0;
   const int nut = vend / 4, nud = voff / 4;
-  const int nb = (cols + P - 1) / P, nbp = nb + (nb & 1), aw = nbp / 2;
+  const int nb = (cols + P - 1) / P, nbp = nb + (nb & 1), npairs = nbp / 2;
+  const int aw = min(npairs, nthr / 32);  // warps; warp w takes block pairs w, w + aw, ...
   if (warp >= aw) return 0;
   const int nbar = aw * 32;
   const float tol2 = tol * tol, is2 = (float)inv_scale2;
@@ -513,8 +515,10 @@ static __device__ __noinline__ int cta_block_hestenes(float* X, int len, int vof
   int br = 0, quiet = 0;
   for (; br < max_br; ++br) {
     const int k = br % (nbp - 1);
+    bool big = false;
+    for (int bp = warp; bp < npairs; bp += aw) {  // the block pairs are disjoint within a round
     int ba, bb;
-    rr_pair(warp, k, nbp, &ba, &bb);
+    rr_pair(bp, k, nbp, &ba, &bb);
     int ti = ba * P + slot, bi = bb * P + slot;  // column ids; >= cols: padding
     float4 tp[NU], bt[NU];
 #pragma unroll
@@ -524,7 +528,6 @@ static __device__ __noinline__ int cta_block_hestenes(float* X, int len, int vof
       tp[t] = (ti < cols && u < nut) ? reinterpret_cast<const float4*>(X + (long)ti * ldx)[u] : z;
       bt[t] = (bi < cols && u < nut) ? reinterpret_cast<const float4*>(X + (long)bi * ldx)[u] : z;
     }
-    bool big = false;
     const int nr = k == 0 ? 2 * P - 1 : P;
     for (int rd = 0; rd < nr; ++rd) {
       // the pair's Gram over the data rows: two accumulator sets halve the chains
@@ -609,6 +612,7 @@ static __device__ __noinline__ int cta_block_hestenes(float* X, int len, int vof
         if (bi < cols) reinterpret_cast<float4*>(X + (long)bi * ldx)[u] = bt[t];
       }
     }
+    }
     quiet = named_barrier_or(kJacobiBarrier, nbar, big) ? 0 : quiet + 1;
     if (quiet >= nbp - 1) {
       ++br;
@@ -620,19 +624,22 @@ static __device__ __noinline__ int cta_block_hestenes(float* X, int len, int vof
 }
 
 // The core's Jacobi: the block-ordered register form when the shape fits
-// it (up to 16 warps of block pairs, at most six units per lane), else the
+// it (up to two block pairs per warp, at most ten units per lane), else the
 // cyclic form.  Same contract as cta_hestenes_any with accum = true.
 static __device__ int core_hestenes(float* X, int len, int voff, int cols, int ldx, float tol,
                                     int max_sweeps, double inv_scale2) {
   const int nut = (voff + ((cols + 3) & ~3)) / 4, nud = voff / 4;
   const int nu = (nut + kBlkLanes - 1) / kBlkLanes, nud_l = (nud + kBlkLanes - 1) / kBlkLanes;
-  const int nb = (cols + 3) / 4, aw = (nb + (nb & 1)) / 2;
+  const int nb = (cols + 3) / 4, npairs = (nb + (nb & 1)) / 2;
+  // up to two block pairs per warp (the wider cores: r = 128, 128-column
+  // pre-fill blocks), at most ten units per lane
   const bool fits = (reinterpret_cast<unsigned long>(X) & 15) == 0 && ldx % 4 == 0 &&
-                    aw <= (int)(blockDim.x / 32);
+                    npairs <= 2 * (int)(blockDim.x / 32);
 #define KVD_BJ(UU, DD)                                                                    \
   if (fits && nu == UU && nud_l == DD)                                                    \
     return cta_block_hestenes<UU, DD>(X, len, voff, cols, ldx, tol, max_sweeps, inv_scale2);
-  KVD_BJ(2, 1) KVD_BJ(3, 2) KVD_BJ(4, 2) KVD_BJ(5, 3) KVD_BJ(6, 3)
+  KVD_BJ(2, 1) KVD_BJ(3, 2) KVD_BJ(4, 2) KVD_BJ(5, 3) KVD_BJ(6, 3) KVD_BJ(7, 4) KVD_BJ(8, 4)
+  KVD_BJ(9, 5) KVD_BJ(10, 5)
 #undef KVD_BJ
   return cta_hestenes_any<float>(X, len, voff, cols, ldx, tol, max_sweeps, inv_scale2);
 }
