@@ -491,17 +491,18 @@ static __device__ __forceinline__ int cta_hestenes_any(float* X, int len, int vo
 // takes pairs w, w + warps, ... of each block round (they are disjoint);
 // returns the sweeps taken less one (max_sweeps when not converged).
 constexpr int kBlkLanes = 8;
-template <int NU, int NUD>
+// ACCUM = false: nothing accumulated (rows [len, voff) are padding, zeroed).
+template <int NU, int NUD, bool ACCUM = true>
 static __device__ __noinline__ int cta_block_hestenes(float* X, int len, int voff, int cols, int ldx,
                                                       float tol, int max_sweeps, double inv_scale2) {
   constexpr int G = kBlkLanes, P = 32 / G;
   constexpr unsigned kAll = 0xffffffffu;
   const int tid = threadIdx.x, nthr = blockDim.x, warp = tid / 32, lane = tid % 32;
   const int slot = lane / G, gl = lane % G;
-  const int vend = voff + ((cols + 3) & ~3);
+  const int vend = voff + (ACCUM ? ((cols + 3) & ~3) : 0);
   for (long e = tid; e < (long)cols * (vend - len); e += nthr) {
     const int c = (int)(e / (vend - len)), k = len + (int)(e % (vend - len));
-    X[(long)c * ldx + k] = (k - voff == c) ? 1.f : 0.f;
+    X[(long)c * ldx + k] = (ACCUM && k - voff == c) ? 1.f : 0.f;
   }
   __syncthreads();
   if (cols <= 1) return 0;
@@ -642,6 +643,23 @@ static __device__ int core_hestenes(float* X, int len, int voff, int cols, int l
   KVD_BJ(9, 5) KVD_BJ(10, 5)
 #undef KVD_BJ
   return cta_hestenes_any<float>(X, len, voff, cols, ldx, tol, max_sweeps, inv_scale2);
+}
+
+// The same for a Jacobi with nothing accumulated (the pre-fill blocks'
+// preconditioner on the Gram factor's rows): the block form when it fits,
+// else cta_hestenes_any with accum = false.
+static __device__ int plain_hestenes(float* X, int len, int voff, int cols, int ldx, float tol,
+                                     int max_sweeps, double inv_scale2) {
+  const int nu = (voff / 4 + kBlkLanes - 1) / kBlkLanes;
+  const int nb = (cols + 3) / 4, npairs = (nb + (nb & 1)) / 2;
+  const bool fits = (reinterpret_cast<unsigned long>(X) & 15) == 0 && ldx % 4 == 0 &&
+                    npairs <= 2 * (int)(blockDim.x / 32);
+#define KVD_BJ(UU)                                                                         \
+  if (fits && nu == UU)                                                                    \
+    return cta_block_hestenes<UU, UU, false>(X, len, voff, cols, ldx, tol, max_sweeps, inv_scale2);
+  KVD_BJ(1) KVD_BJ(2) KVD_BJ(3) KVD_BJ(4)
+#undef KVD_BJ
+  return cta_hestenes_any<float>(X, len, voff, cols, ldx, tol, max_sweeps, inv_scale2, false);
 }
 
 // 16 consecutive floats p[j0 .. j0+16) of a row, zero past `nb`; `vec` =
@@ -1510,10 +1528,10 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
       __syncthreads();
       const double rt = red[1], rt2 = rt * rt;
       for (int i = j + 1 + tid; i < b; i += nthr) G[j * ldgb + i] = G[i * ldgb + j] * rt;
-      const int w = b - j - 1;
-      for (int e = tid; e < w * w; e += nthr) {
-        const int i = j + 1 + e / w, k = j + 1 + e % w;
-        if (k <= i) G[i * ldgb + k] = fma(-G[i * ldgb + j] * rt2, G[k * ldgb + j], G[i * ldgb + k]);
+      // the trailing lower triangle: a warp per row, lanes over its columns
+      for (int i = j + 1 + warp; i < b; i += nthr / 32) {
+        const double gi = -G[i * ldgb + j] * rt2;
+        for (int k = j + 1 + lane; k <= i; k += 32) G[i * ldgb + k] = fma(gi, G[k * ldgb + j], G[i * ldgb + k]);
       }
       __syncthreads();
     }
@@ -1557,8 +1575,7 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
       // sums: one-sided Jacobi on T^T (T's rows), nothing accumulated -- with
       // T = U_T S V_T^T the rotated columns are V_T S, so V_T = the columns over
       // their norms.  A numerically null column leaves V_T = I (no preconditioning).
-      cta_hestenes_any<float>(Tf, b, voffT, b, ldrT, 1.2e-7f * sqrtf((float)b) + 2.4e-7f, 30, inv_x2,
-                              false);
+      plain_hestenes(Tf, b, voffT, b, ldrT, 1.2e-7f * sqrtf((float)b) + 2.4e-7f, 30, inv_x2);
       __syncthreads();
       cta_colnorm_order(Tf, b, b, ldrT, sv, ordh);  // sv = the column norms (order unused)
       if (tid == 0) {
@@ -1581,6 +1598,40 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
       for (long e = tid; e < (long)b * n; e += nthr) XR[e] = Rm[e];  // R, contiguous columns
       __syncthreads();
       const int bq = (b + 3) / 4;
+      if (n % 4 == 0 && ldr % 4 == 0) {
+        // 4 rows x 4 columns per thread: one 16-byte load of R's column l
+        // feeds 16 products (same summation order per element as below)
+        const int nq = n / 4;
+        for (long e = tid; e < (long)bq * nq; e += nthr) {
+          const int jq = (int)(e / nq), i0 = 4 * (int)(e % nq);
+          const int j0 = 4 * jq;
+          const float* vc[4];
+          bool hv[4];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            hv[c] = j0 + c < b;
+            vc[c] = Tf + (long)(hv[c] ? j0 + c : j0) * ldrT;
+          }
+          float acc[4][4] = {};
+#pragma unroll 2
+          for (int l = 0; l < b; ++l) {
+            const float4 x = *reinterpret_cast<const float4*>(XR + (long)l * n + i0);
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const float v = vc[c][l];
+              acc[c][0] = fmaf(x.x, v, acc[c][0]);
+              acc[c][1] = fmaf(x.y, v, acc[c][1]);
+              acc[c][2] = fmaf(x.z, v, acc[c][2]);
+              acc[c][3] = fmaf(x.w, v, acc[c][3]);
+            }
+          }
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            if (hv[c])
+              *reinterpret_cast<float4*>(Rm + (long)(j0 + c) * ldr + i0) =
+                  make_float4(acc[c][0], acc[c][1], acc[c][2], acc[c][3]);
+        }
+      } else {
       for (long e = tid; e < (long)bq * n; e += nthr) {  // R V into the augmented columns,
         const int jq = (int)(e / n), i = (int)(e % n);   // four columns per thread
         const int j0 = 4 * jq;
@@ -1602,6 +1653,7 @@ __global__ void __launch_bounds__(kStepThreads) bug_step_kernel(BugStepBatch bat
         if (h1) Rm[(long)(j0 + 1) * ldr + i] = a1;
         if (h2) Rm[(long)(j0 + 2) * ldr + i] = a2;
         if (h3) Rm[(long)(j0 + 3) * ldr + i] = a3;
+      }
       }
       for (int e = tid; e < b * b; e += nthr) {  // and V below them, the Jacobi's start
         const int j = e / b, l = e % b;
