@@ -92,6 +92,31 @@ def test_chunk_attention_equals_dense_causal(H: int, G: int, T: int, q_len: int,
     layer._group.check_status()
 
 
+def test_chunk_attention_two_sequences() -> None:
+    """Two sequences of one layer (different streams, so different ranks,
+    tiers and coordinates) answered by one call: each equals its own dense
+    causal attention."""
+    H, G, T, q_len, D = 4, 4, 900, 150, 64
+    streams = [lowrank_stream(H, D, T + q_len, n_needles=4, seed=77 + i) for i in range(2)]
+    layer = _layer(H, D, T, 32, 64, "lowrank_surprise")
+    k = torch.stack([torch.from_numpy(st.k_post) for st in streams]).to(DEV, torch.bfloat16)
+    v = torch.stack([torch.from_numpy(st.v) for st in streams]).to(DEV, torch.bfloat16)
+    for st in range(0, T, 128):
+        layer.update(k[:, :, st : min(T, st + 128)], v[:, :, st : min(T, st + 128)])
+        layer.consolidate()
+    layer._append(k[:, :, T:], v[:, :, T:])
+    rng = np.random.default_rng(5)
+    q = torch.from_numpy(rng.standard_normal((2, H * G, q_len, D)).astype(np.float32)).to(DEV, torch.bfloat16)
+    kr, vr = layer._decode_peek()
+    out = layer.factored_chunk_attention(q, scaling=D ** -0.5)
+    for b in range(2):
+        ref = _dense_causal(q[b].float().cpu(), kr[b].float().cpu(), vr[b].float().cpu(), D ** -0.5)
+        got = out[b].float().cpu().numpy()
+        err = float(np.abs(got - ref).max() / np.abs(ref).max())
+        assert err < 2e-2, (b, err)
+    layer._group.check_status()
+
+
 def test_chunk_attention_refuses_unsupported_shape() -> None:
     """fp32 caches (or head_dim != 64, rank > 32) have no chunk kernel: the
     call fails loudly instead of computing something else."""
