@@ -80,6 +80,16 @@ struct SelectOut {
   int* order; long order_sp;               // [P][>= m] slot -> candidate (workspace)
 };
 
+// The ranking fused into the scoring launch: every CTA counts itself done
+// on done[p] (zero before the launch); the CTA that completes problem p's
+// scores ranks it and sets done[p] back to zero.  done == nullptr: scores
+// only.
+struct RankArgs {
+  int* done;
+  int keep_n, hh_neighbor;
+  SelectOut out;
+};
+
 }  // namespace kvd
 
 namespace kvd_host {
@@ -110,10 +120,12 @@ int launch_surprise_f32(int nb, int n, int m, int ld, const float* u, long u_sp,
 int launch_evict(int P, int W, int f_over, int retention, float* c_k, float* c_v, long c_sp, int ld,
                  const int* rk, const int* rv, int* mid_pos, float* mid_sur, long mid_sp,
                  int* keep_ws, long kw_sp, cudaStream_t stream);
+// `fuse` (optional): rank in the same launch where the fp64 scoring kernel
+// runs; *fused tells whether it did (the caller then skips launch_slash_select)
 template <typename T>
 int launch_slash_score(const CandSrc<T>& src, int P, int m, int H, int D, RopeArgs rope,
                        const float* u, long u_sp, int ld, const int* rr, float* scores, long sc_sp,
-                       cudaStream_t stream);
+                       cudaStream_t stream, const kvd::RankArgs* fuse = nullptr, bool* fused = nullptr);
 template <typename T>
 int launch_slash_select(const CandSrc<T>& src, int P, int m, int keep_n, int H, int D,
                         RopeArgs rope, const float* scores, long sc_sp, int hh_neighbor,

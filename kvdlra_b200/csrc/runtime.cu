@@ -152,6 +152,7 @@ struct Ws {
   int* dem;                      // [P]
   int* keep; long keep_sp;       // [P][w_cap]
   int* order;                    // [P][hh_budget + max_block] tier slot order
+  int* done;                     // [P] scoring CTAs finished (fused ranking), zero between launches
   char* step[2]; long step_sp;   // per problem
   size_t total;
 };
@@ -175,6 +176,7 @@ static Ws plan_ws(const kvd_config& c, char* base) {
   w.keep_sp = c.w_cap;
   w.keep = (int*)take(4ul * P * w.keep_sp);
   w.order = (int*)take(4ul * P * w.sc_sp);
+  w.done = (int*)take(4ul * P);
   w.step_sp = bug_step_ws_per_problem(n, mb, ld);
   w.step[0] = take((size_t)P * w.step_sp);
   w.step[1] = take((size_t)P * w.step_sp);
@@ -263,6 +265,7 @@ struct Group {
   CarryBatch pend_cb;          // the last absorb's carry, not yet launched
   int pend_par = -1;
   bool keep_pending = false;   // a tier copy on the side stream the next scoring must wait for
+  bool done_zeroed = false;    // w.done cleared for this call (the fused ranking keeps it zero)
 
   Group(const kvd_config& c_, const kvd_buffers& b_, kvd_counters& k_, char* ws, cudaStream_t s_)
       : c(c_), b(b_), k(k_), w(plan_ws(c_, ws)), s(s_) {
@@ -392,9 +395,6 @@ struct Group {
     src.g_k = (const T*)b.ring_k + (long)gslot * n; src.g_v = (const T*)b.ring_v + (long)gslot * n;
     src.g_sp = row_sp_ring;
     src.hh_len = k.hh_len; src.grad_start = grad_start; src.n = n;
-    int rc = launch_slash_score<T>(src, P, m, c.num_heads, c.head_dim, rope, b.u_k[k.u_sel], u_sp,
-                                   ld, b.r_k, w.scores, w.sc_sp, s);
-    if (rc) return rc;
     if (d > 0 && k.w_len + d > c.w_cap) {
       set_error("coordinate capacity %d too small (need %d)", c.w_cap, k.w_len + d);
       return KVD_ERR_ARG;
@@ -406,9 +406,24 @@ struct Group {
     so.mid_pos = b.mid_pos; so.mid_surprise = track_surprise() ? b.mid_surprise : nullptr;
     so.mid_sp = c.w_cap; so.w_off = k.w_len; so.dem_count = w.dem;
     so.order = w.order; so.order_sp = w.sc_sp;
-    rc = launch_slash_select<T>(src, P, m, keep_n, c.num_heads, c.head_dim, rope, w.scores, w.sc_sp,
-                                c.hh_neighbor, so, s);
+    // scoring and ranking in one launch where the fp64 scoring kernel runs
+    if (!done_zeroed) {
+      if (cudaMemsetAsync(w.done, 0, 4ul * P, s) != cudaSuccess) {
+        set_error("clearing the ranking counters failed");
+        return KVD_ERR_CUDA;
+      }
+      done_zeroed = true;
+    }
+    RankArgs ra{w.done, keep_n, c.hh_neighbor, so};
+    bool fused = false;
+    int rc = launch_slash_score<T>(src, P, m, c.num_heads, c.head_dim, rope, b.u_k[k.u_sel], u_sp,
+                                   ld, b.r_k, w.scores, w.sc_sp, s, &ra, &fused);
     if (rc) return rc;
+    if (!fused) {
+      rc = launch_slash_select<T>(src, P, m, keep_n, c.num_heads, c.head_dim, rope, w.scores, w.sc_sp,
+                                  c.hh_neighbor, so, s);
+      if (rc) return rc;
+    }
     // the kept tokens move into the other tier buffer beside the BUG step
     if (cs) {
       cudaEventRecord(cs->ranked, s);

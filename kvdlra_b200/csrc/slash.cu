@@ -132,10 +132,15 @@ __device__ __forceinline__ void cp_async_wait_all() {
 // aligned (checked by the launcher): the basis and the candidates' raw rows
 // are copied with cp.async, all in flight at once, then un-rotated in place.
 template <typename T>
+__device__ __noinline__ void rank_problem(const CandSrc<T>& src, int p, int m, int keep_n, int H, int D,
+                                          const RopeArgs& rope, const float* scores, long sc_sp,
+                                          int hh_neighbor, const SelectOut& out, float* sel_sm);
+
+template <typename T>
 __global__ void __launch_bounds__(kScThreads) slash_score_dmma_kernel(CandSrc<T> src, int m, int H, int D,
                                                                RopeArgs rope, const float* u,
                                                                long u_sp, int ld, const int* rr,
-                                                               float* scores, long sc_sp) {
+                                                               float* scores, long sc_sp, RankArgs rk) {
   extern __shared__ __align__(16) double dsm[];
   const int p = blockIdx.y;
   const int j0 = blockIdx.x * kScT;
@@ -250,6 +255,19 @@ __global__ void __launch_bounds__(kScThreads) slash_score_dmma_kernel(CandSrc<T>
       scores[p * sc_sp + j] = out;
     }
   }
+  if (rk.done) {
+    __shared__ int s_last;
+    __threadfence();  // this CTA's scores are visible before it counts itself done
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(rk.done + p, 1) == (int)gridDim.x - 1;
+    __syncthreads();
+    if (s_last) {
+      __threadfence();
+      if (tid == 0) rk.done[p] = 0;  // ready for the next launch
+      rank_problem<T>(src, p, m, rk.keep_n, H, D, rope, scores, sc_sp, rk.hh_neighbor, rk.out,
+                      reinterpret_cast<float*>(dsm));
+    }
+  }
 }
 
 // The 16/sizeof(T) elements of one 16-byte chunk, widened to fp32 (dst 16-byte aligned).
@@ -277,21 +295,22 @@ template <> __device__ __forceinline__ void widen16<__nv_bfloat16>(uint4 r, floa
 // all the BUG step needs -- are gathered here (one warp per row: key
 // un-rotated into the fp32 block with cos/sin once per frequency, value
 // widened).  The kept rows move in slash_keep_kernel, off the critical path.
+// The ranking of problem p by the whole CTA (any block size), in `sel_sm`
+// (16 m bytes of shared memory).  Scores are read from L2: another CTA of
+// the same launch may have written them (slash_score_dmma_kernel's fused
+// form).
 template <typename T>
-__global__ void __launch_bounds__(512) slash_rank_kernel(CandSrc<T> src, int m, int keep_n, int H,
-                                                         int D, RopeArgs rope,
-                                                         const float* scores, long sc_sp,
-                                                         int hh_neighbor, SelectOut out) {
-  extern __shared__ __align__(16) float sel_sm[];
+__device__ __noinline__ void rank_problem(const CandSrc<T>& src, int p, int m, int keep_n, int H, int D,
+                                          const RopeArgs& rope, const float* scores, long sc_sp,
+                                          int hh_neighbor, const SelectOut& out, float* sel_sm) {
   __shared__ int scan_scratch[32];
-  const int p = blockIdx.x;
   float* raw = sel_sm;            // [m]
   float* sel = raw + m;           // [m]
   int* pos = reinterpret_cast<int*>(sel + m);  // [m]
   int* ords = pos + m;                         // [m] the slot order, shared copy
   int* order = out.order + p * out.order_sp;
   for (int i = threadIdx.x; i < m; i += blockDim.x) {
-    raw[i] = scores[p * sc_sp + i];
+    raw[i] = __ldcg(scores + p * sc_sp + i);
     pos[i] = src.pos(p, i);
   }
   __syncthreads();
@@ -394,6 +413,15 @@ __global__ void __launch_bounds__(512) slash_rank_kernel(CandSrc<T> src, int m, 
       for (int i = lane; i < n; i += 32) xv[i] = load_f<T>(vss + i);
     }
   }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(512) slash_rank_kernel(CandSrc<T> src, int m, int keep_n, int H,
+                                                         int D, RopeArgs rope,
+                                                         const float* scores, long sc_sp,
+                                                         int hh_neighbor, SelectOut out) {
+  extern __shared__ __align__(16) float sel_sm[];
+  rank_problem<T>(src, blockIdx.x, m, keep_n, H, D, rope, scores, sc_sp, hh_neighbor, out, sel_sm);
 }
 
 constexpr int kMoveWarps = 8;   // rows per CTA of slash_keep_kernel (one warp each)
@@ -571,7 +599,8 @@ using namespace kvd;
 template <typename T>
 int launch_slash_score(const CandSrc<T>& src, int P, int m, int H, int D, RopeArgs rope,
                        const float* u, long u_sp, int ld, const int* rr, float* scores, long sc_sp,
-                       cudaStream_t stream) {
+                       cudaStream_t stream, const RankArgs* fuse, bool* fused) {
+  if (fused) *fused = false;
   if (m <= 0) return KVD_OK;
   if (ld > 8 * kScoreMaxQ) {
     set_error("slash score: rank %d exceeds %d", ld, 8 * kScoreMaxQ);
@@ -588,13 +617,18 @@ int launch_slash_score(const CandSrc<T>& src, int P, int m, int H, int D, RopeAr
                   (src.hh_len == 0 || reinterpret_cast<uintptr_t>(src.hh_k) % 16 == 0) &&
                   (src.hh_sp * (long)sizeof(T)) % 16 == 0 && (src.g_sp * (long)sizeof(T)) % 16 == 0;
   if (ld <= 32 && D % 8 == 0 && n % 16 == 0 && al && dsmem_l <= 200 * 1024) {
+    // the fused ranking reuses the kernel's shared memory (16 m bytes)
+    const bool fuse_ok = fuse && fuse->done && 16L * m <= dsmem_l && fuse->out.order_sp >= m;
+    RankArgs rk{};
+    if (fuse_ok) rk = *fuse;
     const int dsmem = (int)dsmem_l;
     if (int rc = ensure_smem((const void*)slash_score_dmma_kernel<T>, dsmem, "slash_score_kernel")) return rc;
     {
       KTimerScope kts_("slash_score_kernel", stream);
       slash_score_dmma_kernel<T><<<dim3((m + kScT - 1) / kScT, P), kScThreads, dsmem, stream>>>(
-          src, m, H, D, rope, u, u_sp, ld, rr, scores, sc_sp);
+          src, m, H, D, rope, u, u_sp, ld, rr, scores, sc_sp, rk);
     }
+    if (fused) *fused = fuse_ok;
     return check_launch("slash_score_kernel");
   }
   const int smem = 4 * (kScoreTile * half * 2 + kScoreTile * D + D * ld);
@@ -687,7 +721,7 @@ int launch_evict(int P, int W, int f_over, int retention, float* c_k, float* c_v
 #define KVD_INST(T)                                                                              \
   template int launch_slash_score<T>(const CandSrc<T>&, int, int, int, int, RopeArgs,            \
                                      const float*, long, int, const int*, float*, long,          \
-                                     cudaStream_t);                                              \
+                                     cudaStream_t, const RankArgs*, bool*);                      \
   template int launch_slash_select<T>(const CandSrc<T>&, int, int, int, int, int, RopeArgs,      \
                                       const float*, long, int, const SelectOut&, cudaStream_t);  \
   template int launch_slash_keep<T>(const CandSrc<T>&, int, int, int, const SelectOut&,          \
