@@ -8,6 +8,8 @@
 //    top-h (810-812): the slot order of kept and demoted candidates, their
 //    positions and graduation surprise, and the gather of the demoted ones
 //    (un-rotated K, fp32 V) into the BUG-step block (813-825 + 871-888).
+//    The same ranking runs inside slash_score_dmma_kernel's launch (the
+//    last scoring CTA of each problem) where that kernel applies.
 //  * slash_keep_kernel    -- compaction of the kept tokens into the other
 //    exact-tier buffer, one warp per row over the whole GPU.
 //  * gather_block_kernel  -- the no-tier absorb path (743-750).
@@ -128,14 +130,15 @@ __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;\n" ::: "memory");
 }
 
-// Requires rows of n*sizeof(T) and of ld floats in 16-byte multiples, 16-byte
-// aligned (checked by the launcher): the basis and the candidates' raw rows
-// are copied with cp.async, all in flight at once, then un-rotated in place.
 template <typename T>
 __device__ __noinline__ void rank_problem(const CandSrc<T>& src, int p, int m, int keep_n, int H, int D,
                                           const RopeArgs& rope, const float* scores, long sc_sp,
                                           int hh_neighbor, const SelectOut& out, float* sel_sm);
 
+// Requires rows of n*sizeof(T) and of ld floats in 16-byte multiples, 16-byte
+// aligned (checked by the launcher): the basis and the candidates' raw rows
+// are copied with cp.async, all in flight at once, then un-rotated in place.
+// With rk.done, the CTA that completes a problem's scores also ranks it.
 template <typename T>
 __global__ void __launch_bounds__(kScThreads) slash_score_dmma_kernel(CandSrc<T> src, int m, int H, int D,
                                                                RopeArgs rope, const float* u,
