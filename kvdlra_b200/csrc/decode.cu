@@ -1194,8 +1194,8 @@ __host__ __device__ inline DuSmem du_smem(int n, int Hq, int D) {
   m.ck = m.us + n * kDuK * 4;                 // 2 x [128][32] key coordinates, core-matrix layout
   m.cv = m.ck + 2 * kDuTok * kDuK * 4;        // 2 x [128][ldv] value coordinates
   m.qs = m.cv + 2 * kDuTok * m.ldv * 4;       // [Hq][D] queries
-  m.cs = m.qs + Hq * D * 4;                   // [D/2 frequencies][128 tokens] (cos, sin)
-  m.ps = m.cs + (D / 2) * kDuTok * 8;         // [Hq][128] scores, then probabilities
+  m.cs = m.qs + Hq * D * 4;                   // [128 tokens][D/2 + 4] cos, then the same for sin
+  m.ps = m.cs + 2 * kDuTok * (D / 2 + 4) * 4; // [Hq][128] scores, then probabilities
   m.st = m.ps + Hq * kDuTok * 4;              // [Hq][4]: running max, correction
   m.vred = m.st + Hq * 16;                    // [256][4] value-product halves
   m.posb = m.vred + 256 * 16;                 // 2 x [128] positions
@@ -1232,7 +1232,11 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_umma_kernel(DecArgs a, 
   const DuSmem L = du_smem(n, Hq, D);
   unsigned char* us = dsm4 + L.us;
   float* qs = reinterpret_cast<float*>(dsm4 + L.qs);
-  float2* cs = reinterpret_cast<float2*>(dsm4 + L.cs);
+  // rotary tables, a row of HALF + 4 floats per token (16-byte rows, the
+  // 16-byte loads of eight consecutive tokens on distinct banks)
+  constexpr int CSP = HALF + 4;
+  float* cos_t = reinterpret_cast<float*>(dsm4 + L.cs);
+  float* sin_t = cos_t + kDuTok * CSP;
   float* ps = reinterpret_cast<float*>(dsm4 + L.ps);
   float* st = reinterpret_cast<float*>(dsm4 + L.st);
   float* vred = reinterpret_cast<float*>(dsm4 + L.vred);
@@ -1333,7 +1337,8 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_umma_kernel(DecArgs a, 
       for (int f = tid / kDuTok; f < HALF; f += kDuThreads / kDuTok) {
         float c = 1.f, sn = 0.f;
         if (live) rope_cs_fast(pos, a.inv_freq[f], a.rope_scale, &c, &sn);
-        cs[f * kDuTok + t] = make_float2(c, sn);
+        cos_t[t * CSP + f] = c;
+        sin_t[t * CSP + f] = sn;
       }
     }
     __syncthreads();
@@ -1343,37 +1348,48 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_umma_kernel(DecArgs a, 
     if (ok_wait) {
       const uint32_t trow = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
       const int g_lo = gq * gper, g_hi = min(H, g_lo + gper);
+      const float4* cos4 = reinterpret_cast<const float4*>(cos_t + tok * CSP);
+      const float4* sin4 = reinterpret_cast<const float4*>(sin_t + tok * CSP);
       for (int g = g_lo; g < g_hi; ++g) {
-        float s1[kMaxG], s2[kMaxG];
+        // packed fp32 pairs over consecutive frequencies (sm_100 FFMA2): per
+        // head the score's two halves, each as an (even, odd) frequency pair
+        float2 s1[kMaxG], s2[kMaxG];
 #pragma unroll
-        for (int qh = 0; qh < kMaxG; ++qh) { s1[qh] = 0.f; s2[qh] = 0.f; }
+        for (int qh = 0; qh < kMaxG; ++qh) { s1[qh] = make_float2(0.f, 0.f); s2[qh] = s1[qh]; }
 #pragma unroll
         for (int f0 = 0; f0 < HALF; f0 += 16) {
           float x1[16], x2[16];
           umma::tmem_ld16(trow + g * D + f0, x1);
           umma::tmem_ld16(trow + g * D + HALF + f0, x2);
           umma::tmem_wait_ld();
+          float2 y1[8], y2[8];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float2 c = cs[(f0 + i) * kDuTok + tok];
-            float y1, y2;
-            rope_apply_pair(x1[i], x2[i], c.x, c.y, &y1, &y2);
-            x1[i] = y1;
-            x2[i] = y2;
+          for (int i4 = 0; i4 < 4; ++i4) {  // RoPE: y1 = x1 c - x2 s, y2 = x2 c + x1 s
+            const float4 c4 = cos4[(f0 >> 2) + i4], s4 = sin4[(f0 >> 2) + i4];
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2) {
+              const int i = 4 * i4 + 2 * h2;
+              const float2 X1 = make_float2(x1[i], x1[i + 1]), X2 = make_float2(x2[i], x2[i + 1]);
+              const float2 C = h2 ? make_float2(c4.z, c4.w) : make_float2(c4.x, c4.y);
+              const float2 S = h2 ? make_float2(s4.z, s4.w) : make_float2(s4.x, s4.y);
+              const float2 t1 = __fmul2_rn(X2, S), t2 = __fmul2_rn(X1, S);
+              y1[2 * i4 + h2] = __ffma2_rn(X1, C, make_float2(-t1.x, -t1.y));
+              y2[2 * i4 + h2] = __ffma2_rn(X2, C, t2);
+            }
           }
 #pragma unroll
           for (int qh = 0; qh < kMaxG; ++qh) {
             if (qh < G) {
               const float4* qa = qs4 + (g * G + qh) * (D / 4) + f0 / 4;
               const float4* qb = qa + HALF / 4;
-              float u1 = s1[qh], u2 = s2[qh];
+              float2 u1 = s1[qh], u2 = s2[qh];
 #pragma unroll
               for (int i = 0; i < 4; ++i) {
                 const float4 u = qa[i], w = qb[i];
-                u1 = fmaf(x1[4 * i], u.x, u1); u2 = fmaf(x2[4 * i], w.x, u2);
-                u1 = fmaf(x1[4 * i + 1], u.y, u1); u2 = fmaf(x2[4 * i + 1], w.y, u2);
-                u1 = fmaf(x1[4 * i + 2], u.z, u1); u2 = fmaf(x2[4 * i + 2], w.z, u2);
-                u1 = fmaf(x1[4 * i + 3], u.w, u1); u2 = fmaf(x2[4 * i + 3], w.w, u2);
+                u1 = __ffma2_rn(y1[2 * i], make_float2(u.x, u.y), u1);
+                u2 = __ffma2_rn(y2[2 * i], make_float2(w.x, w.y), u2);
+                u1 = __ffma2_rn(y1[2 * i + 1], make_float2(u.z, u.w), u1);
+                u2 = __ffma2_rn(y2[2 * i + 1], make_float2(w.z, w.w), u2);
               }
               s1[qh] = u1;
               s2[qh] = u2;
@@ -1383,7 +1399,8 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_umma_kernel(DecArgs a, 
 #pragma unroll
         for (int qh = 0; qh < kMaxG; ++qh)
           if (qh < G)
-            ps[(g * G + qh) * kDuTok + tok] = tok < ntok ? (s1[qh] + s2[qh]) * a.scaling : -INFINITY;
+            ps[(g * G + qh) * kDuTok + tok] =
+                tok < ntok ? ((s1[qh].x + s1[qh].y) + (s2[qh].x + s2[qh].y)) * a.scaling : -INFINITY;
       }
     }
     umma::fence_before_sync();
