@@ -909,7 +909,9 @@ static __device__ __forceinline__ void cta_basis_rows32(int n, int keep, int r, 
 // pitch 16-byte aligned): a thread owns a 4-row x 8-column tile, so one
 // 16-byte load of a coefficient row serves four rows instead of one.  Each
 // output keeps the operation order of the row-per-thread forms above (the
-// same fmaf chains over k), so the results are the same bit for bit.
+// same fmaf chains over k), so the results are the same bit for bit; the
+// fmas of two adjacent columns issue as one packed pair (sm_100 FFMA2, each
+// lane a round-to-nearest fma).
 
 // Un[i][c] = sum_{k<r} Un[i][k] WU[k][c] + sum_{j<m} Q[j][i] WU[r+j][c], c < keep,
 // in place: a row's old values are read only by the four lanes that own its
@@ -923,19 +925,22 @@ static __device__ __forceinline__ void cta_basis_tiles(int n, int keep, int r, i
     const int rg = rg0 + tid / 4;
     const bool live = rg < ngr;
     const int i0 = live ? 4 * rg : 0;
-    float acc[4][8];
+    float2 acc[4][4];  // columns (2c, 2c + 1) as packed pairs
 #pragma unroll
     for (int q = 0; q < 4; ++q)
 #pragma unroll
-      for (int c = 0; c < 8; ++c) acc[q][c] = 0.f;
+      for (int c = 0; c < 4; ++c) acc[q][c] = make_float2(0.f, 0.f);
     auto step = [&](int k, const float (&av)[4]) {  // acc += av (x) WU[k][8cg..8cg+8)
       const float4 w0 = *reinterpret_cast<const float4*>(WU + k * ldw + 8 * cg);
       const float4 w1 = *reinterpret_cast<const float4*>(WU + k * ldw + 8 * cg + 4);
-      const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      const float2 w[4] = {make_float2(w0.x, w0.y), make_float2(w0.z, w0.w), make_float2(w1.x, w1.y),
+                           make_float2(w1.z, w1.w)};
 #pragma unroll
-      for (int q = 0; q < 4; ++q)
+      for (int q = 0; q < 4; ++q) {
+        const float2 a2 = make_float2(av[q], av[q]);
 #pragma unroll
-        for (int c = 0; c < 8; ++c) acc[q][c] = fmaf(av[q], w[c], acc[q][c]);
+        for (int c = 0; c < 4; ++c) acc[q][c] = __ffma2_rn(a2, w[c], acc[q][c]);
+      }
     };
     int k = 0;
     for (; k + 4 <= r; k += 4) {  // U's columns four at a time
@@ -968,7 +973,7 @@ static __device__ __forceinline__ void cta_basis_tiles(int n, int keep, int r, i
       for (int q = 0; q < 4; ++q)
 #pragma unroll
         for (int c = 0; c < 8; ++c)
-          if (8 * cg + c < keep) Un[(i0 + q) * ldn + 8 * cg + c] = acc[q][c];
+          if (8 * cg + c < keep) Un[(i0 + q) * ldn + 8 * cg + c] = (c & 1) ? acc[q][c >> 1].y : acc[q][c >> 1].x;
     }
     __syncwarp();
   }
@@ -991,24 +996,28 @@ static __device__ __forceinline__ void cta_tn_tiles(int M, int NB, int K, const 
       const int c = it & 3, a = (it >> 2) & 7, sl = it >> 5;
       if (4 * a >= M || j0 + 4 * c >= NB) continue;
       const int i0 = sl * slice, i1 = min(K, i0 + slice);
-      float acc[4][4];
+      float2 acc[4][2];  // columns (2y, 2y + 1) as packed pairs
 #pragma unroll
       for (int x = 0; x < 4; ++x)
 #pragma unroll
-        for (int y = 0; y < 4; ++y) acc[x][y] = 0.f;
+        for (int y = 0; y < 2; ++y) acc[x][y] = make_float2(0.f, 0.f);
       for (int i = i0; i < i1; ++i) {
         const float4 ua = *reinterpret_cast<const float4*>(A + i * lda + 4 * a);
         const float4 uc = *reinterpret_cast<const float4*>(B + i * ldb + j0 + 4 * c);
-        const float va[4] = {ua.x, ua.y, ua.z, ua.w}, vc[4] = {uc.x, uc.y, uc.z, uc.w};
+        const float va[4] = {ua.x, ua.y, ua.z, ua.w};
+        const float2 vc[2] = {make_float2(uc.x, uc.y), make_float2(uc.z, uc.w)};
 #pragma unroll
-        for (int x = 0; x < 4; ++x)
+        for (int x = 0; x < 4; ++x) {
+          const float2 a2 = make_float2(va[x], va[x]);
 #pragma unroll
-          for (int y = 0; y < 4; ++y) acc[x][y] = fmaf(va[x], vc[y], acc[x][y]);
+          for (int y = 0; y < 2; ++y) acc[x][y] = __ffma2_rn(a2, vc[y], acc[x][y]);
+        }
       }
 #pragma unroll
       for (int x = 0; x < 4; ++x)
 #pragma unroll
-        for (int y = 0; y < 4; ++y) part[(sl * 16 + 4 * c + y) * 32 + 4 * a + x] = acc[x][y];
+        for (int y = 0; y < 4; ++y)
+          part[(sl * 16 + 4 * c + y) * 32 + 4 * a + x] = (y & 1) ? acc[x][y >> 1].y : acc[x][y >> 1].x;
     }
     __syncthreads();
     for (int e = tid; e < 16 * 32; e += nthr) {
@@ -1034,25 +1043,29 @@ static __device__ __forceinline__ void cta_rows_sub_tiles(int n, int b, int K, c
   const int ngr = n / 4;
   for (int it = tid; it < ngr * 4; it += nthr) {
     const int j0 = 4 * (it / ngr), rb = it % ngr;
-    float acc[4][4];
+    float2 acc[4][2];  // columns (2y, 2y + 1) as packed pairs
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const int i = rb + q * ngr;
       if (from_xr) {
         const float4 t = *reinterpret_cast<const float4*>(XR + i * ldb + j0);
-        acc[q][0] = t.x; acc[q][1] = t.y; acc[q][2] = t.z; acc[q][3] = t.w;
+        acc[q][0] = make_float2(t.x, t.y); acc[q][1] = make_float2(t.z, t.w);
       } else {
+        float v[4];
 #pragma unroll
-        for (int y = 0; y < 4; ++y) acc[q][y] = j0 + y < b ? Rm[(j0 + y) * ldr + i] : 0.f;
+        for (int y = 0; y < 4; ++y) v[y] = j0 + y < b ? Rm[(j0 + y) * ldr + i] : 0.f;
+        acc[q][0] = make_float2(v[0], v[1]); acc[q][1] = make_float2(v[2], v[3]);
       }
     }
-    auto step = [&](int k, const float (&av)[4]) {
+    auto step = [&](int k, const float (&av)[4]) {  // packed pairs of columns (sm_100 FFMA2)
       const float4 c4 = *reinterpret_cast<const float4*>(C + k * ldc + j0);
-      const float cv[4] = {c4.x, c4.y, c4.z, c4.w};
+      const float2 cv[2] = {make_float2(c4.x, c4.y), make_float2(c4.z, c4.w)};
 #pragma unroll
-      for (int q = 0; q < 4; ++q)
+      for (int q = 0; q < 4; ++q) {
+        const float2 a2 = make_float2(-av[q], -av[q]);
 #pragma unroll
-        for (int y = 0; y < 4; ++y) acc[q][y] = fmaf(-av[q], cv[y], acc[q][y]);
+        for (int y = 0; y < 2; ++y) acc[q][y] = __ffma2_rn(a2, cv[y], acc[q][y]);
+      }
     };
     int k = 0;
     for (; k + 4 <= K; k += 4) {
@@ -1077,12 +1090,11 @@ static __device__ __forceinline__ void cta_rows_sub_tiles(int n, int b, int K, c
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const int i = rb + q * ngr;
+      const float v[4] = {acc[q][0].x, acc[q][0].y, acc[q][1].x, acc[q][1].y};
 #pragma unroll
       for (int y = 0; y < 4; ++y)
-        if (j0 + y < b) Rm[(j0 + y) * ldr + i] = acc[q][y];
-      if (to_xr)
-        *reinterpret_cast<float4*>(XR + i * ldb + j0) =
-            make_float4(acc[q][0], acc[q][1], acc[q][2], acc[q][3]);
+        if (j0 + y < b) Rm[(j0 + y) * ldr + i] = v[y];
+      if (to_xr) *reinterpret_cast<float4*>(XR + i * ldb + j0) = make_float4(v[0], v[1], v[2], v[3]);
     }
   }
   __syncthreads();
@@ -1097,14 +1109,17 @@ static __device__ __forceinline__ void cta_polish_tiles(int n, int keep, const f
   const int ngr = n / 4;
   for (int rg = tid / 4; rg < ngr; rg += nthr / 4) {
     const int i0 = 4 * rg;
-    float acc[4][8];
+    float2 acc[4][4];  // columns (2c, 2c + 1) as packed pairs
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
       const float4 t0 = *reinterpret_cast<const float4*>(S + (i0 + q) * lds + 8 * cg);
       const float4 t1 = *reinterpret_cast<const float4*>(S + (i0 + q) * lds + 8 * cg + 4);
       const float t[8] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w};
+      float v[8];
 #pragma unroll
-      for (int c = 0; c < 8; ++c) acc[q][c] = 8 * cg + c < keep ? t[c] : 0.f;
+      for (int c = 0; c < 8; ++c) v[c] = 8 * cg + c < keep ? t[c] : 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[q][c] = make_float2(v[2 * c], v[2 * c + 1]);
     }
     for (int k0 = 0; k0 < keep; k0 += 4) {  // (columns past keep are read, not used)
       float h4[4][4];
@@ -1123,8 +1138,10 @@ static __device__ __forceinline__ void cta_polish_tiles(int n, int keep, const f
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             const float h = -0.5f * h4[q][kk];
+            const float2 h2 = make_float2(h, h);
 #pragma unroll
-            for (int c = 0; c < 8; ++c) acc[q][c] = fmaf(h, ev[c], acc[q][c]);
+            for (int c = 0; c < 4; ++c)  // packed pairs of columns (sm_100 FFMA2)
+              acc[q][c] = __ffma2_rn(h2, make_float2(ev[2 * c], ev[2 * c + 1]), acc[q][c]);
           }
         }
       }
@@ -1133,12 +1150,12 @@ static __device__ __forceinline__ void cta_polish_tiles(int n, int keep, const f
     for (int q = 0; q < 4; ++q) {
       float* dst = Uo + (long)(i0 + q) * ld + 8 * cg;
       if (uvec && 8 * cg + 8 <= keep) {
-        *reinterpret_cast<float4*>(dst) = make_float4(acc[q][0], acc[q][1], acc[q][2], acc[q][3]);
-        *reinterpret_cast<float4*>(dst + 4) = make_float4(acc[q][4], acc[q][5], acc[q][6], acc[q][7]);
+        *reinterpret_cast<float4*>(dst) = make_float4(acc[q][0].x, acc[q][0].y, acc[q][1].x, acc[q][1].y);
+        *reinterpret_cast<float4*>(dst + 4) = make_float4(acc[q][2].x, acc[q][2].y, acc[q][3].x, acc[q][3].y);
       } else {
 #pragma unroll
         for (int c = 0; c < 8; ++c)
-          if (8 * cg + c < keep) dst[c] = acc[q][c];
+          if (8 * cg + c < keep) dst[c] = (c & 1) ? acc[q][c >> 1].y : acc[q][c >> 1].x;
       }
     }
   }
