@@ -531,21 +531,21 @@ static __device__ __noinline__ int cta_block_hestenes(float* X, int len, int vof
     }
     const int nr = k == 0 ? 2 * P - 1 : P;
     for (int rd = 0; rd < nr; ++rd) {
-      // the pair's Gram over the data rows: two accumulator sets halve the chains
-      float al0 = 0.f, be0 = 0.f, ga0 = 0.f, al1 = 0.f, be1 = 0.f, ga1 = 0.f;
+      // the pair's Gram over the data rows, as packed fp32 pairs (sm_100
+      // FFMA2): (x, y) and (z, w) of every unit in two accumulator pairs
+      float2 al2 = make_float2(0.f, 0.f), be2 = al2, ga2 = al2;
 #pragma unroll
       for (int t = 0; t < NUD; ++t) {
         const bool d = gl + G * t < nud;
         const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
         const float4 a = d ? tp[t] : z, b = d ? bt[t] : z;
-        float& al = (t & 1) ? al1 : al0;
-        float& be = (t & 1) ? be1 : be0;
-        float& ga = (t & 1) ? ga1 : ga0;
-        al = fmaf(a.x, a.x, al); al = fmaf(a.y, a.y, al); al = fmaf(a.z, a.z, al); al = fmaf(a.w, a.w, al);
-        be = fmaf(b.x, b.x, be); be = fmaf(b.y, b.y, be); be = fmaf(b.z, b.z, be); be = fmaf(b.w, b.w, be);
-        ga = fmaf(a.x, b.x, ga); ga = fmaf(a.y, b.y, ga); ga = fmaf(a.z, b.z, ga); ga = fmaf(a.w, b.w, ga);
+        const float2 a01 = make_float2(a.x, a.y), a23 = make_float2(a.z, a.w);
+        const float2 b01 = make_float2(b.x, b.y), b23 = make_float2(b.z, b.w);
+        al2 = __ffma2_rn(a01, a01, al2); al2 = __ffma2_rn(a23, a23, al2);
+        be2 = __ffma2_rn(b01, b01, be2); be2 = __ffma2_rn(b23, b23, be2);
+        ga2 = __ffma2_rn(a01, b01, ga2); ga2 = __ffma2_rn(a23, b23, ga2);
       }
-      float al = al0 + al1, be = be0 + be1, ga = ga0 + ga1;
+      float al = al2.x + al2.y, be = be2.x + be2.y, ga = ga2.x + ga2.y;
 #pragma unroll
       for (int o = G / 2; o > 0; o >>= 1) {
         al += __shfl_xor_sync(kAll, al, o);
@@ -562,11 +562,19 @@ static __device__ __noinline__ int cta_block_hestenes(float* X, int len, int vof
         float c, s;
         jacobi_rotation(swp ? al - be : be - al, 2.f * ga, c, s);
         if (swp) s = -s;
+        // top' = c a - s b, bottom' = s a + c b, on packed pairs
+        const float2 c2 = make_float2(c, c), s2 = make_float2(s, s), ns2 = make_float2(-s, -s);
 #pragma unroll
         for (int t = 0; t < NU; ++t) {
           const float4 a = tp[t], b = bt[t];
-          tp[t] = make_float4(c * a.x - s * b.x, c * a.y - s * b.y, c * a.z - s * b.z, c * a.w - s * b.w);
-          bt[t] = make_float4(s * a.x + c * b.x, s * a.y + c * b.y, s * a.z + c * b.z, s * a.w + c * b.w);
+          const float2 a01 = make_float2(a.x, a.y), a23 = make_float2(a.z, a.w);
+          const float2 b01 = make_float2(b.x, b.y), b23 = make_float2(b.z, b.w);
+          const float2 t01 = __ffma2_rn(c2, a01, __fmul2_rn(ns2, b01));
+          const float2 t23 = __ffma2_rn(c2, a23, __fmul2_rn(ns2, b23));
+          const float2 u01 = __ffma2_rn(s2, a01, __fmul2_rn(c2, b01));
+          const float2 u23 = __ffma2_rn(s2, a23, __fmul2_rn(c2, b23));
+          tp[t] = make_float4(t01.x, t01.y, t23.x, t23.y);
+          bt[t] = make_float4(u01.x, u01.y, u23.x, u23.y);
         }
         big = big || ga * ga > kJacobiQuadStop * kJacobiQuadStop * al * be;
       }
