@@ -78,3 +78,49 @@ def test_mode_context_managers_restore_normal() -> None:
             assert all(ly._mode == "score" for ly in cache.layers)
             raise KeyError("x")
     assert all(ly._mode == "normal" for ly in cache.layers)
+
+
+def test_factored_attention_routing_without_gpu() -> None:
+    """transformers' attention call (attention.py): an untagged key goes to
+    SDPA; a tagged key goes to the chunk kernel in ingest (no tail) and score
+    (the step's own K/V as tail) modes and to the factored decode otherwise,
+    with the output in transformers' (B, q, Hq, D) layout.  The layer is a
+    stand-in that records the calls (nothing runs on a GPU)."""
+    from kvdlra_b200 import attention as A
+
+    calls = []
+
+    class FakeLayer:
+        def __init__(self, mode):
+            self._mode = mode
+
+        def factored_chunk_attention(self, query, scaling=None, tail=None):
+            calls.append(("chunk", self._mode, tail is not None, tuple(query.shape)))
+            b, hq, q, d = query.shape
+            return torch.zeros(b, q, hq, d)
+
+        def factored_attention(self, query, scaling=None):
+            calls.append(("decode", self._mode, False, tuple(query.shape)))
+            return torch.zeros(query.shape)
+
+    module = torch.nn.Module()
+    module.num_key_value_groups, module.is_causal = 2, True
+    q = torch.zeros(1, 4, 5, 8)
+    k = torch.zeros(1, 2, 5, 8)
+    v = torch.zeros(1, 2, 5, 8)
+    out, _ = A.factored_attention_forward(module, q, k, v, None)  # untagged: SDPA
+    assert tuple(out.shape) == (1, 5, 4, 8) and not calls
+    for mode, expect_tail in (("ingest", False), ("score", True)):
+        kk = A.tag_step(k.clone(), FakeLayer(mode))
+        out, w = A.factored_attention_forward(module, q, kk, v, None, scaling=0.5)
+        assert w is None and tuple(out.shape) == (1, 5, 4, 8)
+        assert calls[-1] == ("chunk", mode, expect_tail, (1, 4, 5, 8))
+    q1 = torch.zeros(1, 4, 1, 8)
+    kd = A.tag_step(torch.zeros(1, 2, 1, 8), FakeLayer("normal"))
+    out, _ = A.factored_attention_forward(module, q1, kd, torch.zeros(1, 2, 1, 8), None)
+    assert tuple(out.shape) == (1, 1, 4, 8) and calls[-1][0] == "decode"
+    with pytest.raises(RuntimeError, match="one query token"):
+        A.factored_attention_forward(module, q, A.tag_step(k.clone(), FakeLayer("normal")), v, None)
+    with pytest.raises(NotImplementedError, match="dropout"):
+        A.factored_attention_forward(module, q, A.tag_step(k.clone(), FakeLayer("ingest")), v, None,
+                                     dropout=0.1)
