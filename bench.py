@@ -58,6 +58,14 @@ WORKLOADS = {
         config_tokens=131072, chunk=2048, rank=128, hh=1024, sinks=4, ring=256, absorb=16,
         prefill_block=128, decode=64, theta=500000.0, batch=8, seed_warmup=False,
         needles=dict(n_needles=16)),
+    # the whole-box configuration's single sequence with its 8 KV heads split
+    # over the GPUs (run at a reduced length; ``bench.py --workload
+    # head-sharded``)
+    "head-sharded-kv": dict(
+        name="head-sharded-kv", layers=32, kv_heads=8, head_dim=128, q_heads=32, tokens=8192,
+        config_tokens=131072, chunk=2048, rank=128, hh=1024, sinks=4, ring=256, absorb=16,
+        prefill_block=128, decode=64, theta=500000.0, batch=1, seed_warmup=False,
+        needles=dict(n_needles=16)),
 }
 WORKLOAD = WORKLOADS["llama-3.2-1b-kv"]
 METRIC = "BUG ingest tokens/s + factored-decode tokens/s at 1/2/4/8 B200; % HBM roofline"
@@ -800,6 +808,109 @@ def run_reference_decode(args) -> None:
         "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
 
 
+def run_head_sharded(args, w: dict) -> None:
+    """One sequence with its KV heads split over the ranks (the whole-box
+    configuration's single-sequence mode).  The basis is joint over heads, so
+    every rank ingests the whole sequence into the whole cache (the same
+    kernels on the same inputs: identical caches); each rank answers the
+    decode attention of its own KV heads' query heads
+    (``kvd_factored_decode_heads``) and the per-head outputs of every layer
+    are all-gathered over NCCL, as before each layer's ``o_proj``.  ``value``
+    is the sequence's decode tokens/s (strong scaling: the work is fixed as
+    N grows); ingest tokens/s (replicated work) beside it."""
+    import torch
+    import torch.distributed as dist
+
+    from kvdlra_b200 import _native as N
+    from kvdlra_b200.sharding import init_ranks, max_over_ranks, shard_heads
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    if world > 1:
+        init_ranks("nccl", dev, timeout_s=600)
+    K, V, Q, _ = make_inputs(w, 0, dev, torch)  # one sequence, the same on every rank
+    T, C, dec, L, B, D = w["tokens"], w["chunk"], w["decode"], w["layers"], w["batch"], w["head_dim"]
+    H, G = w["kv_heads"], w["q_heads"] // w["kv_heads"]
+    h0, hc = shard_heads(H, world, rank)
+    Ql = Q[:, :, :, h0 * G : (h0 + hc) * G].contiguous()  # this rank's query heads
+    del Q
+    cache = new_cache(w, torch)
+    gbuf = torch.empty((L, world, B, hc * G, D), dtype=torch.bfloat16, device=dev)
+
+    def step(ev=None):
+        cache.reset()
+        if ev:
+            ev[0].record()
+        for c0 in range(0, T, C):
+            cache.ingest_all(K[:, :, :, c0 : c0 + C], V[:, :, :, c0 : c0 + C], peek=True)
+        if ev:
+            ev[1].record()
+        for j in range(dec):
+            p = T + j
+            o = cache.decode_all(K[:, :, :, p : p + 1], V[:, :, :, p : p + 1], Ql[j], heads=(h0, hc))
+            if world > 1:
+                for li in range(L):  # each layer's heads gathered before its o_proj
+                    dist.all_gather_into_tensor(gbuf[li], o[li])
+        if ev:
+            ev[2].record()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    with ClockSampler(dev.index) as clk:
+        barrier()
+        for i in range(args.steps):
+            step(ev[i])
+        barrier()
+    ingest_ms = sum(e[0].elapsed_time(e[1]) for e in ev)
+    decode_ms = sum(e[1].elapsed_time(e[2]) for e in ev)
+    ingest_ms, decode_ms = max_over_ranks([ingest_ms, decode_ms], dev)
+    N.profile(True)
+    step()
+    torch.cuda.synchronize(dev)
+    prof = N.profile_read()
+    N.profile(False)
+    if rank == 0:
+        total_ms = sum(x[0] for x in prof.values()) or 1e-9
+        cfg = bench_config(w, world)
+        cfg["parallelism"] = f"KV heads {hc} per GPU over {world} GPU(s); whole cache on every GPU"
+        cfg["sequences_per_gpu"] = None
+        print(json.dumps({
+            "metric": "factored-decode tokens/s of one sequence, KV heads sharded over N B200",
+            "value": B * dec * args.steps / (decode_ms / 1e3),
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": (ingest_ms + decode_ms) / args.steps,
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic (seeded low-rank+noise KV stream with needles; inputs > L2)",
+            "config": cfg,
+            "ingest": {"value": B * T * args.steps / (ingest_ms / 1e3), "unit": "tokens/s",
+                       "note": "replicated on every GPU"},
+            "decode_ms_per_step": decode_ms / args.steps,
+            "ingest_ms_per_step": ingest_ms / args.steps,
+            "gpu_launches": int(sum(v[1] for v in prof.values()) * args.steps),
+            "kernels": {k: {"total_ms": round(v[0], 4), "launches": v[1], "share": round(v[0] / total_ms, 4)}
+                        for k, v in sorted(prof.items(), key=lambda kv: -kv[1][0])},
+            "clocks": clk.summary(),
+        }))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_chunk_attention(args) -> None:
     """Chunk attention at the Llama-3.2-1B cache shape (16 layers, 8 KV heads x
     64, 32 query heads, bf16, r=32, h=256): the cache ingests ``tokens - 512``
@@ -908,6 +1019,13 @@ def main() -> None:
         w["tokens"] = args.tokens
     if args.batch:
         w["batch"] = args.batch
+    if w["name"] == "head-sharded-kv":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the reference runs one device; its "
+                              "single-sequence CPU path is the whole-box-kv reference line"}))
+        else:
+            run_head_sharded(args, w)
+        return
     if args.impl == "reference":
         run_reference(args, w)
     else:

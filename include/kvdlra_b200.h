@@ -187,6 +187,27 @@ size_t kvd_chunk_attention_workspace_bytes(const kvd_config* cfg, int32_t count,
 /* 1 when kvd_factored_chunk_attention takes this configuration. */
 int kvd_chunk_attention_supported(const kvd_config* cfg, int32_t num_q_heads);
 
+/* Head-sharded attention (no counterpart in the reference, which runs on one
+ * device): the two calls above restricted to KV heads [head0, head0 +
+ * n_heads) of the cache, for a single sequence whose attention is split over
+ * GPUs by KV head while every GPU keeps the whole cache (the basis is joint
+ * over heads, bug_cache.py:605-607, so each absorb needs every head's keys).
+ * q and out hold only the query heads of those KV heads, grouped as in the
+ * model (num_q_heads a multiple of n_heads); the tail views hold every KV
+ * head.  Concatenating the outputs of a partition of the heads gives the
+ * full call's output.  Workspace: the full call's size covers any range. */
+int kvd_factored_decode_heads(const kvd_config* cfg, const kvd_buffers* buf, const kvd_counters* ctr,
+                              int32_t p0, int32_t count, int32_t head0, int32_t n_heads,
+                              const void* q, int32_t num_q_heads, float scaling, void* out,
+                              void* workspace, size_t ws_bytes, kvd_stream_t stream);
+int kvd_factored_chunk_attention_heads(const kvd_config* cfg, const kvd_buffers* buf,
+                                       const kvd_counters* ctr, int32_t p0, int32_t count,
+                                       int32_t head0, int32_t n_heads, const void* q, int64_t q_sb,
+                                       int64_t q_sh, int64_t q_st, int32_t num_q_heads, int32_t q_len,
+                                       float scaling, kvd_hf_view tail_k, kvd_hf_view tail_v,
+                                       void* out, void* workspace, size_t ws_bytes,
+                                       kvd_stream_t stream);
+
 /* ------------------------------------------------ integrator primitives */
 
 /* Batched augmented rank-adaptive BUG step on `n_batch` independent problems

@@ -128,6 +128,11 @@ def lib() -> C.CDLL:
     i64 = C.c_int64
     L.kvd_factored_chunk_attention.argtypes = [P(Config), P(Buffers), P(Counters), i32, i32, vp, i64, i64,
                                                i64, i32, i32, f32, HFView, HFView, vp, vp, sz, vp]
+    L.kvd_factored_decode_heads.argtypes = [P(Config), P(Buffers), P(Counters), i32, i32, i32, i32, vp, i32,
+                                            f32, vp, vp, sz, vp]
+    L.kvd_factored_chunk_attention_heads.argtypes = [P(Config), P(Buffers), P(Counters), i32, i32, i32, i32, vp,
+                                                     i64, i64, i64, i32, i32, f32, HFView, HFView, vp, vp, sz,
+                                                     vp]
     L.kvd_chunk_attention_workspace_bytes.argtypes = [P(Config), i32, i32, i32]
     L.kvd_chunk_attention_workspace_bytes.restype = sz
     L.kvd_chunk_attention_supported.argtypes = [P(Config), i32]
@@ -145,7 +150,8 @@ def lib() -> C.CDLL:
     L.kvd_blocked_project_workspace_bytes.argtypes = [i32, i32, i32, i32]
     L.kvd_blocked_project_workspace_bytes.restype = sz
     for name in ("kvd_check_status", "kvd_prefill", "kvd_append", "kvd_consolidate", "kvd_absorb_block", "kvd_peek",
-                 "kvd_factored_decode", "kvd_factored_chunk_attention", "kvd_bug_step", "kvd_surprise",
+                 "kvd_factored_decode", "kvd_factored_chunk_attention", "kvd_factored_decode_heads",
+                 "kvd_factored_chunk_attention_heads", "kvd_bug_step", "kvd_surprise",
                  "kvd_select_topk",
                  "kvd_profile", "kvd_profile_read", "kvd_blocked_project", "kvd_rope_table"):
         getattr(L, name).restype = C.c_int

@@ -22,6 +22,11 @@ other shapes, the single-shot prefill and any cache that is not a
 before.  ``update``'s return contract is unchanged for models that
 do not select the function, so lock-step comparisons against the reference's
 dense peek still hold.
+
+An attention module carrying ``kvd_heads = (h0, hc)`` (set by
+:func:`kvdlra_b200.sharding.shard_attention_heads`) answers only the query
+heads of KV heads ``[h0, h0 + hc)``: the factored kernels take the head range,
+SDPA takes those heads of the key/value it was given.
 """
 
 from __future__ import annotations
@@ -47,7 +52,11 @@ def factored_attention_forward(module: torch.nn.Module, query: torch.Tensor, key
     tagged the step, SDPA otherwise.  ``query`` is ``(B, Hq, q_len, D)``; the
     output is ``(B, q_len, Hq, D)`` as transformers expects."""
     layer = getattr(key, _TAG, None)
+    heads = getattr(module, "kvd_heads", None)
     if layer is None:
+        if heads is not None and key.shape[1] != heads[1]:
+            h0, hc = heads
+            key, value = key[:, h0 : h0 + hc], value[:, h0 : h0 + hc]
         return sdpa_attention_forward(module, query, key, value, attention_mask, dropout=dropout,
                                       scaling=scaling, **kwargs)
     if dropout:
@@ -56,10 +65,10 @@ def factored_attention_forward(module: torch.nn.Module, query: torch.Tensor, key
     if mode in ("ingest", "score"):
         # a chunk (or a frozen-scoring window: its own K/V are the tail)
         tail = (key, value) if mode == "score" else None
-        return layer.factored_chunk_attention(query, scaling=scaling, tail=tail), None
+        return layer.factored_chunk_attention(query, scaling=scaling, tail=tail, heads=heads), None
     if query.shape[2] != 1:
         raise RuntimeError("factored decode answers one query token per step")
-    out = layer.factored_attention(query[:, :, 0, :], scaling=scaling)  # (B, Hq, D)
+    out = layer.factored_attention(query[:, :, 0, :], scaling=scaling, heads=heads)  # (B, Hq, D)
     return out.unsqueeze(1), None
 
 

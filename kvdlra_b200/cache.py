@@ -702,11 +702,24 @@ class BugStreamingLayer(CacheLayerMixin):  # type: ignore[misc]
 
     # -------------------------------------------------------- factored decode
 
-    def factored_attention(self, query: Tensor, scaling: float | None = None) -> Tensor:
+    def _head_range(self, heads: tuple[int, int] | None, hq: int) -> tuple[int, int, int]:
+        """(first KV head, KV heads, query heads of the whole cache) of a call
+        answering ``hq`` query heads of KV heads ``heads`` (all when None)."""
+        h0, hc = (0, self.num_heads) if heads is None else (int(heads[0]), int(heads[1]))
+        if h0 < 0 or hc < 1 or h0 + hc > self.num_heads or hq % hc:
+            raise ValueError(f"KV heads [{h0}, {h0 + hc}) of {self.num_heads} cannot answer {hq} query heads")
+        return h0, hc, hq // hc * self.num_heads
+
+    def factored_attention(self, query: Tensor, scaling: float | None = None,
+                           heads: tuple[int, int] | None = None) -> Tensor:
         """Decode attention of one post-RoPE query token per sequence,
         ``query`` ``(B, Hq, D)`` or ``(B, Hq, 1, D)``, against the retained cache
         without materialising the middle.  Returns ``(B, Hq, D)``; equal to
-        softmax attention over :meth:`_decode_peek` up to rounding."""
+        softmax attention over :meth:`_decode_peek` up to rounding.
+
+        ``heads=(h0, hc)`` answers only KV heads ``[h0, h0 + hc)``: ``query``
+        then holds their query heads (grouped as in the model) and the result
+        is the matching slice of the full call's (head-sharded attention)."""
         g = self._group
         assert g is not None
         q = query.reshape(self.batch, -1, self.head_dim)
@@ -714,24 +727,33 @@ class BugStreamingLayer(CacheLayerMixin):  # type: ignore[misc]
             raise ValueError(f"query dtype {q.dtype} != cache dtype {self.dtype}")
         q = q.contiguous()
         hq = int(q.shape[1])
+        h0, hc, hq_all = self._head_range(heads, hq)
         out = torch.empty_like(q)
         sc = (1.0 / math.sqrt(self.head_dim)) if scaling is None else float(scaling)
         cfg, buf = g.config(g.P), g.buffers(0)
-        ws, wsb = g.decode_workspace(self.batch, hq)
-        N.call(g.device, "kvd_factored_decode", C.byref(cfg), C.byref(buf), C.byref(self._ctr),
-               self._p0(), self.batch, q.data_ptr(), hq, sc,
-               out.data_ptr(), ws, wsb, g.stream())
+        ws, wsb = g.decode_workspace(self.batch, hq_all)
+        if heads is None:
+            N.call(g.device, "kvd_factored_decode", C.byref(cfg), C.byref(buf), C.byref(self._ctr),
+                   self._p0(), self.batch, q.data_ptr(), hq, sc,
+                   out.data_ptr(), ws, wsb, g.stream())
+        else:
+            N.call(g.device, "kvd_factored_decode_heads", C.byref(cfg), C.byref(buf), C.byref(self._ctr),
+                   self._p0(), self.batch, h0, hc, q.data_ptr(), hq, sc,
+                   out.data_ptr(), ws, wsb, g.stream())
         return out
 
     def factored_chunk_attention(self, query: Tensor, scaling: float | None = None,
-                                 tail: tuple[Tensor, Tensor] | None = None) -> Tensor:
+                                 tail: tuple[Tensor, Tensor] | None = None,
+                                 heads: tuple[int, int] | None = None) -> Tensor:
         """Attention of a chunk of post-RoPE queries ``(B, Hq, q, D)`` against
         the retained cache, causal over the last ``q`` keys, without
         materialising the middle tier: ingest (the chunk is the end of the
         ring, ``tail`` None) or frozen scoring (the chunk is ``tail``, not
         appended).  Returns ``(B, q, Hq, D)``; equal to softmax attention over
         :meth:`_decode_peek` (with the tail) and the bottom-right causal mask
-        up to bf16 rounding."""
+        up to bf16 rounding.  ``heads=(h0, hc)`` answers only KV heads
+        ``[h0, h0 + hc)`` (query heads of those only; ``tail`` holds every KV
+        head), as :meth:`factored_attention` does."""
         g = self._group
         assert g is not None
         if query.dim() != 4 or query.shape[0] != self.batch or query.shape[3] != self.head_dim:
@@ -740,16 +762,23 @@ class BugStreamingLayer(CacheLayerMixin):  # type: ignore[misc]
             raise ValueError(f"query dtype {query.dtype} != cache dtype {self.dtype}")
         q = query if query.stride(3) == 1 else query.contiguous()
         hq, q_len = int(q.shape[1]), int(q.shape[2])
+        h0, hc, hq_all = self._head_range(heads, hq)
         out = torch.empty(self.batch, q_len, hq, self.head_dim, dtype=self.dtype, device=self.device)
         sc = (1.0 / math.sqrt(self.head_dim)) if scaling is None else float(scaling)
         tk = tv = None
         if tail is not None:
             tk, tv = self._check_kv(tail[0], tail[1])
         cfg, buf = g.config(g.P), g.buffers(0)
-        ws, wsb = g.chunk_workspace(self.batch, hq, q_len)
-        N.call(g.device, "kvd_factored_chunk_attention", C.byref(cfg), C.byref(buf), C.byref(self._ctr),
-               self._p0(), self.batch, q.data_ptr(), q.stride(0), q.stride(1), q.stride(2), hq, q_len, sc,
-               N.hf_view(tk), N.hf_view(tv), out.data_ptr(), ws, wsb, g.stream())
+        ws, wsb = g.chunk_workspace(self.batch, hq_all, q_len)
+        if heads is None:
+            N.call(g.device, "kvd_factored_chunk_attention", C.byref(cfg), C.byref(buf), C.byref(self._ctr),
+                   self._p0(), self.batch, q.data_ptr(), q.stride(0), q.stride(1), q.stride(2), hq, q_len, sc,
+                   N.hf_view(tk), N.hf_view(tv), out.data_ptr(), ws, wsb, g.stream())
+        else:
+            N.call(g.device, "kvd_factored_chunk_attention_heads", C.byref(cfg), C.byref(buf),
+                   C.byref(self._ctr), self._p0(), self.batch, h0, hc, q.data_ptr(), q.stride(0), q.stride(1),
+                   q.stride(2), hq, q_len, sc, N.hf_view(tk), N.hf_view(tv), out.data_ptr(), ws, wsb,
+                   g.stream())
         return out
 
     # ------------------------------------------------------------ state views
@@ -1181,10 +1210,11 @@ class BugStreamingCache(Cache):
         return out_k, out_v
 
     def decode_all(self, keys: Tensor, values: Tensor, queries: Tensor,
-                   scaling: float | None = None) -> Tensor:
+                   scaling: float | None = None, heads: tuple[int, int] | None = None) -> Tensor:
         """One decode step for every layer: append ``(layers, B, H, 1, D)`` K/V,
         run due absorbs, then factored attention of ``queries`` ``(layers, B,
-        Hq, D)``.  Returns ``(layers, B, Hq, D)``."""
+        Hq, D)``.  Returns ``(layers, B, Hq, D)``.  ``heads=(h0, hc)``: the
+        queries and the result cover KV heads ``[h0, h0 + hc)`` only."""
         Ls, B, H, q, D = keys.shape
         layers = self._bug_layers()
         first = layers[0]
@@ -1200,13 +1230,14 @@ class BugStreamingCache(Cache):
             ly._ctr.copy_from(ctr)
         self.consolidate()
         hq = int(queries.shape[2])
+        h0, hc, hq_all = first._head_range(heads, hq)
         qq = queries.reshape(Ls * B, hq, D).contiguous()
         out = torch.empty_like(qq)
         sc = (1.0 / math.sqrt(D)) if scaling is None else float(scaling)
         cfg, buf = g.config(g.P), g.buffers(0)
-        ws, wsb = g.decode_workspace(g.P, hq)
-        N.call(g.device, "kvd_factored_decode", C.byref(cfg), C.byref(buf), C.byref(first._ctr), 0, g.P,
-               qq.data_ptr(), hq, sc, out.data_ptr(), ws, wsb,
+        ws, wsb = g.decode_workspace(g.P, hq_all)
+        N.call(g.device, "kvd_factored_decode_heads", C.byref(cfg), C.byref(buf), C.byref(first._ctr), 0, g.P,
+               h0, hc, qq.data_ptr(), hq, sc, out.data_ptr(), ws, wsb,
                g.stream())
         return out.reshape(Ls, B, hq, D)
 

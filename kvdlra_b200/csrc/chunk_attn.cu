@@ -494,31 +494,39 @@ using namespace kvd;
 
 static bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-bool chunk_attention_applicable(const kvd_config& c, int num_q_heads) {
+bool chunk_attention_applicable(const kvd_config& c, int num_q_heads, int n_heads) {
   return c.dtype == KVD_DTYPE_BF16 && c.head_dim == kCaD && c.rank <= kCaR && c.rank % 4 == 0 &&
-         num_q_heads % c.num_heads == 0 && num_q_heads >= c.num_heads &&
+         n_heads >= 1 && n_heads <= c.num_heads && num_q_heads % n_heads == 0 && num_q_heads >= n_heads &&
          (c.num_heads * c.head_dim) % 8 == 0;
 }
 
 constexpr int kCaMaxSplit = 8;
 
-size_t chunk_attention_ws_bytes(const kvd_config& c, int count, int num_q_heads, int q_len) {
-  const long rows = (long)q_len * (num_q_heads / (c.num_heads > 0 ? c.num_heads : 1));
-  return (size_t)count * c.num_heads * rows * kCaMaxSplit * kCaRec * sizeof(float);
+size_t chunk_attention_ws_bytes(const kvd_config& c, int count, int num_q_heads, int q_len, int n_heads) {
+  const long rows = (long)q_len * (num_q_heads / (n_heads > 0 ? n_heads : 1));
+  return (size_t)count * n_heads * rows * kCaMaxSplit * kCaRec * sizeof(float);
 }
 
 int launch_chunk_attention(const kvd_config& c, const kvd_buffers& bu, const kvd_counters& k, int p0,
-                           int count, const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st, int Hq,
-                           int q_len, float scaling, const kvd_hf_view& tail_k, const kvd_hf_view& tail_v,
-                           void* out, void* ws, size_t ws_bytes, cudaStream_t s) {
-  if (!chunk_attention_applicable(c, Hq)) {
+                           int count, int h0, int hc, const void* q, int64_t q_sb, int64_t q_sh,
+                           int64_t q_st, int Hq, int q_len, float scaling, const kvd_hf_view& tail_k,
+                           const kvd_hf_view& tail_v, void* out, void* ws, size_t ws_bytes,
+                           cudaStream_t s) {
+  if (h0 < 0 || hc < 1 || h0 + hc > c.num_heads) {
+    set_error("factored chunk attention: bad KV head range [%d, %d) of %d", h0, h0 + hc, c.num_heads);
+    return KVD_ERR_ARG;
+  }
+  if (!chunk_attention_applicable(c, Hq, hc)) {
     set_error("factored chunk attention: unsupported shape (bf16, head_dim %d, rank <= %d, rank %% 4 == 0)",
               kCaD, kCaR);
     return KVD_ERR_ARG;
   }
   const int n = c.num_heads * c.head_dim;
   CaArgs a;
-  a.H = c.num_heads; a.G = Hq / c.num_heads; a.ld = c.rank; a.Hq = Hq; a.q_len = q_len;
+  // KV heads [h0, h0 + hc): hc groups whose tier rows start h0 * D features
+  // into each token row and whose basis rows start at row h0 * D; the query
+  // and output hold only their heads
+  a.H = hc; a.G = Hq / hc; a.ld = c.rank; a.Hq = Hq; a.q_len = q_len;
   a.rows = q_len * a.G;
   const int tail_len = tail_k.ptr ? tail_k.tokens : 0;
   const int lens[kCaSegs] = {k.sink_len, k.hh_len, k.w_len, k.ring_len, tail_len};
@@ -528,13 +536,15 @@ int launch_chunk_attention(const kvd_config& c, const kvd_buffers& bu, const kvd
   if (q_len < 1 || q_len > total) { set_error("factored chunk attention: %d queries over %ld keys", q_len, total); return KVD_ERR_ARG; }
   const long sink_sp = (long)c.n_sink * n, hh_sp = (long)c.hh_budget * n, ring_sp = (long)c.ring_cap * n;
   using bf = __nv_bfloat16;
-  a.seg_k[0] = (const bf*)bu.sink_k + p0 * sink_sp; a.seg_v[0] = (const bf*)bu.sink_v + p0 * sink_sp; a.seg_sp[0] = sink_sp;
-  a.seg_k[1] = (const bf*)bu.hh_k[k.hh_sel] + p0 * hh_sp; a.seg_v[1] = (const bf*)bu.hh_v[k.hh_sel] + p0 * hh_sp; a.seg_sp[1] = hh_sp;
+  const long hoff = (long)h0 * c.head_dim;
+  a.seg_k[0] = (const bf*)bu.sink_k + p0 * sink_sp + hoff; a.seg_v[0] = (const bf*)bu.sink_v + p0 * sink_sp + hoff; a.seg_sp[0] = sink_sp;
+  a.seg_k[1] = (const bf*)bu.hh_k[k.hh_sel] + p0 * hh_sp + hoff; a.seg_v[1] = (const bf*)bu.hh_v[k.hh_sel] + p0 * hh_sp + hoff; a.seg_sp[1] = hh_sp;
   a.seg_k[2] = nullptr; a.seg_v[2] = nullptr; a.seg_sp[2] = 0;
-  a.seg_k[3] = (const bf*)bu.ring_k + p0 * ring_sp + (long)k.ring_head * n;
-  a.seg_v[3] = (const bf*)bu.ring_v + p0 * ring_sp + (long)k.ring_head * n; a.seg_sp[3] = ring_sp;
+  a.seg_k[3] = (const bf*)bu.ring_k + p0 * ring_sp + (long)k.ring_head * n + hoff;
+  a.seg_v[3] = (const bf*)bu.ring_v + p0 * ring_sp + (long)k.ring_head * n + hoff; a.seg_sp[3] = ring_sp;
   for (int i = 0; i < 4; ++i) { a.seg_tok[i] = n; a.seg_head[i] = c.head_dim; }
-  a.seg_k[4] = (const bf*)tail_k.ptr; a.seg_v[4] = (const bf*)tail_v.ptr;
+  a.seg_k[4] = tail_k.ptr ? (const bf*)tail_k.ptr + (long)h0 * tail_k.stride_h : nullptr;
+  a.seg_v[4] = tail_v.ptr ? (const bf*)tail_v.ptr + (long)h0 * tail_v.stride_h : nullptr;
   a.seg_sp[4] = tail_k.stride_b; a.seg_tok[4] = tail_k.stride_t; a.seg_head[4] = tail_k.stride_h;
   if (tail_len > 0) {
     const bool same = tail_v.ptr && tail_v.stride_b == tail_k.stride_b && tail_v.stride_h == tail_k.stride_h &&
@@ -544,7 +554,7 @@ int launch_chunk_attention(const kvd_config& c, const kvd_buffers& bu, const kvd
     if (!same || !aligned) { set_error("factored chunk attention: tail views must match and be 16-byte aligned"); return KVD_ERR_ARG; }
   }
   a.u_sp = (long)n * c.rank;
-  a.uk = bu.u_k[k.u_sel] + p0 * a.u_sp; a.uv = bu.u_v[k.u_sel] + p0 * a.u_sp;
+  a.uk = bu.u_k[k.u_sel] + p0 * a.u_sp + hoff * c.rank; a.uv = bu.u_v[k.u_sel] + p0 * a.u_sp + hoff * c.rank;
   a.rk = bu.r_k + p0; a.rv = bu.r_v + p0;
   a.c_sp = (long)c.w_cap * c.rank;
   a.ck = bu.c_k + p0 * a.c_sp; a.cv = bu.c_v + p0 * a.c_sp;

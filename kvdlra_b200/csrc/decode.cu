@@ -24,7 +24,8 @@ constexpr int kMaxNV = 4;         // head_dim <= 128 -> 4 values per lane
 constexpr int kMaxNC = 6;         // rank <= 192 -> 6 coordinates per lane
 
 struct DecArgs {
-  int H, D, G, ld, Hq;
+  int H, D, G, ld, Hq;  // the KV heads (groups) and query heads this launch answers
+  int nrow;             // features per token row of the tier buffers (every KV head of the cache)
   int sink_len, hh_len, W, ring_len, L;
   const void* sink_k; const void* sink_v; long sink_sp;
   const void* hh_k; const void* hh_v; long hh_sp;
@@ -48,7 +49,7 @@ template <typename T, int NV, int NC>
 __global__ void __launch_bounds__(kDecThreads) decode_split_kernel(DecArgs a) {
   extern __shared__ __align__(16) float dsm[];
   const int chunk = blockIdx.x, g = blockIdx.y, p = blockIdx.z;
-  const int D = a.D, G = a.G, ld = a.ld, n = a.H * a.D, half = D / 2;
+  const int D = a.D, G = a.G, ld = a.ld, n = a.nrow, half = D / 2;
   const int lane = threadIdx.x % 32, warp = threadIdx.x / 32;
   const int r_k = a.rk[p], r_v = a.rv[p];
   float* qs = dsm;                       // [G][D]
@@ -247,7 +248,7 @@ __global__ void __launch_bounds__(kTileThreads) decode_tile_kernel(DecArgs a, in
   constexpr int ldk = D + 4;                   // = 4 mod 8: row-per-lane float4 reads conflict-free
   extern __shared__ __align__(16) float tsm[];
   const int chunk = blockIdx.x, g = blockIdx.y, p = blockIdx.z;
-  const int G = a.G, ld = a.ld, n = a.H * D;
+  const int G = a.G, ld = a.ld, n = a.nrow;
   const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
   const int r_k = a.rk[p], r_v = a.rv[p];
   const int ldc = ld + 4;
@@ -491,7 +492,7 @@ __global__ void __launch_bounds__(kTileThreads) decode_mma_kernel(DecArgs a, int
   constexpr int ldps = kTT + 4;  // = 4 mod 32: P fragment reads (4g + t) conflict-free
   extern __shared__ __align__(16) float tsm[];
   const int chunk = blockIdx.x, g = blockIdx.y, p = blockIdx.z;
-  const int G = a.G, ld = a.ld, n = a.H * D;
+  const int G = a.G, ld = a.ld, n = a.nrow;
   const int tid = threadIdx.x, lane = tid % 32, warp = tid / 32;
   const int gq = lane >> 2, tq = lane & 3;
   const int r_k = a.rk[p], r_v = a.rv[p];
@@ -1154,15 +1155,15 @@ using namespace kvd;
 
 static int dec_chunks(int L) { return (L + kChunk - 1) / kChunk; }
 
-size_t decode_ws_bytes(const kvd_config& c, int count, int num_q_heads) {
-  const int G = num_q_heads / c.num_heads;
+size_t decode_ws_bytes(const kvd_config& c, int count, int num_q_heads, int n_heads) {
+  const int G = num_q_heads / n_heads;
   const int L_max = c.n_sink + c.hh_budget + c.w_cap + c.ring_cap;
   const long rec = part_floats(G, c.head_dim, c.rank);
   // tiled paths: one chunk per verbatim tile plus middle chunks of >= 2 tiles
   const int nvt = (c.n_sink + c.hh_budget + kTT - 1) / kTT + (c.ring_cap + kTT - 1) / kTT;
   const int ch_tiled = nvt + ((c.w_cap + kTT - 1) / kTT + 1) / 2;
   const int ch = dec_chunks(L_max) > ch_tiled ? dec_chunks(L_max) : ch_tiled;
-  return (size_t)count * c.num_heads * ch * rec * 4 + 256;
+  return (size_t)count * n_heads * ch * rec * 4 + 256;
 }
 
 // ------------------------------------------------------------------
@@ -1484,12 +1485,20 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_umma_kernel(DecArgs a, 
 
 template <typename T>
 int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_counters& k, int p0,
-                           int count, const void* q, int Hq, float scaling, void* out, char* ws,
-                           size_t ws_bytes, cudaStream_t s, cudaStream_t side, cudaEvent_t ev_fork,
-                           cudaEvent_t ev_join) {
+                           int count, int h0, int hc, const void* q, int Hq, float scaling, void* out,
+                           char* ws, size_t ws_bytes, cudaStream_t s, cudaStream_t side,
+                           cudaEvent_t ev_fork, cudaEvent_t ev_join) {
   DecArgs a;
   const int n = c.num_heads * c.head_dim;
-  a.H = c.num_heads; a.D = c.head_dim; a.G = Hq / c.num_heads; a.ld = c.rank; a.Hq = Hq;
+  if (h0 < 0 || hc < 1 || h0 + hc > c.num_heads || Hq % hc) {
+    set_error("factored decode: bad KV head range [%d, %d) of %d for %d query heads", h0, h0 + hc,
+              c.num_heads, Hq);
+    return KVD_ERR_ARG;
+  }
+  // KV heads [h0, h0 + hc): the kernels see hc groups whose tier rows start
+  // h0 * D features into each token row (stride nrow) and whose basis rows
+  // start at row h0 * D; the query and output hold only their heads
+  a.H = hc; a.D = c.head_dim; a.G = Hq / hc; a.ld = c.rank; a.Hq = Hq; a.nrow = n;
   const bool d_ok = (c.head_dim <= 32) || ((c.head_dim / 2) % 32 == 0);
   if (a.G > kMaxG || c.head_dim > 32 * kMaxNV || c.rank > 32 * kMaxNC || !d_ok) {
     set_error("factored decode: unsupported shape (G=%d D=%d r=%d)", a.G, c.head_dim, c.rank);
@@ -1500,13 +1509,14 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
   if (a.L <= 0) { set_error("factored decode on an empty cache"); return KVD_ERR_ARG; }
   const long sink_sp = (long)c.n_sink * n, hh_sp = (long)c.hh_budget * n, ring_sp = (long)c.ring_cap * n;
   const size_t es = sizeof(T);
-  a.sink_k = (const char*)b.sink_k + es * p0 * sink_sp; a.sink_v = (const char*)b.sink_v + es * p0 * sink_sp; a.sink_sp = sink_sp;
-  a.hh_k = (const char*)b.hh_k[k.hh_sel] + es * p0 * hh_sp; a.hh_v = (const char*)b.hh_v[k.hh_sel] + es * p0 * hh_sp; a.hh_sp = hh_sp;
-  a.ring_k = (const char*)b.ring_k + es * (p0 * ring_sp + (long)k.ring_head * n);
-  a.ring_v = (const char*)b.ring_v + es * (p0 * ring_sp + (long)k.ring_head * n);
+  const long hoff = (long)h0 * c.head_dim;  // first feature of the range in a token row
+  a.sink_k = (const char*)b.sink_k + es * (p0 * sink_sp + hoff); a.sink_v = (const char*)b.sink_v + es * (p0 * sink_sp + hoff); a.sink_sp = sink_sp;
+  a.hh_k = (const char*)b.hh_k[k.hh_sel] + es * (p0 * hh_sp + hoff); a.hh_v = (const char*)b.hh_v[k.hh_sel] + es * (p0 * hh_sp + hoff); a.hh_sp = hh_sp;
+  a.ring_k = (const char*)b.ring_k + es * (p0 * ring_sp + (long)k.ring_head * n + hoff);
+  a.ring_v = (const char*)b.ring_v + es * (p0 * ring_sp + (long)k.ring_head * n + hoff);
   a.ring_sp = ring_sp;
   a.u_sp = (long)n * c.rank;
-  a.uk = b.u_k[k.u_sel] + p0 * a.u_sp; a.uv = b.u_v[k.u_sel] + p0 * a.u_sp;
+  a.uk = b.u_k[k.u_sel] + p0 * a.u_sp + hoff * c.rank; a.uv = b.u_v[k.u_sel] + p0 * a.u_sp + hoff * c.rank;
   a.rk = b.r_k + p0; a.rv = b.r_v + p0;
   a.c_sp = (long)c.w_cap * c.rank;
   a.ck = b.c_k + p0 * a.c_sp; a.cv = b.c_v + p0 * a.c_sp;
@@ -1534,7 +1544,7 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
   // middle tier by decode_mid_kernel (every group per CTA) when the basis of
   // all groups fits in shared memory; verbatim tiles by decode_mma_kernel
   const int Hq_all = a.H * a.G;
-  const MidSmem ms = mid_smem(n, Hq_all, a.D, a.ld);
+  const MidSmem ms = mid_smem(a.H * a.D, Hq_all, a.D, a.ld);
   const bool mid_all = mma && a.W > 0 && Hq_all <= kMidWarps * kMaxRW && a.ld <= 64 &&
                        ((Hq_all + 15) / 16) * (a.ld / 8) <= kMidWarps * kMaxPW &&
                        4L * ms.total <= 200 * 1024 &&
@@ -1673,11 +1683,11 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
   return check_launch("decode_merge_kernel");
 }
 
-template int launch_factored_decode<float>(const kvd_config&, const kvd_buffers&, const kvd_counters&, int, int,
+template int launch_factored_decode<float>(const kvd_config&, const kvd_buffers&, const kvd_counters&, int, int, int, int,
                                            const void*, int, float, void*, char*, size_t, cudaStream_t,
                                            cudaStream_t, cudaEvent_t, cudaEvent_t);
 template int launch_factored_decode<__nv_bfloat16>(const kvd_config&, const kvd_buffers&, const kvd_counters&, int,
-                                                   int, const void*, int, float, void*, char*, size_t,
+                                                   int, int, int, const void*, int, float, void*, char*, size_t,
                                                    cudaStream_t, cudaStream_t, cudaEvent_t, cudaEvent_t);
 
 }  // namespace kvd_host

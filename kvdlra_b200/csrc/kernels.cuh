@@ -149,19 +149,24 @@ template <typename T>
 int launch_peek(const kvd_config& c, const kvd_buffers& b, const kvd_counters& k, int p0, int count,
                 const kvd_hf_view& ok_, const kvd_hf_view& ov_, const kvd_hf_view& tk,
                 const kvd_hf_view& tv, cudaStream_t s);
-size_t decode_ws_bytes(const kvd_config& c, int count, int num_q_heads);
+// workspace of a decode over `n_heads` KV heads answering num_q_heads query heads
+size_t decode_ws_bytes(const kvd_config& c, int count, int num_q_heads, int n_heads);
 template <typename T>
 // `side` (with two events), when given, runs the verbatim tiles concurrently
 // with the middle tier; the merge waits for both on `s`.
+// KV heads [h0, h0 + hc) of the cache; q and out hold their Hq query heads.
 int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_counters& k, int p0,
-                           int count, const void* q, int Hq, float scaling, void* out, char* ws,
+                           int count, int h0, int hc, const void* q, int Hq, float scaling, void* out, char* ws,
                            size_t ws_bytes, cudaStream_t s, cudaStream_t side = nullptr,
                            cudaEvent_t ev_fork = nullptr, cudaEvent_t ev_join = nullptr);
 // Factored chunk attention (chunk_attn.cu): bf16, head_dim 64, rank <= 32.
-bool chunk_attention_applicable(const kvd_config& c, int num_q_heads);
+// KV heads [h0, h0 + hc) of the cache (n_heads = hc); q and out hold their
+// Hq query heads, the tail views every KV head.
+bool chunk_attention_applicable(const kvd_config& c, int num_q_heads, int n_heads);
 int launch_chunk_attention(const kvd_config& c, const kvd_buffers& bu, const kvd_counters& k, int p0,
-                           int count, const void* q, int64_t q_sb, int64_t q_sh, int64_t q_st, int Hq,
-                           int q_len, float scaling, const kvd_hf_view& tail_k, const kvd_hf_view& tail_v,
-                           void* out, void* ws, size_t ws_bytes, cudaStream_t s);
-size_t chunk_attention_ws_bytes(const kvd_config& c, int count, int num_q_heads, int q_len);
+                           int count, int h0, int hc, const void* q, int64_t q_sb, int64_t q_sh,
+                           int64_t q_st, int Hq, int q_len, float scaling, const kvd_hf_view& tail_k,
+                           const kvd_hf_view& tail_v, void* out, void* ws, size_t ws_bytes,
+                           cudaStream_t s);
+size_t chunk_attention_ws_bytes(const kvd_config& c, int count, int num_q_heads, int q_len, int n_heads);
 }  // namespace kvd_host

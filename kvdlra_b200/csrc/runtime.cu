@@ -676,24 +676,59 @@ extern "C" int kvd_peek(const kvd_config* cfg, const kvd_buffers* buf, const kvd
   });
 }
 
-extern "C" int kvd_factored_decode(const kvd_config* cfg, const kvd_buffers* buf,
-                                   const kvd_counters* ctr, int32_t p0, int32_t count,
-                                   const void* q, int32_t num_q_heads, float scaling, void* out,
-                                   void* workspace, size_t ws_bytes, kvd_stream_t stream) {
+static int factored_decode(const kvd_config* cfg, const kvd_buffers* buf, const kvd_counters* ctr,
+                           int32_t p0, int32_t count, int32_t head0, int32_t n_heads, const void* q,
+                           int32_t num_q_heads, float scaling, void* out, void* workspace,
+                           size_t ws_bytes, kvd_stream_t stream) {
   int rc = validate(cfg);
   if (rc) return rc;
   if (p0 < 0 || count < 1 || p0 + count > cfg->n_problems) { set_error("kvd_factored_decode: bad problem range"); return KVD_ERR_ARG; }
-  if (num_q_heads < cfg->num_heads || num_q_heads % cfg->num_heads) { set_error("kvd_factored_decode: %d query heads do not group over %d KV heads", num_q_heads, cfg->num_heads); return KVD_ERR_ARG; }
-  const size_t need = decode_ws_bytes(*cfg, count, num_q_heads);
+  if (head0 < 0 || n_heads < 1 || head0 + n_heads > cfg->num_heads) { set_error("kvd_factored_decode: bad KV head range [%d, %d) of %d", head0, head0 + n_heads, cfg->num_heads); return KVD_ERR_ARG; }
+  if (num_q_heads < n_heads || num_q_heads % n_heads) { set_error("kvd_factored_decode: %d query heads do not group over %d KV heads", num_q_heads, n_heads); return KVD_ERR_ARG; }
+  if (!q || !out) { set_error("kvd_factored_decode: null query or output"); return KVD_ERR_ARG; }
+  const size_t need = decode_ws_bytes(*cfg, count, num_q_heads, n_heads);
   if (ws_bytes < need || !workspace) { set_error("kvd_factored_decode: workspace %zu < %zu", ws_bytes, need); return KVD_ERR_WORKSPACE; }
   return dispatch(cfg, [&](auto* tag) {
     using T = std::remove_pointer_t<decltype(tag)>;
     CarryStream* cs = carry_stream();
-    return launch_factored_decode<T>(*cfg, *buf, *ctr, p0, count, q, num_q_heads, scaling, out,
-                                     align_ws(workspace), ws_bytes - 256, (cudaStream_t)stream,
+    return launch_factored_decode<T>(*cfg, *buf, *ctr, p0, count, head0, n_heads, q, num_q_heads, scaling,
+                                     out, align_ws(workspace), ws_bytes - 256, (cudaStream_t)stream,
                                      cs ? cs->side : nullptr, cs ? cs->dfork : nullptr,
                                      cs ? cs->djoin : nullptr);
   });
+}
+
+extern "C" int kvd_factored_decode(const kvd_config* cfg, const kvd_buffers* buf,
+                                   const kvd_counters* ctr, int32_t p0, int32_t count,
+                                   const void* q, int32_t num_q_heads, float scaling, void* out,
+                                   void* workspace, size_t ws_bytes, kvd_stream_t stream) {
+  if (int rc = validate(cfg)) return rc;
+  return factored_decode(cfg, buf, ctr, p0, count, 0, cfg->num_heads, q, num_q_heads, scaling, out,
+                         workspace, ws_bytes, stream);
+}
+
+extern "C" int kvd_factored_decode_heads(const kvd_config* cfg, const kvd_buffers* buf,
+                                         const kvd_counters* ctr, int32_t p0, int32_t count,
+                                         int32_t head0, int32_t n_heads, const void* q,
+                                         int32_t num_q_heads, float scaling, void* out,
+                                         void* workspace, size_t ws_bytes, kvd_stream_t stream) {
+  return factored_decode(cfg, buf, ctr, p0, count, head0, n_heads, q, num_q_heads, scaling, out,
+                         workspace, ws_bytes, stream);
+}
+
+static int factored_chunk_attention(const kvd_config* cfg, const kvd_buffers* buf,
+                                    const kvd_counters* ctr, int32_t p0, int32_t count, int32_t head0,
+                                    int32_t n_heads, const void* q, int64_t q_sb, int64_t q_sh,
+                                    int64_t q_st, int32_t num_q_heads, int32_t q_len, float scaling,
+                                    kvd_hf_view tail_k, kvd_hf_view tail_v, void* out,
+                                    void* workspace, size_t ws_bytes, kvd_stream_t stream) {
+  int rc = validate(cfg);
+  if (rc) return rc;
+  if (p0 < 0 || count < 1 || p0 + count > cfg->n_problems) { set_error("kvd_factored_chunk_attention: bad problem range"); return KVD_ERR_ARG; }
+  if (!q || !out) { set_error("kvd_factored_chunk_attention: null query or output"); return KVD_ERR_ARG; }
+  return launch_chunk_attention(*cfg, *buf, *ctr, p0, count, head0, n_heads, q, q_sb, q_sh, q_st,
+                                num_q_heads, q_len, scaling, tail_k, tail_v, out, workspace, ws_bytes,
+                                (cudaStream_t)stream);
 }
 
 extern "C" int kvd_factored_chunk_attention(const kvd_config* cfg, const kvd_buffers* buf,
@@ -702,24 +737,35 @@ extern "C" int kvd_factored_chunk_attention(const kvd_config* cfg, const kvd_buf
                                             int32_t num_q_heads, int32_t q_len, float scaling,
                                             kvd_hf_view tail_k, kvd_hf_view tail_v, void* out,
                                             void* workspace, size_t ws_bytes, kvd_stream_t stream) {
-  int rc = validate(cfg);
-  if (rc) return rc;
-  if (p0 < 0 || count < 1 || p0 + count > cfg->n_problems) { set_error("kvd_factored_chunk_attention: bad problem range"); return KVD_ERR_ARG; }
-  if (!q || !out) { set_error("kvd_factored_chunk_attention: null query or output"); return KVD_ERR_ARG; }
-  return launch_chunk_attention(*cfg, *buf, *ctr, p0, count, q, q_sb, q_sh, q_st, num_q_heads, q_len,
-                                scaling, tail_k, tail_v, out, workspace, ws_bytes, (cudaStream_t)stream);
+  if (int rc = validate(cfg)) return rc;
+  return factored_chunk_attention(cfg, buf, ctr, p0, count, 0, cfg->num_heads, q, q_sb, q_sh, q_st,
+                                  num_q_heads, q_len, scaling, tail_k, tail_v, out, workspace, ws_bytes,
+                                  stream);
+}
+
+extern "C" int kvd_factored_chunk_attention_heads(const kvd_config* cfg, const kvd_buffers* buf,
+                                                  const kvd_counters* ctr, int32_t p0, int32_t count,
+                                                  int32_t head0, int32_t n_heads, const void* q,
+                                                  int64_t q_sb, int64_t q_sh, int64_t q_st,
+                                                  int32_t num_q_heads, int32_t q_len, float scaling,
+                                                  kvd_hf_view tail_k, kvd_hf_view tail_v, void* out,
+                                                  void* workspace, size_t ws_bytes, kvd_stream_t stream) {
+  return factored_chunk_attention(cfg, buf, ctr, p0, count, head0, n_heads, q, q_sb, q_sh, q_st,
+                                  num_q_heads, q_len, scaling, tail_k, tail_v, out, workspace, ws_bytes,
+                                  stream);
 }
 
 extern "C" size_t kvd_chunk_attention_workspace_bytes(const kvd_config* cfg, int32_t count,
                                                       int32_t num_q_heads, int32_t q_len) {
   if (!cfg || count < 1 || q_len < 1 || num_q_heads < 1) return 0;
-  return chunk_attention_ws_bytes(*cfg, count, num_q_heads, q_len);
+  return chunk_attention_ws_bytes(*cfg, count, num_q_heads, q_len, cfg->num_heads);
 }
 
 extern "C" int kvd_chunk_attention_supported(const kvd_config* cfg, int32_t num_q_heads) {
-  return cfg && chunk_attention_applicable(*cfg, num_q_heads) ? 1 : 0;
+  return cfg && chunk_attention_applicable(*cfg, num_q_heads, cfg->num_heads) ? 1 : 0;
 }
 
 extern "C" size_t kvd_decode_workspace_bytes(const kvd_config* cfg, int32_t count, int32_t num_q_heads) {
-  return decode_ws_bytes(*cfg, count, num_q_heads) + 256;
+  if (!cfg || cfg->num_heads < 1) return 0;
+  return decode_ws_bytes(*cfg, count, num_q_heads, cfg->num_heads) + 256;
 }

@@ -84,23 +84,26 @@ def test_factored_attention_routing_without_gpu() -> None:
     """transformers' attention call (attention.py): an untagged key goes to
     SDPA; a tagged key goes to the chunk kernel in ingest (no tail) and score
     (the step's own K/V as tail) modes and to the factored decode otherwise,
-    with the output in transformers' (B, q, Hq, D) layout.  The layer is a
-    stand-in that records the calls (nothing runs on a GPU)."""
+    with the output in transformers' (B, q, Hq, D) layout.  A module with a
+    KV-head range passes it to the kernels and gives SDPA only those heads.
+    The layer is a stand-in that records the calls (nothing runs on a GPU)."""
     from kvdlra_b200 import attention as A
 
-    calls = []
+    calls, heads_seen = [], []
 
     class FakeLayer:
         def __init__(self, mode):
             self._mode = mode
 
-        def factored_chunk_attention(self, query, scaling=None, tail=None):
+        def factored_chunk_attention(self, query, scaling=None, tail=None, heads=None):
             calls.append(("chunk", self._mode, tail is not None, tuple(query.shape)))
+            heads_seen.append(heads)
             b, hq, q, d = query.shape
             return torch.zeros(b, q, hq, d)
 
-        def factored_attention(self, query, scaling=None):
+        def factored_attention(self, query, scaling=None, heads=None):
             calls.append(("decode", self._mode, False, tuple(query.shape)))
+            heads_seen.append(heads)
             return torch.zeros(query.shape)
 
     module = torch.nn.Module()
@@ -124,3 +127,15 @@ def test_factored_attention_routing_without_gpu() -> None:
     with pytest.raises(NotImplementedError, match="dropout"):
         A.factored_attention_forward(module, q, A.tag_step(k.clone(), FakeLayer("ingest")), v, None,
                                      dropout=0.1)
+    assert all(h is None for h in heads_seen)
+    # KV head 1 of 2 (query heads 2, 3): the kernels get the range, SDPA the head
+    module.kvd_heads = (1, 1)
+    q2 = torch.randn(1, 2, 5, 8)
+    k2, v2 = torch.randn(1, 2, 5, 8), torch.randn(1, 2, 5, 8)
+    out, _ = A.factored_attention_forward(module, q2, k2, v2, None)
+    ref, _ = A.sdpa_attention_forward(module, q2, k2[:, 1:], v2[:, 1:], None)
+    assert torch.equal(out, ref)
+    A.factored_attention_forward(module, q2, A.tag_step(k2.clone(), FakeLayer("ingest")), v2, None)
+    A.factored_attention_forward(module, q2[:, :, :1], A.tag_step(k2[:, :, :1].clone(), FakeLayer("normal")),
+                                 v2[:, :, :1], None)
+    assert heads_seen[-2:] == [(1, 1), (1, 1)]
