@@ -59,8 +59,7 @@ WORKLOADS = {
         prefill_block=128, decode=64, theta=500000.0, batch=8, seed_warmup=False,
         needles=dict(n_needles=16)),
     # the whole-box configuration's single sequence with its 8 KV heads split
-    # over the GPUs (run at a reduced length; ``bench.py --workload
-    # head-sharded``)
+    # over the GPUs, run at a reduced length
     "head-sharded-kv": dict(
         name="head-sharded-kv", layers=32, kv_heads=8, head_dim=128, q_heads=32, tokens=8192,
         config_tokens=131072, chunk=2048, rank=128, hh=1024, sinks=4, ring=256, absorb=16,
