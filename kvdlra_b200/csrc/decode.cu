@@ -1483,6 +1483,298 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_umma_kernel(DecArgs a, 
   }
 }
 
+// ------------------------------------------------------------------
+// The middle tier on the 5th-generation tensor cores for ranks 33..128
+// (bf16 caches, head_dim 64 or 128).  The basis of every KV group no longer
+// fits shared memory beside a tile's coordinates, so a CTA takes 128 features
+// (one group at head_dim 128, two at 64) and K = 64 or 128 staged rank
+// columns: the key rebuild of a 128-token tile is K/8 kind::tf32 MMAs of
+// 128 x 128 x 8 into 128 TMEM columns.  One buffer each holds a tile's key
+// and value coordinates: the next tile's keys land while this tile's scores
+// are formed (issued once its MMA has read the keys), its values while the
+// next tile's MMA and scores run.  The CTA's (group, 16-frequency block)
+// units are four at both head dims: quarter q of the warps (warps 4q..4q+3
+// cover the 128 TMEM lanes, one token per thread) takes unit q, forms the
+// rotary angles of its token in registers while the MMA runs, rotates its
+// 16 frequency pairs and writes partial scores for the group's query heads;
+// the partials of a head are summed in a fixed order.  Softmax, value product
+// and partial records as in decode_mid_umma_kernel.
+constexpr int kDwN = 128;     // features per CTA
+constexpr int kDwMaxHq = 16;  // query heads per CTA
+
+struct DwSmem { int us, ck, cv, ldv, qs, pp, st, posb, bar, total; };  // bytes
+__host__ __device__ inline DwSmem dw_smem(int K, int Hq, int D) {
+  DwSmem m;
+  m.ldv = K + 4;
+  m.us = 0;                                  // [128 features][K] basis, core-matrix layout
+  m.ck = m.us + kDwN * K * 4;                // [128 tokens][K] key coordinates, core-matrix layout
+  m.cv = m.ck + kDuTok * K * 4;              // [128 tokens][ldv] value coordinates
+  m.qs = m.cv + kDuTok * m.ldv * 4;          // [Hq][D] queries
+  m.pp = m.qs + Hq * D * 4;                  // [4 quarters][Hq][128] partial scores; quarter 0's
+                                             // slots then hold the scores and probabilities; at
+                                             // the end the value-product halves [256][4]
+  const int pp_bytes = 4 * Hq * kDuTok * 4;
+  m.st = m.pp + (pp_bytes > 256 * 16 ? pp_bytes : 256 * 16);  // [Hq][4]: running max, correction
+  m.posb = m.st + Hq * 16;                   // 2 x [128] positions
+  m.bar = m.posb + 2 * kDuTok * 4;           // mbarrier, TMEM base
+  m.total = m.bar + 16;
+  return m;
+}
+
+template <int K>
+__device__ __forceinline__ int dw_off(int row, int k) {  // core-matrix byte offset, K columns
+  return (row >> 3) * (K * 32) + (k >> 2) * 128 + (row & 7) * 16 + (k & 3) * 4;
+}
+
+template <int D, int K>
+__global__ void __launch_bounds__(kDuThreads) decode_mid_wide_kernel(DecArgs a, int tpc, int chunk0,
+                                                                     int* status) {
+  constexpr int HALF = D / 2, HB = kDwN / D, FB = HALF / 16;
+  static_assert(HB * FB == 4, "one (group, frequency block) unit per quarter of the warps");
+  extern __shared__ __align__(1024) unsigned char dsm5[];
+  const int nsg = a.H / HB;
+  const int p = blockIdx.y / nsg, g0 = (blockIdx.y % nsg) * HB;  // this CTA's groups [g0, g0 + HB)
+  const int G = a.G, Hq = HB * a.G, ld = a.ld;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int r_k = a.rk[p];
+  const DwSmem L = dw_smem(K, Hq, D);
+  unsigned char* us = dsm5 + L.us;
+  unsigned char* ckb = dsm5 + L.ck;
+  float* cvb = reinterpret_cast<float*>(dsm5 + L.cv);
+  float* qs = reinterpret_cast<float*>(dsm5 + L.qs);
+  float* pp = reinterpret_cast<float*>(dsm5 + L.pp);
+  float* ps = pp;  // the scores overwrite quarter 0's partials in place
+  float* st = reinterpret_cast<float*>(dsm5 + L.st);
+  int* posb = reinterpret_cast<int*>(dsm5 + L.posb);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(dsm5 + L.bar);
+  uint32_t* tbase = reinterpret_cast<uint32_t*>(dsm5 + L.bar + 8);
+  const int ldv = L.ldv;
+  const int nm = (a.W + kDuTok - 1) / kDuTok;
+  const int t_begin = blockIdx.x * tpc, t_end = min(nm, t_begin + tpc);
+  if (warp == 0) {
+    umma::tmem_alloc(tbase, kDwN);
+    umma::tmem_relinquish();
+  }
+  if (tid == 0) {
+    umma::mbar_init(bar, 1);
+    umma::mbar_fence_init();
+  }
+  {  // the basis rows of the CTA's groups (K-major core matrices, TF32, columns past the rank zero)
+    const float* U = a.uk + p * a.u_sp + (long)g0 * D * ld;
+    for (int e = tid; e < kDwN * (K / 4); e += kDuThreads) {
+      const int row = e / (K / 4), k = 4 * (e % (K / 4));
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (k < r_k) {  // r_k <= ld and ld % 4 == 0: the vector stays inside the row
+        v = *reinterpret_cast<const float4*>(U + (long)row * ld + k);
+        if (k + 1 >= r_k) v.y = 0.f;
+        if (k + 2 >= r_k) v.z = 0.f;
+        if (k + 3 >= r_k) v.w = 0.f;
+      }
+      *reinterpret_cast<float4*>(us + dw_off<K>(row, k)) =
+          make_float4(umma::to_tf32(v.x), umma::to_tf32(v.y), umma::to_tf32(v.z), umma::to_tf32(v.w));
+    }
+  }
+  const __nv_bfloat16* qp = reinterpret_cast<const __nv_bfloat16*>(a.q) + ((long)p * a.Hq + g0 * G) * D;
+  for (int e = tid; e < Hq * D; e += kDuThreads) qs[e] = __bfloat162float(qp[e]);
+  for (int h = tid; h < Hq; h += kDuThreads) st[4 * h] = -INFINITY;
+  // key coordinates straight into the MMA's layout (columns past ld zero-filled
+  // without a read, as are rows past the middle) and the tile's positions
+  auto prefetch_k = [&](int tile, int pb) {
+    const int j0 = tile * kDuTok, ntok = min(kDuTok, a.W - j0);
+    const float* Ck = a.ck + p * a.c_sp + (long)j0 * ld;
+    for (int e = tid; e < kDuTok * (K / 4); e += kDuThreads) {
+      const int row = e / (K / 4), k = 4 * (e % (K / 4));
+      const bool ok = row < ntok && k < ld;
+      cp16_zfill(ckb + dw_off<K>(row, k), Ck + (ok ? (long)row * ld + k : 0), ok);
+    }
+    if (tid < kDuTok)
+      posb[pb * kDuTok + tid] =
+          tid < ntok ? (a.mid_pos ? a.mid_pos[p * a.mid_sp + j0 + tid] : a.pos_base + j0 + tid) : 0;
+    cp_async_commit();
+  };
+  auto prefetch_v = [&](int tile) {
+    const int j0 = tile * kDuTok, ntok = min(kDuTok, a.W - j0);
+    const float* Cv = a.cv + p * a.c_sp + (long)j0 * ld;
+    const int l4 = ld / 4;
+    for (int e = tid; e < kDuTok * l4; e += kDuThreads) {
+      const int row = e / l4, k = 4 * (e % l4);
+      const bool ok = row < ntok;
+      cp16_zfill(cvb + row * ldv + k, Cv + (ok ? (long)row * ld + k : 0), ok);
+    }
+    cp_async_commit();
+  };
+  if (t_begin < t_end) {
+    prefetch_k(t_begin, 0);
+    prefetch_v(t_begin);
+  }
+  umma::fence_before_sync();
+  __syncthreads();
+  umma::fence_after_sync();
+  const uint32_t tmem = *tbase;
+  const uint32_t us_addr = (uint32_t)__cvta_generic_to_shared(us);
+  const uint32_t ck_addr = (uint32_t)__cvta_generic_to_shared(ckb);
+  constexpr uint32_t idesc = umma::idesc_tf32(kDuTok, kDwN);
+  // value product: thread (vh, vc) of token half th accumulates acc_c[vh][vc..vc+4)
+  const int nvq = ld / 4;
+  const int th = tid >> 8, vt = tid & 255;
+  const int vh = vt / nvq, vc = 4 * (vt % nvq);
+  const bool vown = vh < Hq;
+  float vacc[4] = {0.f, 0.f, 0.f, 0.f};
+  float lrow = 0.f;  // running sum of row `warp` (rows < Hq <= 16)
+  uint32_t phase = 0;
+  bool ok_wait = true;
+  const int tok = 32 * (warp & 3) + lane;  // this thread's TMEM lane (token of the tile)
+  const int unit = warp >> 2;              // this quarter's (group, frequency block)
+  const int ug = unit / FB, f0 = 16 * (unit % FB);
+  const float4* qs4 = reinterpret_cast<const float4*>(qs);
+  for (int tile = t_begin; tile < t_end; ++tile) {
+    const int pb = (tile - t_begin) & 1;
+    const int j0 = tile * kDuTok, ntok = min(kDuTok, a.W - j0);
+    const bool more = tile + 1 < t_end;
+    asm volatile("cp.async.wait_group 1;\n" ::: "memory");  // the keys (the values may still land)
+    umma::fence_proxy_async_smem();
+    __syncthreads();
+    if (tid == 0) {
+      umma::fence_after_sync();
+#pragma unroll
+      for (int j = 0; j < K / 8; ++j)
+        umma::mma_tf32(tmem, umma::smem_desc(ck_addr + 256 * j, 128, 32 * K),
+                       umma::smem_desc(us_addr + 256 * j, 128, 32 * K), idesc, j > 0);
+      umma::commit(bar);
+    }
+    // this thread's rotary angles while the MMA runs
+    float cs[16], sn[16];
+    {
+      const int pos = posb[pb * kDuTok + tok];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) rope_cs_fast(pos, a.inv_freq[f0 + i], a.rope_scale, &cs[i], &sn[i]);
+    }
+    ok_wait = umma::mbar_wait_bounded(bar, phase, kDuWaitPolls);
+    phase ^= 1;
+    ok_wait = __syncthreads_and(ok_wait);
+    umma::fence_after_sync();
+    if (!ok_wait) break;
+    if (more) prefetch_k(tile + 1, pb ^ 1);  // the MMA has read the keys
+    {
+      const uint32_t trow = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
+      float x1[16], x2[16];
+      umma::tmem_ld16(trow + ug * D + f0, x1);
+      umma::tmem_ld16(trow + ug * D + HALF + f0, x2);
+      umma::tmem_wait_ld();
+      float2 y1[8], y2[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {  // RoPE on frequency pairs: y1 = x1 c - x2 s, y2 = x2 c + x1 s
+        const float2 X1 = make_float2(x1[2 * i], x1[2 * i + 1]), X2 = make_float2(x2[2 * i], x2[2 * i + 1]);
+        const float2 C = make_float2(cs[2 * i], cs[2 * i + 1]), S = make_float2(sn[2 * i], sn[2 * i + 1]);
+        const float2 t1 = __fmul2_rn(X2, S), t2 = __fmul2_rn(X1, S);
+        y1[i] = __ffma2_rn(X1, C, make_float2(-t1.x, -t1.y));
+        y2[i] = __ffma2_rn(X2, C, t2);
+      }
+#pragma unroll
+      for (int qh = 0; qh < kMaxG; ++qh) {
+        if (qh < G) {
+          const int h = ug * G + qh;
+          const float4* qa = qs4 + h * (D / 4) + f0 / 4;
+          const float4* qb = qa + HALF / 4;
+          float2 u1 = make_float2(0.f, 0.f), u2 = u1;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float4 u = qa[i], w = qb[i];
+            u1 = __ffma2_rn(y1[2 * i], make_float2(u.x, u.y), u1);
+            u2 = __ffma2_rn(y2[2 * i], make_float2(w.x, w.y), u2);
+            u1 = __ffma2_rn(y1[2 * i + 1], make_float2(u.z, u.w), u1);
+            u2 = __ffma2_rn(y2[2 * i + 1], make_float2(w.z, w.w), u2);
+          }
+          pp[(unit * Hq + h) * kDuTok + tok] = (u1.x + u1.y) + (u2.x + u2.y);
+        }
+      }
+    }
+    umma::fence_before_sync();
+    __syncthreads();
+    // a head's score: its group's FB partials in block order, scaled
+    for (int e = tid; e < Hq * kDuTok; e += kDuThreads) {
+      const int h = e / kDuTok, t = e % kDuTok, u0 = (h / G) * FB;
+      float sc = pp[(u0 * Hq + h) * kDuTok + t];
+#pragma unroll
+      for (int b = 1; b < FB; ++b) sc += pp[((u0 + b) * Hq + h) * kDuTok + t];
+      ps[h * kDuTok + t] = t < ntok ? sc * a.scaling : -INFINITY;
+    }
+    __syncthreads();
+    // softmax per query head over the tile, online across tiles (warp owns row `warp`)
+    if (warp < Hq) {
+      float* pr = ps + warp * kDuTok;
+      const float x0 = pr[lane], x1 = pr[lane + 32], x2 = pr[lane + 64], x3 = pr[lane + 96];
+      float mt = fmaxf(fmaxf(x0, x1), fmaxf(x2, x3));
+      mt = warp_max(mt);
+      const float mold = st[4 * warp];
+      const float mnew = fmaxf(mold, mt);
+      const float e0 = mnew == -INFINITY ? 0.f : expf(x0 - mnew);
+      const float e1 = mnew == -INFINITY ? 0.f : expf(x1 - mnew);
+      const float e2 = mnew == -INFINITY ? 0.f : expf(x2 - mnew);
+      const float e3 = mnew == -INFINITY ? 0.f : expf(x3 - mnew);
+      pr[lane] = e0; pr[lane + 32] = e1; pr[lane + 64] = e2; pr[lane + 96] = e3;
+      const float ls = warp_sum((e0 + e1) + (e2 + e3));
+      const float corr = mold == -INFINITY ? 0.f : expf(mold - mnew);
+      lrow = lrow * corr + ls;
+      __syncwarp();
+      if (lane == 0) {
+        st[4 * warp] = mnew;
+        st[4 * warp + 1] = corr;
+      }
+    }
+    // the values of this tile (the next tile's keys may still land)
+    if (more) asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+    else asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+    __syncthreads();
+    if (vown) {  // acc_c[vh][vc..vc+4) = corr * acc + sum_t p[vh][t] c_v[t][vc..] over this half
+      const float corr = st[4 * vh + 1];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) vacc[j] *= corr;
+      const float* pr = ps + vh * kDuTok + 64 * th;
+      const float* cvh = cvb + 64 * th * ldv;
+#pragma unroll 8
+      for (int t = 0; t < 64; ++t) {
+        const float pt = pr[t];
+        const float4 cvv = *reinterpret_cast<const float4*>(cvh + t * ldv + vc);
+        vacc[0] = fmaf(pt, cvv.x, vacc[0]);
+        vacc[1] = fmaf(pt, cvv.y, vacc[1]);
+        vacc[2] = fmaf(pt, cvv.z, vacc[2]);
+        vacc[3] = fmaf(pt, cvv.w, vacc[3]);
+      }
+    }
+    __syncthreads();  // the value buffer is free
+    if (more) prefetch_v(tile + 1);
+  }
+  asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+  if (!ok_wait) {
+    if (tid == 0) atomicOr(&status[kStatusTimeout], 16);
+    umma::mbar_wait_bounded(bar, phase ^ 1, kDuWaitPolls);
+  }
+  __syncthreads();  // every product has read the probabilities before their slots take the halves
+  float* vred = pp;
+  if (th == 1 && vown)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) vred[vt * 4 + j] = vacc[j];
+  __syncthreads();
+  if (warp == 0) umma::tmem_dealloc(tmem, kDwN);
+  // one partial record per group: m[G], l[G], acc_d[G][D] = 0, acc_c[G][ld]
+  const int chunk = chunk0 + blockIdx.x;
+  auto rec = [&](int g) {  // g: this CTA's group index
+    return a.part + ((long)(p * a.H + g0 + g) * a.n_chunks + chunk) * a.part_sp_chunk;
+  };
+  if (warp < Hq && lane == 0) {
+    float* o = rec(warp / G);
+    o[warp % G] = (t_begin < t_end && ok_wait) ? st[4 * warp] : -INFINITY;
+    o[G + warp % G] = ok_wait ? lrow : 0.f;
+  }
+  for (int e = tid; e < HB * G * D; e += kDuThreads) rec(e / (G * D))[2 * G + e % (G * D)] = 0.f;
+  if (th == 0 && vown) {
+    float* o = rec(vh / G) + 2 * G + G * D + (vh % G) * ld + vc;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) o[j] = ok_wait ? vacc[j] + vred[vt * 4 + j] : 0.f;
+  }
+}
+
 template <typename T>
 int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_counters& k, int p0,
                            int count, int h0, int hc, const void* q, int Hq, float scaling, void* out,
@@ -1560,7 +1852,18 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
                         (reinterpret_cast<uintptr_t>(a.cv) & 15) == 0 &&
                         (reinterpret_cast<uintptr_t>(a.uk) & 15) == 0 &&
                         du_smem(du_n, du_hq, a.D).total <= device_smem_optin();
-  if (mid_all || umma_mid) {
+  // bf16, head_dim 64 or 128, rank 33..128: the middle tier on tcgen05 with
+  // 128 features per CTA (decode_mid_wide_kernel)
+  const int dw_K = a.ld <= 64 ? 64 : 128, dw_hb = (a.D == 64 || a.D == 128) ? kDwN / a.D : 1;
+  const int dw_hq = dw_hb * a.G;
+  const bool umma_wide = !umma_mid && sizeof(T) == 2 && (a.D == 64 || a.D == 128) && mma && a.W > 0 &&
+                         a.ld > 32 && a.ld <= 128 && a.ld % 4 == 0 && a.H % dw_hb == 0 &&
+                         dw_hq <= kDwMaxHq && dw_hq * (a.ld / 4) <= 256 && a.c_sp % 4 == 0 &&
+                         (reinterpret_cast<uintptr_t>(a.ck) & 15) == 0 &&
+                         (reinterpret_cast<uintptr_t>(a.cv) & 15) == 0 &&
+                         (reinterpret_cast<uintptr_t>(a.uk) & 15) == 0 &&
+                         dw_smem(dw_K, dw_hq, a.D).total <= device_smem_optin();
+  if (mid_all || umma_mid || umma_wide) {
     const int nvt = nv0 + nr;
     const int n_vch = nvt;  // one verbatim tile per CTA
     // tiles per CTA: one CTA fills an SM, so the launch takes
@@ -1574,11 +1877,12 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
         if (sm_count[dev] > 0) sms = sm_count[dev];
       }
     }
-    const int ttok = umma_mid ? kDuTok : kTT;
+    const bool umma = umma_mid || umma_wide;
+    const int ttok = umma ? kDuTok : kTT;
     const int nmt = (a.W + ttok - 1) / ttok;
-    int tpc = umma_mid ? 1 : 2;
+    int tpc = umma ? 1 : 2;
     long best = -1;
-    const int nsg = umma_mid ? a.H / du_hb : 1;  // CTAs per tile (group ranges)
+    const int nsg = umma_mid ? a.H / du_hb : umma_wide ? a.H / dw_hb : 1;  // CTAs per tile (group ranges)
     for (int t = tpc; t <= 8; ++t) {
       const long waves = ((long)((nmt + t - 1) / t) * count * nsg + sms - 1) / sms;
       const long cost = waves * (2 * t + 1);
@@ -1590,7 +1894,7 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
     if (need2 > ws_bytes) { set_error("factored decode: workspace too small"); return KVD_ERR_WORKSPACE; }
     constexpr bool kSplit = sizeof(T) == 4;
     auto mid_fn = a.D == 64 ? decode_mid_kernel<T, 64, kSplit> : decode_mid_kernel<T, 128, kSplit>;
-    if (!umma_mid)
+    if (!umma)
       if (int rc0 = ensure_smem((const void*)mid_fn, 4 * ms.total, "decode_mid_kernel")) return rc0;
     // the verbatim tiles run beside the middle tier (disjoint partial records)
     const bool fork = side && ev_fork && ev_join && n_vch > 0;
@@ -1625,6 +1929,16 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
       }
       KTimerScope kts_("decode_mid_kernel", s);
       ufn<<<dim3(n_mch, count * nsg), kDuThreads, dsm, s>>>(a, tpc, n_vch, a.status);
+    } else if (umma_wide) {
+      const int dsm = dw_smem(dw_K, dw_hq, a.D).total;
+      auto wfn = a.D == 64 ? (dw_K == 64 ? decode_mid_wide_kernel<64, 64> : decode_mid_wide_kernel<64, 128>)
+                           : (dw_K == 64 ? decode_mid_wide_kernel<128, 64> : decode_mid_wide_kernel<128, 128>);
+      if (int rc0 = ensure_smem((const void*)wfn, dsm, "decode_mid_kernel")) {
+        if (fork) cudaStreamWaitEvent(s, ev_join, 0);
+        return rc0;
+      }
+      KTimerScope kts_("decode_mid_kernel", s);
+      wfn<<<dim3(n_mch, count * nsg), kDuThreads, dsm, s>>>(a, tpc, n_vch, a.status);
     } else {
       KTimerScope kts_("decode_mid_kernel", s);
       mid_fn<<<dim3(n_mch, count), kMidThreads, 4 * ms.total, s>>>(a, tpc, n_vch);

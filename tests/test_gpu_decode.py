@@ -29,6 +29,42 @@ def _rel(a: np.ndarray, b: np.ndarray) -> float:
     return float(np.abs(a.astype(np.float64) - b).max() / max(np.abs(b).max(), 1e-30))
 
 
+@pytest.mark.parametrize("H,D,G,T,rank", [
+    (8, 128, 4, 1300, 128),  # tcgen05 middle tier, 128 rank columns, one group per CTA
+    (4, 128, 8, 900, 64),    # 64 rank columns
+    (4, 64, 4, 1100, 96),    # two groups of 64 per CTA, rank 96 in 128 columns
+    (2, 64, 8, 700, 128),    # 16 query heads per CTA
+    (8, 64, 2, 1000, 40),
+])
+def test_factored_decode_wide_rank_bf16(H: int, D: int, G: int, T: int, rank: int) -> None:
+    """Ranks 33..128 in bf16 (the whole-box and decode-sweep ranks): the
+    middle tier on the tensor cores with the basis staged in 64 or 128 rank
+    columns, against dense attention over the peek within the bf16 rule."""
+    s = lowrank_stream(H, D, T, n_needles=5, seed=H * 7 + D + rank, signal_rank=min(D, max(16, rank // H + 8)))
+    inv = default_inv_freq(D, 500000.0)
+    layer = BugStreamingLayer(RopeAngles(inv_freq=torch.from_numpy(inv), attention_scaling=1.0),
+                              rank=rank, coord_budget=T + 200, recent_window=96, absorb_block=16,
+                              n_sink=4, retention="lowrank_surprise", hh_budget=70,
+                              hh_select="surprise")
+    layer._mode = "ingest"
+    k = torch.from_numpy(s.k_post)[None].to(DEV, torch.bfloat16)
+    v = torch.from_numpy(s.v)[None].to(DEV, torch.bfloat16)
+    for st in range(0, T, 128):
+        layer.update(k[:, :, st : st + 128], v[:, :, st : st + 128])
+        layer.consolidate()
+    kr, vr = layer._decode_peek()
+    kd = kr[0].float().cpu().numpy()
+    vd = vr[0].float().cpu().numpy()
+    assert layer._ranks()[0] > 32  # the basis grew past 32 columns
+    rng = np.random.default_rng(T + rank)
+    for _ in range(3):
+        q = torch.from_numpy(rng.standard_normal((H * G, D)).astype(np.float32)).to(DEV, torch.bfloat16)
+        out = layer.factored_attention(q[None])[0].float().cpu().numpy()
+        ref = gqa_attention(q.float().cpu().numpy(), kd, vd)
+        assert _rel(out, ref) < 2e-2, _rel(out, ref)
+    layer._group.check_status()
+
+
 @pytest.mark.parametrize("H,D,G,T,dtype", [
     (2, 128, 8, 1000, torch.float32),
     (4, 64, 4, 777, torch.float32),
