@@ -498,13 +498,14 @@ __global__ void __launch_bounds__(kTileThreads) decode_mma_kernel(DecArgs a, int
   const int r_k = a.rk[p], r_v = a.rv[p];
   const int ldc = ld + 4;  // key coordinates / basis rows: fragment reads (4g + t) conflict-free
   const int ldv = ld + 8;  // value coordinates: fragment reads (8t + g) conflict-free
-  const int vsz = kTT * (ldk > ldv ? ldk : ldv);
+  // a launch without middle tiles (nm == 0) holds no coordinates or basis
+  const int vsz = kTT * (nm > 0 && ldv > ldk ? ldv : ldk);
   float* qs = tsm;              // [G][D]
   float* ks = qs + G * D;       // [kTT][ldk] keys | [kTT][ldc] key coordinates
   float* vs = ks + kTT * ldk;   // [kTT][ldk] values | [kTT][ldv] value coordinates
   float* ps = vs + vsz;         // [G][ldps] scores, then probabilities
-  float* us = ps + G * ldps;    // [D][ldc] U_k,g rows
-  float* st = us + D * ldc;     // [G][4] -, -, running max, rescale of the tile
+  float* us = ps + G * ldps;    // [D][ldc] U_k,g rows (middle tiles only)
+  float* st = us + (nm > 0 ? D * ldc : 0);  // [G][4] -, -, running max, rescale of the tile
   const T* qp = reinterpret_cast<const T*>(a.q) + (long)p * a.Hq * D;
   for (int e = tid; e < G * D; e += kTileThreads) qs[e] = load_f<T>(qp + (long)(g * G + e / D) * D + e % D);
   if (tid < G) st[4 * tid + 2] = -INFINITY;
@@ -1899,9 +1900,9 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
     // the verbatim tiles run beside the middle tier (disjoint partial records)
     const bool fork = side && ev_fork && ev_join && n_vch > 0;
     if (n_vch > 0) {
-      const int ldk = a.D + 4, ldv = a.ld + 8, ldc = a.ld + 4;
-      const int tsmem = 4 * (a.G * a.D + kTT * ldk + kTT * (ldk > ldv ? ldk : ldv) +
-                             a.G * (kTT + 4) + a.D * ldc + 4 * a.G);
+      // no middle tiles in this launch: keys and values of a tile, no coordinates or basis
+      const int ldk = a.D + 4;
+      const int tsmem = 4 * (a.G * a.D + 2 * kTT * ldk + a.G * (kTT + 4) + 4 * a.G);
       auto fn = a.D == 64 ? decode_mma_kernel<T, 64, kSplit> : decode_mma_kernel<T, 128, kSplit>;
       if (int rc0 = ensure_smem((const void*)fn, tsmem, "decode_mma_kernel")) return rc0;
       cudaStream_t vs = s;
