@@ -739,7 +739,9 @@ __global__ void __launch_bounds__(kTileThreads) decode_mma_kernel(DecArgs a, int
     if (o >= n_outd) break;
     out[2 * G + o] = acc[k];
   }
-  if (gq < G) {
+  if (nm == 0) {  // no middle tiles: acc_c is zero (at any rank)
+    for (int e = tid; e < G * ld; e += kTileThreads) out[2 * G + G * D + e] = 0.f;
+  } else if (gq < G) {
 #pragma unroll
     for (int i = 0; i < kMaxCT; ++i) {
       const int ct = warp + 4 * i;
@@ -1227,7 +1229,10 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_umma_kernel(DecArgs a, 
   constexpr int HALF = D / 2;
   extern __shared__ __align__(1024) unsigned char dsm4[];
   const int hb = du_groups(a.H, D), nsg = a.H / hb;
-  const int p = blockIdx.y / nsg, g0 = (blockIdx.y % nsg) * hb;  // this CTA's groups [g0, g0 + hb)
+  // group ranges fastest: the CTAs that read one coordinate tile run together
+  // and share it through L2
+  const int cx = blockIdx.x / nsg;                         // tile range
+  const int p = blockIdx.y, g0 = (blockIdx.x % nsg) * hb;  // this CTA's groups [g0, g0 + hb)
   const int H = hb, G = a.G, Hq = hb * a.G, ld = a.ld, n = hb * D;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int r_k = a.rk[p];
@@ -1247,7 +1252,7 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_umma_kernel(DecArgs a, 
   uint32_t* tbase = reinterpret_cast<uint32_t*>(dsm4 + L.bar + 8);
   const int ldv = L.ldv;
   const int nm = (a.W + kDuTok - 1) / kDuTok;
-  const int t_begin = blockIdx.x * tpc, t_end = min(nm, t_begin + tpc);
+  const int t_begin = cx * tpc, t_end = min(nm, t_begin + tpc);
   if (warp == 0) {
     umma::tmem_alloc(tbase, 512);
     umma::tmem_relinquish();
@@ -1463,7 +1468,7 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_umma_kernel(DecArgs a, 
   __syncthreads();
   if (warp == 0) umma::tmem_dealloc(tmem, 512);
   // one partial record per group: m[G], l[G], acc_d[G][D] = 0, acc_c[G][ld]
-  const int chunk = chunk0 + blockIdx.x;
+  const int chunk = chunk0 + cx;
   auto rec = [&](int g) {  // g: this CTA's group index
     return a.part + ((long)(p * a.H + g0 + g) * a.n_chunks + chunk) * a.part_sp_chunk;
   };
@@ -1485,15 +1490,17 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_umma_kernel(DecArgs a, 
 }
 
 // ------------------------------------------------------------------
-// The middle tier on the 5th-generation tensor cores for ranks 33..128
+// The middle tier on the 5th-generation tensor cores for ranks 33..192
 // (bf16 caches, head_dim 64 or 128).  The basis of every KV group no longer
 // fits shared memory beside a tile's coordinates, so a CTA takes 128 features
-// (one group at head_dim 128, two at 64) and K = 64 or 128 staged rank
+// (one group at head_dim 128, two at 64) and K = 64, 128 or 192 staged rank
 // columns: the key rebuild of a 128-token tile is K/8 kind::tf32 MMAs of
-// 128 x 128 x 8 into 128 TMEM columns.  One buffer each holds a tile's key
-// and value coordinates: the next tile's keys land while this tile's scores
-// are formed (issued once its MMA has read the keys), its values while the
-// next tile's MMA and scores run.  The CTA's (group, 16-frequency block)
+// 128 x 128 x 8 into 128 TMEM columns.  Up to K = 128 one buffer each holds
+// a tile's key and value coordinates: the next tile's keys land while this
+// tile's scores are formed (issued once its MMA has read the keys), its
+// values while the next tile's MMA and scores run.  At K = 192 one buffer
+// holds both in turn: the values land while the scores are formed, the next
+// tile's keys after the value product.  The CTA's (group, 16-frequency block)
 // units are four at both head dims: quarter q of the warps (warps 4q..4q+3
 // cover the 128 TMEM lanes, one token per thread) takes unit q, forms the
 // rotary angles of its token in registers while the MMA runs, rotates its
@@ -1504,12 +1511,14 @@ constexpr int kDwN = 128;     // features per CTA
 constexpr int kDwMaxHq = 16;  // query heads per CTA
 
 struct DwSmem { int us, ck, cv, ldv, qs, pp, st, posb, bar, total; };  // bytes
+__host__ __device__ constexpr bool dw_one_buffer(int K) { return K > 128; }
 __host__ __device__ inline DwSmem dw_smem(int K, int Hq, int D) {
   DwSmem m;
   m.ldv = K + 4;
   m.us = 0;                                  // [128 features][K] basis, core-matrix layout
   m.ck = m.us + kDwN * K * 4;                // [128 tokens][K] key coordinates, core-matrix layout
-  m.cv = m.ck + kDuTok * K * 4;              // [128 tokens][ldv] value coordinates
+  // [128 tokens][ldv] value coordinates (in the key buffer at K > 128)
+  m.cv = dw_one_buffer(K) ? m.ck : m.ck + kDuTok * K * 4;
   m.qs = m.cv + kDuTok * m.ldv * 4;          // [Hq][D] queries
   m.pp = m.qs + Hq * D * 4;                  // [4 quarters][Hq][128] partial scores; quarter 0's
                                              // slots then hold the scores and probabilities; at
@@ -1531,10 +1540,14 @@ template <int D, int K>
 __global__ void __launch_bounds__(kDuThreads) decode_mid_wide_kernel(DecArgs a, int tpc, int chunk0,
                                                                      int* status) {
   constexpr int HALF = D / 2, HB = kDwN / D, FB = HALF / 16;
+  constexpr bool kOne = dw_one_buffer(K);
   static_assert(HB * FB == 4, "one (group, frequency block) unit per quarter of the warps");
   extern __shared__ __align__(1024) unsigned char dsm5[];
   const int nsg = a.H / HB;
-  const int p = blockIdx.y / nsg, g0 = (blockIdx.y % nsg) * HB;  // this CTA's groups [g0, g0 + HB)
+  // group ranges fastest: the CTAs that read one coordinate tile run together
+  // and share it through L2
+  const int cx = blockIdx.x / nsg;                         // tile range
+  const int p = blockIdx.y, g0 = (blockIdx.x % nsg) * HB;  // this CTA's groups [g0, g0 + HB)
   const int G = a.G, Hq = HB * a.G, ld = a.ld;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int r_k = a.rk[p];
@@ -1551,7 +1564,7 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_wide_kernel(DecArgs a, 
   uint32_t* tbase = reinterpret_cast<uint32_t*>(dsm5 + L.bar + 8);
   const int ldv = L.ldv;
   const int nm = (a.W + kDuTok - 1) / kDuTok;
-  const int t_begin = blockIdx.x * tpc, t_end = min(nm, t_begin + tpc);
+  const int t_begin = cx * tpc, t_end = min(nm, t_begin + tpc);
   if (warp == 0) {
     umma::tmem_alloc(tbase, kDwN);
     umma::tmem_relinquish();
@@ -1606,7 +1619,7 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_wide_kernel(DecArgs a, 
   };
   if (t_begin < t_end) {
     prefetch_k(t_begin, 0);
-    prefetch_v(t_begin);
+    if (!kOne) prefetch_v(t_begin);
   }
   umma::fence_before_sync();
   __syncthreads();
@@ -1632,7 +1645,8 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_wide_kernel(DecArgs a, 
     const int pb = (tile - t_begin) & 1;
     const int j0 = tile * kDuTok, ntok = min(kDuTok, a.W - j0);
     const bool more = tile + 1 < t_end;
-    asm volatile("cp.async.wait_group 1;\n" ::: "memory");  // the keys (the values may still land)
+    if (kOne) asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+    else asm volatile("cp.async.wait_group 1;\n" ::: "memory");  // the keys (the values may still land)
     umma::fence_proxy_async_smem();
     __syncthreads();
     if (tid == 0) {
@@ -1655,7 +1669,8 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_wide_kernel(DecArgs a, 
     ok_wait = __syncthreads_and(ok_wait);
     umma::fence_after_sync();
     if (!ok_wait) break;
-    if (more) prefetch_k(tile + 1, pb ^ 1);  // the MMA has read the keys
+    if (kOne) prefetch_v(tile);                   // the MMA has read the keys: the values in their place
+    else if (more) prefetch_k(tile + 1, pb ^ 1);
     {
       const uint32_t trow = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
       float x1[16], x2[16];
@@ -1724,7 +1739,7 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_wide_kernel(DecArgs a, 
       }
     }
     // the values of this tile (the next tile's keys may still land)
-    if (more) asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+    if (more && !kOne) asm volatile("cp.async.wait_group 1;\n" ::: "memory");
     else asm volatile("cp.async.wait_group 0;\n" ::: "memory");
     __syncthreads();
     if (vown) {  // acc_c[vh][vc..vc+4) = corr * acc + sum_t p[vh][t] c_v[t][vc..] over this half
@@ -1744,7 +1759,10 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_wide_kernel(DecArgs a, 
       }
     }
     __syncthreads();  // the value buffer is free
-    if (more) prefetch_v(tile + 1);
+    if (more) {
+      if (kOne) prefetch_k(tile + 1, pb ^ 1);
+      else prefetch_v(tile + 1);
+    }
   }
   asm volatile("cp.async.wait_group 0;\n" ::: "memory");
   if (!ok_wait) {
@@ -1759,7 +1777,7 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_wide_kernel(DecArgs a, 
   __syncthreads();
   if (warp == 0) umma::tmem_dealloc(tmem, kDwN);
   // one partial record per group: m[G], l[G], acc_d[G][D] = 0, acc_c[G][ld]
-  const int chunk = chunk0 + blockIdx.x;
+  const int chunk = chunk0 + cx;
   auto rec = [&](int g) {  // g: this CTA's group index
     return a.part + ((long)(p * a.H + g0 + g) * a.n_chunks + chunk) * a.part_sp_chunk;
   };
@@ -1855,10 +1873,12 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
                         du_smem(du_n, du_hq, a.D).total <= device_smem_optin();
   // bf16, head_dim 64 or 128, rank 33..128: the middle tier on tcgen05 with
   // 128 features per CTA (decode_mid_wide_kernel)
-  const int dw_K = a.ld <= 64 ? 64 : 128, dw_hb = (a.D == 64 || a.D == 128) ? kDwN / a.D : 1;
+  // (the verbatim tiles then go to decode_mma_kernel alone, at any rank)
+  const int dw_K = a.ld <= 64 ? 64 : (a.ld <= 128 ? 128 : 192);
+  const int dw_hb = (a.D == 64 || a.D == 128) ? kDwN / a.D : 1;
   const int dw_hq = dw_hb * a.G;
-  const bool umma_wide = !umma_mid && sizeof(T) == 2 && (a.D == 64 || a.D == 128) && mma && a.W > 0 &&
-                         a.ld > 32 && a.ld <= 128 && a.ld % 4 == 0 && a.H % dw_hb == 0 &&
+  const bool umma_wide = !umma_mid && sizeof(T) == 2 && (a.D == 64 || a.D == 128) && a.G <= 8 && a.W > 0 &&
+                         a.ld > 32 && a.ld <= 192 && a.ld % 4 == 0 && a.H % dw_hb == 0 &&
                          dw_hq <= kDwMaxHq && dw_hq * (a.ld / 4) <= 256 && a.c_sp % 4 == 0 &&
                          (reinterpret_cast<uintptr_t>(a.ck) & 15) == 0 &&
                          (reinterpret_cast<uintptr_t>(a.cv) & 15) == 0 &&
@@ -1929,17 +1949,20 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
         return rc0;
       }
       KTimerScope kts_("decode_mid_kernel", s);
-      ufn<<<dim3(n_mch, count * nsg), kDuThreads, dsm, s>>>(a, tpc, n_vch, a.status);
+      ufn<<<dim3(n_mch * nsg, count), kDuThreads, dsm, s>>>(a, tpc, n_vch, a.status);
     } else if (umma_wide) {
       const int dsm = dw_smem(dw_K, dw_hq, a.D).total;
-      auto wfn = a.D == 64 ? (dw_K == 64 ? decode_mid_wide_kernel<64, 64> : decode_mid_wide_kernel<64, 128>)
-                           : (dw_K == 64 ? decode_mid_wide_kernel<128, 64> : decode_mid_wide_kernel<128, 128>);
+      auto wfn = a.D == 64
+          ? (dw_K == 64 ? decode_mid_wide_kernel<64, 64>
+                        : dw_K == 128 ? decode_mid_wide_kernel<64, 128> : decode_mid_wide_kernel<64, 192>)
+          : (dw_K == 64 ? decode_mid_wide_kernel<128, 64>
+                        : dw_K == 128 ? decode_mid_wide_kernel<128, 128> : decode_mid_wide_kernel<128, 192>);
       if (int rc0 = ensure_smem((const void*)wfn, dsm, "decode_mid_kernel")) {
         if (fork) cudaStreamWaitEvent(s, ev_join, 0);
         return rc0;
       }
       KTimerScope kts_("decode_mid_kernel", s);
-      wfn<<<dim3(n_mch, count * nsg), kDuThreads, dsm, s>>>(a, tpc, n_vch, a.status);
+      wfn<<<dim3(n_mch * nsg, count), kDuThreads, dsm, s>>>(a, tpc, n_vch, a.status);
     } else {
       KTimerScope kts_("decode_mid_kernel", s);
       mid_fn<<<dim3(n_mch, count), kMidThreads, 4 * ms.total, s>>>(a, tpc, n_vch);

@@ -35,11 +35,14 @@ def _rel(a: np.ndarray, b: np.ndarray) -> float:
     (4, 64, 4, 1100, 96),    # two groups of 64 per CTA, rank 96 in 128 columns
     (2, 64, 8, 700, 128),    # 16 query heads per CTA
     (8, 64, 2, 1000, 40),
+    (8, 128, 4, 1300, 192),  # 192 rank columns: keys and values share one buffer
+    (4, 64, 2, 900, 160),
 ])
 def test_factored_decode_wide_rank_bf16(H: int, D: int, G: int, T: int, rank: int) -> None:
-    """Ranks 33..128 in bf16 (the whole-box and decode-sweep ranks): the
-    middle tier on the tensor cores with the basis staged in 64 or 128 rank
-    columns, against dense attention over the peek within the bf16 rule."""
+    """Ranks 33..192 in bf16 (the whole-box and decode-sweep ranks): the
+    middle tier on the tensor cores with the basis staged in 64, 128 or 192
+    rank columns, against dense attention over the peek within the bf16
+    rule."""
     s = lowrank_stream(H, D, T, n_needles=5, seed=H * 7 + D + rank, signal_rank=min(D, max(16, rank // H + 8)))
     inv = default_inv_freq(D, 500000.0)
     layer = BugStreamingLayer(RopeAngles(inv_freq=torch.from_numpy(inv), attention_scaling=1.0),
