@@ -1189,7 +1189,7 @@ constexpr int kDuThreads = 512;
 constexpr int kDuK = 32;  // staged rank columns (rank <= 32)
 constexpr long kDuWaitPolls = 1L << 22;
 
-struct DuSmem { int us, ck, cv, ldv, qs, cs, ps, st, vred, posb, bar, total; };  // bytes
+struct DuSmem { int us, ck, cv, ldv, qs, cs, ps, st, vred, posb, invf, bar, total; };  // bytes
 // n = this CTA's features (its KV groups x D), Hq = its query heads
 __host__ __device__ inline DuSmem du_smem(int n, int Hq, int D) {
   DuSmem m;
@@ -1203,7 +1203,8 @@ __host__ __device__ inline DuSmem du_smem(int n, int Hq, int D) {
   m.st = m.ps + Hq * kDuTok * 4;              // [Hq][4]: running max, correction
   m.vred = m.st + Hq * 16;                    // [256][4] value-product halves
   m.posb = m.vred + 256 * 16;                 // 2 x [128] positions
-  m.bar = m.posb + 2 * kDuTok * 4;            // mbarrier, TMEM base
+  m.invf = m.posb + 2 * kDuTok * 4;           // [D/2] inverse frequencies
+  m.bar = m.invf + (D / 2) * 4;               // mbarrier, TMEM base
   m.total = m.bar + 16;
   return m;
 }
@@ -1248,6 +1249,7 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_umma_kernel(DecArgs a, 
   float* st = reinterpret_cast<float*>(dsm4 + L.st);
   float* vred = reinterpret_cast<float*>(dsm4 + L.vred);
   int* posb = reinterpret_cast<int*>(dsm4 + L.posb);
+  float* invf = reinterpret_cast<float*>(dsm4 + L.invf);
   uint64_t* bar = reinterpret_cast<uint64_t*>(dsm4 + L.bar);
   uint32_t* tbase = reinterpret_cast<uint32_t*>(dsm4 + L.bar + 8);
   const int ldv = L.ldv;
@@ -1279,6 +1281,7 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_umma_kernel(DecArgs a, 
   const __nv_bfloat16* qp = reinterpret_cast<const __nv_bfloat16*>(a.q) + ((long)p * a.Hq + g0 * G) * D;
   for (int e = tid; e < Hq * D; e += kDuThreads) qs[e] = __bfloat162float(qp[e]);
   for (int h = tid; h < Hq; h += kDuThreads) st[4 * h] = -INFINITY;
+  if (tid < HALF) invf[tid] = a.inv_freq[tid];
   // a tile's coordinates land by cp.async straight into the MMA's layout (keys;
   // rank columns past the basis rank meet zero basis columns) and into a plain
   // pitch (values); rows past the middle are zero-filled without a read
@@ -1295,9 +1298,11 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_umma_kernel(DecArgs a, 
       cp16_zfill(ckb + du_off(row, k), Ck + off, ok);
       cp16_zfill(cvb + row * ldv + k, Cv + off, ok);
     }
-    if (tid < kDuTok)
-      posb[buf * kDuTok + tid] =
-          tid < ntok ? (a.mid_pos ? a.mid_pos[p * a.mid_sp + j0 + tid] : a.pos_base + j0 + tid) : 0;
+    if (tid < kDuTok) {  // positions copied asynchronously too: the issuing warps do not wait on them
+      int* pd = posb + buf * kDuTok + tid;
+      if (tid < ntok && a.mid_pos) cp_async4_dec(pd, a.mid_pos + p * a.mid_sp + j0 + tid);
+      else *pd = tid < ntok ? a.pos_base + j0 + tid : 0;
+    }
     cp_async_commit();
   };
   if (t_begin < t_end) prefetch(t_begin, 0);
@@ -1343,7 +1348,7 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_umma_kernel(DecArgs a, 
       const int pos = posb[buf * kDuTok + t];
       for (int f = tid / kDuTok; f < HALF; f += kDuThreads / kDuTok) {
         float c = 1.f, sn = 0.f;
-        if (live) rope_cs_fast(pos, a.inv_freq[f], a.rope_scale, &c, &sn);
+        if (live) rope_cs_fast(pos, invf[f], a.rope_scale, &c, &sn);
         cos_t[t * CSP + f] = c;
         sin_t[t * CSP + f] = sn;
       }
@@ -1510,7 +1515,7 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_umma_kernel(DecArgs a, 
 constexpr int kDwN = 128;     // features per CTA
 constexpr int kDwMaxHq = 16;  // query heads per CTA
 
-struct DwSmem { int us, ck, cv, ldv, qs, pp, st, posb, bar, total; };  // bytes
+struct DwSmem { int us, ck, cv, ldv, qs, pp, st, posb, invf, bar, total; };  // bytes
 __host__ __device__ constexpr bool dw_one_buffer(int K) { return K > 128; }
 __host__ __device__ inline DwSmem dw_smem(int K, int Hq, int D) {
   DwSmem m;
@@ -1526,7 +1531,8 @@ __host__ __device__ inline DwSmem dw_smem(int K, int Hq, int D) {
   const int pp_bytes = 4 * Hq * kDuTok * 4;
   m.st = m.pp + (pp_bytes > 256 * 16 ? pp_bytes : 256 * 16);  // [Hq][4]: running max, correction
   m.posb = m.st + Hq * 16;                   // 2 x [128] positions
-  m.bar = m.posb + 2 * kDuTok * 4;           // mbarrier, TMEM base
+  m.invf = m.posb + 2 * kDuTok * 4;          // [D/2] inverse frequencies
+  m.bar = m.invf + (D / 2) * 4;              // mbarrier, TMEM base
   m.total = m.bar + 16;
   return m;
 }
@@ -1560,6 +1566,7 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_wide_kernel(DecArgs a, 
   float* ps = pp;  // the scores overwrite quarter 0's partials in place
   float* st = reinterpret_cast<float*>(dsm5 + L.st);
   int* posb = reinterpret_cast<int*>(dsm5 + L.posb);
+  float* invf = reinterpret_cast<float*>(dsm5 + L.invf);
   uint64_t* bar = reinterpret_cast<uint64_t*>(dsm5 + L.bar);
   uint32_t* tbase = reinterpret_cast<uint32_t*>(dsm5 + L.bar + 8);
   const int ldv = L.ldv;
@@ -1591,6 +1598,7 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_wide_kernel(DecArgs a, 
   const __nv_bfloat16* qp = reinterpret_cast<const __nv_bfloat16*>(a.q) + ((long)p * a.Hq + g0 * G) * D;
   for (int e = tid; e < Hq * D; e += kDuThreads) qs[e] = __bfloat162float(qp[e]);
   for (int h = tid; h < Hq; h += kDuThreads) st[4 * h] = -INFINITY;
+  if (tid < HALF) invf[tid] = a.inv_freq[tid];
   // key coordinates straight into the MMA's layout (columns past ld zero-filled
   // without a read, as are rows past the middle) and the tile's positions
   auto prefetch_k = [&](int tile, int pb) {
@@ -1601,9 +1609,11 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_wide_kernel(DecArgs a, 
       const bool ok = row < ntok && k < ld;
       cp16_zfill(ckb + dw_off<K>(row, k), Ck + (ok ? (long)row * ld + k : 0), ok);
     }
-    if (tid < kDuTok)
-      posb[pb * kDuTok + tid] =
-          tid < ntok ? (a.mid_pos ? a.mid_pos[p * a.mid_sp + j0 + tid] : a.pos_base + j0 + tid) : 0;
+    if (tid < kDuTok) {  // positions copied asynchronously too: the issuing warps do not wait on them
+      int* pd = posb + pb * kDuTok + tid;
+      if (tid < ntok && a.mid_pos) cp_async4_dec(pd, a.mid_pos + p * a.mid_sp + j0 + tid);
+      else *pd = tid < ntok ? a.pos_base + j0 + tid : 0;
+    }
     cp_async_commit();
   };
   auto prefetch_v = [&](int tile) {
@@ -1662,7 +1672,7 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_wide_kernel(DecArgs a, 
     {
       const int pos = posb[pb * kDuTok + tok];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) rope_cs_fast(pos, a.inv_freq[f0 + i], a.rope_scale, &cs[i], &sn[i]);
+      for (int i = 0; i < 16; ++i) rope_cs_fast(pos, invf[f0 + i], a.rope_scale, &cs[i], &sn[i]);
     }
     ok_wait = umma::mbar_wait_bounded(bar, phase, kDuWaitPolls);
     phase ^= 1;
