@@ -273,6 +273,158 @@ __global__ void __launch_bounds__(kScThreads) slash_score_dmma_kernel(CandSrc<T>
   }
 }
 
+// The scores for ranks past 32 or feature counts whose basis does not fit
+// shared memory whole (head_dim 128: n = 1024), on the fp64 tensor cores.  A
+// CTA takes kSwT candidates: their un-rotated rows (all heads, fp32) stay in
+// shared memory while the basis streams through in chunks of kSwF feature
+// rows (all rank columns, cp.async double buffer, columns past the rank
+// zero-filled by the copy).  Warp w owns candidate tile w % 2 and the column
+// tiles w / 2 + 4 i: every 8 x 8 x 4 step reuses one A fragment for up to
+// six column tiles.  The projection is summed in fp64 (exact products of the
+// fp32 values); |k|^2 in fp64; the score as in slash_score_dmma_kernel.
+constexpr int kSwT = 16;                    // candidates per CTA
+constexpr int kSwF = 64;                    // basis feature rows per chunk
+constexpr int kSwThreads = 256;
+constexpr int kSwMaxCT = 6;                 // column tiles per warp: rank <= 4 * 6 * 8 = 192
+
+__host__ __device__ inline int sw_ldb(int ld) { return 32 * ((ld + 31) / 32) + 8; }  // = 8 mod 32
+__host__ __device__ inline long sw_smem_bytes(int n, int D, int ld) {
+  return 8L * (kSwT + 4 * kSwT) + 4L * (kSwT * (long)(n + 4) + 2L * kSwF * sw_ldb(ld) + kSwT * (D / 2) * 2);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kSwThreads) slash_score_dmma_wide_kernel(CandSrc<T> src, int m, int H, int D,
+                                                                          RopeArgs rope, const float* u,
+                                                                          long u_sp, int ld, const int* rr,
+                                                                          float* scores, long sc_sp,
+                                                                          RankArgs rk) {
+  extern __shared__ __align__(16) double wsm[];
+  const int p = blockIdx.y;
+  const int j0 = blockIdx.x * kSwT;
+  const int half = D / 2, n = H * D;
+  const int r = rr[p];
+  const int ldx = n + 4, ldb = sw_ldb(ld);
+  double* kk = wsm;                                   // [kSwT] |k|^2
+  double* ccw = kk + kSwT;                            // [4][kSwT] |c|^2 per column-tile set
+  float* xs = reinterpret_cast<float*>(ccw + 4 * kSwT);  // [kSwT][ldx] un-rotated rows
+  float* bs = xs + kSwT * ldx;                        // 2 x [kSwF][ldb] basis chunks
+  float* cs = bs + 2 * kSwF * ldb;                    // [kSwT][half][2] RoPE
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int mt = warp & 1, wc = warp >> 1;
+  const int grp = lane >> 2, tig = lane & 3;
+  const float* U = u + p * u_sp;
+  const int q4 = (r + 3) / 4;          // 16-byte chunks of a basis row that hold rank columns
+  const int nct = (r + 7) / 8;         // column tiles
+  const int nchunks = n / kSwF;
+  auto stage = [&](int c, int buf) {   // basis rows [c kSwF, +kSwF), columns [0, 8 nct)
+    float* dst = bs + buf * kSwF * ldb;
+    const int q8 = 2 * nct;            // 16-byte chunks per row to fill (zeros past the rank)
+    for (int e = tid; e < kSwF * q8; e += kSwThreads) {
+      const int f = e / q8, q = e % q8;
+      const int bytes = q < q4 ? 4 * min(4, r - 4 * q) : 0;
+      const float* srcp = U + (long)(c * kSwF + f) * ld + (q < q4 ? 4 * q : 0);
+      const unsigned sa = (unsigned)__cvta_generic_to_shared(dst + f * ldb + 4 * q);
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(sa), "l"(srcp), "r"(bytes)
+                   : "memory");
+    }
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+  };
+  if (r > 0) stage(0, 0);
+  for (int e = tid; e < kSwT * half; e += kSwThreads) {
+    const int a = e / half, f = e % half;
+    const int jj = j0 + a;
+    float c = 1.f, s = 0.f;
+    if (jj < m) rope_cs(src.pos(p, jj), rope.inv_freq[f], rope.scale, &c, &s);
+    cs[2 * e] = c;
+    cs[2 * e + 1] = s;
+  }
+  __syncthreads();
+  for (int e = tid; e < kSwT * H * half; e += kSwThreads) {  // (candidate, head, pair), pairs fastest
+    const int a = e / (H * half), hf = e % (H * half), h = hf / half, f = hf % half;
+    const int jj = j0 + a;
+    float y1 = 0.f, y2 = 0.f;
+    if (jj < m) {
+      const T* kr = src.krow(p, jj) + h * D;
+      const float x1 = load_f<T>(kr + f), x2 = load_f<T>(kr + f + half);
+      const float c = cs[2 * (a * half + f)], s = cs[2 * (a * half + f) + 1];
+      y1 = (x1 * c + x2 * s) / rope.scale_sq;
+      y2 = (x2 * c - x1 * s) / rope.scale_sq;
+    }
+    xs[a * ldx + h * D + f] = y1;
+    xs[a * ldx + h * D + f + half] = y2;
+  }
+  __syncthreads();
+  {  // |k|^2: 16 threads per candidate, fp64
+    const int a = tid / 16, sub = tid % 16;
+    double sq = 0.0;
+    for (int d = sub; d < n; d += 16) {
+      const double v = xs[a * ldx + d];
+      sq = fma(v, v, sq);
+    }
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    if (sub == 0) kk[a] = sq;
+  }
+  double acc[kSwMaxCT][2];
+#pragma unroll
+  for (int i = 0; i < kSwMaxCT; ++i) { acc[i][0] = 0.0; acc[i][1] = 0.0; }
+  if (r > 0) {
+    const float* xa = xs + (mt * 8 + grp) * ldx + tig;
+    for (int c = 0; c < nchunks; ++c) {
+      asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+      __syncthreads();  // chunk c landed for every thread; chunk c - 1's buffer is free
+      if (c + 1 < nchunks) stage(c + 1, (c + 1) & 1);
+      const float* bb = bs + (c & 1) * kSwF * ldb + tig * ldb + grp;
+      const float* xc = xa + c * kSwF;
+#pragma unroll 4
+      for (int k0 = 0; k0 < kSwF; k0 += 4) {
+        const double av = xc[k0];
+#pragma unroll
+        for (int i = 0; i < kSwMaxCT; ++i) {
+          const int ct = wc + 4 * i;
+          if (ct < nct) dmma_8x8x4(acc[i][0], acc[i][1], av, (double)bb[k0 * ldb + ct * 8]);
+        }
+      }
+    }
+  }
+  {  // |c|^2 of each candidate row: the lane's values, the row's four lanes, then the four warps
+    double cc = 0.0;
+#pragma unroll
+    for (int i = 0; i < kSwMaxCT; ++i) cc += acc[i][0] * acc[i][0] + acc[i][1] * acc[i][1];
+    cc += __shfl_xor_sync(0xffffffffu, cc, 1);
+    cc += __shfl_xor_sync(0xffffffffu, cc, 2);
+    if (tig == 0) ccw[wc * kSwT + mt * 8 + grp] = cc;
+  }
+  __syncthreads();
+  if (tid < kSwT) {
+    const int j = j0 + tid;
+    if (j < m) {
+      float out;
+      if (r == 0) {
+        out = 1.f;
+      } else {
+        const double k2 = kk[tid];
+        const double c2 = (ccw[tid] + ccw[kSwT + tid]) + (ccw[2 * kSwT + tid] + ccw[3 * kSwT + tid]);
+        out = (float)(sqrt(fmax(k2 - c2, 0.0)) / fmax(sqrt(k2), 1e-12));
+      }
+      scores[p * sc_sp + j] = out;
+    }
+  }
+  if (rk.done) {  // the CTA that completes a problem's scores also ranks it
+    __shared__ int s_last;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(rk.done + p, 1) == (int)gridDim.x - 1;
+    __syncthreads();
+    if (s_last) {
+      __threadfence();
+      if (tid == 0) rk.done[p] = 0;
+      rank_problem<T>(src, p, m, rk.keep_n, H, D, rope, scores, sc_sp, rk.hh_neighbor, rk.out,
+                      reinterpret_cast<float*>(wsm));
+    }
+  }
+}
+
 // The 16/sizeof(T) elements of one 16-byte chunk, widened to fp32 (dst 16-byte aligned).
 template <typename T> __device__ __forceinline__ void widen16(uint4 r, float* dst);
 template <> __device__ __forceinline__ void widen16<float>(uint4 r, float* dst) {
@@ -629,6 +781,24 @@ int launch_slash_score(const CandSrc<T>& src, int P, int m, int H, int D, RopeAr
     {
       KTimerScope kts_("slash_score_kernel", stream);
       slash_score_dmma_kernel<T><<<dim3((m + kScT - 1) / kScT, P), kScThreads, dsmem, stream>>>(
+          src, m, H, D, rope, u, u_sp, ld, rr, scores, sc_sp, rk);
+    }
+    if (fused) *fused = fuse_ok;
+    return check_launch("slash_score_kernel");
+  }
+  // ranks past 32, or a basis too large for shared memory whole: the basis
+  // streams through in feature chunks (slash_score_dmma_wide_kernel)
+  const long wsm = sw_smem_bytes((int)n, D, ld);
+  const bool wal = ld % 4 == 0 && u_sp % 4 == 0 && reinterpret_cast<uintptr_t>(u) % 16 == 0;
+  if (ld <= 32 * kSwMaxCT && n % kSwF == 0 && D % 2 == 0 && wal && wsm <= device_smem_optin()) {
+    const bool fuse_ok = fuse && fuse->done && 16L * m <= wsm && fuse->out.order_sp >= m;
+    RankArgs rk{};
+    if (fuse_ok) rk = *fuse;
+    if (int rc = ensure_smem((const void*)slash_score_dmma_wide_kernel<T>, (int)wsm, "slash_score_kernel"))
+      return rc;
+    {
+      KTimerScope kts_("slash_score_kernel", stream);
+      slash_score_dmma_wide_kernel<T><<<dim3((m + kSwT - 1) / kSwT, P), kSwThreads, (int)wsm, stream>>>(
           src, m, H, D, rope, u, u_sp, ld, rr, scores, sc_sp, rk);
     }
     if (fused) *fused = fuse_ok;
