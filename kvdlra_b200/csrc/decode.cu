@@ -40,119 +40,10 @@ struct DecArgs {
   float* part; long part_sp_chunk;  // partial record per (problem, group, chunk)
   int n_chunks;
   int* status;                      // device status words (bounded waits report here)
-  int* done;                        // [problem][group] records written, when the last CTA of a
-                                    // (problem, group) merges them itself (else null: a merge launch)
 };
 
 // Partial record layout (floats): m[G], l[G], acc_d[G][D], acc_c[G][ld]
 __host__ __device__ inline long part_floats(int G, int D, int ld) { return 2L * G + (long)G * D + (long)G * ld; }
-
-// Shared-memory floats merge_groups needs for ng groups.
-__host__ __device__ inline long merge_floats(int ng, int G, int D, int ld, int n_chunks) {
-  return (long)ng * G * (n_chunks + 2 + D + ld);
-}
-
-// The softmax merge of KV groups [g0, g0 + ng) of problem p: every chunk's
-// partial record (m, l, acc_d, acc_c) combined across chunks, then U_v
-// applied to the coordinate-space part, written to the output.  Every thread
-// of the CTA takes part; `sm` holds merge_floats(...) floats.  The records
-// are read through L2 (another CTA of the same launch may have written them).
-template <typename T>
-__device__ void merge_groups(const DecArgs& a, int p, int g0, int ng, float* sm) {
-  const int D = a.D, G = a.G, ld = a.ld, nch = a.n_chunks, NH = ng * G;
-  const long sp = a.part_sp_chunk;
-  float* accc = sm;              // [NH][ld]
-  float* accd = accc + NH * ld;  // [NH][D]
-  float* ml = accd + NH * D;     // [NH][2]: M, Lsum
-  float* sc = ml + 2 * NH;       // [n_chunks][NH]: exp(m_c - M) per chunk and head
-  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32, nw = blockDim.x / 32;
-  for (int hh = warp; hh < NH; hh += nw) {  // a warp per head, lanes over the chunks
-    const int qh = hh % G;
-    const float* parts = a.part + (long)(p * a.H + g0 + hh / G) * nch * sp;
-    float M = -INFINITY;
-    for (int c = lane; c < nch; c += 32) M = fmaxf(M, __ldcg(parts + c * sp + qh));
-    M = warp_max(M);
-    float Ls = 0.f;
-    for (int c = lane; c < nch; c += 32) {
-      const float mc = __ldcg(parts + c * sp + qh);
-      const float f = mc == -INFINITY ? 0.f : expf(mc - M);
-      sc[c * NH + hh] = f;
-      Ls = fmaf(f, __ldcg(parts + c * sp + G + qh), Ls);
-    }
-    Ls = warp_sum(Ls);
-    if (lane == 0) {
-      ml[2 * hh] = M;
-      ml[2 * hh + 1] = Ls;
-    }
-  }
-  __syncthreads();
-  const int per_g = G * (D + ld);
-  for (int e = threadIdx.x; e < ng * per_g; e += blockDim.x) {
-    const int gi = e / per_g, el = e % per_g;
-    const float* parts = a.part + (long)(p * a.H + g0 + gi) * nch * sp;
-    int qh; long off;
-    if (el < G * D) { qh = el / D; off = 2 * G + el; }
-    else { qh = (el - G * D) / ld; off = 2 * G + G * D + (el - G * D); }
-    const int hh = gi * G + qh;
-    float v0 = 0.f, v1 = 0.f, v2 = 0.f, v3 = 0.f;  // four chains, their loads in flight together
-    int c = 0;
-    for (; c + 4 <= nch; c += 4) {
-      const float x0 = __ldcg(parts + c * sp + off), x1 = __ldcg(parts + (c + 1) * sp + off);
-      const float x2 = __ldcg(parts + (c + 2) * sp + off), x3 = __ldcg(parts + (c + 3) * sp + off);
-      v0 = fmaf(sc[c * NH + hh], x0, v0);
-      v1 = fmaf(sc[(c + 1) * NH + hh], x1, v1);
-      v2 = fmaf(sc[(c + 2) * NH + hh], x2, v2);
-      v3 = fmaf(sc[(c + 3) * NH + hh], x3, v3);
-    }
-    for (; c < nch; ++c) v0 = fmaf(sc[c * NH + hh], __ldcg(parts + c * sp + off), v0);
-    const float v = (v0 + v1) + (v2 + v3);
-    if (el < G * D) accd[gi * G * D + el] = v;
-    else accc[gi * G * ld + (el - G * D)] = v;
-  }
-  __syncthreads();
-  const float* Uv = a.uv + p * a.u_sp;
-  const int r_v = a.rv[p];
-  T* out = reinterpret_cast<T*>(a.out) + (long)p * a.Hq * D;
-  for (int e = threadIdx.x; e < NH * D; e += blockDim.x) {
-    const int hh = e / D, d = e % D;
-    const int g = g0 + hh / G, qh = hh % G;
-    float v = accd[e];
-    const float* ur = Uv + (long)(g * D + d) * ld;
-#pragma unroll 8
-    for (int c = 0; c < r_v; ++c) v = fmaf(ur[c], accc[hh * ld + c], v);
-    store_f<T>(out + (long)(g * G + qh) * D + d, v / ml[2 * hh + 1]);
-  }
-}
-
-// The tail of a CTA that wrote the partial records of KV groups [g0, g0 + ng)
-// of problem p: count them in a.done; the CTA that completes a group's count
-// merges that group (all the groups at once when it completes every one).
-template <typename T>
-__device__ void merge_if_last(const DecArgs& a, int p, int g0, int ng, float* sm) {
-  __shared__ int s_last[8];
-  __shared__ int s_all;
-  __threadfence();  // this CTA's records are visible before it counts them
-  __syncthreads();
-  if (threadIdx.x == 0) s_all = 1;
-  __syncthreads();
-  if ((int)threadIdx.x < ng) {
-    const int last = atomicAdd(a.done + p * a.H + g0 + threadIdx.x, 1) == a.n_chunks - 1;
-    s_last[threadIdx.x] = last;
-    if (!last) atomicAnd(&s_all, 0);
-  }
-  __syncthreads();
-  if (s_all) {
-    __threadfence();
-    merge_groups<T>(a, p, g0, ng, sm);
-    return;
-  }
-  for (int i = 0; i < ng; ++i)
-    if (s_last[i]) {
-      __threadfence();
-      merge_groups<T>(a, p, g0 + i, 1, sm);
-      __syncthreads();
-    }
-}
 
 template <typename T, int NV, int NC>
 __global__ void __launch_bounds__(kDecThreads) decode_split_kernel(DecArgs a) {
@@ -860,7 +751,6 @@ __global__ void __launch_bounds__(kTileThreads) decode_mma_kernel(DecArgs a, int
       oc[1] = cacc[i][1];
     }
   }
-  if (a.done) merge_if_last<T>(a, p, g, 1, tsm);
 }
 
 // ------------------------------------------------ middle tier, all groups
@@ -1199,7 +1089,66 @@ __global__ void __launch_bounds__(kMidThreads) decode_mid_kernel(DecArgs a, int 
 template <typename T>
 __global__ void __launch_bounds__(512) decode_merge_kernel(DecArgs a) {
   extern __shared__ __align__(16) float msm2[];
-  merge_groups<T>(a, blockIdx.y, blockIdx.x, 1, msm2);
+  const int g = blockIdx.x, p = blockIdx.y;
+  const int D = a.D, G = a.G, ld = a.ld;
+  const long rec = part_floats(G, D, ld);
+  const float* parts = a.part + (long)(p * a.H + g) * a.n_chunks * a.part_sp_chunk;
+  float* accc = msm2;        // [G][ld]
+  float* accd = accc + G * ld;  // [G][D]
+  float* ml = accd + G * D;     // [G][2]: M, Lsum
+  float* sc = ml + 2 * G;       // [n_chunks][G]: exp(m_c - M) per chunk and head
+  const int lane = threadIdx.x % 32, warp = threadIdx.x / 32, nw = blockDim.x / 32;
+  const int nch = a.n_chunks;
+  const long sp = a.part_sp_chunk;
+  for (int qh = warp; qh < G; qh += nw) {  // a warp per head, lanes over the chunks
+    float M = -INFINITY;
+    for (int c = lane; c < nch; c += 32) M = fmaxf(M, parts[c * sp + qh]);
+    M = warp_max(M);
+    float Ls = 0.f;
+    for (int c = lane; c < nch; c += 32) {
+      const float mc = parts[c * sp + qh];
+      const float f = mc == -INFINITY ? 0.f : expf(mc - M);
+      sc[c * G + qh] = f;
+      Ls = fmaf(f, parts[c * sp + G + qh], Ls);
+    }
+    Ls = warp_sum(Ls);
+    if (lane == 0) {
+      ml[2 * qh] = M;
+      ml[2 * qh + 1] = Ls;
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < G * (D + ld); e += blockDim.x) {
+    int qh; long off;
+    if (e < G * D) { qh = e / D; off = 2 * G + e; }
+    else { qh = (e - G * D) / ld; off = 2 * G + G * D + (e - G * D); }
+    float v0 = 0.f, v1 = 0.f, v2 = 0.f, v3 = 0.f;  // four chains, their loads in flight together
+    int c = 0;
+    for (; c + 4 <= nch; c += 4) {
+      const float x0 = parts[c * sp + off], x1 = parts[(c + 1) * sp + off];
+      const float x2 = parts[(c + 2) * sp + off], x3 = parts[(c + 3) * sp + off];
+      v0 = fmaf(sc[c * G + qh], x0, v0);
+      v1 = fmaf(sc[(c + 1) * G + qh], x1, v1);
+      v2 = fmaf(sc[(c + 2) * G + qh], x2, v2);
+      v3 = fmaf(sc[(c + 3) * G + qh], x3, v3);
+    }
+    for (; c < nch; ++c) v0 = fmaf(sc[c * G + qh], parts[c * sp + off], v0);
+    const float v = (v0 + v1) + (v2 + v3);
+    if (e < G * D) accd[e] = v;
+    else accc[e - G * D] = v;
+  }
+  __syncthreads();
+  const float* Uv = a.uv + p * a.u_sp;
+  const int r_v = a.rv[p];
+  T* out = reinterpret_cast<T*>(a.out) + (long)p * a.Hq * D;
+  for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
+    const int qh = e / D, d = e % D;
+    float v = accd[e];
+    const float* ur = Uv + (long)(g * D + d) * ld;
+#pragma unroll 8
+    for (int c = 0; c < r_v; ++c) v = fmaf(ur[c], accc[qh * ld + c], v);
+    store_f<T>(out + (long)(g * G + qh) * D + d, v / ml[2 * qh + 1]);
+  }
 }
 
 }  // namespace kvd
@@ -1217,8 +1166,7 @@ size_t decode_ws_bytes(const kvd_config& c, int count, int num_q_heads, int n_he
   const int nvt = (c.n_sink + c.hh_budget + kTT - 1) / kTT + (c.ring_cap + kTT - 1) / kTT;
   const int ch_tiled = nvt + ((c.w_cap + kTT - 1) / kTT + 1) / 2;
   const int ch = dec_chunks(L_max) > ch_tiled ? dec_chunks(L_max) : ch_tiled;
-  // the records, then a counter per (problem, group) (16-byte aligned)
-  return (((size_t)count * n_heads * ch * rec * 4 + 15) & ~(size_t)15) + (size_t)count * n_heads * 4 + 256;
+  return (size_t)count * n_heads * ch * rec * 4 + 256;
 }
 
 // ------------------------------------------------------------------
@@ -1544,7 +1492,6 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_umma_kernel(DecArgs a, 
 #pragma unroll
     for (int j = 0; j < 4; ++j) o[j] = ok_wait ? vacc[j] + vred[vt * 4 + j] : 0.f;
   }
-  if (a.done) merge_if_last<__nv_bfloat16>(a, p, g0, H, reinterpret_cast<float*>(dsm4));
 }
 
 // ------------------------------------------------------------------
@@ -1855,7 +1802,6 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_wide_kernel(DecArgs a, 
 #pragma unroll
     for (int j = 0; j < 4; ++j) o[j] = ok_wait ? vacc[j] + vred[vt * 4 + j] : 0.f;
   }
-  if (a.done) merge_if_last<__nv_bfloat16>(a, p, g0, HB, reinterpret_cast<float*>(dsm5));
 }
 
 template <typename T>
@@ -1874,7 +1820,6 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
   // h0 * D features into each token row (stride nrow) and whose basis rows
   // start at row h0 * D; the query and output hold only their heads
   a.H = hc; a.D = c.head_dim; a.G = Hq / hc; a.ld = c.rank; a.Hq = Hq; a.nrow = n;
-  a.done = nullptr;
   const bool d_ok = (c.head_dim <= 32) || ((c.head_dim / 2) % 32 == 0);
   if (a.G > kMaxG || c.head_dim > 32 * kMaxNV || c.rank > 32 * kMaxNC || !d_ok) {
     set_error("factored decode: unsupported shape (G=%d D=%d r=%d)", a.G, c.head_dim, c.rank);
@@ -1979,20 +1924,6 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
     const size_t need2 = (size_t)count * a.H * a.n_chunks * a.part_sp_chunk * 4;
     if (need2 > ws_bytes) { set_error("factored decode: workspace too small"); return KVD_ERR_WORKSPACE; }
     constexpr bool kSplit = sizeof(T) == 4;
-    // tcgen05 middle tier: the CTA that writes the last record of a (problem,
-    // group) merges it, so no merge launch follows (counters after the records,
-    // zeroed here; each kernel's shared memory must hold the merge's scratch)
-    const int tsm_v = 4 * (a.G * a.D + 2 * kTT * (a.D + 4) + a.G * (kTT + 4) + 4 * a.G);
-    const size_t cnt_off = (need2 + 15) & ~(size_t)15;
-    const long mid_sm = umma_mid ? du_smem(du_n, du_hq, a.D).total : umma_wide ? dw_smem(dw_K, dw_hq, a.D).total : 0;
-    const int mid_ng = umma_mid ? du_hb : dw_hb;
-    const bool fuse_merge = (umma_mid || umma_wide) && cnt_off + (size_t)count * a.H * 4 <= ws_bytes &&
-                            4 * merge_floats(1, a.G, a.D, a.ld, a.n_chunks) <= tsm_v &&
-                            4 * merge_floats(mid_ng, a.G, a.D, a.ld, a.n_chunks) <= mid_sm;
-    if (fuse_merge) {
-      a.done = reinterpret_cast<int*>(reinterpret_cast<char*>(a.part) + cnt_off);
-      cudaMemsetAsync(a.done, 0, (size_t)count * a.H * sizeof(int), s);
-    }
     auto mid_fn = a.D == 64 ? decode_mid_kernel<T, 64, kSplit> : decode_mid_kernel<T, 128, kSplit>;
     if (!umma)
       if (int rc0 = ensure_smem((const void*)mid_fn, 4 * ms.total, "decode_mid_kernel")) return rc0;
@@ -2000,7 +1931,8 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
     const bool fork = side && ev_fork && ev_join && n_vch > 0;
     if (n_vch > 0) {
       // no middle tiles in this launch: keys and values of a tile, no coordinates or basis
-      const int tsmem = tsm_v;
+      const int ldk = a.D + 4;
+      const int tsmem = 4 * (a.G * a.D + 2 * kTT * ldk + a.G * (kTT + 4) + 4 * a.G);
       auto fn = a.D == 64 ? decode_mma_kernel<T, 64, kSplit> : decode_mma_kernel<T, 128, kSplit>;
       if (int rc0 = ensure_smem((const void*)fn, tsmem, "decode_mma_kernel")) return rc0;
       cudaStream_t vs = s;
@@ -2047,7 +1979,6 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
     }
     if (fork) cudaStreamWaitEvent(s, ev_join, 0);  // the merge reads both kernels' records
     if (int rc1 = check_launch("decode_mid_kernel")) return rc1;
-    if (fuse_merge) return KVD_OK;
   } else if (mma) {
     const int ldk = a.D + 4, ldv = a.ld + 8, ldc = a.ld + 4;
     const int tsmem = 4 * (a.G * a.D + kTT * ldk + kTT * (ldk > ldv ? ldk : ldv) +
