@@ -1187,6 +1187,9 @@ size_t decode_ws_bytes(const kvd_config& c, int count, int num_q_heads, int n_he
 constexpr int kDuTok = 128;
 constexpr int kDuThreads = 512;
 constexpr int kDuK = 32;  // staged rank columns (rank <= 32)
+// score-row pitch: = 8 mod 32, so the value product's 16-byte probability
+// reads of four heads in a warp fall on distinct banks
+constexpr int kDuPs = kDuTok + 8;
 constexpr long kDuWaitPolls = 1L << 22;
 
 struct DuSmem { int us, ck, cv, ldv, qs, cs, ps, st, vred, posb, invf, bar, total; };  // bytes
@@ -1199,8 +1202,8 @@ __host__ __device__ inline DuSmem du_smem(int n, int Hq, int D) {
   m.cv = m.ck + 2 * kDuTok * kDuK * 4;        // 2 x [128][ldv] value coordinates
   m.qs = m.cv + 2 * kDuTok * m.ldv * 4;       // [Hq][D] queries
   m.cs = m.qs + Hq * D * 4;                   // [128 tokens][D/2 + 4] cos, then the same for sin
-  m.ps = m.cs + 2 * kDuTok * (D / 2 + 4) * 4; // [Hq][128] scores, then probabilities
-  m.st = m.ps + Hq * kDuTok * 4;              // [Hq][4]: running max, correction
+  m.ps = m.cs + 2 * kDuTok * (D / 2 + 4) * 4; // [Hq][kDuPs] scores, then probabilities
+  m.st = m.ps + Hq * kDuPs * 4;               // [Hq][4]: running max, correction
   m.vred = m.st + Hq * 16;                    // [256][4] value-product halves
   m.posb = m.vred + 256 * 16;                 // 2 x [128] positions
   m.invf = m.posb + 2 * kDuTok * 4;           // [D/2] inverse frequencies
@@ -1411,7 +1414,7 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_umma_kernel(DecArgs a, 
 #pragma unroll
         for (int qh = 0; qh < kMaxG; ++qh)
           if (qh < G)
-            ps[(g * G + qh) * kDuTok + tok] =
+            ps[(g * G + qh) * kDuPs + tok] =
                 tok < ntok ? ((s1[qh].x + s1[qh].y) + (s2[qh].x + s2[qh].y)) * a.scaling : -INFINITY;
       }
     }
@@ -1423,7 +1426,7 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_umma_kernel(DecArgs a, 
     for (int i = 0; i < 4; ++i) {
       const int row = warp + 16 * i;
       if (row >= Hq) continue;
-      float* pr = ps + row * kDuTok;
+      float* pr = ps + row * kDuPs;
       const float x0 = pr[lane], x1 = pr[lane + 32], x2 = pr[lane + 64], x3 = pr[lane + 96];
       float mt = fmaxf(fmaxf(x0, x1), fmaxf(x2, x3));
       mt = warp_max(mt);
@@ -1448,16 +1451,20 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_umma_kernel(DecArgs a, 
       const float corr = st[4 * vh + 1];
 #pragma unroll
       for (int j = 0; j < 4; ++j) vacc[j] *= corr;
-      const float* pr = ps + vh * kDuTok + 64 * th;
+      const float* pr = ps + vh * kDuPs + 64 * th;
       const float* cvb = reinterpret_cast<const float*>(dsm4 + L.cv) + buf * kDuTok * ldv + 64 * th * ldv;
-#pragma unroll 8
-      for (int t = 0; t < 64; ++t) {
-        const float pt = pr[t];
-        const float4 cvv = *reinterpret_cast<const float4*>(cvb + t * ldv + vc);
-        vacc[0] = fmaf(pt, cvv.x, vacc[0]);
-        vacc[1] = fmaf(pt, cvv.y, vacc[1]);
-        vacc[2] = fmaf(pt, cvv.z, vacc[2]);
-        vacc[3] = fmaf(pt, cvv.w, vacc[3]);
+#pragma unroll 2
+      for (int t = 0; t < 64; t += 4) {  // four tokens' probabilities in one 16-byte read
+        const float4 p4 = *reinterpret_cast<const float4*>(pr + t);
+        const float pt[4] = {p4.x, p4.y, p4.z, p4.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float4 cvv = *reinterpret_cast<const float4*>(cvb + (t + u) * ldv + vc);
+          vacc[0] = fmaf(pt[u], cvv.x, vacc[0]);
+          vacc[1] = fmaf(pt[u], cvv.y, vacc[1]);
+          vacc[2] = fmaf(pt[u], cvv.z, vacc[2]);
+          vacc[3] = fmaf(pt[u], cvv.w, vacc[3]);
+        }
       }
     }
     __syncthreads();  // this tile's buffers free for the prefetch after next
@@ -1758,14 +1765,18 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_wide_kernel(DecArgs a, 
       for (int j = 0; j < 4; ++j) vacc[j] *= corr;
       const float* pr = ps + vh * kDuTok + 64 * th;
       const float* cvh = cvb + 64 * th * ldv;
-#pragma unroll 8
-      for (int t = 0; t < 64; ++t) {
-        const float pt = pr[t];
-        const float4 cvv = *reinterpret_cast<const float4*>(cvh + t * ldv + vc);
-        vacc[0] = fmaf(pt, cvv.x, vacc[0]);
-        vacc[1] = fmaf(pt, cvv.y, vacc[1]);
-        vacc[2] = fmaf(pt, cvv.z, vacc[2]);
-        vacc[3] = fmaf(pt, cvv.w, vacc[3]);
+#pragma unroll 2
+      for (int t = 0; t < 64; t += 4) {  // four tokens' probabilities in one 16-byte read
+        const float4 p4 = *reinterpret_cast<const float4*>(pr + t);
+        const float pt[4] = {p4.x, p4.y, p4.z, p4.w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float4 cvv = *reinterpret_cast<const float4*>(cvh + (t + u) * ldv + vc);
+          vacc[0] = fmaf(pt[u], cvv.x, vacc[0]);
+          vacc[1] = fmaf(pt[u], cvv.y, vacc[1]);
+          vacc[2] = fmaf(pt[u], cvv.z, vacc[2]);
+          vacc[3] = fmaf(pt[u], cvv.w, vacc[3]);
+        }
       }
     }
     __syncthreads();  // the value buffer is free
