@@ -1187,16 +1187,17 @@ size_t decode_ws_bytes(const kvd_config& c, int count, int num_q_heads, int n_he
 constexpr int kDuTok = 128;
 constexpr int kDuThreads = 512;
 constexpr int kDuK = 32;  // staged rank columns (rank <= 32)
-// score-row pitch: = 8 mod 32, so the value product's 16-byte probability
-// reads of four heads in a warp fall on distinct banks
-constexpr int kDuPs = kDuTok + 8;
+// score-row pitch = 4 mod 32 and value-coordinate pitch = 8 mod 32: the
+// value product's TF32 fragment loads (rows g, columns t of the
+// probabilities; rows t, columns g of the coordinates) hit distinct banks
+constexpr int kDuPs = kDuTok + 4;
 constexpr long kDuWaitPolls = 1L << 22;
 
-struct DuSmem { int us, ck, cv, ldv, qs, cs, ps, st, vred, posb, invf, bar, total; };  // bytes
+struct DuSmem { int us, ck, cv, ldv, qs, cs, ps, st, posb, invf, bar, total; };  // bytes
 // n = this CTA's features (its KV groups x D), Hq = its query heads
 __host__ __device__ inline DuSmem du_smem(int n, int Hq, int D) {
   DuSmem m;
-  m.ldv = kDuK + 4;
+  m.ldv = kDuK + 8;
   m.us = 0;                                   // [n][32] basis, core-matrix layout
   m.ck = m.us + n * kDuK * 4;                 // 2 x [128][32] key coordinates, core-matrix layout
   m.cv = m.ck + 2 * kDuTok * kDuK * 4;        // 2 x [128][ldv] value coordinates
@@ -1204,8 +1205,7 @@ __host__ __device__ inline DuSmem du_smem(int n, int Hq, int D) {
   m.cs = m.qs + Hq * D * 4;                   // [128 tokens][D/2 + 4] cos, then the same for sin
   m.ps = m.cs + 2 * kDuTok * (D / 2 + 4) * 4; // [Hq][kDuPs] scores, then probabilities
   m.st = m.ps + Hq * kDuPs * 4;               // [Hq][4]: running max, correction
-  m.vred = m.st + Hq * 16;                    // [256][4] value-product halves
-  m.posb = m.vred + 256 * 16;                 // 2 x [128] positions
+  m.posb = m.st + Hq * 16;                    // 2 x [128] positions
   m.invf = m.posb + 2 * kDuTok * 4;           // [D/2] inverse frequencies
   m.bar = m.invf + (D / 2) * 4;               // mbarrier, TMEM base
   m.total = m.bar + 16;
@@ -1250,7 +1250,6 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_umma_kernel(DecArgs a, 
   float* sin_t = cos_t + kDuTok * CSP;
   float* ps = reinterpret_cast<float*>(dsm4 + L.ps);
   float* st = reinterpret_cast<float*>(dsm4 + L.st);
-  float* vred = reinterpret_cast<float*>(dsm4 + L.vred);
   int* posb = reinterpret_cast<int*>(dsm4 + L.posb);
   float* invf = reinterpret_cast<float*>(dsm4 + L.invf);
   uint64_t* bar = reinterpret_cast<uint64_t*>(dsm4 + L.bar);
@@ -1315,12 +1314,12 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_umma_kernel(DecArgs a, 
   const uint32_t tmem = *tbase;
   const uint32_t us_addr = (uint32_t)__cvta_generic_to_shared(us);
   const uint32_t idesc = umma::idesc_tf32(kDuTok, 256);
-  // value product: thread (vh, vc) of token half th accumulates acc_c[vh][vc..vc+4)
-  const int nvq = ld / 4;
-  const int th = tid >> 8, vt = tid & 255;
-  const int vh = vt / nvq, vc = 4 * (vt % nvq);
-  const bool vown = vh < Hq;
-  float vacc[4] = {0.f, 0.f, 0.f, 0.f};
+  // value product acc_c (Hq x ld) += P (Hq x tokens) C_v (tokens x ld) on
+  // warp-level TF32 MMAs (m16n8k8): a task is a 16-head m-tile, an 8-column
+  // n-tile and a 64-token half of the tile; warp w takes tasks w and w + 16
+  const int n_nt = (ld + 7) / 8, n_task = 2 * ((Hq + 15) / 16) * n_nt;
+  const int fg = lane >> 2, ft = lane & 3;
+  float vfr[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
   float lrow[4] = {0.f, 0.f, 0.f, 0.f};  // sums of the rows warp + 16 i
   uint32_t phase = 0;
   bool ok_wait = true;
@@ -1447,23 +1446,27 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_umma_kernel(DecArgs a, 
       }
     }
     __syncthreads();
-    if (vown) {  // acc_c[vh][vc..vc+4) = corr * acc + sum_t p[vh][t] c_v[t][vc..] over this half
-      const float corr = st[4 * vh + 1];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) vacc[j] *= corr;
-      const float* pr = ps + vh * kDuPs + 64 * th;
-      const float* cvb = reinterpret_cast<const float*>(dsm4 + L.cv) + buf * kDuTok * ldv + 64 * th * ldv;
-#pragma unroll 2
-      for (int t = 0; t < 64; t += 4) {  // four tokens' probabilities in one 16-byte read
-        const float4 p4 = *reinterpret_cast<const float4*>(pr + t);
-        const float pt[4] = {p4.x, p4.y, p4.z, p4.w};
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float4 cvv = *reinterpret_cast<const float4*>(cvb + (t + u) * ldv + vc);
-          vacc[0] = fmaf(pt[u], cvv.x, vacc[0]);
-          vacc[1] = fmaf(pt[u], cvv.y, vacc[1]);
-          vacc[2] = fmaf(pt[u], cvv.z, vacc[2]);
-          vacc[3] = fmaf(pt[u], cvv.w, vacc[3]);
+    for (int k = 0; k < 2; ++k) {  // acc = corr * acc + P C_v over the task's token half
+      const int task = warp + 16 * k;
+      if (task < n_task) {
+        const int kh = task & 1, ot = task >> 1, mt = ot / n_nt, nt = ot % n_nt;
+        const int r0 = 16 * mt + fg, r1 = r0 + 8;
+        // rows past Hq read row Hq - 1 (inside the buffer) and use zero
+        const bool v0 = r0 < Hq, v1 = r1 < Hq;
+        const int q0 = v0 ? r0 : Hq - 1, q1 = v1 ? r1 : Hq - 1;
+        const float c0 = v0 ? st[4 * q0 + 1] : 0.f, c1 = v1 ? st[4 * q1 + 1] : 0.f;
+        vfr[k][0] *= c0; vfr[k][1] *= c0; vfr[k][2] *= c1; vfr[k][3] *= c1;
+        const float* p0 = ps + q0 * kDuPs + 64 * kh + ft;
+        const float* p1 = ps + q1 * kDuPs + 64 * kh + ft;
+        const float* cb = reinterpret_cast<const float*>(dsm4 + L.cv) + buf * kDuTok * ldv +
+                          (64 * kh + ft) * ldv + 8 * nt + fg;
+#pragma unroll 4
+        for (int k0 = 0; k0 < 64; k0 += 8) {
+          const float x0 = p0[k0], x1 = p1[k0], x2 = p0[k0 + 4], x3 = p1[k0 + 4];
+          const uint32_t af[4] = {v0 ? tf32_bits(x0) : 0u, v1 ? tf32_bits(x1) : 0u,
+                                  v0 ? tf32_bits(x2) : 0u, v1 ? tf32_bits(x3) : 0u};
+          mma_tf32(vfr[k], af, tf32_bits(cb[k0 * ldv]), tf32_bits(cb[(k0 + 4) * ldv]));
         }
       }
     }
@@ -1474,9 +1477,17 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_umma_kernel(DecArgs a, 
     if (tid == 0) atomicOr(&status[kStatusTimeout], 16);
     umma::mbar_wait_bounded(bar, phase ^ 1, kDuWaitPolls);
   }
-  if (th == 1 && vown)
+  __syncthreads();  // every product has read the probabilities before their rows take the halves
+  float* hsum = ps;  // [Hq][32] the second token half's products
 #pragma unroll
-    for (int j = 0; j < 4; ++j) vred[vt * 4 + j] = vacc[j];
+  for (int k = 0; k < 2; ++k) {
+    const int task = warp + 16 * k;
+    if (task < n_task && (task & 1)) {
+      const int ot = task >> 1, r0 = 16 * (ot / n_nt) + fg, r1 = r0 + 8, cc = 8 * (ot % n_nt) + 2 * ft;
+      if (r0 < Hq) { hsum[r0 * 32 + cc] = vfr[k][0]; hsum[r0 * 32 + cc + 1] = vfr[k][1]; }
+      if (r1 < Hq) { hsum[r1 * 32 + cc] = vfr[k][2]; hsum[r1 * 32 + cc + 1] = vfr[k][3]; }
+    }
+  }
   __syncthreads();
   if (warp == 0) umma::tmem_dealloc(tmem, 512);
   // one partial record per group: m[G], l[G], acc_d[G][D] = 0, acc_c[G][ld]
@@ -1494,10 +1505,23 @@ __global__ void __launch_bounds__(kDuThreads) decode_mid_umma_kernel(DecArgs a, 
     }
   }
   for (int e = tid; e < H * G * D; e += kDuThreads) rec(e / (G * D))[2 * G + e % (G * D)] = 0.f;
-  if (th == 0 && vown) {
-    float* o = rec(vh / G) + 2 * G + G * D + (vh % G) * ld + vc;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) o[j] = ok_wait ? vacc[j] + vred[vt * 4 + j] : 0.f;
+  for (int k = 0; k < 2; ++k) {  // acc_c[G][ld] of each group: the two token halves
+    const int task = warp + 16 * k;
+    if (task < n_task && !(task & 1)) {
+      const int ot = task >> 1, r0 = 16 * (ot / n_nt) + fg, cc = 8 * (ot % n_nt) + 2 * ft;
+      if (cc < ld) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int row = r0 + 8 * h;
+          if (row < Hq) {
+            float* o = rec(row / G) + 2 * G + G * D + (row % G) * ld + cc;
+            o[0] = ok_wait ? vfr[k][2 * h] + hsum[row * 32 + cc] : 0.f;
+            o[1] = ok_wait ? vfr[k][2 * h + 1] + hsum[row * 32 + cc + 1] : 0.f;
+          }
+        }
+      }
+    }
   }
 }
 
@@ -1887,7 +1911,7 @@ int launch_factored_decode(const kvd_config& c, const kvd_buffers& b, const kvd_
   const int du_hb = du_groups(a.H, a.D), du_n = du_hb * a.D, du_hq = du_hb * a.G;
   const bool umma_mid = sizeof(T) == 2 && (a.D == 64 || a.D == 128) && mma && a.W > 0 &&
                         a.H % du_hb == 0 && du_n % 256 == 0 && a.ld <= kDuK &&
-                        a.ld % 4 == 0 && du_hq <= 64 && du_hq * (a.ld / 4) <= 256 &&
+                        a.ld % 4 == 0 && du_hq <= 64 &&
                         a.c_sp % 4 == 0 && (reinterpret_cast<uintptr_t>(a.ck) & 15) == 0 &&
                         (reinterpret_cast<uintptr_t>(a.cv) & 15) == 0 &&
                         (reinterpret_cast<uintptr_t>(a.uk) & 15) == 0 &&
